@@ -1,0 +1,227 @@
+"""fenix_b200 — B200 (sm_100a) surface-prediction inference: Python bindings over the C ABI.
+
+Every call goes through ``libfenix_b200.so`` (the ``extern "C"`` functions declared in
+``include/fenix_b200.h``). There is no Python or CPU fallback for any compute entry point: when
+the library is missing, :func:`lib` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "_build" / "libfenix_b200.so"
+_lib = None
+
+FX_OK = 0
+STATUS_NAMES = {
+    0: "ok",
+    1: "invalid_argument",
+    2: "not_found",
+    3: "io_error",
+    4: "fetch_failed",
+    5: "decode_error",
+    6: "unsupported",
+    7: "unimplemented",
+    8: "internal",
+}
+PREC_BF16, PREC_FP8 = 0, 1
+
+
+class FxError(RuntimeError):
+    """A non-zero fx_status from the library; ``code`` holds the status, the message fx_last_error()."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+class InferOpts(C.Structure):
+    """fx_infer_opts (mirrors the reference's ml::InferOptions subset)."""
+
+    _fields_ = [
+        ("patch", C.c_int),
+        ("overlap", C.c_double),
+        ("channel", C.c_int),
+        ("sigmoid", C.c_int),
+        ("batch", C.c_int),
+    ]
+
+
+def _sig(lib, name, res, args):
+    f = getattr(lib, name)
+    f.restype = res
+    f.argtypes = args
+
+
+def lib():
+    """Load libfenix_b200.so (building is done by ``fenix_b200.build``); raise if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("FENIX_B200_LIB", LIB_PATH))
+    if not path.exists():
+        raise FileNotFoundError(f"{path} not built: run `python -m fenix_b200.build` (or __graft_entry__.build())")
+    L = C.CDLL(str(path))
+    vp, i64, i32, f32p, u8p = C.c_void_p, C.c_int64, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_uint8)
+    _sig(L, "fx_last_error", C.c_char_p, [])
+    _sig(L, "fx_device_count", i32, [])
+    _sig(L, "fx_net_create", i32, [C.c_char_p, i32, i32, i32, i32, C.POINTER(vp)])
+    _sig(L, "fx_net_destroy", None, [vp])
+    _sig(L, "fx_net_patch", i32, [vp])
+    _sig(L, "fx_net_max_batch", i32, [vp])
+    _sig(L, "fx_net_classes", i32, [vp])
+    _sig(L, "fx_net_features", i32, [vp, C.POINTER(C.c_int), i32])
+    _sig(L, "fx_net_calibrate", i32, [vp, u8p, i32])
+    _sig(L, "fx_net_act_scales", i32, [vp, f32p, i32])
+    _sig(L, "fx_net_forward", i32, [vp, vp, i32, vp, i32, i32, vp])
+    _sig(L, "fx_predict_volume", i32, [vp, u8p, i64, i64, i64, C.POINTER(InferOpts), f32p, u8p])
+    _sig(L, "fx_predict_tiles_dev", i32, [vp, vp, i64, i64, i64, C.POINTER(InferOpts), i64, i64, vp, vp])
+    _sig(L, "fx_tile_starts", i64, [i64, i32, C.c_double, C.POINTER(C.c_int64), i64])
+    _sig(L, "fx_gaussian1d", None, [i32, f32p])
+    _sig(L, "fx_weight_profile", None, [f32p, i32, C.POINTER(C.c_int64), i64, i64, i64, i64, f32p])
+    _sig(L, "fx_norm_tiles", i32, [vp, i64, i64, i64, C.POINTER(C.c_int64), i32, i32, vp, vp])
+    _sig(L, "fx_conv3d", i32, [vp, i32, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp])
+    _sig(L, "fx_conv_transpose2", i32, [vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp])
+    _sig(L, "fx_accum_finalize", i32, [vp, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp])
+    _lib = L
+    return L
+
+
+def check(code: int) -> None:
+    if code != FX_OK:
+        raise FxError(code, lib().fx_last_error().decode())
+
+
+def _f32(a: np.ndarray):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+# ---- tiling math (host) --------------------------------------------------------------------
+def tile_starts(dim: int, patch: int, overlap: float) -> np.ndarray:
+    L = lib()
+    n = L.fx_tile_starts(dim, patch, overlap, None, 0)
+    out = np.zeros(n, dtype=np.int64)
+    L.fx_tile_starts(dim, patch, overlap, out.ctypes.data_as(C.POINTER(C.c_int64)), n)
+    return out
+
+
+def gaussian1d(n: int) -> np.ndarray:
+    out = np.zeros(n, dtype=np.float32)
+    lib().fx_gaussian1d(n, out.ctypes.data_as(C.POINTER(C.c_float)))
+    return out
+
+
+def weight_profile(g: np.ndarray, patch: int, starts: np.ndarray, c0: int, cn: int, dim: int) -> np.ndarray:
+    g = _f32(g)
+    st = np.ascontiguousarray(starts, dtype=np.int64)
+    out = np.zeros(cn, dtype=np.float32)
+    lib().fx_weight_profile(
+        g.ctypes.data_as(C.POINTER(C.c_float)),
+        patch,
+        st.ctypes.data_as(C.POINTER(C.c_int64)),
+        len(st),
+        c0,
+        cn,
+        dim,
+        out.ctypes.data_as(C.POINTER(C.c_float)),
+    )
+    return out
+
+
+def device_count() -> int:
+    return lib().fx_device_count()
+
+
+# ---- nets ----------------------------------------------------------------------------------
+class Net:
+    """A UNet on one GPU (fx_net). ``precision`` is "bf16" or "fp8"."""
+
+    def __init__(self, weights_path: str, patch: int, max_batch: int = 1, precision: str = "bf16", device: int = 0):
+        L = lib()
+        h = C.c_void_p()
+        prec = {"bf16": PREC_BF16, "fp8": PREC_FP8}[precision]
+        check(L.fx_net_create(str(weights_path).encode(), patch, max_batch, prec, device, C.byref(h)))
+        self._h = h
+        self.patch = patch
+        self.precision = precision
+        self.device = device
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().fx_net_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def classes(self) -> int:
+        return lib().fx_net_classes(self._h)
+
+    @property
+    def max_batch(self) -> int:
+        return lib().fx_net_max_batch(self._h)
+
+    def features(self) -> list[int]:
+        buf = (C.c_int * 16)()
+        n = lib().fx_net_features(self._h, buf, 16)
+        return list(buf[:n])
+
+    def calibrate(self, patches_u8: np.ndarray) -> None:
+        p = np.ascontiguousarray(patches_u8, dtype=np.uint8)
+        check(lib().fx_net_calibrate(self._h, p.ctypes.data_as(C.POINTER(C.c_uint8)), p.shape[0]))
+
+    def act_scales(self) -> np.ndarray:
+        buf = np.zeros(256, dtype=np.float32)
+        n = lib().fx_net_act_scales(self._h, buf.ctypes.data_as(C.POINTER(C.c_float)), 256)
+        return buf[:n]
+
+    def forward_dev(self, dev_tiles_ptr: int, nb: int, dev_prob_ptr: int, channel: int = 1, sigmoid: int = 0,
+                    stream: int | None = None) -> None:
+        check(lib().fx_net_forward(self._h, dev_tiles_ptr, nb, dev_prob_ptr, channel, sigmoid, stream))
+
+    def predict_volume(self, vol_u8: np.ndarray, overlap: float = 0.5, batch: int = 1, channel: int = 1,
+                       sigmoid: int = 0, want_prob: bool = True, want_u8: bool = True):
+        v = np.ascontiguousarray(vol_u8, dtype=np.uint8)
+        dz, dy, dx = v.shape
+        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch)
+        prob = np.zeros(v.shape, dtype=np.float32) if want_prob else None
+        u8 = np.zeros(v.shape, dtype=np.uint8) if want_u8 else None
+        check(
+            lib().fx_predict_volume(
+                self._h,
+                v.ctypes.data_as(C.POINTER(C.c_uint8)),
+                dz,
+                dy,
+                dx,
+                C.byref(opts),
+                prob.ctypes.data_as(C.POINTER(C.c_float)) if prob is not None else None,
+                u8.ctypes.data_as(C.POINTER(C.c_uint8)) if u8 is not None else None,
+            )
+        )
+        return prob, u8
+
+    def predict_tiles_dev(self, dev_vol_ptr: int, shape, overlap: float, batch: int, tile_begin: int, tile_end: int,
+                          dev_acc_ptr: int, channel: int = 1, sigmoid: int = 0, stream: int | None = None) -> None:
+        dz, dy, dx = shape
+        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch)
+        check(lib().fx_predict_tiles_dev(self._h, dev_vol_ptr, dz, dy, dx, C.byref(opts), tile_begin, tile_end,
+                                         dev_acc_ptr, stream))
+
+
+def default_stream_ptr():
+    """The current torch CUDA stream as a raw pointer (torch is only plumbing here)."""
+    import torch
+
+    return torch.cuda.current_stream().cuda_stream

@@ -1,0 +1,448 @@
+// capi.cu — the extern "C" boundary (include/fenix_b200.h). Statuses map 1:1 to the
+// reference's fenix::Errc; no exception crosses the ABI; messages go to a thread-local
+// last-error string.
+#include "fenix_b200.h"
+#include "fenix_b200/ml/tiling.hpp"
+#include "net.cuh"
+#include "pack.cuh"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <exception>
+#include <memory>
+#include <new>
+#include <string>
+#include <vector>
+
+struct fx_net {
+    fxh::Net net;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+fx_status set_err(const fxh::Status& st) {
+    g_last_error = st.msg;
+    return static_cast<fx_status>(st.code);
+}
+fx_status set_err(int code, const std::string& m) {
+    g_last_error = m;
+    return static_cast<fx_status>(code);
+}
+
+template <class F>
+fx_status guarded(F&& f) {
+    try {
+        g_last_error.clear();
+        return f();
+    } catch (const std::bad_alloc&) {
+        return set_err(FX_INTERNAL, "out of host memory");
+    } catch (const std::exception& e) {
+        return set_err(FX_INTERNAL, std::string("internal error: ") + e.what());
+    } catch (...) {
+        return set_err(FX_INTERNAL, "internal error");
+    }
+}
+
+int sm_count_of_current() {
+    int dev = 0, n = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+bool is_sm100() {
+    int dev = 0, major = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    return major == 10;
+}
+
+// Scoped device allocations for the single-op entry points.
+struct Scratch {
+    std::vector<void*> ptrs;
+    ~Scratch() {
+        for (void* p : ptrs) cudaFree(p);
+    }
+    void* get(size_t bytes) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+        ptrs.push_back(p);
+        return p;
+    }
+};
+
+float device_absmax(const float* x, int64_t n, cudaStream_t s, Scratch& sc) {
+    unsigned* d = static_cast<unsigned*>(sc.get(sizeof(unsigned)));
+    if (!d) return 0.f;
+    cudaMemsetAsync(d, 0, sizeof(unsigned), s);
+    fxk::launch_absmax(x, n, d, s);
+    unsigned bits = 0;
+    cudaMemcpyAsync(&bits, d, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+    cudaStreamSynchronize(s);
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fx_last_error(void) { return g_last_error.c_str(); }
+
+int fx_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+fx_status fx_net_create(const char* path, int patch, int max_batch, fx_precision precision, int device, fx_net** out) {
+    return guarded([&]() -> fx_status {
+        if (!path || !out) return set_err(FX_INVALID_ARGUMENT, "fx_net_create: null argument");
+        *out = nullptr;
+        auto h = std::make_unique<fx_net>();
+        fxh::Status st = h->net.create(path, patch, max_batch, static_cast<int>(precision), device);
+        if (!st.ok()) return set_err(st);
+        *out = h.release();
+        return FX_OK;
+    });
+}
+
+void fx_net_destroy(fx_net* net) { delete net; }
+
+int fx_net_patch(const fx_net* n) { return n ? n->net.patch() : 0; }
+int fx_net_max_batch(const fx_net* n) { return n ? n->net.max_batch() : 0; }
+int fx_net_classes(const fx_net* n) { return n ? n->net.classes() : 0; }
+int fx_net_features(const fx_net* n, int* out, int cap) {
+    if (!n) return 0;
+    const auto& f = n->net.features();
+    for (int i = 0; i < cap && i < static_cast<int>(f.size()); ++i) out[i] = f[i];
+    return static_cast<int>(f.size());
+}
+
+fx_status fx_net_calibrate(fx_net* n, const uint8_t* host_patches, int count) {
+    return guarded([&]() -> fx_status {
+        if (!n || !host_patches) return set_err(FX_INVALID_ARGUMENT, "fx_net_calibrate: null argument");
+        fxh::Status st = n->net.calibrate(host_patches, count);
+        return st.ok() ? FX_OK : set_err(st);
+    });
+}
+
+int fx_net_act_scales(const fx_net* n, float* out, int cap) {
+    if (!n) return 0;
+    auto v = n->net.act_scales();
+    for (int i = 0; i < cap && i < static_cast<int>(v.size()); ++i) out[i] = v[i];
+    return static_cast<int>(v.size());
+}
+
+fx_status fx_net_forward(fx_net* n, const uint8_t* dev_tiles, int nb, float* dev_prob, int channel, int sigmoid,
+                         void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!n || !dev_tiles || !dev_prob) return set_err(FX_INVALID_ARGUMENT, "fx_net_forward: null argument");
+        cudaSetDevice(n->net.device());
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : n->net.stream();
+        const int P = n->net.patch();
+        if (nb < 1 || nb > n->net.max_batch()) return set_err(FX_INVALID_ARGUMENT, "fx_net_forward: batch out of range");
+        if (!sigmoid && (channel < 0 || channel >= n->net.classes()))
+            return set_err(FX_INVALID_ARGUMENT, "fx_net_forward: channel out of range");
+        // The nb tiles are stacked along z: tile b is the volume's z-range [b P, (b+1) P).
+        std::vector<fxk::TileOrigin> org(nb);
+        for (int b = 0; b < nb; ++b) org[b] = {static_cast<int64_t>(b) * P, 0, 0};
+        fxk::TileOrigin* d_org = nullptr;
+        if (cudaMalloc(&d_org, sizeof(fxk::TileOrigin) * nb) != cudaSuccess)
+            return set_err(FX_INTERNAL, "cudaMalloc failed");
+        cudaMemcpyAsync(d_org, org.data(), sizeof(fxk::TileOrigin) * nb, cudaMemcpyHostToDevice, s);
+        fxh::Status st = n->net.forward(dev_tiles, static_cast<int64_t>(nb) * P, P, P, d_org, nb, channel, sigmoid,
+                                        nullptr, dev_prob, false, s);
+        cudaError_t e = cudaStreamSynchronize(s);
+        cudaFree(d_org);
+        if (!st.ok()) return set_err(st);
+        if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "forward"));
+        return FX_OK;
+    });
+}
+
+fx_status fx_predict_tiles_dev(fx_net* n, const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx,
+                               const fx_infer_opts* o, int64_t tile_begin, int64_t tile_end, float* dev_acc,
+                               void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!n || !dev_vol || !o || !dev_acc) return set_err(FX_INVALID_ARGUMENT, "fx_predict_tiles_dev: null argument");
+        if (dz < 1 || dy < 1 || dx < 1) return set_err(FX_INVALID_ARGUMENT, "fx_predict_tiles_dev: empty volume");
+        cudaSetDevice(n->net.device());
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : n->net.stream();
+        fxh::Status st = n->net.predict_tiles(dev_vol, dz, dy, dx, o->patch, o->overlap, o->channel, o->sigmoid,
+                                              o->batch, tile_begin, tile_end, dev_acc, s);
+        return st.ok() ? FX_OK : set_err(st);
+    });
+}
+
+fx_status fx_predict_volume(fx_net* n, const uint8_t* host_vol, int64_t dz, int64_t dy, int64_t dx,
+                            const fx_infer_opts* o, float* host_prob, uint8_t* host_u8) {
+    return guarded([&]() -> fx_status {
+        if (!n || !host_vol || !o) return set_err(FX_INVALID_ARGUMENT, "fx_predict_volume: null argument");
+        if (dz < 1 || dy < 1 || dx < 1) return set_err(FX_INVALID_ARGUMENT, "fx_predict_volume: empty volume");
+        if (o->patch % 64 != 0)  // the reference's own check (src/ml/infer.hpp:459)
+            return set_err(FX_INVALID_ARGUMENT, "patch must be divisible by 64");
+        cudaSetDevice(n->net.device());
+        cudaStream_t s = n->net.stream();
+        const size_t nv = static_cast<size_t>(dz) * dy * dx;
+        Scratch sc;
+        uint8_t* d_vol = static_cast<uint8_t*>(sc.get(nv));
+        float* d_acc = static_cast<float*>(sc.get(nv * sizeof(float)));
+        if (!d_vol || !d_acc) return set_err(FX_INTERNAL, "cudaMalloc: volume buffers");
+        cudaMemcpyAsync(d_vol, host_vol, nv, cudaMemcpyHostToDevice, s);
+        cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
+        fxh::Status st = n->net.predict_tiles(d_vol, dz, dy, dx, o->patch, o->overlap, o->channel, o->sigmoid, o->batch,
+                                              0, -1, d_acc, s);
+        if (!st.ok()) return set_err(st);
+        const int P = o->patch;
+        const auto g = fenix::ml::gaussian1d(P);
+        const auto zs = fenix::ml::tile_starts(dz, P, o->overlap), ys = fenix::ml::tile_starts(dy, P, o->overlap),
+                   xs = fenix::ml::tile_starts(dx, P, o->overlap);
+        const auto Wz = fenix::ml::weight_profile(g, zs, 0, dz, dz, P), Wy = fenix::ml::weight_profile(g, ys, 0, dy, dy, P),
+                   Wx = fenix::ml::weight_profile(g, xs, 0, dx, dx, P);
+        float* d_w = static_cast<float*>(sc.get(sizeof(float) * (dz + dy + dx)));
+        float* d_prob = host_prob ? static_cast<float*>(sc.get(nv * sizeof(float))) : nullptr;
+        uint8_t* d_u8 = host_u8 ? static_cast<uint8_t*>(sc.get(nv)) : nullptr;
+        if (!d_w || (host_prob && !d_prob) || (host_u8 && !d_u8)) return set_err(FX_INTERNAL, "cudaMalloc: outputs");
+        cudaMemcpyAsync(d_w, Wz.data(), sizeof(float) * dz, cudaMemcpyHostToDevice, s);
+        cudaMemcpyAsync(d_w + dz, Wy.data(), sizeof(float) * dy, cudaMemcpyHostToDevice, s);
+        cudaMemcpyAsync(d_w + dz + dy, Wx.data(), sizeof(float) * dx, cudaMemcpyHostToDevice, s);
+        cudaError_t e = fxk::launch_accum_finalize(d_acc, dz, dy, dx, 0, dz, d_w, d_w + dz, d_w + dz + dy, d_prob, d_u8, s);
+        if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "accum_finalize"));
+        if (host_prob) cudaMemcpyAsync(host_prob, d_prob, nv * sizeof(float), cudaMemcpyDeviceToHost, s);
+        if (host_u8) cudaMemcpyAsync(host_u8, d_u8, nv, cudaMemcpyDeviceToHost, s);
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "predict_volume"));
+        return FX_OK;
+    });
+}
+
+int64_t fx_tile_starts(int64_t dim, int patch, double overlap, int64_t* out, int64_t cap) {
+    const auto v = fenix::ml::tile_starts(dim, patch, overlap);
+    for (int64_t i = 0; i < cap && i < static_cast<int64_t>(v.size()); ++i) out[i] = v[static_cast<size_t>(i)];
+    return static_cast<int64_t>(v.size());
+}
+
+void fx_gaussian1d(int n, float* out) {
+    const auto v = fenix::ml::gaussian1d(n);
+    std::copy(v.begin(), v.end(), out);
+}
+
+void fx_weight_profile(const float* g, int patch, const int64_t* starts, int64_t nstarts, int64_t c0, int64_t cn,
+                       int64_t dim, float* out) {
+    std::vector<float> gv(g, g + patch);
+    std::vector<int64_t> sv(starts, starts + nstarts);
+    const auto w = fenix::ml::weight_profile(gv, sv, c0, cn, dim, patch);
+    std::copy(w.begin(), w.end(), out);
+}
+
+fx_status fx_norm_tiles(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx, const int64_t* host_origins,
+                        int ntiles, int patch, float* dev_out, void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!dev_vol || !host_origins || !dev_out || ntiles < 1 || patch < 1)
+            return set_err(FX_INVALID_ARGUMENT, "fx_norm_tiles: bad argument");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Scratch sc;
+        std::vector<fxk::TileOrigin> org(ntiles);
+        for (int i = 0; i < ntiles; ++i) org[i] = {host_origins[3 * i], host_origins[3 * i + 1], host_origins[3 * i + 2]};
+        auto* d_org = static_cast<fxk::TileOrigin*>(sc.get(sizeof(fxk::TileOrigin) * ntiles));
+        auto* d_sums = static_cast<unsigned long long*>(sc.get(sizeof(unsigned long long) * 2 * ntiles));
+        const fxh::ActGeom g{patch, patch, patch};
+        auto* d_l0 = static_cast<uint8_t*>(sc.get(static_cast<size_t>(ntiles) * g.gs()));
+        if (!d_org || !d_sums || !d_l0) return set_err(FX_INTERNAL, "cudaMalloc failed");
+        cudaMemcpyAsync(d_org, org.data(), sizeof(fxk::TileOrigin) * ntiles, cudaMemcpyHostToDevice, s);
+        cudaMemsetAsync(d_sums, 0, sizeof(unsigned long long) * 2 * ntiles, s);
+        cudaError_t e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, s);
+        if (e == cudaSuccess)
+            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, d_l0, g.gs(), dev_out, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles"));
+    });
+}
+
+fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, const float* dev_w, int Cout, int stride,
+                    int fp8, float* dev_y, float* dev_stats, void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!dev_x || !dev_w || !dev_y || B < 1 || Cin < 1 || Cout < 1 || D < 1 || H < 1 || W < 1)
+            return set_err(FX_INVALID_ARGUMENT, "fx_conv3d: bad argument");
+        if (stride != 1 && stride != 2) return set_err(FX_INVALID_ARGUMENT, "fx_conv3d: stride must be 1 or 2");
+        if (stride == 2 && (D % 2 || H % 2 || W % 2)) return set_err(FX_INVALID_ARGUMENT, "fx_conv3d: stride 2 needs even extents");
+        if (Cin == 1 && (stride != 1 || fp8)) return set_err(FX_UNSUPPORTED, "fx_conv3d: 1-channel input is bf16 stride 1");
+        if (Cout % 16) return set_err(FX_UNSUPPORTED, "fx_conv3d: Cout must be a multiple of 16");
+        if (!is_sm100()) return set_err(FX_UNSUPPORTED, "fx_conv3d: needs an sm_100 GPU");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Scratch sc;
+        fxh::Layer L;
+        L.name = "fx_conv3d";
+        L.kind = Cin == 1 ? fxh::Layer::kFirst : fxh::Layer::kConv;
+        L.Cin = Cin;
+        L.Cout = Cout;
+        L.stride = stride;
+        L.w.resize(static_cast<size_t>(Cout) * Cin * 27);
+        cudaMemcpyAsync(L.w.data(), dev_w, L.w.size() * sizeof(float), cudaMemcpyDeviceToHost, s);
+        cudaStreamSynchronize(s);
+        const int q = fp8 ? 1 : 0;
+        const int cg = q ? 16 : 8;
+        if (Cin > 1 && Cin % (2 * cg)) return set_err(FX_UNSUPPORTED, "fx_conv3d: Cin must be a multiple of 16 (bf16) / 32 (fp8)");
+        const fxh::ActGeom gin{D, H, W};
+        const fxh::ActGeom gout{D / stride, H / stride, W / stride};
+        const int64_t vin = static_cast<int64_t>(D) * H * W;
+        if (q) L.in_scale = std::max(device_absmax(dev_x, vin * B * Cin, s, sc), 1e-8f) / 448.f;
+        std::vector<void*> allocs;
+        struct Free {
+            std::vector<void*>& a;
+            ~Free() {
+                for (void* p : a) cudaFree(p);
+            }
+        } fr{allocs};
+        fxh::Status st = fxh::build_layer_program(L, q, gin, gout, B, sm_count_of_current(), allocs);
+        if (!st.ok()) return set_err(st);
+        // input in the kernel's layout
+        uint8_t* in;
+        int64_t ibs, igs;
+        if (L.kind == fxh::Layer::kFirst) {
+            igs = gin.gs();
+            ibs = igs;
+            in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * ibs));
+            if (!in) return set_err(FX_INTERNAL, "cudaMalloc failed");
+            cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
+            fxk::launch_pack_first(dev_x, B, D, H, W, in, ibs, s);
+        } else if (stride == 1) {
+            igs = gin.gs();
+            ibs = (Cin / cg) * igs;
+            in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * ibs));
+            if (!in) return set_err(FX_INTERNAL, "cudaMalloc failed");
+            cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
+            fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, q ? 1.f / L.in_scale : 1.f, 0, 0, 0, 0, s);
+        } else {
+            const int64_t ps = gout.gs();
+            igs = 8 * ps;
+            ibs = (Cin / cg) * igs;
+            in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * ibs));
+            if (!in) return set_err(FX_INTERNAL, "cudaMalloc failed");
+            cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
+            fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, q ? 1.f / L.in_scale : 1.f, 1, gout.H + 2,
+                             gout.W + 2, ps, s);
+        }
+        const int64_t ogs = gout.gs(), obs = (Cout / 8) * ogs;
+        auto* out = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * obs));
+        const int64_t rows = static_cast<int64_t>(gout.D) * (gout.H + 2) * (gout.W + 2);
+        const int64_t nrec = ((rows + 127) / 128) * 4;
+        L.d_partials = static_cast<float*>(sc.get(sizeof(float) * B * nrec * Cout * 2));
+        auto* d_status = static_cast<uint32_t*>(sc.get(sizeof(uint32_t)));
+        if (!out || !L.d_partials || !d_status) return set_err(FX_INTERNAL, "cudaMalloc failed");
+        cudaMemsetAsync(out, 0, static_cast<size_t>(B) * obs, s);
+        cudaMemsetAsync(d_status, 0, sizeof(uint32_t), s);
+        st = fxh::launch_layer(L, q, gin, gout, in, ibs, igs, out, obs, ogs, 0, 1.f, nullptr, B, sm_count_of_current(),
+                               d_status, s);
+        if (!st.ok()) return set_err(st);
+        fxk::launch_unpack(out, obs, ogs, 0, 1.f, B, Cout, gout.D, gout.H, gout.W, dev_y, s);
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "fx_conv3d"));
+        uint32_t status = 0;
+        cudaMemcpy(&status, d_status, 4, cudaMemcpyDeviceToHost);
+        if (status) return set_err(FX_INTERNAL, "fx_conv3d: device status " + std::to_string(status));
+        if (dev_stats) {
+            std::vector<float> part(static_cast<size_t>(B) * L.nrec * Cout * 2);
+            cudaMemcpy(part.data(), L.d_partials, part.size() * sizeof(float), cudaMemcpyDeviceToHost);
+            std::vector<float> res(static_cast<size_t>(B) * Cout * 2);
+            const double cnt = static_cast<double>(gout.D) * gout.H * gout.W;
+            for (int b = 0; b < B; ++b)
+                for (int c = 0; c < Cout; ++c) {
+                    double a1 = 0, a2 = 0;
+                    for (int r = 0; r < L.nrec; ++r) {
+                        a1 += part[((static_cast<size_t>(b) * L.nrec + r) * Cout + c) * 2];
+                        a2 += part[((static_cast<size_t>(b) * L.nrec + r) * Cout + c) * 2 + 1];
+                    }
+                    const double m = a1 / cnt;
+                    res[(static_cast<size_t>(b) * Cout + c) * 2] = static_cast<float>(m);
+                    res[(static_cast<size_t>(b) * Cout + c) * 2 + 1] = static_cast<float>(a2 / cnt - m * m);
+                }
+            cudaMemcpy(dev_stats, res.data(), res.size() * sizeof(float), cudaMemcpyHostToDevice);
+        }
+        return FX_OK;
+    });
+}
+
+fx_status fx_conv_transpose2(const float* dev_x, int B, int Cin, int D, int H, int W, const float* dev_w,
+                             const float* dev_bias, int Cout, int fp8, float* dev_y, void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!dev_x || !dev_w || !dev_bias || !dev_y || B < 1 || Cin < 1 || Cout < 1 || D < 1 || H < 1 || W < 1)
+            return set_err(FX_INVALID_ARGUMENT, "fx_conv_transpose2: bad argument");
+        if (!is_sm100()) return set_err(FX_UNSUPPORTED, "fx_conv_transpose2: needs an sm_100 GPU");
+        const int q = fp8 ? 1 : 0;
+        const int cg = q ? 16 : 8;
+        if (Cin % (2 * cg) || Cout % 16)
+            return set_err(FX_UNSUPPORTED, "fx_conv_transpose2: channel counts not supported");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Scratch sc;
+        fxh::Layer L;
+        L.name = "fx_conv_transpose2";
+        L.kind = fxh::Layer::kUp;
+        L.Cin = Cin;
+        L.Cout = Cout;
+        L.stride = 2;
+        L.w.resize(static_cast<size_t>(Cin) * Cout * 8);
+        L.b.resize(Cout);
+        cudaMemcpyAsync(L.w.data(), dev_w, L.w.size() * sizeof(float), cudaMemcpyDeviceToHost, s);
+        cudaMemcpyAsync(L.b.data(), dev_bias, L.b.size() * sizeof(float), cudaMemcpyDeviceToHost, s);
+        cudaStreamSynchronize(s);
+        const fxh::ActGeom gin{D, H, W}, gout{2 * D, 2 * H, 2 * W};
+        const int64_t vin = static_cast<int64_t>(D) * H * W;
+        if (q) L.in_scale = std::max(device_absmax(dev_x, vin * B * Cin, s, sc), 1e-8f) / 448.f;
+        std::vector<void*> allocs;
+        struct Free {
+            std::vector<void*>& a;
+            ~Free() {
+                for (void* p : a) cudaFree(p);
+            }
+        } fr{allocs};
+        fxh::Status st = fxh::build_layer_program(L, q, gin, gout, B, sm_count_of_current(), allocs);
+        if (!st.ok()) return set_err(st);
+        const int64_t igs = gin.gs(), ibs = (Cin / cg) * igs;
+        const int64_t ogs = gout.gs(), obs = (Cout / 8) * ogs;  // output cells are bf16 here
+        auto* in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * ibs));
+        auto* out = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * obs));
+        auto* d_status = static_cast<uint32_t*>(sc.get(sizeof(uint32_t)));
+        auto* d_amax = static_cast<unsigned*>(sc.get(sizeof(unsigned)));
+        if (!in || !out || !d_status || !d_amax) return set_err(FX_INTERNAL, "cudaMalloc failed");
+        cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
+        cudaMemsetAsync(out, 0, static_cast<size_t>(B) * obs, s);
+        cudaMemsetAsync(d_status, 0, sizeof(uint32_t), s);
+        fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, q ? 1.f / L.in_scale : 1.f, 0, 0, 0, 0, s);
+        // fp8 output: scale from a bf16 dry run would need two passes; the test entry point
+        // writes bf16 output in both modes (operands still e4m3 when fp8).
+        st = fxh::launch_layer(L, q, gin, gout, in, ibs, igs, out, obs, ogs, 0, 1.f, d_amax, B, sm_count_of_current(),
+                               d_status, s);
+        if (!st.ok()) return set_err(st);
+        fxk::launch_unpack(out, obs, ogs, 0, 1.f, B, Cout, gout.D, gout.H, gout.W, dev_y, s);
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "fx_conv_transpose2"));
+        uint32_t status = 0;
+        cudaMemcpy(&status, d_status, 4, cudaMemcpyDeviceToHost);
+        if (status) return set_err(FX_INTERNAL, "fx_conv_transpose2: device status " + std::to_string(status));
+        return FX_OK;
+    });
+}
+
+fx_status fx_accum_finalize(const float* dev_acc, int64_t dz, int64_t dy, int64_t dx, int64_t z_begin, int64_t z_end,
+                            const float* dev_wz, const float* dev_wy, const float* dev_wx, float* dev_prob,
+                            uint8_t* dev_u8, void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!dev_acc || !dev_wz || !dev_wy || !dev_wx || z_begin < 0 || z_end > dz || z_begin > z_end)
+            return set_err(FX_INVALID_ARGUMENT, "fx_accum_finalize: bad argument");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        cudaError_t e =
+            fxk::launch_accum_finalize(dev_acc, dz, dy, dx, z_begin, z_end, dev_wz, dev_wy, dev_wx, dev_prob, dev_u8, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_accum_finalize"));
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// conv_tc.cuh — the one tensor-core kernel behind every convolution of the UNet forward
+// (3x3x3 stride 1, 3x3x3 stride 2, the 1-channel first layer, and the 2x2x2 stride-2
+// transposed conv).
+//
+// Activation layout ("padded group planes"): a tensor of C channels over D x H x W voxels is
+// stored as [batch][group][D+2][H+2][W+2][16 bytes], one group = 16 bytes of channels
+// (8 bf16 or 16 e4m3), with a one-voxel zero border. Flattening (z, y, x) of one group gives a
+// 1-D array of 16-byte "rows"; a 3x3x3 stride-1 conv is then a sum over 27 row shifts, and the
+// A operand of every tap is a contiguous run of rows. The tcgen05 K-major no-swizzle smem
+// layout keeps rows 16 B apart (SBO = 128 B), so a tap's A tile is just a descriptor whose start
+// address is shifted by (tap offset x 16 B) inside one staged window — no im2col and no halo
+// bookkeeping in the kernel. Stride-2 convs read a phase-split copy of their input (8 parity
+// sub-volumes with the output's padded geometry), which turns the strided taps into row
+// shifts as well.
+//
+// The host compiles each layer into a small "program": a list of pipeline stages (one bulk
+// copy of a window of rows for a range of groups + the matching packed weight block) and, per
+// stage, the list of MMAs (A offset, K-half stride, B offset). The kernel is persistent and
+// warp specialised: warp 0 issues the bulk copies, warp 1 issues tcgen05.mma from one thread
+// and owns the TMEM allocation, warps 2..5 drain the TMEM accumulators (epilogue).
+#pragma once
+
+#include <cstdint>
+
+namespace fxk {
+
+constexpr int kConvThreads = 192;
+constexpr int kMaxSrc = 8;
+
+struct ConvStage {
+    int32_t src;        // source array index
+    int32_t row_off;    // first window row relative to the unit's first output row
+    int32_t rows;       // window length in rows
+    int32_t g0, ng;     // group range copied
+    int32_t b_off;      // byte offset of the packed B block (within one N tile's weights)
+    int32_t b_bytes;
+    int32_t mma_begin, mma_count;
+};
+
+struct ConvMma {
+    int32_t a_off;  // byte offset inside the stage's A buffer for M-block 0
+    int32_t lbo;    // byte distance between the two K-halves of this MMA's A operand
+    int32_t b_off;  // byte offset inside the stage's B buffer
+};
+
+struct ConvSrc {
+    const uint8_t* ptr;    // row 0 of group 0 of batch item 0
+    int64_t batch_stride;  // bytes
+    int64_t group_stride;  // bytes
+    int64_t rows;          // rows that exist per (batch, group)
+};
+
+enum ConvMode : int32_t {
+    kModePrenorm = 0,  // store bf16 pre-norm output, emit per-channel sum / sum of squares
+    kModeUpsample = 1, // transposed conv: + bias, scatter 8 phases into the 2x finer grid
+};
+
+struct ConvParams {
+    ConvSrc src[kMaxSrc];
+    const ConvStage* stages;
+    const ConvMma* mmas;
+    const uint8_t* wpack;  // packed B blocks of N tile 0; tile t starts at + t * wtile_bytes
+    int64_t wtile_bytes;
+    int32_t n_stages;
+    int32_t fp8;  // operands are e4m3 (kind::f8f6f4) instead of bf16 (kind::f16)
+
+    // output-row space of one batch item: the padded geometry rows are indexed in
+    int32_t batch;
+    int32_t Dp, Hp, Wp;          // padded extents of the row space
+    int64_t row_begin, row_end;  // rows computed per batch item
+    int32_t R;                   // 128-row M blocks per work unit
+    int32_t n_units_m;           // ceil((row_end - row_begin) / (128 R))
+    int32_t n_tiles;             // N tiles
+    int32_t N_tile;              // accumulator columns per tile (multiple of 16)
+    int32_t acc_slots;           // accumulator buffers in TMEM (1 or 2)
+    uint32_t tmem_cols;          // power of two >= acc_slots * R * N_tile
+    int32_t n_pipe;              // smem pipeline depth
+    int32_t stage_bytes;         // bytes per pipeline stage
+    int32_t stage_a_bytes;       // B block offset within a stage
+
+    // epilogue
+    int32_t mode;
+    const float* col_scale;  // per output channel multiplier (fp8 dequant) or null
+    const float* bias;       // per output channel bias (upsample mode) or null
+    uint8_t* out;            // output tensor, group 0 of the written channel slice, batch 0
+    int64_t out_batch_stride, out_group_stride;  // bytes
+    int32_t out_fp8;         // upsample mode: write e4m3 (scaled by out_qscale) instead of bf16
+    float out_qscale;
+    int32_t cout;            // upsample mode: channels per phase
+    int32_t oHp, oWp;        // upsample mode: padded H, W of the output grid
+    unsigned* amax;          // upsample mode: max |output| (float bits) when non-null
+    float* stats;            // prenorm mode: [batch][n_units_m][4][C][2] partial sums
+    int32_t stats_C;         // channels per stats record (= n_tiles * N_tile)
+    uint32_t* status;
+};
+
+}  // namespace fxk

@@ -1,0 +1,85 @@
+// eltwise.cuh — the HBM-bound kernels around the convolutions: per-tile z-score normalise of
+// the gathered u8 patch, InstanceNorm statistics finalise, normalise + LeakyReLU + requantise
+// into the consumers' layouts, the fused 1x1x1 head + softmax/sigmoid + Gaussian blend, and the
+// accumulator -> probability / u8 finalise.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace fxk {
+
+// A view of one tensor in the padded group-plane layout (see conv_tc.cuh).
+struct GridGeom {
+    int32_t D, H, W;  // interior extents; padded extents are +2
+};
+
+struct TileOrigin {
+    int64_t z0, y0, x0;
+};
+
+// ---- tiler ----------------------------------------------------------------------------------
+// Integer sum and sum of squares of every tile's P^3 u8 voxels (edge-clamped reads), into
+// sums[2*b + {0,1}] (exact; the caller zeroes `sums`).
+cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
+                             int ntiles, int P, unsigned long long* sums, cudaStream_t s);
+// Writes the first conv's input for every tile: each interior voxel's 16-byte cell holds the
+// z-scored values at x-1, x, x+1 (zero outside the tile) as bf16, then five zeros. The z-score
+// goes through a 256-entry table built with the reference's double-precision expression, so
+// the normalised value of each u8 level is the same float the reference computes.
+cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
+                             int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
+                             float* f32_out, cudaStream_t s);
+
+// ---- InstanceNorm ----------------------------------------------------------------------------
+// partials [B][nrec][C][2] -> ss [B][C][2] = {scale, shift} with scale = gamma * rstd and
+// shift = beta - mean * scale over `count` voxels.
+cudaError_t launch_in_finalize(const float* partials, int B, int nrec, int C, double count, const float* gamma,
+                               const float* beta, float eps, float* ss, cudaStream_t s);
+
+struct NormDest {
+    uint8_t* ptr;          // group 0 of the written slice, batch 0 (null = unused)
+    int64_t batch_stride;  // bytes
+    int64_t group_stride;  // bytes
+    int32_t fp8;           // 1: e4m3 scaled by qscale, 0: bf16
+    float qscale;
+    int32_t phase;         // 1: write the stride-2 phase-split copy (8 parity sub-volumes)
+    int32_t pHp, pWp;      // phase sub-volume padded H, W (= output grid of the stride-2 conv)
+    int64_t phase_stride;  // bytes between parity sub-volumes
+};
+
+// y = leaky_relu(x * scale[c] + shift[c], slope) over the interior of a bf16 pre-norm tensor,
+// written to up to two destinations; optionally records max |y| into *amax (float bits).
+cudaError_t launch_norm_act(const uint8_t* pre, int64_t pre_batch_stride, int64_t pre_group_stride, GridGeom g,
+                            int C, int B, const float* ss, float slope, NormDest d0, NormDest d1, unsigned* amax,
+                            cudaStream_t s);
+
+// Last decoder layer: normalise + LeakyReLU, 1x1x1 head (ncls <= 2), softmax channel `channel`
+// (or sigmoid of channel 0), NaN -> 0 / +inf -> 1, then Gaussian-blend into the volume
+// accumulator at each tile's origin (acc may be null) and/or store the tile probability
+// (prob may be null, [B][P^3] f32).
+struct HeadParams {
+    const uint8_t* pre;
+    int64_t pre_batch_stride, pre_group_stride;
+    int32_t P, C, B, ncls, channel, sigmoid;
+    const float* ss;     // [B][C][2]
+    float slope;
+    const float* wh;     // [ncls][C]
+    const float* bh;     // [ncls]
+    const float* gauss;  // [P] gaussian1d(P)
+    const TileOrigin* tiles;
+    float* acc;          // [dz][dy][dx] accumulator or null
+    int64_t dz, dy, dx;
+    float* prob;         // [B][P^3] or null
+};
+cudaError_t launch_head_blend(const HeadParams& h, cudaStream_t s);
+
+// acc / (Wz[z]*Wy[y]*Wx[x]) where the weight is > 0 (the reference's normalize), then
+// u8 = (u8)(clamp(p, 0, 1) * 255 + 0.5). Either output may be null. Rows [z_begin, z_end).
+cudaError_t launch_accum_finalize(const float* acc, int64_t dz, int64_t dy, int64_t dx, int64_t z_begin,
+                                  int64_t z_end, const float* Wz, const float* Wy, const float* Wx, float* prob,
+                                  uint8_t* u8, cudaStream_t s);
+
+cudaError_t launch_zero(void* p, size_t bytes, cudaStream_t s);
+
+}  // namespace fxk

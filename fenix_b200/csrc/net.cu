@@ -1,0 +1,694 @@
+// net.cu — plain 3D UNet on the tcgen05 conv kernel + sliding-window driver (see net.cuh).
+#include "net.cuh"
+#include "pack.cuh"
+#include "fenix_b200/ml/tiling.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+
+namespace fxk {
+cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cudaStream_t stream);
+}
+
+namespace fxh {
+
+using fenix::ml::gaussian1d;
+using fenix::ml::tile_starts;
+
+namespace {
+constexpr float kE4M3Max = 448.f;
+constexpr float kSlope = 0.01f;  // LeakyReLU negative slope (resenc_unet.hpp:49)
+constexpr float kEps = 1e-5f;    // InstanceNorm3d eps (resenc_unet.hpp:44)
+
+template <class T>
+Status upload(T*& dst, const std::vector<T>& v, Net* /*unused*/, std::vector<void*>& allocs) {
+    if (v.empty()) {
+        dst = nullptr;
+        return ok();
+    }
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, v.size() * sizeof(T));
+    if (e != cudaSuccess) return cuda_status(e, "cudaMalloc");
+    allocs.push_back(p);
+    e = cudaMemcpy(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_status(e, "cudaMemcpy");
+    dst = static_cast<T*>(p);
+    return ok();
+}
+}  // namespace
+
+Status cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return ok();
+    return fail(kInternal, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+Net::~Net() {
+    if (dev_ >= 0) cudaSetDevice(dev_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (void* p : allocs_) cudaFree(p);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void* Net::dalloc(size_t bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    allocs_.push_back(p);
+    return p;
+}
+
+// ---- weights -> layer plans ------------------------------------------------------------------
+Status Net::parse(const WeightMap& wm) {
+    auto get = [&](const std::string& n) -> const HostTensor* {
+        auto it = wm.find(n);
+        return it == wm.end() ? nullptr : &it->second;
+    };
+    // encoder.stages.{s}.convs.{i}.conv.weight
+    S_ = 0;
+    while (get("encoder.stages." + std::to_string(S_) + ".convs.0.conv.weight")) ++S_;
+    if (S_ < 2) return fail(kDecode, "fxweights: expected >= 2 encoder stages (encoder.stages.{s}.convs.{i}.conv.weight)");
+    nconv_ = 0;
+    while (get("encoder.stages.0.convs." + std::to_string(nconv_) + ".conv.weight")) ++nconv_;
+    if (nconv_ < 1) return fail(kDecode, "fxweights: no convs in encoder stage 0");
+    F_.clear();
+    auto conv_layer = [&](const std::string& pre, Layer& L) -> Status {
+        const HostTensor* w = get(pre + ".conv.weight");
+        const HostTensor* g = get(pre + ".norm.weight");
+        const HostTensor* b = get(pre + ".norm.bias");
+        if (!w || !g || !b) return fail(kDecode, "fxweights: missing " + pre + ".{conv.weight,norm.weight,norm.bias}");
+        if (w->shape.size() != 5 || w->shape[2] != 3 || w->shape[3] != 3 || w->shape[4] != 3)
+            return fail(kUnsupported, "fxweights: " + pre + " must be a 3x3x3 conv");
+        L.Cout = static_cast<int>(w->shape[0]);
+        L.Cin = static_cast<int>(w->shape[1]);
+        L.w = w->data;
+        L.gamma = g->data;
+        L.beta = b->data;
+        L.name = pre;
+        return ok();
+    };
+    enc_.assign(static_cast<size_t>(S_) * nconv_, Layer{});
+    int prev = 1;
+    for (int s = 0; s < S_; ++s)
+        for (int i = 0; i < nconv_; ++i) {
+            Layer& L = enc_[s * nconv_ + i];
+            Status st = conv_layer("encoder.stages." + std::to_string(s) + ".convs." + std::to_string(i), L);
+            if (!st.ok()) return st;
+            if (L.Cin != (i == 0 ? prev : L.Cout)) return fail(kDecode, "fxweights: channel mismatch at " + L.name);
+            L.stride = (i == 0 && s > 0) ? 2 : 1;
+            L.kind = (s == 0 && i == 0) ? Layer::kFirst : Layer::kConv;
+            L.lin = (i == 0 && s > 0) ? s - 1 : s;
+            L.lout = s;
+            if (i == 0) F_.push_back(L.Cout);
+            prev = L.Cout;
+        }
+    if (F_[0] < 1 || enc_[0].Cin != 1) return fail(kUnsupported, "net: the first conv must take 1 input channel");
+    up_.assign(S_ - 1, Layer{});
+    dec_.assign(static_cast<size_t>(S_ - 1) * nconv_, Layer{});
+    for (int t = 0; t < S_ - 1; ++t) {
+        const int lvl = S_ - 2 - t;
+        const std::string tp = "decoder.transpconvs." + std::to_string(t);
+        const HostTensor* w = get(tp + ".weight");
+        const HostTensor* b = get(tp + ".bias");
+        if (!w || !b) return fail(kDecode, "fxweights: missing " + tp + ".{weight,bias}");
+        if (w->shape.size() != 5 || w->shape[2] != 2 || w->shape[3] != 2 || w->shape[4] != 2)
+            return fail(kUnsupported, "fxweights: " + tp + " must be a 2x2x2 transposed conv");
+        Layer& U = up_[lvl];
+        U.kind = Layer::kUp;
+        U.name = tp;
+        U.Cin = static_cast<int>(w->shape[0]);
+        U.Cout = static_cast<int>(w->shape[1]);
+        if (U.Cin != F_[lvl + 1] || U.Cout != F_[lvl]) return fail(kDecode, "fxweights: channel mismatch at " + tp);
+        U.w = w->data;
+        U.b = b->data;
+        U.stride = 2;
+        U.lin = lvl + 1;
+        U.lout = lvl;
+        for (int i = 0; i < nconv_; ++i) {
+            Layer& L = dec_[lvl * nconv_ + i];
+            Status st = conv_layer("decoder.stages." + std::to_string(t) + ".convs." + std::to_string(i), L);
+            if (!st.ok()) return st;
+            if (L.Cout != F_[lvl] || L.Cin != (i == 0 ? 2 * F_[lvl] : F_[lvl]))
+                return fail(kDecode, "fxweights: channel mismatch at " + L.name);
+            L.lin = L.lout = lvl;
+        }
+    }
+    const std::string sl = "decoder.seg_layers." + std::to_string(S_ - 2);
+    const HostTensor* hw = get(sl + ".weight");
+    const HostTensor* hb = get(sl + ".bias");
+    if (!hw || !hb) return fail(kDecode, "fxweights: missing " + sl + ".{weight,bias}");
+    ncls_ = static_cast<int>(hw->shape[0]);
+    if (hw->shape[1] != F_[0] || ncls_ < 1 || ncls_ > 2) return fail(kUnsupported, "net: head must map F0 -> 1 or 2 classes");
+    head_w_ = hw->data;
+    head_b_ = hb->data;
+    return ok();
+}
+
+// ---- layer program construction -------------------------------------------------------------
+Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax, int sm_count,
+                           std::vector<void*>& allocs_) {
+    DevProgram& dp = L.prog[q];
+    ProgramSpec sp;
+    const bool fp8 = q == 1;
+    sp.elem = fp8 ? 1 : 2;
+    sp.cg = fp8 ? 16 : 8;
+    const int Bmax_ = Bmax, sm_count_ = sm_count;
+    Net* this_net = nullptr;
+    if (fp8 && L.wscale.empty()) {
+        // per-output-channel weight scale amax/448 (tools/ml-export/fp8_conv3d_op.py:1494-1504)
+        L.wscale.assign(L.Cout, 1.f);
+        if (L.kind == Layer::kUp) {
+            for (int co = 0; co < L.Cout; ++co) {
+                float m = 0.f;
+                for (int ci = 0; ci < L.Cin; ++ci)
+                    for (int a = 0; a < 8; ++a) m = std::max(m, std::fabs(L.w[(static_cast<size_t>(ci) * L.Cout + co) * 8 + a]));
+                L.wscale[co] = std::max(m, 1e-8f) / kE4M3Max;
+            }
+        } else {
+            const size_t per = static_cast<size_t>(L.Cin) * 27;
+            for (int co = 0; co < L.Cout; ++co) {
+                float m = 0.f;
+                for (size_t k = 0; k < per; ++k) m = std::max(m, std::fabs(L.w[co * per + k]));
+                L.wscale[co] = std::max(m, 1e-8f) / kE4M3Max;
+            }
+        }
+    }
+    std::vector<float> colscale;
+    if (L.kind == Layer::kFirst) {
+        if (fp8) return fail(kInternal, "first layer runs in bf16");
+        sp.G = 1;
+        sp.pair_taps = true;
+        const ActGeom g = gout;
+        const int64_t Wp = g.W + 2, P2 = static_cast<int64_t>(g.H + 2) * Wp;
+        for (int kz = 0; kz < 3; ++kz)
+            for (int ky = 0; ky < 3; ++ky) sp.taps.push_back({0, (kz - 1) * P2 + (ky - 1) * Wp, kz * 3 + ky, kz});
+        const Layer* Lp = &L;
+        sp.wval = [Lp](int n, int j, int wk) { return j < 3 ? Lp->w[static_cast<size_t>(n) * 27 + wk * 3 + j] : 0.f; };
+        sp.N_total = L.Cout;
+        dp.rowspace = gout;
+    } else if (L.kind == Layer::kConv) {
+        if (L.Cin % sp.cg) return fail(kUnsupported, L.name + ": input channels must be a multiple of " + std::to_string(sp.cg));
+        sp.G = L.Cin / sp.cg;
+        if (L.stride == 1) {
+            const int64_t Wp = gin.W + 2, P2 = static_cast<int64_t>(gin.H + 2) * Wp;
+            for (int kz = 0; kz < 3; ++kz)
+                for (int ky = 0; ky < 3; ++ky)
+                    for (int kx = 0; kx < 3; ++kx)
+                        sp.taps.push_back({0, (kz - 1) * P2 + (ky - 1) * Wp + (kx - 1), kz * 9 + ky * 3 + kx, kz});
+        } else {
+            const int64_t Wp = gout.W + 2, P2 = static_cast<int64_t>(gout.H + 2) * Wp;
+            for (int kz = 0; kz < 3; ++kz)
+                for (int ky = 0; ky < 3; ++ky)
+                    for (int kx = 0; kx < 3; ++kx) {
+                        const int phi = ((kz & 1) << 2) | ((ky & 1) << 1) | (kx & 1);
+                        const int64_t off = (kz / 2 - 1) * P2 + (ky / 2 - 1) * Wp + (kx / 2 - 1);
+                        sp.taps.push_back({phi, off, kz * 9 + ky * 3 + kx, phi * 2 + kz / 2});
+                    }
+        }
+        const Layer* Lp = &L;
+        const bool f8 = fp8;
+        sp.wval = [Lp, f8](int n, int ci, int wk) {
+            if (ci >= Lp->Cin) return 0.f;
+            const float v = Lp->w[(static_cast<size_t>(n) * Lp->Cin + ci) * 27 + wk];
+            return f8 ? v / Lp->wscale[n] : v;
+        };
+        sp.N_total = L.Cout;
+        dp.rowspace = gout;
+        if (fp8) {
+            colscale.resize(L.Cout);
+            for (int co = 0; co < L.Cout; ++co) colscale[co] = L.in_scale * L.wscale[co];
+        }
+    } else {  // kUp
+        if (L.Cin % sp.cg) return fail(kUnsupported, L.name + ": input channels must be a multiple of " + std::to_string(sp.cg));
+        sp.G = L.Cin / sp.cg;
+        sp.taps.push_back({0, 0, 0, 0});
+        const Layer* Lp = &L;
+        const bool f8 = fp8;
+        sp.wval = [Lp, f8](int n, int ci, int) {
+            if (ci >= Lp->Cin) return 0.f;
+            const int co = n % Lp->Cout, a = n / Lp->Cout;
+            const float v = Lp->w[(static_cast<size_t>(ci) * Lp->Cout + co) * 8 + a];
+            return f8 ? v / Lp->wscale[co] : v;
+        };
+        sp.N_total = 8 * L.Cout;
+        dp.rowspace = gin;
+        if (fp8) {
+            colscale.resize(L.Cout);
+            for (int co = 0; co < L.Cout; ++co) colscale[co] = L.in_scale * L.wscale[co];
+        }
+    }
+    // tiling of N and M
+    const int N_total = sp.N_total;
+    int N_tile = N_total <= 256 ? N_total : (N_total == 320 ? 320 : 256);
+    if (N_total % N_tile) return fail(kUnsupported, L.name + ": output width " + std::to_string(N_total) + " not tileable");
+    int R = N_tile <= 64 ? 4 : (N_tile <= 128 ? 2 : 1);
+    const ActGeom& rs = dp.rowspace;
+    const int64_t rows = static_cast<int64_t>(rs.D) * (rs.H + 2) * (rs.W + 2);
+    auto units = [&](int r) { return ((rows + 128 * r - 1) / (128 * r)) * Bmax_ * (N_total / N_tile); };
+    while (R > 1 && units(R) < 2 * sm_count_) R /= 2;
+    const int slots = R * N_tile <= 256 ? 2 : 1;
+    uint32_t cols = 32;
+    while (cols < static_cast<uint32_t>(slots * R * N_tile)) cols <<= 1;
+    if (cols > 512) return fail(kInternal, L.name + ": accumulator does not fit in TMEM");
+    sp.N_tile = N_tile;
+    sp.R = R;
+    Status st;
+    {
+        std::string err = build_program(sp, dp.host);
+        if (!err.empty()) return fail(kInternal, L.name + ": " + err);
+    }
+    dp.R = R;
+    dp.N_tile = N_tile;
+    dp.acc_slots = slots;
+    dp.tmem_cols = cols;
+    dp.n_units_m = static_cast<int>((rows + 128 * R - 1) / (128 * R));
+    dp.fp8 = fp8;
+    if ((st = upload(dp.stages, dp.host.stages, this_net, allocs_)).code) return st;
+    if ((st = upload(dp.mmas, dp.host.mmas, this_net, allocs_)).code) return st;
+    if ((st = upload(dp.wpack, dp.host.wpack, this_net, allocs_)).code) return st;
+    if ((st = upload(dp.colscale, colscale, this_net, allocs_)).code) return st;
+    if (L.kind == Layer::kUp && (st = upload(dp.bias, L.b, this_net, allocs_)).code) return st;
+    dp.built = true;
+    return ok();
+}
+
+Status Net::build_layer(Layer& L, int q) {
+    Status st = build_layer_program(L, q, level(L.lin), level(L.lout), Bmax_, sm_count_, allocs_);
+    if (!st.ok()) return st;
+    // statistics buffers (shared by both precisions): one record per 128-row block and warp
+    if (L.kind != Layer::kUp && !L.d_partials) {
+        const ActGeom g = level(L.lout);
+        const int64_t rows = static_cast<int64_t>(g.D) * (g.H + 2) * (g.W + 2);
+        const int64_t nrec_max = ((rows + 127) / 128) * 4;
+        L.d_partials = static_cast<float*>(dalloc(sizeof(float) * Bmax_ * nrec_max * L.Cout * 2));
+        L.d_ss = static_cast<float*>(dalloc(sizeof(float) * Bmax_ * L.Cout * 2));
+        if (!L.d_partials || !L.d_ss) return fail(kInternal, "cudaMalloc: stats buffers");
+        if ((st = upload(L.d_gamma, L.gamma, this, allocs_)).code) return st;
+        if ((st = upload(L.d_beta, L.beta, this, allocs_)).code) return st;
+    }
+    return ok();
+}
+
+Status Net::alloc() {
+    const ActGeom g0 = level(0);
+    l0_ = static_cast<uint8_t*>(dalloc(static_cast<size_t>(Bmax_) * g0.gs()));
+    if (!l0_) return fail(kInternal, "cudaMalloc: first-layer input");
+    cudaMemset(l0_, 0, static_cast<size_t>(Bmax_) * g0.gs());
+    pn_.assign(S_, nullptr);
+    act_.assign(S_, nullptr);
+    cat_.assign(S_, nullptr);
+    ph_.assign(S_, nullptr);
+    for (int s = 0; s < S_; ++s) {
+        const ActGeom g = level(s);
+        const size_t bytes = static_cast<size_t>(Bmax_) * (F_[s] / 8) * g.gs();
+        pn_[s] = static_cast<uint8_t*>(dalloc(bytes));
+        act_[s] = static_cast<uint8_t*>(dalloc(bytes));
+        if (!pn_[s] || !act_[s]) return fail(kInternal, "cudaMalloc: activations");
+        cudaMemset(act_[s], 0, bytes);
+        if (s < S_ - 1) {
+            cat_[s] = static_cast<uint8_t*>(dalloc(2 * bytes));
+            const ActGeom gn = level(s + 1);
+            const size_t pbytes = static_cast<size_t>(Bmax_) * (F_[s] / 8) * 8 * gn.gs();
+            ph_[s] = static_cast<uint8_t*>(dalloc(pbytes));
+            if (!cat_[s] || !ph_[s]) return fail(kInternal, "cudaMalloc: skip buffers");
+            cudaMemset(cat_[s], 0, 2 * bytes);
+            cudaMemset(ph_[s], 0, pbytes);
+        }
+    }
+    d_sums_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * 2 * Bmax_));
+    d_amax_ = static_cast<unsigned*>(dalloc(sizeof(unsigned) * 5 * S_));
+    d_status_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t)));
+    if (!d_sums_ || !d_amax_ || !d_status_) return fail(kInternal, "cudaMalloc: control buffers");
+    cudaMemset(d_status_, 0, sizeof(uint32_t));
+    std::vector<float> g = gaussian1d(P_);
+    Status st = upload(d_gauss_, g, this, allocs_);
+    if (!st.ok()) return st;
+    if ((st = upload(d_head_w_, head_w_, this, allocs_)).code) return st;
+    if ((st = upload(d_head_b_, head_b_, this, allocs_)).code) return st;
+    return cuda_status(cudaDeviceSynchronize(), "allocation");
+}
+
+Status Net::create(const std::string& path, int patch, int max_batch, int precision, int device) {
+    P_ = patch;
+    Bmax_ = max_batch;
+    prec_ = precision;
+    dev_ = device;
+    if (patch <= 0 || max_batch <= 0) return fail(kInvalid, "net: patch and max_batch must be positive");
+    if (precision != 0 && precision != 1) return fail(kInvalid, "net: precision must be bf16 (0) or fp8 (1)");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return fail(kInvalid, "net: CUDA device " + std::to_string(device) + " not available");
+    Status st = cuda_status(cudaSetDevice(device), "cudaSetDevice");
+    if (!st.ok()) return st;
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, device);
+    if (prop.major != 10) return fail(kUnsupported, "net: needs an sm_100 (B200-class) GPU, found sm_" +
+                                                        std::to_string(prop.major) + std::to_string(prop.minor));
+    sm_count_ = prop.multiProcessorCount;
+    WeightMap wm;
+    std::string err = load_fxweights(path, wm);
+    if (!err.empty()) return fail(err.find("open") != std::string::npos ? kIo : kDecode, err);
+    if ((st = parse(wm)).code) return st;
+    const int div = 1 << (S_ - 1);
+    if (P_ % div) return fail(kInvalid, "patch must be divisible by " + std::to_string(div));
+    for (int s = 0; s < S_; ++s)
+        if (F_[s] % 16) return fail(kUnsupported, "net: stage features must be multiples of 16");
+    if (F_[0] > 64) return fail(kUnsupported, "net: first stage wider than 64 channels");
+    if ((st = cuda_status(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate")).code) return st;
+    if ((st = alloc()).code) return st;
+    for (auto* v : {&enc_, &up_, &dec_})
+        for (Layer& L : *v)
+            if ((st = build_layer(L, 0)).code) return st;
+    amax_.assign(5 * S_, 0.f);
+    return ok();
+}
+
+// ---- one conv launch ----------------------------------------------------------------------
+Status Net::run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs, uint8_t* out_ptr,
+                     int64_t out_bs, int64_t out_gs, int out_fp8, float out_qscale, unsigned* amax, int nb,
+                     cudaStream_t s) {
+    return launch_layer(L, q, level(L.lin), level(L.lout), in_ptr, in_bs, in_gs, out_ptr, out_bs, out_gs, out_fp8,
+                        out_qscale, amax, nb, sm_count_, d_status_, s);
+}
+
+Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
+                    uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_fp8, float out_qscale, unsigned* amax,
+                    int nb, int sm_count_, uint32_t* d_status_, cudaStream_t s) {
+    DevProgram& dp = L.prog[q];
+    if (!dp.built) return fail(kInternal, L.name + ": program not built");
+    fxk::ConvParams p{};
+    const ActGeom& rs = dp.rowspace;
+    if (L.kind == Layer::kConv && L.stride == 2) {
+        const int64_t ps = gout.gs();
+        for (int phi = 0; phi < 8; ++phi) p.src[phi] = {in_ptr + phi * ps, in_bs, in_gs, gout.rows()};
+    } else {
+        p.src[0] = {in_ptr, in_bs, in_gs, gin.rows()};
+    }
+    p.stages = dp.stages;
+    p.mmas = dp.mmas;
+    p.wpack = dp.wpack;
+    p.wtile_bytes = dp.host.wtile_bytes;
+    p.n_stages = static_cast<int32_t>(dp.host.stages.size());
+    p.fp8 = dp.fp8 ? 1 : 0;
+    p.batch = nb;
+    p.Dp = rs.D + 2;
+    p.Hp = rs.H + 2;
+    p.Wp = rs.W + 2;
+    const int64_t P2 = static_cast<int64_t>(p.Hp) * p.Wp;
+    p.row_begin = P2;
+    p.row_end = static_cast<int64_t>(p.Dp - 1) * P2;
+    p.R = dp.R;
+    p.n_units_m = dp.n_units_m;
+    p.n_tiles = dp.host.n_tiles;
+    p.N_tile = dp.N_tile;
+    p.acc_slots = dp.acc_slots;
+    p.tmem_cols = dp.tmem_cols;
+    p.n_pipe = dp.host.n_pipe;
+    p.stage_bytes = dp.host.stage_bytes;
+    p.stage_a_bytes = dp.host.stage_a_bytes;
+    p.col_scale = dp.colscale;
+    p.out = out_ptr;
+    p.out_batch_stride = out_bs;
+    p.out_group_stride = out_gs;
+    p.status = d_status_;
+    if (L.kind == Layer::kUp) {
+        p.mode = fxk::kModeUpsample;
+        p.bias = dp.bias;
+        p.out_fp8 = out_fp8;
+        p.out_qscale = out_qscale;
+        p.cout = L.Cout;
+        p.oHp = gout.H + 2;
+        p.oWp = gout.W + 2;
+        p.amax = amax;
+    } else {
+        p.mode = fxk::kModePrenorm;
+        p.stats = L.d_partials;
+        p.stats_C = L.Cout;
+        L.nrec = dp.n_units_m * 4;
+    }
+    const int64_t units = static_cast<int64_t>(nb) * p.n_units_m * p.n_tiles;
+    const int grid = static_cast<int>(std::min<int64_t>(units, sm_count_));
+    return cuda_status(fxk::launch_conv_tc(p, grid, dp.smem(), s), L.name.c_str());
+}
+
+Status Net::finalize_in(Layer& L, int nb, cudaStream_t s) {
+    const ActGeom g = level(L.lout);
+    const double count = static_cast<double>(g.D) * g.H * g.W;
+    return cuda_status(fxk::launch_in_finalize(L.d_partials, nb, L.nrec, L.Cout, count, L.d_gamma, L.d_beta, kEps,
+                                               L.d_ss, s),
+                       "in_finalize");
+}
+
+// ---- forward -----------------------------------------------------------------------------------
+Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
+                    int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s) {
+    if (nb < 1 || nb > Bmax_) return fail(kInvalid, "forward: batch out of range");
+    const int q = (prec_ == 1 && !calib) ? 1 : 0;
+    if (q == 1 && !calibrated_) return fail(kInvalid, "forward: fp8 net used before fx_net_calibrate");
+    Status st;
+    const ActGeom g0 = level(0);
+    if ((st = cuda_status(cudaMemsetAsync(d_sums_, 0, sizeof(unsigned long long) * 2 * nb, s), "memset")).code) return st;
+    if ((st = cuda_status(fxk::launch_tile_sums(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, s), "tile_sums")).code) return st;
+    if ((st = cuda_status(fxk::launch_tile_norm(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, l0_, g0.gs(), nullptr, s),
+                          "tile_norm"))
+            .code)
+        return st;
+    auto amax_slot = [&](int k) -> unsigned* { return calib ? d_amax_ + k : nullptr; };
+    const int cgq = q ? 16 : 8;
+    auto act_bs = [&](int lvl, int C) { return static_cast<int64_t>(C / cgq) * level(lvl).gs(); };
+    auto dest = [&](uint8_t* ptr, int lvl, int Cbuf, int g0off, float scale) {
+        fxk::NormDest d{};
+        d.ptr = ptr + static_cast<int64_t>(g0off) * level(lvl).gs();
+        d.batch_stride = act_bs(lvl, Cbuf);
+        d.group_stride = level(lvl).gs();
+        d.fp8 = q;
+        d.qscale = q ? 1.f / scale : 1.f;
+        return d;
+    };
+    auto phase_dest = [&](int s, float scale) {
+        fxk::NormDest d{};
+        const ActGeom gn = level(s + 1);
+        d.ptr = ph_[s];
+        d.phase = 1;
+        d.pHp = gn.H + 2;
+        d.pWp = gn.W + 2;
+        d.phase_stride = gn.gs();
+        d.group_stride = 8 * gn.gs();
+        d.batch_stride = static_cast<int64_t>(F_[s] / cgq) * d.group_stride;
+        d.fp8 = q;
+        d.qscale = q ? 1.f / scale : 1.f;
+        return d;
+    };
+    auto norm = [&](Layer& L, fxk::NormDest d0, fxk::NormDest d1, int slot) -> Status {
+        Status r = finalize_in(L, nb, s);
+        if (!r.ok()) return r;
+        const ActGeom g = level(L.lout);
+        return cuda_status(fxk::launch_norm_act(pn_[L.lout], static_cast<int64_t>(L.Cout / 8) * g.gs(), g.gs(),
+                                                {g.D, g.H, g.W}, L.Cout, nb, L.d_ss, kSlope, d0, d1, amax_slot(slot), s),
+                           "norm_act");
+    };
+    const fxk::NormDest none{};
+    auto s_of = [&](const Layer& L) { return L.in_scale; };
+    // encoder
+    for (int st_ = 0; st_ < S_; ++st_) {
+        const ActGeom g = level(st_);
+        const int64_t pn_bs = static_cast<int64_t>(F_[st_] / 8) * g.gs();
+        for (int i = 0; i < nconv_; ++i) {
+            Layer& L = enc_[st_ * nconv_ + i];
+            const int qe = L.kind == Layer::kFirst ? 0 : q;
+            const uint8_t* in;
+            int64_t ibs, igs;
+            if (L.kind == Layer::kFirst) {
+                in = l0_;
+                ibs = g0.gs();
+                igs = g0.gs();
+            } else if (i == 0) {  // stride-2: phase copy of the previous stage's output
+                in = ph_[st_ - 1];
+                igs = 8 * g.gs();
+                ibs = static_cast<int64_t>(F_[st_ - 1] / cgq) * igs;
+            } else {
+                in = act_[st_];
+                ibs = act_bs(st_, F_[st_]);
+                igs = g.gs();
+            }
+            if ((st = run_conv(L, qe, in, ibs, igs, pn_[st_], pn_bs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
+            const bool last = i == nconv_ - 1;
+            if (!last) {
+                const Layer& nxt = enc_[st_ * nconv_ + i + 1];
+                if ((st = norm(L, dest(act_[st_], st_, F_[st_], 0, s_of(nxt)), none, st_)).code) return st;
+            } else if (st_ < S_ - 1) {
+                const float scat = dec_[st_ * nconv_].in_scale;
+                const float sph = enc_[(st_ + 1) * nconv_].in_scale;
+                if ((st = norm(L, dest(cat_[st_], st_, 2 * F_[st_], F_[st_] / cgq, scat), phase_dest(st_, sph),
+                               S_ + st_))
+                        .code)
+                    return st;
+            } else {
+                if ((st = norm(L, dest(act_[st_], st_, F_[st_], 0, s_of(up_[S_ - 2])), none, S_ + st_)).code) return st;
+            }
+        }
+    }
+    // decoder
+    for (int lvl = S_ - 2; lvl >= 0; --lvl) {
+        const ActGeom g = level(lvl);
+        Layer& U = up_[lvl];
+        const float scat = dec_[lvl * nconv_].in_scale;
+        if ((st = run_conv(U, q, act_[lvl + 1], act_bs(lvl + 1, F_[lvl + 1]), level(lvl + 1).gs(), cat_[lvl],
+                           act_bs(lvl, 2 * F_[lvl]), g.gs(), q, q ? 1.f / scat : 1.f, amax_slot(2 * S_ + lvl), nb, s))
+                .code)
+            return st;
+        const int64_t pn_bs = static_cast<int64_t>(F_[lvl] / 8) * g.gs();
+        for (int i = 0; i < nconv_; ++i) {
+            Layer& L = dec_[lvl * nconv_ + i];
+            const uint8_t* in = i == 0 ? cat_[lvl] : act_[lvl];
+            const int64_t ibs = i == 0 ? act_bs(lvl, 2 * F_[lvl]) : act_bs(lvl, F_[lvl]);
+            if ((st = run_conv(L, q, in, ibs, g.gs(), pn_[lvl], pn_bs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
+            const bool last = i == nconv_ - 1;
+            if (!last) {
+                const Layer& nxt = dec_[lvl * nconv_ + i + 1];
+                if ((st = norm(L, dest(act_[lvl], lvl, F_[lvl], 0, s_of(nxt)), none, 3 * S_ + lvl)).code) return st;
+            } else if (lvl > 0) {
+                if ((st = norm(L, dest(act_[lvl], lvl, F_[lvl], 0, s_of(up_[lvl - 1])), none, 4 * S_ + lvl)).code)
+                    return st;
+            } else {
+                if ((st = finalize_in(L, nb, s)).code) return st;
+                fxk::HeadParams h{};
+                h.pre = pn_[0];
+                h.pre_batch_stride = pn_bs;
+                h.pre_group_stride = g.gs();
+                h.P = P_;
+                h.C = F_[0];
+                h.B = nb;
+                h.ncls = ncls_;
+                h.channel = channel;
+                h.sigmoid = sigmoid;
+                h.ss = L.d_ss;
+                h.slope = kSlope;
+                h.wh = d_head_w_;
+                h.bh = d_head_b_;
+                h.gauss = d_gauss_;
+                h.tiles = d_tiles;
+                h.acc = acc;
+                h.dz = dz;
+                h.dy = dy;
+                h.dx = dx;
+                h.prob = prob;
+                if ((st = cuda_status(fxk::launch_head_blend(h, s), "head_blend")).code) return st;
+            }
+        }
+    }
+    return ok();
+}
+
+// ---- calibration ------------------------------------------------------------------------------
+Status Net::set_scales_from_amax() {
+    auto sc = [&](int k) { return std::max(amax_[k], 1e-8f) / kE4M3Max; };
+    for (int s = 0; s < S_; ++s) {
+        for (int i = 1; i < nconv_; ++i) enc_[s * nconv_ + i].in_scale = sc(s);  // nA
+        if (s + 1 < S_) enc_[(s + 1) * nconv_].in_scale = sc(S_ + s);           // skip -> phase copy
+    }
+    for (int lvl = 0; lvl < S_ - 1; ++lvl) {
+        const float scat = std::max(sc(S_ + lvl), sc(2 * S_ + lvl));
+        dec_[lvl * nconv_].in_scale = scat;
+        for (int i = 1; i < nconv_; ++i) dec_[lvl * nconv_ + i].in_scale = sc(3 * S_ + lvl);
+        up_[lvl].in_scale = lvl == S_ - 2 ? sc(S_ + S_ - 1) : sc(4 * S_ + lvl + 1);
+    }
+    return ok();
+}
+
+Status Net::calibrate(const uint8_t* host_patches, int n) {
+    if (prec_ != 1) return fail(kInvalid, "calibrate: net is not fp8");
+    if (n < 1) return fail(kInvalid, "calibrate: need at least one patch");
+    cudaSetDevice(dev_);
+    const size_t pv = static_cast<size_t>(P_) * P_ * P_;
+    uint8_t* d_vol = static_cast<uint8_t*>(dalloc(pv * Bmax_));
+    if (!d_vol) return fail(kInternal, "cudaMalloc: calibration patches");
+    std::vector<fxk::TileOrigin> org(Bmax_);
+    for (int b = 0; b < Bmax_; ++b) org[b] = {static_cast<int64_t>(b) * P_, 0, 0};
+    fxk::TileOrigin* d_org = nullptr;
+    Status st = upload(d_org, org, this, allocs_);
+    if (!st.ok()) return st;
+    cudaMemsetAsync(d_amax_, 0, sizeof(unsigned) * 5 * S_, stream_);
+    for (int i0 = 0; i0 < n; i0 += Bmax_) {
+        const int nb = std::min(Bmax_, n - i0);
+        if ((st = cuda_status(cudaMemcpyAsync(d_vol, host_patches + pv * i0, pv * nb, cudaMemcpyHostToDevice, stream_),
+                              "H2D calibration"))
+                .code)
+            return st;
+        if ((st = forward(d_vol, static_cast<int64_t>(nb) * P_, P_, P_, d_org, nb, 1, 0, nullptr, nullptr, true,
+                          stream_))
+                .code)
+            return st;
+    }
+    std::vector<unsigned> bits(5 * S_);
+    if ((st = cuda_status(cudaMemcpyAsync(bits.data(), d_amax_, sizeof(unsigned) * bits.size(), cudaMemcpyDeviceToHost,
+                                          stream_),
+                          "D2H amax"))
+            .code)
+        return st;
+    if ((st = cuda_status(cudaStreamSynchronize(stream_), "calibration forward")).code) return st;
+    uint32_t status = 0;
+    cudaMemcpy(&status, d_status_, 4, cudaMemcpyDeviceToHost);
+    if (status) return fail(kInternal, "calibration: device status " + std::to_string(status));
+    for (size_t k = 0; k < bits.size(); ++k) {
+        float f;
+        std::memcpy(&f, &bits[k], 4);
+        amax_[k] = std::max(amax_[k], f);  // running max over calls
+    }
+    set_scales_from_amax();
+    for (auto* v : {&enc_, &up_, &dec_})
+        for (Layer& L : *v) {
+            if (L.kind == Layer::kFirst) continue;
+            L.prog[1] = DevProgram{};
+            if ((st = build_layer(L, 1)).code) return st;
+        }
+    calibrated_ = true;
+    return ok();
+}
+
+std::vector<float> Net::act_scales() const {
+    std::vector<float> out;
+    for (auto* v : {&enc_, &up_, &dec_})
+        for (const Layer& L : *v) out.push_back(L.in_scale);
+    return out;
+}
+
+// ---- sliding window ---------------------------------------------------------------------------
+Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int patch, double overlap,
+                          int channel, int sigmoid, int batch, int64_t tile_begin, int64_t tile_end, float* d_acc,
+                          cudaStream_t s) {
+    if (patch != P_) return fail(kInvalid, "predict: patch differs from the net's patch");
+    if (batch < 1) batch = 1;
+    batch = std::min(batch, Bmax_);
+    const auto zs = tile_starts(dz, P_, overlap), ys = tile_starts(dy, P_, overlap), xs = tile_starts(dx, P_, overlap);
+    const int64_t total = static_cast<int64_t>(zs.size()) * ys.size() * xs.size();
+    if (tile_end < 0 || tile_end > total) tile_end = total;
+    if (tile_begin < 0) tile_begin = 0;
+    if (tile_begin >= tile_end) return ok();
+    std::vector<fxk::TileOrigin> tiles;
+    tiles.reserve(static_cast<size_t>(tile_end - tile_begin));
+    for (int64_t i = tile_begin; i < tile_end; ++i) {
+        const int64_t xi = i % static_cast<int64_t>(xs.size());
+        const int64_t yi = (i / static_cast<int64_t>(xs.size())) % static_cast<int64_t>(ys.size());
+        const int64_t zi = i / (static_cast<int64_t>(xs.size()) * ys.size());
+        tiles.push_back({zs[zi], ys[yi], xs[xi]});
+    }
+    if (static_cast<int64_t>(tiles.size()) > d_tiles_cap_) {
+        void* p = dalloc(sizeof(fxk::TileOrigin) * tiles.size());
+        if (!p) return fail(kInternal, "cudaMalloc: tile list");
+        d_tiles_ = static_cast<fxk::TileOrigin*>(p);
+        d_tiles_cap_ = static_cast<int64_t>(tiles.size());
+    }
+    Status st = cuda_status(cudaMemcpyAsync(d_tiles_, tiles.data(), sizeof(fxk::TileOrigin) * tiles.size(),
+                                            cudaMemcpyHostToDevice, s),
+                            "H2D tiles");
+    if (!st.ok()) return st;
+    for (size_t i0 = 0; i0 < tiles.size(); i0 += batch) {
+        const int nb = static_cast<int>(std::min<size_t>(batch, tiles.size() - i0));
+        if ((st = forward(d_vol, dz, dy, dx, d_tiles_ + i0, nb, channel, sigmoid, d_acc, nullptr, false, s)).code)
+            return st;
+    }
+    return ok();
+}
+
+}  // namespace fxh

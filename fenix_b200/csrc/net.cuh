@@ -1,0 +1,140 @@
+// net.cuh — the plain 3D UNet (nnU-Net style: per stage 2 x [conv3 + InstanceNorm + LeakyReLU],
+// stride-2 conv downsampling, ConvTranspose3d 2^3 upsampling, skip concat, 1x1x1 head) run on
+// the B200 kernels, plus the sliding-window driver around it. Module semantics follow the
+// reference's nets::ConvNormAct / ConvStack / Decoder (src/ml/nets/resenc_unet.hpp:35-52,
+// 141-158, 197-239); the driver follows ml::predict_surface_filled (src/ml/infer.hpp:456-864).
+#pragma once
+
+#include "conv_tc.cuh"
+#include "eltwise.cuh"
+#include "fxweights.hpp"
+#include "program.hpp"
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace fxh {
+
+// Status code (values of fx_status) + message.
+struct Status {
+    int code = 0;
+    std::string msg;
+    bool ok() const { return code == 0; }
+};
+inline Status ok() { return {}; }
+inline Status fail(int code, std::string m) { return {code, std::move(m)}; }
+constexpr int kInvalid = 1, kNotFound = 2, kIo = 3, kDecode = 5, kUnsupported = 6, kInternal = 8;
+
+Status cuda_status(cudaError_t e, const char* what);
+
+// Padded group-plane tensor geometry (see conv_tc.cuh).
+struct ActGeom {
+    int D = 0, H = 0, W = 0;
+    int64_t rows() const { return static_cast<int64_t>(D + 2) * (H + 2) * (W + 2); }
+    int64_t gs() const { return rows() * 16; }
+};
+
+struct DevProgram {
+    fxk::ConvStage* stages = nullptr;
+    fxk::ConvMma* mmas = nullptr;
+    uint8_t* wpack = nullptr;
+    float* colscale = nullptr;
+    float* bias = nullptr;
+    Program host;
+    int R = 1, N_tile = 0, acc_slots = 1, n_units_m = 0;
+    uint32_t tmem_cols = 32;
+    ActGeom rowspace;  // output grid (conv) or input grid (transposed conv)
+    bool fp8 = false, built = false;
+    size_t smem() const { return static_cast<size_t>(host.n_pipe) * host.stage_bytes + 1024; }
+};
+
+struct Layer {
+    enum Kind { kConv, kFirst, kUp } kind = kConv;
+    std::string name;
+    int Cin = 0, Cout = 0, stride = 1;
+    int lin = 0, lout = 0;            // resolution levels of input and output
+    std::vector<float> w;             // conv: [Cout][Cin][27]; up: [Cin][Cout][8]
+    std::vector<float> b;             // up: bias (conv biases cancel inside InstanceNorm)
+    std::vector<float> gamma, beta;   // InstanceNorm affine
+    std::vector<float> wscale;        // fp8 per-output-channel weight scale (amax / 448)
+    float in_scale = 1.f;             // fp8 per-tensor scale of the input activation
+    DevProgram prog[2];               // [0] bf16, [1] e4m3
+    float* d_gamma = nullptr;
+    float* d_beta = nullptr;
+    float* d_partials = nullptr;      // [Bmax][n_units_m][4][Cout][2]
+    float* d_ss = nullptr;            // [Bmax][Cout][2]
+    int nrec = 0;
+};
+
+// Compile one layer's program for precision q (0 bf16, 1 e4m3) and upload it; gin/gout are
+// the input and output grids. Device buffers are appended to `allocs` (owned by the caller).
+Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax, int sm_count,
+                           std::vector<void*>& allocs);
+// Launch one layer. Stride-2 convs read the phase-split copy (gout geometry per phase); the
+// prenorm mode writes L.d_partials and sets L.nrec.
+Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
+                    uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_fp8, float out_qscale, unsigned* amax,
+                    int nb, int sm_count, uint32_t* d_status, cudaStream_t s);
+
+class Net {
+  public:
+    ~Net();
+    Status create(const std::string& path, int patch, int max_batch, int precision, int device);
+    Status calibrate(const uint8_t* host_patches, int n);
+    // Forward nb tiles of a device volume at the given device tile origins. Head output:
+    // Gaussian blend into acc (dims) and/or probabilities into prob ([nb][P^3]).
+    Status forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
+                   int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s);
+    Status predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int patch, double overlap,
+                         int channel, int sigmoid, int batch, int64_t tile_begin, int64_t tile_end, float* d_acc,
+                         cudaStream_t s);
+
+    int patch() const { return P_; }
+    int max_batch() const { return Bmax_; }
+    int classes() const { return ncls_; }
+    const std::vector<int>& features() const { return F_; }
+    int precision() const { return prec_; }
+    int device() const { return dev_; }
+    cudaStream_t stream() const { return stream_; }
+    bool calibrated() const { return calibrated_; }
+    std::vector<float> act_scales() const;
+
+  private:
+    Status parse(const WeightMap& wm);
+    Status alloc();
+    Status build_layer(Layer& L, int q);
+    Status run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs, uint8_t* out_ptr,
+                    int64_t out_bs, int64_t out_gs, int out_fp8, float out_qscale, unsigned* amax, int nb,
+                    cudaStream_t s);
+    Status finalize_in(Layer& L, int nb, cudaStream_t s);
+    Status set_scales_from_amax();
+    ActGeom level(int s) const { return {P_ >> s, P_ >> s, P_ >> s}; }
+    void* dalloc(size_t bytes);
+
+    int P_ = 0, Bmax_ = 0, ncls_ = 2, prec_ = 0, dev_ = 0, S_ = 0, nconv_ = 2, sm_count_ = 148;
+    std::vector<int> F_;
+    std::vector<Layer> enc_;  // S * nconv, stage-major
+    std::vector<Layer> up_;   // S-1, index = level
+    std::vector<Layer> dec_;  // (S-1) * nconv, index = level * nconv + i
+    std::vector<float> head_w_, head_b_;
+    float* d_head_w_ = nullptr;
+    float* d_head_b_ = nullptr;
+    // activations (allocated at bf16 size; fp8 uses the first half of every group run)
+    uint8_t* l0_ = nullptr;
+    std::vector<uint8_t*> pn_, act_, cat_, ph_;
+    unsigned long long* d_sums_ = nullptr;
+    unsigned* d_amax_ = nullptr;  // calibration amax slots
+    std::vector<float> amax_;
+    float* d_gauss_ = nullptr;
+    uint32_t* d_status_ = nullptr;
+    fxk::TileOrigin* d_tiles_ = nullptr;
+    int64_t d_tiles_cap_ = 0;
+    cudaStream_t stream_ = nullptr;
+    bool calibrated_ = false;
+    std::vector<void*> allocs_;
+};
+
+}  // namespace fxh

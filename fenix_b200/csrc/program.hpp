@@ -1,0 +1,224 @@
+// program.hpp — host-side compiler from one convolution (taps x row offsets over the padded
+// group-plane layout) to the stage/MMA program and packed weights that conv_tc_kernel runs.
+#pragma once
+
+#include "conv_tc.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <string>
+#include <vector>
+
+namespace fxh {
+
+struct Tap {
+    int src;      // source array index (ConvParams::src)
+    int64_t off;  // row offset relative to the output row
+    int wkey;     // weight tap id passed to the weight accessor
+    int window;   // taps with the same window share one staged run of rows
+};
+
+struct ProgramSpec {
+    int G = 0;         // input groups (16 bytes each)
+    int cg = 8;        // channels per group: 8 (bf16) or 16 (e4m3)
+    int elem = 2;      // bytes per element
+    int N_total = 0;   // output columns
+    int N_tile = 0;    // columns per work unit
+    int R = 1;         // 128-row M blocks per unit
+    bool pair_taps = false;  // G == 1: the two K-halves of one MMA come from two taps
+    std::vector<Tap> taps;
+    // B value for output column n, input channel ci (0 <= ci < G*cg), tap key
+    std::function<float(int n, int ci, int wkey)> wval;
+    int smem_total = 220 * 1024;
+};
+
+struct Program {
+    std::vector<fxk::ConvStage> stages;
+    std::vector<fxk::ConvMma> mmas;
+    std::vector<uint8_t> wpack;  // n_tiles blocks of wtile_bytes
+    int64_t wtile_bytes = 0;
+    int stage_bytes = 0, stage_a_bytes = 0, n_pipe = 0;
+    int n_tiles = 0;
+};
+
+// e4m3 encode with round-to-nearest-even and saturation to +-448 (finite), host side.
+inline uint8_t float_to_e4m3(float f) {
+    if (std::isnan(f)) return 0x7f;
+    uint8_t sign = std::signbit(f) ? 0x80 : 0x00;
+    float a = std::fabs(f);
+    if (a >= 448.f) return sign | 0x7e;  // max finite 448
+    if (a < std::ldexp(1.f, -10)) {  // below half of the smallest subnormal (2^-9)
+        return sign;
+    }
+    // candidates: enumerate all 126 finite positive codes and pick nearest (ties to even code)
+    static float table[127];
+    static bool init = false;
+    if (!init) {
+        for (int c = 0; c < 127; ++c) {
+            const int e = (c >> 3) & 0xf, m = c & 7;
+            table[c] = e == 0 ? std::ldexp(static_cast<float>(m), -9) : std::ldexp(1.f + m / 8.f, e - 7);
+        }
+        init = true;
+    }
+    int lo = 0, hi = 126;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) / 2;
+        if (table[mid] <= a) lo = mid; else hi = mid;
+    }
+    int best;
+    const float dl = a - table[lo], dh = table[hi] - a;
+    if (dl < dh) best = lo;
+    else if (dh < dl) best = hi;
+    else best = (lo & 1) ? hi : lo;
+    return sign | static_cast<uint8_t>(best);
+}
+
+inline uint16_t float_to_bf16(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;
+    const uint32_t lsb = (u >> 16) & 1u;
+    u += 0x7fffu + lsb;
+    return static_cast<uint16_t>(u >> 16);
+}
+
+// Returns "" on success.
+inline std::string build_program(const ProgramSpec& s, Program& pg) {
+    if (s.N_tile <= 0 || s.N_tile % 16 || s.N_total % s.N_tile) return "program: bad N tiling";
+    if (s.N_tile > 256 && s.N_tile != 320) return "program: N tile > 256 must be 320";
+    if (!s.pair_taps && (s.G % 2)) return "program: group count must be even";
+    const int Mtot = 128 * s.R;
+    // windows
+    std::map<int, std::vector<Tap>> win;
+    for (const Tap& t : s.taps) win[t.window].push_back(t);
+    struct W {
+        int src;
+        int64_t lo, hi;
+        std::vector<Tap> taps;
+    };
+    std::vector<W> ws;
+    int max_rows = 0, max_taps = 0;
+    for (auto& kv : win) {
+        W w;
+        w.src = kv.second[0].src;
+        w.taps = kv.second;
+        std::sort(w.taps.begin(), w.taps.end(), [](const Tap& a, const Tap& b) { return a.off < b.off; });
+        w.lo = w.taps.front().off;
+        w.hi = w.taps.back().off;
+        for (auto& t : w.taps)
+            if (t.src != w.src) return "program: window mixes sources";
+        max_rows = std::max<int>(max_rows, static_cast<int>(Mtot + (w.hi - w.lo)));
+        max_taps = std::max<int>(max_taps, static_cast<int>(w.taps.size()));
+        ws.push_back(std::move(w));
+    }
+    // groups per stage: largest that keeps >= 3 stages in the smem budget (>= 2 as a fallback)
+    const int bblk = s.N_tile * 32;  // bytes of one MMA's B block
+    auto stage_bytes_for = [&](int gc) {
+        const int nm = s.pair_taps ? (max_taps + 1) / 2 : max_taps * (gc / 2);
+        return max_rows * gc * 16 + nm * bblk;
+    };
+    int gc = s.pair_taps ? 1 : 2;
+    if (!s.pair_taps) {
+        for (int c = s.G; c >= 2; c -= 2)
+            if (stage_bytes_for(c) * 3 <= s.smem_total) {
+                gc = c;
+                break;
+            }
+    }
+    int sb = stage_bytes_for(gc);
+    int n_pipe = std::min(8, s.smem_total / sb);
+    if (n_pipe < 2) return "program: stage does not fit in shared memory (" + std::to_string(sb) + " bytes)";
+    pg.stage_bytes = (sb + 127) / 128 * 128;
+    pg.stage_a_bytes = max_rows * gc * 16;
+    n_pipe = std::min(8, s.smem_total / pg.stage_bytes);
+    pg.n_pipe = n_pipe;
+    pg.n_tiles = s.N_total / s.N_tile;
+    pg.stages.clear();
+    pg.mmas.clear();
+
+    // B blocks are recorded as (tap A, tap B or -1, group pair) and packed per N tile below.
+    struct BRec {
+        int wk0, wk1;  // tap keys for the two K-halves (-1 = zeros)
+        int g0, g1;    // input groups of the two K-halves
+    };
+    std::vector<BRec> brecs;
+    int32_t boff = 0;
+    for (const W& w : ws) {
+        const int rows = static_cast<int>(Mtot + (w.hi - w.lo));
+        for (int g0 = 0; g0 < s.G; g0 += gc) {
+            const int ng = std::min(gc, s.G - g0);
+            fxk::ConvStage st{};
+            st.src = w.src;
+            st.row_off = static_cast<int32_t>(w.lo);
+            st.rows = rows;
+            st.g0 = g0;
+            st.ng = ng;
+            st.b_off = boff;
+            st.mma_begin = static_cast<int32_t>(pg.mmas.size());
+            int32_t local_b = 0;
+            if (s.pair_taps) {
+                for (size_t i = 0; i < w.taps.size(); i += 2) {
+                    const Tap& a = w.taps[i];
+                    const bool two = i + 1 < w.taps.size();
+                    fxk::ConvMma m{};
+                    m.a_off = static_cast<int32_t>((a.off - w.lo) * 16);
+                    m.lbo = two ? static_cast<int32_t>((w.taps[i + 1].off - a.off) * 16) : 0;
+                    m.b_off = local_b;
+                    pg.mmas.push_back(m);
+                    brecs.push_back({a.wkey, two ? w.taps[i + 1].wkey : -1, 0, 0});
+                    local_b += bblk;
+                }
+            } else {
+                for (const Tap& t : w.taps)
+                    for (int gp = g0; gp < g0 + ng; gp += 2) {
+                        fxk::ConvMma m{};
+                        m.a_off = static_cast<int32_t>((gp - g0) * rows * 16 + (t.off - w.lo) * 16);
+                        m.lbo = rows * 16;
+                        m.b_off = local_b;
+                        pg.mmas.push_back(m);
+                        brecs.push_back({t.wkey, t.wkey, gp, gp + 1});
+                        local_b += bblk;
+                    }
+            }
+            st.mma_count = static_cast<int32_t>(pg.mmas.size()) - st.mma_begin;
+            st.b_bytes = local_b;
+            boff += local_b;
+            pg.stages.push_back(st);
+        }
+    }
+    pg.wtile_bytes = boff;
+    pg.wpack.assign(static_cast<size_t>(boff) * pg.n_tiles, 0);
+    const int cg = s.cg;
+    for (int nt = 0; nt < pg.n_tiles; ++nt) {
+        uint8_t* tile = pg.wpack.data() + static_cast<size_t>(nt) * boff;
+        for (size_t k = 0; k < brecs.size(); ++k) {
+            const BRec& br = brecs[k];
+            uint8_t* blk = tile + k * bblk;
+            for (int h = 0; h < 2; ++h) {
+                const int wk = h == 0 ? br.wk0 : br.wk1;
+                const int g = h == 0 ? br.g0 : br.g1;
+                if (wk < 0) continue;
+                for (int n = 0; n < s.N_tile; ++n) {
+                    const int col = nt * s.N_tile + n;
+                    uint8_t* row = blk + (static_cast<size_t>(h) * s.N_tile + n) * 16;
+                    for (int j = 0; j < cg; ++j) {
+                        const float v = s.wval(col, g * cg + j, wk);
+                        if (s.elem == 2) {
+                            const uint16_t b = float_to_bf16(v);
+                            std::memcpy(row + 2 * j, &b, 2);
+                        } else {
+                            row[j] = float_to_e4m3(v);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    return {};
+}
+
+}  // namespace fxh

@@ -1,0 +1,137 @@
+/* fenix_b200.h — C ABI of the B200 (sm_100a) surface-prediction inference library.
+ *
+ * Plain C types only: pointers, sizes, enums. No exception crosses this boundary; every call
+ * returns an fx_status (1:1 with the reference's fenix::Errc, src/core/error.hpp:19-29) and the
+ * message of the last failure on the calling thread is available from fx_last_error().
+ *
+ * Which reference interface each entry point replaces:
+ *   fx_net_create / fx_net_destroy  — building nets::ResEncUNet-style modules + load_fxweights /
+ *                                     load_into (src/ml/inference.cpp:668-711,
+ *                                     src/ml/weights.hpp:63-142), the TrtNet/AotiNet adapters'
+ *                                     static batch/patch/classes (src/ml/trt_engine.hpp:35-106)
+ *   fx_net_calibrate                — fp8 static calibration (tools/ml-export/fp8_forward.py:88-127)
+ *   fx_net_forward                  — the operator concept net->forward(x) followed by the
+ *                                     softmax/sigmoid channel select + nan_to_num
+ *                                     (src/ml/infer.hpp:760-767, src/ml/inference.cpp:226-233)
+ *   fx_predict_volume               — ml::predict_surface_filled over a dense u8 volume
+ *                                     (src/ml/infer.hpp:456-864) plus the u8 encode of
+ *                                     run_predict_core (src/ml/inference.cpp:309-351)
+ *   fx_tile_starts / fx_gaussian1d / fx_weight_profile
+ *                                   — src/ml/tiling.hpp:16-42, src/ml/infer.hpp:499-509,
+ *                                     src/ml/global_accum.hpp:29-35
+ *   fx_norm_tiles                   — the dense u8 filler + detail::norm_patch (zscore)
+ *                                     (src/ml/inference.cpp:309-321, src/ml/infer.hpp:350-385)
+ *   fx_conv3d / fx_conv_transpose2  — one ConvNormAct conv / nn::ConvTranspose3d
+ *                                     (src/ml/nets/resenc_unet.hpp:35-52, 211)
+ *   fx_accum_finalize               — normalize() + u8 quantise (src/ml/infer.hpp:510-521,
+ *                                     src/ml/global_accum.hpp:123-152)
+ */
+#ifndef FENIX_B200_H
+#define FENIX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum fx_status {
+    FX_OK = 0,
+    FX_INVALID_ARGUMENT = 1,
+    FX_NOT_FOUND = 2,
+    FX_IO_ERROR = 3,
+    FX_FETCH_FAILED = 4,
+    FX_DECODE_ERROR = 5,
+    FX_UNSUPPORTED = 6,
+    FX_UNIMPLEMENTED = 7,
+    FX_INTERNAL = 8
+} fx_status;
+
+typedef enum fx_precision { FX_PREC_BF16 = 0, FX_PREC_FP8 = 1 } fx_precision;
+
+/* Mirrors ml::InferOptions (src/ml/infer.hpp:38-103), the subset this path implements. */
+typedef struct fx_infer_opts {
+    int patch;      /* tile side P, divisible by 2^(stages-1) */
+    double overlap; /* step = (int64)(P * (1 - overlap)) */
+    int channel;    /* softmax channel to emit (surface = 1); ignored with sigmoid */
+    int sigmoid;    /* 1-class head -> sigmoid */
+    int batch;      /* tiles per forward, <= the net's max batch */
+} fx_infer_opts;
+
+typedef struct fx_net fx_net;
+
+/* Last error message of the calling thread ("" when none). */
+const char* fx_last_error(void);
+
+/* Number of CUDA devices visible (0 when no driver or GPU). */
+int fx_device_count(void);
+
+/* Build a plain 3D UNet from an .fxweights file (FXWT v1, src/ml/weights.hpp:1-10) on device
+ * `device`, for tiles of side `patch` and up to `max_batch` tiles per forward. The stage count,
+ * features and classes are read from the tensor shapes (encoder.stages.{s}.convs.{i}.conv.*,
+ * decoder.transpconvs.{t}.*, decoder.stages.{t}.convs.{i}.*, decoder.seg_layers.{t}.*). */
+fx_status fx_net_create(const char* fxweights_path, int patch, int max_batch, fx_precision precision, int device,
+                        fx_net** out);
+void fx_net_destroy(fx_net* net);
+/* Static net shape, like TrtNet's batch()/patch()/classes(). */
+int fx_net_patch(const fx_net* net);
+int fx_net_max_batch(const fx_net* net);
+int fx_net_classes(const fx_net* net);
+int fx_net_features(const fx_net* net, int* out, int cap); /* returns the stage count */
+
+/* fp8 only: record per-tensor activation amax over `n` host u8 patches ([n][P][P][P]) in a
+ * bf16 calibration forward, and fix every activation scale to running-max(amax) / 448. */
+fx_status fx_net_calibrate(fx_net* net, const uint8_t* host_patches, int n);
+/* Per-tensor activation scales after calibration (cap entries); returns the count. */
+int fx_net_act_scales(const fx_net* net, float* out, int cap);
+
+/* Forward `nb` device-resident u8 tiles ([nb][P][P][P]) through the net and write the selected
+ * class probability ([nb][P][P][P] f32, device). Each tile is z-scored on its own (norm_patch).
+ * `stream` is a cudaStream_t (NULL = the net's stream). */
+fx_status fx_net_forward(fx_net* net, const uint8_t* dev_tiles, int nb, float* dev_prob, int channel, int sigmoid,
+                         void* stream);
+
+/* Sliding-window prediction over a host-resident dense u8 volume [dz][dy][dx] (ZYX, x fastest).
+ * Outputs (either may be NULL): the normalised probability (f32) and its u8 encoding. */
+fx_status fx_predict_volume(fx_net* net, const uint8_t* host_vol, int64_t dz, int64_t dy, int64_t dx,
+                            const fx_infer_opts* opts, float* host_prob, uint8_t* host_u8);
+
+/* Same over a device-resident volume, restricted to the flat tile range [tile_begin, tile_end)
+ * of the z-major tile list (for z-slab sharding); accumulates into the caller's device
+ * accumulator `dev_acc` ([dz][dy][dx] f32, caller-zeroed) without finalising. */
+fx_status fx_predict_tiles_dev(fx_net* net, const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx,
+                               const fx_infer_opts* opts, int64_t tile_begin, int64_t tile_end, float* dev_acc,
+                               void* stream);
+
+/* ---- tiling math (host) ---- */
+/* Start positions along one axis; returns the count (writes at most cap). */
+int64_t fx_tile_starts(int64_t dim, int patch, double overlap, int64_t* out, int64_t cap);
+void fx_gaussian1d(int n, float* out);
+/* Accumulated Gaussian weight over [c0, c0+cn) of an axis of length dim. */
+void fx_weight_profile(const float* g, int patch, const int64_t* starts, int64_t nstarts, int64_t c0, int64_t cn,
+                       int64_t dim, float* out);
+
+/* ---- device kernels, for parity tests and custom drivers (device pointers) ---- */
+/* z-score `ntiles` tiles at the given origins of a device u8 volume into f32 [ntiles][P^3]. */
+fx_status fx_norm_tiles(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx, const int64_t* host_origins,
+                        int ntiles, int patch, float* dev_out, void* stream);
+/* One 3x3x3 conv (pad 1, stride 1 or 2, no bias) in f32 NCDHW device tensors, computed by the
+ * tcgen05 kernel in bf16 (or e4m3 with per-output-channel weight scales and a per-tensor input
+ * scale when fp8 != 0), f32 accumulate. Also writes per-channel mean and biased variance of the
+ * output per batch item into dev_stats [B][Cout][2] when non-NULL. */
+fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, const float* dev_w, int Cout,
+                    int stride, int fp8, float* dev_y, float* dev_stats, void* stream);
+/* nn::ConvTranspose3d(k=2, s=2) with bias, f32 NCDHW device tensors, bf16 or e4m3 operands. */
+fx_status fx_conv_transpose2(const float* dev_x, int B, int Cin, int D, int H, int W, const float* dev_w,
+                             const float* dev_bias, int Cout, int fp8, float* dev_y, void* stream);
+/* Normalise an f32 accumulator by the factorised weights and encode u8 (rows [z_begin, z_end)). */
+fx_status fx_accum_finalize(const float* dev_acc, int64_t dz, int64_t dy, int64_t dx, int64_t z_begin, int64_t z_end,
+                            const float* dev_wz, const float* dev_wy, const float* dev_wx, float* dev_prob,
+                            uint8_t* dev_u8, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FENIX_B200_H */
