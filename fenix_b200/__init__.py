@@ -51,6 +51,28 @@ class InferOpts(C.Structure):
     ]
 
 
+class SpiralParams(C.Structure):
+    """fx_spiral_params (include/fenix_b200_synth.h)."""
+
+    _fields_ = [
+        ("pitch", C.c_double),
+        ("thickness", C.c_double),
+        ("sheet_mean", C.c_double),
+        ("sheet_sd", C.c_double),
+        ("bg_mean", C.c_double),
+        ("bg_sd", C.c_double),
+        ("blur_sigma", C.c_double),
+        ("speckle_sd", C.c_double),
+    ]
+
+
+# Synthetic volumes of the benchmark configurations (spiral pitch / thickness / intensities).
+SPIRAL_CONFIG1 = dict(pitch=12, thickness=3, sheet_mean=170, sheet_sd=15, bg_mean=40, bg_sd=10, blur_sigma=1.0,
+                      speckle_sd=0.0)
+SPIRAL_CONFIG3 = dict(SPIRAL_CONFIG1, pitch=16, speckle_sd=8.0)
+SPIRAL_CONFIG5 = dict(SPIRAL_CONFIG1, pitch=14)
+
+
 def _sig(lib, name, res, args):
     f = getattr(lib, name)
     f.restype = res
@@ -87,6 +109,7 @@ def lib():
     _sig(L, "fx_conv3d", i32, [vp, i32, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp])
     _sig(L, "fx_conv_transpose2", i32, [vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp])
     _sig(L, "fx_accum_finalize", i32, [vp, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp])
+    _sig(L, "fx_synth_spiral", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
     _lib = L
     return L
 
@@ -129,6 +152,18 @@ def weight_profile(g: np.ndarray, patch: int, starts: np.ndarray, c0: int, cn: i
         dim,
         out.ctypes.data_as(C.POINTER(C.c_float)),
     )
+    return out
+
+
+def synth_spiral(shape, seed: int, params: dict | None = None, z_begin: int = 0, z_end: int | None = None) -> np.ndarray:
+    """Spiral-sheet synthetic CT [z_end-z_begin][dy][dx] u8 (deterministic; see fenix_b200_synth.h)."""
+    dz, dy, dx = shape
+    z_end = dz if z_end is None else z_end
+    p = SpiralParams(**(params or SPIRAL_CONFIG1))
+    out = np.empty((z_end - z_begin, dy, dx), dtype=np.uint8)
+    rc = lib().fx_synth_spiral(out.ctypes.data_as(C.POINTER(C.c_uint8)), dz, dy, dx, C.byref(p), seed, z_begin, z_end)
+    if rc != 0:
+        raise ValueError("fx_synth_spiral: bad arguments")
     return out
 
 

@@ -44,7 +44,7 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     BUILD.mkdir(exist_ok=True)
     nvcc = _nvcc()
     hdr = _newest_header()
-    sources = sorted(CSRC.glob("*.cu"))
+    sources = sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cpp")))
     jobs = []
     for src in sources:
         obj = BUILD / (src.stem + ".o")
@@ -69,7 +69,7 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     objs = [BUILD / (s.stem + ".o") for s in sources]
     if force or jobs or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [nvcc, *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(tmp), "-lcudart"]
+        cmd = [nvcc, *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(tmp), "-lcudart", "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

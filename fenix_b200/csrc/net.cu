@@ -440,11 +440,17 @@ Status Net::finalize_in(Layer& L, int nb, cudaStream_t s) {
 }
 
 // ---- forward -----------------------------------------------------------------------------------
+// Operand precision of one layer: e4m3 for fp8 nets once calibrated, except the first conv
+// (always bf16) and layers whose input channels do not fill whole e4m3 MMA K-steps (32).
+int Net::layer_q(const Layer& L, bool calib) const {
+    if (prec_ != 1 || calib || L.kind == Layer::kFirst) return 0;
+    return L.Cin % 32 == 0 ? 1 : 0;
+}
+
 Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
                     int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s) {
     if (nb < 1 || nb > Bmax_) return fail(kInvalid, "forward: batch out of range");
-    const int q = (prec_ == 1 && !calib) ? 1 : 0;
-    if (q == 1 && !calibrated_) return fail(kInvalid, "forward: fp8 net used before fx_net_calibrate");
+    if (prec_ == 1 && !calib && !calibrated_) return fail(kInvalid, "forward: fp8 net used before fx_net_calibrate");
     Status st;
     const ActGeom g0 = level(0);
     if ((st = cuda_status(cudaMemsetAsync(d_sums_, 0, sizeof(unsigned long long) * 2 * nb, s), "memset")).code) return st;
@@ -454,29 +460,33 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
             .code)
         return st;
     auto amax_slot = [&](int k) -> unsigned* { return calib ? d_amax_ + k : nullptr; };
-    const int cgq = q ? 16 : 8;
-    auto act_bs = [&](int lvl, int C) { return static_cast<int64_t>(C / cgq) * level(lvl).gs(); };
-    auto dest = [&](uint8_t* ptr, int lvl, int Cbuf, int g0off, float scale) {
+    auto qof = [&](const Layer& L) { return layer_q(L, calib); };
+    // bytes per batch item of a tensor of C channels at level lvl stored with precision q
+    auto bstride = [&](int lvl, int C, int q) { return static_cast<int64_t>(C / (q ? 16 : 8)) * level(lvl).gs(); };
+    // destination written for consumer layer `cons` (its precision and input scale)
+    auto dest = [&](uint8_t* ptr, int lvl, int Cbuf, int ch0, const Layer& cons) {
+        const int q = qof(cons);
         fxk::NormDest d{};
-        d.ptr = ptr + static_cast<int64_t>(g0off) * level(lvl).gs();
-        d.batch_stride = act_bs(lvl, Cbuf);
+        d.ptr = ptr + static_cast<int64_t>(ch0 / (q ? 16 : 8)) * level(lvl).gs();
+        d.batch_stride = bstride(lvl, Cbuf, q);
         d.group_stride = level(lvl).gs();
         d.fp8 = q;
-        d.qscale = q ? 1.f / scale : 1.f;
+        d.qscale = q ? 1.f / cons.in_scale : 1.f;
         return d;
     };
-    auto phase_dest = [&](int s, float scale) {
+    auto phase_dest = [&](int lvl, const Layer& cons) {
+        const int q = qof(cons);
         fxk::NormDest d{};
-        const ActGeom gn = level(s + 1);
-        d.ptr = ph_[s];
+        const ActGeom gn = level(lvl + 1);
+        d.ptr = ph_[lvl];
         d.phase = 1;
         d.pHp = gn.H + 2;
         d.pWp = gn.W + 2;
         d.phase_stride = gn.gs();
         d.group_stride = 8 * gn.gs();
-        d.batch_stride = static_cast<int64_t>(F_[s] / cgq) * d.group_stride;
+        d.batch_stride = static_cast<int64_t>(F_[lvl] / (q ? 16 : 8)) * d.group_stride;
         d.fp8 = q;
-        d.qscale = q ? 1.f / scale : 1.f;
+        d.qscale = q ? 1.f / cons.in_scale : 1.f;
         return d;
     };
     auto norm = [&](Layer& L, fxk::NormDest d0, fxk::NormDest d1, int slot) -> Status {
@@ -488,68 +498,65 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
                            "norm_act");
     };
     const fxk::NormDest none{};
-    auto s_of = [&](const Layer& L) { return L.in_scale; };
     // encoder
-    for (int st_ = 0; st_ < S_; ++st_) {
-        const ActGeom g = level(st_);
-        const int64_t pn_bs = static_cast<int64_t>(F_[st_] / 8) * g.gs();
+    for (int lv = 0; lv < S_; ++lv) {
+        const ActGeom g = level(lv);
+        const int64_t pn_bs = static_cast<int64_t>(F_[lv] / 8) * g.gs();
         for (int i = 0; i < nconv_; ++i) {
-            Layer& L = enc_[st_ * nconv_ + i];
-            const int qe = L.kind == Layer::kFirst ? 0 : q;
+            Layer& L = enc_[lv * nconv_ + i];
+            const int q = qof(L);
             const uint8_t* in;
             int64_t ibs, igs;
             if (L.kind == Layer::kFirst) {
                 in = l0_;
                 ibs = g0.gs();
                 igs = g0.gs();
-            } else if (i == 0) {  // stride-2: phase copy of the previous stage's output
-                in = ph_[st_ - 1];
+            } else if (i == 0) {  // stride 2: phase-split copy of the previous stage's output
+                in = ph_[lv - 1];
                 igs = 8 * g.gs();
-                ibs = static_cast<int64_t>(F_[st_ - 1] / cgq) * igs;
+                ibs = static_cast<int64_t>(F_[lv - 1] / (q ? 16 : 8)) * igs;
             } else {
-                in = act_[st_];
-                ibs = act_bs(st_, F_[st_]);
+                in = act_[lv];
+                ibs = bstride(lv, F_[lv], q);
                 igs = g.gs();
             }
-            if ((st = run_conv(L, qe, in, ibs, igs, pn_[st_], pn_bs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
-            const bool last = i == nconv_ - 1;
-            if (!last) {
-                const Layer& nxt = enc_[st_ * nconv_ + i + 1];
-                if ((st = norm(L, dest(act_[st_], st_, F_[st_], 0, s_of(nxt)), none, st_)).code) return st;
-            } else if (st_ < S_ - 1) {
-                const float scat = dec_[st_ * nconv_].in_scale;
-                const float sph = enc_[(st_ + 1) * nconv_].in_scale;
-                if ((st = norm(L, dest(cat_[st_], st_, 2 * F_[st_], F_[st_] / cgq, scat), phase_dest(st_, sph),
-                               S_ + st_))
+            if ((st = run_conv(L, q, in, ibs, igs, pn_[lv], pn_bs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
+            if (i < nconv_ - 1) {
+                if ((st = norm(L, dest(act_[lv], lv, F_[lv], 0, enc_[lv * nconv_ + i + 1]), none, lv)).code) return st;
+            } else if (lv < S_ - 1) {
+                const Layer& dcat = dec_[lv * nconv_];
+                if ((st = norm(L, dest(cat_[lv], lv, 2 * F_[lv], F_[lv], dcat), phase_dest(lv, enc_[(lv + 1) * nconv_]),
+                               S_ + lv))
                         .code)
                     return st;
             } else {
-                if ((st = norm(L, dest(act_[st_], st_, F_[st_], 0, s_of(up_[S_ - 2])), none, S_ + st_)).code) return st;
+                if ((st = norm(L, dest(act_[lv], lv, F_[lv], 0, up_[S_ - 2]), none, S_ + lv)).code) return st;
             }
         }
     }
     // decoder
-    for (int lvl = S_ - 2; lvl >= 0; --lvl) {
-        const ActGeom g = level(lvl);
-        Layer& U = up_[lvl];
-        const float scat = dec_[lvl * nconv_].in_scale;
-        if ((st = run_conv(U, q, act_[lvl + 1], act_bs(lvl + 1, F_[lvl + 1]), level(lvl + 1).gs(), cat_[lvl],
-                           act_bs(lvl, 2 * F_[lvl]), g.gs(), q, q ? 1.f / scat : 1.f, amax_slot(2 * S_ + lvl), nb, s))
+    for (int lv = S_ - 2; lv >= 0; --lv) {
+        const ActGeom g = level(lv);
+        Layer& U = up_[lv];
+        const Layer& dcat = dec_[lv * nconv_];
+        const int qu = qof(U), qc = qof(dcat);
+        if ((st = run_conv(U, qu, act_[lv + 1], bstride(lv + 1, F_[lv + 1], qu), level(lv + 1).gs(), cat_[lv],
+                           bstride(lv, 2 * F_[lv], qc), g.gs(), qc, qc ? 1.f / dcat.in_scale : 1.f,
+                           amax_slot(2 * S_ + lv), nb, s))
                 .code)
             return st;
-        const int64_t pn_bs = static_cast<int64_t>(F_[lvl] / 8) * g.gs();
+        const int64_t pn_bs = static_cast<int64_t>(F_[lv] / 8) * g.gs();
         for (int i = 0; i < nconv_; ++i) {
-            Layer& L = dec_[lvl * nconv_ + i];
-            const uint8_t* in = i == 0 ? cat_[lvl] : act_[lvl];
-            const int64_t ibs = i == 0 ? act_bs(lvl, 2 * F_[lvl]) : act_bs(lvl, F_[lvl]);
-            if ((st = run_conv(L, q, in, ibs, g.gs(), pn_[lvl], pn_bs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
-            const bool last = i == nconv_ - 1;
-            if (!last) {
-                const Layer& nxt = dec_[lvl * nconv_ + i + 1];
-                if ((st = norm(L, dest(act_[lvl], lvl, F_[lvl], 0, s_of(nxt)), none, 3 * S_ + lvl)).code) return st;
-            } else if (lvl > 0) {
-                if ((st = norm(L, dest(act_[lvl], lvl, F_[lvl], 0, s_of(up_[lvl - 1])), none, 4 * S_ + lvl)).code)
+            Layer& L = dec_[lv * nconv_ + i];
+            const int q = qof(L);
+            const uint8_t* in = i == 0 ? cat_[lv] : act_[lv];
+            const int64_t ibs = i == 0 ? bstride(lv, 2 * F_[lv], q) : bstride(lv, F_[lv], q);
+            if ((st = run_conv(L, q, in, ibs, g.gs(), pn_[lv], pn_bs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
+            if (i < nconv_ - 1) {
+                if ((st = norm(L, dest(act_[lv], lv, F_[lv], 0, dec_[lv * nconv_ + i + 1]), none, 3 * S_ + lv)).code)
                     return st;
+            } else if (lv > 0) {
+                if ((st = norm(L, dest(act_[lv], lv, F_[lv], 0, up_[lv - 1]), none, 4 * S_ + lv)).code) return st;
             } else {
                 if ((st = finalize_in(L, nb, s)).code) return st;
                 fxk::HeadParams h{};
@@ -638,7 +645,7 @@ Status Net::calibrate(const uint8_t* host_patches, int n) {
     set_scales_from_amax();
     for (auto* v : {&enc_, &up_, &dec_})
         for (Layer& L : *v) {
-            if (L.kind == Layer::kFirst) continue;
+            if (layer_q(L, false) != 1) continue;
             L.prog[1] = DevProgram{};
             if ((st = build_layer(L, 1)).code) return st;
         }

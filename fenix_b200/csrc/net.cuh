@@ -111,6 +111,7 @@ class Net {
                     cudaStream_t s);
     Status finalize_in(Layer& L, int nb, cudaStream_t s);
     Status set_scales_from_amax();
+    int layer_q(const Layer& L, bool calib) const;
     ActGeom level(int s) const { return {P_ >> s, P_ >> s, P_ >> s}; }
     void* dalloc(size_t bytes);
 

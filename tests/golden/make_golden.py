@@ -1,0 +1,99 @@
+"""Regenerate the golden fixtures in tests/golden/ from the REFERENCE's own code.
+
+Runs only where the reference tree is present (it compiles oracle/_ref from it):
+  * tiling_ref.npz  — tile starts, gaussian1d windows and accumulated weight profiles printed by
+                      oracle/_ref/ref_tiler_dump (the reference's src/ml/tiling.hpp and
+                      src/ml/global_accum.hpp), bit patterns kept exactly.
+  * net_<case>.npz  — the reference's CPU inference (oracle/_ref/ref_infer: predict_surface_filled
+                      + nets::ConvStack through libtorch, fp32, batch 2 so no fp16 round trip) on
+                      seeded synthetic volumes with seeded random-init plain UNets: the u8-encoded
+                      probability map, exact f32 values at 4096 sampled voxels, and sum / mean.
+
+usage: python tests/golden/make_golden.py [--only CASE]
+"""
+from __future__ import annotations
+
+import argparse
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+
+import fenix_b200 as fx  # noqa: E402
+from fenix_b200.weights import make_plain_unet  # noqa: E402
+from oracle import oracle as orc  # noqa: E402
+
+# name: (features, weight seed, volume shape, volume seed, spiral params, patch, overlap)
+CASES = {
+    "small3": ((16, 32, 64), 5, (72, 64, 80), 7, fx.SPIRAL_CONFIG1, 64, 0.5),
+    "cfg1_p64": ((16, 32, 64, 128), 0, (64, 96, 64), 11, fx.SPIRAL_CONFIG1, 64, 0.25),
+    "cfg2_p64": ((32, 64, 128, 256, 320), 1, (64, 64, 64), 1, fx.SPIRAL_CONFIG1, 64, 0.5),
+    "cfg3_p64": ((32, 64, 128, 256, 320), 2, (96, 96, 96), 2, fx.SPIRAL_CONFIG3, 64, 0.5),
+}
+
+
+def tiling():
+    out = subprocess.run([str(orc.REF / "ref_tiler_dump")], capture_output=True, text=True, check=True).stdout
+    d = {}
+    for line in out.splitlines():
+        head, vals = line.split(":", 1)
+        parts = head.split()
+        kind = parts[0]
+        key = "_".join(parts[1:])
+        vals = vals.split()
+        if kind == "starts":
+            d[f"starts_{key}"] = np.array([int(v) for v in vals], dtype=np.int64)
+        else:
+            d[f"{kind}_{key}"] = np.array([float.fromhex(v) for v in vals], dtype=np.float32)
+    np.savez_compressed(HERE / "tiling_ref.npz", **d)
+    print(f"tiling_ref.npz: {len(d)} arrays")
+
+
+def net_case(name):
+    feats, wseed, shape, vseed, sp, P, ov = CASES[name]
+    with tempfile.TemporaryDirectory() as td:
+        w = make_plain_unet(Path(td) / "w.fxweights", feats, nconv=2, ncls=2, seed=wseed)
+        vol = fx.synth_spiral(shape, vseed, sp)
+        prob, info = orc.ref_infer(w, vol, P, ov, batch=2)
+    rng = np.random.default_rng(1234)
+    idx = rng.choice(prob.size, size=min(4096, prob.size), replace=False).astype(np.int64)
+    np.savez_compressed(
+        HERE / f"net_{name}.npz",
+        u8=orc.prob_to_u8(prob),
+        sample_idx=idx,
+        sample_val=prob.reshape(-1)[idx],
+        prob_sum=np.float64(prob.astype(np.float64).sum()),
+        features=np.array(feats, dtype=np.int64),
+        weight_seed=np.int64(wseed),
+        shape=np.array(shape, dtype=np.int64),
+        volume_seed=np.int64(vseed),
+        spiral=np.array([sp[k] for k in ("pitch", "thickness", "sheet_mean", "sheet_sd", "bg_mean", "bg_sd",
+                                         "blur_sigma", "speckle_sd")]),
+        patch=np.int64(P),
+        overlap=np.float64(ov),
+        ref_seconds=np.float64(info["seconds"]),
+        ref_threads=np.int64(info["threads"]),
+    )
+    print(f"net_{name}.npz: shape {shape}, {info}")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default=None)
+    a = ap.parse_args()
+    subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "all", "ref"], check=True)
+    if a.only in (None, "tiling"):
+        tiling()
+    for name in CASES:
+        if a.only in (None, name):
+            net_case(name)
+
+
+if __name__ == "__main__":
+    main()
