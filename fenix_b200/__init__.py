@@ -28,7 +28,8 @@ STATUS_NAMES = {
     7: "unimplemented",
     8: "internal",
 }
-PREC_BF16, PREC_FP8 = 0, 1
+PREC_BF16, PREC_FP8, PREC_F16 = 0, 1, 2
+PRECISIONS = {"bf16": PREC_BF16, "fp8": PREC_FP8, "f16": PREC_F16}
 
 
 class FxError(RuntimeError):
@@ -173,12 +174,12 @@ def device_count() -> int:
 
 # ---- nets ----------------------------------------------------------------------------------
 class Net:
-    """A UNet on one GPU (fx_net). ``precision`` is "bf16" or "fp8"."""
+    """A UNet on one GPU (fx_net). ``precision`` is "f16", "bf16" or "fp8"."""
 
     def __init__(self, weights_path: str, patch: int, max_batch: int = 1, precision: str = "bf16", device: int = 0):
         L = lib()
         h = C.c_void_p()
-        prec = {"bf16": PREC_BF16, "fp8": PREC_FP8}[precision]
+        prec = PRECISIONS[precision]
         check(L.fx_net_create(str(weights_path).encode(), patch, max_batch, prec, device, C.byref(h)))
         self._h = h
         self.patch = patch

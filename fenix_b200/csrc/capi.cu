@@ -5,6 +5,7 @@
 #include "fenix_b200/ml/tiling.hpp"
 #include "net.cuh"
 #include "pack.cuh"
+#include "ptx.cuh"
 
 #include <cuda_runtime.h>
 
@@ -260,20 +261,24 @@ fx_status fx_norm_tiles(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t 
         cudaMemsetAsync(d_sums, 0, sizeof(unsigned long long) * 2 * ntiles, s);
         cudaError_t e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, s);
         if (e == cudaSuccess)
-            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, d_l0, g.gs(), dev_out, s);
+            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, d_l0, g.gs(), fxk::kOpF16,
+                                      dev_out, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles"));
     });
 }
 
 fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, const float* dev_w, int Cout, int stride,
-                    int fp8, float* dev_y, float* dev_stats, void* stream) {
+                    fx_precision precision, float* dev_y, float* dev_stats, void* stream) {
     return guarded([&]() -> fx_status {
         if (!dev_x || !dev_w || !dev_y || B < 1 || Cin < 1 || Cout < 1 || D < 1 || H < 1 || W < 1)
             return set_err(FX_INVALID_ARGUMENT, "fx_conv3d: bad argument");
         if (stride != 1 && stride != 2) return set_err(FX_INVALID_ARGUMENT, "fx_conv3d: stride must be 1 or 2");
         if (stride == 2 && (D % 2 || H % 2 || W % 2)) return set_err(FX_INVALID_ARGUMENT, "fx_conv3d: stride 2 needs even extents");
-        if (Cin == 1 && (stride != 1 || fp8)) return set_err(FX_UNSUPPORTED, "fx_conv3d: 1-channel input is bf16 stride 1");
+        if (precision < FX_PREC_BF16 || precision > FX_PREC_F16) return set_err(FX_INVALID_ARGUMENT, "fx_conv3d: bad precision");
+        const int q = static_cast<int>(precision);  // fx_precision values are the kernel's operand types
+        const bool fp8 = q == fxk::kOpE4M3;
+        if (Cin == 1 && (stride != 1 || fp8)) return set_err(FX_UNSUPPORTED, "fx_conv3d: 1-channel input is 16-bit stride 1");
         if (Cout % 16) return set_err(FX_UNSUPPORTED, "fx_conv3d: Cout must be a multiple of 16");
         if (!is_sm100()) return set_err(FX_UNSUPPORTED, "fx_conv3d: needs an sm_100 GPU");
         cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -287,13 +292,12 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
         L.w.resize(static_cast<size_t>(Cout) * Cin * 27);
         cudaMemcpyAsync(L.w.data(), dev_w, L.w.size() * sizeof(float), cudaMemcpyDeviceToHost, s);
         cudaStreamSynchronize(s);
-        const int q = fp8 ? 1 : 0;
-        const int cg = q ? 16 : 8;
+        const int cg = fp8 ? 16 : 8;
         if (Cin > 1 && Cin % (2 * cg)) return set_err(FX_UNSUPPORTED, "fx_conv3d: Cin must be a multiple of 16 (bf16) / 32 (fp8)");
         const fxh::ActGeom gin{D, H, W};
         const fxh::ActGeom gout{D / stride, H / stride, W / stride};
         const int64_t vin = static_cast<int64_t>(D) * H * W;
-        if (q) L.in_scale = std::max(device_absmax(dev_x, vin * B * Cin, s, sc), 1e-8f) / 448.f;
+        if (fp8) L.in_scale = std::max(device_absmax(dev_x, vin * B * Cin, s, sc), 1e-8f) / 448.f;
         std::vector<void*> allocs;
         struct Free {
             std::vector<void*>& a;
@@ -312,14 +316,14 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
             in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * ibs));
             if (!in) return set_err(FX_INTERNAL, "cudaMalloc failed");
             cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
-            fxk::launch_pack_first(dev_x, B, D, H, W, in, ibs, s);
+            fxk::launch_pack_first(dev_x, B, D, H, W, in, ibs, q, s);
         } else if (stride == 1) {
             igs = gin.gs();
             ibs = (Cin / cg) * igs;
             in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * ibs));
             if (!in) return set_err(FX_INTERNAL, "cudaMalloc failed");
             cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
-            fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, q ? 1.f / L.in_scale : 1.f, 0, 0, 0, 0, s);
+            fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, fp8 ? 1.f / L.in_scale : 1.f, 0, 0, 0, 0, s);
         } else {
             const int64_t ps = gout.gs();
             igs = 8 * ps;
@@ -327,7 +331,7 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
             in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * ibs));
             if (!in) return set_err(FX_INTERNAL, "cudaMalloc failed");
             cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
-            fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, q ? 1.f / L.in_scale : 1.f, 1, gout.H + 2,
+            fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, fp8 ? 1.f / L.in_scale : 1.f, 1, gout.H + 2,
                              gout.W + 2, ps, s);
         }
         const int64_t ogs = gout.gs(), obs = (Cout / 8) * ogs;
@@ -342,7 +346,7 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
         st = fxh::launch_layer(L, q, gin, gout, in, ibs, igs, out, obs, ogs, 0, 1.f, nullptr, B, sm_count_of_current(),
                                d_status, s);
         if (!st.ok()) return set_err(st);
-        fxk::launch_unpack(out, obs, ogs, 0, 1.f, B, Cout, gout.D, gout.H, gout.W, dev_y, s);
+        fxk::launch_unpack(out, obs, ogs, fxk::kOpF16, 1.f, B, Cout, gout.D, gout.H, gout.W, dev_y, s);
         cudaError_t e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "fx_conv3d"));
         uint32_t status = 0;
@@ -371,13 +375,16 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
 }
 
 fx_status fx_conv_transpose2(const float* dev_x, int B, int Cin, int D, int H, int W, const float* dev_w,
-                             const float* dev_bias, int Cout, int fp8, float* dev_y, void* stream) {
+                             const float* dev_bias, int Cout, fx_precision precision, float* dev_y, void* stream) {
     return guarded([&]() -> fx_status {
         if (!dev_x || !dev_w || !dev_bias || !dev_y || B < 1 || Cin < 1 || Cout < 1 || D < 1 || H < 1 || W < 1)
             return set_err(FX_INVALID_ARGUMENT, "fx_conv_transpose2: bad argument");
         if (!is_sm100()) return set_err(FX_UNSUPPORTED, "fx_conv_transpose2: needs an sm_100 GPU");
-        const int q = fp8 ? 1 : 0;
-        const int cg = q ? 16 : 8;
+        if (precision < FX_PREC_BF16 || precision > FX_PREC_F16)
+            return set_err(FX_INVALID_ARGUMENT, "fx_conv_transpose2: bad precision");
+        const int q = static_cast<int>(precision);
+        const bool fp8 = q == fxk::kOpE4M3;
+        const int cg = fp8 ? 16 : 8;
         if (Cin % (2 * cg) || Cout % 16)
             return set_err(FX_UNSUPPORTED, "fx_conv_transpose2: channel counts not supported");
         cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -395,7 +402,7 @@ fx_status fx_conv_transpose2(const float* dev_x, int B, int Cin, int D, int H, i
         cudaStreamSynchronize(s);
         const fxh::ActGeom gin{D, H, W}, gout{2 * D, 2 * H, 2 * W};
         const int64_t vin = static_cast<int64_t>(D) * H * W;
-        if (q) L.in_scale = std::max(device_absmax(dev_x, vin * B * Cin, s, sc), 1e-8f) / 448.f;
+        if (fp8) L.in_scale = std::max(device_absmax(dev_x, vin * B * Cin, s, sc), 1e-8f) / 448.f;
         std::vector<void*> allocs;
         struct Free {
             std::vector<void*>& a;
@@ -415,13 +422,13 @@ fx_status fx_conv_transpose2(const float* dev_x, int B, int Cin, int D, int H, i
         cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
         cudaMemsetAsync(out, 0, static_cast<size_t>(B) * obs, s);
         cudaMemsetAsync(d_status, 0, sizeof(uint32_t), s);
-        fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, q ? 1.f / L.in_scale : 1.f, 0, 0, 0, 0, s);
-        // fp8 output: scale from a bf16 dry run would need two passes; the test entry point
-        // writes bf16 output in both modes (operands still e4m3 when fp8).
-        st = fxh::launch_layer(L, q, gin, gout, in, ibs, igs, out, obs, ogs, 0, 1.f, d_amax, B, sm_count_of_current(),
-                               d_status, s);
+        fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, fp8 ? 1.f / L.in_scale : 1.f, 0, 0, 0, 0, s);
+        // This entry point writes f16 output cells whatever the operand type (an e4m3 output
+        // would need its scale before the run).
+        st = fxh::launch_layer(L, q, gin, gout, in, ibs, igs, out, obs, ogs, fxk::kOpF16, 1.f, d_amax, B,
+                               sm_count_of_current(), d_status, s);
         if (!st.ok()) return set_err(st);
-        fxk::launch_unpack(out, obs, ogs, 0, 1.f, B, Cout, gout.D, gout.H, gout.W, dev_y, s);
+        fxk::launch_unpack(out, obs, ogs, fxk::kOpF16, 1.f, B, Cout, gout.D, gout.H, gout.W, dev_y, s);
         cudaError_t e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "fx_conv_transpose2"));
         uint32_t status = 0;

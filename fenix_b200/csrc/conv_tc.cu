@@ -119,9 +119,9 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
                         for (int n0 = 0; n0 < p.N_tile; n0 += 256) {
                             const int nn = p.N_tile - n0 < 256 ? p.N_tile - n0 : 256;
                             const uint64_t bdesc = smem_desc(sb + mm.b_off + n0 * 16, b_lbo, 128);
-                            const uint32_t idesc = instr_desc(128, nn, p.fp8 != 0);
+                            const uint32_t idesc = instr_desc(128, nn, p.optype);
                             const uint32_t d = dcol0 + r * p.N_tile + n0;
-                            if (p.fp8)
+                            if (p.optype == kOpE4M3)
                                 mma_f8(d, adesc, bdesc, idesc, first ? 0u : 1u);
                             else
                                 mma_f16(d, adesc, bdesc, idesc, first ? 0u : 1u);
@@ -220,14 +220,8 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                         uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + row * 16 +
                                      static_cast<int64_t>(n0 / 8) * p.out_group_stride;
 #pragma unroll
-                        for (int g = 0; g < 2; ++g) {
-                            uint4 w;
-                            w.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-                            w.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-                            w.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-                            w.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-                            *reinterpret_cast<uint4*>(o + g * p.out_group_stride) = w;
-                        }
+                        for (int g = 0; g < 2; ++g)
+                            *reinterpret_cast<uint4*>(o + g * p.out_group_stride) = pack_cell16(v + g * 8, kOpF16);
                     }
                     float q[16];
 #pragma unroll
@@ -258,7 +252,7 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                     const int64_t orow =
                         ((2 * zi - 1 + az) * static_cast<int64_t>(p.oHp) + (2 * yi - 1 + ay)) * p.oWp + (2 * xi - 1 + ax);
                     uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + orow * 16;
-                    if (p.out_fp8) {
+                    if (p.out_type == kOpE4M3) {
                         const float s = p.out_qscale;
                         uint4 w;
                         w.x = pack_e4m3x4(v[0] * s, v[1] * s, v[2] * s, v[3] * s);
@@ -268,14 +262,9 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                         *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 16) * p.out_group_stride) = w;
                     } else {
 #pragma unroll
-                        for (int g = 0; g < 2; ++g) {
-                            uint4 w;
-                            w.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-                            w.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-                            w.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-                            w.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-                            *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 8 + g) * p.out_group_stride) = w;
-                        }
+                        for (int g = 0; g < 2; ++g)
+                            *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 8 + g) * p.out_group_stride) =
+                                pack_cell16(v + g * 8, p.out_type);
                     }
                 }
             }

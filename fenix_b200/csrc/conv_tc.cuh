@@ -22,6 +22,8 @@
 
 #include <cstdint>
 
+#include "optype.cuh"
+
 namespace fxk {
 
 constexpr int kConvThreads = 192;
@@ -51,7 +53,7 @@ struct ConvSrc {
 };
 
 enum ConvMode : int32_t {
-    kModePrenorm = 0,  // store bf16 pre-norm output, emit per-channel sum / sum of squares
+    kModePrenorm = 0,  // store f16 pre-norm output, emit per-channel sum / sum of squares
     kModeUpsample = 1, // transposed conv: + bias, scatter 8 phases into the 2x finer grid
 };
 
@@ -62,7 +64,7 @@ struct ConvParams {
     const uint8_t* wpack;  // packed B blocks of N tile 0; tile t starts at + t * wtile_bytes
     int64_t wtile_bytes;
     int32_t n_stages;
-    int32_t fp8;  // operands are e4m3 (kind::f8f6f4) instead of bf16 (kind::f16)
+    int32_t optype;  // OpType of both operands: bf16 / f16 (kind::f16) or e4m3 (kind::f8f6f4)
 
     // output-row space of one batch item: the padded geometry rows are indexed in
     int32_t batch;
@@ -84,7 +86,7 @@ struct ConvParams {
     const float* bias;       // per output channel bias (upsample mode) or null
     uint8_t* out;            // output tensor, group 0 of the written channel slice, batch 0
     int64_t out_batch_stride, out_group_stride;  // bytes
-    int32_t out_fp8;         // upsample mode: write e4m3 (scaled by out_qscale) instead of bf16
+    int32_t out_type;        // upsample mode: OpType of the written cells (e4m3 scaled by out_qscale)
     float out_qscale;
     int32_t cout;            // upsample mode: channels per phase
     int32_t oHp, oWp;        // upsample mode: padded H, W of the output grid

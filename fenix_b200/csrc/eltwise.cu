@@ -79,7 +79,7 @@ __device__ __forceinline__ void build_lut(float* lut, unsigned long long S, unsi
 __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, int64_t dy, int64_t dx,
                                  const TileOrigin* __restrict__ tiles, int P,
                                  const unsigned long long* __restrict__ sums, uint8_t* __restrict__ l0,
-                                 int64_t l0_batch_stride, float* __restrict__ f32_out) {
+                                 int64_t l0_batch_stride, int l0_type, float* __restrict__ f32_out) {
     const int b = blockIdx.y;
     __shared__ float lut[256];
     const int64_t n = static_cast<int64_t>(P) * P * P;
@@ -107,12 +107,10 @@ __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, in
             }
         }
         const int64_t row = (static_cast<int64_t>(z + 1) * Pp + (y + 1)) * Pp + (x + 1);
-        uint4 w;
-        w.x = pack_bf16x2(v[0], v[1]);
-        w.y = pack_bf16x2(v[2], 0.f);
-        w.z = 0u;
-        w.w = 0u;
-        *reinterpret_cast<uint4*>(l0 + b * l0_batch_stride + row * 16) = w;
+        if (l0) {
+            const float cell[8] = {v[0], v[1], v[2], 0.f, 0.f, 0.f, 0.f, 0.f};
+            *reinterpret_cast<uint4*>(l0 + b * l0_batch_stride + row * 16) = pack_cell16(cell, l0_type);
+        }
         if (f32_out) f32_out[b * n + i] = v[1];
     }
 }
@@ -155,15 +153,6 @@ __global__ void in_finalize_kernel(const float* __restrict__ partials, int nrec,
     }
 }
 
-__device__ __forceinline__ void unpack_bf16x8(const uint4 w, float (&f)[8]) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 t = __bfloat1622float2(h[i]);
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
-    }
-}
 
 __device__ __forceinline__ void store_dest(const NormDest& d, int b, int gout, int64_t row, int zp, int yp, int xp,
                                            const float* y, int n) {
@@ -177,22 +166,17 @@ __device__ __forceinline__ void store_dest(const NormDest& d, int b, int gout, i
         off = row * 16;
     }
     uint8_t* o = d.ptr + b * d.batch_stride + gout * d.group_stride + off;
-    uint4 w;
-    if (d.fp8) {  // n == 16
+    if (d.dtype == kOpE4M3) {  // n == 16
         const float s = d.qscale;
+        uint4 w;
         w.x = pack_e4m3x4(y[0] * s, y[1] * s, y[2] * s, y[3] * s);
         w.y = pack_e4m3x4(y[4] * s, y[5] * s, y[6] * s, y[7] * s);
         w.z = pack_e4m3x4(y[8] * s, y[9] * s, y[10] * s, y[11] * s);
         w.w = pack_e4m3x4(y[12] * s, y[13] * s, y[14] * s, y[15] * s);
         *reinterpret_cast<uint4*>(o) = w;
     } else {  // 8 channels per cell; n == 8 or 16 (then two cells)
-        for (int c0 = 0; c0 < n; c0 += 8) {
-            w.x = pack_bf16x2(y[c0 + 0], y[c0 + 1]);
-            w.y = pack_bf16x2(y[c0 + 2], y[c0 + 3]);
-            w.z = pack_bf16x2(y[c0 + 4], y[c0 + 5]);
-            w.w = pack_bf16x2(y[c0 + 6], y[c0 + 7]);
-            *reinterpret_cast<uint4*>(o + (c0 / 8) * d.group_stride) = w;
-        }
+        for (int c0 = 0; c0 < n; c0 += 8)
+            *reinterpret_cast<uint4*>(o + (c0 / 8) * d.group_stride) = pack_cell16(y + c0, d.dtype);
     }
 }
 
@@ -223,7 +207,7 @@ __global__ void norm_act_kernel(const uint8_t* __restrict__ pre, int64_t pbs, in
         for (int k = 0; k < cpt / 8; ++k) {
             const uint4 w = *reinterpret_cast<const uint4*>(pre + b * pbs + (gi0 + k) * pgs + row * 16);
             float f[8];
-            unpack_bf16x8(w, f);
+            unpack_cell16(w, kOpF16, f);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int c = (gi0 + k) * 8 + j;
@@ -234,8 +218,8 @@ __global__ void norm_act_kernel(const uint8_t* __restrict__ pre, int64_t pbs, in
                 mx = fmaxf(mx, fabsf(yv));
             }
         }
-        store_dest(d0, b, d0.fp8 ? go : gi0, row, zp, yp, xp, v, cpt);
-        store_dest(d1, b, d1.fp8 ? go : gi0, row, zp, yp, xp, v, cpt);
+        store_dest(d0, b, d0.dtype == kOpE4M3 ? go : gi0, row, zp, yp, xp, v, cpt);
+        store_dest(d1, b, d1.dtype == kOpE4M3 ? go : gi0, row, zp, yp, xp, v, cpt);
     }
     if (amax) {
         for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -263,7 +247,7 @@ __global__ void head_blend_kernel(HeadParams h) {
             const uint4 w = *reinterpret_cast<const uint4*>(h.pre + b * h.pre_batch_stride + gi * h.pre_group_stride +
                                                             row * 16);
             float f[8];
-            unpack_bf16x8(w, f);
+            unpack_cell16(w, kOpF16, f);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int c = gi * 8 + j;
@@ -342,11 +326,11 @@ cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
 
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
                              int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
-                             float* f32_out, cudaStream_t s) {
+                             int l0_type, float* f32_out, cudaStream_t s) {
     const int64_t n = static_cast<int64_t>(P) * P * P;
     int gx = grid_for(n, kEwThreads * 4);
     tile_norm_kernel<<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums, l0, l0_batch_stride,
-                                                             f32_out);
+                                                             l0_type, f32_out);
     return cudaGetLastError();
 }
 
@@ -358,7 +342,7 @@ cudaError_t launch_in_finalize(const float* partials, int B, int nrec, int C, do
 
 cudaError_t launch_norm_act(const uint8_t* pre, int64_t pbs, int64_t pgs, GridGeom g, int C, int B, const float* ss,
                             float slope, NormDest d0, NormDest d1, unsigned* amax, cudaStream_t s) {
-    const bool any_fp8 = (d0.ptr && d0.fp8) || (d1.ptr && d1.fp8);
+    const bool any_fp8 = (d0.ptr && d0.dtype == kOpE4M3) || (d1.ptr && d1.dtype == kOpE4M3);
     const int cpt = (any_fp8 || C % 16 == 0) ? 16 : 8;
     const int64_t total = static_cast<int64_t>(g.D) * g.H * g.W * (C / cpt) * B;
     norm_act_kernel<<<grid_for(total, kEwThreads), kEwThreads, 0, s>>>(pre, pbs, pgs, g, C, B, ss, slope, d0, d1,

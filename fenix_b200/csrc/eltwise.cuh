@@ -24,12 +24,13 @@ struct TileOrigin {
 cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
                              int ntiles, int P, unsigned long long* sums, cudaStream_t s);
 // Writes the first conv's input for every tile: each interior voxel's 16-byte cell holds the
-// z-scored values at x-1, x, x+1 (zero outside the tile) as bf16, then five zeros. The z-score
+// z-scored values at x-1, x, x+1 (zero outside the tile) as 16-bit floats, then five zeros. The z-score
 // goes through a 256-entry table built with the reference's double-precision expression, so
 // the normalised value of each u8 level is the same float the reference computes.
+// `l0_type` is the first conv's operand type (kOpBF16 or kOpF16); l0 may be null.
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
                              int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
-                             float* f32_out, cudaStream_t s);
+                             int l0_type, float* f32_out, cudaStream_t s);
 
 // ---- InstanceNorm ----------------------------------------------------------------------------
 // partials [B][nrec][C][2] -> ss [B][C][2] = {scale, shift} with scale = gamma * rstd and
@@ -41,14 +42,14 @@ struct NormDest {
     uint8_t* ptr;          // group 0 of the written slice, batch 0 (null = unused)
     int64_t batch_stride;  // bytes
     int64_t group_stride;  // bytes
-    int32_t fp8;           // 1: e4m3 scaled by qscale, 0: bf16
+    int32_t dtype;         // OpType of the written cells (e4m3 values are y * qscale)
     float qscale;
     int32_t phase;         // 1: write the stride-2 phase-split copy (8 parity sub-volumes)
     int32_t pHp, pWp;      // phase sub-volume padded H, W (= output grid of the stride-2 conv)
     int64_t phase_stride;  // bytes between parity sub-volumes
 };
 
-// y = leaky_relu(x * scale[c] + shift[c], slope) over the interior of a bf16 pre-norm tensor,
+// y = leaky_relu(x * scale[c] + shift[c], slope) over the interior of an f16 pre-norm tensor,
 // written to up to two destinations; optionally records max |y| into *amax (float bits).
 cudaError_t launch_norm_act(const uint8_t* pre, int64_t pre_batch_stride, int64_t pre_group_stride, GridGeom g,
                             int C, int B, const float* ss, float slope, NormDest d0, NormDest d1, unsigned* amax,

@@ -150,6 +150,7 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     DevProgram& dp = L.prog[q];
     ProgramSpec sp;
     const bool fp8 = q == 1;
+    sp.optype = q;
     sp.elem = fp8 ? 1 : 2;
     sp.cg = fp8 ? 16 : 8;
     const int Bmax_ = Bmax, sm_count_ = sm_count;
@@ -175,7 +176,7 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     }
     std::vector<float> colscale;
     if (L.kind == Layer::kFirst) {
-        if (fp8) return fail(kInternal, "first layer runs in bf16");
+        if (fp8) return fail(kInternal, "first layer runs with 16-bit operands");
         sp.G = 1;
         sp.pair_taps = true;
         const ActGeom g = gout;
@@ -262,7 +263,7 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     dp.acc_slots = slots;
     dp.tmem_cols = cols;
     dp.n_units_m = static_cast<int>((rows + 128 * R - 1) / (128 * R));
-    dp.fp8 = fp8;
+    dp.optype = q;
     if ((st = upload(dp.stages, dp.host.stages, this_net, allocs_)).code) return st;
     if ((st = upload(dp.mmas, dp.host.mmas, this_net, allocs_)).code) return st;
     if ((st = upload(dp.wpack, dp.host.wpack, this_net, allocs_)).code) return st;
@@ -334,7 +335,7 @@ Status Net::create(const std::string& path, int patch, int max_batch, int precis
     prec_ = precision;
     dev_ = device;
     if (patch <= 0 || max_batch <= 0) return fail(kInvalid, "net: patch and max_batch must be positive");
-    if (precision != 0 && precision != 1) return fail(kInvalid, "net: precision must be bf16 (0) or fp8 (1)");
+    if (precision < 0 || precision > 2) return fail(kInvalid, "net: precision must be bf16 (0), fp8 (1) or f16 (2)");
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
         return fail(kInvalid, "net: CUDA device " + std::to_string(device) + " not available");
@@ -358,21 +359,21 @@ Status Net::create(const std::string& path, int patch, int max_batch, int precis
     if ((st = alloc()).code) return st;
     for (auto* v : {&enc_, &up_, &dec_})
         for (Layer& L : *v)
-            if ((st = build_layer(L, 0)).code) return st;
+            if ((st = build_layer(L, t16())).code) return st;
     amax_.assign(5 * S_, 0.f);
     return ok();
 }
 
 // ---- one conv launch ----------------------------------------------------------------------
 Status Net::run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs, uint8_t* out_ptr,
-                     int64_t out_bs, int64_t out_gs, int out_fp8, float out_qscale, unsigned* amax, int nb,
+                     int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax, int nb,
                      cudaStream_t s) {
-    return launch_layer(L, q, level(L.lin), level(L.lout), in_ptr, in_bs, in_gs, out_ptr, out_bs, out_gs, out_fp8,
+    return launch_layer(L, q, level(L.lin), level(L.lout), in_ptr, in_bs, in_gs, out_ptr, out_bs, out_gs, out_type,
                         out_qscale, amax, nb, sm_count_, d_status_, s);
 }
 
 Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
-                    uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_fp8, float out_qscale, unsigned* amax,
+                    uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax,
                     int nb, int sm_count_, uint32_t* d_status_, cudaStream_t s) {
     DevProgram& dp = L.prog[q];
     if (!dp.built) return fail(kInternal, L.name + ": program not built");
@@ -389,7 +390,7 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     p.wpack = dp.wpack;
     p.wtile_bytes = dp.host.wtile_bytes;
     p.n_stages = static_cast<int32_t>(dp.host.stages.size());
-    p.fp8 = dp.fp8 ? 1 : 0;
+    p.optype = dp.optype;
     p.batch = nb;
     p.Dp = rs.D + 2;
     p.Hp = rs.H + 2;
@@ -414,7 +415,7 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     if (L.kind == Layer::kUp) {
         p.mode = fxk::kModeUpsample;
         p.bias = dp.bias;
-        p.out_fp8 = out_fp8;
+        p.out_type = out_type;
         p.out_qscale = out_qscale;
         p.cout = L.Cout;
         p.oHp = gout.H + 2;
@@ -443,8 +444,8 @@ Status Net::finalize_in(Layer& L, int nb, cudaStream_t s) {
 // Operand precision of one layer: e4m3 for fp8 nets once calibrated, except the first conv
 // (always bf16) and layers whose input channels do not fill whole e4m3 MMA K-steps (32).
 int Net::layer_q(const Layer& L, bool calib) const {
-    if (prec_ != 1 || calib || L.kind == Layer::kFirst) return 0;
-    return L.Cin % 32 == 0 ? 1 : 0;
+    if (prec_ != 1 || calib || L.kind == Layer::kFirst) return t16();
+    return L.Cin % 32 == 0 ? fxk::kOpE4M3 : t16();
 }
 
 Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
@@ -455,23 +456,25 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
     const ActGeom g0 = level(0);
     if ((st = cuda_status(cudaMemsetAsync(d_sums_, 0, sizeof(unsigned long long) * 2 * nb, s), "memset")).code) return st;
     if ((st = cuda_status(fxk::launch_tile_sums(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, s), "tile_sums")).code) return st;
-    if ((st = cuda_status(fxk::launch_tile_norm(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, l0_, g0.gs(), nullptr, s),
+    if ((st = cuda_status(fxk::launch_tile_norm(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, l0_, g0.gs(), t16(), nullptr,
+                                                s),
                           "tile_norm"))
             .code)
         return st;
     auto amax_slot = [&](int k) -> unsigned* { return calib ? d_amax_ + k : nullptr; };
     auto qof = [&](const Layer& L) { return layer_q(L, calib); };
     // bytes per batch item of a tensor of C channels at level lvl stored with precision q
-    auto bstride = [&](int lvl, int C, int q) { return static_cast<int64_t>(C / (q ? 16 : 8)) * level(lvl).gs(); };
+    auto cgof = [](int q) { return q == fxk::kOpE4M3 ? 16 : 8; };
+    auto bstride = [&](int lvl, int C, int q) { return static_cast<int64_t>(C / cgof(q)) * level(lvl).gs(); };
     // destination written for consumer layer `cons` (its precision and input scale)
     auto dest = [&](uint8_t* ptr, int lvl, int Cbuf, int ch0, const Layer& cons) {
         const int q = qof(cons);
         fxk::NormDest d{};
-        d.ptr = ptr + static_cast<int64_t>(ch0 / (q ? 16 : 8)) * level(lvl).gs();
+        d.ptr = ptr + static_cast<int64_t>(ch0 / cgof(q)) * level(lvl).gs();
         d.batch_stride = bstride(lvl, Cbuf, q);
         d.group_stride = level(lvl).gs();
-        d.fp8 = q;
-        d.qscale = q ? 1.f / cons.in_scale : 1.f;
+        d.dtype = q;
+        d.qscale = q == fxk::kOpE4M3 ? 1.f / cons.in_scale : 1.f;
         return d;
     };
     auto phase_dest = [&](int lvl, const Layer& cons) {
@@ -484,9 +487,9 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
         d.pWp = gn.W + 2;
         d.phase_stride = gn.gs();
         d.group_stride = 8 * gn.gs();
-        d.batch_stride = static_cast<int64_t>(F_[lvl] / (q ? 16 : 8)) * d.group_stride;
-        d.fp8 = q;
-        d.qscale = q ? 1.f / cons.in_scale : 1.f;
+        d.batch_stride = static_cast<int64_t>(F_[lvl] / cgof(q)) * d.group_stride;
+        d.dtype = q;
+        d.qscale = q == fxk::kOpE4M3 ? 1.f / cons.in_scale : 1.f;
         return d;
     };
     auto norm = [&](Layer& L, fxk::NormDest d0, fxk::NormDest d1, int slot) -> Status {
@@ -514,7 +517,7 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
             } else if (i == 0) {  // stride 2: phase-split copy of the previous stage's output
                 in = ph_[lv - 1];
                 igs = 8 * g.gs();
-                ibs = static_cast<int64_t>(F_[lv - 1] / (q ? 16 : 8)) * igs;
+                ibs = static_cast<int64_t>(F_[lv - 1] / cgof(q)) * igs;
             } else {
                 in = act_[lv];
                 ibs = bstride(lv, F_[lv], q);
@@ -541,7 +544,7 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
         const Layer& dcat = dec_[lv * nconv_];
         const int qu = qof(U), qc = qof(dcat);
         if ((st = run_conv(U, qu, act_[lv + 1], bstride(lv + 1, F_[lv + 1], qu), level(lv + 1).gs(), cat_[lv],
-                           bstride(lv, 2 * F_[lv], qc), g.gs(), qc, qc ? 1.f / dcat.in_scale : 1.f,
+                           bstride(lv, 2 * F_[lv], qc), g.gs(), qc, qc == fxk::kOpE4M3 ? 1.f / dcat.in_scale : 1.f,
                            amax_slot(2 * S_ + lv), nb, s))
                 .code)
             return st;
@@ -645,7 +648,7 @@ Status Net::calibrate(const uint8_t* host_patches, int n) {
     set_scales_from_amax();
     for (auto* v : {&enc_, &up_, &dec_})
         for (Layer& L : *v) {
-            if (layer_q(L, false) != 1) continue;
+            if (layer_q(L, false) != fxk::kOpE4M3) continue;
             L.prog[1] = DevProgram{};
             if ((st = build_layer(L, 1)).code) return st;
         }

@@ -47,7 +47,8 @@ struct DevProgram {
     int R = 1, N_tile = 0, acc_slots = 1, n_units_m = 0;
     uint32_t tmem_cols = 32;
     ActGeom rowspace;  // output grid (conv) or input grid (transposed conv)
-    bool fp8 = false, built = false;
+    int optype = 0;    // fxk::OpType of the operands
+    bool built = false;
     size_t smem() const { return static_cast<size_t>(host.n_pipe) * host.stage_bytes + 1024; }
 };
 
@@ -61,7 +62,7 @@ struct Layer {
     std::vector<float> gamma, beta;   // InstanceNorm affine
     std::vector<float> wscale;        // fp8 per-output-channel weight scale (amax / 448)
     float in_scale = 1.f;             // fp8 per-tensor scale of the input activation
-    DevProgram prog[2];               // [0] bf16, [1] e4m3
+    DevProgram prog[3];               // indexed by fxk::OpType: bf16, e4m3, f16
     float* d_gamma = nullptr;
     float* d_beta = nullptr;
     float* d_partials = nullptr;      // [Bmax][n_units_m][4][Cout][2]
@@ -69,14 +70,14 @@ struct Layer {
     int nrec = 0;
 };
 
-// Compile one layer's program for precision q (0 bf16, 1 e4m3) and upload it; gin/gout are
+// Compile one layer's program for operand type q (fxk::OpType) and upload it; gin/gout are
 // the input and output grids. Device buffers are appended to `allocs` (owned by the caller).
 Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax, int sm_count,
                            std::vector<void*>& allocs);
 // Launch one layer. Stride-2 convs read the phase-split copy (gout geometry per phase); the
 // prenorm mode writes L.d_partials and sets L.nrec.
 Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
-                    uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_fp8, float out_qscale, unsigned* amax,
+                    uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax,
                     int nb, int sm_count, uint32_t* d_status, cudaStream_t s);
 
 class Net {
@@ -97,6 +98,7 @@ class Net {
     int classes() const { return ncls_; }
     const std::vector<int>& features() const { return F_; }
     int precision() const { return prec_; }
+    int t16() const { return prec_ == 0 ? 0 : 2; }  // 16-bit operand type: bf16 nets bf16, else f16
     int device() const { return dev_; }
     cudaStream_t stream() const { return stream_; }
     bool calibrated() const { return calibrated_; }
@@ -107,7 +109,7 @@ class Net {
     Status alloc();
     Status build_layer(Layer& L, int q);
     Status run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs, uint8_t* out_ptr,
-                    int64_t out_bs, int64_t out_gs, int out_fp8, float out_qscale, unsigned* amax, int nb,
+                    int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax, int nb,
                     cudaStream_t s);
     Status finalize_in(Layer& L, int nb, cudaStream_t s);
     Status set_scales_from_amax();

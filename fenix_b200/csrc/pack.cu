@@ -3,6 +3,7 @@
 #include "ptx.cuh"
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
 namespace fxk {
@@ -17,7 +18,8 @@ int grid_for(int64_t n, int threads) {
 }
 
 __global__ void pack_kernel(const float* __restrict__ x, int B, int C, int D, int H, int W, uint8_t* out,
-                            int64_t bs, int64_t gs, int fp8, float qs, int phase, int pHp, int pWp, int64_t ps) {
+                            int64_t bs, int64_t gs, int dtype, float qs, int phase, int pHp, int pWp, int64_t ps) {
+    const bool fp8 = dtype == kOpE4M3;
     const int cg = fp8 ? 16 : 8;
     const int G = (C + cg - 1) / cg;
     const int64_t vox = static_cast<int64_t>(D) * H * W;
@@ -52,16 +54,14 @@ __global__ void pack_kernel(const float* __restrict__ x, int B, int C, int D, in
             w.z = pack_e4m3x4(f[8] * qs, f[9] * qs, f[10] * qs, f[11] * qs);
             w.w = pack_e4m3x4(f[12] * qs, f[13] * qs, f[14] * qs, f[15] * qs);
         } else {
-            w.x = pack_bf16x2(f[0], f[1]);
-            w.y = pack_bf16x2(f[2], f[3]);
-            w.z = pack_bf16x2(f[4], f[5]);
-            w.w = pack_bf16x2(f[6], f[7]);
+            w = pack_cell16(f, dtype);
         }
         *reinterpret_cast<uint4*>(out + b * bs + g * gs + off) = w;
     }
 }
 
-__global__ void pack_first_kernel(const float* __restrict__ x, int B, int D, int H, int W, uint8_t* out, int64_t bs) {
+__global__ void pack_first_kernel(const float* __restrict__ x, int B, int D, int H, int W, uint8_t* out, int64_t bs,
+                                  int dtype) {
     const int64_t vox = static_cast<int64_t>(D) * H * W;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vox * B;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -74,18 +74,16 @@ __global__ void pack_first_kernel(const float* __restrict__ x, int B, int D, int
         const float a = xx > 0 ? row[xx - 1] : 0.f;
         const float c = row[xx];
         const float d = xx + 1 < W ? row[xx + 1] : 0.f;
-        uint4 w;
-        w.x = pack_bf16x2(a, c);
-        w.y = pack_bf16x2(d, 0.f);
-        w.z = 0u;
-        w.w = 0u;
+        const float cell[8] = {a, c, d, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const uint4 w = pack_cell16(cell, dtype);
         const int64_t r = ((static_cast<int64_t>(zz + 1) * (H + 2) + (yy + 1)) * (W + 2) + (xx + 1));
         *reinterpret_cast<uint4*>(out + b * bs + r * 16) = w;
     }
 }
 
-__global__ void unpack_kernel(const uint8_t* __restrict__ in, int64_t bs, int64_t gs, int fp8, float scale, int B,
+__global__ void unpack_kernel(const uint8_t* __restrict__ in, int64_t bs, int64_t gs, int dtype, float scale, int B,
                               int C, int D, int H, int W, float* __restrict__ y) {
+    const bool fp8 = dtype == kOpE4M3;
     const int cg = fp8 ? 16 : 8;
     const int64_t vox = static_cast<int64_t>(D) * H * W;
     const int64_t total = vox * C * B;
@@ -105,9 +103,10 @@ __global__ void unpack_kernel(const uint8_t* __restrict__ in, int64_t bs, int64_
             __nv_fp8_e4m3 q;
             q.__x = cell[c % cg];
             val = static_cast<float>(q) * scale;
+        } else if (dtype == kOpF16) {
+            val = __half2float(reinterpret_cast<const __half*>(cell)[c % cg]);
         } else {
-            __nv_bfloat16 h = reinterpret_cast<const __nv_bfloat16*>(cell)[c % cg];
-            val = __bfloat162float(h);
+            val = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(cell)[c % cg]);
         }
         y[i] = val;
     }
@@ -125,23 +124,24 @@ __global__ void absmax_kernel(const float* __restrict__ x, int64_t n, unsigned* 
 }  // namespace
 
 cudaError_t launch_pack(const float* x, int B, int C, int D, int H, int W, uint8_t* out, int64_t bs, int64_t gs,
-                        int fp8, float qs, int phase, int pHp, int pWp, int64_t ps, cudaStream_t s) {
-    const int cg = fp8 ? 16 : 8;
+                        int dtype, float qs, int phase, int pHp, int pWp, int64_t ps, cudaStream_t s) {
+    const int cg = dtype == kOpE4M3 ? 16 : 8;
     const int64_t total = static_cast<int64_t>(D) * H * W * ((C + cg - 1) / cg) * B;
-    pack_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, B, C, D, H, W, out, bs, gs, fp8, qs, phase, pHp, pWp, ps);
+    pack_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, B, C, D, H, W, out, bs, gs, dtype, qs, phase, pHp, pWp, ps);
     return cudaGetLastError();
 }
 
-cudaError_t launch_pack_first(const float* x, int B, int D, int H, int W, uint8_t* out, int64_t bs, cudaStream_t s) {
+cudaError_t launch_pack_first(const float* x, int B, int D, int H, int W, uint8_t* out, int64_t bs, int dtype,
+                              cudaStream_t s) {
     const int64_t total = static_cast<int64_t>(D) * H * W * B;
-    pack_first_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, B, D, H, W, out, bs);
+    pack_first_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, B, D, H, W, out, bs, dtype);
     return cudaGetLastError();
 }
 
-cudaError_t launch_unpack(const uint8_t* in, int64_t bs, int64_t gs, int fp8, float scale, int B, int C, int D,
+cudaError_t launch_unpack(const uint8_t* in, int64_t bs, int64_t gs, int dtype, float scale, int B, int C, int D,
                           int H, int W, float* y, cudaStream_t s) {
     const int64_t total = static_cast<int64_t>(D) * H * W * C * B;
-    unpack_kernel<<<grid_for(total, 256), 256, 0, s>>>(in, bs, gs, fp8, scale, B, C, D, H, W, y);
+    unpack_kernel<<<grid_for(total, 256), 256, 0, s>>>(in, bs, gs, dtype, scale, B, C, D, H, W, y);
     return cudaGetLastError();
 }
 

@@ -7,17 +7,17 @@
 
 namespace fxk {
 
-// f32 [B][C][D][H][W] -> padded group planes (bf16, or e4m3 of x*qscale when fp8). With
+// f32 [B][C][D][H][W] -> padded group planes of OpType `dtype` (e4m3 values are x*qscale). With
 // `phase`, writes the stride-2 phase-split copy (sub-volume padded dims pHp x pWp,
 // `phase_stride` bytes apart). Channels >= C inside the last group are written as zero.
 cudaError_t launch_pack(const float* x, int B, int C, int D, int H, int W, uint8_t* out, int64_t batch_stride,
-                        int64_t group_stride, int fp8, float qscale, int phase, int pHp, int pWp,
+                        int64_t group_stride, int dtype, float qscale, int phase, int pHp, int pWp,
                         int64_t phase_stride, cudaStream_t s);
-// f32 [B][1][D][H][W] -> the first layer's x-folded bf16 cells (x-1, x, x+1, 0...).
+// f32 [B][1][D][H][W] -> the first layer's x-folded 16-bit cells (x-1, x, x+1, 0...).
 cudaError_t launch_pack_first(const float* x, int B, int D, int H, int W, uint8_t* out, int64_t batch_stride,
-                              cudaStream_t s);
-// padded group planes -> f32 [B][C][D][H][W] (bf16, or e4m3 times `scale` when fp8).
-cudaError_t launch_unpack(const uint8_t* in, int64_t batch_stride, int64_t group_stride, int fp8, float scale, int B,
+                              int dtype, cudaStream_t s);
+// padded group planes of OpType `dtype` -> f32 [B][C][D][H][W] (e4m3 values times `scale`).
+cudaError_t launch_unpack(const uint8_t* in, int64_t batch_stride, int64_t group_stride, int dtype, float scale, int B,
                           int C, int D, int H, int W, float* y, cudaStream_t s);
 // max |x| over n floats into *amax (float bits; caller zeroes).
 cudaError_t launch_absmax(const float* x, int64_t n, unsigned* amax, cudaStream_t s);

@@ -23,6 +23,7 @@ struct Tap {
 };
 
 struct ProgramSpec {
+    int optype = 0;    // fxk::OpType of the packed weights: 0 bf16, 1 e4m3, 2 f16
     int G = 0;         // input groups (16 bytes each)
     int cg = 8;        // channels per group: 8 (bf16) or 16 (e4m3)
     int elem = 2;      // bytes per element
@@ -75,6 +76,33 @@ inline uint8_t float_to_e4m3(float f) {
     else if (dh < dl) best = hi;
     else best = (lo & 1) ? hi : lo;
     return sign | static_cast<uint8_t>(best);
+}
+
+// IEEE binary16, round to nearest even, saturated to +-65504.
+inline uint16_t float_to_f16(float f) {
+    if (std::isnan(f)) return 0x7e00;
+    f = std::fmax(-65504.f, std::fmin(65504.f, f));
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    const uint32_t sign = (u >> 16) & 0x8000u;
+    const float a = std::fabs(f);
+    if (a < std::ldexp(1.f, -25)) return static_cast<uint16_t>(sign);  // rounds to zero
+    if (a < std::ldexp(1.f, -14)) {  // subnormal: multiples of 2^-24
+        const float q = a * 16777216.f;  // exact
+        float r = std::nearbyint(q);     // default rounding mode: nearest even
+        return static_cast<uint16_t>(sign | static_cast<uint32_t>(r));
+    }
+    int e;
+    const float m = std::frexp(a, &e);  // a = m * 2^e, m in [0.5, 1)
+    // 11 significant bits
+    float sig = std::nearbyint(std::ldexp(m, 11));  // in [1024, 2048]
+    if (sig >= 2048.f) {
+        sig = 1024.f;
+        ++e;
+    }
+    const uint32_t exp = static_cast<uint32_t>(e - 1 + 15);
+    if (exp >= 31) return static_cast<uint16_t>(sign | 0x7bffu);
+    return static_cast<uint16_t>(sign | (exp << 10) | (static_cast<uint32_t>(sig) & 0x3ffu));
 }
 
 inline uint16_t float_to_bf16(float f) {
@@ -208,7 +236,7 @@ inline std::string build_program(const ProgramSpec& s, Program& pg) {
                     for (int j = 0; j < cg; ++j) {
                         const float v = s.wval(col, g * cg + j, wk);
                         if (s.elem == 2) {
-                            const uint16_t b = float_to_bf16(v);
+                            const uint16_t b = s.optype == 2 ? float_to_f16(v) : float_to_bf16(v);
                             std::memcpy(row + 2 * j, &b, 2);
                         } else {
                             row[j] = float_to_e4m3(v);

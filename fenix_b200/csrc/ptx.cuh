@@ -7,7 +7,10 @@
 
 #include <cstdint>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
+
+#include "optype.cuh"
 
 namespace fxk {
 
@@ -170,14 +173,14 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 }
 
 // Instruction descriptor: f32 accumulate, K-major A and B, dense.
-//   kind::f16      : a/b format 1 = bf16
+//   kind::f16      : a/b format 0 = f16, 1 = bf16
 //   kind::f8f6f4   : a/b format 0 = e4m3
-__host__ __device__ constexpr uint32_t instr_desc(int M, int N, bool fp8) {
-    return (1u << 4)                                   // D format f32
-           | ((fp8 ? 0u : 1u) << 7)                    // A format
-           | ((fp8 ? 0u : 1u) << 10)                   // B format
-           | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
-           | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
+__host__ __device__ constexpr uint32_t instr_desc(int M, int N, int optype) {
+    return (1u << 4)                                                  // D format f32
+           | ((optype == kOpBF16 ? 1u : 0u) << 7)                     // A format
+           | ((optype == kOpBF16 ? 1u : 0u) << 10)                    // B format
+           | (static_cast<uint32_t>(N >> 3) << 17)                    // N / 8
+           | (static_cast<uint32_t>(M >> 4) << 24);                   // M / 16
 }
 
 // ---- small numeric helpers ---------------------------------------------------------------------
@@ -185,11 +188,56 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
 }
+// Two floats -> two f16 (round to nearest, saturated to +-65504 so a large value never
+// becomes inf).
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+    a = fminf(fmaxf(a, -65504.f), 65504.f);
+    b = fminf(fmaxf(b, -65504.f), 65504.f);
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+// Eight floats -> one 16-byte cell of 16-bit values (bf16 or f16).
+__device__ __forceinline__ uint4 pack_cell16(const float* v, int optype) {
+    uint4 w;
+    if (optype == kOpF16) {
+        w.x = pack_f16x2(v[0], v[1]);
+        w.y = pack_f16x2(v[2], v[3]);
+        w.z = pack_f16x2(v[4], v[5]);
+        w.w = pack_f16x2(v[6], v[7]);
+    } else {
+        w.x = pack_bf16x2(v[0], v[1]);
+        w.y = pack_bf16x2(v[2], v[3]);
+        w.z = pack_bf16x2(v[4], v[5]);
+        w.w = pack_bf16x2(v[6], v[7]);
+    }
+    return w;
+}
 // Four floats -> four e4m3 bytes (satfinite), little-endian in one u32.
 __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
     __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
     __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
     return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// One 16-byte cell of eight 16-bit values (bf16 or f16) -> floats.
+__device__ __forceinline__ void unpack_cell16(const uint4 w, int optype, float (&f)[8]) {
+    if (optype == kOpF16) {
+        const __half2* h = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 t = __half22float2(h[i]);
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        }
+    } else {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 t = __bfloat1622float2(h[i]);
+            f[2 * i] = t.x;
+            f[2 * i + 1] = t.y;
+        }
+    }
 }
 
 }  // namespace fxk

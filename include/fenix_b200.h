@@ -48,7 +48,11 @@ typedef enum fx_status {
     FX_INTERNAL = 8
 } fx_status;
 
-typedef enum fx_precision { FX_PREC_BF16 = 0, FX_PREC_FP8 = 1 } fx_precision;
+/* Operand precision of the tensor-core convolutions (f32 accumulate in every case):
+ * bf16 and f16 run tcgen05 kind::f16, fp8 runs kind::f8f6f4 with e4m3 activations (per-tensor
+ * scale) and e4m3 weights (per-output-channel scale); in an fp8 net the first conv and any conv
+ * whose input channels are not a multiple of 32 use f16. */
+typedef enum fx_precision { FX_PREC_BF16 = 0, FX_PREC_FP8 = 1, FX_PREC_F16 = 2 } fx_precision;
 
 /* Mirrors ml::InferOptions (src/ml/infer.hpp:38-103), the subset this path implements. */
 typedef struct fx_infer_opts {
@@ -117,14 +121,16 @@ void fx_weight_profile(const float* g, int patch, const int64_t* starts, int64_t
 fx_status fx_norm_tiles(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx, const int64_t* host_origins,
                         int ntiles, int patch, float* dev_out, void* stream);
 /* One 3x3x3 conv (pad 1, stride 1 or 2, no bias) in f32 NCDHW device tensors, computed by the
- * tcgen05 kernel in bf16 (or e4m3 with per-output-channel weight scales and a per-tensor input
- * scale when fp8 != 0), f32 accumulate. Also writes per-channel mean and biased variance of the
- * output per batch item into dev_stats [B][Cout][2] when non-NULL. */
+ * tcgen05 kernel with `precision` operands (fp8: per-output-channel weight scales and a per-tensor
+ * input scale), f32 accumulate, the output rounded once to f16 as the net's pre-norm store does.
+ * Also writes per-channel mean and biased variance of the f32 output per batch item into
+ * dev_stats [B][Cout][2] when non-NULL. */
 fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, const float* dev_w, int Cout,
-                    int stride, int fp8, float* dev_y, float* dev_stats, void* stream);
-/* nn::ConvTranspose3d(k=2, s=2) with bias, f32 NCDHW device tensors, bf16 or e4m3 operands. */
+                    int stride, fx_precision precision, float* dev_y, float* dev_stats, void* stream);
+/* nn::ConvTranspose3d(k=2, s=2) with bias, f32 NCDHW device tensors, `precision` operands,
+ * output rounded once to f16. */
 fx_status fx_conv_transpose2(const float* dev_x, int B, int Cin, int D, int H, int W, const float* dev_w,
-                             const float* dev_bias, int Cout, int fp8, float* dev_y, void* stream);
+                             const float* dev_bias, int Cout, fx_precision precision, float* dev_y, void* stream);
 /* Normalise an f32 accumulator by the factorised weights and encode u8 (rows [z_begin, z_end)). */
 fx_status fx_accum_finalize(const float* dev_acc, int64_t dz, int64_t dy, int64_t dx, int64_t z_begin, int64_t z_end,
                             const float* dev_wz, const float* dev_wy, const float* dev_wx, float* dev_prob,
