@@ -100,6 +100,7 @@ def lib():
     _sig(L, "fx_net_features", i32, [vp, C.POINTER(C.c_int), i32])
     _sig(L, "fx_net_calibrate", i32, [vp, u8p, i32])
     _sig(L, "fx_net_act_scales", i32, [vp, f32p, i32])
+    _sig(L, "fx_net_set_act_scales", i32, [vp, f32p, i32])
     _sig(L, "fx_net_forward", i32, [vp, vp, i32, vp, i32, i32, vp])
     _sig(L, "fx_predict_volume", i32, [vp, u8p, i64, i64, i64, C.POINTER(InferOpts), f32p, u8p])
     _sig(L, "fx_predict_tiles_dev", i32, [vp, vp, i64, i64, i64, C.POINTER(InferOpts), i64, i64, vp, vp])
@@ -110,6 +111,10 @@ def lib():
     _sig(L, "fx_conv3d", i32, [vp, i32, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp])
     _sig(L, "fx_conv_transpose2", i32, [vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp])
     _sig(L, "fx_accum_finalize", i32, [vp, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp])
+    _sig(L, "fx_net_profile", i32, [vp, i32])
+    _sig(L, "fx_net_profile_read", i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                         C.POINTER(C.c_int64), C.POINTER(C.c_double), i32])
+    _sig(L, "fx_kernel_launches", C.c_ulonglong, [])
     _sig(L, "fx_synth_spiral", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
     _lib = L
     return L
@@ -168,6 +173,11 @@ def synth_spiral(shape, seed: int, params: dict | None = None, z_begin: int = 0,
     return out
 
 
+def kernel_launches() -> int:
+    """Kernel launches issued by libfenix_b200 in this process."""
+    return int(lib().fx_kernel_launches())
+
+
 def device_count() -> int:
     return lib().fx_device_count()
 
@@ -218,10 +228,27 @@ class Net:
         p = np.ascontiguousarray(patches_u8, dtype=np.uint8)
         check(lib().fx_net_calibrate(self._h, p.ctypes.data_as(C.POINTER(C.c_uint8)), p.shape[0]))
 
+    def set_act_scales(self, scales) -> None:
+        s = np.ascontiguousarray(scales, dtype=np.float32)
+        check(lib().fx_net_set_act_scales(self._h, s.ctypes.data_as(C.POINTER(C.c_float)), len(s)))
+
     def act_scales(self) -> np.ndarray:
         buf = np.zeros(256, dtype=np.float32)
         n = lib().fx_net_act_scales(self._h, buf.ctypes.data_as(C.POINTER(C.c_float)), 256)
         return buf[:n]
+
+    def profile(self, enable: bool) -> None:
+        check(lib().fx_net_profile(self._h, 1 if enable else 0))
+
+    def profile_read(self, per_launch_cap: int = 4096) -> dict:
+        ms, fl, f8 = C.c_double(), C.c_double(), C.c_double()
+        n = C.c_int64()
+        per = np.zeros(2 * per_launch_cap, dtype=np.float64)
+        check(lib().fx_net_profile_read(self._h, C.byref(ms), C.byref(fl), C.byref(f8), C.byref(n),
+                                        per.ctypes.data_as(C.POINTER(C.c_double)), per_launch_cap))
+        k = min(n.value, per_launch_cap)
+        return {"conv_ms": ms.value, "conv_flops": fl.value, "fp8_flops": f8.value, "conv_launches": n.value,
+                "per_launch": per[: 2 * k].reshape(k, 2)}
 
     def forward_dev(self, dev_tiles_ptr: int, nb: int, dev_prob_ptr: int, channel: int = 1, sigmoid: int = 0,
                     stream: int | None = None) -> None:

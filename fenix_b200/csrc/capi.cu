@@ -4,6 +4,7 @@
 #include "fenix_b200.h"
 #include "fenix_b200/ml/tiling.hpp"
 #include "net.cuh"
+#include "counters.hpp"
 #include "pack.cuh"
 #include "ptx.cuh"
 
@@ -134,6 +135,14 @@ fx_status fx_net_calibrate(fx_net* n, const uint8_t* host_patches, int count) {
     });
 }
 
+fx_status fx_net_set_act_scales(fx_net* n, const float* scales, int count) {
+    return guarded([&]() -> fx_status {
+        if (!n || !scales) return set_err(FX_INVALID_ARGUMENT, "fx_net_set_act_scales: null argument");
+        fxh::Status st = n->net.set_act_scales(scales, count);
+        return st.ok() ? FX_OK : set_err(st);
+    });
+}
+
 int fx_net_act_scales(const fx_net* n, float* out, int cap) {
     if (!n) return 0;
     auto v = n->net.act_scales();
@@ -223,6 +232,29 @@ fx_status fx_predict_volume(fx_net* n, const uint8_t* host_vol, int64_t dz, int6
         return FX_OK;
     });
 }
+
+fx_status fx_net_profile(fx_net* n, int enable) {
+    if (!n) return set_err(FX_INVALID_ARGUMENT, "fx_net_profile: null net");
+    n->net.profile(enable != 0);
+    return FX_OK;
+}
+
+fx_status fx_net_profile_read(fx_net* n, double* conv_ms, double* conv_flops, double* fp8_flops,
+                              int64_t* conv_launches, double* per_launch, int cap) {
+    return guarded([&]() -> fx_status {
+        if (!n) return set_err(FX_INVALID_ARGUMENT, "fx_net_profile_read: null net");
+        fxh::Net::ProfileTotals t;
+        fxh::Status st = n->net.profile_read(t, per_launch, cap);
+        if (!st.ok()) return set_err(st);
+        if (conv_ms) *conv_ms = t.conv_ms;
+        if (conv_flops) *conv_flops = t.conv_flops;
+        if (fp8_flops) *fp8_flops = t.fp8_flops;
+        if (conv_launches) *conv_launches = t.conv_launches;
+        return FX_OK;
+    });
+}
+
+unsigned long long fx_kernel_launches(void) { return fxk::launch_count(); }
 
 int64_t fx_tile_starts(int64_t dim, int patch, double overlap, int64_t* out, int64_t cap) {
     const auto v = fenix::ml::tile_starts(dim, patch, overlap);

@@ -1,6 +1,7 @@
 // conv_tc.cu — persistent warp-specialised tcgen05 implicit-GEMM kernel (see conv_tc.cuh for
 // the data layout and the per-layer program it executes).
 #include "conv_tc.cuh"
+#include "counters.hpp"
 #include "ptx.cuh"
 
 #include <cuda_runtime.h>
@@ -10,6 +11,7 @@ namespace fxk {
 namespace {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate stage wait
+constexpr int kMaxCols = 512;                      // per-channel scale / bias table entries
 
 struct SmemCtl {
     uint64_t full[16];
@@ -19,6 +21,8 @@ struct SmemCtl {
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
+    float colscale[kMaxCols];
+    float bias[kMaxCols];
 };
 
 __device__ __forceinline__ void unit_coords(const ConvParams& p, int unit, int& b, int& mu, int& nt) {
@@ -68,13 +72,11 @@ __device__ void producer_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, 
         }
     }
 drain:
-    // Drain: wait until every stage we filled has landed (the consumer may have aborted).
+    // Wait until every stage we filled has landed (the consumer may have aborted).
     const uint32_t n_issued = k;
     for (uint32_t j = (n_issued > static_cast<uint32_t>(p.n_pipe) ? n_issued - p.n_pipe : 0u); j < n_issued; ++j) {
         const int slot = j % p.n_pipe;
-        if (!mbar_wait(smem_u32(&ctl->full[slot]), (j / p.n_pipe) & 1u, nullptr,
-                       kWaitLimitNs)) {
-            // An abort elsewhere is fine; a copy that never lands is recorded.
+        if (!mbar_wait(smem_u32(&ctl->full[slot]), (j / p.n_pipe) & 1u, nullptr, kWaitLimitNs)) {
             if (!ctl->abort) set_status(p.status, kStatusTimeoutDrain);
             break;
         }
@@ -82,12 +84,21 @@ drain:
 }
 
 // MMA issuer: one thread walks the program and issues tcgen05.mma into TMEM accumulators.
+// Descriptor words are precomputed so each MMA costs a couple of integer ops to issue.
 __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n_units) {
     uint32_t k = 0;
     uint32_t j = 0;  // unit counter for accumulator slots
     const uint32_t tbase = ctl->tmem_base;
     const uint32_t slot_cols = static_cast<uint32_t>(p.R * p.N_tile);
     const uint32_t smem_base = smem_u32(smem);
+    // descriptor high words: SBO = 128 B, version 1, no swizzle
+    const uint64_t hi = (static_cast<uint64_t>(128 >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
+    const uint64_t b_lbo = static_cast<uint64_t>((p.N_tile * 16) >> 4) << 16;
+    const bool split = p.N_tile > 256;
+    const int n0b = split ? 256 : p.N_tile;  // columns of the first sub-MMA
+    const uint32_t idesc0 = instr_desc(128, n0b, p.optype);
+    const uint32_t idesc1 = instr_desc(128, split ? p.N_tile - 256 : 16, p.optype);
+    const bool f8 = p.optype == kOpE4M3;
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
         const int aslot = j % p.acc_slots;
         const uint32_t aph = (j / p.acc_slots) & 1u;
@@ -98,55 +109,57 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
         }
         tc_fence_after();
         const uint32_t dcol0 = tbase + aslot * slot_cols;
-        bool first = true;
+        uint32_t acc = 0;
+        bool aborted = false;
         for (int s = 0; s < p.n_stages; ++s, ++k) {
             const int slot = k % p.n_pipe;
+            const ConvStage st = p.stages[s];
             if (!mbar_wait(smem_u32(&ctl->full[slot]), (k / p.n_pipe) & 1u, &ctl->abort, kWaitLimitNs)) {
                 set_status(p.status, kStatusTimeoutFull);
                 ctl->abort = 1;
-                goto done;
+                aborted = true;
+                break;
             }
             tc_fence_after();
-            {
-                const ConvStage st = p.stages[s];
-                const uint32_t sa = smem_base + static_cast<uint32_t>(slot * p.stage_bytes);
-                const uint32_t sb = sa + static_cast<uint32_t>(p.stage_a_bytes);
-                const uint32_t b_lbo = static_cast<uint32_t>(p.N_tile * 16);
-                for (int m = 0; m < st.mma_count; ++m) {
-                    const ConvMma mm = p.mmas[st.mma_begin + m];
-                    for (int r = 0; r < p.R; ++r) {
-                        const uint64_t adesc = smem_desc(sa + mm.a_off + r * 2048, mm.lbo, 128);
-                        for (int n0 = 0; n0 < p.N_tile; n0 += 256) {
-                            const int nn = p.N_tile - n0 < 256 ? p.N_tile - n0 : 256;
-                            const uint64_t bdesc = smem_desc(sb + mm.b_off + n0 * 16, b_lbo, 128);
-                            const uint32_t idesc = instr_desc(128, nn, p.optype);
-                            const uint32_t d = dcol0 + r * p.N_tile + n0;
-                            if (p.optype == kOpE4M3)
-                                mma_f8(d, adesc, bdesc, idesc, first ? 0u : 1u);
-                            else
-                                mma_f16(d, adesc, bdesc, idesc, first ? 0u : 1u);
-                        }
+            const uint32_t sa = smem_base + static_cast<uint32_t>(slot * p.stage_bytes);
+            const uint32_t sb = sa + static_cast<uint32_t>(p.stage_a_bytes);
+            const uint64_t bdesc0 = hi | b_lbo;
+            ConvMma mm = p.mmas[st.mma_begin];
+            for (int m = 0; m < st.mma_count; ++m) {
+                const ConvMma nxt = p.mmas[st.mma_begin + (m + 1 < st.mma_count ? m + 1 : m)];
+                const uint64_t adesc =
+                    hi | (static_cast<uint64_t>((static_cast<uint32_t>(mm.lbo) >> 4) & 0x3FFFu) << 16) |
+                    static_cast<uint64_t>(((sa + static_cast<uint32_t>(mm.a_off)) >> 4) & 0x3FFFu);
+                const uint64_t bdesc =
+                    bdesc0 | static_cast<uint64_t>(((sb + static_cast<uint32_t>(mm.b_off)) >> 4) & 0x3FFFu);
+                for (int r = 0; r < p.R; ++r) {
+                    const uint64_t ad = adesc + static_cast<uint64_t>(r * (2048 >> 4));
+                    const uint32_t d = dcol0 + r * p.N_tile;
+                    if (f8) mma_f8(d, ad, bdesc, idesc0, acc);
+                    else mma_f16(d, ad, bdesc, idesc0, acc);
+                    if (split) {
+                        const uint64_t bd1 = bdesc + static_cast<uint64_t>((256 * 16) >> 4);
+                        if (f8) mma_f8(d + 256, ad, bd1, idesc1, acc);
+                        else mma_f16(d + 256, ad, bd1, idesc1, acc);
                     }
-                    first = false;
                 }
+                acc = 1;
+                mm = nxt;
             }
             mma_commit(smem_u32(&ctl->empty[slot]));  // stage buffer free once these MMAs finish
         }
+        if (aborted) break;
         mma_commit(smem_u32(&ctl->accf[aslot]));  // accumulator ready for the epilogue
     }
-done:
     // Make sure nothing we issued is still running before TMEM is released.
     mma_commit(smem_u32(&ctl->drain));
-    if (!mbar_wait(smem_u32(&ctl->drain), 0u, nullptr, kWaitLimitNs)) {
-        // abort set by another role: still give in-flight MMAs time to finish
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < kWaitLimitNs) {
-        }
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < kWaitLimitNs) {
     }
 }
 
 // Butterfly "transpose-reduce" over 16 channels: on entry each lane holds 16 per-channel values
-// of its row; on exit lane l holds the sum over all 32 rows of channel (l & 15).
+// of its row; on exit lane l holds the sum over all 32 lanes of channel (l & 15).
 __device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16], int lane) {
 #pragma unroll
     for (int off = 8; off >= 1; off >>= 1) {
@@ -161,24 +174,38 @@ __device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16], int lan
     return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 16);
 }
 
-__device__ __forceinline__ bool row_interior(int64_t row, int P2, int Wp, int Dp, int Hp) {
-    const int64_t z = row / P2;
-    const int rem = static_cast<int>(row - z * P2);
-    const int y = rem / Wp;
-    const int x = rem - y * Wp;
-    return z >= 1 && z <= Dp - 2 && y >= 1 && y <= Hp - 2 && x >= 1 && x <= Wp - 2;
-}
+// (z, y, x) of a row of the padded row space by multiply-high division (exact for row * d < 2^64).
+struct RowDecomp {
+    uint64_t mP2, mWp;
+    uint32_t P2, Wp;
+    __device__ __forceinline__ void split(uint32_t row, uint32_t& z, uint32_t& y, uint32_t& x) const {
+        z = static_cast<uint32_t>(__umul64hi(row, mP2));
+        const uint32_t rem = row - z * P2;
+        y = static_cast<uint32_t>(__umul64hi(rem, mWp));
+        x = rem - y * Wp;
+    }
+};
 
-constexpr int kMaxChunks = 20;  // 320 columns / 16
-
+// Epilogue for N_tile = 16 * NCH columns: 4 warps drain the TMEM accumulator of each unit
+// (warp w owns TMEM lanes 32 (w % 4) .. +31, i.e. one output row per thread per M block).
+template <int NCH>
 __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const int lane = threadIdx.x & 31;
-    const int wq = (threadIdx.x >> 5) & 3;  // TMEM lane quarter this warp may access
+    const int wq = (threadIdx.x >> 5) & 3;
     const uint32_t tbase = ctl->tmem_base;
     const uint32_t slot_cols = static_cast<uint32_t>(p.R * p.N_tile);
     const int Mtot = 128 * p.R;
-    const int P2 = p.Hp * p.Wp;
-    const int nch = p.N_tile / 16;
+    RowDecomp rd;
+    rd.P2 = static_cast<uint32_t>(p.Hp * p.Wp);
+    rd.Wp = static_cast<uint32_t>(p.Wp);
+    rd.mP2 = ~0ull / rd.P2 + 1;
+    rd.mWp = ~0ull / rd.Wp + 1;
+    const uint32_t zmax = static_cast<uint32_t>(p.Dp - 2), ymax = static_cast<uint32_t>(p.Hp - 2),
+                   xmax = static_cast<uint32_t>(p.Wp - 2);
+    const bool prenorm = p.mode == kModePrenorm;
+    constexpr bool kAccR = NCH <= 2;         // sum over M blocks in registers, one butterfly per unit
+    constexpr int kGrp = NCH < 4 ? NCH : 4;  // chunks loaded from TMEM per wait
+    constexpr int kR = kAccR ? NCH : 1;
     uint32_t j = 0;
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
         int b, mu, nt;
@@ -191,80 +218,92 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         }
         tc_fence_after();
         const int64_t q0 = p.row_begin + static_cast<int64_t>(mu) * Mtot;
-        float s1[kMaxChunks], s2[kMaxChunks];
+        const int cbase = nt * p.N_tile;  // first global column of this tile
+        float s1[NCH], s2[NCH];
+        float r1[kR][16], r2[kR][16];
 #pragma unroll
-        for (int c = 0; c < kMaxChunks; ++c) s1[c] = s2[c] = 0.f;
+        for (int c = 0; c < NCH; ++c) s1[c] = s2[c] = 0.f;
+#pragma unroll
+        for (int c = 0; c < kR; ++c)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
         for (int r = 0; r < p.R; ++r) {
             const int64_t row = q0 + r * 128 + wq * 32 + lane;
-            const bool valid = row < p.row_end && row_interior(row, P2, p.Wp, p.Dp, p.Hp);
-            const uint32_t taddr = tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + r * p.N_tile;
-            int64_t zi = 0;
-            int yi = 0, xi = 0;
-            if (p.mode == kModeUpsample) {
-                zi = row / P2;
-                const int rem = static_cast<int>(row - zi * P2);
-                yi = rem / p.Wp;
-                xi = rem - yi * p.Wp;
-            }
-#pragma unroll 1
-            for (int cc = 0; cc < nch; ++cc) {
-                float v[16];
-                tmem_ld16(taddr + cc * 16, v);
-                const int n0 = nt * p.N_tile + cc * 16;  // global column of v[0]
-                if (p.mode == kModePrenorm) {
-                    if (p.col_scale) {
+            uint32_t z, y, x;
+            rd.split(static_cast<uint32_t>(row), z, y, x);
+            const bool valid = row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 && x <= xmax;
+            const uint32_t taddr =
+                tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + r * p.N_tile;
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) v[i] *= __ldg(p.col_scale + n0 + i);
-                    }
-                    if (valid) {
-                        uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + row * 16 +
-                                     static_cast<int64_t>(n0 / 8) * p.out_group_stride;
+            for (int g0 = 0; g0 < NCH; g0 += kGrp) {
+                uint32_t raw[kGrp][16];
 #pragma unroll
-                        for (int g = 0; g < 2; ++g)
-                            *reinterpret_cast<uint4*>(o + g * p.out_group_stride) = pack_cell16(v + g * 8, kOpF16);
-                    }
-                    float q[16];
+                for (int c = 0; c < kGrp; ++c) tmem_ld16_nowait(taddr + (g0 + c) * 16, raw[c]);
+                tmem_wait();
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        v[i] = valid ? v[i] : 0.f;
-                        q[i] = v[i] * v[i];
-                    }
-                    const float a1 = warp_transpose_reduce16(v, lane);
-                    const float a2 = warp_transpose_reduce16(q, lane);
+                for (int c = 0; c < kGrp; ++c) tmem_regs_ready(raw[c]);
 #pragma unroll
-                    for (int c = 0; c < kMaxChunks; ++c)
-                        if (c == cc) {
-                            s1[c] += a1;
-                            s2[c] += a2;
+                for (int c = 0; c < kGrp; ++c) {
+                    const int cc = g0 + c;
+                    float v[16];
+                    if (prenorm) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            v[i] = __uint_as_float(raw[c][i]) * ctl->colscale[cbase + cc * 16 + i];
+                        if (valid) {
+                            uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + row * 16 +
+                                         static_cast<int64_t>((cbase + cc * 16) / 8) * p.out_group_stride;
+                            *reinterpret_cast<uint4*>(o) = pack_cell16(v, kOpF16);
+                            *reinterpret_cast<uint4*>(o + p.out_group_stride) = pack_cell16(v + 8, kOpF16);
                         }
-                } else if (valid) {  // kModeUpsample: column n = phase * cout + channel
-                    const int a = n0 / p.cout;
-                    const int co0 = n0 - a * p.cout;  // 16 consecutive channels of one phase
-                    float mx = 0.f;
+                        if constexpr (kAccR) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        if (p.col_scale) v[i] *= __ldg(p.col_scale + co0 + i);
-                        v[i] += __ldg(p.bias + co0 + i);
-                        mx = fmaxf(mx, fabsf(v[i]));
-                    }
-                    if (p.amax) atomicMax(p.amax, __float_as_uint(mx));
-                    const int az = a >> 2, ay = (a >> 1) & 1, ax = a & 1;
-                    const int64_t orow =
-                        ((2 * zi - 1 + az) * static_cast<int64_t>(p.oHp) + (2 * yi - 1 + ay)) * p.oWp + (2 * xi - 1 + ax);
-                    uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + orow * 16;
-                    if (p.out_type == kOpE4M3) {
-                        const float s = p.out_qscale;
-                        uint4 w;
-                        w.x = pack_e4m3x4(v[0] * s, v[1] * s, v[2] * s, v[3] * s);
-                        w.y = pack_e4m3x4(v[4] * s, v[5] * s, v[6] * s, v[7] * s);
-                        w.z = pack_e4m3x4(v[8] * s, v[9] * s, v[10] * s, v[11] * s);
-                        w.w = pack_e4m3x4(v[12] * s, v[13] * s, v[14] * s, v[15] * s);
-                        *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 16) * p.out_group_stride) = w;
-                    } else {
+                            for (int i = 0; i < 16; ++i) {
+                                const float t = valid ? v[i] : 0.f;
+                                r1[cc][i] += t;
+                                r2[cc][i] = fmaf(t, t, r2[cc][i]);
+                            }
+                        } else {
+                            float q[16];
 #pragma unroll
-                        for (int g = 0; g < 2; ++g)
-                            *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 8 + g) * p.out_group_stride) =
-                                pack_cell16(v + g * 8, p.out_type);
+                            for (int i = 0; i < 16; ++i) {
+                                v[i] = valid ? v[i] : 0.f;
+                                q[i] = v[i] * v[i];
+                            }
+                            s1[cc] += warp_transpose_reduce16(v, lane);
+                            s2[cc] += warp_transpose_reduce16(q, lane);
+                        }
+                    } else if (valid) {  // kModeUpsample: column n = phase * cout + channel
+                        const int n0 = cbase + cc * 16;
+                        const int a = n0 / p.cout;
+                        const int co0 = n0 - a * p.cout;  // 16 consecutive channels of one phase
+                        float mx = 0.f;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            v[i] = fmaf(__uint_as_float(raw[c][i]), ctl->colscale[co0 + i], ctl->bias[co0 + i]);
+                            mx = fmaxf(mx, fabsf(v[i]));
+                        }
+                        if (p.amax) atomicMax(p.amax, __float_as_uint(mx));
+                        const int az = a >> 2, ay = (a >> 1) & 1, ax = a & 1;
+                        const int64_t orow =
+                            ((2 * static_cast<int64_t>(z) - 1 + az) * p.oHp + (2 * static_cast<int64_t>(y) - 1 + ay)) *
+                                p.oWp +
+                            (2 * static_cast<int64_t>(x) - 1 + ax);
+                        uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + orow * 16;
+                        if (p.out_type == kOpE4M3) {
+                            const float sc = p.out_qscale;
+                            uint4 w;
+                            w.x = pack_e4m3x4(v[0] * sc, v[1] * sc, v[2] * sc, v[3] * sc);
+                            w.y = pack_e4m3x4(v[4] * sc, v[5] * sc, v[6] * sc, v[7] * sc);
+                            w.z = pack_e4m3x4(v[8] * sc, v[9] * sc, v[10] * sc, v[11] * sc);
+                            w.w = pack_e4m3x4(v[12] * sc, v[13] * sc, v[14] * sc, v[15] * sc);
+                            *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 16) * p.out_group_stride) = w;
+                        } else {
+                            *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 8) * p.out_group_stride) =
+                                pack_cell16(v, p.out_type);
+                            *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 8 + 1) * p.out_group_stride) =
+                                pack_cell16(v + 8, p.out_type);
+                        }
                     }
                 }
             }
@@ -273,20 +312,20 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&ctl->acce[aslot]));
-        if (p.mode == kModePrenorm) {
-            float* dst = p.stats + ((static_cast<int64_t>(b) * p.n_units_m + mu) * 4 + wq) * p.stats_C * 2;
-            for (int cc = 0; cc < nch; ++cc) {
-                float a1 = 0.f, a2 = 0.f;
+        if (prenorm) {
+            if constexpr (kAccR) {
 #pragma unroll
-                for (int c = 0; c < kMaxChunks; ++c)
-                    if (c == cc) {
-                        a1 = s1[c];
-                        a2 = s2[c];
-                    }
-                if (lane < 16) {
-                    const int ch = nt * p.N_tile + cc * 16 + lane;
-                    dst[ch * 2 + 0] = a1;
-                    dst[ch * 2 + 1] = a2;
+                for (int c = 0; c < NCH; ++c) {
+                    s1[c] = warp_transpose_reduce16(r1[c], lane);
+                    s2[c] = warp_transpose_reduce16(r2[c], lane);
+                }
+            }
+            float* dst = p.stats + ((static_cast<int64_t>(b) * p.n_units_m + mu) * 4 + wq) * p.stats_C * 2;
+            if (lane < 16) {
+#pragma unroll
+                for (int c = 0; c < NCH; ++c) {
+                    const int ch = cbase + c * 16 + lane;
+                    *reinterpret_cast<float2*>(dst + ch * 2) = make_float2(s1[c], s2[c]);
                 }
             }
         }
@@ -316,6 +355,12 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         ctl->abort = 0;
         fence_mbar_init();
     }
+    // per-channel dequant scale and bias tables (prenorm: by column; upsample: by channel)
+    const int ncols = p.mode == kModeUpsample ? p.cout : p.stats_C;
+    for (int i = threadIdx.x; i < kMaxCols; i += blockDim.x) {
+        ctl->colscale[i] = (i < ncols && p.col_scale) ? p.col_scale[i] : 1.f;
+        ctl->bias[i] = (i < ncols && p.bias) ? p.bias[i] : 0.f;
+    }
     if (warp == 1) {
         tmem_alloc(smem_u32(&ctl->tmem_base), p.tmem_cols);
         tmem_relinquish();
@@ -330,7 +375,15 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         if (lane == 0) mma_loop(p, smem, ctl, n_units);
         __syncwarp();
     } else {
-        epilogue_loop(p, ctl, n_units);
+        switch (p.N_tile / 16) {
+            case 1: epilogue_loop<1>(p, ctl, n_units); break;
+            case 2: epilogue_loop<2>(p, ctl, n_units); break;
+            case 4: epilogue_loop<4>(p, ctl, n_units); break;
+            case 8: epilogue_loop<8>(p, ctl, n_units); break;
+            case 16: epilogue_loop<16>(p, ctl, n_units); break;
+            case 20: epilogue_loop<20>(p, ctl, n_units); break;
+            default: break;  // rejected on the host (launch_conv_tc)
+        }
     }
 
     tc_fence_before();
@@ -341,6 +394,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     }
 }
 
+size_t conv_tc_ctl_bytes() { return sizeof(SmemCtl); }
+
 cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cudaStream_t stream) {
     static bool configured = false;
     if (!configured) {
@@ -349,6 +404,12 @@ cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cud
         if (e != cudaSuccess) return e;
         configured = true;
     }
+    const int nch = p.N_tile / 16;
+    if (p.N_tile % 16 || !(nch == 1 || nch == 2 || nch == 4 || nch == 8 || nch == 16 || nch == 20))
+        return cudaErrorInvalidValue;
+    if ((p.mode == kModeUpsample ? p.cout : p.stats_C) > kMaxCols) return cudaErrorInvalidValue;
+    if (smem_bytes < static_cast<size_t>(p.n_pipe) * p.stage_bytes + sizeof(SmemCtl)) return cudaErrorInvalidValue;
+    count_launch();
     conv_tc_kernel<<<grid, kConvThreads, smem_bytes, stream>>>(p);
     return cudaGetLastError();
 }

@@ -1,5 +1,6 @@
 // eltwise.cu — HBM-bound kernels of the inference path (see eltwise.cuh).
 #include "eltwise.cuh"
+#include "counters.hpp"
 #include "ptx.cuh"
 
 #include <cuda_bf16.h>
@@ -320,6 +321,7 @@ cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
                              int ntiles, int P, unsigned long long* sums, cudaStream_t s) {
     const int64_t n = static_cast<int64_t>(P) * P * P;
     int gx = grid_for(n, kEwThreads * 8);
+    count_launch();
     tile_sums_kernel<<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums);
     return cudaGetLastError();
 }
@@ -329,6 +331,7 @@ cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
                              int l0_type, float* f32_out, cudaStream_t s) {
     const int64_t n = static_cast<int64_t>(P) * P * P;
     int gx = grid_for(n, kEwThreads * 4);
+    count_launch();
     tile_norm_kernel<<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums, l0, l0_batch_stride,
                                                              l0_type, f32_out);
     return cudaGetLastError();
@@ -336,6 +339,7 @@ cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
 
 cudaError_t launch_in_finalize(const float* partials, int B, int nrec, int C, double count, const float* gamma,
                                const float* beta, float eps, float* ss, cudaStream_t s) {
+    count_launch();
     in_finalize_kernel<<<dim3((C + 31) / 32, B), 1024, 0, s>>>(partials, nrec, C, count, gamma, beta, eps, ss);
     return cudaGetLastError();
 }
@@ -345,6 +349,7 @@ cudaError_t launch_norm_act(const uint8_t* pre, int64_t pbs, int64_t pgs, GridGe
     const bool any_fp8 = (d0.ptr && d0.dtype == kOpE4M3) || (d1.ptr && d1.dtype == kOpE4M3);
     const int cpt = (any_fp8 || C % 16 == 0) ? 16 : 8;
     const int64_t total = static_cast<int64_t>(g.D) * g.H * g.W * (C / cpt) * B;
+    count_launch();
     norm_act_kernel<<<grid_for(total, kEwThreads), kEwThreads, 0, s>>>(pre, pbs, pgs, g, C, B, ss, slope, d0, d1,
                                                                        amax, cpt);
     return cudaGetLastError();
@@ -358,6 +363,7 @@ cudaError_t launch_head_blend(const HeadParams& h, cudaStream_t s) {
     e = cudaMemcpyToSymbolAsync(c_head_b, h.bh, sizeof(float) * h.ncls, 0, cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return e;
     const int64_t n = static_cast<int64_t>(h.P) * h.P * h.P * h.B;
+    count_launch();
     head_blend_kernel<<<grid_for(n, kEwThreads), kEwThreads, 0, s>>>(h);
     return cudaGetLastError();
 }
@@ -367,6 +373,7 @@ cudaError_t launch_accum_finalize(const float* acc, int64_t dz, int64_t dy, int6
                                   uint8_t* u8, cudaStream_t s) {
     const int64_t n = (z_end - z_begin) * dy * dx;
     if (n <= 0) return cudaSuccess;
+    count_launch();
     accum_finalize_kernel<<<grid_for(n, kEwThreads), kEwThreads, 0, s>>>(acc, dz, dy, dx, z_begin, z_end, Wz, Wy,
                                                                          Wx, prob, u8);
     return cudaGetLastError();

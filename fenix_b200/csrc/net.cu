@@ -39,6 +39,10 @@ Status upload(T*& dst, const std::vector<T>& v, Net* /*unused*/, std::vector<voi
 }
 }  // namespace
 
+size_t DevProgram::smem() const {
+    return static_cast<size_t>(host.n_pipe) * host.stage_bytes + fxk::conv_tc_ctl_bytes();
+}
+
 Status cuda_status(cudaError_t e, const char* what) {
     if (e == cudaSuccess) return ok();
     return fail(kInternal, std::string(what) + ": " + cudaGetErrorString(e));
@@ -242,7 +246,7 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     const int N_total = sp.N_total;
     int N_tile = N_total <= 256 ? N_total : (N_total == 320 ? 320 : 256);
     if (N_total % N_tile) return fail(kUnsupported, L.name + ": output width " + std::to_string(N_total) + " not tileable");
-    int R = N_tile <= 64 ? 4 : (N_tile <= 128 ? 2 : 1);
+    int R = N_tile <= 32 ? 8 : (N_tile <= 64 ? 4 : (N_tile <= 128 ? 2 : 1));
     const ActGeom& rs = dp.rowspace;
     const int64_t rows = static_cast<int64_t>(rs.D) * (rs.H + 2) * (rs.W + 2);
     auto units = [&](int r) { return ((rows + 128 * r - 1) / (128 * r)) * Bmax_ * (N_total / N_tile); };
@@ -368,8 +372,50 @@ Status Net::create(const std::string& path, int patch, int max_batch, int precis
 Status Net::run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs, uint8_t* out_ptr,
                      int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax, int nb,
                      cudaStream_t s) {
-    return launch_layer(L, q, level(L.lin), level(L.lout), in_ptr, in_bs, in_gs, out_ptr, out_bs, out_gs, out_type,
-                        out_qscale, amax, nb, sm_count_, d_status_, s);
+    ProfEv ev{};
+    if (profile_) {
+        const ActGeom gi = level(L.lin), go = level(L.lout);
+        const double vin = static_cast<double>(gi.D) * gi.H * gi.W, vout = static_cast<double>(go.D) * go.H * go.W;
+        // algorithmic FLOPs = 2 x MACs: conv 27 Cin Cout Vout, transposed conv Cin Cout Vout
+        ev.flops = L.kind == Layer::kUp ? 2.0 * L.Cin * L.Cout * 8.0 * vin * nb : 2.0 * 27.0 * L.Cin * L.Cout * vout * nb;
+        ev.optype = q;
+        cudaEventCreate(&ev.a);
+        cudaEventCreate(&ev.b);
+        cudaEventRecord(ev.a, s);
+    }
+    Status st = launch_layer(L, q, level(L.lin), level(L.lout), in_ptr, in_bs, in_gs, out_ptr, out_bs, out_gs, out_type,
+                             out_qscale, amax, nb, sm_count_, d_status_, s);
+    if (profile_) {
+        cudaEventRecord(ev.b, s);
+        prof_.push_back(ev);
+    }
+    return st;
+}
+
+void Net::profile(bool on) { profile_ = on; }
+
+Status Net::profile_read(ProfileTotals& out, double* per, int cap) {
+    out = ProfileTotals{};
+    int k = 0;
+    for (ProfEv& e : prof_) {
+        cudaError_t err = cudaEventSynchronize(e.b);
+        if (err != cudaSuccess) return cuda_status(err, "profile");
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e.a, e.b);
+        out.conv_ms += ms;
+        out.conv_flops += e.flops;
+        if (e.optype == fxk::kOpE4M3) out.fp8_flops += e.flops;
+        ++out.conv_launches;
+        if (per && k < cap) {
+            per[2 * k] = ms;
+            per[2 * k + 1] = e.flops;
+        }
+        ++k;
+        cudaEventDestroy(e.a);
+        cudaEventDestroy(e.b);
+    }
+    prof_.clear();
+    return ok();
 }
 
 Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
@@ -646,6 +692,27 @@ Status Net::calibrate(const uint8_t* host_patches, int n) {
         amax_[k] = std::max(amax_[k], f);  // running max over calls
     }
     set_scales_from_amax();
+    for (auto* v : {&enc_, &up_, &dec_})
+        for (Layer& L : *v) {
+            if (layer_q(L, false) != fxk::kOpE4M3) continue;
+            L.prog[1] = DevProgram{};
+            if ((st = build_layer(L, 1)).code) return st;
+        }
+    calibrated_ = true;
+    return ok();
+}
+
+Status Net::set_act_scales(const float* scales, int n) {
+    if (prec_ != 1) return fail(kInvalid, "set_act_scales: net is not fp8");
+    const int total = static_cast<int>(enc_.size() + up_.size() + dec_.size());
+    if (n != total) return fail(kInvalid, "set_act_scales: expected " + std::to_string(total) + " scales");
+    for (int i = 0; i < n; ++i)
+        if (!(scales[i] > 0.f) || !std::isfinite(scales[i])) return fail(kInvalid, "set_act_scales: scales must be finite and > 0");
+    cudaSetDevice(dev_);
+    int k = 0;
+    Status st;
+    for (auto* v : {&enc_, &up_, &dec_})
+        for (Layer& L : *v) L.in_scale = scales[k++];
     for (auto* v : {&enc_, &up_, &dec_})
         for (Layer& L : *v) {
             if (layer_q(L, false) != fxk::kOpE4M3) continue;

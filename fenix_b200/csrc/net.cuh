@@ -16,6 +16,10 @@
 #include <string>
 #include <vector>
 
+namespace fxk {
+size_t conv_tc_ctl_bytes();
+}
+
 namespace fxh {
 
 // Status code (values of fx_status) + message.
@@ -49,7 +53,7 @@ struct DevProgram {
     ActGeom rowspace;  // output grid (conv) or input grid (transposed conv)
     int optype = 0;    // fxk::OpType of the operands
     bool built = false;
-    size_t smem() const { return static_cast<size_t>(host.n_pipe) * host.stage_bytes + 1024; }
+    size_t smem() const;
 };
 
 struct Layer {
@@ -85,6 +89,8 @@ class Net {
     ~Net();
     Status create(const std::string& path, int patch, int max_batch, int precision, int device);
     Status calibrate(const uint8_t* host_patches, int n);
+    // Install per-layer input scales (act_scales() order) and build the e4m3 programs.
+    Status set_act_scales(const float* scales, int n);
     // Forward nb tiles of a device volume at the given device tile origins. Head output:
     // Gaussian blend into acc (dims) and/or probabilities into prob ([nb][P^3]).
     Status forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
@@ -104,7 +110,23 @@ class Net {
     bool calibrated() const { return calibrated_; }
     std::vector<float> act_scales() const;
 
+    // Per-conv-launch device timing with CUDA events on the launching stream (off by default).
+    struct ProfileTotals {
+        double conv_ms = 0, conv_flops = 0, fp8_flops = 0;
+        int64_t conv_launches = 0;
+    };
+    void profile(bool on);
+    // synchronises the recorded events; per-launch (ms, flops) pairs into `per` (up to cap)
+    Status profile_read(ProfileTotals& out, double* per = nullptr, int cap = 0);
+
   private:
+    struct ProfEv {
+        cudaEvent_t a, b;
+        double flops;
+        int optype;
+    };
+    bool profile_ = false;
+    std::vector<ProfEv> prof_;
     Status parse(const WeightMap& wm);
     Status alloc();
     Status build_layer(Layer& L, int q);

@@ -1,5 +1,6 @@
 // pack.cu — f32 NCDHW <-> padded group-plane conversions (see pack.cuh).
 #include "pack.cuh"
+#include "counters.hpp"
 #include "ptx.cuh"
 
 #include <cuda_bf16.h>
@@ -127,6 +128,7 @@ cudaError_t launch_pack(const float* x, int B, int C, int D, int H, int W, uint8
                         int dtype, float qs, int phase, int pHp, int pWp, int64_t ps, cudaStream_t s) {
     const int cg = dtype == kOpE4M3 ? 16 : 8;
     const int64_t total = static_cast<int64_t>(D) * H * W * ((C + cg - 1) / cg) * B;
+    count_launch();
     pack_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, B, C, D, H, W, out, bs, gs, dtype, qs, phase, pHp, pWp, ps);
     return cudaGetLastError();
 }
@@ -134,6 +136,7 @@ cudaError_t launch_pack(const float* x, int B, int C, int D, int H, int W, uint8
 cudaError_t launch_pack_first(const float* x, int B, int D, int H, int W, uint8_t* out, int64_t bs, int dtype,
                               cudaStream_t s) {
     const int64_t total = static_cast<int64_t>(D) * H * W * B;
+    count_launch();
     pack_first_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, B, D, H, W, out, bs, dtype);
     return cudaGetLastError();
 }
@@ -141,11 +144,13 @@ cudaError_t launch_pack_first(const float* x, int B, int D, int H, int W, uint8_
 cudaError_t launch_unpack(const uint8_t* in, int64_t bs, int64_t gs, int dtype, float scale, int B, int C, int D,
                           int H, int W, float* y, cudaStream_t s) {
     const int64_t total = static_cast<int64_t>(D) * H * W * C * B;
+    count_launch();
     unpack_kernel<<<grid_for(total, 256), 256, 0, s>>>(in, bs, gs, dtype, scale, B, C, D, H, W, y);
     return cudaGetLastError();
 }
 
 cudaError_t launch_absmax(const float* x, int64_t n, unsigned* amax, cudaStream_t s) {
+    count_launch();
     absmax_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, n, amax);
     return cudaGetLastError();
 }

@@ -87,8 +87,12 @@ int fx_net_features(const fx_net* net, int* out, int cap); /* returns the stage 
 /* fp8 only: record per-tensor activation amax over `n` host u8 patches ([n][P][P][P]) in a
  * bf16 calibration forward, and fix every activation scale to running-max(amax) / 448. */
 fx_status fx_net_calibrate(fx_net* net, const uint8_t* host_patches, int n);
-/* Per-tensor activation scales after calibration (cap entries); returns the count. */
+/* Per-tensor activation scales after calibration (cap entries); returns the count. One per conv
+ * layer, in the order encoder convs (stage-major), transposed convs (finest level first),
+ * decoder convs (finest level first): the scale of that layer's input activation. */
 int fx_net_act_scales(const fx_net* net, float* out, int cap);
+/* fp8 only: install previously calibrated scales (same order and count) instead of calibrating. */
+fx_status fx_net_set_act_scales(fx_net* net, const float* scales, int count);
 
 /* Forward `nb` device-resident u8 tiles ([nb][P][P][P]) through the net and write the selected
  * class probability ([nb][P][P][P] f32, device). Each tile is z-scored on its own (norm_patch).
@@ -107,6 +111,17 @@ fx_status fx_predict_volume(fx_net* net, const uint8_t* host_vol, int64_t dz, in
 fx_status fx_predict_tiles_dev(fx_net* net, const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx,
                                const fx_infer_opts* opts, int64_t tile_begin, int64_t tile_end, float* dev_acc,
                                void* stream);
+
+/* Device timing of the tensor-core convolutions: with profiling enabled every conv launch of
+ * this net is bracketed by CUDA events on its stream; fx_net_profile_read synchronises them and
+ * returns the summed duration (ms), the algorithmic FLOPs (2 x MACs) of those launches, the
+ * part of them run with e4m3 operands, the launch count and (when per_launch is non-NULL) up to
+ * `cap` per-launch (ms, FLOPs) pairs in launch order, then clears the record. */
+fx_status fx_net_profile(fx_net* net, int enable);
+fx_status fx_net_profile_read(fx_net* net, double* conv_ms, double* conv_flops, double* fp8_flops,
+                              int64_t* conv_launches, double* per_launch, int cap);
+/* Kernel launches issued by this library since the process started. */
+unsigned long long fx_kernel_launches(void);
 
 /* ---- tiling math (host) ---- */
 /* Start positions along one axis; returns the count (writes at most cap). */
