@@ -1,0 +1,316 @@
+#!/usr/bin/env python3
+"""Benchmark: fp8 3D-UNet sliding-window inference over a 1024^3 u8 volume on 1..8 B200.
+
+Workload (the benchmark configuration): the 5-stage plain UNet (32/64/128/256/320, 2 convs +
+InstanceNorm + LeakyReLU per stage, stride-2 conv down, ConvTranspose 2^3 up, 1x1x1 head to 2
+classes + softmax), random Kaiming init (seed 1), fp8 e4m3 operands with per-output-channel weight
+scales and per-tensor activation scales calibrated on 4 seeded patches; a synthetic 1024^3 u8
+spiral-sheet volume (pitch 16, thickness 3, N(0,8) speckle, seed 2); 128^3 tiles at overlap 0.5
+(3375 tiles) with Gaussian blending, normalised and encoded to u8. One step = one full pass over
+the volume. Multi-GPU: the volume is split into z-slabs by tile ranges (fenix_b200/shard.py), the
+tile-overlap bands are exchanged over NCCL, each GPU finalises the planes it owns.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fenix|reference] [--precision fp8|f16|bf16]
+
+For N > 1 launch one process per GPU with torch.distributed.run. Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Mvoxels/s fp8 3D-UNet sliding-window inference @1/2/4/8 B200; % tcgen05 peak"
+FEATURES = (32, 64, 128, 256, 320)
+WEIGHT_SEED, VOLUME_SEED, CALIB_SEED0 = 1, 2, 1000
+
+
+def env_int(name, default):
+    v = os.environ.get(name)
+    return int(v) if v not in (None, "") else default
+
+
+def peaks():
+    """Roofline denominators: MEASURED_PEAKS.json (driver-written) or the recipe's fallback."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), float(d["hbm_gbs"]), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region (200 ms period)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.rows = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def cpu_reference(weights, P, overlap, threads=None, dims=(192, 128, 128)):
+    """The reference's own CPU inference (oracle/_ref/ref_infer: predict_surface_filled + ConvStack via
+    libtorch, fp32) on a bounded sub-volume. Returns (seconds per 128^3 tile, threads, sample text)."""
+    import fenix_b200 as fx
+    from oracle import oracle as orc
+
+    vol = fx.synth_spiral(dims, VOLUME_SEED, fx.SPIRAL_CONFIG3)
+    _, info = orc.ref_infer(weights, vol, P, overlap, batch=2, threads=threads)
+    per_tile = info["seconds"] / info["tiles"]
+    sample = (f"reference predict_surface_filled fp32 on a {dims[0]}x{dims[1]}x{dims[2]} sub-volume of the same "
+              f"synthetic ({info['tiles']} tiles of {P}^3, {info['seconds']:.2f} s); full-job rate projected from "
+              f"the per-tile time over the 1024^3 volume's tiles")
+    return per_tile, int(info["threads"]), sample
+
+
+def run_reference_arm(args):
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return 0
+    import fenix_b200 as fx
+    from fenix_b200.weights import make_plain_unet
+
+    S = args.size
+    tiles = len(fx.tile_starts(S, args.patch, args.overlap)) ** 3
+    with tempfile.TemporaryDirectory() as td:
+        w = make_plain_unet(Path(td) / "w.fxweights", FEATURES, seed=WEIGHT_SEED)
+        ex = ROOT / "oracle" / "_ref" / "ref_infer"
+        if not ex.exists():
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/ref_infer not built (needs the reference tree at build time)"}))
+            return 0
+        for _ in range(args.warmup):
+            cpu_reference(w, args.patch, args.overlap, dims=(128, 128, 128))
+        times, thr, sample = [], 0, ""
+        for _ in range(args.steps):
+            per_tile, thr, sample = cpu_reference(w, args.patch, args.overlap, dims=(128, 128, 128))
+            times.append(per_tile)
+    per_tile = sum(times) / len(times)
+    value = S ** 3 / (tiles * per_tile) / 1e6
+    line = {"metric": METRIC, "value": value, "unit": "Mvoxels/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_tile * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"sliding-window {S}^3, {args.patch}^3 tiles, overlap {args.overlap}, 5-stage UNet "
+                                   "32/64/128/256/320 (each step: one 128^3 tile through the reference's CPU path)"},
+            "cpu_baseline": {"value": value, "unit": "Mvoxels/s", "cores": thr, "kind": "reference", "sample": sample},
+            "e2e": {"value": value, "unit": "Mvoxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="fenix", choices=["fenix", "reference"])
+    ap.add_argument("--precision", default="fp8", choices=["fp8", "f16", "bf16"])
+    ap.add_argument("--size", type=int, default=1024)
+    ap.add_argument("--patch", type=int, default=128)
+    ap.add_argument("--overlap", type=float, default=0.5)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+
+    import fenix_b200 as fx
+    from fenix_b200.shard import ShardedPredictor
+    from fenix_b200.weights import make_plain_unet
+
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    S, P = args.size, args.patch
+    shape = (S, S, S)
+    tmp = tempfile.mkdtemp(prefix=f"fxbench{rank}_")
+    wpath = make_plain_unet(Path(tmp) / "w.fxweights", FEATURES, seed=WEIGHT_SEED)
+    net = fx.Net(wpath, P, max_batch=args.batch, precision=args.precision, device=local)
+    if args.precision == "fp8":
+        calib = np.stack([fx.synth_spiral((P, P, P), CALIB_SEED0 + i, fx.SPIRAL_CONFIG3) for i in range(4)])
+        net.calibrate(calib)
+    sp = ShardedPredictor(net, shape, args.overlap, args.batch, rank=rank, world=world, group=group)
+    me = sp.me
+    # this rank's input slab, generated on the host (pinned), and its output planes
+    host_slab = torch.from_numpy(fx.synth_spiral(shape, VOLUME_SEED, fx.SPIRAL_CONFIG3, me.z_lo, max(me.z_hi, me.z_lo + 1))
+                                 if me.z_hi > me.z_lo else np.zeros((1, S, S), np.uint8)).pin_memory()
+    host_out = torch.empty((max(me.own_hi - me.own_lo, 1), S, S), dtype=torch.uint8).pin_memory()
+    sp.slab.copy_(host_slab)
+    torch.cuda.synchronize()
+    # a real (non-null) stream: every kernel of the step and both timing events go on it
+    stream = torch.cuda.Stream(device=local)
+
+    def timed(fn, k):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(k):
+            fn()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = ev0.elapsed_time(ev1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    dev_step = lambda: sp.run(stream=stream)  # noqa: E731  inputs resident in HBM
+    if world == 1:
+        # the drop-in call: fx_predict_volume with host (pinned) input and u8 output buffers
+        hv, hu = host_slab.numpy(), host_out.numpy()
+
+        def e2e_step():
+            import ctypes as C
+
+            opts = fx.InferOpts(P, args.overlap, 1, 0, args.batch)
+            fx.check(fx.lib().fx_predict_volume(net.handle, hv.ctypes.data_as(C.POINTER(C.c_uint8)), S, S, S,
+                                                C.byref(opts), None, hu.ctypes.data_as(C.POINTER(C.c_uint8))))
+        e2e_path = "fx_predict_volume (C ABI) with pinned host u8 input and u8 output"
+    else:
+        e2e_step = lambda: sp.run(host_slab=host_slab, host_out=host_out, stream=stream)  # noqa: E731
+        e2e_path = ("fenix_b200.shard.ShardedPredictor over fx_predict_tiles_dev / fx_accum_add / fx_accum_finalize "
+                    "with pinned host input slab and output planes")
+    for _ in range(args.warmup):
+        dev_step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    l0 = fx.kernel_launches()
+    ms = timed(dev_step, args.steps)
+    launches = fx.kernel_launches() - l0
+    clk = clocks.stop()
+    for _ in range(1):
+        e2e_step()
+    ms_e2e = timed(e2e_step, args.steps)
+    # one profiled pass: per-launch CUDA events around every conv launch (not in the timed region)
+    net.profile(True)
+    dev_step()
+    net.profile(False)
+    prof = net.profile_read()
+    if world > 1:
+        t = torch.tensor([float(launches)], device="cuda")
+        torch.distributed.all_reduce(t)
+        launches = int(t.item())
+    vox = float(S) ** 3
+    value = vox * args.steps / (ms / 1e3) / 1e6
+    e2e = vox * args.steps / (ms_e2e / 1e3) / 1e6
+    bf16_burst, bf16_sus, hbm, peak_src = peaks()
+    conv_tflops = prof["conv_flops"] / (prof["conv_ms"] / 1e3) / 1e12
+    peak = 2.0 * bf16_burst if args.precision == "fp8" else bf16_burst
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline and (ROOT / "oracle" / "_ref" / "ref_infer").exists():
+        try:
+            per_tile, thr, sample = cpu_reference(wpath, P, args.overlap)
+            tiles = len(fx.tile_starts(S, P, args.overlap)) ** 3
+            cpu = {"value": vox / (tiles * per_tile) / 1e6, "unit": "Mvoxels/s", "cores": thr, "kind": "reference",
+                   "sample": sample}
+        except Exception as e:  # reported, never fatal for the GPU number
+            cpu = {"value": None, "unit": "Mvoxels/s", "cores": None, "kind": "reference", "sample": f"failed: {e}"}
+    if rank == 0:
+        tiles = len(fx.tile_starts(S, P, args.overlap)) ** 3
+        line = {
+            "metric": METRIC, "value": value, "unit": "Mvoxels/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": {"fp8": "e4m3", "f16": "f16", "bf16": "bf16"}[args.precision],
+            "data": "synthetic: 1024^3 u8 spiral sheet (pitch 16, thickness 3, N(170,15)/N(40,10), blur 1, N(0,8) "
+                    "speckle, seed 2); random-init Kaiming weights (seed 1); fp8 scales calibrated on 4 seeded patches",
+            "config": {
+                "workload": f"fp8 sliding-window inference, {S}^3 u8 volume, {P}^3 tiles, overlap {args.overlap}, "
+                            f"{tiles} tiles, Gaussian blend, u8 output; 5-stage UNet 32/64/128/256/320",
+                "volume": [S, S, S], "patch": P, "overlap": args.overlap, "tiles": tiles, "batch": args.batch,
+                "precision": args.precision, "parallelism": f"z-slab x{world}",
+                "l2": "inputs larger than L2: 1 GiB u8 volume + 4 GiB f32 accumulator per step",
+            },
+            "roofline": {
+                "bound": "tensor", "achieved": conv_tflops, "peak": peak, "unit": "TFLOP/s", "frac": conv_tflops / peak,
+                "traffic": None,
+                "kernel": "conv_tc_kernel (all 22 conv launches of one forward, summed)",
+                "peak_source": (f"2 x {peak_src} bf16 burst (e4m3 rate is twice bf16 on tcgen05)" if args.precision == "fp8"
+                                else f"{peak_src} bf16 burst"),
+                "conv_ms_per_step": prof["conv_ms"], "conv_flops_per_step": prof["conv_flops"],
+                "fp8_flop_share": prof["fp8_flops"] / max(prof["conv_flops"], 1.0),
+                "conv_share_of_step": prof["conv_ms"] / (ms / args.steps),
+                "frac_nominal_4500": conv_tflops / (4500.0 if args.precision == "fp8" else 2250.0),
+            },
+            "e2e": {"value": e2e, "unit": "Mvoxels/s", "h2d_bytes_per_step": sp.h2d_bytes * world,
+                    "d2h_bytes_per_step": sp.d2h_bytes * world, "path": e2e_path},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    net.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -103,7 +103,8 @@ def lib():
     _sig(L, "fx_net_set_act_scales", i32, [vp, f32p, i32])
     _sig(L, "fx_net_forward", i32, [vp, vp, i32, vp, i32, i32, vp])
     _sig(L, "fx_predict_volume", i32, [vp, u8p, i64, i64, i64, C.POINTER(InferOpts), f32p, u8p])
-    _sig(L, "fx_predict_tiles_dev", i32, [vp, vp, i64, i64, i64, C.POINTER(InferOpts), i64, i64, vp, vp])
+    _sig(L, "fx_predict_tiles_dev", i32, [vp, vp, i64, i64, i64, i64, i64, C.POINTER(InferOpts), i64, i64, vp, vp])
+    _sig(L, "fx_accum_add", i32, [vp, vp, i64, vp])
     _sig(L, "fx_tile_starts", i64, [i64, i32, C.c_double, C.POINTER(C.c_int64), i64])
     _sig(L, "fx_gaussian1d", None, [i32, f32p])
     _sig(L, "fx_weight_profile", None, [f32p, i32, C.POINTER(C.c_int64), i64, i64, i64, i64, f32p])
@@ -275,12 +276,13 @@ class Net:
         )
         return prob, u8
 
-    def predict_tiles_dev(self, dev_vol_ptr: int, shape, overlap: float, batch: int, tile_begin: int, tile_end: int,
-                          dev_acc_ptr: int, channel: int = 1, sigmoid: int = 0, stream: int | None = None) -> None:
-        dz, dy, dx = shape
+    def predict_tiles_dev(self, dev_slab_ptr: int, slab_shape, z_origin: int, full_dz: int, overlap: float,
+                          batch: int, tile_begin: int, tile_end: int, dev_acc_ptr: int, channel: int = 1,
+                          sigmoid: int = 0, stream: int | None = None) -> None:
+        dz, dy, dx = slab_shape
         opts = InferOpts(self.patch, overlap, channel, sigmoid, batch)
-        check(lib().fx_predict_tiles_dev(self._h, dev_vol_ptr, dz, dy, dx, C.byref(opts), tile_begin, tile_end,
-                                         dev_acc_ptr, stream))
+        check(lib().fx_predict_tiles_dev(self._h, dev_slab_ptr, dz, dy, dx, z_origin, full_dz, C.byref(opts),
+                                         tile_begin, tile_end, dev_acc_ptr, stream))
 
 
 def default_stream_ptr():

@@ -19,6 +19,10 @@
 #include <string>
 #include <vector>
 
+namespace fxh {
+extern unsigned long long* g_conv_trace;
+}
+
 struct fx_net {
     fxh::Net net;
 };
@@ -177,17 +181,27 @@ fx_status fx_net_forward(fx_net* n, const uint8_t* dev_tiles, int nb, float* dev
     });
 }
 
-fx_status fx_predict_tiles_dev(fx_net* n, const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx,
-                               const fx_infer_opts* o, int64_t tile_begin, int64_t tile_end, float* dev_acc,
-                               void* stream) {
+fx_status fx_predict_tiles_dev(fx_net* n, const uint8_t* dev_slab, int64_t slab_dz, int64_t dy, int64_t dx,
+                               int64_t z_origin, int64_t full_dz, const fx_infer_opts* o, int64_t tile_begin,
+                               int64_t tile_end, float* dev_acc, void* stream) {
     return guarded([&]() -> fx_status {
-        if (!n || !dev_vol || !o || !dev_acc) return set_err(FX_INVALID_ARGUMENT, "fx_predict_tiles_dev: null argument");
-        if (dz < 1 || dy < 1 || dx < 1) return set_err(FX_INVALID_ARGUMENT, "fx_predict_tiles_dev: empty volume");
+        if (!n || !dev_slab || !o || !dev_acc) return set_err(FX_INVALID_ARGUMENT, "fx_predict_tiles_dev: null argument");
+        if (slab_dz < 1 || dy < 1 || dx < 1 || full_dz < slab_dz || z_origin < 0 || z_origin + slab_dz > full_dz)
+            return set_err(FX_INVALID_ARGUMENT, "fx_predict_tiles_dev: bad slab geometry");
+        if (o->patch % 64 != 0) return set_err(FX_INVALID_ARGUMENT, "patch must be divisible by 64");
         cudaSetDevice(n->net.device());
         cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : n->net.stream();
-        fxh::Status st = n->net.predict_tiles(dev_vol, dz, dy, dx, o->patch, o->overlap, o->channel, o->sigmoid,
-                                              o->batch, tile_begin, tile_end, dev_acc, s);
+        fxh::Status st = n->net.predict_tiles(dev_slab, slab_dz, dy, dx, z_origin, full_dz, o->patch, o->overlap,
+                                              o->channel, o->sigmoid, o->batch, tile_begin, tile_end, dev_acc, s);
         return st.ok() ? FX_OK : set_err(st);
+    });
+}
+
+fx_status fx_accum_add(float* dev_dst, const float* dev_src, int64_t n, void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!dev_dst || !dev_src || n < 0) return set_err(FX_INVALID_ARGUMENT, "fx_accum_add: bad argument");
+        cudaError_t e = fxk::launch_accum_add(dev_dst, dev_src, n, static_cast<cudaStream_t>(stream));
+        return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_accum_add"));
     });
 }
 
@@ -202,13 +216,14 @@ fx_status fx_predict_volume(fx_net* n, const uint8_t* host_vol, int64_t dz, int6
         cudaStream_t s = n->net.stream();
         const size_t nv = static_cast<size_t>(dz) * dy * dx;
         Scratch sc;
-        uint8_t* d_vol = static_cast<uint8_t*>(sc.get(nv));
-        float* d_acc = static_cast<float*>(sc.get(nv * sizeof(float)));
-        if (!d_vol || !d_acc) return set_err(FX_INTERNAL, "cudaMalloc: volume buffers");
+        uint8_t *d_vol = nullptr, *d_u8 = nullptr;
+        float* d_acc = nullptr;
+        fxh::Status st = n->net.workspace(nv, nv * sizeof(float), host_u8 ? nv : 0, &d_vol, &d_acc, &d_u8);
+        if (!st.ok()) return set_err(st);
         cudaMemcpyAsync(d_vol, host_vol, nv, cudaMemcpyHostToDevice, s);
         cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
-        fxh::Status st = n->net.predict_tiles(d_vol, dz, dy, dx, o->patch, o->overlap, o->channel, o->sigmoid, o->batch,
-                                              0, -1, d_acc, s);
+        st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, o->patch, o->overlap, o->channel, o->sigmoid, o->batch, 0,
+                                  -1, d_acc, s);
         if (!st.ok()) return set_err(st);
         const int P = o->patch;
         const auto g = fenix::ml::gaussian1d(P);
@@ -217,9 +232,9 @@ fx_status fx_predict_volume(fx_net* n, const uint8_t* host_vol, int64_t dz, int6
         const auto Wz = fenix::ml::weight_profile(g, zs, 0, dz, dz, P), Wy = fenix::ml::weight_profile(g, ys, 0, dy, dy, P),
                    Wx = fenix::ml::weight_profile(g, xs, 0, dx, dx, P);
         float* d_w = static_cast<float*>(sc.get(sizeof(float) * (dz + dy + dx)));
-        float* d_prob = host_prob ? static_cast<float*>(sc.get(nv * sizeof(float))) : nullptr;
-        uint8_t* d_u8 = host_u8 ? static_cast<uint8_t*>(sc.get(nv)) : nullptr;
-        if (!d_w || (host_prob && !d_prob) || (host_u8 && !d_u8)) return set_err(FX_INTERNAL, "cudaMalloc: outputs");
+        // the normalised probability overwrites the accumulator in place
+        float* d_prob = host_prob ? d_acc : nullptr;
+        if (!d_w) return set_err(FX_INTERNAL, "cudaMalloc: weight profiles");
         cudaMemcpyAsync(d_w, Wz.data(), sizeof(float) * dz, cudaMemcpyHostToDevice, s);
         cudaMemcpyAsync(d_w + dz, Wy.data(), sizeof(float) * dy, cudaMemcpyHostToDevice, s);
         cudaMemcpyAsync(d_w + dz + dy, Wx.data(), sizeof(float) * dx, cudaMemcpyHostToDevice, s);
@@ -255,6 +270,8 @@ fx_status fx_net_profile_read(fx_net* n, double* conv_ms, double* conv_flops, do
 }
 
 unsigned long long fx_kernel_launches(void) { return fxk::launch_count(); }
+
+void fx_conv_trace_buffer(void* dev_counters) { fxh::g_conv_trace = static_cast<unsigned long long*>(dev_counters); }
 
 int64_t fx_tile_starts(int64_t dim, int patch, double overlap, int64_t* out, int64_t cap) {
     const auto v = fenix::ml::tile_starts(dim, patch, overlap);

@@ -11,7 +11,27 @@ namespace fxk {
 namespace {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate stage wait
-constexpr int kMaxCols = 512;                      // per-channel scale / bias table entries
+
+// Optional cycle accounting per role (build with -DFX_CONV_TRACE; p.trace gets 16 counters):
+// [0] producer waiting for free stages, [1] producer issuing, [2] MMA waiting for drained
+// accumulators, [3] MMA waiting for full stages, [4] MMA issuing, [5] epilogue waiting for
+// accumulators, [6] epilogue draining, [7] MMAs issued, [8] units.
+#ifdef FX_CONV_TRACE
+#define FX_T0() const long long fx_t0_ = clock64()
+#define FX_TADD(p, i) \
+    do { \
+        if ((p).trace) atomicAdd((p).trace + (i), static_cast<unsigned long long>(clock64() - fx_t0_)); \
+    } while (0)
+#define FX_TCNT(p, i, n) \
+    do { \
+        if ((p).trace) atomicAdd((p).trace + (i), static_cast<unsigned long long>(n)); \
+    } while (0)
+#else
+#define FX_T0() ((void)0)
+#define FX_TADD(p, i) ((void)0)
+#define FX_TCNT(p, i, n) ((void)0)
+#endif
+constexpr int kMaxCols = 512;  // per-channel scale / bias table entries
 
 struct SmemCtl {
     uint64_t full[16];
@@ -32,8 +52,10 @@ __device__ __forceinline__ void unit_coords(const ConvParams& p, int unit, int& 
     b = t / p.n_units_m;
 }
 
-// Producer: one elected thread issues the bulk copies of every stage of every unit.
+// Producer warp: the whole warp walks the program (warp-uniform control flow); one elected lane
+// issues the bulk copies of every stage of every unit.
 __device__ void producer_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n_units) {
+    const bool leader = elect_one();
     uint32_t k = 0;  // global stage counter
     const int Mtot = 128 * p.R;
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
@@ -43,11 +65,19 @@ __device__ void producer_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, 
         for (int s = 0; s < p.n_stages; ++s, ++k) {
             const int slot = k % p.n_pipe;
             const uint32_t ph = (k / p.n_pipe) & 1u;
-            if (!mbar_wait(smem_u32(&ctl->empty[slot]), ph ^ 1u, &ctl->abort, kWaitLimitNs)) {
-                set_status(p.status, kStatusTimeoutEmpty);
-                ctl->abort = 1;
-                goto drain;
+            {
+                FX_T0();
+                const bool ok = mbar_wait(smem_u32(&ctl->empty[slot]), ph ^ 1u, &ctl->abort, kWaitLimitNs);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    if (leader) {
+                        set_status(p.status, kStatusTimeoutEmpty);
+                        ctl->abort = 1;
+                    }
+                    goto drain;
+                }
+                if (leader) FX_TADD(p, 0);
             }
+            FX_T0();
             const ConvStage st = p.stages[s];
             const ConvSrc& src = p.src[st.src];
             uint8_t* sbuf = smem + static_cast<size_t>(slot) * p.stage_bytes;
@@ -58,17 +88,21 @@ __device__ void producer_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, 
             const uint32_t a_bytes = chi > clo ? static_cast<uint32_t>((chi - clo) * 16) : 0u;
             const uint32_t total = a_bytes * static_cast<uint32_t>(st.ng) + static_cast<uint32_t>(st.b_bytes);
             const uint32_t fb = smem_u32(&ctl->full[slot]);
-            mbar_arrive_expect_tx(fb, total);
-            if (a_bytes) {
-                const uint8_t* gbase = src.ptr + static_cast<int64_t>(b) * src.batch_stride + clo * 16;
-                const uint32_t dbase = smem_u32(sbuf) + static_cast<uint32_t>((clo - lo) * 16);
-                for (int g = 0; g < st.ng; ++g)
-                    bulk_g2s(dbase + static_cast<uint32_t>(g * st.rows * 16),
-                             gbase + static_cast<int64_t>(st.g0 + g) * src.group_stride, a_bytes, fb);
+            if (leader) {
+                mbar_arrive_expect_tx(fb, total);
+                if (a_bytes) {
+                    const uint8_t* gbase = src.ptr + static_cast<int64_t>(b) * src.batch_stride + clo * 16;
+                    const uint32_t dbase = smem_u32(sbuf) + static_cast<uint32_t>((clo - lo) * 16);
+                    for (int g = 0; g < st.ng; ++g)
+                        bulk_g2s(dbase + static_cast<uint32_t>(g * st.rows * 16),
+                                 gbase + static_cast<int64_t>(st.g0 + g) * src.group_stride, a_bytes, fb);
+                }
+                if (st.b_bytes)
+                    bulk_g2s(smem_u32(sbuf + p.stage_a_bytes), p.wpack + nt * p.wtile_bytes + st.b_off,
+                             static_cast<uint32_t>(st.b_bytes), fb);
+                FX_TADD(p, 1);
             }
-            if (st.b_bytes)
-                bulk_g2s(smem_u32(sbuf + p.stage_a_bytes), p.wpack + nt * p.wtile_bytes + st.b_off,
-                         static_cast<uint32_t>(st.b_bytes), fb);
+            __syncwarp();
         }
     }
 drain:
@@ -76,36 +110,46 @@ drain:
     const uint32_t n_issued = k;
     for (uint32_t j = (n_issued > static_cast<uint32_t>(p.n_pipe) ? n_issued - p.n_pipe : 0u); j < n_issued; ++j) {
         const int slot = j % p.n_pipe;
-        if (!mbar_wait(smem_u32(&ctl->full[slot]), (j / p.n_pipe) & 1u, nullptr, kWaitLimitNs)) {
-            if (!ctl->abort) set_status(p.status, kStatusTimeoutDrain);
+        const bool ok = mbar_wait(smem_u32(&ctl->full[slot]), (j / p.n_pipe) & 1u, nullptr, kWaitLimitNs);
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (leader && !ctl->abort) set_status(p.status, kStatusTimeoutDrain);
             break;
         }
     }
 }
 
-// MMA issuer: one thread walks the program and issues tcgen05.mma into TMEM accumulators.
-// Descriptor words are precomputed so each MMA costs a couple of integer ops to issue.
+// MMA warp: the whole warp runs this loop in lockstep so that its control flow and every operand
+// are warp-uniform (program entries come from the parameter space, hence uniform registers); the
+// MMA / commit instructions are predicated on the elected lane. R (M blocks per unit), the
+// operand kind and the N split are compile-time, so issuing an MMA is a couple of uniform adds.
+template <int R, bool F8, bool SPLIT>
 __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n_units) {
+    const uint32_t leader = elect_one() ? 1u : 0u;
     uint32_t k = 0;
     uint32_t j = 0;  // unit counter for accumulator slots
     const uint32_t tbase = ctl->tmem_base;
-    const uint32_t slot_cols = static_cast<uint32_t>(p.R * p.N_tile);
+    const uint32_t slot_cols = static_cast<uint32_t>(R * p.N_tile);
     const uint32_t smem_base = smem_u32(smem);
     // descriptor high words: SBO = 128 B, version 1, no swizzle
     const uint64_t hi = (static_cast<uint64_t>(128 >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
     const uint64_t b_lbo = static_cast<uint64_t>((p.N_tile * 16) >> 4) << 16;
-    const bool split = p.N_tile > 256;
-    const int n0b = split ? 256 : p.N_tile;  // columns of the first sub-MMA
-    const uint32_t idesc0 = instr_desc(128, n0b, p.optype);
-    const uint32_t idesc1 = instr_desc(128, split ? p.N_tile - 256 : 16, p.optype);
-    const bool f8 = p.optype == kOpE4M3;
+    const uint32_t idesc0 = instr_desc(128, SPLIT ? 256 : p.N_tile, p.optype);
+    const uint32_t idesc1 = instr_desc(128, SPLIT ? p.N_tile - 256 : 16, p.optype);
+    const uint32_t ncol = static_cast<uint32_t>(p.N_tile);
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
         const int aslot = j % p.acc_slots;
         const uint32_t aph = (j / p.acc_slots) & 1u;
-        if (!mbar_wait(smem_u32(&ctl->acce[aslot]), aph ^ 1u, &ctl->abort, kWaitLimitNs)) {
-            set_status(p.status, kStatusTimeoutAccFree);
-            ctl->abort = 1;
-            break;
+        {
+            FX_T0();
+            const bool ok = mbar_wait(smem_u32(&ctl->acce[aslot]), aph ^ 1u, &ctl->abort, kWaitLimitNs);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (leader) {
+                    set_status(p.status, kStatusTimeoutAccFree);
+                    ctl->abort = 1;
+                }
+                break;
+            }
+            if (leader) FX_TADD(p, 2);
         }
         tc_fence_after();
         const uint32_t dcol0 = tbase + aslot * slot_cols;
@@ -113,49 +157,62 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
         bool aborted = false;
         for (int s = 0; s < p.n_stages; ++s, ++k) {
             const int slot = k % p.n_pipe;
-            const ConvStage st = p.stages[s];
-            if (!mbar_wait(smem_u32(&ctl->full[slot]), (k / p.n_pipe) & 1u, &ctl->abort, kWaitLimitNs)) {
-                set_status(p.status, kStatusTimeoutFull);
-                ctl->abort = 1;
-                aborted = true;
-                break;
+            const int mb = p.stages[s].mma_begin, mc = p.stages[s].mma_count;
+            {
+                FX_T0();
+                const bool ok =
+                    mbar_wait(smem_u32(&ctl->full[slot]), (k / p.n_pipe) & 1u, &ctl->abort, kWaitLimitNs);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    if (leader) {
+                        set_status(p.status, kStatusTimeoutFull);
+                        ctl->abort = 1;
+                    }
+                    aborted = true;
+                    break;
+                }
+                if (leader) FX_TADD(p, 3);
             }
             tc_fence_after();
-            const uint32_t sa = smem_base + static_cast<uint32_t>(slot * p.stage_bytes);
-            const uint32_t sb = sa + static_cast<uint32_t>(p.stage_a_bytes);
-            const uint64_t bdesc0 = hi | b_lbo;
-            ConvMma mm = p.mmas[st.mma_begin];
-            for (int m = 0; m < st.mma_count; ++m) {
-                const ConvMma nxt = p.mmas[st.mma_begin + (m + 1 < st.mma_count ? m + 1 : m)];
-                const uint64_t adesc =
-                    hi | (static_cast<uint64_t>((static_cast<uint32_t>(mm.lbo) >> 4) & 0x3FFFu) << 16) |
-                    static_cast<uint64_t>(((sa + static_cast<uint32_t>(mm.a_off)) >> 4) & 0x3FFFu);
-                const uint64_t bdesc =
-                    bdesc0 | static_cast<uint64_t>(((sb + static_cast<uint32_t>(mm.b_off)) >> 4) & 0x3FFFu);
-                for (int r = 0; r < p.R; ++r) {
+            FX_T0();
+            const uint32_t sa16 = (smem_base + static_cast<uint32_t>(slot * p.stage_bytes)) >> 4;
+            const uint32_t sb16 = sa16 + (static_cast<uint32_t>(p.stage_a_bytes) >> 4);
+            const uint64_t ahi = hi + sa16;          // + packed (lbo, A offset) per MMA
+            const uint64_t bhi = hi | b_lbo;         // + (stage B base + B offset) per MMA
+            for (int m = mb; m < mb + mc; ++m) {
+                const ConvMma mm = p.mmas[m];
+                const uint64_t adesc = ahi + mm.a;  // lbo lands in bits 16..29, the address in 0..13
+                const uint64_t bdesc = bhi + (sb16 + mm.b);
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
                     const uint64_t ad = adesc + static_cast<uint64_t>(r * (2048 >> 4));
-                    const uint32_t d = dcol0 + r * p.N_tile;
-                    if (f8) mma_f8(d, ad, bdesc, idesc0, acc);
-                    else mma_f16(d, ad, bdesc, idesc0, acc);
-                    if (split) {
+                    const uint32_t d = dcol0 + static_cast<uint32_t>(r) * ncol;
+                    if (F8) mma_f8_if(leader, d, ad, bdesc, idesc0, acc);
+                    else mma_f16_if(leader, d, ad, bdesc, idesc0, acc);
+                    if (SPLIT) {
                         const uint64_t bd1 = bdesc + static_cast<uint64_t>((256 * 16) >> 4);
-                        if (f8) mma_f8(d + 256, ad, bd1, idesc1, acc);
-                        else mma_f16(d + 256, ad, bd1, idesc1, acc);
+                        if (F8) mma_f8_if(leader, d + 256, ad, bd1, idesc1, acc);
+                        else mma_f16_if(leader, d + 256, ad, bd1, idesc1, acc);
                     }
                 }
                 acc = 1;
-                mm = nxt;
             }
-            mma_commit(smem_u32(&ctl->empty[slot]));  // stage buffer free once these MMAs finish
+            mma_commit_if(leader, smem_u32(&ctl->empty[slot]));  // stage buffer free once these MMAs finish
+            if (leader) {
+                FX_TADD(p, 4);
+                FX_TCNT(p, 7, mc * R);
+            }
         }
         if (aborted) break;
-        mma_commit(smem_u32(&ctl->accf[aslot]));  // accumulator ready for the epilogue
+        mma_commit_if(leader, smem_u32(&ctl->accf[aslot]));  // accumulator ready for the epilogue
     }
     // Make sure nothing we issued is still running before TMEM is released.
-    mma_commit(smem_u32(&ctl->drain));
-    const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < kWaitLimitNs) {
+    mma_commit_if(leader, smem_u32(&ctl->drain));
+    if (leader) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
     }
+    __syncwarp();
 }
 
 // Butterfly "transpose-reduce" over 16 channels: on entry each lane holds 16 per-channel values
@@ -211,12 +268,17 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         int b, mu, nt;
         unit_coords(p, unit, b, mu, nt);
         const int aslot = j % p.acc_slots;
-        if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, kWaitLimitNs)) {
-            set_status(p.status, kStatusTimeoutAcc);
-            ctl->abort = 1;
-            return;
+        {
+            FX_T0();
+            if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, kWaitLimitNs)) {
+                set_status(p.status, kStatusTimeoutAcc);
+                ctl->abort = 1;
+                return;
+            }
+            if (threadIdx.x == 64) FX_TADD(p, 5);
         }
         tc_fence_after();
+        FX_T0();
         const int64_t q0 = p.row_begin + static_cast<int64_t>(mu) * Mtot;
         const int cbase = nt * p.N_tile;  // first global column of this tile
         float s1[NCH], s2[NCH];
@@ -329,6 +391,10 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                 }
             }
         }
+        if (threadIdx.x == 64) {
+            FX_TADD(p, 6);
+            FX_TCNT(p, 8, 1);
+        }
     }
 }
 
@@ -368,12 +434,22 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    (void)lane;
 
     if (warp == 0) {
-        if (lane == 0) producer_loop(p, smem, ctl, n_units);
+        producer_loop(p, smem, ctl, n_units);
     } else if (warp == 1) {
-        if (lane == 0) mma_loop(p, smem, ctl, n_units);
-        __syncwarp();
+        const bool f8 = p.optype == kOpE4M3, split = p.N_tile > 256;
+        switch (p.R) {
+            case 1:
+                if (split) f8 ? mma_loop<1, true, true>(p, smem, ctl, n_units) : mma_loop<1, false, true>(p, smem, ctl, n_units);
+                else f8 ? mma_loop<1, true, false>(p, smem, ctl, n_units) : mma_loop<1, false, false>(p, smem, ctl, n_units);
+                break;
+            case 2: f8 ? mma_loop<2, true, false>(p, smem, ctl, n_units) : mma_loop<2, false, false>(p, smem, ctl, n_units); break;
+            case 4: f8 ? mma_loop<4, true, false>(p, smem, ctl, n_units) : mma_loop<4, false, false>(p, smem, ctl, n_units); break;
+            case 8: f8 ? mma_loop<8, true, false>(p, smem, ctl, n_units) : mma_loop<8, false, false>(p, smem, ctl, n_units); break;
+            default: break;  // rejected on the host (launch_conv_tc)
+        }
     } else {
         switch (p.N_tile / 16) {
             case 1: epilogue_loop<1>(p, ctl, n_units); break;
@@ -408,6 +484,8 @@ cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cud
     if (p.N_tile % 16 || !(nch == 1 || nch == 2 || nch == 4 || nch == 8 || nch == 16 || nch == 20))
         return cudaErrorInvalidValue;
     if ((p.mode == kModeUpsample ? p.cout : p.stats_C) > kMaxCols) return cudaErrorInvalidValue;
+    if (!(p.R == 1 || p.R == 2 || p.R == 4 || p.R == 8) || (p.N_tile > 256 && p.R != 1)) return cudaErrorInvalidValue;
+    if (p.n_stages > kMaxStages || p.n_mmas > kMaxMmas) return cudaErrorInvalidValue;
     if (smem_bytes < static_cast<size_t>(p.n_pipe) * p.stage_bytes + sizeof(SmemCtl)) return cudaErrorInvalidValue;
     count_launch();
     conv_tc_kernel<<<grid, kConvThreads, smem_bytes, stream>>>(p);

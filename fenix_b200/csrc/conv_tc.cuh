@@ -39,11 +39,15 @@ struct ConvStage {
     int32_t mma_begin, mma_count;
 };
 
+// One MMA of a stage, pre-packed into the low words of its smem descriptors (16-byte units):
+//   a = (lbo >> 4) << 16 | (A offset in the stage >> 4), b = B offset in the stage >> 4.
 struct ConvMma {
-    int32_t a_off;  // byte offset inside the stage's A buffer for M-block 0
-    int32_t lbo;    // byte distance between the two K-halves of this MMA's A operand
-    int32_t b_off;  // byte offset inside the stage's B buffer
+    uint32_t a;
+    uint32_t b;
 };
+
+constexpr int kMaxStages = 320;   // program capacity (kept in the kernel's parameter space)
+constexpr int kMaxMmas = 1536;
 
 struct ConvSrc {
     const uint8_t* ptr;    // row 0 of group 0 of batch item 0
@@ -59,11 +63,10 @@ enum ConvMode : int32_t {
 
 struct ConvParams {
     ConvSrc src[kMaxSrc];
-    const ConvStage* stages;
-    const ConvMma* mmas;
     const uint8_t* wpack;  // packed B blocks of N tile 0; tile t starts at + t * wtile_bytes
     int64_t wtile_bytes;
     int32_t n_stages;
+    int32_t n_mmas;
     int32_t optype;  // OpType of both operands: bf16 / f16 (kind::f16) or e4m3 (kind::f8f6f4)
 
     // output-row space of one batch item: the padded geometry rows are indexed in
@@ -94,6 +97,11 @@ struct ConvParams {
     float* stats;            // prenorm mode: [batch][n_units_m][4][C][2] partial sums
     int32_t stats_C;         // channels per stats record (= n_tiles * N_tile)
     uint32_t* status;
+    unsigned long long* trace;  // per-role cycle counters (kernel built with FX_CONV_TRACE), or null
+    // The program itself travels in the parameter space: warp-uniform indexed loads of it land in
+    // uniform registers, so issuing an MMA costs a few uniform adds.
+    ConvStage stages[kMaxStages];
+    ConvMma mmas[kMaxMmas];
 };
 
 }  // namespace fxk

@@ -283,10 +283,12 @@ __global__ void head_blend_kernel(HeadParams h) {
     }
 }
 
-__global__ void accum_finalize_kernel(const float* __restrict__ acc, int64_t dz, int64_t dy, int64_t dx,
+// acc and prob may alias when z_begin == 0 (in-place normalise): each element is read before it
+// is written, by the same thread.
+__global__ void accum_finalize_kernel(const float* acc, int64_t dz, int64_t dy, int64_t dx,
                                       int64_t z_begin, int64_t z_end, const float* __restrict__ Wz,
-                                      const float* __restrict__ Wy, const float* __restrict__ Wx,
-                                      float* __restrict__ prob, uint8_t* __restrict__ u8) {
+                                      const float* __restrict__ Wy, const float* __restrict__ Wx, float* prob,
+                                      uint8_t* __restrict__ u8) {
     const int64_t plane = dy * dx;
     const int64_t total = (z_end - z_begin) * plane;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -294,18 +296,38 @@ __global__ void accum_finalize_kernel(const float* __restrict__ acc, int64_t dz,
         const int64_t z = z_begin + i / plane;
         const int64_t r = i % plane;
         const int64_t y = r / dx, x = r % dx;
-        const int64_t idx = z * plane + r;
+        const int64_t idx = z * plane + r;  // accumulator index
+        const int64_t oidx = i;               // output index: plane z_begin is output plane 0
         // w = (Wz*Wy)*Wx; v /= w when w > 0 (src/ml/infer.hpp:510-521)
         const float w = __fmul_rn(__fmul_rn(__ldg(Wz + z), __ldg(Wy + y)), __ldg(Wx + x));
         float v = acc[idx];
         if (w > 0.f) v = __fdiv_rn(v, w);
-        if (prob) prob[idx] = v;
+        if (prob) prob[oidx] = v;
         if (u8) {
             const float c = fminf(fmaxf(v, 0.f), 1.f);
             // (u8)(clamp(v,0,1)*255+0.5) (src/ml/inference.cpp:343-351)
-            u8[idx] = static_cast<uint8_t>(__fadd_rn(__fmul_rn(c, 255.f), 0.5f));
+            u8[oidx] = static_cast<uint8_t>(__fadd_rn(__fmul_rn(c, 255.f), 0.5f));
         }
     }
+}
+
+__global__ void accum_add_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
+    const int64_t n4 = n / 4;
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float4 a = d4[i];
+        const float4 b = s4[i];
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
+        d4[i] = a;
+    }
+    for (int64_t i = n4 * 4 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dst[i] += src[i];
 }
 
 int grid_for(int64_t n, int threads) {
@@ -380,5 +402,13 @@ cudaError_t launch_accum_finalize(const float* acc, int64_t dz, int64_t dy, int6
 }
 
 cudaError_t launch_zero(void* p, size_t bytes, cudaStream_t s) { return cudaMemsetAsync(p, 0, bytes, s); }
+
+cudaError_t launch_accum_add(float* dst, const float* src, int64_t n, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    if ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) return cudaErrorMisalignedAddress;
+    count_launch();
+    accum_add_kernel<<<grid_for(n / 4 + 1, kEwThreads), kEwThreads, 0, s>>>(dst, src, n);
+    return cudaGetLastError();
+}
 
 }  // namespace fxk

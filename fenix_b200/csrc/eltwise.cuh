@@ -76,11 +76,14 @@ struct HeadParams {
 cudaError_t launch_head_blend(const HeadParams& h, cudaStream_t s);
 
 // acc / (Wz[z]*Wy[y]*Wx[x]) where the weight is > 0 (the reference's normalize), then
-// u8 = (u8)(clamp(p, 0, 1) * 255 + 0.5). Either output may be null. Rows [z_begin, z_end).
+// u8 = (u8)(clamp(p, 0, 1) * 255 + 0.5), for planes [z_begin, z_end) of acc; the outputs hold
+// just those planes (output plane 0 = plane z_begin). Either output may be null.
 cudaError_t launch_accum_finalize(const float* acc, int64_t dz, int64_t dy, int64_t dx, int64_t z_begin,
                                   int64_t z_end, const float* Wz, const float* Wy, const float* Wx, float* prob,
                                   uint8_t* u8, cudaStream_t s);
 
 cudaError_t launch_zero(void* p, size_t bytes, cudaStream_t s);
+// dst[i] += src[i] (f32, n elements): folds another rank's accumulator band into this one.
+cudaError_t launch_accum_add(float* dst, const float* src, int64_t n, cudaStream_t s);
 
 }  // namespace fxk

@@ -14,6 +14,10 @@ cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cud
 
 namespace fxh {
 
+// Cycle counters of conv launches when the kernel is built with FX_CONV_TRACE (set by a trace
+// driver through fx_conv_trace_buffer); null otherwise.
+unsigned long long* g_conv_trace = nullptr;
+
 using fenix::ml::gaussian1d;
 using fenix::ml::tile_starts;
 
@@ -268,8 +272,6 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     dp.tmem_cols = cols;
     dp.n_units_m = static_cast<int>((rows + 128 * R - 1) / (128 * R));
     dp.optype = q;
-    if ((st = upload(dp.stages, dp.host.stages, this_net, allocs_)).code) return st;
-    if ((st = upload(dp.mmas, dp.host.mmas, this_net, allocs_)).code) return st;
     if ((st = upload(dp.wpack, dp.host.wpack, this_net, allocs_)).code) return st;
     if ((st = upload(dp.colscale, colscale, this_net, allocs_)).code) return st;
     if (L.kind == Layer::kUp && (st = upload(dp.bias, L.b, this_net, allocs_)).code) return st;
@@ -423,7 +425,8 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
                     int nb, int sm_count_, uint32_t* d_status_, cudaStream_t s) {
     DevProgram& dp = L.prog[q];
     if (!dp.built) return fail(kInternal, L.name + ": program not built");
-    fxk::ConvParams p{};
+    static thread_local fxk::ConvParams p;  // ~22 KB: kept off the stack
+    p = fxk::ConvParams{};
     const ActGeom& rs = dp.rowspace;
     if (L.kind == Layer::kConv && L.stride == 2) {
         const int64_t ps = gout.gs();
@@ -431,11 +434,12 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     } else {
         p.src[0] = {in_ptr, in_bs, in_gs, gin.rows()};
     }
-    p.stages = dp.stages;
-    p.mmas = dp.mmas;
+    std::copy(dp.host.stages.begin(), dp.host.stages.end(), p.stages);
+    std::copy(dp.host.mmas.begin(), dp.host.mmas.end(), p.mmas);
     p.wpack = dp.wpack;
     p.wtile_bytes = dp.host.wtile_bytes;
     p.n_stages = static_cast<int32_t>(dp.host.stages.size());
+    p.n_mmas = static_cast<int32_t>(dp.host.mmas.size());
     p.optype = dp.optype;
     p.batch = nb;
     p.Dp = rs.D + 2;
@@ -458,6 +462,7 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     p.out_batch_stride = out_bs;
     p.out_group_stride = out_gs;
     p.status = d_status_;
+    p.trace = g_conv_trace;
     if (L.kind == Layer::kUp) {
         p.mode = fxk::kModeUpsample;
         p.bias = dp.bias;
@@ -731,13 +736,42 @@ std::vector<float> Net::act_scales() const {
 }
 
 // ---- sliding window ---------------------------------------------------------------------------
-Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int patch, double overlap,
-                          int channel, int sigmoid, int batch, int64_t tile_begin, int64_t tile_end, float* d_acc,
-                          cudaStream_t s) {
+Status Net::workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint8_t** vol, float** acc,
+                      uint8_t** out) {
+    auto grow = [&](void** p, size_t& cap, size_t need) -> bool {
+        if (need <= cap) return true;
+        if (*p) {
+            cudaStreamSynchronize(stream_);
+            cudaFree(*p);
+            allocs_.erase(std::remove(allocs_.begin(), allocs_.end(), *p), allocs_.end());
+            *p = nullptr;
+            cap = 0;
+        }
+        void* q = dalloc(need);
+        if (!q) return false;
+        *p = q;
+        cap = need;
+        return true;
+    };
+    if (!grow(reinterpret_cast<void**>(&ws_vol_), ws_vol_cap_, vol_bytes) ||
+        !grow(reinterpret_cast<void**>(&ws_acc_), ws_acc_cap_, acc_bytes) ||
+        (out_bytes && !grow(reinterpret_cast<void**>(&ws_out_), ws_out_cap_, out_bytes)))
+        return fail(kInternal, "cudaMalloc: volume workspace");
+    *vol = ws_vol_;
+    *acc = ws_acc_;
+    if (out) *out = ws_out_;
+    return ok();
+}
+
+Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
+                          int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
+                          int64_t tile_end, float* d_acc, cudaStream_t s) {
     if (patch != P_) return fail(kInvalid, "predict: patch differs from the net's patch");
     if (batch < 1) batch = 1;
     batch = std::min(batch, Bmax_);
-    const auto zs = tile_starts(dz, P_, overlap), ys = tile_starts(dy, P_, overlap), xs = tile_starts(dx, P_, overlap);
+    if (full_dz <= 0) full_dz = dz;
+    const auto zs = tile_starts(full_dz, P_, overlap), ys = tile_starts(dy, P_, overlap),
+               xs = tile_starts(dx, P_, overlap);
     const int64_t total = static_cast<int64_t>(zs.size()) * ys.size() * xs.size();
     if (tile_end < 0 || tile_end > total) tile_end = total;
     if (tile_begin < 0) tile_begin = 0;
@@ -748,7 +782,10 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
         const int64_t xi = i % static_cast<int64_t>(xs.size());
         const int64_t yi = (i / static_cast<int64_t>(xs.size())) % static_cast<int64_t>(ys.size());
         const int64_t zi = i / (static_cast<int64_t>(xs.size()) * ys.size());
-        tiles.push_back({zs[zi], ys[yi], xs[xi]});
+        const int64_t zl = zs[zi] - z_origin;  // slab-local
+        if (zl < 0 || (zl + P_ > dz && full_dz >= P_))
+            return fail(kInvalid, "predict: tile " + std::to_string(i) + " is outside the z-slab");
+        tiles.push_back({zl, ys[yi], xs[xi]});
     }
     if (static_cast<int64_t>(tiles.size()) > d_tiles_cap_) {
         void* p = dalloc(sizeof(fxk::TileOrigin) * tiles.size());

@@ -42,8 +42,6 @@ struct ActGeom {
 };
 
 struct DevProgram {
-    fxk::ConvStage* stages = nullptr;
-    fxk::ConvMma* mmas = nullptr;
     uint8_t* wpack = nullptr;
     float* colscale = nullptr;
     float* bias = nullptr;
@@ -95,9 +93,14 @@ class Net {
     // Gaussian blend into acc (dims) and/or probabilities into prob ([nb][P^3]).
     Status forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
                    int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s);
-    Status predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int patch, double overlap,
-                         int channel, int sigmoid, int batch, int64_t tile_begin, int64_t tile_end, float* d_acc,
-                         cudaStream_t s);
+    // Tiles [tile_begin, tile_end) of the z-major grid over a (full_dz, dy, dx) volume. d_vol and
+    // d_acc hold the z-slab [z_origin, z_origin + dz) of that volume; every tile of the range must
+    // lie inside the slab.
+    Status predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
+                         int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
+                         int64_t tile_end, float* d_acc, cudaStream_t s);
+    // Device workspace for whole-volume calls: grown on demand, kept for the net's lifetime.
+    Status workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint8_t** vol, float** acc, uint8_t** out);
 
     int patch() const { return P_; }
     int max_batch() const { return Bmax_; }
@@ -157,6 +160,10 @@ class Net {
     uint32_t* d_status_ = nullptr;
     fxk::TileOrigin* d_tiles_ = nullptr;
     int64_t d_tiles_cap_ = 0;
+    uint8_t* ws_vol_ = nullptr;
+    float* ws_acc_ = nullptr;
+    uint8_t* ws_out_ = nullptr;
+    size_t ws_vol_cap_ = 0, ws_acc_cap_ = 0, ws_out_cap_ = 0;
     cudaStream_t stream_ = nullptr;
     bool calibrated_ = false;
     std::vector<void*> allocs_;

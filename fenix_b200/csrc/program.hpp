@@ -34,7 +34,7 @@ struct ProgramSpec {
     std::vector<Tap> taps;
     // B value for output column n, input channel ci (0 <= ci < G*cg), tap key
     std::function<float(int n, int ci, int wkey)> wval;
-    int smem_total = 220 * 1024;
+    int smem_total = 212 * 1024;  // stage buffers; the control block takes the rest
 };
 
 struct Program {
@@ -112,6 +112,14 @@ inline uint16_t float_to_bf16(float f) {
     const uint32_t lsb = (u >> 16) & 1u;
     u += 0x7fffu + lsb;
     return static_cast<uint16_t>(u >> 16);
+}
+
+// A / B smem offsets of one MMA packed into descriptor low words (see fxk::ConvMma).
+inline fxk::ConvMma pack_mma(int64_t a_off, int64_t lbo, int64_t b_off) {
+    fxk::ConvMma m{};
+    m.a = (static_cast<uint32_t>(lbo >> 4) << 16) | static_cast<uint32_t>(a_off >> 4);
+    m.b = static_cast<uint32_t>(b_off >> 4);
+    return m;
 }
 
 // Returns "" on success.
@@ -192,22 +200,17 @@ inline std::string build_program(const ProgramSpec& s, Program& pg) {
                 for (size_t i = 0; i < w.taps.size(); i += 2) {
                     const Tap& a = w.taps[i];
                     const bool two = i + 1 < w.taps.size();
-                    fxk::ConvMma m{};
-                    m.a_off = static_cast<int32_t>((a.off - w.lo) * 16);
-                    m.lbo = two ? static_cast<int32_t>((w.taps[i + 1].off - a.off) * 16) : 0;
-                    m.b_off = local_b;
-                    pg.mmas.push_back(m);
+                    const int64_t a_off = (a.off - w.lo) * 16;
+                    const int64_t lbo = two ? (w.taps[i + 1].off - a.off) * 16 : 0;
+                    pg.mmas.push_back(pack_mma(a_off, lbo, local_b));
                     brecs.push_back({a.wkey, two ? w.taps[i + 1].wkey : -1, 0, 0});
                     local_b += bblk;
                 }
             } else {
                 for (const Tap& t : w.taps)
                     for (int gp = g0; gp < g0 + ng; gp += 2) {
-                        fxk::ConvMma m{};
-                        m.a_off = static_cast<int32_t>((gp - g0) * rows * 16 + (t.off - w.lo) * 16);
-                        m.lbo = rows * 16;
-                        m.b_off = local_b;
-                        pg.mmas.push_back(m);
+                        const int64_t a_off = static_cast<int64_t>(gp - g0) * rows * 16 + (t.off - w.lo) * 16;
+                        pg.mmas.push_back(pack_mma(a_off, static_cast<int64_t>(rows) * 16, local_b));
                         brecs.push_back({t.wkey, t.wkey, gp, gp + 1});
                         local_b += bblk;
                     }
@@ -218,6 +221,12 @@ inline std::string build_program(const ProgramSpec& s, Program& pg) {
             pg.stages.push_back(st);
         }
     }
+    if (pg.stages.size() > static_cast<size_t>(fxk::kMaxStages) || pg.mmas.size() > static_cast<size_t>(fxk::kMaxMmas))
+        return "program: " + std::to_string(pg.stages.size()) + " stages / " + std::to_string(pg.mmas.size()) +
+               " MMAs exceed the kernel's program capacity";
+    // every packed offset must fit its 14-bit descriptor field (smem < 256 KB)
+    for (const auto& m : pg.mmas)
+        if ((m.a & 0xFFFFu) >= 0x4000u || (m.a >> 16) >= 0x4000u || m.b >= 0x4000u) return "program: smem offset overflow";
     pg.wtile_bytes = boff;
     pg.wpack.assign(static_cast<size_t>(boff) * pg.n_tiles, 0);
     const int cg = s.cg;

@@ -105,12 +105,18 @@ fx_status fx_net_forward(fx_net* net, const uint8_t* dev_tiles, int nb, float* d
 fx_status fx_predict_volume(fx_net* net, const uint8_t* host_vol, int64_t dz, int64_t dy, int64_t dx,
                             const fx_infer_opts* opts, float* host_prob, uint8_t* host_u8);
 
-/* Same over a device-resident volume, restricted to the flat tile range [tile_begin, tile_end)
- * of the z-major tile list (for z-slab sharding); accumulates into the caller's device
- * accumulator `dev_acc` ([dz][dy][dx] f32, caller-zeroed) without finalising. */
-fx_status fx_predict_tiles_dev(fx_net* net, const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx,
-                               const fx_infer_opts* opts, int64_t tile_begin, int64_t tile_end, float* dev_acc,
-                               void* stream);
+/* Device-resident sliding window restricted to the flat tile range [tile_begin, tile_end) of the
+ * z-major tile grid over a (full_dz, dy, dx) volume (z-slab sharding, the tile grid of
+ * predict-scroll's global mode, src/ml/inference.cpp:1282-1372). dev_slab holds planes
+ * [z_origin, z_origin + slab_dz) of the volume and dev_acc ([slab_dz][dy][dx] f32, caller-zeroed)
+ * the matching accumulator planes; every tile of the range must lie inside the slab. Only
+ * accumulates (Gaussian-weighted sums); fx_accum_finalize normalises. */
+fx_status fx_predict_tiles_dev(fx_net* net, const uint8_t* dev_slab, int64_t slab_dz, int64_t dy, int64_t dx,
+                               int64_t z_origin, int64_t full_dz, const fx_infer_opts* opts, int64_t tile_begin,
+                               int64_t tile_end, float* dev_acc, void* stream);
+/* dev_dst[i] += dev_src[i] over n f32 values (both 16-byte aligned): folds the band another GPU
+ * accumulated for planes this GPU owns into its own accumulator. */
+fx_status fx_accum_add(float* dev_dst, const float* dev_src, int64_t n, void* stream);
 
 /* Device timing of the tensor-core convolutions: with profiling enabled every conv launch of
  * this net is bracketed by CUDA events on its stream; fx_net_profile_read synchronises them and
@@ -122,6 +128,10 @@ fx_status fx_net_profile_read(fx_net* net, double* conv_ms, double* conv_flops, 
                               int64_t* conv_launches, double* per_launch, int cap);
 /* Kernel launches issued by this library since the process started. */
 unsigned long long fx_kernel_launches(void);
+/* Device buffer of 16 u64 cycle counters that conv launches add to when the library is built
+ * with FX_CONV_TRACE (producer / MMA issuer / epilogue waiting and working time); NULL detaches.
+ * Without that build flag the counters are never touched. */
+void fx_conv_trace_buffer(void* dev_counters);
 
 /* ---- tiling math (host) ---- */
 /* Start positions along one axis; returns the count (writes at most cap). */
@@ -146,7 +156,9 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
  * output rounded once to f16. */
 fx_status fx_conv_transpose2(const float* dev_x, int B, int Cin, int D, int H, int W, const float* dev_w,
                              const float* dev_bias, int Cout, fx_precision precision, float* dev_y, void* stream);
-/* Normalise an f32 accumulator by the factorised weights and encode u8 (rows [z_begin, z_end)). */
+/* Normalise planes [z_begin, z_end) of an f32 accumulator [dz][dy][dx] by the factorised weights
+ * Wz[z] Wy[y] Wx[x] and encode u8; dev_prob / dev_u8 (either may be NULL) receive just those
+ * planes, plane z_begin first. */
 fx_status fx_accum_finalize(const float* dev_acc, int64_t dz, int64_t dy, int64_t dx, int64_t z_begin, int64_t z_end,
                             const float* dev_wz, const float* dev_wy, const float* dev_wx, float* dev_prob,
                             uint8_t* dev_u8, void* stream);

@@ -203,6 +203,6 @@ def test_accum_finalize_constant_roundtrip(cuda_torch):
     u8b = torch.zeros_like(u8)  # a z-sweep in two halves gives the same bytes as one pass
     for zb, ze in ((0, 70), (70, dims[0])):
         fx.check(fx.lib().fx_accum_finalize(da.data_ptr(), *dims, zb, ze, dw[0].data_ptr(), dw[1].data_ptr(),
-                                            dw[2].data_ptr(), None, u8b.data_ptr(), None))
+                                            dw[2].data_ptr(), None, u8b[zb:].data_ptr(), None))
     torch.cuda.synchronize()
     assert torch.equal(u8, u8b)
