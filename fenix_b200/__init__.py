@@ -109,6 +109,7 @@ def lib():
     _sig(L, "fx_gaussian1d", None, [i32, f32p])
     _sig(L, "fx_weight_profile", None, [f32p, i32, C.POINTER(C.c_int64), i64, i64, i64, i64, f32p])
     _sig(L, "fx_norm_tiles", i32, [vp, i64, i64, i64, C.POINTER(C.c_int64), i32, i32, vp, vp])
+    _sig(L, "fx_norm_tiles_noalloc", i32, [vp, i64, i64, i64, C.POINTER(C.c_int64), i32, i32, vp, vp])
     _sig(L, "fx_conv3d", i32, [vp, i32, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp])
     _sig(L, "fx_conv_transpose2", i32, [vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp])
     _sig(L, "fx_accum_finalize", i32, [vp, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp])

@@ -15,6 +15,7 @@
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -26,6 +27,19 @@ extern unsigned long long* g_conv_trace;
 struct fx_net {
     fxh::Net net;
 };
+
+// Static device scratch of fx_norm_tiles_noalloc: the tile origins, then the per-tile exact
+// sums (Σv, Σv² as u64). One copy per device (a __device__ variable lives in every context).
+// Concurrent calls on one device share it and race.
+namespace {
+constexpr int kNoAllocMaxTiles = 4096;
+constexpr size_t kNoAllocOrgBytes = sizeof(fxk::TileOrigin) * kNoAllocMaxTiles;        // 96 KiB
+constexpr size_t kNoAllocSumBytes = 2 * sizeof(unsigned long long) * kNoAllocMaxTiles;  // 64 KiB
+static_assert(kNoAllocOrgBytes % 256 == 0, "sums must start 256-byte aligned");
+static_assert(sizeof(fxk::TileOrigin) == 3 * sizeof(int64_t), "origins are copied as int64 triples");
+constexpr int kNoAllocMaxDevices = 64;
+}  // namespace
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocOrgBytes + kNoAllocSumBytes];
 
 namespace {
 
@@ -498,6 +512,53 @@ fx_status fx_accum_finalize(const float* dev_acc, int64_t dz, int64_t dy, int64_
             fxk::launch_accum_finalize(dev_acc, dz, dy, dx, z_begin, z_end, dev_wz, dev_wy, dev_wx, dev_prob, dev_u8, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_accum_finalize"));
+    });
+}
+
+
+fx_status fx_norm_tiles_noalloc(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx,
+                                const int64_t* host_origins, int ntiles, int patch, float* dev_out, void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!dev_vol || !host_origins || !dev_out || ntiles < 1 || patch < 1 || dz < 1 || dy < 1 || dx < 1)
+            return set_err(FX_INVALID_ARGUMENT, "fx_norm_tiles_noalloc: bad argument");
+        if (ntiles > kNoAllocMaxTiles)
+            return set_err(FX_INVALID_ARGUMENT, "fx_norm_tiles_noalloc: " + std::to_string(ntiles) +
+                                                    " tiles exceed the static scratch limit of " +
+                                                    std::to_string(kNoAllocMaxTiles) + " tiles per call");
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "fx_norm_tiles_noalloc: cudaGetDevice"));
+        if (dev < 0 || dev >= kNoAllocMaxDevices)
+            return set_err(FX_UNSUPPORTED, "fx_norm_tiles_noalloc: device index beyond 63");
+        // Set-up, once per device with that device current: the first call on a device resolves
+        // the scratch's address there.
+        static std::mutex mu;
+        static unsigned char* base_of[kNoAllocMaxDevices] = {};
+        unsigned char* base;
+        {
+            std::lock_guard<std::mutex> lock(mu);
+            if (!base_of[dev]) {
+                void* p = nullptr;
+                e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+                if (e != cudaSuccess || !p)
+                    return set_err(fxh::cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                                                    "fx_norm_tiles_noalloc: cudaGetSymbolAddress"));
+                base_of[dev] = static_cast<unsigned char*>(p);
+            }
+            base = base_of[dev];
+        }
+        auto* org = reinterpret_cast<fxk::TileOrigin*>(base);
+        auto* sums = reinterpret_cast<unsigned long long*>(base + kNoAllocOrgBytes);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        e = cudaMemcpyAsync(org, host_origins, sizeof(fxk::TileOrigin) * ntiles, cudaMemcpyHostToDevice, s);
+        // the sums are accumulated with atomics: they start at zero on every call
+        if (e == cudaSuccess) e = cudaMemsetAsync(sums, 0, 2 * sizeof(unsigned long long) * ntiles, s);
+        if (e == cudaSuccess) e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, org, ntiles, patch, sums, s);
+        if (e == cudaSuccess)
+            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, org, ntiles, patch, sums, nullptr, 0, fxk::kOpF16, dev_out,
+                                      s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles_noalloc"));
     });
 }
 

@@ -145,6 +145,17 @@ void fx_weight_profile(const float* g, int patch, const int64_t* starts, int64_t
 /* z-score `ntiles` tiles at the given origins of a device u8 volume into f32 [ntiles][P^3]. */
 fx_status fx_norm_tiles(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx, const int64_t* host_origins,
                         int ntiles, int patch, float* dev_out, void* stream);
+/* fx_norm_tiles without any device allocation. No reference counterpart: the reference
+ * allocates its patch buffers per call. This one keeps its scratch (tile origins and the
+ * per-tile exact sums) in a static 160 KiB __device__ array, so it serves callers that must not
+ * allocate: a process that has committed the device's memory to its volume and accumulators,
+ * and callers with work in flight on other streams, which cudaFree's implicit device-wide
+ * synchronisation would stall. Limit: ntiles <= 4096 per call; more is rejected with
+ * FX_INVALID_ARGUMENT. The first call on each device resolves the scratch's address
+ * (cudaGetSymbolAddress) and should come before any stream capture. Calls that overlap in time
+ * on the same device share the scratch and race. Synchronises `stream` before returning. */
+fx_status fx_norm_tiles_noalloc(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx,
+                                const int64_t* host_origins, int ntiles, int patch, float* dev_out, void* stream);
 /* One 3x3x3 conv (pad 1, stride 1 or 2, no bias) in f32 NCDHW device tensors, computed by the
  * tcgen05 kernel with `precision` operands (fp8: per-output-channel weight scales and a per-tensor
  * input scale), f32 accumulate, the output rounded once to f16 as the net's pre-norm store does.
