@@ -116,35 +116,77 @@ __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, in
     }
 }
 
-__global__ void in_finalize_kernel(const float* __restrict__ partials, int nrec, int C, double count,
-                                   const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
-                                   float* __restrict__ ss) {
-    // block: 32 channels x 32 record slices
-    const int b = blockIdx.y;
-    const int lane = threadIdx.x & 31;
-    const int slice = threadIdx.x >> 5;
+// Division by a divisor fixed at launch, by multiply and shift (Granlund & Montgomery, "Division
+// by invariant integers using multiplication", 1994): n / d = (umulhi(n, m) + n) >> s, exact for
+// n < 2^31 with s = ceil(log2 d) and m = floor(2^32 (2^s - d) / d) + 1.
+struct FastDiv {
+    uint32_t d, m, s;
+};
+FastDiv make_fastdiv(uint32_t d) {
+    uint32_t s = 0;
+    while ((1ull << s) < d) ++s;
+    const uint64_t m = ((1ull << 32) * ((1ull << s) - d)) / d + 1;
+    return {d, static_cast<uint32_t>(m), s};
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) { return (__umulhi(n, f.m) + n) >> f.s; }
+
+// InstanceNorm statistics, two levels. Block (channel block, batch, slice) sums its slice of the
+// records [B][nrec][C][2] in double and stores {Σ, Σ²} for 32 channels in work[B][S][C][2]; the
+// last block of a (batch, channel block) to finish — counted in done[], which it resets — adds
+// the S slices in slice order (the result does not depend on block scheduling) and writes
+// ss[B][C][2] = {gamma * rstd, beta - mean * gamma * rstd}.
+__global__ void __launch_bounds__(256) in_stats_kernel(const float* __restrict__ partials, int nrec, int C, int S,
+                                                       double count, const float* __restrict__ gamma,
+                                                       const float* __restrict__ beta, float eps,
+                                                       double* __restrict__ work, unsigned* __restrict__ done,
+                                                       float* __restrict__ ss) {
+    const int b = blockIdx.y, sl = blockIdx.z;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
+    const int r0 = static_cast<int>(static_cast<int64_t>(nrec) * sl / S);
+    const int r1 = static_cast<int>(static_cast<int64_t>(nrec) * (sl + 1) / S);
     double a1 = 0.0, a2 = 0.0;
     if (c < C) {
-        const float* base = partials + static_cast<int64_t>(b) * nrec * C * 2;
-        for (int r = slice; r < nrec; r += 32) {
-            const float2 v = *reinterpret_cast<const float2*>(base + (static_cast<int64_t>(r) * C + c) * 2);
+        const float2* base = reinterpret_cast<const float2*>(partials) + static_cast<int64_t>(b) * nrec * C + c;
+#pragma unroll 4
+        for (int r = r0 + w; r < r1; r += 8) {
+            const float2 v = __ldg(base + static_cast<int64_t>(r) * C);
             a1 += v.x;
             a2 += v.y;
         }
     }
-    __shared__ double s1[32][33], s2[32][33];
-    s1[slice][lane] = a1;
-    s2[slice][lane] = a2;
+    __shared__ double s1[8][32], s2[8][32];
+    s1[w][lane] = a1;
+    s2[w][lane] = a2;
     __syncthreads();
-    if (slice == 0 && c < C) {
-        double t1 = 0.0, t2 = 0.0;
-        for (int i = 0; i < 32; ++i) {
-            t1 += s1[i][lane];
-            t2 += s2[i][lane];
+    if (w != 0) return;
+    double t1 = 0.0, t2 = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        t1 += s1[i][lane];
+        t2 += s2[i][lane];
+    }
+    double* wb = work + static_cast<int64_t>(b) * S * C * 2;
+    if (c < C) {
+        wb[(static_cast<int64_t>(sl) * C + c) * 2] = t1;
+        wb[(static_cast<int64_t>(sl) * C + c) * 2 + 1] = t2;
+    }
+    __threadfence();
+    __syncwarp();
+    unsigned prev = 0;
+    unsigned* cnt = done + b * gridDim.x + blockIdx.x;
+    if (lane == 0) prev = atomicAdd(cnt, 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != static_cast<unsigned>(S - 1)) return;
+    __threadfence();
+    if (c < C) {
+        double u1 = 0.0, u2 = 0.0;
+        for (int k = 0; k < S; ++k) {
+            u1 += __ldcg(wb + (static_cast<int64_t>(k) * C + c) * 2);
+            u2 += __ldcg(wb + (static_cast<int64_t>(k) * C + c) * 2 + 1);
         }
-        const double mean = t1 / count;
-        double var = t2 / count - mean * mean;
+        const double mean = u1 / count;
+        double var = u2 / count - mean * mean;
         if (var < 0.0) var = 0.0;
         const double rstd = 1.0 / sqrt(var + static_cast<double>(eps));
         const double sc = static_cast<double>(gamma ? gamma[c] : 1.f) * rstd;
@@ -152,8 +194,8 @@ __global__ void in_finalize_kernel(const float* __restrict__ partials, int nrec,
         ss[(static_cast<int64_t>(b) * C + c) * 2 + 0] = static_cast<float>(sc);
         ss[(static_cast<int64_t>(b) * C + c) * 2 + 1] = static_cast<float>(sh);
     }
+    if (lane == 0) *cnt = 0u;
 }
-
 
 __device__ __forceinline__ void store_dest(const NormDest& d, int b, int gout, int64_t row, int zp, int yp, int xp,
                                            const float* y, int n) {
@@ -181,46 +223,65 @@ __device__ __forceinline__ void store_dest(const NormDest& d, int b, int gout, i
     }
 }
 
-// One thread = one interior voxel x one 16-channel pair of bf16 pre-norm cells (or the single
-// 8-channel cell when C is not a multiple of 16).
-__global__ void norm_act_kernel(const uint8_t* __restrict__ pre, int64_t pbs, int64_t pgs, GridGeom g, int C,
-                                int B, const float* __restrict__ ss, float slope, NormDest d0, NormDest d1,
-                                unsigned* amax, int cpt) {
+// Block = (plane chunk, z, batch x channel group); thread = kNormVox interior voxels of one z
+// plane x CPT channels (one 16-channel e4m3 cell, or one or two 8-channel f16 cells). The cells
+// of all kNormVox voxels are loaded before any is used, for memory-level parallelism.
+constexpr int kNormThreads = 256, kNormVox = 4;
+template <int CPT>
+__global__ void __launch_bounds__(kNormThreads, 2) norm_act_kernel(const uint8_t* __restrict__ pre, int64_t pbs,
+                                                                int64_t pgs, GridGeom g, FastDiv fw, int C,
+                                                                const float* __restrict__ ss, float slope,
+                                                                NormDest d0, NormDest d1, unsigned* amax) {
+    constexpr int NC = CPT / 8;  // f16 cells per voxel
+    const int ngo = C / CPT;
+    const int b = blockIdx.z / ngo, go = blockIdx.z - b * ngo;
+    const int gi0 = go * NC;
+    const int zp = blockIdx.y + 1;
     const int Hp = g.H + 2, Wp = g.W + 2;
-    const int64_t vox = static_cast<int64_t>(g.D) * g.H * g.W;
-    const int ngo = C / cpt;
-    const int64_t total = vox * ngo * B;
+    const uint32_t HW = static_cast<uint32_t>(g.H) * g.W;
+    __shared__ float2 s_ss[CPT];  // {scale, shift} of the block's channels
+    if (threadIdx.x < CPT)
+        s_ss[threadIdx.x] = __ldg(reinterpret_cast<const float2*>(ss) + static_cast<int64_t>(b) * C + gi0 * 8 +
+                                  threadIdx.x);
+    __syncthreads();
+    const uint8_t* pb = pre + b * pbs + gi0 * pgs;
+    uint4 cell[kNormVox][NC];
+    int yp[kNormVox], xp[kNormVox];
+    const uint32_t i0 = blockIdx.x * (kNormThreads * kNormVox) + threadIdx.x;
+#pragma unroll
+    for (int k = 0; k < kNormVox; ++k) {
+        const uint32_t i = i0 + k * kNormThreads;
+        yp[k] = -1;
+        if (i < HW) {
+            const uint32_t y = fdiv(i, fw);
+            yp[k] = static_cast<int>(y) + 1;
+            xp[k] = static_cast<int>(i - y * fw.d) + 1;
+            const int64_t row = (static_cast<int64_t>(zp) * Hp + yp[k]) * Wp + xp[k];
+#pragma unroll
+            for (int q = 0; q < NC; ++q) cell[k][q] = __ldcs(reinterpret_cast<const uint4*>(pb + q * pgs + row * 16));
+        }
+    }
     float mx = 0.f;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int x = static_cast<int>(i % g.W);
-        int64_t t = i / g.W;
-        const int y = static_cast<int>(t % g.H);
-        t /= g.H;
-        const int z = static_cast<int>(t % g.D);
-        t /= g.D;
-        const int go = static_cast<int>(t % ngo);
-        const int b = static_cast<int>(t / ngo);
-        const int zp = z + 1, yp = y + 1, xp = x + 1;
-        const int64_t row = (static_cast<int64_t>(zp) * Hp + yp) * Wp + xp;
-        float v[16];
-        const int gi0 = go * cpt / 8;
-        for (int k = 0; k < cpt / 8; ++k) {
-            const uint4 w = *reinterpret_cast<const uint4*>(pre + b * pbs + (gi0 + k) * pgs + row * 16);
+#pragma unroll
+    for (int k = 0; k < kNormVox; ++k) {
+        if (yp[k] < 0) continue;
+        float v[CPT];
+#pragma unroll
+        for (int q = 0; q < NC; ++q) {
             float f[8];
-            unpack_cell16(w, kOpF16, f);
+            unpack_cell16(cell[k][q], kOpF16, f);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                const int c = (gi0 + k) * 8 + j;
-                const float2 sc = *reinterpret_cast<const float2*>(ss + (static_cast<int64_t>(b) * C + c) * 2);
-                float yv = fmaf(f[j], sc.x, sc.y);
+                const float2 t = s_ss[q * 8 + j];
+                float yv = fmaf(f[j], t.x, t.y);
                 yv = yv >= 0.f ? yv : yv * slope;
-                v[k * 8 + j] = yv;
+                v[q * 8 + j] = yv;
                 mx = fmaxf(mx, fabsf(yv));
             }
         }
-        store_dest(d0, b, d0.dtype == kOpE4M3 ? go : gi0, row, zp, yp, xp, v, cpt);
-        store_dest(d1, b, d1.dtype == kOpE4M3 ? go : gi0, row, zp, yp, xp, v, cpt);
+        const int64_t row = (static_cast<int64_t>(zp) * Hp + yp[k]) * Wp + xp[k];
+        store_dest(d0, b, d0.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
+        store_dest(d1, b, d1.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
     }
     if (amax) {
         for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -231,54 +292,62 @@ __global__ void norm_act_kernel(const uint8_t* __restrict__ pre, int64_t pbs, in
 __constant__ float c_head_w[2 * 64];
 __constant__ float c_head_b[2];
 
-__global__ void head_blend_kernel(HeadParams h) {
+// Block = (plane chunk, z, batch item); thread = one voxel. Scale/shift of the batch item's C
+// channels sit in shared memory, the head weights in constant memory.
+__global__ void __launch_bounds__(kEwThreads) head_blend_kernel(HeadParams h, FastDiv fp) {
     const int P = h.P, Pp = P + 2;
-    const int64_t n = static_cast<int64_t>(P) * P * P;
+    const int b = blockIdx.z, z = blockIdx.y;
+    __shared__ float2 s_ss[64];
+    if (threadIdx.x < h.C)
+        s_ss[threadIdx.x] = __ldg(reinterpret_cast<const float2*>(h.ss) + static_cast<int64_t>(b) * h.C + threadIdx.x);
+    __syncthreads();
+    const uint32_t i = blockIdx.x * kEwThreads + threadIdx.x;
+    if (i >= static_cast<uint32_t>(P) * P) return;
+    const int y = static_cast<int>(fdiv(i, fp));
+    const int x = static_cast<int>(i - static_cast<uint32_t>(y) * P);
     const int G = h.C / 8;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n * h.B;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int b = static_cast<int>(i / n);
-        const int64_t li = i - b * n;
-        const int x = static_cast<int>(li % P);
-        const int y = static_cast<int>((li / P) % P);
-        const int z = static_cast<int>(li / (static_cast<int64_t>(P) * P));
-        const int64_t row = (static_cast<int64_t>(z + 1) * Pp + (y + 1)) * Pp + (x + 1);
-        float l0 = c_head_b[0], l1 = h.ncls > 1 ? c_head_b[1] : 0.f;
-        for (int gi = 0; gi < G; ++gi) {
-            const uint4 w = *reinterpret_cast<const uint4*>(h.pre + b * h.pre_batch_stride + gi * h.pre_group_stride +
-                                                            row * 16);
-            float f[8];
-            unpack_cell16(w, kOpF16, f);
+    const int64_t row = (static_cast<int64_t>(z + 1) * Pp + (y + 1)) * Pp + (x + 1);
+    const uint8_t* pb = h.pre + b * h.pre_batch_stride + row * 16;
+    uint4 cells[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int c = gi * 8 + j;
-                const float2 sc = *reinterpret_cast<const float2*>(h.ss + (static_cast<int64_t>(b) * h.C + c) * 2);
-                float yv = fmaf(f[j], sc.x, sc.y);
-                yv = yv >= 0.f ? yv : yv * h.slope;
-                l0 = fmaf(c_head_w[c], yv, l0);
-                if (h.ncls > 1) l1 = fmaf(c_head_w[h.C + c], yv, l1);
-            }
+    for (int gi = 0; gi < 8; ++gi)
+        if (gi < G) cells[gi] = __ldcs(reinterpret_cast<const uint4*>(pb + gi * h.pre_group_stride));
+    float l0 = c_head_b[0], l1 = h.ncls > 1 ? c_head_b[1] : 0.f;
+#pragma unroll
+    for (int gi = 0; gi < 8; ++gi) {
+        if (gi >= G) break;
+        float f[8];
+        unpack_cell16(cells[gi], kOpF16, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int c = gi * 8 + j;
+            const float2 sc = s_ss[c];
+            float yv = fmaf(f[j], sc.x, sc.y);
+            yv = yv >= 0.f ? yv : yv * h.slope;
+            l0 = fmaf(c_head_w[c], yv, l0);
+            if (h.ncls > 1) l1 = fmaf(c_head_w[h.C + c], yv, l1);
         }
-        float p;
-        if (h.sigmoid) {
-            p = 1.f / (1.f + expf(-l0));
-        } else {
-            const float m = fmaxf(l0, l1);
-            const float e0 = expf(l0 - m), e1 = expf(l1 - m);
-            p = (h.channel == 1 ? e1 : e0) / (e0 + e1);
-        }
-        if (isnan(p)) p = 0.f;
-        else if (isinf(p)) p = p > 0.f ? 1.f : 0.f;
-        if (h.prob) h.prob[i] = p;
-        if (h.acc) {
-            const TileOrigin t = h.tiles[b];
-            const int64_t oz = t.z0 + z, oy = t.y0 + y, ox = t.x0 + x;
-            if (oz < h.dz && oy < h.dy && ox < h.dx) {
-                // (gz*gy)*gx*p in the reference's order (src/ml/infer.hpp:631-653)
-                const float wzy = __fmul_rn(__ldg(h.gauss + z), __ldg(h.gauss + y));
-                const float c = __fmul_rn(__fmul_rn(wzy, __ldg(h.gauss + x)), p);
-                atomicAdd(h.acc + (oz * h.dy + oy) * h.dx + ox, c);
-            }
+    }
+    float p;
+    if (h.sigmoid) {
+        p = 1.f / (1.f + expf(-l0));
+    } else {
+        const float m = fmaxf(l0, l1);
+        const float e0 = expf(l0 - m), e1 = expf(l1 - m);
+        p = (h.channel == 1 ? e1 : e0) / (e0 + e1);
+    }
+    if (isnan(p)) p = 0.f;
+    else if (isinf(p)) p = p > 0.f ? 1.f : 0.f;
+    const int64_t n = static_cast<int64_t>(P) * P * P;
+    if (h.prob) h.prob[b * n + static_cast<int64_t>(z) * P * P + i] = p;
+    if (h.acc) {
+        const TileOrigin t = h.tiles[b];
+        const int64_t oz = t.z0 + z, oy = t.y0 + y, ox = t.x0 + x;
+        if (oz < h.dz && oy < h.dy && ox < h.dx) {
+            // (gz*gy)*gx*p in the reference's order (src/ml/infer.hpp:631-653)
+            const float wzy = __fmul_rn(__ldg(h.gauss + z), __ldg(h.gauss + y));
+            const float c = __fmul_rn(__fmul_rn(wzy, __ldg(h.gauss + x)), p);
+            atomicAdd(h.acc + (oz * h.dy + oy) * h.dx + ox, c);
         }
     }
 }
@@ -359,10 +428,15 @@ cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
     return cudaGetLastError();
 }
 
+int in_stats_slices(int nrec) { return nrec < 256 ? 1 : (nrec / 256 < kMaxStatSlices ? nrec / 256 : kMaxStatSlices); }
+
 cudaError_t launch_in_finalize(const float* partials, int B, int nrec, int C, double count, const float* gamma,
-                               const float* beta, float eps, float* ss, cudaStream_t s) {
+                               const float* beta, float eps, double* work, unsigned* done, float* ss, cudaStream_t s) {
+    if (nrec < 1 || C < 1 || B < 1) return cudaErrorInvalidValue;
+    const int S = in_stats_slices(nrec);
     count_launch();
-    in_finalize_kernel<<<dim3((C + 31) / 32, B), 1024, 0, s>>>(partials, nrec, C, count, gamma, beta, eps, ss);
+    in_stats_kernel<<<dim3((C + 31) / 32, B, S), 256, 0, s>>>(partials, nrec, C, S, count, gamma, beta, eps, work,
+                                                             done, ss);
     return cudaGetLastError();
 }
 
@@ -370,23 +444,30 @@ cudaError_t launch_norm_act(const uint8_t* pre, int64_t pbs, int64_t pgs, GridGe
                             float slope, NormDest d0, NormDest d1, unsigned* amax, cudaStream_t s) {
     const bool any_fp8 = (d0.ptr && d0.dtype == kOpE4M3) || (d1.ptr && d1.dtype == kOpE4M3);
     const int cpt = (any_fp8 || C % 16 == 0) ? 16 : 8;
-    const int64_t total = static_cast<int64_t>(g.D) * g.H * g.W * (C / cpt) * B;
+    if (C % cpt || static_cast<int64_t>(g.H) * g.W >= (1ll << 31) || g.D > 65535 || B * (C / cpt) > 65535)
+        return cudaErrorInvalidValue;
+    const uint32_t HW = static_cast<uint32_t>(g.H) * g.W;
+    const dim3 grid((HW + kNormThreads * kNormVox - 1) / (kNormThreads * kNormVox), g.D, B * (C / cpt));
+    const FastDiv fw = make_fastdiv(static_cast<uint32_t>(g.W));
     count_launch();
-    norm_act_kernel<<<grid_for(total, kEwThreads), kEwThreads, 0, s>>>(pre, pbs, pgs, g, C, B, ss, slope, d0, d1,
-                                                                       amax, cpt);
+    if (cpt == 16)
+        norm_act_kernel<16><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+    else
+        norm_act_kernel<8><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
     return cudaGetLastError();
 }
 
 cudaError_t launch_head_blend(const HeadParams& h, cudaStream_t s) {
-    if (h.ncls < 1 || h.ncls > 2 || h.C > 64 || h.C % 8) return cudaErrorInvalidValue;
+    if (h.ncls < 1 || h.ncls > 2 || h.C > 64 || h.C % 8 || h.P > 46340 || h.B > 65535) return cudaErrorInvalidValue;
     cudaError_t e = cudaMemcpyToSymbolAsync(c_head_w, h.wh, sizeof(float) * h.ncls * h.C, 0,
                                             cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return e;
     e = cudaMemcpyToSymbolAsync(c_head_b, h.bh, sizeof(float) * h.ncls, 0, cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return e;
-    const int64_t n = static_cast<int64_t>(h.P) * h.P * h.P * h.B;
+    const uint32_t PP = static_cast<uint32_t>(h.P) * h.P;
     count_launch();
-    head_blend_kernel<<<grid_for(n, kEwThreads), kEwThreads, 0, s>>>(h);
+    head_blend_kernel<<<dim3((PP + kEwThreads - 1) / kEwThreads, h.P, h.B), kEwThreads, 0, s>>>(
+        h, make_fastdiv(static_cast<uint32_t>(h.P)));
     return cudaGetLastError();
 }
 

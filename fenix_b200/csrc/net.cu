@@ -325,8 +325,14 @@ Status Net::alloc() {
     d_sums_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * 2 * Bmax_));
     d_amax_ = static_cast<unsigned*>(dalloc(sizeof(unsigned) * 5 * S_));
     d_status_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t)));
-    if (!d_sums_ || !d_amax_ || !d_status_) return fail(kInternal, "cudaMalloc: control buffers");
+    const int cmax = *std::max_element(F_.begin(), F_.end());
+    const size_t ndone = static_cast<size_t>(Bmax_) * ((cmax + 31) / 32);
+    d_stat_work_ = static_cast<double*>(dalloc(sizeof(double) * Bmax_ * fxk::kMaxStatSlices * cmax * 2));
+    d_stat_done_ = static_cast<unsigned*>(dalloc(sizeof(unsigned) * ndone));
+    if (!d_sums_ || !d_amax_ || !d_status_ || !d_stat_work_ || !d_stat_done_)
+        return fail(kInternal, "cudaMalloc: control buffers");
     cudaMemset(d_status_, 0, sizeof(uint32_t));
+    cudaMemset(d_stat_done_, 0, sizeof(unsigned) * ndone);
     std::vector<float> g = gaussian1d(P_);
     Status st = upload(d_gauss_, g, this, allocs_);
     if (!st.ok()) return st;
@@ -487,7 +493,7 @@ Status Net::finalize_in(Layer& L, int nb, cudaStream_t s) {
     const ActGeom g = level(L.lout);
     const double count = static_cast<double>(g.D) * g.H * g.W;
     return cuda_status(fxk::launch_in_finalize(L.d_partials, nb, L.nrec, L.Cout, count, L.d_gamma, L.d_beta, kEps,
-                                               L.d_ss, s),
+                                               d_stat_work_, d_stat_done_, L.d_ss, s),
                        "in_finalize");
 }
 

@@ -155,6 +155,8 @@ class Net {
     std::vector<uint8_t*> pn_, act_, cat_, ph_;
     unsigned long long* d_sums_ = nullptr;
     unsigned* d_amax_ = nullptr;  // calibration amax slots
+    double* d_stat_work_ = nullptr;  // InstanceNorm slice sums [Bmax][kMaxStatSlices][Cmax][2]
+    unsigned* d_stat_done_ = nullptr;  // slice counters [Bmax][Cmax / 32], zero between launches
     std::vector<float> amax_;
     float* d_gauss_ = nullptr;
     uint32_t* d_status_ = nullptr;
