@@ -35,6 +35,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "Mvoxels/s fp8 3D-UNet sliding-window inference @1/2/4/8 B200; % tcgen05 peak"
 FEATURES = (32, 64, 128, 256, 320)
 WEIGHT_SEED, VOLUME_SEED, CALIB_SEED0 = 1, 2, 1000
+# DRAM traffic of the 22 conv launches of one fp8 forward, per 128^3 tile (dram__bytes_read.sum +
+# dram__bytes_write.sum from an ncu launch list of `bench.py --size 256 --steps 1 --warmup 3`:
+# 4.565 GB read + 5.806 GB written per forward of 8 tiles). ncu cannot run inside the timed bench,
+# so the captured figure is carried here and re-captured when the conv kernel changes.
+CONV_DRAM_BYTES_PER_TILE = (4.565e9 + 5.806e9) / 8
 
 
 def env_int(name, default):
@@ -110,6 +115,17 @@ def cpu_reference(weights, P, overlap, threads=None, dims=(192, 128, 128)):
     return per_tile, int(info["threads"]), sample
 
 
+def workload_config(args, tiles, world):
+    S, P = args.size, args.patch
+    return {
+        "workload": f"fp8 sliding-window inference, {S}^3 u8 volume, {P}^3 tiles, overlap {args.overlap}, "
+                    f"{tiles} tiles, Gaussian blend, u8 output; 5-stage UNet 32/64/128/256/320",
+        "volume": [S, S, S], "patch": P, "overlap": args.overlap, "tiles": tiles, "batch": args.batch,
+        "precision": args.precision, "parallelism": f"z-slab x{world}",
+        "l2": f"inputs larger than L2: {S}^3 u8 volume + {S}^3 f32 accumulator per step",
+    }
+
+
 def run_reference_arm(args):
     rank = env_int("RANK", 0)
     if rank != 0:
@@ -136,9 +152,9 @@ def run_reference_arm(args):
     line = {"metric": METRIC, "value": value, "unit": "Mvoxels/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_tile * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"sliding-window {S}^3, {args.patch}^3 tiles, overlap {args.overlap}, 5-stage UNet "
-                                   "32/64/128/256/320 (each step: one 128^3 tile through the reference's CPU path)"},
-            "cpu_baseline": {"value": value, "unit": "Mvoxels/s", "cores": thr, "kind": "reference", "sample": sample},
+            "config": workload_config(args, tiles, args.gpus),
+            "cpu_baseline": {"value": value, "unit": "Mvoxels/s", "cores": thr, "kind": "reference",
+                             "sample": sample + "; each step: one 128^3 tile through the reference's CPU path, fp32"},
             "e2e": {"value": value, "unit": "Mvoxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
@@ -278,18 +294,14 @@ def main():
             "metric": METRIC, "value": value, "unit": "Mvoxels/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": {"fp8": "e4m3", "f16": "f16", "bf16": "bf16"}[args.precision],
-            "data": "synthetic: 1024^3 u8 spiral sheet (pitch 16, thickness 3, N(170,15)/N(40,10), blur 1, N(0,8) "
+            "data": f"synthetic: {S}^3 u8 spiral sheet (pitch 16, thickness 3, N(170,15)/N(40,10), blur 1, N(0,8) "
                     "speckle, seed 2); random-init Kaiming weights (seed 1); fp8 scales calibrated on 4 seeded patches",
-            "config": {
-                "workload": f"fp8 sliding-window inference, {S}^3 u8 volume, {P}^3 tiles, overlap {args.overlap}, "
-                            f"{tiles} tiles, Gaussian blend, u8 output; 5-stage UNet 32/64/128/256/320",
-                "volume": [S, S, S], "patch": P, "overlap": args.overlap, "tiles": tiles, "batch": args.batch,
-                "precision": args.precision, "parallelism": f"z-slab x{world}",
-                "l2": "inputs larger than L2: 1 GiB u8 volume + 4 GiB f32 accumulator per step",
-            },
+            "config": workload_config(args, tiles, world),
             "roofline": {
                 "bound": "tensor", "achieved": conv_tflops, "peak": peak, "unit": "TFLOP/s", "frac": conv_tflops / peak,
-                "traffic": None,
+                "traffic": CONV_DRAM_BYTES_PER_TILE if args.precision == "fp8" else None,
+                "traffic_unit": "DRAM bytes per 128^3 tile over the 22 conv launches (ncu capture, 256^3 bench)",
+                "algorithmic_flops_per_tile": 945.2e9,
                 "kernel": "conv_tc_kernel (all 22 conv launches of one forward, summed)",
                 "peak_source": (f"2 x {peak_src} bf16 burst (e4m3 rate is twice bf16 on tcgen05)" if args.precision == "fp8"
                                 else f"{peak_src} bf16 burst"),

@@ -64,6 +64,22 @@ def exchanges(plans: list[RankPlan]):
     return ex
 
 
+def exchange_bands(acc, z_lo: int, send, recv, group, add) -> None:
+    """Send this rank's accumulator planes that other ranks own, receive the bands it owns and
+    fold them in with add(dst_view, src). acc holds planes [z_lo, z_lo + len(acc)); send is a list
+    of (dst, z0, z1), recv of (src, z0, z1, buffer). Works for any torch device the process group
+    supports (NCCL on GPUs, gloo on CPU tensors)."""
+    import torch.distributed as dist
+
+    ops = [dist.P2POp(dist.isend, acc[z0 - z_lo:z1 - z_lo].contiguous(), dst, group=group) for dst, z0, z1 in send]
+    ops += [dist.P2POp(dist.irecv, buf, src, group=group) for src, z0, z1, buf in recv]
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+    for src, z0, z1, buf in recv:
+        add(acc[z0 - z_lo:z1 - z_lo], buf)
+
+
 class ShardedPredictor:
     """Runs one rank's share of a sliding-window prediction of a (D, H, W) u8 volume."""
 
@@ -122,19 +138,8 @@ class ShardedPredictor:
                                            self.batch, me.tile_begin, me.tile_end, self.acc.data_ptr(),
                                            channel=self.channel, sigmoid=self.sigmoid, stream=sp)
             if self.world > 1 and self.ex:
-                import torch.distributed as dist
-
-                ops = []
-                for dst, z0, z1 in self.send:
-                    ops.append(dist.P2POp(dist.isend, self.acc[z0 - me.z_lo:z1 - me.z_lo], dst, group=self.group))
-                for src, z0, z1, buf in self.recv:
-                    ops.append(dist.P2POp(dist.irecv, buf, src, group=self.group))
-                if ops:
-                    for w in dist.batch_isend_irecv(ops):
-                        w.wait()
-                for src, z0, z1, buf in self.recv:
-                    dst = self.acc[z0 - me.z_lo:z1 - me.z_lo]
-                    check(L.fx_accum_add(dst.data_ptr(), buf.data_ptr(), buf.numel(), sp))
+                exchange_bands(self.acc, me.z_lo, self.send, self.recv, self.group,
+                               lambda dst, src: check(L.fx_accum_add(dst.data_ptr(), src.data_ptr(), src.numel(), sp)))
             n_own = me.own_hi - me.own_lo
             if n_own > 0:
                 # Wz is indexed by slab-local z: start the profile at plane z_lo

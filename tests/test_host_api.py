@@ -45,6 +45,10 @@ def test_host_api_window_matches_binding(cuda_torch, host_api_bin, tmp_path):
     window, u8_b2, vol = (raw[i * n:(i + 1) * n].reshape(dims) for i in range(3))
     net = fx.Net(w, 128, max_batch=3, precision="f16")
     _, want = net.predict_volume(vol, overlap=0.25, batch=3)
-    # at most two tiles cover any voxel here, so the blend sums do not depend on tile order
+    # same net shape and batch: identical (at most two tiles cover any voxel here, so the blend
+    # sums do not depend on tile order)
     assert np.array_equal(window, want)
-    assert np.array_equal(u8_b2, want)
+    # another max batch changes the conv's row blocking and so the float summation order of the
+    # InstanceNorm statistics: equal within the f16 path's tolerance (u8 steps of 1/255)
+    d = np.abs(u8_b2.astype(int) - want.astype(int))
+    assert d.max() <= 4 and d.mean() < 0.05
