@@ -15,7 +15,8 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitima
 // Optional cycle accounting per role (build with -DFX_CONV_TRACE; p.trace gets 16 counters):
 // [0] producer waiting for free stages, [1] producer issuing, [2] MMA waiting for drained
 // accumulators, [3] MMA waiting for full stages, [4] MMA issuing, [5] epilogue waiting for
-// accumulators, [6] epilogue draining, [7] MMAs issued, [8] units.
+// accumulators, [6] epilogue draining, [7] MMAs issued, [8] units, [9] epilogue waiting for
+// TMEM loads (part of [6]).
 #ifdef FX_CONV_TRACE
 #define FX_T0() const long long fx_t0_ = clock64()
 #define FX_TADD(p, i) \
@@ -243,12 +244,15 @@ struct RowDecomp {
     }
 };
 
-// Epilogue for N_tile = 16 * NCH columns: 4 warps drain the TMEM accumulator of each unit
-// (warp w owns TMEM lanes 32 (w % 4) .. +31, i.e. one output row per thread per M block).
+// Epilogue for N_tile = 16 * NCH columns: 8 warps drain the TMEM accumulator of each unit
+// (warp w owns TMEM lanes 32 (w % 4) .. +31, i.e. one output row per thread per M block; the two
+// warps of a lane quarter take alternate M blocks). Each warp writes one statistics record per
+// unit (zeros when the unit has no M block for it).
 template <int NCH>
 __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const int lane = threadIdx.x & 31;
-    const int wq = (threadIdx.x >> 5) & 3;
+    const int wq = (threadIdx.x >> 5) & 3;            // TMEM lane quarter of this warp (warp id % 4)
+    const int half = ((threadIdx.x >> 5) - 2) >> 2;   // 0: even M blocks of a unit, 1: odd
     const uint32_t tbase = ctl->tmem_base;
     const uint32_t slot_cols = static_cast<uint32_t>(p.R * p.N_tile);
     const int Mtot = 128 * p.R;
@@ -289,7 +293,7 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         for (int c = 0; c < kR; ++c)
 #pragma unroll
             for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
-        for (int r = 0; r < p.R; ++r) {
+        for (int r = half; r < p.R; r += 2) {
             const int64_t row = q0 + r * 128 + wq * 32 + lane;
             uint32_t z, y, x;
             rd.split(static_cast<uint32_t>(row), z, y, x);
@@ -299,9 +303,16 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
 #pragma unroll
             for (int g0 = 0; g0 < NCH; g0 += kGrp) {
                 uint32_t raw[kGrp][16];
+#ifdef FX_CONV_TRACE
+                const long long fx_tl0_ = clock64();
+#endif
 #pragma unroll
                 for (int c = 0; c < kGrp; ++c) tmem_ld16_nowait(taddr + (g0 + c) * 16, raw[c]);
                 tmem_wait();
+#ifdef FX_CONV_TRACE
+                if (threadIdx.x == 64 && p.trace)
+                    atomicAdd(p.trace + 9, static_cast<unsigned long long>(clock64() - fx_tl0_));
+#endif
 #pragma unroll
                 for (int c = 0; c < kGrp; ++c) tmem_regs_ready(raw[c]);
 #pragma unroll
@@ -382,7 +393,8 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                     s2[c] = warp_transpose_reduce16(r2[c], lane);
                 }
             }
-            float* dst = p.stats + ((static_cast<int64_t>(b) * p.n_units_m + mu) * 4 + wq) * p.stats_C * 2;
+            float* dst = p.stats +
+                         ((static_cast<int64_t>(b) * p.n_units_m + mu) * kStatRecsPerUnit + half * 4 + wq) * p.stats_C * 2;
             if (lane < 16) {
 #pragma unroll
                 for (int c = 0; c < NCH; ++c) {
@@ -415,7 +427,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&ctl->accf[i]), 1);
-            mbar_init(smem_u32(&ctl->acce[i]), 4);
+            mbar_init(smem_u32(&ctl->acce[i]), kEpiWarps);
         }
         mbar_init(smem_u32(&ctl->drain), 1);
         ctl->abort = 0;

@@ -17,7 +17,7 @@
 // copy of a window of rows for a range of groups + the matching packed weight block) and, per
 // stage, the list of MMAs (A offset, K-half stride, B offset). The kernel is persistent and
 // warp specialised: warp 0 issues the bulk copies, warp 1 issues tcgen05.mma from one thread
-// and owns the TMEM allocation, warps 2..5 drain the TMEM accumulators (epilogue).
+// and owns the TMEM allocation, warps 2..9 drain the TMEM accumulators (epilogue).
 #pragma once
 
 #include <cstdint>
@@ -26,7 +26,10 @@
 
 namespace fxk {
 
-constexpr int kConvThreads = 192;
+constexpr int kConvThreads = 320;  // warp 0 producer, warp 1 MMA issuer, warps 2..9 epilogue
+constexpr int kEpiWarps = 8;        // two per TMEM lane quarter, splitting the M blocks of a unit
+// InstanceNorm partial records written per work unit: one per epilogue warp.
+constexpr int kStatRecsPerUnit = kEpiWarps;
 constexpr int kMaxSrc = 8;
 
 struct ConvStage {

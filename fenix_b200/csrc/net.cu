@@ -286,7 +286,7 @@ Status Net::build_layer(Layer& L, int q) {
     if (L.kind != Layer::kUp && !L.d_partials) {
         const ActGeom g = level(L.lout);
         const int64_t rows = static_cast<int64_t>(g.D) * (g.H + 2) * (g.W + 2);
-        const int64_t nrec_max = ((rows + 127) / 128) * 4;
+        const int64_t nrec_max = ((rows + 127) / 128) * fxk::kStatRecsPerUnit;
         L.d_partials = static_cast<float*>(dalloc(sizeof(float) * Bmax_ * nrec_max * L.Cout * 2));
         L.d_ss = static_cast<float*>(dalloc(sizeof(float) * Bmax_ * L.Cout * 2));
         if (!L.d_partials || !L.d_ss) return fail(kInternal, "cudaMalloc: stats buffers");
@@ -482,7 +482,7 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
         p.mode = fxk::kModePrenorm;
         p.stats = L.d_partials;
         p.stats_C = L.Cout;
-        L.nrec = dp.n_units_m * 4;
+        L.nrec = dp.n_units_m * fxk::kStatRecsPerUnit;
     }
     const int64_t units = static_cast<int64_t>(nb) * p.n_units_m * p.n_tiles;
     const int grid = static_cast<int>(std::min<int64_t>(units, sm_count_));
