@@ -245,14 +245,15 @@ struct RowDecomp {
 };
 
 // Epilogue for N_tile = 16 * NCH columns: 8 warps drain the TMEM accumulator of each unit
-// (warp w owns TMEM lanes 32 (w % 4) .. +31, i.e. one output row per thread per M block; the two
-// warps of a lane quarter take alternate M blocks). Each warp writes one statistics record per
-// unit (zeros when the unit has no M block for it).
-template <int NCH>
+// (warp w owns TMEM lanes 32 (w % 4) .. +31, i.e. one output row per thread per M block). The two
+// warps of a lane quarter split the work: alternate M blocks when a unit has several (SPLITC
+// false), alternate 16-column chunks when it has one (SPLITC true). Each warp writes one
+// statistics record per unit; entries of channels it did not handle are written as zeros.
+template <int NCH, bool SPLITC>
 __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const int lane = threadIdx.x & 31;
     const int wq = (threadIdx.x >> 5) & 3;            // TMEM lane quarter of this warp (warp id % 4)
-    const int half = ((threadIdx.x >> 5) - 2) >> 2;   // 0: even M blocks of a unit, 1: odd
+    const int half = ((threadIdx.x >> 5) - 2) >> 2;   // which of the two warps of the quarter
     const uint32_t tbase = ctl->tmem_base;
     const uint32_t slot_cols = static_cast<uint32_t>(p.R * p.N_tile);
     const int Mtot = 128 * p.R;
@@ -264,9 +265,14 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const uint32_t zmax = static_cast<uint32_t>(p.Dp - 2), ymax = static_cast<uint32_t>(p.Hp - 2),
                    xmax = static_cast<uint32_t>(p.Wp - 2);
     const bool prenorm = p.mode == kModePrenorm;
-    constexpr bool kAccR = NCH <= 2;         // sum over M blocks in registers, one butterfly per unit
-    constexpr int kGrp = NCH < 4 ? NCH : 4;  // chunks loaded from TMEM per wait
-    constexpr int kR = kAccR ? NCH : 1;
+    constexpr int kMy = SPLITC ? NCH / 2 : NCH;  // chunks of an M block handled by this warp
+    constexpr int kCs = SPLITC ? 2 : 1;           // chunk stride
+    const int c0 = SPLITC ? half : 0;             // first chunk
+    const int rb = SPLITC ? 0 : half, rs = SPLITC ? 1 : 2;
+    constexpr bool kAccR = kMy <= 2;         // sum over M blocks in registers, one butterfly per unit
+    constexpr int kGrp = kMy < 4 ? kMy : (kMy == 4 ? 4 : 2);  // chunks loaded from TMEM per wait
+    constexpr int kR = kAccR ? kMy : 1;
+    const bool e4out = p.out_type == kOpE4M3;
     uint32_t j = 0;
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
         int b, mu, nt;
@@ -285,15 +291,15 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         FX_T0();
         const int64_t q0 = p.row_begin + static_cast<int64_t>(mu) * Mtot;
         const int cbase = nt * p.N_tile;  // first global column of this tile
-        float s1[NCH], s2[NCH];
+        float s1[kMy], s2[kMy];
         float r1[kR][16], r2[kR][16];
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) s1[c] = s2[c] = 0.f;
+        for (int c = 0; c < kMy; ++c) s1[c] = s2[c] = 0.f;
 #pragma unroll
         for (int c = 0; c < kR; ++c)
 #pragma unroll
             for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
-        for (int r = half; r < p.R; r += 2) {
+        for (int r = rb; r < p.R; r += rs) {
             const int64_t row = q0 + r * 128 + wq * 32 + lane;
             uint32_t z, y, x;
             rd.split(static_cast<uint32_t>(row), z, y, x);
@@ -301,13 +307,13 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
             const uint32_t taddr =
                 tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + r * p.N_tile;
 #pragma unroll
-            for (int g0 = 0; g0 < NCH; g0 += kGrp) {
+            for (int g0 = 0; g0 < kMy; g0 += kGrp) {
                 uint32_t raw[kGrp][16];
 #ifdef FX_CONV_TRACE
                 const long long fx_tl0_ = clock64();
 #endif
 #pragma unroll
-                for (int c = 0; c < kGrp; ++c) tmem_ld16_nowait(taddr + (g0 + c) * 16, raw[c]);
+                for (int c = 0; c < kGrp; ++c) tmem_ld16_nowait(taddr + (c0 + (g0 + c) * kCs) * 16, raw[c]);
                 tmem_wait();
 #ifdef FX_CONV_TRACE
                 if (threadIdx.x == 64 && p.trace)
@@ -317,7 +323,8 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                 for (int c = 0; c < kGrp; ++c) tmem_regs_ready(raw[c]);
 #pragma unroll
                 for (int c = 0; c < kGrp; ++c) {
-                    const int cc = g0 + c;
+                    const int ci = g0 + c;              // position among this warp's chunks
+                    const int cc = c0 + ci * kCs;       // chunk within the tile
                     float v[16];
                     if (prenorm) {
 #pragma unroll
@@ -326,15 +333,15 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                         if (valid) {
                             uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + row * 16 +
                                          static_cast<int64_t>((cbase + cc * 16) / 8) * p.out_group_stride;
-                            *reinterpret_cast<uint4*>(o) = pack_cell16(v, kOpF16);
-                            *reinterpret_cast<uint4*>(o + p.out_group_stride) = pack_cell16(v + 8, kOpF16);
+                            *reinterpret_cast<uint4*>(o) = pack_cell_f16_sat(v);
+                            *reinterpret_cast<uint4*>(o + p.out_group_stride) = pack_cell_f16_sat(v + 8);
                         }
                         if constexpr (kAccR) {
 #pragma unroll
                             for (int i = 0; i < 16; ++i) {
                                 const float t = valid ? v[i] : 0.f;
-                                r1[cc][i] += t;
-                                r2[cc][i] = fmaf(t, t, r2[cc][i]);
+                                r1[ci][i] += t;
+                                r2[ci][i] = fmaf(t, t, r2[ci][i]);
                             }
                         } else {
                             float q[16];
@@ -343,33 +350,36 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                                 v[i] = valid ? v[i] : 0.f;
                                 q[i] = v[i] * v[i];
                             }
-                            s1[cc] += warp_transpose_reduce16(v, lane);
-                            s2[cc] += warp_transpose_reduce16(q, lane);
+                            s1[ci] += warp_transpose_reduce16(v, lane);
+                            s2[ci] += warp_transpose_reduce16(q, lane);
                         }
                     } else if (valid) {  // kModeUpsample: column n = phase * cout + channel
                         const int n0 = cbase + cc * 16;
                         const int a = n0 / p.cout;
                         const int co0 = n0 - a * p.cout;  // 16 consecutive channels of one phase
-                        float mx = 0.f;
+                        // scale and bias already include the e4m3 output scale (ctl->up_scale/bias)
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
+                        for (int i = 0; i < 16; ++i)
                             v[i] = fmaf(__uint_as_float(raw[c][i]), ctl->colscale[co0 + i], ctl->bias[co0 + i]);
-                            mx = fmaxf(mx, fabsf(v[i]));
+                        if (p.amax) {
+                            float mx = 0.f;
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(v[i]));
+                            if (e4out) mx /= p.out_qscale;
+                            atomicMax(p.amax, __float_as_uint(mx));
                         }
-                        if (p.amax) atomicMax(p.amax, __float_as_uint(mx));
                         const int az = a >> 2, ay = (a >> 1) & 1, ax = a & 1;
                         const int64_t orow =
                             ((2 * static_cast<int64_t>(z) - 1 + az) * p.oHp + (2 * static_cast<int64_t>(y) - 1 + ay)) *
                                 p.oWp +
                             (2 * static_cast<int64_t>(x) - 1 + ax);
                         uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + orow * 16;
-                        if (p.out_type == kOpE4M3) {
-                            const float sc = p.out_qscale;
+                        if (e4out) {
                             uint4 w;
-                            w.x = pack_e4m3x4(v[0] * sc, v[1] * sc, v[2] * sc, v[3] * sc);
-                            w.y = pack_e4m3x4(v[4] * sc, v[5] * sc, v[6] * sc, v[7] * sc);
-                            w.z = pack_e4m3x4(v[8] * sc, v[9] * sc, v[10] * sc, v[11] * sc);
-                            w.w = pack_e4m3x4(v[12] * sc, v[13] * sc, v[14] * sc, v[15] * sc);
+                            w.x = pack_e4m3x4(v[0], v[1], v[2], v[3]);
+                            w.y = pack_e4m3x4(v[4], v[5], v[6], v[7]);
+                            w.z = pack_e4m3x4(v[8], v[9], v[10], v[11]);
+                            w.w = pack_e4m3x4(v[12], v[13], v[14], v[15]);
                             *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 16) * p.out_group_stride) = w;
                         } else {
                             *reinterpret_cast<uint4*>(o + static_cast<int64_t>(co0 / 8) * p.out_group_stride) =
@@ -388,7 +398,7 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         if (prenorm) {
             if constexpr (kAccR) {
 #pragma unroll
-                for (int c = 0; c < NCH; ++c) {
+                for (int c = 0; c < kMy; ++c) {
                     s1[c] = warp_transpose_reduce16(r1[c], lane);
                     s2[c] = warp_transpose_reduce16(r2[c], lane);
                 }
@@ -397,9 +407,13 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                          ((static_cast<int64_t>(b) * p.n_units_m + mu) * kStatRecsPerUnit + half * 4 + wq) * p.stats_C * 2;
             if (lane < 16) {
 #pragma unroll
-                for (int c = 0; c < NCH; ++c) {
-                    const int ch = cbase + c * 16 + lane;
+                for (int c = 0; c < kMy; ++c) {
+                    const int ch = cbase + (c0 + c * kCs) * 16 + lane;
                     *reinterpret_cast<float2*>(dst + ch * 2) = make_float2(s1[c], s2[c]);
+                    if (SPLITC) {  // the other warp's chunks: zero in this record
+                        const int cho = cbase + ((c0 ^ 1) + c * kCs) * 16 + lane;
+                        *reinterpret_cast<float2*>(dst + cho * 2) = make_float2(0.f, 0.f);
+                    }
                 }
             }
         }
@@ -435,9 +449,11 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     }
     // per-channel dequant scale and bias tables (prenorm: by column; upsample: by channel)
     const int ncols = p.mode == kModeUpsample ? p.cout : p.stats_C;
+    // upsample mode writes e4m3 cells as y * out_qscale: fold that factor into both tables
+    const float osc = (p.mode == kModeUpsample && p.out_type == kOpE4M3) ? p.out_qscale : 1.f;
     for (int i = threadIdx.x; i < kMaxCols; i += blockDim.x) {
-        ctl->colscale[i] = (i < ncols && p.col_scale) ? p.col_scale[i] : 1.f;
-        ctl->bias[i] = (i < ncols && p.bias) ? p.bias[i] : 0.f;
+        ctl->colscale[i] = ((i < ncols && p.col_scale) ? p.col_scale[i] : 1.f) * osc;
+        ctl->bias[i] = ((i < ncols && p.bias) ? p.bias[i] : 0.f) * osc;
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(&ctl->tmem_base), p.tmem_cols);
@@ -463,13 +479,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             default: break;  // rejected on the host (launch_conv_tc)
         }
     } else {
+        const bool sc = p.R == 1;  // one M block per unit: split its chunks between the warp pair
         switch (p.N_tile / 16) {
-            case 1: epilogue_loop<1>(p, ctl, n_units); break;
-            case 2: epilogue_loop<2>(p, ctl, n_units); break;
-            case 4: epilogue_loop<4>(p, ctl, n_units); break;
-            case 8: epilogue_loop<8>(p, ctl, n_units); break;
-            case 16: epilogue_loop<16>(p, ctl, n_units); break;
-            case 20: epilogue_loop<20>(p, ctl, n_units); break;
+            case 1: epilogue_loop<1, false>(p, ctl, n_units); break;
+            case 2: sc ? epilogue_loop<2, true>(p, ctl, n_units) : epilogue_loop<2, false>(p, ctl, n_units); break;
+            case 4: sc ? epilogue_loop<4, true>(p, ctl, n_units) : epilogue_loop<4, false>(p, ctl, n_units); break;
+            case 8: sc ? epilogue_loop<8, true>(p, ctl, n_units) : epilogue_loop<8, false>(p, ctl, n_units); break;
+            case 16: epilogue_loop<16, true>(p, ctl, n_units); break;   // N 256: always R = 1
+            case 20: epilogue_loop<20, true>(p, ctl, n_units); break;   // N 320: always R = 1
             default: break;  // rejected on the host (launch_conv_tc)
         }
     }

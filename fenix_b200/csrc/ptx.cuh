@@ -268,6 +268,15 @@ __device__ __forceinline__ uint4 pack_cell16(const float* v, int optype) {
     }
     return w;
 }
+// Eight floats -> one 16-byte cell of f16, round to nearest, saturated to +-65504 (one
+// cvt.rn.satfinite.f16x2.f32 per pair; the first value of a pair lands in the low half).
+__device__ __forceinline__ uint4 pack_cell_f16_sat(const float* v) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(w[i]) : "f"(v[2 * i + 1]), "f"(v[2 * i]));
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
 // Four floats -> four e4m3 bytes (satfinite), little-endian in one u32.
 __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
     __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
