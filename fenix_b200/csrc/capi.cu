@@ -407,7 +407,7 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
         cudaMemsetAsync(out, 0, static_cast<size_t>(B) * obs, s);
         cudaMemsetAsync(d_status, 0, sizeof(uint32_t), s);
         st = fxh::launch_layer(L, q, gin, gout, in, ibs, igs, out, obs, ogs, 0, 1.f, nullptr, B, sm_count_of_current(),
-                               d_status, s);
+                               d_status, s, /*per_column=*/true);
         if (!st.ok()) return set_err(st);
         fxk::launch_unpack(out, obs, ogs, fxk::kOpF16, 1.f, B, Cout, gout.D, gout.H, gout.W, dev_y, s);
         cudaError_t e = cudaStreamSynchronize(s);

@@ -273,6 +273,10 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     constexpr int kGrp = kMy < 4 ? kMy : (kMy == 4 ? 4 : 2);  // chunks loaded from TMEM per wait
     constexpr int kR = kAccR ? kMy : 1;
     const bool e4out = p.out_type == kOpE4M3;
+    // prenorm: a per-column scale table, or one scale for all columns (the per-channel part then
+    // travels to the InstanceNorm statistics, which a per-channel factor does not change)
+    const bool percol = p.col_scale != nullptr;
+    const float acc_scale = p.acc_scale;
     uint32_t j = 0;
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
         int b, mu, nt;
@@ -327,9 +331,14 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                     const int cc = c0 + ci * kCs;       // chunk within the tile
                     float v[16];
                     if (prenorm) {
+                        if (percol) {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i)
-                            v[i] = __uint_as_float(raw[c][i]) * ctl->colscale[cbase + cc * 16 + i];
+                            for (int i = 0; i < 16; ++i)
+                                v[i] = __uint_as_float(raw[c][i]) * ctl->colscale[cbase + cc * 16 + i];
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(raw[c][i]) * acc_scale;
+                        }
                         if (valid) {
                             uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + row * 16 +
                                          static_cast<int64_t>((cbase + cc * 16) / 8) * p.out_group_stride;

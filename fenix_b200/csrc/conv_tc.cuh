@@ -89,6 +89,7 @@ struct ConvParams {
     // epilogue
     int32_t mode;
     const float* col_scale;  // per output channel multiplier (fp8 dequant) or null
+    float acc_scale;         // prenorm mode without col_scale: one multiplier for every column
     const float* bias;       // per output channel bias (upsample mode) or null
     uint8_t* out;            // output tensor, group 0 of the written channel slice, batch 0
     int64_t out_batch_stride, out_group_stride;  // bytes
@@ -97,7 +98,7 @@ struct ConvParams {
     int32_t cout;            // upsample mode: channels per phase
     int32_t oHp, oWp;        // upsample mode: padded H, W of the output grid
     unsigned* amax;          // upsample mode: max |output| (float bits) when non-null
-    float* stats;            // prenorm mode: [batch][n_units_m][4][C][2] partial sums
+    float* stats;            // prenorm mode: [batch][n_units_m][kStatRecsPerUnit][C][2] partial sums
     int32_t stats_C;         // channels per stats record (= n_tiles * N_tile)
     uint32_t* status;
     unsigned long long* trace;  // per-role cycle counters (kernel built with FX_CONV_TRACE), or null

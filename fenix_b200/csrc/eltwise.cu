@@ -134,10 +134,13 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) { return 
 // records [B][nrec][C][2] in double and stores {Σ, Σ²} for 32 channels in work[B][S][C][2]; the
 // last block of a (batch, channel block) to finish — counted in done[], which it resets — adds
 // the S slices in slice order (the result does not depend on block scheduling) and writes
-// ss[B][C][2] = {gamma * rstd, beta - mean * gamma * rstd}.
+// ss[B][C][2] = {gamma * rstd, beta - mean * gamma * rstd}. With ratio, the records hold the
+// channel's values divided by ratio[c]: the statistics of the true values are mean * r and
+// var * r^2, and ss is written for the stored values (scale multiplied by r).
 __global__ void __launch_bounds__(256) in_stats_kernel(const float* __restrict__ partials, int nrec, int C, int S,
                                                        double count, const float* __restrict__ gamma,
-                                                       const float* __restrict__ beta, float eps,
+                                                       const float* __restrict__ beta,
+                                                       const float* __restrict__ ratio, float eps,
                                                        double* __restrict__ work, unsigned* __restrict__ done,
                                                        float* __restrict__ ss) {
     const int b = blockIdx.y, sl = blockIdx.z;
@@ -185,13 +188,15 @@ __global__ void __launch_bounds__(256) in_stats_kernel(const float* __restrict__
             u1 += __ldcg(wb + (static_cast<int64_t>(k) * C + c) * 2);
             u2 += __ldcg(wb + (static_cast<int64_t>(k) * C + c) * 2 + 1);
         }
-        const double mean = u1 / count;
-        double var = u2 / count - mean * mean;
+        const double r = ratio ? static_cast<double>(ratio[c]) : 1.0;
+        const double ms = u1 / count;
+        double var = (u2 / count - ms * ms) * r * r;
         if (var < 0.0) var = 0.0;
+        const double mean = ms * r;
         const double rstd = 1.0 / sqrt(var + static_cast<double>(eps));
         const double sc = static_cast<double>(gamma ? gamma[c] : 1.f) * rstd;
         const double sh = static_cast<double>(beta ? beta[c] : 0.f) - mean * sc;
-        ss[(static_cast<int64_t>(b) * C + c) * 2 + 0] = static_cast<float>(sc);
+        ss[(static_cast<int64_t>(b) * C + c) * 2 + 0] = static_cast<float>(sc * r);
         ss[(static_cast<int64_t>(b) * C + c) * 2 + 1] = static_cast<float>(sh);
     }
     if (lane == 0) *cnt = 0u;
@@ -431,12 +436,13 @@ cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
 int in_stats_slices(int nrec) { return nrec < 256 ? 1 : (nrec / 256 < kMaxStatSlices ? nrec / 256 : kMaxStatSlices); }
 
 cudaError_t launch_in_finalize(const float* partials, int B, int nrec, int C, double count, const float* gamma,
-                               const float* beta, float eps, double* work, unsigned* done, float* ss, cudaStream_t s) {
+                               const float* beta, const float* ratio, float eps, double* work, unsigned* done,
+                               float* ss, cudaStream_t s) {
     if (nrec < 1 || C < 1 || B < 1) return cudaErrorInvalidValue;
     const int S = in_stats_slices(nrec);
     count_launch();
-    in_stats_kernel<<<dim3((C + 31) / 32, B, S), 256, 0, s>>>(partials, nrec, C, S, count, gamma, beta, eps, work,
-                                                             done, ss);
+    in_stats_kernel<<<dim3((C + 31) / 32, B, S), 256, 0, s>>>(partials, nrec, C, S, count, gamma, beta, ratio, eps,
+                                                             work, done, ss);
     return cudaGetLastError();
 }
 

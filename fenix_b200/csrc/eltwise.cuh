@@ -36,10 +36,12 @@ cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
 // partials [B][nrec][C][2] -> ss [B][C][2] = {scale, shift} with scale = gamma * rstd and
 // shift = beta - mean * scale over `count` voxels. work holds B * kMaxStatSlices * C * 2 doubles;
 // done holds B * ceil(C / 32) counters that are zero before the first launch (each launch leaves
-// them zero). Launches sharing work/done must be stream-ordered.
+// them zero). Launches sharing work/done must be stream-ordered. ratio (per channel, or null):
+// the records hold each channel's values divided by ratio[c] (see in_stats_kernel).
 constexpr int kMaxStatSlices = 128;
 cudaError_t launch_in_finalize(const float* partials, int B, int nrec, int C, double count, const float* gamma,
-                               const float* beta, float eps, double* work, unsigned* done, float* ss, cudaStream_t s);
+                               const float* beta, const float* ratio, float eps, double* work, unsigned* done,
+                               float* ss, cudaStream_t s);
 
 struct NormDest {
     uint8_t* ptr;          // group 0 of the written slice, batch 0 (null = unused)

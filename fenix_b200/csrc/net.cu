@@ -182,7 +182,8 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
             }
         }
     }
-    std::vector<float> colscale;
+    std::vector<float> colscale, ratio;
+    dp.acc_scale = 1.f;
     if (L.kind == Layer::kFirst) {
         if (fp8) return fail(kInternal, "first layer runs with 16-bit operands");
         sp.G = 1;
@@ -226,6 +227,11 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
         if (fp8) {
             colscale.resize(L.Cout);
             for (int co = 0; co < L.Cout; ++co) colscale[co] = L.in_scale * L.wscale[co];
+            // one epilogue factor = the largest channel's, so stored f16 values are never larger
+            // than that channel's own range; the per-channel remainder (<= 1) goes to the stats
+            dp.acc_scale = *std::max_element(colscale.begin(), colscale.end());
+            ratio.resize(L.Cout);
+            for (int co = 0; co < L.Cout; ++co) ratio[co] = colscale[co] / dp.acc_scale;
         }
     } else {  // kUp
         if (L.Cin % sp.cg) return fail(kUnsupported, L.name + ": input channels must be a multiple of " + std::to_string(sp.cg));
@@ -274,6 +280,7 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     dp.optype = q;
     if ((st = upload(dp.wpack, dp.host.wpack, this_net, allocs_)).code) return st;
     if ((st = upload(dp.colscale, colscale, this_net, allocs_)).code) return st;
+    if ((st = upload(dp.ratio, ratio, this_net, allocs_)).code) return st;
     if (L.kind == Layer::kUp && (st = upload(dp.bias, L.b, this_net, allocs_)).code) return st;
     dp.built = true;
     return ok();
@@ -428,7 +435,7 @@ Status Net::profile_read(ProfileTotals& out, double* per, int cap) {
 
 Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
                     uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax,
-                    int nb, int sm_count_, uint32_t* d_status_, cudaStream_t s) {
+                    int nb, int sm_count_, uint32_t* d_status_, cudaStream_t s, bool per_column) {
     DevProgram& dp = L.prog[q];
     if (!dp.built) return fail(kInternal, L.name + ": program not built");
     static thread_local fxk::ConvParams p;  // ~22 KB: kept off the stack
@@ -482,6 +489,13 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
         p.mode = fxk::kModePrenorm;
         p.stats = L.d_partials;
         p.stats_C = L.Cout;
+        p.acc_scale = dp.acc_scale;  // used when there is no per-column table
+        if (!per_column) {
+            p.col_scale = nullptr;
+            L.cur_ratio = dp.ratio;
+        } else {
+            L.cur_ratio = nullptr;
+        }
         L.nrec = dp.n_units_m * fxk::kStatRecsPerUnit;
     }
     const int64_t units = static_cast<int64_t>(nb) * p.n_units_m * p.n_tiles;
@@ -492,8 +506,8 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
 Status Net::finalize_in(Layer& L, int nb, cudaStream_t s) {
     const ActGeom g = level(L.lout);
     const double count = static_cast<double>(g.D) * g.H * g.W;
-    return cuda_status(fxk::launch_in_finalize(L.d_partials, nb, L.nrec, L.Cout, count, L.d_gamma, L.d_beta, kEps,
-                                               d_stat_work_, d_stat_done_, L.d_ss, s),
+    return cuda_status(fxk::launch_in_finalize(L.d_partials, nb, L.nrec, L.Cout, count, L.d_gamma, L.d_beta,
+                                               L.cur_ratio, kEps, d_stat_work_, d_stat_done_, L.d_ss, s),
                        "in_finalize");
 }
 

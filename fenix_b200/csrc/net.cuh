@@ -45,6 +45,10 @@ struct DevProgram {
     uint8_t* wpack = nullptr;
     float* colscale = nullptr;
     float* bias = nullptr;
+    // prenorm layers: the epilogue scales every column by acc_scale; ratio[c] = colscale[c] /
+    // acc_scale (null when 1) goes to the InstanceNorm statistics instead
+    float acc_scale = 1.f;
+    float* ratio = nullptr;
     Program host;
     int R = 1, N_tile = 0, acc_slots = 1, n_units_m = 0;
     uint32_t tmem_cols = 32;
@@ -67,9 +71,10 @@ struct Layer {
     DevProgram prog[3];               // indexed by fxk::OpType: bf16, e4m3, f16
     float* d_gamma = nullptr;
     float* d_beta = nullptr;
-    float* d_partials = nullptr;      // [Bmax][n_units_m][4][Cout][2]
+    float* d_partials = nullptr;      // [Bmax][n_units_m][kStatRecsPerUnit][Cout][2]
     float* d_ss = nullptr;            // [Bmax][Cout][2]
     int nrec = 0;
+    const float* cur_ratio = nullptr; // ratio of the last prenorm launch (its statistics' scale)
 };
 
 // Compile one layer's program for operand type q (fxk::OpType) and upload it; gin/gout are
@@ -78,9 +83,11 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
                            std::vector<void*>& allocs);
 // Launch one layer. Stride-2 convs read the phase-split copy (gout geometry per phase); the
 // prenorm mode writes L.d_partials and sets L.nrec.
+// per_column: prenorm output scaled per column in the epilogue (exact pre-norm values, for
+// callers that read them); otherwise by one factor, with the per-channel part in L.cur_ratio.
 Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
                     uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax,
-                    int nb, int sm_count, uint32_t* d_status, cudaStream_t s);
+                    int nb, int sm_count, uint32_t* d_status, cudaStream_t s, bool per_column = false);
 
 class Net {
   public:
