@@ -400,8 +400,9 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
         const int64_t ogs = gout.gs(), obs = (Cout / 8) * ogs;
         auto* out = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * obs));
         const int64_t rows = static_cast<int64_t>(gout.D) * (gout.H + 2) * (gout.W + 2);
-        const int64_t nrec = ((rows + 127) / 128) * fxk::kStatRecsPerUnit;
+        const int64_t nrec = ((rows + 125) / 126) * fxk::kStatRecsPerUnit;
         L.d_partials = static_cast<float*>(sc.get(sizeof(float) * B * nrec * Cout * 2));
+        L.nrec_cap = nrec;
         auto* d_status = static_cast<uint32_t*>(sc.get(sizeof(uint32_t)));
         if (!out || !L.d_partials || !d_status) return set_err(FX_INTERNAL, "cudaMalloc failed");
         cudaMemsetAsync(out, 0, static_cast<size_t>(B) * obs, s);

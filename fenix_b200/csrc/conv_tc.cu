@@ -40,6 +40,7 @@ struct SmemCtl {
     uint64_t accf[2];
     uint64_t acce[2];
     uint64_t drain;
+    uint64_t xready[2][2];  // fold epilogue: row exchange of [half][parity] published by its 4 warps
     uint32_t tmem_base;
     int abort;
     float colscale[kMaxCols];
@@ -58,7 +59,7 @@ __device__ __forceinline__ void unit_coords(const ConvParams& p, int unit, int& 
 __device__ void producer_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n_units) {
     const bool leader = elect_one();
     uint32_t k = 0;  // global stage counter
-    const int Mtot = 128 * p.R;
+    const int64_t Mtot = static_cast<int64_t>(p.block_rows) * p.R;
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
         int b, mu, nt;
         unit_coords(p, unit, b, mu, nt);
@@ -123,7 +124,8 @@ drain:
 // are warp-uniform (program entries come from the parameter space, hence uniform registers); the
 // MMA / commit instructions are predicated on the elected lane. R (M blocks per unit), the
 // operand kind and the N split are compile-time, so issuing an MMA is a couple of uniform adds.
-template <int R, bool F8, bool SPLIT>
+// FOLD: every program MMA is three MMAs of N = N_tile / 3 sharing the A tile (x-tap fold).
+template <int R, bool F8, bool SPLIT, bool FOLD>
 __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n_units) {
     const uint32_t leader = elect_one() ? 1u : 0u;
     uint32_t k = 0;
@@ -134,9 +136,12 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
     // descriptor high words: SBO = 128 B, version 1, no swizzle
     const uint64_t hi = (static_cast<uint64_t>(128 >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
     const uint64_t b_lbo = static_cast<uint64_t>((p.N_tile * 16) >> 4) << 16;
-    const uint32_t idesc0 = instr_desc(128, SPLIT ? 256 : p.N_tile, p.optype);
+    const uint32_t nf = static_cast<uint32_t>(p.N_tile / 3);  // FOLD: columns of each accumulator
+    const uint32_t idesc0 = instr_desc(128, SPLIT ? 256 : (FOLD ? static_cast<int>(nf) : p.N_tile), p.optype);
     const uint32_t idesc1 = instr_desc(128, SPLIT ? p.N_tile - 256 : 16, p.optype);
     const uint32_t ncol = static_cast<uint32_t>(p.N_tile);
+    const uint32_t brow16 = static_cast<uint32_t>(p.block_rows);  // M block stride in 16-byte rows
+    const uint64_t bk1 = static_cast<uint64_t>((nf * 16) >> 4), bk2 = 2 * bk1;  // FOLD: B of x taps 1, 2
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
         const int aslot = j % p.acc_slots;
         const uint32_t aph = (j / p.acc_slots) & 1u;
@@ -185,8 +190,13 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
                 const uint64_t bdesc = bhi + (sb16 + mm.b);
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
-                    const uint64_t ad = adesc + static_cast<uint64_t>(r * (2048 >> 4));
+                    const uint64_t ad = adesc + static_cast<uint64_t>(r * brow16);
                     const uint32_t d = dcol0 + static_cast<uint32_t>(r) * ncol;
+                    if (FOLD) {
+                        if (F8) mma3_f8_if(leader, d, d + nf, d + 2 * nf, ad, bdesc, bdesc + bk1, bdesc + bk2, idesc0, acc);
+                        else mma3_f16_if(leader, d, d + nf, d + 2 * nf, ad, bdesc, bdesc + bk1, bdesc + bk2, idesc0, acc);
+                        continue;
+                    }
                     if (F8) mma_f8_if(leader, d, ad, bdesc, idesc0, acc);
                     else mma_f16_if(leader, d, ad, bdesc, idesc0, acc);
                     if (SPLIT) {
@@ -200,7 +210,7 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
             mma_commit_if(leader, smem_u32(&ctl->empty[slot]));  // stage buffer free once these MMAs finish
             if (leader) {
                 FX_TADD(p, 4);
-                FX_TCNT(p, 7, mc * R);
+                FX_TCNT(p, 7, mc * R * (FOLD ? 3 : 1));
             }
         }
         if (aborted) break;
@@ -433,6 +443,195 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     }
 }
 
+// Epilogue of the x-tap fold (prenorm mode, Cout = 16 NC): a block's TMEM holds D0 | D1 | D2
+// (N = 16 NC columns each); output row j = D0[j] + D1[j + 1] + D2[j + 2] for j < 126. Within a
+// warp the row shifts are shuffles; the two rows that cross into the next lane quarter come
+// through shared memory: every warp first publishes D1 of its lane 0 and D2 of its lanes 0 and 1,
+// then the four warps of its half meet at an mbarrier (a bounded wait, like every wait of this
+// kernel). The publish slots alternate between two parities so one meeting per M block suffices. The warp pair of a quarter splits the work
+// like epilogue_loop (alternate M blocks, or alternate chunks when a unit has one M block).
+template <int NC, bool SPLITC>
+__device__ void epilogue_fold(const ConvParams& p, SmemCtl* ctl, float* xbuf, int n_units) {
+    constexpr int N = NC * 16;
+    const int lane = threadIdx.x & 31;
+    const int wq = (threadIdx.x >> 5) & 3;
+    const int half = ((threadIdx.x >> 5) - 2) >> 2;
+    const uint32_t tbase = ctl->tmem_base;
+    const uint32_t slot_cols = static_cast<uint32_t>(p.R * 3 * N);
+    const int BR = p.block_rows;
+    const int64_t Mtot = static_cast<int64_t>(BR) * p.R;
+    RowDecomp rd;
+    rd.P2 = static_cast<uint32_t>(p.Hp * p.Wp);
+    rd.Wp = static_cast<uint32_t>(p.Wp);
+    rd.mP2 = ~0ull / rd.P2 + 1;
+    rd.mWp = ~0ull / rd.Wp + 1;
+    const uint32_t zmax = static_cast<uint32_t>(p.Dp - 2), ymax = static_cast<uint32_t>(p.Hp - 2),
+                   xmax = static_cast<uint32_t>(p.Wp - 2);
+    const bool percol = p.col_scale != nullptr;
+    const float acc_scale = p.acc_scale;
+    constexpr int kMy = SPLITC ? NC / 2 : NC;
+    constexpr int kCs = SPLITC ? 2 : 1;
+    const int c0 = SPLITC ? half : 0;
+    const int rb = SPLITC ? 0 : half, rs = SPLITC ? 1 : 2;
+    constexpr bool kAccR = kMy == 1;
+    float* xh = xbuf + half * (2 * 4 * 3 * N);  // [parity][quarter][D1 lane 0 | D2 lane 0 | D2 lane 1][N]
+    uint32_t par = 0;
+    uint32_t xph[2] = {0u, 0u};  // phase parity of xready[half][0 / 1]
+    const int m = wq * 32 + lane;  // accumulator row of this thread
+    uint32_t j = 0;
+    for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
+        int b, mu, nt;
+        unit_coords(p, unit, b, mu, nt);
+        const int aslot = j % p.acc_slots;
+        {
+            FX_T0();
+            if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, kWaitLimitNs)) {
+                set_status(p.status, kStatusTimeoutAcc);
+                ctl->abort = 1;
+                return;
+            }
+            if (threadIdx.x == 64) FX_TADD(p, 5);
+        }
+        tc_fence_after();
+        FX_T0();
+        const int64_t q0 = p.row_begin + static_cast<int64_t>(mu) * Mtot;
+        float s1[kMy], s2[kMy];
+        float r1[kAccR ? 1 : 1][16], r2[kAccR ? 1 : 1][16];
+#pragma unroll
+        for (int c = 0; c < kMy; ++c) s1[c] = s2[c] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r1[0][i] = r2[0][i] = 0.f;
+        for (int r = rb; r < p.R; r += rs) {
+            const int64_t row = q0 + static_cast<int64_t>(r) * BR + m;
+            uint32_t z, y, x;
+            rd.split(static_cast<uint32_t>(row), z, y, x);
+            const bool valid = m < BR && row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 &&
+                               x <= xmax;
+            const uint32_t taddr =
+                tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + static_cast<uint32_t>(r * 3 * N);
+            float* xw = xh + (par * 4 + wq) * 3 * N;
+            const float* xn = xh + (par * 4 + ((wq + 1) & 3)) * 3 * N;
+            // publish the rows the previous lane quarter needs
+#pragma unroll
+            for (int i = 0; i < kMy; ++i) {
+                const int cc = c0 + i * kCs;
+                uint32_t u1[16], u2[16];
+                tmem_ld16_nowait(taddr + N + cc * 16, u1);
+                tmem_ld16_nowait(taddr + 2 * N + cc * 16, u2);
+                tmem_wait();
+                tmem_regs_ready(u1);
+                tmem_regs_ready(u2);
+                if (lane == 0) {
+#pragma unroll
+                    for (int t = 0; t < 16; t += 4) {
+                        *reinterpret_cast<float4*>(xw + cc * 16 + t) =
+                            make_float4(__uint_as_float(u1[t]), __uint_as_float(u1[t + 1]), __uint_as_float(u1[t + 2]),
+                                        __uint_as_float(u1[t + 3]));
+                        *reinterpret_cast<float4*>(xw + N + cc * 16 + t) =
+                            make_float4(__uint_as_float(u2[t]), __uint_as_float(u2[t + 1]), __uint_as_float(u2[t + 2]),
+                                        __uint_as_float(u2[t + 3]));
+                    }
+                } else if (lane == 1) {
+#pragma unroll
+                    for (int t = 0; t < 16; t += 4)
+                        *reinterpret_cast<float4*>(xw + 2 * N + cc * 16 + t) =
+                            make_float4(__uint_as_float(u2[t]), __uint_as_float(u2[t + 1]), __uint_as_float(u2[t + 2]),
+                                        __uint_as_float(u2[t + 3]));
+                }
+            }
+            __syncwarp();  // lane 1's publish is ordered before lane 0's arrive
+            if (lane == 0) mbar_arrive(smem_u32(&ctl->xready[half][par]));
+            if (!mbar_wait(smem_u32(&ctl->xready[half][par]), xph[par], &ctl->abort, kWaitLimitNs)) {
+                set_status(p.status, kStatusTimeoutExchange);
+                ctl->abort = 1;
+                return;
+            }
+            xph[par] ^= 1u;
+#pragma unroll
+            for (int i = 0; i < kMy; ++i) {
+                const int cc = c0 + i * kCs;
+                uint32_t u0[16], u1[16], u2[16];
+                tmem_ld16_nowait(taddr + cc * 16, u0);
+                tmem_ld16_nowait(taddr + N + cc * 16, u1);
+                tmem_ld16_nowait(taddr + 2 * N + cc * 16, u2);
+                tmem_wait();
+                tmem_regs_ready(u0);
+                tmem_regs_ready(u1);
+                tmem_regs_ready(u2);
+                float a[16], bb[16];
+#pragma unroll
+                for (int t = 0; t < 16; ++t) {
+                    a[t] = __shfl_down_sync(0xffffffffu, __uint_as_float(u1[t]), 1);
+                    bb[t] = __shfl_down_sync(0xffffffffu, __uint_as_float(u2[t]), 2);
+                }
+                if (lane >= 30) {  // rows 31 / 30 of the quarter: D1, D2 of the next quarter's rows 0 / 1
+                    const float* sa = xn + cc * 16;
+                    const float* sb = xn + (lane == 31 ? 2 * N : N) + cc * 16;
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) {
+                        if (lane == 31) a[t] = sa[t];
+                        bb[t] = sb[t];
+                    }
+                }
+                float v[16];
+#pragma unroll
+                for (int t = 0; t < 16; ++t) {
+                    const float sc = percol ? ctl->colscale[cc * 16 + t] : acc_scale;
+                    v[t] = (__uint_as_float(u0[t]) + a[t] + bb[t]) * sc;
+                }
+                if (valid) {
+                    uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + row * 16 +
+                                 static_cast<int64_t>(cc * 2) * p.out_group_stride;
+                    *reinterpret_cast<uint4*>(o) = pack_cell_f16_sat(v);
+                    *reinterpret_cast<uint4*>(o + p.out_group_stride) = pack_cell_f16_sat(v + 8);
+                }
+                if constexpr (kAccR) {
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) {
+                        const float w = valid ? v[t] : 0.f;
+                        r1[0][t] += w;
+                        r2[0][t] = fmaf(w, w, r2[0][t]);
+                    }
+                } else {
+                    float q[16];
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) {
+                        v[t] = valid ? v[t] : 0.f;
+                        q[t] = v[t] * v[t];
+                    }
+                    s1[i] += warp_transpose_reduce16(v, lane);
+                    s2[i] += warp_transpose_reduce16(q, lane);
+                }
+            }
+            par ^= 1u;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl->acce[aslot]));
+        if constexpr (kAccR) {
+            s1[0] = warp_transpose_reduce16(r1[0], lane);
+            s2[0] = warp_transpose_reduce16(r2[0], lane);
+        }
+        float* dst = p.stats +
+                     ((static_cast<int64_t>(b) * p.n_units_m + mu) * kStatRecsPerUnit + half * 4 + wq) * p.stats_C * 2;
+        if (lane < 16) {
+#pragma unroll
+            for (int c = 0; c < kMy; ++c) {
+                const int ch = (c0 + c * kCs) * 16 + lane;
+                *reinterpret_cast<float2*>(dst + ch * 2) = make_float2(s1[c], s2[c]);
+                if (SPLITC) {
+                    const int cho = ((c0 ^ 1) + c * kCs) * 16 + lane;
+                    *reinterpret_cast<float2*>(dst + cho * 2) = make_float2(0.f, 0.f);
+                }
+            }
+        }
+        if (threadIdx.x == 64) {
+            FX_TADD(p, 6);
+            FX_TCNT(p, 8, 1);
+        }
+    }
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_constant__ ConvParams p) {
@@ -453,6 +652,8 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             mbar_init(smem_u32(&ctl->acce[i]), kEpiWarps);
         }
         mbar_init(smem_u32(&ctl->drain), 1);
+        for (int h = 0; h < 2; ++h)
+            for (int q = 0; q < 2; ++q) mbar_init(smem_u32(&ctl->xready[h][q]), 4);
         ctl->abort = 0;
         fence_mbar_init();
     }
@@ -475,16 +676,33 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
 
     if (warp == 0) {
         producer_loop(p, smem, ctl, n_units);
+    } else if (warp == 1 && p.fold) {
+        const bool f8 = p.optype == kOpE4M3;
+        switch (p.R) {
+            case 1: f8 ? mma_loop<1, true, false, true>(p, smem, ctl, n_units) : mma_loop<1, false, false, true>(p, smem, ctl, n_units); break;
+            case 2: f8 ? mma_loop<2, true, false, true>(p, smem, ctl, n_units) : mma_loop<2, false, false, true>(p, smem, ctl, n_units); break;
+            case 4: f8 ? mma_loop<4, true, false, true>(p, smem, ctl, n_units) : mma_loop<4, false, false, true>(p, smem, ctl, n_units); break;
+            default: break;  // rejected on the host (launch_conv_tc)
+        }
     } else if (warp == 1) {
         const bool f8 = p.optype == kOpE4M3, split = p.N_tile > 256;
         switch (p.R) {
             case 1:
-                if (split) f8 ? mma_loop<1, true, true>(p, smem, ctl, n_units) : mma_loop<1, false, true>(p, smem, ctl, n_units);
-                else f8 ? mma_loop<1, true, false>(p, smem, ctl, n_units) : mma_loop<1, false, false>(p, smem, ctl, n_units);
+                if (split) f8 ? mma_loop<1, true, true, false>(p, smem, ctl, n_units) : mma_loop<1, false, true, false>(p, smem, ctl, n_units);
+                else f8 ? mma_loop<1, true, false, false>(p, smem, ctl, n_units) : mma_loop<1, false, false, false>(p, smem, ctl, n_units);
                 break;
-            case 2: f8 ? mma_loop<2, true, false>(p, smem, ctl, n_units) : mma_loop<2, false, false>(p, smem, ctl, n_units); break;
-            case 4: f8 ? mma_loop<4, true, false>(p, smem, ctl, n_units) : mma_loop<4, false, false>(p, smem, ctl, n_units); break;
-            case 8: f8 ? mma_loop<8, true, false>(p, smem, ctl, n_units) : mma_loop<8, false, false>(p, smem, ctl, n_units); break;
+            case 2: f8 ? mma_loop<2, true, false, false>(p, smem, ctl, n_units) : mma_loop<2, false, false, false>(p, smem, ctl, n_units); break;
+            case 4: f8 ? mma_loop<4, true, false, false>(p, smem, ctl, n_units) : mma_loop<4, false, false, false>(p, smem, ctl, n_units); break;
+            case 8: f8 ? mma_loop<8, true, false, false>(p, smem, ctl, n_units) : mma_loop<8, false, false, false>(p, smem, ctl, n_units); break;
+            default: break;  // rejected on the host (launch_conv_tc)
+        }
+    } else if (p.fold) {
+        float* xbuf = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ctl) + sizeof(SmemCtl));
+        const bool sc = p.R == 1;
+        switch (p.N_tile / 48) {
+            case 1: epilogue_fold<1, false>(p, ctl, xbuf, n_units); break;
+            case 2: sc ? epilogue_fold<2, true>(p, ctl, xbuf, n_units) : epilogue_fold<2, false>(p, ctl, xbuf, n_units); break;
+            case 4: sc ? epilogue_fold<4, true>(p, ctl, xbuf, n_units) : epilogue_fold<4, false>(p, ctl, xbuf, n_units); break;
             default: break;  // rejected on the host (launch_conv_tc)
         }
     } else {
@@ -509,6 +727,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
 }
 
 size_t conv_tc_ctl_bytes() { return sizeof(SmemCtl); }
+size_t conv_tc_fold_bytes(int cout) { return static_cast<size_t>(2 * 2 * 4 * 3) * cout * sizeof(float); }
 
 cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cudaStream_t stream) {
     static bool configured = false;
@@ -519,12 +738,23 @@ cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cud
         configured = true;
     }
     const int nch = p.N_tile / 16;
-    if (p.N_tile % 16 || !(nch == 1 || nch == 2 || nch == 4 || nch == 8 || nch == 16 || nch == 20))
+    if (!p.fold && (p.N_tile % 16 || !(nch == 1 || nch == 2 || nch == 4 || nch == 8 || nch == 16 || nch == 20)))
         return cudaErrorInvalidValue;
     if ((p.mode == kModeUpsample ? p.cout : p.stats_C) > kMaxCols) return cudaErrorInvalidValue;
     if (!(p.R == 1 || p.R == 2 || p.R == 4 || p.R == 8) || (p.N_tile > 256 && p.R != 1)) return cudaErrorInvalidValue;
     if (p.n_stages > kMaxStages || p.n_mmas > kMaxMmas) return cudaErrorInvalidValue;
-    if (smem_bytes < static_cast<size_t>(p.n_pipe) * p.stage_bytes + sizeof(SmemCtl)) return cudaErrorInvalidValue;
+    size_t need = static_cast<size_t>(p.n_pipe) * p.stage_bytes + sizeof(SmemCtl);
+    if (p.fold) {
+        const int nf = p.N_tile / 3;
+        if (p.mode != kModePrenorm || p.N_tile % 48 || !(nf == 16 || nf == 32 || nf == 64) || p.stats_C != nf ||
+            p.n_tiles != 1 || p.block_rows != 126 || !(p.R == 1 || p.R == 2 || p.R == 4) ||
+            p.acc_slots * p.R * p.N_tile > static_cast<int>(p.tmem_cols))
+            return cudaErrorInvalidValue;
+        need += conv_tc_fold_bytes(nf);
+    } else if (p.block_rows != 128) {
+        return cudaErrorInvalidValue;
+    }
+    if (smem_bytes < need || smem_bytes > 232448) return cudaErrorInvalidValue;
     count_launch();
     conv_tc_kernel<<<grid, kConvThreads, smem_bytes, stream>>>(p);
     return cudaGetLastError();

@@ -13,6 +13,13 @@
 // sub-volumes with the output's padded geometry), which turns the strided taps into row
 // shifts as well.
 //
+// x-tap fold (3x3x3 stride 1, Cout <= 64): the program lists the 9 (kz, ky) taps with the A tile
+// starting one row early, and each program MMA becomes three MMAs of N = Cout that share its A
+// tile through the A collector (read from shared memory once) and accumulate x taps 0, 1, 2 into
+// three accumulators D0, D1, D2 of the same M block. Output row j of the block is
+// D0[j] + D1[j + 1] + D2[j + 2], so a block yields 126 output rows; the epilogue does the row
+// shifts across lanes (shuffles, and shared memory across the warps' lane quarters).
+//
 // The host compiles each layer into a small "program": a list of pipeline stages (one bulk
 // copy of a window of rows for a range of groups + the matching packed weight block) and, per
 // stage, the list of MMAs (A offset, K-half stride, B offset). The kernel is persistent and
@@ -20,6 +27,7 @@
 // and owns the TMEM allocation, warps 2..9 drain the TMEM accumulators (epilogue).
 #pragma once
 
+#include <cstddef>
 #include <cstdint>
 
 #include "optype.cuh"
@@ -64,6 +72,9 @@ enum ConvMode : int32_t {
     kModeUpsample = 1, // transposed conv: + bias, scatter 8 phases into the 2x finer grid
 };
 
+// Shared-memory bytes of the fold epilogue's row exchange for Cout output channels.
+size_t conv_tc_fold_bytes(int cout);
+
 struct ConvParams {
     ConvSrc src[kMaxSrc];
     const uint8_t* wpack;  // packed B blocks of N tile 0; tile t starts at + t * wtile_bytes
@@ -76,8 +87,10 @@ struct ConvParams {
     int32_t batch;
     int32_t Dp, Hp, Wp;          // padded extents of the row space
     int64_t row_begin, row_end;  // rows computed per batch item
-    int32_t R;                   // 128-row M blocks per work unit
-    int32_t n_units_m;           // ceil((row_end - row_begin) / (128 R))
+    int32_t R;                   // M blocks (of 128 accumulator rows) per work unit
+    int32_t block_rows;          // output rows advanced per M block: 128, or 126 with fold
+    int32_t fold;                // 1: the three x taps share each A tile (see below)
+    int32_t n_units_m;           // ceil((row_end - row_begin) / (block_rows R))
     int32_t n_tiles;             // N tiles
     int32_t N_tile;              // accumulator columns per tile (multiple of 16)
     int32_t acc_slots;           // accumulator buffers in TMEM (1 or 2)

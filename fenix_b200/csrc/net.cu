@@ -4,6 +4,7 @@
 #include "fenix_b200/ml/tiling.hpp"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -44,7 +45,8 @@ Status upload(T*& dst, const std::vector<T>& v, Net* /*unused*/, std::vector<voi
 }  // namespace
 
 size_t DevProgram::smem() const {
-    return static_cast<size_t>(host.n_pipe) * host.stage_bytes + fxk::conv_tc_ctl_bytes();
+    return static_cast<size_t>(host.n_pipe) * host.stage_bytes + fxk::conv_tc_ctl_bytes() +
+           (fold ? fxk::conv_tc_fold_bytes(N_tile / 3) : 0);
 }
 
 Status cuda_status(cudaError_t e, const char* what) {
@@ -153,6 +155,15 @@ Status Net::parse(const WeightMap& wm) {
 }
 
 // ---- layer program construction -------------------------------------------------------------
+// The x-tap fold (A collector shared by the three x taps) is off unless FENIX_B200_CONV_FOLD=1:
+// its MMAs run 1.6x faster, but its epilogue (three accumulators and a cross-lane row shift)
+// costs more than it saves with the current epilogue, measured on the 32- and 64-channel layers.
+// Read whenever a program is built, so one process can run and compare both programs.
+static bool fold_enabled() {
+    const char* v = std::getenv("FENIX_B200_CONV_FOLD");
+    return v && v[0] == '1';
+}
+
 Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax, int sm_count,
                            std::vector<void*>& allocs_) {
     DevProgram& dp = L.prog[q];
@@ -184,6 +195,7 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     }
     std::vector<float> colscale, ratio;
     dp.acc_scale = 1.f;
+    bool fold = false;
     if (L.kind == Layer::kFirst) {
         if (fp8) return fail(kInternal, "first layer runs with 16-bit operands");
         sp.G = 1;
@@ -199,7 +211,14 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     } else if (L.kind == Layer::kConv) {
         if (L.Cin % sp.cg) return fail(kUnsupported, L.name + ": input channels must be a multiple of " + std::to_string(sp.cg));
         sp.G = L.Cin / sp.cg;
-        if (L.stride == 1) {
+        fold = L.stride == 1 && (L.Cout == 16 || L.Cout == 32 || L.Cout == 64) && fold_enabled();
+        if (fold) {
+            // x-tap fold: 9 (kz, ky) taps whose A tile starts one row early; B column n holds x tap
+            // n / Cout of output channel n % Cout
+            const int64_t Wp = gin.W + 2, P2 = static_cast<int64_t>(gin.H + 2) * Wp;
+            for (int kz = 0; kz < 3; ++kz)
+                for (int ky = 0; ky < 3; ++ky) sp.taps.push_back({0, (kz - 1) * P2 + (ky - 1) * Wp - 1, kz * 9 + ky * 3, kz});
+        } else if (L.stride == 1) {
             const int64_t Wp = gin.W + 2, P2 = static_cast<int64_t>(gin.H + 2) * Wp;
             for (int kz = 0; kz < 3; ++kz)
                 for (int ky = 0; ky < 3; ++ky)
@@ -217,12 +236,14 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
         }
         const Layer* Lp = &L;
         const bool f8 = fp8;
-        sp.wval = [Lp, f8](int n, int ci, int wk) {
+        const int fc = fold ? L.Cout : 0;
+        sp.wval = [Lp, f8, fc](int n, int ci, int wk) {
             if (ci >= Lp->Cin) return 0.f;
-            const float v = Lp->w[(static_cast<size_t>(n) * Lp->Cin + ci) * 27 + wk];
-            return f8 ? v / Lp->wscale[n] : v;
+            const int co = fc ? n % fc : n, kx = fc ? n / fc : 0;  // fold: wk is kz*9 + ky*3
+            const float v = Lp->w[(static_cast<size_t>(co) * Lp->Cin + ci) * 27 + wk + kx];
+            return f8 ? v / Lp->wscale[co] : v;
         };
-        sp.N_total = L.Cout;
+        sp.N_total = fold ? 3 * L.Cout : L.Cout;
         dp.rowspace = gout;
         if (fp8) {
             colscale.resize(L.Cout);
@@ -257,9 +278,11 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     int N_tile = N_total <= 256 ? N_total : (N_total == 320 ? 320 : 256);
     if (N_total % N_tile) return fail(kUnsupported, L.name + ": output width " + std::to_string(N_total) + " not tileable");
     int R = N_tile <= 32 ? 8 : (N_tile <= 64 ? 4 : (N_tile <= 128 ? 2 : 1));
+    const int brows = fold ? 126 : 128;
+    if (fold) R = N_tile <= 48 ? 4 : (N_tile <= 96 ? 2 : 1);  // two slots of R x 3 Cout columns in 512
     const ActGeom& rs = dp.rowspace;
     const int64_t rows = static_cast<int64_t>(rs.D) * (rs.H + 2) * (rs.W + 2);
-    auto units = [&](int r) { return ((rows + 128 * r - 1) / (128 * r)) * Bmax_ * (N_total / N_tile); };
+    auto units = [&](int r) { return ((rows + brows * r - 1) / (brows * r)) * Bmax_ * (N_total / N_tile); };
     while (R > 1 && units(R) < 2 * sm_count_) R /= 2;
     const int slots = R * N_tile <= 256 ? 2 : 1;
     uint32_t cols = 32;
@@ -267,6 +290,8 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     if (cols > 512) return fail(kInternal, L.name + ": accumulator does not fit in TMEM");
     sp.N_tile = N_tile;
     sp.R = R;
+    sp.block_rows = brows;
+    if (fold) sp.smem_total -= static_cast<int>(fxk::conv_tc_fold_bytes(L.Cout));
     Status st;
     {
         std::string err = build_program(sp, dp.host);
@@ -276,7 +301,9 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     dp.N_tile = N_tile;
     dp.acc_slots = slots;
     dp.tmem_cols = cols;
-    dp.n_units_m = static_cast<int>((rows + 128 * R - 1) / (128 * R));
+    dp.n_units_m = static_cast<int>((rows + static_cast<int64_t>(brows) * R - 1) / (static_cast<int64_t>(brows) * R));
+    dp.fold = fold;
+    dp.block_rows = brows;
     dp.optype = q;
     if ((st = upload(dp.wpack, dp.host.wpack, this_net, allocs_)).code) return st;
     if ((st = upload(dp.colscale, colscale, this_net, allocs_)).code) return st;
@@ -293,8 +320,9 @@ Status Net::build_layer(Layer& L, int q) {
     if (L.kind != Layer::kUp && !L.d_partials) {
         const ActGeom g = level(L.lout);
         const int64_t rows = static_cast<int64_t>(g.D) * (g.H + 2) * (g.W + 2);
-        const int64_t nrec_max = ((rows + 127) / 128) * fxk::kStatRecsPerUnit;
+        const int64_t nrec_max = ((rows + 125) / 126) * fxk::kStatRecsPerUnit;
         L.d_partials = static_cast<float*>(dalloc(sizeof(float) * Bmax_ * nrec_max * L.Cout * 2));
+        L.nrec_cap = nrec_max;
         L.d_ss = static_cast<float*>(dalloc(sizeof(float) * Bmax_ * L.Cout * 2));
         if (!L.d_partials || !L.d_ss) return fail(kInternal, "cudaMalloc: stats buffers");
         if ((st = upload(L.d_gamma, L.gamma, this, allocs_)).code) return st;
@@ -462,6 +490,8 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     p.row_begin = P2;
     p.row_end = static_cast<int64_t>(p.Dp - 1) * P2;
     p.R = dp.R;
+    p.block_rows = dp.block_rows;
+    p.fold = dp.fold ? 1 : 0;
     p.n_units_m = dp.n_units_m;
     p.n_tiles = dp.host.n_tiles;
     p.N_tile = dp.N_tile;
@@ -497,6 +527,7 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
             L.cur_ratio = nullptr;
         }
         L.nrec = dp.n_units_m * fxk::kStatRecsPerUnit;
+        if (L.nrec > L.nrec_cap) return fail(kInternal, L.name + ": statistics buffer too small");
     }
     const int64_t units = static_cast<int64_t>(nb) * p.n_units_m * p.n_tiles;
     const int grid = static_cast<int>(std::min<int64_t>(units, sm_count_));

@@ -54,6 +54,8 @@ struct DevProgram {
     uint32_t tmem_cols = 32;
     ActGeom rowspace;  // output grid (conv) or input grid (transposed conv)
     int optype = 0;    // fxk::OpType of the operands
+    bool fold = false;     // x-tap fold (fxk::ConvParams::fold)
+    int block_rows = 128;
     bool built = false;
     size_t smem() const;
 };
@@ -74,6 +76,7 @@ struct Layer {
     float* d_partials = nullptr;      // [Bmax][n_units_m][kStatRecsPerUnit][Cout][2]
     float* d_ss = nullptr;            // [Bmax][Cout][2]
     int nrec = 0;
+    int64_t nrec_cap = 0;             // records per batch item that d_partials holds
     const float* cur_ratio = nullptr; // ratio of the last prenorm launch (its statistics' scale)
 };
 

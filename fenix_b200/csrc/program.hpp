@@ -29,7 +29,8 @@ struct ProgramSpec {
     int elem = 2;      // bytes per element
     int N_total = 0;   // output columns
     int N_tile = 0;    // columns per work unit
-    int R = 1;         // 128-row M blocks per unit
+    int R = 1;         // M blocks per unit
+    int block_rows = 128;  // window rows advanced per M block (126 with the x-tap fold)
     bool pair_taps = false;  // G == 1: the two K-halves of one MMA come from two taps
     std::vector<Tap> taps;
     // B value for output column n, input channel ci (0 <= ci < G*cg), tap key
@@ -127,7 +128,7 @@ inline std::string build_program(const ProgramSpec& s, Program& pg) {
     if (s.N_tile <= 0 || s.N_tile % 16 || s.N_total % s.N_tile) return "program: bad N tiling";
     if (s.N_tile > 256 && s.N_tile != 320) return "program: N tile > 256 must be 320";
     if (!s.pair_taps && (s.G % 2)) return "program: group count must be even";
-    const int Mtot = 128 * s.R;
+    const int Mtot = s.block_rows * (s.R - 1) + 128;  // rows spanned by a unit's M blocks
     // windows
     std::map<int, std::vector<Tap>> win;
     for (const Tap& t : s.taps) win[t.window].push_back(t);

@@ -23,6 +23,7 @@ enum : uint32_t {
     kStatusTimeoutAcc = 0x300,     // epilogue waited too long for an accumulator
     kStatusTimeoutAccFree = 0x400, // MMA issuer waited too long for a drained accumulator
     kStatusTimeoutDrain = 0x500,   // final drain of in-flight copies timed out
+    kStatusTimeoutExchange = 0x600, // fold epilogue waited too long for the row exchange
     kStatusBadTmem = 0x600,        // TMEM allocation returned an unexpected address
 };
 
@@ -152,6 +153,27 @@ __device__ __forceinline__ void mma_f8_if(uint32_t issue, uint32_t d_tmem, uint6
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
         : "memory");
 }
+// Three MMAs sharing one A tile (the x-tap fold): the first reads A from shared memory into the
+// A collector, the second reuses it, the third reuses and releases it; B and D differ.
+#define FX_MMA3(KIND)                                                                                           \
+    asm volatile(                                                                                               \
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %6, 0;\n\tsetp.ne.b32 q, %7, 0;\n\t"                    \
+        "@q tcgen05.mma.cta_group::1.kind::" KIND ".collector::a::fill [%0], %3, %4, %5, p;\n\t"              \
+        "@q tcgen05.mma.cta_group::1.kind::" KIND ".collector::a::use [%1], %3, %8, %5, p;\n\t"               \
+        "@q tcgen05.mma.cta_group::1.kind::" KIND ".collector::a::lastuse [%2], %3, %9, %5, p;\n\t}" ::"r"(d0), \
+        "r"(d1), "r"(d2), "l"(a_desc), "l"(b0), "r"(idesc), "r"(accumulate), "r"(issue), "l"(b1), "l"(b2)     \
+        : "memory")
+__device__ __forceinline__ void mma3_f16_if(uint32_t issue, uint32_t d0, uint32_t d1, uint32_t d2, uint64_t a_desc,
+                                            uint64_t b0, uint64_t b1, uint64_t b2, uint32_t idesc,
+                                            uint32_t accumulate) {
+    FX_MMA3("f16");
+}
+__device__ __forceinline__ void mma3_f8_if(uint32_t issue, uint32_t d0, uint32_t d1, uint32_t d2, uint64_t a_desc,
+                                           uint64_t b0, uint64_t b1, uint64_t b2, uint32_t idesc,
+                                           uint32_t accumulate) {
+    FX_MMA3("f8f6f4");
+}
+#undef FX_MMA3
 __device__ __forceinline__ void mma_commit_if(uint32_t issue, uint32_t bar) {
     asm volatile(
         "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"

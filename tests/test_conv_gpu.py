@@ -62,14 +62,32 @@ CONV_CASES = [
     (1, 256, 320, (4, 4, 4), 2),
     (1, 320, 320, (4, 4, 4), 1),
     (1, 1, 32, (16, 12, 20), 1),  # the 1-channel first layer (x-folded taps)
+    (1, 32, 32, (3, 5, 7), 1),     # fewer rows than one M block
+    (2, 32, 16, (20, 14, 30), 1),
+    (1, 64, 32, (24, 20, 18), 1),
 ]
+
+
+def _foldable(Cin, Cout, stride):
+    return stride == 1 and Cin > 1 and Cout in (16, 32, 64)
+
+
+@pytest.fixture(params=["fold", "nofold"])
+def fold_mode(request, monkeypatch):
+    """Stride-1 convs with 16/32/64 output channels run the x-tap fold when
+    FENIX_B200_CONV_FOLD=1: test both programs."""
+    monkeypatch.setenv("FENIX_B200_CONV_FOLD", "1" if request.param == "fold" else "0")
+    return request.param
 
 
 @pytest.mark.parametrize("kind", ["bf16", "f16"])
 @pytest.mark.parametrize("B,Cin,Cout,dims,stride", CONV_CASES)
-def test_conv3d_16bit(cuda_torch, B, Cin, Cout, dims, stride, kind):
+def test_conv3d_16bit(cuda_torch, fold_mode, B, Cin, Cout, dims, stride, kind):
     torch = cuda_torch
     import torch.nn.functional as F
+
+    if fold_mode == "nofold" and not _foldable(Cin, Cout, stride):
+        pytest.skip("same program either way")
 
     g = torch.Generator().manual_seed(1000 + Cin * 7 + Cout + stride)
     D, H, W = dims
@@ -92,9 +110,12 @@ def test_conv3d_16bit(cuda_torch, B, Cin, Cout, dims, stride, kind):
 
 
 @pytest.mark.parametrize("B,Cin,Cout,dims,stride", [c for c in CONV_CASES if c[1] >= 32])
-def test_conv3d_fp8(cuda_torch, B, Cin, Cout, dims, stride):
+def test_conv3d_fp8(cuda_torch, fold_mode, B, Cin, Cout, dims, stride):
     torch = cuda_torch
     import torch.nn.functional as F
+
+    if fold_mode == "nofold" and not _foldable(Cin, Cout, stride):
+        pytest.skip("same program either way")
 
     g = torch.Generator().manual_seed(2000 + Cin * 7 + Cout + stride)
     D, H, W = dims
