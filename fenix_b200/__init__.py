@@ -110,6 +110,16 @@ def lib():
     _sig(L, "fx_weight_profile", None, [f32p, i32, C.POINTER(C.c_int64), i64, i64, i64, i64, f32p])
     _sig(L, "fx_norm_tiles", i32, [vp, i64, i64, i64, C.POINTER(C.c_int64), i32, i32, vp, vp])
     _sig(L, "fx_norm_tiles_noalloc", i32, [vp, i64, i64, i64, C.POINTER(C.c_int64), i32, i32, vp, vp])
+    i64p = C.POINTER(C.c_int64)
+    _sig(L, "fx_gaccum_create", i32, [i64p, i64p, i32, C.c_double, i64, i32, C.POINTER(vp)])
+    _sig(L, "fx_gaccum_destroy", None, [vp])
+    for n in ("fx_gaccum_chunk_rows", "fx_gaccum_floor_row", "fx_gaccum_window_planes", "fx_gaccum_tile_rows"):
+        _sig(L, n, i64, [vp])
+    _sig(L, "fx_gaccum_row_start", i64, [vp, i64])
+    _sig(L, "fx_gaccum_set_floor_row", i32, [vp, i64])
+    _sig(L, "fx_gaccum_scatter", i32, [vp, i64, i64, i64, f32p])
+    _sig(L, "fx_gaccum_predict_row", i32, [vp, vp, i64, u8p, C.POINTER(InferOpts)])
+    _sig(L, "fx_gaccum_finalize_below", i32, [vp, i64, u8p, i64, i64p])
     _sig(L, "fx_conv3d", i32, [vp, i32, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp])
     _sig(L, "fx_conv_transpose2", i32, [vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp])
     _sig(L, "fx_accum_finalize", i32, [vp, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp])

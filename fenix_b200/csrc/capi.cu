@@ -68,6 +68,25 @@ fx_status guarded(F&& f) {
     }
 }
 
+}  // namespace
+
+namespace fxh {
+fx_status abi_error(int code, const std::string& msg) { return set_err(code, msg); }
+fx_status abi_exception() {
+    try {
+        throw;
+    } catch (const std::bad_alloc&) {
+        return set_err(FX_INTERNAL, "out of host memory");
+    } catch (const std::exception& e) {
+        return set_err(FX_INTERNAL, std::string("internal error: ") + e.what());
+    } catch (...) {
+        return set_err(FX_INTERNAL, "internal error");
+    }
+}
+}  // namespace fxh
+
+namespace {
+
 int sm_count_of_current() {
     int dev = 0, n = 148;
     cudaGetDevice(&dev);

@@ -280,13 +280,14 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const int c0 = SPLITC ? half : 0;             // first chunk
     const int rb = SPLITC ? 0 : half, rs = SPLITC ? 1 : 2;
     constexpr bool kAccR = kMy <= 2;         // sum over M blocks in registers, one butterfly per unit
-    constexpr int kGrp = kMy < 4 ? kMy : (kMy == 4 ? 4 : 2);  // chunks loaded from TMEM per wait
+    constexpr int kGrp = kMy <= 4 ? kMy : 1;  // chunks loaded from TMEM per wait
     constexpr int kR = kAccR ? kMy : 1;
     const bool e4out = p.out_type == kOpE4M3;
     // prenorm: a per-column scale table, or one scale for all columns (the per-channel part then
     // travels to the InstanceNorm statistics, which a per-channel factor does not change)
     const bool percol = p.col_scale != nullptr;
     const float acc_scale = p.acc_scale;
+    const int32_t oP2 = p.oHp * p.oWp;  // upsample: padded plane of the output grid
     uint32_t j = 0;
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
         int b, mu, nt;
@@ -320,6 +321,11 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
             const bool valid = row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 && x <= xmax;
             const uint32_t taddr =
                 tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + r * p.N_tile;
+            // upsample: phase-0 output cell of this input voxel (2z-1, 2y-1, 2x-1 in the padded grid)
+            uint8_t* ob = nullptr;
+            if (!prenorm && valid)
+                ob = p.out + static_cast<int64_t>(b) * p.out_batch_stride +
+                     ((static_cast<int64_t>(2 * z - 1) * p.oHp + (2 * y - 1)) * p.oWp + (2 * x - 1)) * 16;
 #pragma unroll
             for (int g0 = 0; g0 < kMy; g0 += kGrp) {
                 uint32_t raw[kGrp][16];
@@ -376,7 +382,7 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                         const int n0 = cbase + cc * 16;
                         const int a = n0 / p.cout;
                         const int co0 = n0 - a * p.cout;  // 16 consecutive channels of one phase
-                        // scale and bias already include the e4m3 output scale (ctl->up_scale/bias)
+                        // scale and bias already include the e4m3 output scale
 #pragma unroll
                         for (int i = 0; i < 16; ++i)
                             v[i] = fmaf(__uint_as_float(raw[c][i]), ctl->colscale[co0 + i], ctl->bias[co0 + i]);
@@ -388,11 +394,7 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                             atomicMax(p.amax, __float_as_uint(mx));
                         }
                         const int az = a >> 2, ay = (a >> 1) & 1, ax = a & 1;
-                        const int64_t orow =
-                            ((2 * static_cast<int64_t>(z) - 1 + az) * p.oHp + (2 * static_cast<int64_t>(y) - 1 + ay)) *
-                                p.oWp +
-                            (2 * static_cast<int64_t>(x) - 1 + ax);
-                        uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + orow * 16;
+                        uint8_t* o = ob + static_cast<int64_t>(az * oP2 + ay * p.oWp + ax) * 16;
                         if (e4out) {
                             uint4 w;
                             w.x = pack_e4m3x4(v[0], v[1], v[2], v[3]);

@@ -348,13 +348,34 @@ __global__ void __launch_bounds__(kEwThreads) head_blend_kernel(HeadParams h, Fa
     if (h.acc) {
         const TileOrigin t = h.tiles[b];
         const int64_t oz = t.z0 + z, oy = t.y0 + y, ox = t.x0 + x;
-        if (oz < h.dz && oy < h.dy && ox < h.dx) {
+        const int64_t az = oz + h.acc_z_shift;
+        if (oz < h.dz && oy < h.dy && ox < h.dx && az >= 0 && az < h.acc_dz) {
             // (gz*gy)*gx*p in the reference's order (src/ml/infer.hpp:631-653)
             const float wzy = __fmul_rn(__ldg(h.gauss + z), __ldg(h.gauss + y));
             const float c = __fmul_rn(__fmul_rn(wzy, __ldg(h.gauss + x)), p);
-            atomicAdd(h.acc + (oz * h.dy + oy) * h.dx + ox, c);
+            atomicAdd(h.acc + (az * h.dy + oy) * h.dx + ox, c);
         }
     }
+}
+
+__global__ void __launch_bounds__(kEwThreads) scatter_tile_kernel(const float* __restrict__ prob, int P, int64_t z0,
+                                                                   int64_t y0, int64_t x0, int64_t dz, int64_t dy,
+                                                                   int64_t dx, int64_t z_floor,
+                                                                   const float* __restrict__ gauss, float* acc,
+                                                                   int64_t acc_z_shift, int64_t acc_dz, FastDiv fp) {
+    const int z = blockIdx.y;
+    const uint32_t i = blockIdx.x * kEwThreads + threadIdx.x;
+    if (i >= static_cast<uint32_t>(P) * P) return;
+    const int y = static_cast<int>(fdiv(i, fp));
+    const int x = static_cast<int>(i - static_cast<uint32_t>(y) * P);
+    const int64_t oz = z0 + z, oy = y0 + y, ox = x0 + x;
+    const int64_t az = oz + acc_z_shift;
+    if (oz < 0 || oz >= dz || oy < 0 || oy >= dy || ox < 0 || ox >= dx || oz < z_floor || az < 0 || az >= acc_dz)
+        return;
+    const float p = __ldg(prob + static_cast<int64_t>(z) * P * P + i);
+    // (gz*gy)*gx*p in the reference's order (src/ml/global_accum.hpp:103-111)
+    const float wzy = __fmul_rn(__ldg(gauss + z), __ldg(gauss + y));
+    atomicAdd(acc + (az * dy + oy) * dx + ox, __fmul_rn(__fmul_rn(wzy, __ldg(gauss + x)), p));
 }
 
 // acc and prob may alias when z_begin == 0 (in-place normalise): each element is read before it
@@ -474,6 +495,17 @@ cudaError_t launch_head_blend(const HeadParams& h, cudaStream_t s) {
     count_launch();
     head_blend_kernel<<<dim3((PP + kEwThreads - 1) / kEwThreads, h.P, h.B), kEwThreads, 0, s>>>(
         h, make_fastdiv(static_cast<uint32_t>(h.P)));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_tile(const float* prob, int P, int64_t z0, int64_t y0, int64_t x0, int64_t dz, int64_t dy,
+                                int64_t dx, int64_t z_floor, const float* gauss, float* acc, int64_t acc_z_shift,
+                                int64_t acc_dz, cudaStream_t s) {
+    if (P < 1 || P > 46340 || !prob || !gauss || !acc) return cudaErrorInvalidValue;
+    const uint32_t PP = static_cast<uint32_t>(P) * P;
+    count_launch();
+    scatter_tile_kernel<<<dim3((PP + kEwThreads - 1) / kEwThreads, P), kEwThreads, 0, s>>>(
+        prob, P, z0, y0, x0, dz, dy, dx, z_floor, gauss, acc, acc_z_shift, acc_dz, make_fastdiv(static_cast<uint32_t>(P)));
     return cudaGetLastError();
 }
 

@@ -74,11 +74,21 @@ struct HeadParams {
     const float* bh;     // [ncls]
     const float* gauss;  // [P] gaussian1d(P)
     const TileOrigin* tiles;
-    float* acc;          // [dz][dy][dx] accumulator or null
-    int64_t dz, dy, dx;
+    float* acc;          // accumulator planes or null (see acc_z_shift)
+    int64_t dz, dy, dx;  // volume extents the tile origins refer to (voxels at z >= dz are skipped)
+    // accumulator plane of volume plane z is z + acc_z_shift; planes outside [0, acc_dz) are not
+    // written (a sliding window over a longer volume). acc_dz = dz, shift 0: the whole volume.
+    int64_t acc_z_shift, acc_dz;
     float* prob;         // [B][P^3] or null
 };
 cudaError_t launch_head_blend(const HeadParams& h, cudaStream_t s);
+
+// acc[z + acc_z_shift][y][x] += (gz * gy) * gx * p over one P^3 tile of probabilities at volume
+// origin (z0, y0, x0) (the reference's scatter, src/ml/global_accum.hpp:79-116): voxels outside
+// [0, dz) x [0, dy) x [0, dx), below plane z_floor, or outside the window [0, acc_dz) are skipped.
+cudaError_t launch_scatter_tile(const float* prob, int P, int64_t z0, int64_t y0, int64_t x0, int64_t dz, int64_t dy,
+                                int64_t dx, int64_t z_floor, const float* gauss, float* acc, int64_t acc_z_shift,
+                                int64_t acc_dz, cudaStream_t s);
 
 // acc / (Wz[z]*Wy[y]*Wx[x]) where the weight is > 0 (the reference's normalize), then
 // u8 = (u8)(clamp(p, 0, 1) * 255 + 0.5), for planes [z_begin, z_end) of acc; the outputs hold

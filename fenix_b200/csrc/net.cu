@@ -551,7 +551,8 @@ int Net::layer_q(const Layer& L, bool calib) const {
 }
 
 Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
-                    int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s) {
+                    int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s,
+                    int64_t acc_z_shift, int64_t acc_dz) {
     if (nb < 1 || nb > Bmax_) return fail(kInvalid, "forward: batch out of range");
     if (prec_ == 1 && !calib && !calibrated_) return fail(kInvalid, "forward: fp8 net used before fx_net_calibrate");
     Status st;
@@ -684,6 +685,8 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
                 h.dz = dz;
                 h.dy = dy;
                 h.dx = dx;
+                h.acc_z_shift = acc_z_shift;
+                h.acc_dz = acc_dz < 0 ? dz : acc_dz;
                 h.prob = prob;
                 if ((st = cuda_status(fxk::launch_head_blend(h, s), "head_blend")).code) return st;
             }
@@ -816,7 +819,7 @@ Status Net::workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint
 
 Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
                           int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
-                          int64_t tile_end, float* d_acc, cudaStream_t s) {
+                          int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin, int64_t acc_dz) {
     if (patch != P_) return fail(kInvalid, "predict: patch differs from the net's patch");
     if (batch < 1) batch = 1;
     batch = std::min(batch, Bmax_);
@@ -850,7 +853,11 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
     if (!st.ok()) return st;
     for (size_t i0 = 0; i0 < tiles.size(); i0 += batch) {
         const int nb = static_cast<int>(std::min<size_t>(batch, tiles.size() - i0));
-        if ((st = forward(d_vol, dz, dy, dx, d_tiles_ + i0, nb, channel, sigmoid, d_acc, nullptr, false, s)).code)
+        // accumulator window: acc plane 0 is volume plane acc_z_origin (default: the slab's origin)
+        const int64_t shift = acc_dz < 0 ? 0 : z_origin - acc_z_origin;
+        if ((st = forward(d_vol, dz, dy, dx, d_tiles_ + i0, nb, channel, sigmoid, d_acc, nullptr, false, s, shift,
+                          acc_dz))
+                .code)
             return st;
     }
     return ok();

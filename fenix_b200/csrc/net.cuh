@@ -101,14 +101,20 @@ class Net {
     Status set_act_scales(const float* scales, int n);
     // Forward nb tiles of a device volume at the given device tile origins. Head output:
     // Gaussian blend into acc (dims) and/or probabilities into prob ([nb][P^3]).
+    // acc_z_shift / acc_dz: the accumulator is a window of acc_dz planes whose plane 0 is slab
+    // plane -acc_z_shift (acc_dz < 0: the slab's own dz planes, shift 0).
     Status forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
-                   int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s);
+                   int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s,
+                   int64_t acc_z_shift = 0, int64_t acc_dz = -1);
     // Tiles [tile_begin, tile_end) of the z-major grid over a (full_dz, dy, dx) volume. d_vol and
     // d_acc hold the z-slab [z_origin, z_origin + dz) of that volume; every tile of the range must
     // lie inside the slab.
+    // With acc_dz >= 0, d_acc is a window of acc_dz planes starting at volume plane acc_z_origin
+    // (contributions outside it are dropped), independent of the input slab.
     Status predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
                          int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
-                         int64_t tile_end, float* d_acc, cudaStream_t s);
+                         int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin = 0,
+                         int64_t acc_dz = -1);
     // Device workspace for whole-volume calls: grown on demand, kept for the net's lifetime.
     Status workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint8_t** vol, float** acc, uint8_t** out);
 

@@ -25,6 +25,10 @@
  *                                     (src/ml/nets/resenc_unet.hpp:35-52, 211)
  *   fx_accum_finalize               — normalize() + u8 quantise (src/ml/infer.hpp:510-521,
  *                                     src/ml/global_accum.hpp:123-152)
+ *   fx_gaccum_*                     — ml::GlobalAccum: global-grid accumulator, z-sweep
+ *                                     finalize_rows_below, resume floor
+ *                                     (src/ml/global_accum.hpp:37-198), and a tile row of
+ *                                     predict-scroll's global mode (src/ml/inference.cpp:1282-1372)
  */
 #ifndef FENIX_B200_H
 #define FENIX_B200_H
@@ -85,7 +89,7 @@ int fx_net_classes(const fx_net* net);
 int fx_net_features(const fx_net* net, int* out, int cap); /* returns the stage count */
 
 /* fp8 only: record per-tensor activation amax over `n` host u8 patches ([n][P][P][P]) in a
- * bf16 calibration forward, and fix every activation scale to running-max(amax) / 448. */
+ * 16-bit (f16) calibration forward, and fix every activation scale to running-max(amax) / 448. */
 fx_status fx_net_calibrate(fx_net* net, const uint8_t* host_patches, int n);
 /* Per-tensor activation scales after calibration (cap entries); returns the count. One per conv
  * layer, in the order encoder convs (stage-major), transposed convs (finest level first),
@@ -132,6 +136,38 @@ unsigned long long fx_kernel_launches(void);
  * with FX_CONV_TRACE (producer / MMA issuer / epilogue waiting and working time); NULL detaches.
  * Without that build flag the counters are never touched. */
 void fx_conv_trace_buffer(void* dev_counters);
+
+/* ---- streaming global accumulator: GlobalAccum (src/ml/global_accum.hpp:37-198) on the device ----
+ * The global tile grid of predict-scroll over the 64-aligned bbox [org, org + ext): tile_starts
+ * of `patch` / `overlap` along each axis of ext. The f32 accumulator is a window of
+ * window_planes planes in HBM (rounded up to 64; 0 = patch + 64, enough for a z-sweep that
+ * finalizes the chunk rows below each tile row before running it), starting at the finalize floor.
+ * Chunk rows are 64 planes. Calls on one accumulator are serialised by the caller. */
+typedef struct fx_gaccum fx_gaccum;
+fx_status fx_gaccum_create(const int64_t* org3, const int64_t* ext3, int patch, double overlap, int64_t window_planes,
+                           int device, fx_gaccum** out);
+void fx_gaccum_destroy(fx_gaccum* acc);
+int64_t fx_gaccum_chunk_rows(const fx_gaccum* acc);    /* ceil(ext.z / 64) */
+int64_t fx_gaccum_floor_row(const fx_gaccum* acc);     /* chunk rows below are finalized */
+int64_t fx_gaccum_window_planes(const fx_gaccum* acc);
+int64_t fx_gaccum_tile_rows(const fx_gaccum* acc);     /* tile rows (z starts) of the grid */
+int64_t fx_gaccum_row_start(const fx_gaccum* acc, int64_t zi); /* bbox-local z start of tile row zi */
+/* Resume: chunk rows below floor_row are already finalized; contributions below are dropped
+ * (GlobalAccum::set_floor_row). */
+fx_status fx_gaccum_set_floor_row(fx_gaccum* acc, int64_t floor_row);
+/* Gaussian-blend one host P^3 probability tile at scroll coordinates (GlobalAccum::scatter).
+ * Fails with FX_INVALID_ARGUMENT when the tile reaches past the window. */
+fx_status fx_gaccum_scatter(fx_gaccum* acc, int64_t z0, int64_t y0, int64_t x0, const float* host_prob);
+/* Run every tile of tile row zi through `net` and blend it in: host_planes holds bbox-local
+ * planes [row_start(zi), min(row_start(zi) + patch, ext.z)) of the u8 input, [n][ext.y][ext.x]. */
+fx_status fx_gaccum_predict_row(fx_gaccum* acc, fx_net* net, int64_t zi, const uint8_t* host_planes,
+                                const fx_infer_opts* opts);
+/* Finalize chunk rows [floor_row, row_lim) (GlobalAccum::finalize_rows_below): normalise by
+ * Wz.Wy.Wx, (u8)(clamp(v, 0, 1) * 255 + 0.5), written to host_u8 as the planes
+ * [floor_row * 64, min(row_lim * 64, ext.z)) x ext.y x ext.x (cap_bytes >= that); *planes_out
+ * receives their count. The window then starts at row_lim. */
+fx_status fx_gaccum_finalize_below(fx_gaccum* acc, int64_t row_lim, uint8_t* host_u8, int64_t cap_bytes,
+                                   int64_t* planes_out);
 
 /* ---- tiling math (host) ---- */
 /* Start positions along one axis; returns the count (writes at most cap). */

@@ -9,7 +9,9 @@
 //   - ml::predict_surface over a dense u8 volume (src/ml/infer.hpp:456-878 driven by the dense u8
 //     filler of src/ml/inference.cpp:309-321) and its u8 encode (src/ml/inference.cpp:343-351),
 //   - ml::predict_surface_window (src/ml/ml_api.hpp:16-24, src/ml/inference.cpp:914-962),
-//   - the predict-surface stage argument grammar (src/ml/inference.cpp:369-420).
+//   - the predict-surface stage argument grammar (src/ml/inference.cpp:369-420),
+//   - ml::GlobalAccum, the global-grid accumulator with its z-sweep finalize and resume floor
+//     (src/ml/global_accum.hpp:37-198), kept on the device.
 // Every computation runs on the GPU through the extern "C" ABI of fenix_b200.h. Options the device
 // path does not implement (TTA, non-zscore normalisation, core crops, multi-scale, checkpoints,
 // tile filters) return Errc::unsupported; there is no CPU fallback.
@@ -17,6 +19,7 @@
 
 #include "fenix_b200.h"
 
+#include <algorithm>
 #include <charconv>
 #include <cstdint>
 #include <cstring>
@@ -65,6 +68,11 @@ struct Extent3 {
 struct Index3 {
     s64 z = 0, y = 0, x = 0;
     friend constexpr bool operator==(Index3, Index3) = default;
+};
+// Chunk coordinate = voxel >> 6 (64^3 chunks).
+struct ChunkCoord {
+    s64 z = 0, y = 0, x = 0;
+    friend constexpr bool operator==(ChunkCoord, ChunkCoord) = default;
 };
 
 // Non-owning strided ZYX view (x fastest when contiguous).
@@ -270,6 +278,106 @@ inline Expected<void> run(VolumeView<const u8> in, B200Net& net, const InferOpti
     }
     return predict_surface_u8(ct, cache.net, opt);
 }
+
+// The global tile grid of predict-scroll over a 64-aligned bbox with its accumulator on the
+// device (fx_gaccum_*): scatter tiles or run whole tile rows through a net, then finalize chunk
+// rows below a z-front; finalize_rows_below hands every 64^3 chunk of those rows to
+// sink(ChunkCoord /*archive coordinates*/, const u8* /*64^3 ZYX*/), voxels past the bbox as 0.
+class GlobalAccum {
+public:
+    static constexpr s64 T = 64;
+    GlobalAccum() = default;
+    GlobalAccum(const GlobalAccum&) = delete;
+    GlobalAccum& operator=(const GlobalAccum&) = delete;
+    GlobalAccum(GlobalAccum&& o) noexcept
+        : h_(std::exchange(o.h_, nullptr)), org_(o.org_), ext_(o.ext_), patch_(o.patch_), overlap_(o.overlap_) {}
+    GlobalAccum& operator=(GlobalAccum&& o) noexcept {
+        if (this != &o) {
+            if (h_) fx_gaccum_destroy(h_);
+            h_ = std::exchange(o.h_, nullptr);
+            org_ = o.org_;
+            ext_ = o.ext_;
+            patch_ = o.patch_;
+            overlap_ = o.overlap_;
+        }
+        return *this;
+    }
+    ~GlobalAccum() {
+        if (h_) fx_gaccum_destroy(h_);
+    }
+
+    // window_planes: accumulator planes kept on the device (0 = patch + 64, enough for a sweep
+    // that finalizes the chunk rows below each tile row before running it).
+    [[nodiscard]] static Expected<GlobalAccum> create(Index3 org, Extent3 ext, int patch, double overlap,
+                                                      s64 window_planes = 0, int device = 0) {
+        GlobalAccum a;
+        const int64_t o[3] = {org.z, org.y, org.x}, e[3] = {ext.z, ext.y, ext.x};
+        const fx_status st = fx_gaccum_create(o, e, patch, overlap, window_planes, device, &a.h_);
+        if (st != FX_OK) return err_status(st, "GlobalAccum::create");
+        a.org_ = org;
+        a.ext_ = ext;
+        a.patch_ = patch;
+        a.overlap_ = overlap;
+        return a;
+    }
+    [[nodiscard]] s64 chunk_rows() const { return fx_gaccum_chunk_rows(h_); }
+    [[nodiscard]] s64 floor_row() const { return fx_gaccum_floor_row(h_); }
+    [[nodiscard]] s64 tile_rows() const { return fx_gaccum_tile_rows(h_); }
+    [[nodiscard]] s64 row_start(s64 zi) const { return fx_gaccum_row_start(h_, zi); }
+    [[nodiscard]] Expected<void> set_floor_row(s64 floor_row) {
+        const fx_status st = fx_gaccum_set_floor_row(h_, floor_row);
+        if (st != FX_OK) return err_status(st, "GlobalAccum::set_floor_row");
+        return {};
+    }
+    // Gaussian-blend one P^3 probability tile at scroll coordinates (P = the grid's patch).
+    [[nodiscard]] Expected<void> scatter(s64 z0, s64 y0, s64 x0, int P, const float* sp) {
+        if (P != patch_) return err(Errc::invalid_argument, "GlobalAccum::scatter: patch differs from the grid's");
+        const fx_status st = fx_gaccum_scatter(h_, z0, y0, x0, sp);
+        if (st != FX_OK) return err_status(st, "GlobalAccum::scatter");
+        return {};
+    }
+    // All tiles of tile row zi through `net`; planes = bbox-local input planes
+    // [row_start(zi), min(row_start(zi) + patch, ext.z)), [n][ext.y][ext.x].
+    [[nodiscard]] Expected<void> predict_row(B200Net& net, s64 zi, const u8* planes, const InferOptions& opt) {
+        auto o = to_fx(opt);
+        if (!o) return std::unexpected(o.error());
+        const fx_status st = fx_gaccum_predict_row(h_, net.handle(), zi, planes, &*o);
+        if (st != FX_OK) return err_status(st, "GlobalAccum::predict_row");
+        return {};
+    }
+    template <class Sink>
+    [[nodiscard]] Expected<void> finalize_rows_below(s64 row_lim, Sink&& sink) {
+        const s64 r0 = floor_row(), r1 = std::min(row_lim, chunk_rows());
+        if (r1 <= r0) return {};
+        const s64 z0 = r0 * T, z1 = std::min(r1 * T, ext_.z), plane = ext_.y * ext_.x;
+        std::vector<u8> planes(static_cast<std::size_t>((z1 - z0) * plane));
+        int64_t n = 0;
+        const fx_status st = fx_gaccum_finalize_below(h_, row_lim, planes.data(), static_cast<int64_t>(planes.size()), &n);
+        if (st != FX_OK) return err_status(st, "GlobalAccum::finalize_rows_below");
+        std::vector<u8> blk(static_cast<std::size_t>(T * T * T));
+        const s64 ncy = (ext_.y + T - 1) / T, ncx = (ext_.x + T - 1) / T;
+        for (s64 cz = r0; cz < r1; ++cz)
+            for (s64 cy = 0; cy < ncy; ++cy)
+                for (s64 cx = 0; cx < ncx; ++cx) {
+                    std::fill(blk.begin(), blk.end(), u8{0});
+                    for (s64 z = 0; z < T && cz * T + z < z1; ++z)
+                        for (s64 y = 0; y < T && cy * T + y < ext_.y; ++y) {
+                            const s64 xs = std::min<s64>(T, ext_.x - cx * T);
+                            const u8* src = planes.data() + ((cz * T + z - z0) * ext_.y + cy * T + y) * ext_.x + cx * T;
+                            std::memcpy(blk.data() + (z * T + y) * T, src, static_cast<std::size_t>(xs));
+                        }
+                    sink(ChunkCoord{org_.z / T + cz, org_.y / T + cy, org_.x / T + cx}, static_cast<const u8*>(blk.data()));
+                }
+        return {};
+    }
+
+private:
+    fx_gaccum* h_ = nullptr;
+    Index3 org_{};
+    Extent3 ext_{};
+    int patch_ = 0;
+    double overlap_ = 0.5;
+};
 
 // Arguments of the predict-surface stage: <in> <weights> <out> [patch] [overlap] [tta] [batch],
 // positional slots holding a key=value token are skipped, then key=value options. Keys this path

@@ -3,6 +3,7 @@
 //   host_api_test gpu <weights> <out>   — predict_surface_window and predict_surface_u8 on a
 //                                         synthetic window; writes both outputs to <out>
 #include "fenix_b200/ml/infer.hpp"
+#include "fenix_b200/ml/tiling.hpp"
 #include "fenix_b200_synth.h"
 
 #include <cstdio>
@@ -79,6 +80,10 @@ static int cpu() {
         CHECK(!r && r.error().code == Errc::invalid_argument);
     }
     CHECK(static_cast<int>(Errc::internal) == FX_INTERNAL && static_cast<int>(Errc::unsupported) == FX_UNSUPPORTED);
+    {  // the grid origin must be 64-aligned (checked before any device work)
+        auto g = ml::GlobalAccum::create({32, 0, 0}, {128, 64, 64}, 64, 0.5);
+        CHECK(!g && g.error().code == Errc::invalid_argument);
+    }
     std::printf("%s\n", fails ? "FAIL" : "ok");
     return fails ? 1 : 0;
 }
@@ -116,6 +121,22 @@ static int gpu(const char* weights, const char* outpath) {
     f.write(reinterpret_cast<const char*>(w1->data()), static_cast<std::streamsize>(vol.size()));
     f.write(reinterpret_cast<const char*>(u->data()), static_cast<std::streamsize>(vol.size()));
     f.write(reinterpret_cast<const char*>(vol.data()), static_cast<std::streamsize>(vol.size()));
+    {  // GlobalAccum sink: the reference's constant round trip (18 chunks of exactly 153)
+        auto g = ml::GlobalAccum::create({64, 0, 64}, {192, 128, 192}, 64, 0.5, 192);
+        if (!g) return 6;
+        std::vector<float> sp(64 * 64 * 64, 0.6f);
+        const auto zs = fenix::ml::tile_starts(192, 64, 0.5), ys = fenix::ml::tile_starts(128, 64, 0.5);
+        for (s64 z0 : zs)
+            for (s64 y0 : ys)
+                for (s64 x0 : zs) CHECK(g->scatter(64 + z0, y0, 64 + x0, 64, sp.data()).has_value());
+        int chunks = 0, bad = 0;
+        auto r = g->finalize_rows_below(g->chunk_rows(), [&](ChunkCoord c, const u8* blk) {
+            ++chunks;
+            if (c.z < 1 || c.x < 1) ++bad;
+            for (int i = 0; i < 64 * 64 * 64; ++i) bad += blk[i] != 153;
+        });
+        CHECK(r.has_value() && chunks == 18 && bad == 0);
+    }
     std::printf("%s\n", fails ? "FAIL" : "ok");
     return fails ? 1 : 0;
 }
