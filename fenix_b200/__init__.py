@@ -49,6 +49,7 @@ class InferOpts(C.Structure):
         ("channel", C.c_int),
         ("sigmoid", C.c_int),
         ("batch", C.c_int),
+        ("tta", C.c_int),
     ]
 
 
@@ -267,10 +268,10 @@ class Net:
         check(lib().fx_net_forward(self._h, dev_tiles_ptr, nb, dev_prob_ptr, channel, sigmoid, stream))
 
     def predict_volume(self, vol_u8: np.ndarray, overlap: float = 0.5, batch: int = 1, channel: int = 1,
-                       sigmoid: int = 0, want_prob: bool = True, want_u8: bool = True):
+                       sigmoid: int = 0, want_prob: bool = True, want_u8: bool = True, tta: int = 0):
         v = np.ascontiguousarray(vol_u8, dtype=np.uint8)
         dz, dy, dx = v.shape
-        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch)
+        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch, tta)
         prob = np.zeros(v.shape, dtype=np.float32) if want_prob else None
         u8 = np.zeros(v.shape, dtype=np.uint8) if want_u8 else None
         check(
@@ -289,9 +290,9 @@ class Net:
 
     def predict_tiles_dev(self, dev_slab_ptr: int, slab_shape, z_origin: int, full_dz: int, overlap: float,
                           batch: int, tile_begin: int, tile_end: int, dev_acc_ptr: int, channel: int = 1,
-                          sigmoid: int = 0, stream: int | None = None) -> None:
+                          sigmoid: int = 0, stream: int | None = None, tta: int = 0) -> None:
         dz, dy, dx = slab_shape
-        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch)
+        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch, tta)
         check(lib().fx_predict_tiles_dev(self._h, dev_slab_ptr, dz, dy, dx, z_origin, full_dz, C.byref(opts),
                                          tile_begin, tile_end, dev_acc_ptr, stream))
 

@@ -225,7 +225,8 @@ fx_status fx_predict_tiles_dev(fx_net* n, const uint8_t* dev_slab, int64_t slab_
         cudaSetDevice(n->net.device());
         cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : n->net.stream();
         fxh::Status st = n->net.predict_tiles(dev_slab, slab_dz, dy, dx, z_origin, full_dz, o->patch, o->overlap,
-                                              o->channel, o->sigmoid, o->batch, tile_begin, tile_end, dev_acc, s);
+                                              o->channel, o->sigmoid, o->batch, tile_begin, tile_end, dev_acc, s, 0,
+                                              -1, o->tta);
         return st.ok() ? FX_OK : set_err(st);
     });
 }
@@ -256,7 +257,7 @@ fx_status fx_predict_volume(fx_net* n, const uint8_t* host_vol, int64_t dz, int6
         cudaMemcpyAsync(d_vol, host_vol, nv, cudaMemcpyHostToDevice, s);
         cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
         st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, o->patch, o->overlap, o->channel, o->sigmoid, o->batch, 0,
-                                  -1, d_acc, s);
+                                  -1, d_acc, s, 0, -1, o->tta);
         if (!st.ok()) return set_err(st);
         const int P = o->patch;
         const auto g = fenix::ml::gaussian1d(P);

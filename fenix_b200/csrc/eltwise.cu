@@ -80,7 +80,8 @@ __device__ __forceinline__ void build_lut(float* lut, unsigned long long S, unsi
 __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, int64_t dy, int64_t dx,
                                  const TileOrigin* __restrict__ tiles, int P,
                                  const unsigned long long* __restrict__ sums, uint8_t* __restrict__ l0,
-                                 int64_t l0_batch_stride, int l0_type, float* __restrict__ f32_out) {
+                                 int64_t l0_batch_stride, int l0_type, float* __restrict__ f32_out,
+                                 const uint8_t* __restrict__ tta) {
     const int b = blockIdx.y;
     __shared__ float lut[256];
     const int64_t n = static_cast<int64_t>(P) * P * P;
@@ -102,8 +103,10 @@ __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, in
             if (xx < 0 || xx >= P) {
                 v[k] = 0.f;
             } else {
-                const uint8_t u = inside ? __ldg(vol + ((t.z0 + z) * dy + (t.y0 + y)) * dx + (t.x0 + xx))
-                                         : vol_at(vol, dz, dy, dx, t.z0 + z, t.y0 + y, t.x0 + xx);
+                int sz = z, sy = y, sx = xx;  // source voxel of this member's frame voxel
+                if (tta) tta_source(tta[b], P, z, y, xx, sz, sy, sx);
+                const uint8_t u = inside ? __ldg(vol + ((t.z0 + sz) * dy + (t.y0 + sy)) * dx + (t.x0 + sx))
+                                         : vol_at(vol, dz, dy, dx, t.z0 + sz, t.y0 + sy, t.x0 + sx);
                 v[k] = lut[u];
             }
         }
@@ -344,9 +347,15 @@ __global__ void __launch_bounds__(kEwThreads) head_blend_kernel(HeadParams h, Fa
     if (isnan(p)) p = 0.f;
     else if (isinf(p)) p = p > 0.f ? 1.f : 0.f;
     const int64_t n = static_cast<int64_t>(P) * P * P;
-    if (h.prob) h.prob[b * n + static_cast<int64_t>(z) * P * P + i] = p;
+    int sz = z, sy = y, sx = x;  // tile voxel this output belongs to (its TTA member's source)
+    if (h.tta) {
+        tta_source(h.tta[b], P, z, y, x, sz, sy, sx);
+        p *= h.tta_scale;
+    }
+    if (h.prob) h.prob[b * n + (static_cast<int64_t>(sz) * P + sy) * P + sx] = p;
     if (h.acc) {
         const TileOrigin t = h.tiles[b];
+        const int z = sz, y = sy, x = sx;
         const int64_t oz = t.z0 + z, oy = t.y0 + y, ox = t.x0 + x;
         const int64_t az = oz + h.acc_z_shift;
         if (oz < h.dz && oy < h.dy && ox < h.dx && az >= 0 && az < h.acc_dz) {
@@ -445,12 +454,12 @@ cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
 
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
                              int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
-                             int l0_type, float* f32_out, cudaStream_t s) {
+                             int l0_type, float* f32_out, cudaStream_t s, const uint8_t* tta) {
     const int64_t n = static_cast<int64_t>(P) * P * P;
     int gx = grid_for(n, kEwThreads * 4);
     count_launch();
     tile_norm_kernel<<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums, l0, l0_batch_stride,
-                                                             l0_type, f32_out);
+                                                             l0_type, f32_out, tta);
     return cudaGetLastError();
 }
 

@@ -28,9 +28,29 @@ cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
 // goes through a 256-entry table built with the reference's double-precision expression, so
 // the normalised value of each u8 level is the same float the reference computes.
 // `l0_type` is the first conv's operand type (kOpBF16 or kOpF16); l0 may be null.
+// tta (one byte per tile, or null): octahedral test-time-augmentation member of each tile; the
+// tile is written in that member's frame (see tta_source).
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
                              int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
-                             int l0_type, float* f32_out, cudaStream_t s);
+                             int l0_type, float* f32_out, cudaStream_t s, const uint8_t* tta = nullptr);
+
+// Octahedral TTA (src/ml/infer.hpp:346, 393-441): member m of the first N of 48 uses the axis
+// permutation perms[m / 8] and flips the transformed frame's axes in the bits of m % 8 (bit 0 z,
+// bit 1 y, bit 2 x). Voxel a of the member's frame is voxel o of the tile with
+// o[perm[d]] = (flip_d ? P - 1 - a[d] : a[d]); the network's output at a belongs to o.
+constexpr int kTtaMaxMembers = 48;
+__host__ __device__ inline void tta_source(int m, int P, int a0, int a1, int a2, int& o0, int& o1, int& o2) {
+    const int perm[6][3] = {{0, 1, 2}, {0, 2, 1}, {1, 0, 2}, {1, 2, 0}, {2, 0, 1}, {2, 1, 0}};
+    const int pi = m >> 3, fm = m & 7;
+    const int a[3] = {(fm & 1) ? P - 1 - a0 : a0, (fm & 2) ? P - 1 - a1 : a1, (fm & 4) ? P - 1 - a2 : a2};
+    int o[3];
+    o[perm[pi][0]] = a[0];
+    o[perm[pi][1]] = a[1];
+    o[perm[pi][2]] = a[2];
+    o0 = o[0];
+    o1 = o[1];
+    o2 = o[2];
+}
 
 // ---- InstanceNorm ----------------------------------------------------------------------------
 // partials [B][nrec][C][2] -> ss [B][C][2] = {scale, shift} with scale = gamma * rstd and
@@ -74,6 +94,8 @@ struct HeadParams {
     const float* bh;     // [ncls]
     const float* gauss;  // [P] gaussian1d(P)
     const TileOrigin* tiles;
+    const uint8_t* tta;  // TTA member of each tile (null: none); the output at a goes to tta_source(a)
+    float tta_scale;     // 1 / members (the blend adds the members' mean)
     float* acc;          // accumulator planes or null (see acc_z_shift)
     int64_t dz, dy, dx;  // volume extents the tile origins refer to (voxels at z >= dz are skipped)
     // accumulator plane of volume plane z is z + acc_z_shift; planes outside [0, acc_dz) are not

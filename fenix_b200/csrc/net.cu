@@ -552,7 +552,7 @@ int Net::layer_q(const Layer& L, bool calib) const {
 
 Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
                     int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s,
-                    int64_t acc_z_shift, int64_t acc_dz) {
+                    int64_t acc_z_shift, int64_t acc_dz, const uint8_t* d_tta, float tta_scale) {
     if (nb < 1 || nb > Bmax_) return fail(kInvalid, "forward: batch out of range");
     if (prec_ == 1 && !calib && !calibrated_) return fail(kInvalid, "forward: fp8 net used before fx_net_calibrate");
     Status st;
@@ -560,7 +560,7 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
     if ((st = cuda_status(cudaMemsetAsync(d_sums_, 0, sizeof(unsigned long long) * 2 * nb, s), "memset")).code) return st;
     if ((st = cuda_status(fxk::launch_tile_sums(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, s), "tile_sums")).code) return st;
     if ((st = cuda_status(fxk::launch_tile_norm(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, l0_, g0.gs(), t16(), nullptr,
-                                                s),
+                                                s, d_tta),
                           "tile_norm"))
             .code)
         return st;
@@ -681,6 +681,8 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
                 h.bh = d_head_b_;
                 h.gauss = d_gauss_;
                 h.tiles = d_tiles;
+                h.tta = d_tta;
+                h.tta_scale = tta_scale;
                 h.acc = acc;
                 h.dz = dz;
                 h.dy = dy;
@@ -819,7 +821,8 @@ Status Net::workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint
 
 Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
                           int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
-                          int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin, int64_t acc_dz) {
+                          int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin, int64_t acc_dz,
+                          int tta) {
     if (patch != P_) return fail(kInvalid, "predict: patch differs from the net's patch");
     if (batch < 1) batch = 1;
     batch = std::min(batch, Bmax_);
@@ -830,8 +833,11 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
     if (tile_end < 0 || tile_end > total) tile_end = total;
     if (tile_begin < 0) tile_begin = 0;
     if (tile_begin >= tile_end) return ok();
+    // TTA: every tile once per member (src/ml/infer.hpp:554)
+    const int ne = tta <= 1 ? 1 : std::min(tta, fxk::kTtaMaxMembers);
     std::vector<fxk::TileOrigin> tiles;
-    tiles.reserve(static_cast<size_t>(tile_end - tile_begin));
+    std::vector<uint8_t> members;
+    tiles.reserve(static_cast<size_t>(tile_end - tile_begin) * ne);
     for (int64_t i = tile_begin; i < tile_end; ++i) {
         const int64_t xi = i % static_cast<int64_t>(xs.size());
         const int64_t yi = (i / static_cast<int64_t>(xs.size())) % static_cast<int64_t>(ys.size());
@@ -839,24 +845,33 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
         const int64_t zl = zs[zi] - z_origin;  // slab-local
         if (zl < 0 || (zl + P_ > dz && full_dz >= P_))
             return fail(kInvalid, "predict: tile " + std::to_string(i) + " is outside the z-slab");
-        tiles.push_back({zl, ys[yi], xs[xi]});
+        for (int m = 0; m < ne; ++m) {
+            tiles.push_back({zl, ys[yi], xs[xi]});
+            members.push_back(static_cast<uint8_t>(m));
+        }
     }
     if (static_cast<int64_t>(tiles.size()) > d_tiles_cap_) {
         void* p = dalloc(sizeof(fxk::TileOrigin) * tiles.size());
-        if (!p) return fail(kInternal, "cudaMalloc: tile list");
+        void* q = dalloc(tiles.size());
+        if (!p || !q) return fail(kInternal, "cudaMalloc: tile list");
         d_tiles_ = static_cast<fxk::TileOrigin*>(p);
+        d_tta_ = static_cast<uint8_t*>(q);
         d_tiles_cap_ = static_cast<int64_t>(tiles.size());
     }
     Status st = cuda_status(cudaMemcpyAsync(d_tiles_, tiles.data(), sizeof(fxk::TileOrigin) * tiles.size(),
                                             cudaMemcpyHostToDevice, s),
                             "H2D tiles");
     if (!st.ok()) return st;
+    if (ne > 1 && (st = cuda_status(cudaMemcpyAsync(d_tta_, members.data(), members.size(), cudaMemcpyHostToDevice, s),
+                                    "H2D tta"))
+                      .code)
+        return st;
     for (size_t i0 = 0; i0 < tiles.size(); i0 += batch) {
         const int nb = static_cast<int>(std::min<size_t>(batch, tiles.size() - i0));
         // accumulator window: acc plane 0 is volume plane acc_z_origin (default: the slab's origin)
         const int64_t shift = acc_dz < 0 ? 0 : z_origin - acc_z_origin;
         if ((st = forward(d_vol, dz, dy, dx, d_tiles_ + i0, nb, channel, sigmoid, d_acc, nullptr, false, s, shift,
-                          acc_dz))
+                          acc_dz, ne > 1 ? d_tta_ + i0 : nullptr, 1.f / static_cast<float>(ne)))
                 .code)
             return st;
     }

@@ -103,9 +103,11 @@ class Net {
     // Gaussian blend into acc (dims) and/or probabilities into prob ([nb][P^3]).
     // acc_z_shift / acc_dz: the accumulator is a window of acc_dz planes whose plane 0 is slab
     // plane -acc_z_shift (acc_dz < 0: the slab's own dz planes, shift 0).
+    // d_tta: TTA member of each tile (null: none), tta_scale = 1 / members.
     Status forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const fxk::TileOrigin* d_tiles, int nb,
                    int channel, int sigmoid, float* acc, float* prob, bool calib, cudaStream_t s,
-                   int64_t acc_z_shift = 0, int64_t acc_dz = -1);
+                   int64_t acc_z_shift = 0, int64_t acc_dz = -1, const uint8_t* d_tta = nullptr,
+                   float tta_scale = 1.f);
     // Tiles [tile_begin, tile_end) of the z-major grid over a (full_dz, dy, dx) volume. d_vol and
     // d_acc hold the z-slab [z_origin, z_origin + dz) of that volume; every tile of the range must
     // lie inside the slab.
@@ -114,7 +116,7 @@ class Net {
     Status predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
                          int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
                          int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin = 0,
-                         int64_t acc_dz = -1);
+                         int64_t acc_dz = -1, int tta = 0);
     // Device workspace for whole-volume calls: grown on demand, kept for the net's lifetime.
     Status workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint8_t** vol, float** acc, uint8_t** out);
 
@@ -177,6 +179,7 @@ class Net {
     float* d_gauss_ = nullptr;
     uint32_t* d_status_ = nullptr;
     fxk::TileOrigin* d_tiles_ = nullptr;
+    uint8_t* d_tta_ = nullptr;  // TTA member of each entry of d_tiles_
     int64_t d_tiles_cap_ = 0;
     uint8_t* ws_vol_ = nullptr;
     float* ws_acc_ = nullptr;

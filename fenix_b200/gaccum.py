@@ -57,9 +57,10 @@ class GlobalAccum:
         assert p.size == self.patch ** 3
         check(lib().fx_gaccum_scatter(self._h, z0, y0, x0, p.ctypes.data_as(C.POINTER(C.c_float))))
 
-    def predict_row(self, net, zi: int, planes: np.ndarray, batch: int = 1, channel: int = 1, sigmoid: int = 0):
+    def predict_row(self, net, zi: int, planes: np.ndarray, batch: int = 1, channel: int = 1, sigmoid: int = 0,
+                    tta: int = 0):
         v = np.ascontiguousarray(planes, dtype=np.uint8)
-        opts = InferOpts(self.patch, self.overlap, channel, sigmoid, batch)
+        opts = InferOpts(self.patch, self.overlap, channel, sigmoid, batch, tta)
         check(lib().fx_gaccum_predict_row(self._h, net.handle, zi, v.ctypes.data_as(C.POINTER(C.c_uint8)),
                                           C.byref(opts)))
 

@@ -65,6 +65,8 @@ typedef struct fx_infer_opts {
     int channel;    /* softmax channel to emit (surface = 1); ignored with sigmoid */
     int sigmoid;    /* 1-class head -> sigmoid */
     int batch;      /* tiles per forward, <= the net's max batch */
+    int tta;        /* octahedral test-time augmentation: <= 1 off, else the first min(tta, 48)
+                       symmetries, averaged (src/ml/infer.hpp:393-441); each costs a forward */
 } fx_infer_opts;
 
 typedef struct fx_net fx_net;

@@ -13,8 +13,8 @@
 //   - ml::GlobalAccum, the global-grid accumulator with its z-sweep finalize and resume floor
 //     (src/ml/global_accum.hpp:37-198), kept on the device.
 // Every computation runs on the GPU through the extern "C" ABI of fenix_b200.h. Options the device
-// path does not implement (TTA, non-zscore normalisation, core crops, multi-scale, checkpoints,
-// tile filters) return Errc::unsupported; there is no CPU fallback.
+// path does not implement (non-zscore normalisation, core crops, multi-scale, rotation / noise /
+// offset TTA, checkpoints, tile filters) return Errc::unsupported; there is no CPU fallback.
 #pragma once
 
 #include "fenix_b200.h"
@@ -133,7 +133,7 @@ struct InferOptions {
     int channel = 1;       // softmax channel to emit; ignored with sigmoid
     bool sigmoid = false;  // 1-class head -> sigmoid
     Norm norm = Norm::zscore;
-    int tta = 0;  // <= 1: off (octahedral TTA is not implemented on this path)
+    int tta = 0;  // <= 1: off; else the first min(tta, 48) octahedral symmetries, averaged
     Index3 core_org{0, 0, 0};
     Extent3 core_ext{-1, -1, -1};  // whole input
     int batch = 3;                 // tiles per forward
@@ -141,14 +141,13 @@ struct InferOptions {
 
 // The options as the ABI struct, or unsupported/invalid_argument for what this path lacks.
 [[nodiscard]] inline Expected<fx_infer_opts> to_fx(const InferOptions& o) {
-    if (o.tta > 1) return err(Errc::unsupported, "InferOptions: test-time augmentation is not implemented on the B200 path");
     if (o.norm != Norm::zscore) return err(Errc::unsupported, "InferOptions: only zscore normalisation is implemented");
     if (o.core_ext.z >= 0 || o.core_ext.y >= 0 || o.core_ext.x >= 0)
         return err(Errc::unsupported, "InferOptions: core crops are not implemented on the B200 path");
     if (o.patch < 1 || o.batch < 1 || !(o.overlap >= 0.0 && o.overlap < 1.0))
         return err(Errc::invalid_argument, "InferOptions: bad patch, batch or overlap");
     if (o.channel < 0 || o.channel > 1) return err(Errc::invalid_argument, "InferOptions: channel must be 0 or 1");
-    return fx_infer_opts{o.patch, o.overlap, o.channel, o.sigmoid ? 1 : 0, o.batch};
+    return fx_infer_opts{o.patch, o.overlap, o.channel, o.sigmoid ? 1 : 0, o.batch, o.tta};
 }
 
 // One net on one device (the operator concept of the reference's TrtNet / AotiNet).

@@ -39,7 +39,10 @@ static int cpu() {
     }
     CHECK(!parse({"in", "w"}) && parse({"in", "w"}).error().code == Errc::invalid_argument);
     CHECK(parse({"in", "w", "out", "12x"}).error().code == Errc::invalid_argument);
-    CHECK(parse({"in", "w", "out", "128", "0.5", "8"}).error().code == Errc::unsupported);  // tta 8
+    {  // positional tta: the octahedral members go to the ABI
+        auto a = parse({"in", "w", "out", "128", "0.5", "8"});
+        CHECK(a && a->opt.tta == 8 && ml::to_fx(a->opt) && ml::to_fx(a->opt)->tta == 8);
+    }
     CHECK(parse({"in", "w", "out", "scales=0.8,1.0"}).error().code == Errc::unsupported);
     CHECK(parse({"in", "w", "out", "bogus=1"}).error().code == Errc::invalid_argument);
     CHECK(parse({"in", "w", "out", "precision=int4"}).error().code == Errc::invalid_argument);
