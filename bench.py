@@ -37,9 +37,9 @@ FEATURES = (32, 64, 128, 256, 320)
 WEIGHT_SEED, VOLUME_SEED, CALIB_SEED0 = 1, 2, 1000
 # DRAM traffic of the 22 conv launches of one fp8 forward, per 128^3 tile (dram__bytes_read.sum +
 # dram__bytes_write.sum from an ncu launch list of `bench.py --size 256 --steps 1 --warmup 3`:
-# 4.565 GB read + 5.806 GB written per forward of 8 tiles). ncu cannot run inside the timed bench,
+# 4.563 GB read + 5.933 GB written per forward of 8 tiles). ncu cannot run inside the timed bench,
 # so the captured figure is carried here and re-captured when the conv kernel changes.
-CONV_DRAM_BYTES_PER_TILE = (4.565e9 + 5.806e9) / 8
+CONV_DRAM_BYTES_PER_TILE = (4.563e9 + 5.933e9) / 8
 
 
 def env_int(name, default):
