@@ -234,12 +234,15 @@ __device__ __forceinline__ void store_dest(const NormDest& d, int b, int gout, i
 // Block = (plane chunk, z, batch x channel group); thread = kNormVox interior voxels of one z
 // plane x CPT channels (one 16-channel e4m3 cell, or one or two 8-channel f16 cells). The cells
 // of all kNormVox voxels are loaded before any is used, for memory-level parallelism.
+// E4 (16 channels, one plain e4m3 destination, no second destination): the common case, with
+// the store reduced to one 16-byte e4m3 cell and registers for three CTAs per SM.
 constexpr int kNormThreads = 256, kNormVox = 4;
-template <int CPT>
-__global__ void __launch_bounds__(kNormThreads, 2) norm_act_kernel(const uint8_t* __restrict__ pre, int64_t pbs,
-                                                                int64_t pgs, GridGeom g, FastDiv fw, int C,
-                                                                const float* __restrict__ ss, float slope,
-                                                                NormDest d0, NormDest d1, unsigned* amax) {
+template <int CPT, bool E4>
+__global__ void __launch_bounds__(kNormThreads, E4 ? 3 : 2) norm_act_kernel(const uint8_t* __restrict__ pre,
+                                                                         int64_t pbs, int64_t pgs, GridGeom g,
+                                                                         FastDiv fw, int C,
+                                                                         const float* __restrict__ ss, float slope,
+                                                                         NormDest d0, NormDest d1, unsigned* amax) {
     constexpr int NC = CPT / 8;  // f16 cells per voxel
     const int ngo = C / CPT;
     const int b = blockIdx.z / ngo, go = blockIdx.z - b * ngo;
@@ -288,8 +291,18 @@ __global__ void __launch_bounds__(kNormThreads, 2) norm_act_kernel(const uint8_t
             }
         }
         const int64_t row = (static_cast<int64_t>(zp) * Hp + yp[k]) * Wp + xp[k];
-        store_dest(d0, b, d0.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
-        store_dest(d1, b, d1.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
+        if constexpr (E4) {
+            const float qs = d0.qscale;
+            uint4 w;
+            w.x = pack_e4m3x4(v[0] * qs, v[1] * qs, v[2] * qs, v[3] * qs);
+            w.y = pack_e4m3x4(v[4] * qs, v[5] * qs, v[6] * qs, v[7] * qs);
+            w.z = pack_e4m3x4(v[8] * qs, v[9] * qs, v[10] * qs, v[11] * qs);
+            w.w = pack_e4m3x4(v[12] * qs, v[13] * qs, v[14] * qs, v[15] * qs);
+            *reinterpret_cast<uint4*>(d0.ptr + b * d0.batch_stride + go * d0.group_stride + row * 16) = w;
+        } else {
+            store_dest(d0, b, d0.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
+            store_dest(d1, b, d1.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
+        }
     }
     if (amax) {
         for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -486,10 +499,13 @@ cudaError_t launch_norm_act(const uint8_t* pre, int64_t pbs, int64_t pgs, GridGe
     const dim3 grid((HW + kNormThreads * kNormVox - 1) / (kNormThreads * kNormVox), g.D, B * (C / cpt));
     const FastDiv fw = make_fastdiv(static_cast<uint32_t>(g.W));
     count_launch();
-    if (cpt == 16)
-        norm_act_kernel<16><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+    const bool e4 = cpt == 16 && d0.ptr && d0.dtype == kOpE4M3 && !d0.phase && !d1.ptr;
+    if (e4)
+        norm_act_kernel<16, true><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+    else if (cpt == 16)
+        norm_act_kernel<16, false><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
     else
-        norm_act_kernel<8><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+        norm_act_kernel<8, false><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
     return cudaGetLastError();
 }
 
