@@ -310,6 +310,121 @@ __global__ void __launch_bounds__(kNormThreads, E4 ? 3 : 2) norm_act_kernel(cons
     }
 }
 
+// One thread = one interior voxel x 16 channels (two f16 cells of every tensor).
+__global__ void __launch_bounds__(kEwThreads) block_out_kernel(BlockOut p, FastDiv fw) {
+    const int ngo = p.C / 16;
+    const int b = blockIdx.z / ngo, go = blockIdx.z - b * ngo;
+    const int zp = blockIdx.y + 1;
+    const uint32_t HW = static_cast<uint32_t>(p.g.H) * p.g.W;
+    const uint32_t i = blockIdx.x * kEwThreads + threadIdx.x;
+    __shared__ float s_ss[16][2], s_rs[16][2], s_cg[16];
+    if (threadIdx.x < 16) {
+        const int c = go * 16 + threadIdx.x;
+        const float2 t = __ldg(reinterpret_cast<const float2*>(p.ss) + static_cast<int64_t>(b) * p.C + c);
+        s_ss[threadIdx.x][0] = t.x;
+        s_ss[threadIdx.x][1] = t.y;
+        const float2 r = p.res_ss ? __ldg(reinterpret_cast<const float2*>(p.res_ss) + static_cast<int64_t>(b) * p.C + c)
+                                  : make_float2(1.f, 0.f);
+        s_rs[threadIdx.x][0] = r.x;
+        s_rs[threadIdx.x][1] = r.y;
+        s_cg[threadIdx.x] = p.cgate ? __ldg(p.cgate + c) : 1.f;
+    }
+    __syncthreads();
+    if (i >= HW) return;
+    const uint32_t y = fdiv(i, fw);
+    const int yp = static_cast<int>(y) + 1, xp = static_cast<int>(i - y * fw.d) + 1;
+    const int Hp = p.g.H + 2, Wp = p.g.W + 2;
+    const int64_t row = (static_cast<int64_t>(zp) * Hp + yp) * Wp + xp;
+    const float sg = p.sgate ? __ldg(p.sgate + ((static_cast<int64_t>(b) * p.g.D + (zp - 1)) * p.g.H + y) * p.g.W +
+                                     (xp - 1))
+                             : 0.f;
+    float v[16];
+    float mx = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int gi = go * 2 + h;
+        float o[8], r[8];
+        unpack_cell16(__ldcs(reinterpret_cast<const uint4*>(p.pre + b * p.pre_bs + gi * p.pre_gs + row * 16)), kOpF16,
+                      o);
+        unpack_cell16(__ldcs(reinterpret_cast<const uint4*>(p.res + b * p.res_bs + gi * p.res_gs + row * 16)), kOpF16,
+                      r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int c = h * 8 + j;
+            const float out = fmaf(o[j], s_ss[c][0], s_ss[c][1]);
+            const float res = fmaf(r[j], s_rs[c][0], s_rs[c][1]);
+            float t = fmaf(out, s_cg[c] + sg, res);
+            t = t >= 0.f ? t : t * p.slope;
+            v[c] = t;
+            mx = fmaxf(mx, fabsf(t));
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+        store_dest(p.d[k], b, p.d[k].dtype == kOpE4M3 ? go : go * 2, row, zp, yp, xp, v, 16);
+    if (p.amax) {
+        for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if ((threadIdx.x & 31) == 0) atomicMax(p.amax, __float_as_uint(mx));
+    }
+}
+
+// One thread = one interior voxel: a dot product over all C channels of the normalised tensor.
+__global__ void __launch_bounds__(kEwThreads) sse_gate_kernel(const uint8_t* __restrict__ pre, int64_t pbs,
+                                                               int64_t pgs, const float* __restrict__ ss,
+                                                               const float* __restrict__ w, float bias, GridGeom g,
+                                                               int C, FastDiv fw, float* __restrict__ sgate) {
+    const int b = blockIdx.z, z = blockIdx.y;
+    extern __shared__ float s_coef[];  // [C][2]: w * scale, w * shift
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        const float2 t = __ldg(reinterpret_cast<const float2*>(ss) + static_cast<int64_t>(b) * C + c);
+        s_coef[2 * c] = w[c] * t.x;
+        s_coef[2 * c + 1] = w[c] * t.y;
+    }
+    __syncthreads();
+    const uint32_t HW = static_cast<uint32_t>(g.H) * g.W;
+    const uint32_t i = blockIdx.x * kEwThreads + threadIdx.x;
+    if (i >= HW) return;
+    const uint32_t y = fdiv(i, fw);
+    const int x = static_cast<int>(i - y * fw.d);
+    const int64_t row = (static_cast<int64_t>(z + 1) * (g.H + 2) + y + 1) * (g.W + 2) + x + 1;
+    float acc = bias;
+    for (int gi = 0; gi < C / 8; ++gi) {
+        float f[8];
+        unpack_cell16(__ldg(reinterpret_cast<const uint4*>(pre + b * pbs + gi * pgs + row * 16)), kOpF16, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(f[j], s_coef[2 * (gi * 8 + j)], acc + s_coef[2 * (gi * 8 + j) + 1]);
+    }
+    sgate[((static_cast<int64_t>(b) * g.D + z) * g.H + y) * g.W + x] = 1.f / (1.f + expf(-acc));
+}
+
+// One thread = one output voxel x one 8-channel f16 group.
+__global__ void __launch_bounds__(kEwThreads) avgpool2_f16_kernel(const uint8_t* __restrict__ src, int64_t sbs,
+                                                                   int64_t sgs, GridGeom gin, uint8_t* dst,
+                                                                   int64_t dbs, int64_t dgs, int groups,
+                                                                   FastDiv fw) {
+    const int bg = blockIdx.z, b = bg / groups, gi = bg - b * groups, z = blockIdx.y;
+    const int Ho = gin.H / 2, Wo = gin.W / 2;
+    const uint32_t i = blockIdx.x * kEwThreads + threadIdx.x;
+    if (i >= static_cast<uint32_t>(Ho) * Wo) return;
+    const uint32_t y = fdiv(i, fw);
+    const int x = static_cast<int>(i - y * fw.d);
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const uint8_t* sb = src + b * sbs + gi * sgs;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int zz = 2 * z + (k >> 2), yy = 2 * static_cast<int>(y) + ((k >> 1) & 1), xx = 2 * x + (k & 1);
+        const int64_t row = (static_cast<int64_t>(zz + 1) * (gin.H + 2) + yy + 1) * (gin.W + 2) + xx + 1;
+        float f[8];
+        unpack_cell16(__ldg(reinterpret_cast<const uint4*>(sb + row * 16)), kOpF16, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] += f[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] *= 0.125f;
+    const int64_t orow = (static_cast<int64_t>(z + 1) * (Ho + 2) + y + 1) * (Wo + 2) + x + 1;
+    *reinterpret_cast<uint4*>(dst + b * dbs + gi * dgs + orow * 16) = pack_cell16(a, kOpF16);
+}
+
 __constant__ float c_head_w[2 * 64];
 __constant__ float c_head_b[2];
 
@@ -506,6 +621,35 @@ cudaError_t launch_norm_act(const uint8_t* pre, int64_t pbs, int64_t pgs, GridGe
         norm_act_kernel<16, false><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
     else
         norm_act_kernel<8, false><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_block_out(const BlockOut& p, cudaStream_t s) {
+    if (p.C % 16 || !p.pre || !p.ss || !p.res || p.g.D > 65535 || p.B * (p.C / 16) > 65535) return cudaErrorInvalidValue;
+    const uint32_t HW = static_cast<uint32_t>(p.g.H) * p.g.W;
+    count_launch();
+    block_out_kernel<<<dim3((HW + kEwThreads - 1) / kEwThreads, p.g.D, p.B * (p.C / 16)), kEwThreads, 0, s>>>(
+        p, make_fastdiv(static_cast<uint32_t>(p.g.W)));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sse_gate(const uint8_t* pre, int64_t pre_bs, int64_t pre_gs, const float* ss, const float* w,
+                            float bias, GridGeom g, int C, int B, float* sgate, cudaStream_t s) {
+    if (C % 8 || C > 4096 || g.D > 65535 || B > 65535) return cudaErrorInvalidValue;
+    const uint32_t HW = static_cast<uint32_t>(g.H) * g.W;
+    count_launch();
+    sse_gate_kernel<<<dim3((HW + kEwThreads - 1) / kEwThreads, g.D, B), kEwThreads, sizeof(float) * 2 * C, s>>>(
+        pre, pre_bs, pre_gs, ss, w, bias, g, C, make_fastdiv(static_cast<uint32_t>(g.W)), sgate);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_avgpool2_f16(const uint8_t* src, int64_t src_bs, int64_t src_gs, GridGeom gin, uint8_t* dst,
+                                int64_t dst_bs, int64_t dst_gs, int groups, int B, cudaStream_t s) {
+    if (gin.D % 2 || gin.H % 2 || gin.W % 2 || B * groups > 65535) return cudaErrorInvalidValue;
+    const uint32_t HW = static_cast<uint32_t>(gin.H / 2) * (gin.W / 2);
+    count_launch();
+    avgpool2_f16_kernel<<<dim3((HW + kEwThreads - 1) / kEwThreads, gin.D / 2, B * groups), kEwThreads, 0, s>>>(
+        src, src_bs, src_gs, gin, dst, dst_bs, dst_gs, groups, make_fastdiv(static_cast<uint32_t>(gin.W / 2)));
     return cudaGetLastError();
 }
 

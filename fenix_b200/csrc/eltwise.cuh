@@ -80,6 +80,40 @@ cudaError_t launch_norm_act(const uint8_t* pre, int64_t pre_batch_stride, int64_
                             int C, int B, const float* ss, float slope, NormDest d0, NormDest d1, unsigned* amax,
                             cudaStream_t s);
 
+// ---- residual encoder blocks (src/ml/nets/resenc_unet.hpp:103-135) ---------------------------
+// Output of one BasicBlockD: y = leaky(out * (cgate[c] + sgate[v]) + res), out = the second conv's
+// pre-norm x * ss[c].x + ss[c].y (InstanceNorm, no activation). Without scSE, cgate = 1 and
+// sgate = 0 (pass null for both). res is the skip path: InstanceNorm of a projection's pre-norm
+// output (res_ss non-null) or an f16 tensor (identity or average-pooled input) taken as is. All
+// tensors are f16 padded group planes over the block's output grid; y goes to up to three
+// destinations in their operand types. C % 16 == 0.
+struct BlockOut {
+    const uint8_t* pre;
+    int64_t pre_bs, pre_gs;
+    const float* ss;       // [B][C][2]
+    const float* cgate;    // [C] or null
+    const float* sgate;    // [B][D][H][W] f32 or null
+    const uint8_t* res;
+    int64_t res_bs, res_gs;
+    const float* res_ss;   // [B][C][2] or null
+    float slope;
+    NormDest d[3];
+    unsigned* amax;        // max |y| (float bits) or null
+    GridGeom g;
+    int32_t C, B;
+};
+cudaError_t launch_block_out(const BlockOut& p, cudaStream_t s);
+
+// sgate[b][v] = sigmoid(sum_c w[c] * (pre[c] * ss[c].x + ss[c].y) + bias): the spatial squeeze-
+// excitation gate (sSE conv 1x1 C -> 1) of the normalised second conv of a block.
+cudaError_t launch_sse_gate(const uint8_t* pre, int64_t pre_bs, int64_t pre_gs, const float* ss, const float* w,
+                            float bias, GridGeom g, int C, int B, float* sgate, cudaStream_t s);
+
+// dst = AvgPool3d(2, stride 2) of an f16 padded group-plane tensor over grid gin into grid
+// gout = gin / 2 (f16, same channel groups; the zero border of dst is left untouched).
+cudaError_t launch_avgpool2_f16(const uint8_t* src, int64_t src_bs, int64_t src_gs, GridGeom gin, uint8_t* dst,
+                                int64_t dst_bs, int64_t dst_gs, int groups, int B, cudaStream_t s);
+
 // Last decoder layer: normalise + LeakyReLU, 1x1x1 head (ncls <= 2), softmax channel `channel`
 // (or sigmoid of channel 0), NaN -> 0 / +inf -> 1, then Gaussian-blend into the volume
 // accumulator at each tile's origin (acc may be null) and/or store the tile probability

@@ -74,6 +74,18 @@ Status Net::parse(const WeightMap& wm) {
         auto it = wm.find(n);
         return it == wm.end() ? nullptr : &it->second;
     };
+    // residual-encoder checkpoints: {encoder|shared_encoder}.stem + stages.{s}.blocks.{b}
+    if (get("encoder.stem.convs.0.conv.weight")) return parse_resenc(wm, "encoder", "decoder");
+    if (get("shared_encoder.stem.convs.0.conv.weight")) {
+        // task_decoders.<task>: the one task holding seg_layers
+        for (const auto& kv : wm) {
+            const std::string& n = kv.first;
+            const std::string pre = "task_decoders.";
+            const size_t k = n.find(".seg_layers.");
+            if (n.rfind(pre, 0) == 0 && k != std::string::npos) return parse_resenc(wm, "shared_encoder", n.substr(0, k));
+        }
+        return fail(kUnsupported, "fxweights: residual encoder without task_decoders.<task>.seg_layers");
+    }
     // encoder.stages.{s}.convs.{i}.conv.weight
     S_ = 0;
     while (get("encoder.stages." + std::to_string(S_) + ".convs.0.conv.weight")) ++S_;
@@ -154,6 +166,162 @@ Status Net::parse(const WeightMap& wm) {
     return ok();
 }
 
+// Residual-encoder UNet (nets::ResEncUNet, src/ml/nets/resenc_unet.hpp:159-318): stem ConvStack
+// (1 conv), stages of BasicBlockD (conv1 with the stage's stride, conv2 without activation,
+// optional scSE, skip = [AvgPool(2)] + [1x1 conv + norm], add, LeakyReLU), and the plain decoder
+// (transpconvs, one ConvStack per stage, seg_layers) under `dec`.
+Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std::string& dec) {
+    auto get = [&](const std::string& n) -> const HostTensor* {
+        auto it = wm.find(n);
+        return it == wm.end() ? nullptr : &it->second;
+    };
+    auto conv_layer = [&](const std::string& pre, Layer& L, int k) -> Status {
+        const HostTensor* w = get(pre + ".conv.weight");
+        const HostTensor* g = get(pre + ".norm.weight");
+        const HostTensor* b = get(pre + ".norm.bias");
+        if (!w || !g || !b) return fail(kDecode, "fxweights: missing " + pre + ".{conv.weight,norm.weight,norm.bias}");
+        if (w->shape.size() != 5 || w->shape[2] != k || w->shape[3] != k || w->shape[4] != k)
+            return fail(kUnsupported, "fxweights: " + pre + " must be a " + std::to_string(k) + "^3 conv");
+        L.Cout = static_cast<int>(w->shape[0]);
+        L.Cin = static_cast<int>(w->shape[1]);
+        L.w = w->data;
+        L.gamma = g->data;
+        L.beta = b->data;
+        L.name = pre;
+        return ok();
+    };
+    resenc_ = true;
+    enc_.clear();
+    blocks_.clear();
+    F_.clear();
+    Layer stem;
+    Status st = conv_layer(enc + ".stem.convs.0", stem, 3);
+    if (!st.ok()) return st;
+    if (stem.Cin != 1) return fail(kUnsupported, "net: the stem must take 1 input channel");
+    stem.kind = Layer::kFirst;
+    stem.stride = 1;
+    stem.lin = stem.lout = 0;
+    enc_.push_back(stem);
+    S_ = 0;
+    while (get(enc + ".stages." + std::to_string(S_) + ".blocks.0.conv1.conv.weight")) ++S_;
+    if (S_ < 2) return fail(kDecode, "fxweights: expected >= 2 residual stages");
+    if (S_ > 16) return fail(kUnsupported, "net: more than 16 stages");
+    int prev = stem.Cout;
+    int slot = 5 * S_;
+    for (int s = 0; s < S_; ++s) {
+        for (int b = 0;; ++b) {
+            const std::string pre = enc + ".stages." + std::to_string(s) + ".blocks." + std::to_string(b);
+            if (!get(pre + ".conv1.conv.weight")) {
+                if (b == 0) return fail(kDecode, "fxweights: empty stage " + std::to_string(s));
+                break;
+            }
+            ResBlock K;
+            K.stage = s;
+            K.stride = (b == 0 && s > 0) ? 2 : 1;
+            Layer c1, c2;
+            if ((st = conv_layer(pre + ".conv1", c1, 3)).code || (st = conv_layer(pre + ".conv2", c2, 3)).code) return st;
+            if (c1.Cin != (b == 0 ? prev : c1.Cout) || c2.Cin != c1.Cout || c2.Cout != c1.Cout)
+                return fail(kDecode, "fxweights: channel mismatch at " + pre);
+            c1.kind = c2.kind = Layer::kConv;
+            c1.stride = K.stride;
+            c2.stride = 1;
+            c1.lin = K.stride == 2 ? s - 1 : s;
+            c1.lout = c2.lin = c2.lout = s;
+            K.c1 = static_cast<int>(enc_.size());
+            enc_.push_back(c1);
+            K.c2 = static_cast<int>(enc_.size());
+            enc_.push_back(c2);
+            const std::string pj = pre + ".skip." + std::to_string(K.stride == 2 ? 1 : 0);
+            if (c1.Cin != c1.Cout) {
+                Layer pl;
+                if ((st = conv_layer(pj, pl, 1)).code) return st;
+                pl.kind = Layer::kProj;
+                pl.stride = K.stride;
+                pl.lin = c1.lin;
+                pl.lout = s;
+                K.proj = static_cast<int>(enc_.size());
+                enc_.push_back(pl);
+            } else {
+                K.avgpool = K.stride == 2;
+            }
+            const std::string se = pre + ".squeeze_excitation.";
+            if (get(se + "sSE.conv.weight")) {
+                const HostTensor *f1w = get(se + "cSE.fc1.weight"), *f1b = get(se + "cSE.fc1.bias"),
+                                 *f2w = get(se + "cSE.fc2.weight"), *f2b = get(se + "cSE.fc2.bias"),
+                                 *sw = get(se + "sSE.conv.weight"), *sb = get(se + "sSE.conv.bias");
+                const int C = c2.Cout;
+                if (!f1w || !f1b || !f2w || !f2b || !sb || f1w->shape.size() != 5 || f1w->shape[1] != C ||
+                    f2w->shape[0] != C || sw->shape[1] != C)
+                    return fail(kDecode, "fxweights: malformed " + se + "*");
+                const int rd = static_cast<int>(f1w->shape[0]);
+                K.se = true;
+                // GAP of IN(conv2) (no activation) is the norm's bias: the cSE gate is a constant
+                std::vector<float> hid(rd);
+                for (int r = 0; r < rd; ++r) {
+                    double a = f1b->data[r];
+                    for (int c = 0; c < C; ++c) a += static_cast<double>(f1w->data[static_cast<size_t>(r) * C + c]) * c2.beta[c];
+                    hid[r] = a > 0.0 ? static_cast<float>(a) : 0.f;
+                }
+                K.cgate.resize(C);
+                for (int c = 0; c < C; ++c) {
+                    double a = f2b->data[c];
+                    for (int r = 0; r < rd; ++r) a += static_cast<double>(f2w->data[static_cast<size_t>(c) * rd + r]) * hid[r];
+                    K.cgate[c] = static_cast<float>(1.0 / (1.0 + std::exp(-a)));
+                }
+                K.sse_w.assign(sw->data.begin(), sw->data.begin() + C);
+                K.sse_b = sb->data[0];
+            }
+            K.slot_x = slot++;
+            K.slot_h = slot++;
+            blocks_.push_back(std::move(K));
+            prev = c1.Cout;
+        }
+        F_.push_back(prev);
+    }
+    nslots_ = slot + 1;  // + the last stage's output (the first transposed conv's input)
+    // decoder: transpconvs, one or more convs per stage, seg_layers (as the plain decoder)
+    nconv_ = 0;
+    while (get(dec + ".stages.0.convs." + std::to_string(nconv_) + ".conv.weight")) ++nconv_;
+    if (nconv_ < 1) return fail(kDecode, "fxweights: no convs in " + dec + ".stages.0");
+    up_.assign(S_ - 1, Layer{});
+    dec_.assign(static_cast<size_t>(S_ - 1) * nconv_, Layer{});
+    for (int t = 0; t < S_ - 1; ++t) {
+        const int lvl = S_ - 2 - t;
+        const std::string tp = dec + ".transpconvs." + std::to_string(t);
+        const HostTensor* w = get(tp + ".weight");
+        const HostTensor* b = get(tp + ".bias");
+        if (!w || !b) return fail(kDecode, "fxweights: missing " + tp + ".{weight,bias}");
+        Layer& U = up_[lvl];
+        U.kind = Layer::kUp;
+        U.name = tp;
+        U.Cin = static_cast<int>(w->shape[0]);
+        U.Cout = static_cast<int>(w->shape[1]);
+        if (U.Cin != F_[lvl + 1] || U.Cout != F_[lvl]) return fail(kDecode, "fxweights: channel mismatch at " + tp);
+        U.w = w->data;
+        U.b = b->data;
+        U.stride = 2;
+        U.lin = lvl + 1;
+        U.lout = lvl;
+        for (int i = 0; i < nconv_; ++i) {
+            Layer& L = dec_[lvl * nconv_ + i];
+            if ((st = conv_layer(dec + ".stages." + std::to_string(t) + ".convs." + std::to_string(i), L, 3)).code)
+                return st;
+            if (L.Cout != F_[lvl] || L.Cin != (i == 0 ? 2 * F_[lvl] : F_[lvl]))
+                return fail(kDecode, "fxweights: channel mismatch at " + L.name);
+            L.lin = L.lout = lvl;
+        }
+    }
+    const std::string sl = dec + ".seg_layers." + std::to_string(S_ - 2);
+    const HostTensor* hw = get(sl + ".weight");
+    const HostTensor* hb = get(sl + ".bias");
+    if (!hw || !hb) return fail(kDecode, "fxweights: missing " + sl + ".{weight,bias}");
+    ncls_ = static_cast<int>(hw->shape[0]);
+    if (hw->shape[1] != F_[0] || ncls_ < 1 || ncls_ > 2) return fail(kUnsupported, "net: head must map F0 -> 1 or 2 classes");
+    head_w_ = hw->data;
+    head_b_ = hb->data;
+    return ok();
+}
+
 // ---- layer program construction -------------------------------------------------------------
 // The x-tap fold (A collector shared by the three x taps) is off unless FENIX_B200_CONV_FOLD=1:
 // its MMAs run 1.6x faster, but its epilogue (three accumulators and a cross-lane row shift)
@@ -185,7 +353,7 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
                 L.wscale[co] = std::max(m, 1e-8f) / kE4M3Max;
             }
         } else {
-            const size_t per = static_cast<size_t>(L.Cin) * 27;
+            const size_t per = static_cast<size_t>(L.Cin) * (L.kind == Layer::kProj ? 1 : 27);
             for (int co = 0; co < L.Cout; ++co) {
                 float m = 0.f;
                 for (size_t k = 0; k < per; ++k) m = std::max(m, std::fabs(L.w[co * per + k]));
@@ -250,6 +418,41 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
             for (int co = 0; co < L.Cout; ++co) colscale[co] = L.in_scale * L.wscale[co];
             // one epilogue factor = the largest channel's, so stored f16 values are never larger
             // than that channel's own range; the per-channel remainder (<= 1) goes to the stats
+            dp.acc_scale = *std::max_element(colscale.begin(), colscale.end());
+            ratio.resize(L.Cout);
+            for (int co = 0; co < L.Cout; ++co) ratio[co] = colscale[co] / dp.acc_scale;
+        }
+    } else if (L.kind == Layer::kProj) {
+        // 1x1x1 projection; with stride 2 the AvgPool(2) in front of it makes it a 2x2x2 stride-2
+        // conv with weights / 8: taps (kz, ky, kx) in {1, 2}^3 of the stride-2 tap scheme
+        if (L.Cin % sp.cg) return fail(kUnsupported, L.name + ": input channels must be a multiple of " + std::to_string(sp.cg));
+        sp.G = L.Cin / sp.cg;
+        float wmul = 1.f;
+        if (L.stride == 1) {
+            sp.taps.push_back({0, 0, 0, 0});
+        } else {
+            wmul = 0.125f;
+            const int64_t Wp = gout.W + 2, P2 = static_cast<int64_t>(gout.H + 2) * Wp;
+            for (int kz = 1; kz < 3; ++kz)
+                for (int ky = 1; ky < 3; ++ky)
+                    for (int kx = 1; kx < 3; ++kx) {
+                        const int phi = ((kz & 1) << 2) | ((ky & 1) << 1) | (kx & 1);
+                        const int64_t off = (kz / 2 - 1) * P2 + (ky / 2 - 1) * Wp + (kx / 2 - 1);
+                        sp.taps.push_back({phi, off, 0, phi});
+                    }
+        }
+        const Layer* Lp = &L;
+        const bool f8 = fp8;
+        sp.wval = [Lp, f8, wmul](int n, int ci, int) {
+            if (ci >= Lp->Cin) return 0.f;
+            const float v = Lp->w[static_cast<size_t>(n) * Lp->Cin + ci] * wmul;
+            return f8 ? v / (Lp->wscale[n] * wmul) : v;
+        };
+        sp.N_total = L.Cout;
+        dp.rowspace = gout;
+        if (fp8) {
+            colscale.resize(L.Cout);
+            for (int co = 0; co < L.Cout; ++co) colscale[co] = L.in_scale * L.wscale[co] * wmul;
             dp.acc_scale = *std::max_element(colscale.begin(), colscale.end());
             ratio.resize(L.Cout);
             for (int co = 0; co < L.Cout; ++co) ratio[co] = colscale[co] / dp.acc_scale;
@@ -357,8 +560,42 @@ Status Net::alloc() {
             cudaMemset(ph_[s], 0, pbytes);
         }
     }
+    if (resenc_) {
+        h_.assign(S_, nullptr);
+        xf_.assign(S_, nullptr);
+        pnx_.assign(S_, nullptr);
+        res_.assign(S_, nullptr);
+        sg_.assign(S_, nullptr);
+        for (int s = 0; s < S_; ++s) {
+            const ActGeom g = level(s);
+            const size_t bytes = static_cast<size_t>(Bmax_) * (F_[s] / 8) * g.gs();
+            bool proj = false, pool = false, se = false;
+            for (const ResBlock& K : blocks_)
+                if (K.stage == s) {
+                    proj |= K.proj >= 0;
+                    pool |= K.avgpool;
+                    se |= K.se;
+                }
+            for (uint8_t** p : {&h_[s], &xf_[s]}) {
+                *p = static_cast<uint8_t*>(dalloc(bytes));
+                if (!*p) return fail(kInternal, "cudaMalloc: residual buffers");
+                cudaMemset(*p, 0, bytes);
+            }
+            if (proj && !(pnx_[s] = static_cast<uint8_t*>(dalloc(bytes)))) return fail(kInternal, "cudaMalloc: projection");
+            if (pool && !(res_[s] = static_cast<uint8_t*>(dalloc(bytes)))) return fail(kInternal, "cudaMalloc: pooled residual");
+            if (se && !(sg_[s] = static_cast<float*>(dalloc(sizeof(float) * Bmax_ * g.D * g.H * g.W))))
+                return fail(kInternal, "cudaMalloc: sSE gate");
+        }
+        for (ResBlock& K : blocks_) {
+            if (!K.se) continue;
+            Status st = upload(K.d_cgate, K.cgate, this, allocs_);
+            if (st.ok()) st = upload(K.d_sse_w, K.sse_w, this, allocs_);
+            if (!st.ok()) return st;
+        }
+    }
+    nslots_ = std::max(nslots_, 5 * S_);
     d_sums_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * 2 * Bmax_));
-    d_amax_ = static_cast<unsigned*>(dalloc(sizeof(unsigned) * 5 * S_));
+    d_amax_ = static_cast<unsigned*>(dalloc(sizeof(unsigned) * nslots_));
     d_status_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t)));
     const int cmax = *std::max_element(F_.begin(), F_.end());
     const size_t ndone = static_cast<size_t>(Bmax_) * ((cmax + 31) / 32);
@@ -407,7 +644,7 @@ Status Net::create(const std::string& path, int patch, int max_batch, int precis
     for (auto* v : {&enc_, &up_, &dec_})
         for (Layer& L : *v)
             if ((st = build_layer(L, t16())).code) return st;
-    amax_.assign(5 * S_, 0.f);
+    amax_.assign(nslots_, 0.f);
     return ok();
 }
 
@@ -420,7 +657,9 @@ Status Net::run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int6
         const ActGeom gi = level(L.lin), go = level(L.lout);
         const double vin = static_cast<double>(gi.D) * gi.H * gi.W, vout = static_cast<double>(go.D) * go.H * go.W;
         // algorithmic FLOPs = 2 x MACs: conv 27 Cin Cout Vout, transposed conv Cin Cout Vout
-        ev.flops = L.kind == Layer::kUp ? 2.0 * L.Cin * L.Cout * 8.0 * vin * nb : 2.0 * 27.0 * L.Cin * L.Cout * vout * nb;
+        // (a strided projection counts its AvgPool as 8 taps of the conv it runs as)
+        const double taps = L.kind == Layer::kProj ? (L.stride == 2 ? 8.0 : 1.0) : 27.0;
+        ev.flops = L.kind == Layer::kUp ? 2.0 * L.Cin * L.Cout * 8.0 * vin * nb : 2.0 * taps * L.Cin * L.Cout * vout * nb;
         ev.optype = q;
         cudaEventCreate(&ev.a);
         cudaEventCreate(&ev.b);
@@ -469,7 +708,7 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     static thread_local fxk::ConvParams p;  // ~22 KB: kept off the stack
     p = fxk::ConvParams{};
     const ActGeom& rs = dp.rowspace;
-    if (L.kind == Layer::kConv && L.stride == 2) {
+    if ((L.kind == Layer::kConv || L.kind == Layer::kProj) && L.stride == 2) {
         const int64_t ps = gout.gs();
         for (int phi = 0; phi < 8; ++phi) p.src[phi] = {in_ptr + phi * ps, in_bs, in_gs, gout.rows()};
     } else {
@@ -604,39 +843,148 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
                            "norm_act");
     };
     const fxk::NormDest none{};
-    // encoder
-    for (int lv = 0; lv < S_; ++lv) {
-        const ActGeom g = level(lv);
-        const int64_t pn_bs = static_cast<int64_t>(F_[lv] / 8) * g.gs();
-        for (int i = 0; i < nconv_; ++i) {
-            Layer& L = enc_[lv * nconv_ + i];
-            const int q = qof(L);
-            const uint8_t* in;
+    // encoder: residual stages (stem + BasicBlockD)
+    if (resenc_) {
+        const Layer& stem = enc_[0];
+        const ActGeom g0l = level(0);
+        const int64_t pn0 = static_cast<int64_t>(F_[0] / 8) * g0l.gs();
+        // f16 copy of a level's block input (identity / pooled residual source)
+        auto f16dest = [&](uint8_t* ptr, int lvl, int C) {
+            fxk::NormDest d{};
+            d.ptr = ptr;
+            d.batch_stride = static_cast<int64_t>(C / 8) * level(lvl).gs();
+            d.group_stride = level(lvl).gs();
+            d.dtype = fxk::kOpF16;
+            d.qscale = 1.f;
+            return d;
+        };
+        if ((st = run_conv(enc_[0], qof(stem), l0_, g0.gs(), g0.gs(), pn_[0], pn0, g0l.gs(), 0, 1.f, nullptr, nb, s)).code)
+            return st;
+        if ((st = norm(enc_[0], dest(act_[0], 0, F_[0], 0, enc_[blocks_[0].c1]), f16dest(xf_[0], 0, F_[0]),
+                       blocks_[0].slot_x))
+                .code)
+            return st;
+        for (size_t k = 0; k < blocks_.size(); ++k) {
+            const ResBlock& K = blocks_[k];
+            const int lv = K.stage;
+            const ActGeom g = level(lv);
+            const int64_t pbs = static_cast<int64_t>(F_[lv] / 8) * g.gs();
+            Layer& L1 = enc_[K.c1];
+            Layer& L2 = enc_[K.c2];
+            const int q1 = qof(L1), q2 = qof(L2);
+            // conv1 (and the projection) read the block input: the phase-split copy when strided
+            const uint8_t* in1;
             int64_t ibs, igs;
-            if (L.kind == Layer::kFirst) {
-                in = l0_;
-                ibs = g0.gs();
-                igs = g0.gs();
-            } else if (i == 0) {  // stride 2: phase-split copy of the previous stage's output
-                in = ph_[lv - 1];
+            if (K.stride == 2) {
+                in1 = ph_[lv - 1];
                 igs = 8 * g.gs();
-                ibs = static_cast<int64_t>(F_[lv - 1] / cgof(q)) * igs;
+                ibs = static_cast<int64_t>(L1.Cin / cgof(q1)) * igs;
             } else {
-                in = act_[lv];
-                ibs = bstride(lv, F_[lv], q);
+                in1 = act_[lv];
                 igs = g.gs();
+                ibs = bstride(lv, L1.Cin, q1);
             }
-            if ((st = run_conv(L, q, in, ibs, igs, pn_[lv], pn_bs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
-            if (i < nconv_ - 1) {
-                if ((st = norm(L, dest(act_[lv], lv, F_[lv], 0, enc_[lv * nconv_ + i + 1]), none, lv)).code) return st;
-            } else if (lv < S_ - 1) {
-                const Layer& dcat = dec_[lv * nconv_];
-                if ((st = norm(L, dest(cat_[lv], lv, 2 * F_[lv], F_[lv], dcat), phase_dest(lv, enc_[(lv + 1) * nconv_]),
-                               S_ + lv))
+            if ((st = run_conv(L1, q1, in1, ibs, igs, pn_[lv], pbs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
+            if ((st = norm(L1, dest(h_[lv], lv, F_[lv], 0, L2), none, K.slot_h)).code) return st;
+            if ((st = run_conv(L2, q2, h_[lv], bstride(lv, F_[lv], q2), g.gs(), pn_[lv], pbs, g.gs(), 0, 1.f, nullptr,
+                               nb, s))
+                    .code)
+                return st;
+            if ((st = finalize_in(L2, nb, s)).code) return st;
+            fxk::BlockOut bo{};
+            if (K.proj >= 0) {
+                Layer& Lp = enc_[K.proj];
+                const int qp = qof(Lp);
+                const int64_t pibs = K.stride == 2 ? static_cast<int64_t>(Lp.Cin / cgof(qp)) * igs : bstride(lv, Lp.Cin, qp);
+                if ((st = run_conv(Lp, qp, in1, pibs, igs, pnx_[lv], pbs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
+                if ((st = finalize_in(Lp, nb, s)).code) return st;
+                bo.res = pnx_[lv];
+                bo.res_ss = Lp.d_ss;
+            } else if (K.avgpool) {
+                const ActGeom gi = level(lv - 1);
+                if ((st = cuda_status(fxk::launch_avgpool2_f16(xf_[lv - 1], static_cast<int64_t>(F_[lv - 1] / 8) * gi.gs(),
+                                                               gi.gs(), {gi.D, gi.H, gi.W}, res_[lv], pbs, g.gs(),
+                                                               F_[lv] / 8, nb, s),
+                                      "avgpool"))
                         .code)
                     return st;
+                bo.res = res_[lv];
             } else {
-                if ((st = norm(L, dest(act_[lv], lv, F_[lv], 0, up_[S_ - 2]), none, S_ + lv)).code) return st;
+                bo.res = xf_[lv];
+            }
+            bo.res_bs = pbs;
+            bo.res_gs = g.gs();
+            if (K.se) {
+                if ((st = cuda_status(fxk::launch_sse_gate(pn_[lv], pbs, g.gs(), L2.d_ss, K.d_sse_w, K.sse_b,
+                                                           {g.D, g.H, g.W}, F_[lv], nb, sg_[lv], s),
+                                      "sse_gate"))
+                        .code)
+                    return st;
+                bo.cgate = K.d_cgate;
+                bo.sgate = sg_[lv];
+            }
+            bo.pre = pn_[lv];
+            bo.pre_bs = pbs;
+            bo.pre_gs = g.gs();
+            bo.ss = L2.d_ss;
+            bo.slope = kSlope;
+            bo.g = {g.D, g.H, g.W};
+            bo.C = F_[lv];
+            bo.B = nb;
+            const bool last_in_stage = k + 1 == blocks_.size() || blocks_[k + 1].stage != lv;
+            int slot;
+            if (!last_in_stage) {  // next block of the stage: its conv1 operands + the f16 residual copy
+                bo.d[0] = dest(act_[lv], lv, F_[lv], 0, enc_[blocks_[k + 1].c1]);
+                bo.d[1] = f16dest(xf_[lv], lv, F_[lv]);
+                slot = blocks_[k + 1].slot_x;
+            } else if (lv < S_ - 1) {  // next stage (phase-split), decoder skip half, f16 copy
+                const ResBlock& Kn = blocks_[k + 1];
+                bo.d[0] = phase_dest(lv, enc_[Kn.c1]);
+                bo.d[1] = dest(cat_[lv], lv, 2 * F_[lv], F_[lv], dec_[lv * nconv_]);
+                if (Kn.avgpool) bo.d[2] = f16dest(xf_[lv], lv, F_[lv]);
+                slot = Kn.slot_x;
+            } else {  // the bottleneck: input of the first transposed conv
+                bo.d[0] = dest(act_[lv], lv, F_[lv], 0, up_[S_ - 2]);
+                slot = nslots_ - 1;
+            }
+            bo.amax = amax_slot(slot);
+            if ((st = cuda_status(fxk::launch_block_out(bo, s), "block_out")).code) return st;
+        }
+    } else {
+        // encoder
+        for (int lv = 0; lv < S_; ++lv) {
+            const ActGeom g = level(lv);
+            const int64_t pn_bs = static_cast<int64_t>(F_[lv] / 8) * g.gs();
+            for (int i = 0; i < nconv_; ++i) {
+                Layer& L = enc_[lv * nconv_ + i];
+                const int q = qof(L);
+                const uint8_t* in;
+                int64_t ibs, igs;
+                if (L.kind == Layer::kFirst) {
+                    in = l0_;
+                    ibs = g0.gs();
+                    igs = g0.gs();
+                } else if (i == 0) {  // stride 2: phase-split copy of the previous stage's output
+                    in = ph_[lv - 1];
+                    igs = 8 * g.gs();
+                    ibs = static_cast<int64_t>(F_[lv - 1] / cgof(q)) * igs;
+                } else {
+                    in = act_[lv];
+                    ibs = bstride(lv, F_[lv], q);
+                    igs = g.gs();
+                }
+                if ((st = run_conv(L, q, in, ibs, igs, pn_[lv], pn_bs, g.gs(), 0, 1.f, nullptr, nb, s)).code) return st;
+                if (i < nconv_ - 1) {
+                    if ((st = norm(L, dest(act_[lv], lv, F_[lv], 0, enc_[lv * nconv_ + i + 1]), none, lv)).code) return st;
+                } else if (lv < S_ - 1) {
+                    const Layer& dcat = dec_[lv * nconv_];
+                    if ((st = norm(L, dest(cat_[lv], lv, 2 * F_[lv], F_[lv], dcat), phase_dest(lv, enc_[(lv + 1) * nconv_]),
+                                   S_ + lv))
+                            .code)
+                        return st;
+                } else {
+                    if ((st = norm(L, dest(act_[lv], lv, F_[lv], 0, up_[S_ - 2]), none, S_ + lv)).code) return st;
+                }
             }
         }
     }
@@ -700,6 +1048,25 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
 // ---- calibration ------------------------------------------------------------------------------
 Status Net::set_scales_from_amax() {
     auto sc = [&](int k) { return std::max(amax_[k], 1e-8f) / kE4M3Max; };
+    if (resenc_) {
+        // block b's input (conv1, projection) and conv2 input; a stage's last block output is the
+        // next stage's first block input and the decoder's skip half at that level
+        int first_of_stage[64] = {};
+        for (int k = static_cast<int>(blocks_.size()) - 1; k >= 0; --k) first_of_stage[blocks_[k].stage] = k;
+        for (const ResBlock& K : blocks_) {
+            enc_[K.c1].in_scale = sc(K.slot_x);
+            enc_[K.c2].in_scale = sc(K.slot_h);
+            if (K.proj >= 0) enc_[K.proj].in_scale = sc(K.slot_x);
+        }
+        const int last = nslots_ - 1;  // the last stage's output
+        for (int lvl = 0; lvl < S_ - 1; ++lvl) {
+            const int skip = blocks_[first_of_stage[lvl + 1]].slot_x;
+            dec_[lvl * nconv_].in_scale = std::max(sc(skip), sc(2 * S_ + lvl));
+            for (int i = 1; i < nconv_; ++i) dec_[lvl * nconv_ + i].in_scale = sc(3 * S_ + lvl);
+            up_[lvl].in_scale = lvl == S_ - 2 ? sc(last) : sc(4 * S_ + lvl + 1);
+        }
+        return ok();
+    }
     for (int s = 0; s < S_; ++s) {
         for (int i = 1; i < nconv_; ++i) enc_[s * nconv_ + i].in_scale = sc(s);  // nA
         if (s + 1 < S_) enc_[(s + 1) * nconv_].in_scale = sc(S_ + s);           // skip -> phase copy
@@ -725,7 +1092,7 @@ Status Net::calibrate(const uint8_t* host_patches, int n) {
     fxk::TileOrigin* d_org = nullptr;
     Status st = upload(d_org, org, this, allocs_);
     if (!st.ok()) return st;
-    cudaMemsetAsync(d_amax_, 0, sizeof(unsigned) * 5 * S_, stream_);
+    cudaMemsetAsync(d_amax_, 0, sizeof(unsigned) * nslots_, stream_);
     for (int i0 = 0; i0 < n; i0 += Bmax_) {
         const int nb = std::min(Bmax_, n - i0);
         if ((st = cuda_status(cudaMemcpyAsync(d_vol, host_patches + pv * i0, pv * nb, cudaMemcpyHostToDevice, stream_),
@@ -737,7 +1104,7 @@ Status Net::calibrate(const uint8_t* host_patches, int n) {
                 .code)
             return st;
     }
-    std::vector<unsigned> bits(5 * S_);
+    std::vector<unsigned> bits(nslots_);
     if ((st = cuda_status(cudaMemcpyAsync(bits.data(), d_amax_, sizeof(unsigned) * bits.size(), cudaMemcpyDeviceToHost,
                                           stream_),
                           "D2H amax"))

@@ -61,7 +61,9 @@ struct DevProgram {
 };
 
 struct Layer {
-    enum Kind { kConv, kFirst, kUp } kind = kConv;
+    // kProj: a residual block's skip projection, 1x1x1 (stride 1) or AvgPool(2) + 1x1x1 as one
+    // stride-2 program of 8 taps over the phase-split input with weights / 8
+    enum Kind { kConv, kFirst, kUp, kProj } kind = kConv;
     std::string name;
     int Cin = 0, Cout = 0, stride = 1;
     int lin = 0, lout = 0;            // resolution levels of input and output
@@ -91,6 +93,23 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
 Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
                     uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax,
                     int nb, int sm_count, uint32_t* d_status, cudaStream_t s, bool per_column = false);
+
+// One BasicBlockD of a residual encoder (src/ml/nets/resenc_unet.hpp:103-135): indices into the
+// net's encoder layers, the skip path and the scSE parameters.
+struct ResBlock {
+    int stage = 0;
+    int c1 = -1, c2 = -1, proj = -1;  // conv1 (3x3x3, stride), conv2 (3x3x3), skip projection or -1
+    int stride = 1;
+    bool avgpool = false;             // stride 2 without projection: residual = AvgPool(2)(input)
+    bool se = false;
+    std::vector<float> cgate;         // cSE gate per channel: the block's GAP of IN(conv2) is the
+                                      // norm's bias, so sigmoid(fc2(relu(fc1(beta)))) is a constant
+    std::vector<float> sse_w;         // sSE conv 1x1 C -> 1
+    float sse_b = 0.f;
+    float* d_cgate = nullptr;
+    float* d_sse_w = nullptr;
+    int slot_x = 0, slot_h = 0;       // calibration amax slots of the block input / conv2 input
+};
 
 class Net {
   public:
@@ -149,6 +168,7 @@ class Net {
     bool profile_ = false;
     std::vector<ProfEv> prof_;
     Status parse(const WeightMap& wm);
+    Status parse_resenc(const WeightMap& wm, const std::string& enc, const std::string& dec);
     Status alloc();
     Status build_layer(Layer& L, int q);
     Status run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs, uint8_t* out_ptr,
@@ -165,6 +185,13 @@ class Net {
     std::vector<Layer> enc_;  // S * nconv, stage-major
     std::vector<Layer> up_;   // S-1, index = level
     std::vector<Layer> dec_;  // (S-1) * nconv, index = level * nconv + i
+    // residual encoder (stem + BasicBlockD stages) instead of the plain ConvStack encoder: enc_
+    // holds the stem, then conv1, conv2, [projection] of every block in order
+    bool resenc_ = false;
+    std::vector<ResBlock> blocks_;
+    std::vector<uint8_t*> h_, xf_, pnx_, res_;  // per level: conv2 input, f16 block input, projection pre-norm, pooled residual
+    std::vector<float*> sg_;                    // per level: sSE gate
+    int nslots_ = 0;                            // calibration amax slots
     std::vector<float> head_w_, head_b_;
     float* d_head_w_ = nullptr;
     float* d_head_b_ = nullptr;

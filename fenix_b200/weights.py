@@ -129,3 +129,75 @@ def plain_unet_params(features, nconv: int = 2, ncls: int = 2, seed: int = 0) ->
 def make_plain_unet(path: str | Path, features, nconv: int = 2, ncls: int = 2, seed: int = 0) -> Path:
     write_fxweights(path, plain_unet_params(features, nconv, ncls, seed))
     return Path(path)
+
+
+def se_reduced(channels: int, rd_ratio: float = 1.0 / 16.0, divisor: int = 8) -> int:
+    """The scSE bottleneck width: make_divisible(channels / 16, 8) (timm / nnU-Net)."""
+    v = channels * rd_ratio
+    return max(divisor, int(v + divisor / 2.0) // divisor * divisor)
+
+
+def resenc_unet_params(features, blocks, ncls: int = 2, se: bool = False, plain_naming: bool = True,
+                       task: str = "surface", seed: int = 0) -> dict[str, np.ndarray]:
+    """Seeded random init of the residual-encoder UNet (src/ml/nets/resenc_unet.hpp:55-318) with
+    its checkpoint names: ``{enc}.stem.convs.0.*``, ``{enc}.stages.{s}.blocks.{b}.conv1/conv2.*``,
+    ``...squeeze_excitation.cSE.fc1/fc2`` + ``sSE.conv`` (scSE), ``...skip.{i}.conv/norm`` (the 1x1
+    projection after an optional AvgPool), and the plain decoder with one conv per stage.
+    enc/dec = encoder/decoder (plain naming) or shared_encoder / task_decoders.<task>. Stage 0
+    has stride 1, the others stride 2. Same draws as plain_unet_params."""
+    import torch
+
+    g = torch.Generator().manual_seed(int(seed))
+
+    def kaiming(shape, fan_in):
+        gain = (2.0 / (1 + 0.01 ** 2)) ** 0.5
+        return (torch.randn(*shape, generator=g) * (gain / fan_in ** 0.5)).numpy()
+
+    def small(n, base=0.0):
+        return (base + 0.1 * torch.randn(n, generator=g)).numpy()
+
+    enc, dec = ("encoder", "decoder") if plain_naming else ("shared_encoder", f"task_decoders.{task}")
+    P: dict[str, np.ndarray] = {}
+
+    def cna(pre, cin, cout, k, bias=True):
+        P[pre + ".conv.weight"] = kaiming((cout, cin, k, k, k), cin * k ** 3)
+        if bias:
+            P[pre + ".conv.bias"] = small(cout)
+        P[pre + ".norm.weight"] = small(cout, 1.0)
+        P[pre + ".norm.bias"] = small(cout)
+
+    S = len(features)
+    cna(f"{enc}.stem.convs.0", 1, features[0], 3)
+    prev = features[0]
+    for s in range(S):
+        for b in range(blocks[s]):
+            cin, cout = (prev if b == 0 else features[s]), features[s]
+            stride = (1 if s == 0 else 2) if b == 0 else 1
+            pre = f"{enc}.stages.{s}.blocks.{b}"
+            cna(pre + ".conv1", cin, cout, 3)
+            cna(pre + ".conv2", cout, cout, 3)
+            if se:
+                rd = se_reduced(cout)
+                P[pre + ".squeeze_excitation.cSE.fc1.weight"] = kaiming((rd, cout, 1, 1, 1), cout)
+                P[pre + ".squeeze_excitation.cSE.fc1.bias"] = small(rd)
+                P[pre + ".squeeze_excitation.cSE.fc2.weight"] = kaiming((cout, rd, 1, 1, 1), rd)
+                P[pre + ".squeeze_excitation.cSE.fc2.bias"] = small(cout)
+                P[pre + ".squeeze_excitation.sSE.conv.weight"] = kaiming((1, cout, 1, 1, 1), cout)
+                P[pre + ".squeeze_excitation.sSE.conv.bias"] = small(1)
+            if cin != cout:  # projection; AvgPool (no parameters) takes index 0 when strided
+                cna(pre + f".skip.{1 if stride != 1 else 0}", cin, cout, 1, bias=False)
+        prev = features[s]
+    for t in range(S - 1):
+        below, skipc = features[S - 1 - t], features[S - 2 - t]
+        P[f"{dec}.transpconvs.{t}.weight"] = kaiming((below, skipc, 2, 2, 2), skipc * 8)
+        P[f"{dec}.transpconvs.{t}.bias"] = small(skipc)
+        cna(f"{dec}.stages.{t}.convs.0", 2 * skipc, skipc, 3)
+        P[f"{dec}.seg_layers.{t}.weight"] = kaiming((ncls, skipc, 1, 1, 1), skipc)
+        P[f"{dec}.seg_layers.{t}.bias"] = small(ncls)
+    return P
+
+
+def make_resenc_unet(path: str | Path, features, blocks, ncls: int = 2, se: bool = False,
+                     plain_naming: bool = True, seed: int = 0) -> Path:
+    write_fxweights(path, resenc_unet_params(features, blocks, ncls, se, plain_naming, seed=seed))
+    return Path(path)

@@ -77,10 +77,15 @@ const char* fx_last_error(void);
 /* Number of CUDA devices visible (0 when no driver or GPU). */
 int fx_device_count(void);
 
-/* Build a plain 3D UNet from an .fxweights file (FXWT v1, src/ml/weights.hpp:1-10) on device
- * `device`, for tiles of side `patch` and up to `max_batch` tiles per forward. The stage count,
- * features and classes are read from the tensor shapes (encoder.stages.{s}.convs.{i}.conv.*,
- * decoder.transpconvs.{t}.*, decoder.stages.{t}.convs.{i}.*, decoder.seg_layers.{t}.*). */
+/* Build a 3D UNet from an .fxweights file (FXWT v1, src/ml/weights.hpp:1-10) on device `device`,
+ * for tiles of side `patch` and up to `max_batch` tiles per forward. The architecture, stage
+ * count, features and classes are read from the tensor names and shapes:
+ *   plain UNet      — encoder.stages.{s}.convs.{i}.conv.*, decoder.transpconvs.{t}.*,
+ *                     decoder.stages.{t}.convs.{i}.*, decoder.seg_layers.{t}.*
+ *   residual UNet   — nets::ResEncUNet (src/ml/nets/resenc_unet.hpp:159-318):
+ *                     {encoder|shared_encoder}.stem.convs.0.*, ...stages.{s}.blocks.{b}.conv1/conv2/
+ *                     skip.{i}/squeeze_excitation.*, with the decoder under decoder.* or
+ *                     task_decoders.<task>.* (BasicBlockD with AvgPool + 1x1 projection skips, scSE). */
 fx_status fx_net_create(const char* fxweights_path, int patch, int max_batch, fx_precision precision, int device,
                         fx_net** out);
 void fx_net_destroy(fx_net* net);

@@ -98,36 +98,9 @@ struct PlainImpl : nn::Module {
 };
 TORCH_MODULE(Plain);
 
-int main(int argc, char** argv) {
-    if (argc < 10) {
-        std::fprintf(stderr, "usage: ref_infer <w.fxweights> <vol.u8> dz dy dx patch overlap batch <out.f32|-> [threads]\n");
-        return 2;
-    }
-    const std::string wpath = argv[1], vpath = argv[2], opath = argv[9];
-    const Extent3 d{std::atoll(argv[3]), std::atoll(argv[4]), std::atoll(argv[5])};
-    if (argc > 10) torch::set_num_threads(std::atoi(argv[10]));
-    auto wm = ml::load_fxweights(wpath);
-    if (!wm) {
-        std::fprintf(stderr, "load_fxweights: %s\n", wm.error().message.c_str());
-        return 1;
-    }
-    std::vector<int> f;
-    int nconv = 0;
-    for (;;) {
-        auto it = wm->find("encoder.stages." + std::to_string(f.size()) + ".convs.0.conv.weight");
-        if (it == wm->end()) break;
-        f.push_back(static_cast<int>(it->second.size(0)));
-    }
-    while (wm->count("encoder.stages.0.convs." + std::to_string(nconv) + ".conv.weight")) ++nconv;
-    const int ncls = static_cast<int>(wm->at("decoder.seg_layers." + std::to_string(f.size() - 2) + ".weight").size(0));
-    Plain net(f, nconv, ncls);
-    net->eval();
-    std::vector<std::string> missing;
-    ml::load_into(*net, *wm, &missing);
-    if (!missing.empty()) {
-        std::fprintf(stderr, "weights missing %s\n", missing[0].c_str());
-        return 1;
-    }
+// Run the reference's predict_surface_filled with `net` on the volume file and write the result.
+template <class Net>
+int run(Net& net, char** argv, Extent3 d, const std::string& vpath, const std::string& opath) {
     Volume<u8> vol(d);
     {
         std::FILE* fp = std::fopen(vpath.c_str(), "rb");
@@ -171,4 +144,68 @@ int main(int argc, char** argv) {
                                          ml::tile_starts(d.x, opt.patch, opt.overlap).size());
     std::printf("{\"seconds\": %.6f, \"threads\": %d, \"tiles\": %ld}\n", dt, torch::get_num_threads(), tiles);
     return 0;
+}
+
+int main(int argc, char** argv) {
+    if (argc < 10) {
+        std::fprintf(stderr, "usage: ref_infer <w.fxweights> <vol.u8> dz dy dx patch overlap batch <out.f32|-> [threads]\n");
+        return 2;
+    }
+    const std::string wpath = argv[1], vpath = argv[2], opath = argv[9];
+    const Extent3 d{std::atoll(argv[3]), std::atoll(argv[4]), std::atoll(argv[5])};
+    if (argc > 10) torch::set_num_threads(std::atoi(argv[10]));
+    auto wm = ml::load_fxweights(wpath);
+    if (!wm) {
+        std::fprintf(stderr, "load_fxweights: %s\n", wm.error().message.c_str());
+        return 1;
+    }
+    // residual-encoder UNet (the reference's own nets::ResEncUNet): stem + blocks in the weights
+    for (const std::string enc : {"encoder", "shared_encoder"}) {
+        if (!wm->count(enc + ".stem.convs.0.conv.weight")) continue;
+        nets::ResEncUNetConfig cfg;
+        cfg.plain_naming = enc == "encoder";
+        cfg.features.clear();
+        cfg.blocks.clear();
+        cfg.strides.clear();
+        for (int s = 0;; ++s) {
+            const std::string st = enc + ".stages." + std::to_string(s) + ".blocks.";
+            if (!wm->count(st + "0.conv1.conv.weight")) break;
+            cfg.features.push_back(static_cast<int>(wm->at(st + "0.conv1.conv.weight").size(0)));
+            int nb = 0;
+            while (wm->count(st + std::to_string(nb) + ".conv1.conv.weight")) ++nb;
+            cfg.blocks.push_back(nb);
+            cfg.strides.push_back(s ? 2 : 1);
+        }
+        cfg.squeeze_excitation = wm->count(enc + ".stages.0.blocks.0.squeeze_excitation.sSE.conv.weight") > 0;
+        const std::string dec = cfg.plain_naming ? "decoder" : "task_decoders." + cfg.task;
+        cfg.num_classes = static_cast<int>(
+            wm->at(dec + ".seg_layers." + std::to_string(cfg.features.size() - 2) + ".weight").size(0));
+        nets::ResEncUNet rnet(cfg);
+        rnet->eval();
+        std::vector<std::string> miss;
+        ml::load_into(*rnet, *wm, &miss);
+        if (!miss.empty()) {
+            std::fprintf(stderr, "weights missing %s\n", miss[0].c_str());
+            return 1;
+        }
+        return run(rnet, argv, d, vpath, opath);
+    }
+    std::vector<int> f;
+    int nconv = 0;
+    for (;;) {
+        auto it = wm->find("encoder.stages." + std::to_string(f.size()) + ".convs.0.conv.weight");
+        if (it == wm->end()) break;
+        f.push_back(static_cast<int>(it->second.size(0)));
+    }
+    while (wm->count("encoder.stages.0.convs." + std::to_string(nconv) + ".conv.weight")) ++nconv;
+    const int ncls = static_cast<int>(wm->at("decoder.seg_layers." + std::to_string(f.size() - 2) + ".weight").size(0));
+    Plain net(f, nconv, ncls);
+    net->eval();
+    std::vector<std::string> missing;
+    ml::load_into(*net, *wm, &missing);
+    if (!missing.empty()) {
+        std::fprintf(stderr, "weights missing %s\n", missing[0].c_str());
+        return 1;
+    }
+    return run(net, argv, d, vpath, opath);
 }

@@ -8,6 +8,8 @@ Runs only where the reference tree is present (it compiles oracle/_ref from it):
                       + nets::ConvStack through libtorch, fp32, batch 2 so no fp16 round trip) on
                       seeded synthetic volumes with seeded random-init plain UNets: the u8-encoded
                       probability map, exact f32 values at 4096 sampled voxels, and sum / mean.
+  * resenc_<case>.npz — the same with the reference's own nets::ResEncUNet (residual encoder,
+                      optional scSE, plain or task naming) loaded from seeded random-init weights.
 
 usage: python tests/golden/make_golden.py [--only CASE]
 """
@@ -26,7 +28,7 @@ ROOT = HERE.parents[1]
 sys.path.insert(0, str(ROOT))
 
 import fenix_b200 as fx  # noqa: E402
-from fenix_b200.weights import make_plain_unet  # noqa: E402
+from fenix_b200.weights import make_plain_unet, make_resenc_unet  # noqa: E402
 from oracle import oracle as orc  # noqa: E402
 
 # name: (features, weight seed, volume shape, volume seed, spiral params, patch, overlap)
@@ -35,6 +37,12 @@ CASES = {
     "cfg1_p64": ((16, 32, 64, 128), 0, (64, 96, 64), 11, fx.SPIRAL_CONFIG1, 64, 0.25),
     "cfg2_p64": ((32, 64, 128, 256, 320), 1, (64, 64, 64), 1, fx.SPIRAL_CONFIG1, 64, 0.5),
     "cfg3_p64": ((32, 64, 128, 256, 320), 2, (96, 96, 96), 2, fx.SPIRAL_CONFIG3, 64, 0.5),
+}
+
+# name: (features, blocks, scSE, plain naming, weight seed, volume shape, volume seed, patch, overlap)
+RESENC = {
+    "plain": ((16, 32, 64, 64), (1, 2, 2, 1), False, True, 6, (80, 72, 96), 8, 64, 0.5),
+    "scse": ((16, 32, 64), (1, 2, 2), True, False, 7, (64, 80, 64), 9, 64, 0.5),
 }
 
 
@@ -83,6 +91,33 @@ def net_case(name):
     print(f"net_{name}.npz: shape {shape}, {info}")
 
 
+def resenc_case(name):
+    feats, blocks, se, plain, wseed, shape, vseed, P, ov = RESENC[name]
+    sp = fx.SPIRAL_CONFIG1
+    with tempfile.TemporaryDirectory() as td:
+        w = make_resenc_unet(Path(td) / "w.fxweights", feats, blocks, ncls=2, se=se, plain_naming=plain, seed=wseed)
+        vol = fx.synth_spiral(shape, vseed, sp)
+        prob, info = orc.ref_infer(w, vol, P, ov, batch=2)
+    rng = np.random.default_rng(4321)
+    idx = rng.choice(prob.size, size=min(4096, prob.size), replace=False).astype(np.int64)
+    np.savez_compressed(
+        HERE / f"resenc_{name}.npz",
+        u8=orc.prob_to_u8(prob),
+        sample_idx=idx,
+        sample_val=prob.reshape(-1)[idx],
+        features=np.array(feats, dtype=np.int64),
+        blocks=np.array(blocks, dtype=np.int64),
+        se=np.int64(se),
+        plain_naming=np.int64(plain),
+        weight_seed=np.int64(wseed),
+        shape=np.array(shape, dtype=np.int64),
+        volume_seed=np.int64(vseed),
+        patch=np.int64(P),
+        overlap=np.float64(ov),
+    )
+    print(f"resenc_{name}.npz: shape {shape}, {info}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None)
@@ -93,6 +128,9 @@ def main():
     for name in CASES:
         if a.only in (None, name):
             net_case(name)
+    for name in RESENC:
+        if a.only in (None, "resenc_" + name):
+            resenc_case(name)
 
 
 if __name__ == "__main__":
