@@ -129,6 +129,21 @@ def lib():
                                          C.POINTER(C.c_int64), C.POINTER(C.c_double), i32])
     _sig(L, "fx_kernel_launches", C.c_ulonglong, [])
     _sig(L, "fx_synth_spiral", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
+    u64p, u32p = C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)
+    _sig(L, "fx_fxvol_open", i32, [C.c_char_p, C.POINTER(vp)])
+    _sig(L, "fx_fxvol_create", i32, [C.c_char_p, i64, i64, i64, C.c_float, i32, C.POINTER(vp)])
+    _sig(L, "fx_fxvol_get_info", i32, [vp, vp])
+    _sig(L, "fx_fxvol_chunk_payload", i32, [vp, i32, i64, i64, i64, C.POINTER(C.c_int), C.POINTER(vp), u64p])
+    _sig(L, "fx_fxvol_write_chunk_payload", i32, [vp, i32, i64, i64, i64, vp, C.c_uint64])
+    _sig(L, "fx_fxvol_set_nlods", i32, [vp, C.c_uint32])
+    _sig(L, "fx_fxvol_close", i32, [vp])
+    _sig(L, "fx_fxvol_read_volume_u8", i32, [vp, i32, u8p])
+    _sig(L, "fx_fxvol_write_volume_u8", i32, [vp, u8p, i32])
+    _sig(L, "fx_fxvol_decode_tiles", i32, [vp, C.c_uint64, u64p, u32p, i64, C.c_float, C.c_float, C.c_float, i32,
+                                           vp, vp])
+    _sig(L, "fx_fxvol_encode_tiles", i32, [vp, vp, i64, C.c_float, C.c_float, C.c_float, i32, vp, C.c_uint64, u64p,
+                                           u32p])
+    _sig(L, "fx_predict_fxvol", i32, [vp, C.c_char_p, C.c_char_p, C.POINTER(InferOpts), C.c_float])
     _lib = L
     return L
 
@@ -287,6 +302,12 @@ class Net:
             )
         )
         return prob, u8
+
+    def predict_fxvol(self, in_path, out_path, overlap: float = 0.5, batch: int = 1, channel: int = 1,
+                      sigmoid: int = 0, tta: int = 0, out_q: float = 32.0) -> None:
+        """predict-surface over archives: u8 .fxvol in, u8 .fxvol (q = out_q, LOD pyramid) out."""
+        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch, tta)
+        check(lib().fx_predict_fxvol(self._h, str(in_path).encode(), str(out_path).encode(), C.byref(opts), out_q))
 
     def predict_tiles_dev(self, dev_slab_ptr: int, slab_shape, z_origin: int, full_dz: int, overlap: float,
                           batch: int, tile_begin: int, tile_end: int, dev_acc_ptr: int, channel: int = 1,

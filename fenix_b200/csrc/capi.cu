@@ -24,9 +24,6 @@ namespace fxh {
 extern unsigned long long* g_conv_trace;
 }
 
-struct fx_net {
-    fxh::Net net;
-};
 
 // Static device scratch of fx_norm_tiles_noalloc: the tile origins, then the per-tile exact
 // sums (Σv, Σv² as u64). One copy per device (a __device__ variable lives in every context).
@@ -82,6 +79,36 @@ fx_status abi_exception() {
     } catch (...) {
         return set_err(FX_INTERNAL, "internal error");
     }
+}
+// The device part of fx_predict_volume (src/ml/infer.hpp:456-864 + inference.cpp:343-351): d_vol
+// (resident, dims dz, dy, dx) -> Gaussian blend in d_acc -> normalised probability in d_prob
+// (may alias d_acc) and/or u8 in d_u8. Stream-ordered on the net's stream; no final sync.
+fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx,
+                           const fx_infer_opts* o, float* d_acc, float* d_prob, uint8_t* d_u8) {
+    cudaStream_t s = n->net.stream();
+    const size_t nv = static_cast<size_t>(dz) * dy * dx;
+    cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
+    Status st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, o->patch, o->overlap, o->channel, o->sigmoid, o->batch,
+                                     0, -1, d_acc, s, 0, -1, o->tta);
+    if (!st.ok()) return set_err(st);
+    const int P = o->patch;
+    const auto g = fenix::ml::gaussian1d(P);
+    const auto zs = fenix::ml::tile_starts(dz, P, o->overlap), ys = fenix::ml::tile_starts(dy, P, o->overlap),
+               xs = fenix::ml::tile_starts(dx, P, o->overlap);
+    const auto Wz = fenix::ml::weight_profile(g, zs, 0, dz, dz, P), Wy = fenix::ml::weight_profile(g, ys, 0, dy, dy, P),
+               Wx = fenix::ml::weight_profile(g, xs, 0, dx, dx, P);
+    std::vector<float> w(static_cast<size_t>(dz + dy + dx));
+    std::copy(Wz.begin(), Wz.end(), w.begin());
+    std::copy(Wy.begin(), Wy.end(), w.begin() + dz);
+    std::copy(Wx.begin(), Wx.end(), w.begin() + dz + dy);
+    float* d_w = nullptr;
+    if (cudaMalloc(&d_w, sizeof(float) * w.size()) != cudaSuccess) return set_err(FX_INTERNAL, "cudaMalloc: weight profiles");
+    cudaMemcpyAsync(d_w, w.data(), sizeof(float) * w.size(), cudaMemcpyHostToDevice, s);
+    cudaError_t e = fxk::launch_accum_finalize(d_acc, dz, dy, dx, 0, dz, d_w, d_w + dz, d_w + dz + dy, d_prob, d_u8, s);
+    cudaStreamSynchronize(s);
+    cudaFree(d_w);
+    if (e != cudaSuccess) return set_err(cuda_status(e, "accum_finalize"));
+    return FX_OK;
 }
 }  // namespace fxh
 
@@ -249,34 +276,18 @@ fx_status fx_predict_volume(fx_net* n, const uint8_t* host_vol, int64_t dz, int6
         cudaSetDevice(n->net.device());
         cudaStream_t s = n->net.stream();
         const size_t nv = static_cast<size_t>(dz) * dy * dx;
-        Scratch sc;
         uint8_t *d_vol = nullptr, *d_u8 = nullptr;
         float* d_acc = nullptr;
         fxh::Status st = n->net.workspace(nv, nv * sizeof(float), host_u8 ? nv : 0, &d_vol, &d_acc, &d_u8);
         if (!st.ok()) return set_err(st);
         cudaMemcpyAsync(d_vol, host_vol, nv, cudaMemcpyHostToDevice, s);
-        cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
-        st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, o->patch, o->overlap, o->channel, o->sigmoid, o->batch, 0,
-                                  -1, d_acc, s, 0, -1, o->tta);
-        if (!st.ok()) return set_err(st);
-        const int P = o->patch;
-        const auto g = fenix::ml::gaussian1d(P);
-        const auto zs = fenix::ml::tile_starts(dz, P, o->overlap), ys = fenix::ml::tile_starts(dy, P, o->overlap),
-                   xs = fenix::ml::tile_starts(dx, P, o->overlap);
-        const auto Wz = fenix::ml::weight_profile(g, zs, 0, dz, dz, P), Wy = fenix::ml::weight_profile(g, ys, 0, dy, dy, P),
-                   Wx = fenix::ml::weight_profile(g, xs, 0, dx, dx, P);
-        float* d_w = static_cast<float*>(sc.get(sizeof(float) * (dz + dy + dx)));
         // the normalised probability overwrites the accumulator in place
         float* d_prob = host_prob ? d_acc : nullptr;
-        if (!d_w) return set_err(FX_INTERNAL, "cudaMalloc: weight profiles");
-        cudaMemcpyAsync(d_w, Wz.data(), sizeof(float) * dz, cudaMemcpyHostToDevice, s);
-        cudaMemcpyAsync(d_w + dz, Wy.data(), sizeof(float) * dy, cudaMemcpyHostToDevice, s);
-        cudaMemcpyAsync(d_w + dz + dy, Wx.data(), sizeof(float) * dx, cudaMemcpyHostToDevice, s);
-        cudaError_t e = fxk::launch_accum_finalize(d_acc, dz, dy, dx, 0, dz, d_w, d_w + dz, d_w + dz + dy, d_prob, d_u8, s);
-        if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "accum_finalize"));
+        if (fx_status r = fxh::predict_resident(n, d_vol, dz, dy, dx, o, d_acc, d_prob, host_u8 ? d_u8 : nullptr))
+            return r;
         if (host_prob) cudaMemcpyAsync(host_prob, d_prob, nv * sizeof(float), cudaMemcpyDeviceToHost, s);
         if (host_u8) cudaMemcpyAsync(host_u8, d_u8, nv, cudaMemcpyDeviceToHost, s);
-        e = cudaStreamSynchronize(s);
+        cudaError_t e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "predict_volume"));
         return FX_OK;
     });

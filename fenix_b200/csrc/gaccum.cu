@@ -20,10 +20,6 @@
 #include <string>
 #include <vector>
 
-struct fx_net {
-    fxh::Net net;
-};
-
 namespace fxh {
 fx_status abi_error(int code, const std::string& msg);  // capi.cu: sets the thread's last error
 fx_status abi_exception();                              // capi.cu: status + message of a caught exception

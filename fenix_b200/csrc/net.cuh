@@ -5,6 +5,7 @@
 // 141-158, 197-239); the driver follows ml::predict_surface_filled (src/ml/infer.hpp:456-864).
 #pragma once
 
+#include "fenix_b200.h"
 #include "conv_tc.cuh"
 #include "eltwise.cuh"
 #include "fxweights.hpp"
@@ -217,4 +218,15 @@ class Net {
     std::vector<void*> allocs_;
 };
 
+}  // namespace fxh
+
+// The opaque handle of include/fenix_b200.h.
+struct fx_net {
+    fxh::Net net;
+};
+
+namespace fxh {
+// fx_predict_volume's device part (capi.cu), shared with the .fxvol entry points.
+fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx,
+                           const fx_infer_opts* o, float* d_acc, float* d_prob, uint8_t* d_u8);
 }  // namespace fxh

@@ -29,6 +29,15 @@
  *                                     finalize_rows_below, resume floor
  *                                     (src/ml/global_accum.hpp:37-198), and a tile row of
  *                                     predict-scroll's global mode (src/ml/inference.cpp:1282-1372)
+ *   fx_fxvol_*                      — codec::VolumeArchive, the .fxvol v5 container
+ *                                     (src/codec/archive.hpp:132-1217) with LOD-0 reads and
+ *                                     write_volume encoded / decoded on the device
+ *   fx_fxvol_encode_tiles / _decode_tiles
+ *                                   — codec::encode_tile_dct / decode_tile_dct with bpa = 4
+ *                                     (src/codec/dct_block.hpp:318-588)
+ *   fx_predict_fxvol                — the predict-surface command over archives: .fxvol input
+ *                                     read (src/ml/inference.cpp:540-567), prediction, u8 q=32
+ *                                     .fxvol output (src/ml/inference.cpp:333-355)
  */
 #ifndef FENIX_B200_H
 #define FENIX_B200_H
@@ -216,6 +225,57 @@ fx_status fx_conv_transpose2(const float* dev_x, int B, int Cin, int D, int H, i
 fx_status fx_accum_finalize(const float* dev_acc, int64_t dz, int64_t dy, int64_t dx, int64_t z_begin, int64_t z_end,
                             const float* dev_wz, const float* dev_wy, const float* dev_wx, float* dev_prob,
                             uint8_t* dev_u8, void* stream);
+
+/* ---- .fxvol archives and the chunk codec ---------------------------------------------------
+ * A 64^3 chunk is one tile of 4^3 DCT-16 blocks whose magnitude categories share up to 8 clustered
+ * rANS tables. Payloads and files are bit-compatible with the reference's codec and container. */
+typedef struct fx_fxvol fx_fxvol;
+
+typedef struct fx_fxvol_info {
+    int64_t dims[3];  /* LOD-0 z, y, x */
+    float q, hf_exp, dz_frac;
+    uint32_t nlods;
+    int32_t src_dtype; /* codec::DType: 0 u8, 1 u16, 2 u32, 3 s8, 4 s16, 5 s32, 6 f16, 7 f32 */
+    int32_t sealed;    /* a finalize()d (SEALED) archive */
+} fx_fxvol_info;
+
+/* VolumeArchive::open, read-only (archive.hpp:161-262). */
+fx_status fx_fxvol_open(const char* path, fx_fxvol** out);
+/* VolumeArchive::create (archive.hpp:135-158): DctParams{.q = q}, hf_exp 0.65, dz_frac 0.80. */
+fx_status fx_fxvol_create(const char* path, int64_t dz, int64_t dy, int64_t dx, float q, int32_t src_dtype,
+                          fx_fxvol** out);
+/* dims() / params() / nlods() / src_dtype() */
+fx_status fx_fxvol_get_info(const fx_fxvol* a, fx_fxvol_info* out);
+/* coverage() (0 ABSENT, 1 ZERO, 2 REAL) and, for REAL chunks, the crc-checked payload, valid until
+ * fx_fxvol_close (archive.hpp:376-399 up to the decode). */
+fx_status fx_fxvol_chunk_payload(const fx_fxvol* a, int lod, int64_t cz, int64_t cy, int64_t cx, int* coverage,
+                                 const uint8_t** payload, uint64_t* len);
+/* write_chunk_payload (archive.hpp:350-362); len 0 records a ZERO chunk (commit_encoded_). */
+fx_status fx_fxvol_write_chunk_payload(fx_fxvol* a, int lod, int64_t cz, int64_t cy, int64_t cx,
+                                       const uint8_t* payload, uint64_t len);
+/* the LOD count written at close (write_volume sets it after the pyramid, archive.hpp:428-439) */
+fx_status fx_fxvol_set_nlods(fx_fxvol* a, uint32_t nlods);
+/* close(): commit + trim for writers (archive.hpp:867-894); frees the handle. */
+fx_status fx_fxvol_close(fx_fxvol* a);
+/* read_volume_as<u8>(0) (archive.hpp:550-590), decoded on `device`: out holds dims z*y*x voxels. */
+fx_status fx_fxvol_read_volume_u8(const fx_fxvol* a, int device, uint8_t* out);
+/* write_volume<u8> (archive.hpp:418-440): LOD 0 and the 2x octave pyramid, encoded on `device`. */
+fx_status fx_fxvol_write_volume_u8(fx_fxvol* a, const uint8_t* vol, int device);
+/* decode_tile_dct over n payloads (payloads + offsets[k], lengths[k] bytes) into n 64^3 tiles:
+ * u8 (out_u8) and/or the f32 reconstruction (out_f32); either may be NULL, not both. */
+fx_status fx_fxvol_decode_tiles(const uint8_t* payloads, uint64_t payload_bytes, const uint64_t* offsets,
+                                const uint32_t* lengths, int64_t n, float q, float hf_exp, float dz_frac, int device,
+                                uint8_t* out_u8, float* out_f32);
+/* encode_tile_dct over n 64^3 tiles (u8 or f32, exactly one non-NULL) into out (cap bytes):
+ * payload k at out + offsets[k], lengths[k] bytes. FX_INVALID_ARGUMENT if cap is too small. */
+fx_status fx_fxvol_encode_tiles(const uint8_t* tiles_u8, const float* tiles_f32, int64_t n, float q, float hf_exp,
+                                float dz_frac, int device, uint8_t* out, uint64_t cap, uint64_t* offsets,
+                                uint32_t* lengths);
+/* predict-surface over archives: decode the u8 input archive's LOD 0 on the net's device, predict
+ * (opts as fx_predict_volume), write the u8 prediction as an .fxvol at q = out_q (<= 0: 32) with
+ * its LOD pyramid. The volume stays on the device from decode to encode. */
+fx_status fx_predict_fxvol(fx_net* net, const char* in_path, const char* out_path, const fx_infer_opts* opts,
+                           float out_q);
 
 #ifdef __cplusplus
 }

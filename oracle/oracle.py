@@ -1,4 +1,5 @@
-"""ctypes binding of the C oracle (oracle/fxo.c). TEST INFRASTRUCTURE ONLY: imported by tests/,
+"""ctypes binding of the C oracle (oracle/fxo.c inference, oracle/fxv.c .fxvol codec) and a plain
+Python reader of the .fxvol container. TEST INFRASTRUCTURE ONLY: imported by tests/,
 __graft_entry__.smoke() and bench.py's CPU-baseline leg as the checker; the product never
 imports it."""
 from __future__ import annotations
@@ -39,6 +40,21 @@ def lib():
         L.fxo_net_forward.argtypes = [vp, f32p, i32, i32, i32, i32, f32p]
         L.fxo_predict_surface.argtypes = [vp, u8p, i64, i64, i64, i32, C.c_double, i32, i32, f32p]
         L.fxo_prob_to_u8.argtypes = [f32p, i64, u8p]
+        L.fxv_params_default.argtypes = [vp, C.c_float]
+        L.fxv_dct3_fwd.argtypes = [f32p]
+        L.fxv_dct3_inv.argtypes = [f32p]
+        L.fxv_decode_tile.restype = i32
+        L.fxv_decode_tile.argtypes = [vp, C.c_size_t, vp, f32p, u8p]
+        L.fxv_encode_tile_u8.restype = i64
+        L.fxv_encode_tile_u8.argtypes = [u8p, vp, i32, u8p, C.c_size_t]
+        L.fxv_encode_tile_f32.restype = i64
+        L.fxv_encode_tile_f32.argtypes = [f32p, vp, i32, u8p, C.c_size_t]
+        L.fxv_log2_series.restype = C.c_double
+        L.fxv_log2_series.argtypes = [C.c_double]
+        L.fxv_crc32c.restype = C.c_uint32
+        L.fxv_crc32c.argtypes = [vp, C.c_size_t]
+        L.fxv_morton3.restype = C.c_uint64
+        L.fxv_morton3.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64]
         _lib = L
     return _lib
 
@@ -133,3 +149,121 @@ def ref_infer(weights, vol, P, overlap, batch=1, threads=None, out_path=None):
         info = json.loads(r.stdout.strip().splitlines()[-1])
         prob = np.fromfile(op, dtype=np.float32).reshape(v.shape)
     return prob, info
+
+
+# ---- .fxvol chunk codec (oracle/fxv.c) ----------------------------------------------------------
+
+class FxvParams(C.Structure):
+    """DctParams (src/codec/dct_block.hpp:26-37)."""
+
+    _fields_ = [("q", C.c_float), ("hf_exp", C.c_float), ("dz_frac", C.c_float), ("rdoq", C.c_int),
+                ("rdoq_lambda", C.c_float), ("deblock", C.c_int), ("deblock_beta", C.c_float),
+                ("deblock_tc", C.c_float), ("dc_predict", C.c_int)]
+
+
+def fxv_params(q: float, hf_exp: float = 0.65, dz_frac: float = 0.80) -> FxvParams:
+    p = FxvParams()
+    lib().fxv_params_default(C.byref(p), q)
+    p.hf_exp, p.dz_frac = hf_exp, dz_frac
+    return p
+
+
+def fxv_decode(payload: bytes, q: float, hf_exp: float = 0.65, dz_frac: float = 0.80):
+    """decode_tile_dct: (status, u8 tile, f32 reconstruction)."""
+    b = np.frombuffer(payload, dtype=np.uint8) if payload else np.zeros(1, dtype=np.uint8)
+    u8 = np.zeros((64, 64, 64), dtype=np.uint8)
+    f = np.zeros((64, 64, 64), dtype=np.float32)
+    p = fxv_params(q, hf_exp, dz_frac)
+    rc = lib().fxv_decode_tile(b.ctypes.data, len(payload), C.byref(p), _fp(f), u8.ctypes.data_as(C.POINTER(C.c_uint8)))
+    return rc, u8, f
+
+
+def fxv_encode(tile: np.ndarray, q: float, log2_mode: int = 1, hf_exp: float = 0.65, dz_frac: float = 0.80) -> bytes:
+    """encode_tile_dct of one 64^3 u8 or f32 tile; log2_mode 0 = glibc log2 (the reference's), 1 =
+    the portable series (the device's)."""
+    t = np.ascontiguousarray(tile)
+    cap = 4 * 64 ** 3 + 4096
+    out = np.zeros(cap, dtype=np.uint8)
+    p = fxv_params(q, hf_exp, dz_frac)
+    up = out.ctypes.data_as(C.POINTER(C.c_uint8))
+    if t.dtype == np.uint8:
+        n = lib().fxv_encode_tile_u8(t.ctypes.data_as(C.POINTER(C.c_uint8)), C.byref(p), log2_mode, up, cap)
+    else:
+        n = lib().fxv_encode_tile_f32(_fp(t.astype(np.float32, copy=False)), C.byref(p), log2_mode, up, cap)
+    if n < 0:
+        raise RuntimeError("fxv_encode failed")
+    return out[:n].tobytes()
+
+
+def fxv_dct3(block: np.ndarray, inverse: bool = False) -> np.ndarray:
+    b = np.ascontiguousarray(block, dtype=np.float32).copy()
+    (lib().fxv_dct3_inv if inverse else lib().fxv_dct3_fwd)(_fp(b))
+    return b
+
+
+def fxvol_read_slots(path) -> dict:
+    """A plain reader of the .fxvol v5 container (src/codec/archive.hpp:42-130 layout, 161-262 open,
+    1080-1107 radix walk): {"dims", "q", "hf_exp", "dz_frac", "nlods", "dtype", "slots"}, slots
+    mapping (lod, cz, cy, cx) -> (coverage, payload or None) for every chunk of every LOD."""
+    import struct
+
+    buf = Path(path).read_bytes()
+    best = None
+    for s in range(2):
+        b = buf[s * 4096:(s + 1) * 4096]
+        magic, version = struct.unpack_from("<II", b, 0)
+        crc_stored = struct.unpack_from("<I", b, 236)[0]
+        if magic != 0x4C565846 or version != 5 or lib().fxv_crc32c(b, 236) != crc_stored:
+            continue
+        seq = struct.unpack_from("<Q", b, 8)[0]
+        if best is None or seq > best[0]:
+            best = (seq, b)
+    if best is None:
+        raise ValueError("no valid superblock")
+    b = best[1]
+    eof, nlods, dtype = struct.unpack_from("<QII", b, 16)
+    dims = struct.unpack_from("<qqq", b, 32)
+    q, hf, dzf = struct.unpack_from("<fff", b, 56)
+    roots = struct.unpack_from("<20Q", b, 68)
+    u64 = lambda off: struct.unpack_from("<Q", buf, off)[0]
+    slots = {}
+    d = list(dims)
+    for lod in range(nlods):
+        ce = [(v + 63) // 64 for v in d]
+        for cz in range(ce[0]):
+            for cy in range(ce[1]):
+                for cx in range(ce[2]):
+                    m = lib().fxv_morton3(cz, cy, cx)
+                    cov, pay = 0, None
+                    if roots[lod]:
+                        c1 = u64(roots[lod] + 8 * ((m >> 24) & 0xFFF))
+                        c2 = u64(c1 + 8 * ((m >> 12) & 0xFFF)) if c1 else 0
+                        if c2:
+                            off, n = struct.unpack_from("<QQ", buf, c2 + 16 * (m & 0xFFF))
+                            if off != 0xFFFFFFFFFFFFFFFF:
+                                cov = 1 if n == 0 else 2
+                                if n:
+                                    pay = buf[off:off + n]
+                                    if struct.unpack_from("<I", buf, off + n)[0] != lib().fxv_crc32c(pay, n):
+                                        raise ValueError("chunk crc mismatch")
+                    slots[(lod, cz, cy, cx)] = (cov, pay)
+        d = [(v + 1) // 2 for v in d]
+    return {"dims": dims, "q": q, "hf_exp": hf, "dz_frac": dzf, "nlods": nlods, "dtype": dtype, "eof": eof,
+            "slots": slots}
+
+
+def fxvol_read_u8(path) -> np.ndarray:
+    """read_volume_as<u8>(0) through the C oracle's tile decoder."""
+    a = fxvol_read_slots(path)
+    dz, dy, dx = a["dims"]
+    out = np.zeros((dz, dy, dx), dtype=np.uint8)
+    for (lod, cz, cy, cx), (cov, pay) in a["slots"].items():
+        if lod or cov != 2:
+            continue
+        rc, t, _ = fxv_decode(pay, a["q"], a["hf_exp"], a["dz_frac"])
+        if rc:
+            raise ValueError(f"chunk {(cz, cy, cx)}: decode error {rc}")
+        z0, y0, x0 = cz * 64, cy * 64, cx * 64
+        sz, sy, sx = min(64, dz - z0), min(64, dy - y0), min(64, dx - x0)
+        out[z0:z0 + sz, y0:y0 + sy, x0:x0 + sx] = t[:sz, :sy, :sx]
+    return out

@@ -10,6 +10,12 @@ Runs only where the reference tree is present (it compiles oracle/_ref from it):
                       probability map, exact f32 values at 4096 sampled voxels, and sum / mean.
   * resenc_<case>.npz — the same with the reference's own nets::ResEncUNet (residual encoder,
                       optional scSE, plain or task naming) loaded from seeded random-init weights.
+  * fxvol_tiles.npz — the reference's encode_tile_dct payloads of the 64^3 chunks of
+                      tests/golden/fxvol_cases.py, and SHA-256 digests of its decode_tile_dct output
+                      (u8, and the f32 reconstruction) of those payloads (oracle/_ref/ref_fxvol).
+  * fxvol_small.fxvol + fxvol_small.npz — an archive written by the reference's
+                      VolumeArchive::create + write_volume<u8> + close from the fixture volume, the
+                      coverage of every chunk of every LOD, and the digest of read_volume_as<u8>(0).
 
 usage: python tests/golden/make_golden.py [--only CASE]
 """
@@ -118,6 +124,46 @@ def resenc_case(name):
     print(f"resenc_{name}.npz: shape {shape}, {info}")
 
 
+def fxvol():
+    import hashlib
+    import os
+
+    sys.path.insert(0, str(HERE))
+    import fxvol_cases as fc
+
+    tool = str(orc.REF / "ref_fxvol")
+    sha = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+    d = {}
+    with tempfile.TemporaryDirectory() as td:
+        for dtype, cases, gen in (("u8", fc.TILE_CASES_U8, fc.chunk_u8), ("f32", fc.TILE_CASES_F32, fc.chunk_f32)):
+            for k, (kind, q) in enumerate(cases):
+                src = Path(td) / "in.raw"
+                gen(kind).tofile(src)
+                subprocess.run([tool, "enc", dtype, repr(q), "1", str(src), f"{td}/p.bin"], check=True)
+                blob = (Path(td) / "p.bin").read_bytes()
+                n = int.from_bytes(blob[:4], "little")
+                key = f"{dtype}_{kind}_q{q:g}"
+                d[f"pay_{key}"] = np.frombuffer(blob[4:4 + n], dtype=np.uint8)
+                subprocess.run([tool, "dec", "u8", repr(q), f"{td}/p.bin", f"{td}/o.raw"], check=True)
+                d[f"sha_u8_{key}"] = np.array(sha(np.fromfile(f"{td}/o.raw", dtype=np.uint8)))
+                subprocess.run([tool, "dec", "f32", repr(q), f"{td}/p.bin", f"{td}/o.raw"], check=True)
+                d[f"sha_f32_{key}"] = np.array(sha(np.fromfile(f"{td}/o.raw", dtype=np.float32)))
+        np.savez_compressed(HERE / "fxvol_tiles.npz", **d)
+        vol = fc.archive_volume()
+        vol.tofile(f"{td}/v.raw")
+        dz, dy, dx = fc.ARCHIVE_DIMS
+        out = HERE / "fxvol_small.fxvol"
+        if out.exists():
+            os.remove(out)
+        subprocess.run([tool, "write", repr(fc.ARCHIVE_Q), str(dz), str(dy), str(dx), f"{td}/v.raw", str(out)], check=True)
+        subprocess.run([tool, "read", str(out), f"{td}/r.raw"], check=True, capture_output=True)
+        slots = subprocess.run([tool, "slots", str(out)], check=True, capture_output=True, text=True).stdout
+        cov = np.array([[int(v) for v in line.split()] for line in slots.splitlines()], dtype=np.int64)
+        np.savez_compressed(HERE / "fxvol_small.npz", coverage=cov,
+                            sha_read=np.array(sha(np.fromfile(f"{td}/r.raw", dtype=np.uint8))))
+    print(f"fxvol: {len(fc.TILE_CASES_U8) + len(fc.TILE_CASES_F32)} tiles, archive {out.stat().st_size} bytes")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None)
@@ -131,6 +177,8 @@ def main():
     for name in RESENC:
         if a.only in (None, "resenc_" + name):
             resenc_case(name)
+    if a.only in (None, "fxvol"):
+        fxvol()
 
 
 if __name__ == "__main__":
