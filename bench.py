@@ -160,6 +160,64 @@ def run_reference_arm(args):
     return 0
 
 
+def fxvol_measure(vol_u8: np.ndarray, pred_u8: np.ndarray, tmp: str, reps: int = 2) -> dict:
+    """The .fxvol IO either side of the path, timed end to end through the C ABI (host volume <->
+    archive file, chunks decoded / encoded on the GPU): the input volume read from an archive at the
+    reference's default q = 8 (predict-surface's .fxvol input, inference.cpp:553-567) and the u8
+    prediction written at q = 32 with its LOD pyramid (inference.cpp:343-356). The reference's own
+    VolumeArchive (oracle/_ref/ref_fxvol, all host threads) is timed on the same files."""
+    import fenix_b200.fxvol as fv
+
+    inp, out = Path(tmp) / "in.fxvol", Path(tmp) / "pred.fxvol"
+    with fv.VolumeArchive.create(inp, vol_u8.shape, 8.0) as a:
+        a.write_volume_u8(vol_u8)
+
+    def best(fn):
+        ts = []
+        for _ in range(reps + 1):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return min(ts[1:])
+
+    def write():
+        with fv.VolumeArchive.create(out, pred_u8.shape, 32.0) as a:
+            a.write_volume_u8(pred_u8)
+
+    def read():
+        with fv.VolumeArchive.open(inp) as a:
+            a.read_volume_u8()
+
+    t_w, t_r = best(write), best(read)
+    vox = float(vol_u8.size)
+    res = {
+        "unit": "Gvoxels/s",
+        "decode": {"value": vox / t_r / 1e9, "s": t_r, "archive_bytes": inp.stat().st_size, "q": 8.0,
+                   "what": "fx_fxvol_read_volume_u8: LOD-0 read of the input volume's archive"},
+        "encode": {"value": vox / t_w / 1e9, "s": t_w, "archive_bytes": out.stat().st_size, "q": 32.0,
+                   "what": "fx_fxvol_write_volume_u8: the u8 prediction, LOD 0 + pyramid"},
+    }
+    tool = ROOT / "oracle" / "_ref" / "ref_fxvol"
+    if tool.exists():
+        raw = Path(tmp) / "pred.raw"
+        pred_u8.tofile(raw)
+        thr = os.cpu_count() or 1
+        env = dict(os.environ, OMP_NUM_THREADS=str(thr))
+        dz, dy, dx = pred_u8.shape
+        t0 = time.perf_counter()
+        subprocess.run([str(tool), "read", str(inp), str(Path(tmp) / "back.raw")], check=True, env=env,
+                       capture_output=True)
+        t_cr = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        subprocess.run([str(tool), "write", "32", str(dz), str(dy), str(dx), str(raw), str(Path(tmp) / "cpu.fxvol")],
+                       check=True, env=env, capture_output=True)
+        t_cw = time.perf_counter() - t0
+        res["cpu_baseline"] = {"kind": "reference", "cores": thr, "decode": vox / t_cr / 1e9,
+                               "encode": vox / t_cw / 1e9, "unit": "Gvoxels/s",
+                               "sample": "the same two archives, one run each, process wall time"}
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -172,6 +230,7 @@ def main():
     ap.add_argument("--overlap", type=float, default=0.5)
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fxvol", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -264,6 +323,12 @@ def main():
     for _ in range(1):
         e2e_step()
     ms_e2e = timed(e2e_step, args.steps)
+    fxv = None
+    if world == 1 and not args.no_fxvol:
+        try:
+            fxv = fxvol_measure(host_slab.numpy(), host_out.numpy(), tmp)
+        except Exception as e:  # reported, never fatal for the inference number
+            fxv = {"failed": str(e)}
     # one profiled pass: per-launch CUDA events around every conv launch (not in the timed region)
     net.profile(True)
     dev_step()
@@ -313,6 +378,7 @@ def main():
             "e2e": {"value": e2e, "unit": "Mvoxels/s", "h2d_bytes_per_step": sp.h2d_bytes * world,
                     "d2h_bytes_per_step": sp.d2h_bytes * world, "path": e2e_path},
             "cpu_baseline": cpu,
+            "fxvol": fxv,
             "clocks": clk,
             "gpu_launches": launches,
         }

@@ -303,13 +303,13 @@ __global__ void __launch_bounds__(kWalkTiles) fxv_dec_walk(const uint8_t* __rest
                                                           float2* __restrict__ ent, int64_t n) {
     extern __shared__ uint32_t dsm[];
     uint32_t* scan = dsm;                    // [4096] packed idx | fsum << 16 | edge << 24
-    uint32_t* sigw = dsm + kV;               // [kWalkTiles][257] 2-bit significance
+    uint32_t* sigw = dsm + kV;               // [tiles per CTA][257] 2-bit significance
     __shared__ float stepv[48];
     __shared__ uint8_t cmaps[kWalkTiles][kRawCtx];
     for (int k = threadIdx.x; k < kV; k += blockDim.x) scan[k] = scan_g[k];
     for (int k = threadIdx.x; k < 48; k += blockDim.x) stepv[k] = P.stepv[k];
     __syncthreads();
-    const int64_t t = blockIdx.x * static_cast<int64_t>(kWalkTiles) + threadIdx.x;
+    const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (t >= n) return;
     DecHdr& h = hdr[t];
     if (h.err) return;
@@ -560,6 +560,8 @@ __global__ void __launch_bounds__(512) fxv_dec_recon(const DecHdr* __restrict__ 
 struct EncBlk {
     int32_t dclev;
     uint32_t nsig;
+    uint32_t cnt[kMaxCl + 1];  // symbols per cluster, raw bits (last)
+    uint32_t off[kMaxCl + 1];  // their offsets within the tile's planes / bit stream
 };
 
 struct EncHdr {
@@ -568,6 +570,7 @@ struct EncHdr {
     uint8_t cmap[kRawCtx];
     float bc[kMaxCl][kNCat];
     uint32_t plane_n[kMaxCl];
+    uint32_t cc[kMaxCl][kNCat];  // category counts per cluster plane
     uint32_t freq[kMaxCl][kNCat];
     uint32_t enc_start[kMaxCl], enc_len[kMaxCl];
     uint64_t enc_off[kMaxCl];
@@ -701,7 +704,8 @@ __global__ void __launch_bounds__(256) fxv_enc_quant(const uint8_t* __restrict__
     if (lt == 0) {
         int m = -1;
         for (int w = 0; w < 8; ++w) m = max(m, red_i[w]);
-        blk[t * 64 + b] = EncBlk{s_dl, static_cast<uint32_t>(m + 1)};
+        blk[t * 64 + b].dclev = s_dl;
+        blk[t * 64 + b].nsig = static_cast<uint32_t>(m + 1);
     }
 }
 
@@ -872,120 +876,189 @@ __global__ void __launch_bounds__(32) fxv_enc_cluster(EncHdr* __restrict__ eh) {
     }
 }
 
-// RDOQ (dct_block.hpp:372-412), one thread per block walking its coefficients in scan order.
-__global__ void __launch_bounds__(64) fxv_enc_rdoq(int16_t* __restrict__ lev, const float* __restrict__ coef,
-                                                   EncBlk* __restrict__ blk, const uint32_t* __restrict__ scan,
-                                                   const EncHdr* __restrict__ eh, FxvParams P) {
+// RDOQ (dct_block.hpp:372-412), one CTA per block. The reference decides in scan order; every
+// coefficient's causal neighbours lie in the previous frequency shell (z+y+x one less), so the
+// decisions of one shell are independent and a shell is decided in parallel, shell after shell.
+__global__ void __launch_bounds__(128) fxv_enc_rdoq(int16_t* __restrict__ lev, const float* __restrict__ coef,
+                                                    EncBlk* __restrict__ blk, const uint32_t* __restrict__ scan,
+                                                    const uint16_t* __restrict__ shell, const EncHdr* __restrict__ eh,
+                                                    FxvParams P) {
     __shared__ float bc[kMaxCl][kNCat];
     __shared__ uint8_t cmap[kRawCtx];
     __shared__ float stepv[48];
-    const int64_t t = blockIdx.x;
+    __shared__ int red[4];
+    const int b = blockIdx.x;
+    const int64_t t = blockIdx.y;
     const EncHdr& h = eh[t];
     if (!h.nonzero) return;
-    for (int k = threadIdx.x; k < kMaxCl * kNCat; k += 64) bc[k / kNCat][k % kNCat] = h.bc[k / kNCat][k % kNCat];
-    for (int k = threadIdx.x; k < kRawCtx; k += 64) cmap[k] = h.cmap[k];
-    for (int k = threadIdx.x; k < 48; k += 64) stepv[k] = P.stepv[k];
+    for (int k = threadIdx.x; k < kMaxCl * kNCat; k += 128) bc[k / kNCat][k % kNCat] = h.bc[k / kNCat][k % kNCat];
+    for (int k = threadIdx.x; k < kRawCtx; k += 128) cmap[k] = h.cmap[k];
+    for (int k = threadIdx.x; k < 48; k += 128) stepv[k] = P.stepv[k];
     __syncthreads();
-    const int b = threadIdx.x;
     int16_t* L = lev + (t * 64 + b) * static_cast<int64_t>(kV);
     const float* C = coef + (t * 64 + b) * static_cast<int64_t>(kV);
     const uint32_t ns = blk[t * 64 + b].nsig;
     const float dz = P.dz_frac, lamq = P.rdoq_lambda;
-    for (uint32_t pos = 0; pos < ns; ++pos) {
-        const uint32_t e = scan[pos];
-        const int i = e & 0xffff, fsum = (e >> 16) & 0xff, edge = e >> 24;
-        const int l = L[i];
-        const uint32_t m0 = static_cast<uint32_t>(abs(l));
-        if (m0 == 0) continue;
-        const int cl = cmap[raw_ctx(fsum, nsum_lev(L, i, edge))];
-        const float s = stepv[fsum], lam = fm(fm(lamq, s), s), ac = fabsf(C[i]);
-        auto rd = [&](uint32_t m) {
-            const float dq = m ? fm(s, fa(fa(fs(static_cast<float>(m), 1.0f), dz), 0.40f)) : 0.0f;
-            const int cat = m ? bitw(m) : 0;
-            const float df = fs(ac, dq);
-            return fa(fm(df, df), fm(lam, fa(bc[cl][cat], static_cast<float>(m ? cat : 0))));
-        };
-        uint32_t bm = m0;
-        float best = rd(m0);
-        const float c0 = rd(0);
-        if (c0 < best) {
-            best = c0;
-            bm = 0;
-        }
-        if (m0 >= 2) {
-            const float c1 = rd(m0 - 1);
-            if (c1 < best) {
-                best = c1;
-                bm = m0 - 1;
+    for (int f = 0; f < 46; ++f) {
+        const uint32_t s0 = shell[f];
+        if (s0 >= ns) break;
+        const uint32_t s1 = min(static_cast<uint32_t>(shell[f + 1]), ns);
+        for (uint32_t pos = s0 + threadIdx.x; pos < s1; pos += 128) {
+            const uint32_t e = scan[pos];
+            const int i = e & 0xffff, fsum = (e >> 16) & 0xff, edge = e >> 24;
+            const int l = L[i];
+            const uint32_t m0 = static_cast<uint32_t>(abs(l));
+            if (m0 == 0) continue;
+            const int cl = cmap[raw_ctx(fsum, nsum_lev(L, i, edge))];
+            const float s = stepv[fsum], lam = fm(fm(lamq, s), s), ac = fabsf(C[i]);
+            auto rd = [&](uint32_t m) {
+                const float dq = m ? fm(s, fa(fa(fs(static_cast<float>(m), 1.0f), dz), 0.40f)) : 0.0f;
+                const int cat = m ? bitw(m) : 0;
+                const float df = fs(ac, dq);
+                return fa(fm(df, df), fm(lam, fa(bc[cl][cat], static_cast<float>(m ? cat : 0))));
+            };
+            uint32_t bm = m0;
+            float best = rd(m0);
+            const float c0 = rd(0);
+            if (c0 < best) {
+                best = c0;
+                bm = 0;
             }
+            if (m0 >= 2) {
+                const float c1 = rd(m0 - 1);
+                if (c1 < best) {
+                    best = c1;
+                    bm = m0 - 1;
+                }
+            }
+            L[i] = static_cast<int16_t>(l < 0 ? -static_cast<int>(bm) : static_cast<int>(bm));
         }
-        L[i] = static_cast<int16_t>(l < 0 ? -static_cast<int>(bm) : static_cast<int>(bm));
+        __syncthreads();
     }
-    uint32_t n2 = 0;
-    for (int pos = static_cast<int>(ns) - 1; pos >= 0; --pos)
-        if (L[scan[pos] & 0xffff] != 0) {
-            n2 = static_cast<uint32_t>(pos + 1);
-            break;
-        }
-    blk[t * 64 + b].nsig = n2;
+    int m = -1;
+    for (uint32_t pos = threadIdx.x; pos < ns; pos += 128)
+        if (L[scan[pos] & 0xffff] != 0) m = max(m, static_cast<int>(pos));
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) blk[t * 64 + b].nsig = static_cast<uint32_t>(max(max(red[0], red[1]), max(red[2], red[3])) + 1);
 }
 
-// Symbol emission (dct_block.hpp:415-439), one thread per block: a counting pass, per-tile
-// prefix sums over the blocks, then each block writes its category symbols into the clustered
-// streams and its raw bits at its own offsets (bits into u32 words, little-endian = the
-// reference's LSB-first byte stream).
-__global__ void __launch_bounds__(64) fxv_enc_emit(const int16_t* __restrict__ lev, const EncBlk* __restrict__ blk,
-                                                   const uint32_t* __restrict__ scan, EncHdr* __restrict__ eh,
-                                                   uint8_t* __restrict__ work) {
-    __shared__ uint32_t cnt[64][kMaxCl + 1];
-    __shared__ uint32_t pref[64][kMaxCl + 1];
-    __shared__ uint32_t pbase[kMaxCl];
+// Symbol emission (dct_block.hpp:415-439) in three steps. count: one CTA per block, the cluster
+// and category of every coefficient (its context depends only on the final neighbour levels) into
+// the block's per-cluster symbol and raw-bit counts and the plane's category histogram.
+__global__ void __launch_bounds__(256) fxv_enc_count(const int16_t* __restrict__ lev, EncBlk* __restrict__ blk,
+                                                     const uint32_t* __restrict__ scan, EncHdr* __restrict__ eh) {
+    __shared__ uint32_t cnt[kMaxCl + 1];
+    __shared__ uint32_t cc[kMaxCl * kNCat];
     __shared__ uint8_t cmap[kRawCtx];
-    __shared__ uint32_t s_nbits;
-    const int64_t t = blockIdx.x;
+    const int b = blockIdx.x;
+    const int64_t t = blockIdx.y;
     EncHdr& h = eh[t];
     if (!h.nonzero) return;
-    const int b = threadIdx.x;
-    if (b < kRawCtx) cmap[b] = h.cmap[b];
+    for (int k = threadIdx.x; k < kMaxCl * kNCat; k += 256) cc[k] = 0;
+    if (threadIdx.x <= kMaxCl) cnt[threadIdx.x] = 0;
+    if (threadIdx.x < kRawCtx) cmap[threadIdx.x] = h.cmap[threadIdx.x];
     __syncthreads();
     const int16_t* L = lev + (t * 64 + b) * static_cast<int64_t>(kV);
     const uint32_t ns = blk[t * 64 + b].nsig;
-    uint32_t c[kMaxCl + 1] = {};
-    for (uint32_t pos = 0; pos < ns; ++pos) {
+    for (uint32_t pos = threadIdx.x; pos < ns; pos += 256) {
         const uint32_t e = scan[pos];
         const int i = e & 0xffff, fsum = (e >> 16) & 0xff, edge = e >> 24;
         const int cl = cmap[raw_ctx(fsum, nsum_lev(L, i, edge))];
         const int cat = bitw(static_cast<uint32_t>(abs(static_cast<int>(L[i]))));
+        atomicAdd(&cnt[cl], 1u);
+        if (cat) atomicAdd(&cnt[kMaxCl], static_cast<uint32_t>(cat));
+        atomicAdd(&cc[cl * kNCat + cat], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x <= kMaxCl) blk[t * 64 + b].cnt[threadIdx.x] = cnt[threadIdx.x];
+    for (int k = threadIdx.x; k < kMaxCl * kNCat; k += 256)
+        if (cc[k]) atomicAdd(&h.cc[k / kNCat][k % kNCat], cc[k]);
+}
+
+// prefix: one CTA per tile, the blocks' offsets within each plane and the bit stream, the plane
+// lengths, and the zeroed bit-stream words.
+__global__ void __launch_bounds__(64) fxv_enc_prefix(EncBlk* __restrict__ blk, EncHdr* __restrict__ eh,
+                                                     uint8_t* __restrict__ work) {
+    __shared__ uint32_t s_nbits;
+    const int64_t t = blockIdx.x;
+    EncHdr& h = eh[t];
+    if (!h.nonzero) return;
+    if (threadIdx.x <= kMaxCl) {
+        const int k = threadIdx.x;
+        uint32_t run = 0;
+        for (int b = 0; b < 64; ++b) {
+            blk[t * 64 + b].off[k] = run;
+            run += blk[t * 64 + b].cnt[k];
+        }
+        if (k < kMaxCl) h.plane_n[k] = run;
+        else {
+            h.nbits = run;
+            s_nbits = run;
+        }
+    }
+    __syncthreads();
+    uint32_t* W = reinterpret_cast<uint32_t*>(work + t * kWorkPerTile + kSymCap + kEncCap);
+    const uint32_t nwords = (s_nbits + 31) / 32;
+    for (uint32_t k = threadIdx.x; k < nwords; k += 64) W[k] = 0;
+}
+
+// write: one CTA per block; each thread takes 16 consecutive scan positions, a block-wide scan gives
+// every position its rank within its cluster stream and its raw-bit offset, then symbols and bits
+// go out (bits into u32 words by atomicOr, little-endian = the reference's LSB-first byte stream).
+__global__ void __launch_bounds__(256) fxv_enc_write(const int16_t* __restrict__ lev, const EncBlk* __restrict__ blk,
+                                                     const uint32_t* __restrict__ scan, const EncHdr* __restrict__ eh,
+                                                     uint8_t* __restrict__ work) {
+    __shared__ uint32_t sv[kMaxCl + 1][257];
+    __shared__ uint32_t base[kMaxCl + 1];
+    __shared__ uint8_t cmap[kRawCtx];
+    const int b = blockIdx.x;
+    const int64_t t = blockIdx.y;
+    const EncHdr& h = eh[t];
+    if (!h.nonzero) return;
+    const int tid = threadIdx.x;
+    if (tid < kRawCtx) cmap[tid] = h.cmap[tid];
+    if (tid <= kMaxCl) {
+        uint32_t pb = 0;
+        if (tid < kMaxCl)
+            for (int k = 0; k < tid; ++k) pb += h.plane_n[k];
+        base[tid] = pb + blk[t * 64 + b].off[tid];
+    }
+    __syncthreads();
+    const int16_t* L = lev + (t * 64 + b) * static_cast<int64_t>(kV);
+    const uint32_t ns = blk[t * 64 + b].nsig;
+    const uint32_t p0 = tid * 16, p1 = min(p0 + 16, ns);
+    uint32_t c[kMaxCl + 1] = {};
+    uint8_t cls[16], cats[16];
+    for (uint32_t pos = p0; pos < p1; ++pos) {
+        const uint32_t e = scan[pos];
+        const int i = e & 0xffff, fsum = (e >> 16) & 0xff, edge = e >> 24;
+        const int cl = cmap[raw_ctx(fsum, nsum_lev(L, i, edge))];
+        const int cat = bitw(static_cast<uint32_t>(abs(static_cast<int>(L[i]))));
+        cls[pos - p0] = static_cast<uint8_t>(cl);
+        cats[pos - p0] = static_cast<uint8_t>(cat);
         ++c[cl];
         c[kMaxCl] += cat;
     }
-    for (int k = 0; k <= kMaxCl; ++k) cnt[b][k] = c[k];
+#pragma unroll
+    for (int k = 0; k <= kMaxCl; ++k) sv[k][tid] = c[k];
     __syncthreads();
-    if (b == 0) {
-        uint32_t run[kMaxCl + 1] = {};
-        for (int bb = 0; bb < 64; ++bb)
-            for (int k = 0; k <= kMaxCl; ++k) {
-                pref[bb][k] = run[k];
-                run[k] += cnt[bb][k];
-            }
-        uint32_t s = 0;
-        for (int k = 0; k < kMaxCl; ++k) {
-            h.plane_n[k] = run[k];
-            pbase[k] = s;
-            s += run[k];
+    if (tid <= kMaxCl) {  // exclusive scan over the threads, one value per thread
+        uint32_t run = 0;
+        for (int k = 0; k < 256; ++k) {
+            const uint32_t v = sv[tid][k];
+            sv[tid][k] = run;
+            run += v;
         }
-        h.nbits = run[kMaxCl];
-        s_nbits = run[kMaxCl];
     }
     __syncthreads();
     uint8_t* syms = work + t * kWorkPerTile;
     uint32_t* W = reinterpret_cast<uint32_t*>(work + t * kWorkPerTile + kSymCap + kEncCap);
-    const uint32_t nwords = (s_nbits + 31) / 32;
-    for (uint32_t k = b; k < nwords; k += 64) W[k] = 0;
-    __syncthreads();
     uint32_t k_cl[kMaxCl];
-    for (int k = 0; k < kMaxCl; ++k) k_cl[k] = pbase[k] + pref[b][k];
-    uint32_t B = pref[b][kMaxCl];
+#pragma unroll
+    for (int k = 0; k < kMaxCl; ++k) k_cl[k] = base[k] + sv[k][tid];
+    uint32_t B = base[kMaxCl] + sv[kMaxCl][tid];
     auto put = [&](uint32_t v, int w) {
         if (w <= 0) return;
         const uint32_t wd = B >> 5, sh = B & 31;
@@ -993,15 +1066,16 @@ __global__ void __launch_bounds__(64) fxv_enc_emit(const int16_t* __restrict__ l
         if (sh + w > 32) atomicOr(&W[wd + 1], v >> (32 - sh));
         B += w;
     };
-    for (uint32_t pos = 0; pos < ns; ++pos) {
-        const uint32_t e = scan[pos];
-        const int i = e & 0xffff, fsum = (e >> 16) & 0xff, edge = e >> 24;
-        const int cl = cmap[raw_ctx(fsum, nsum_lev(L, i, edge))];
-        const int l = L[i];
-        const uint32_t a = static_cast<uint32_t>(abs(l));
-        const int cat = bitw(a);
-        syms[k_cl[cl]++] = static_cast<uint8_t>(cat);
+    for (uint32_t pos = p0; pos < p1; ++pos) {
+        const int cl = cls[pos - p0], cat = cats[pos - p0];
+        uint32_t kk = 0;
+#pragma unroll
+        for (int k = 0; k < kMaxCl; ++k)
+            if (k == cl) kk = k_cl[k]++;
+        syms[kk] = static_cast<uint8_t>(cat);
         if (cat > 0) {
+            const int l = L[scan[pos] & 0xffff];
+            const uint32_t a = static_cast<uint32_t>(abs(l));
             put(a - (1u << (cat - 1)), cat - 1);
             put(l < 0 ? 1u : 0u, 1);
         }
@@ -1026,8 +1100,8 @@ __global__ void fxv_enc_rans(EncHdr* __restrict__ eh, uint8_t* __restrict__ work
     h.enc_len[cl] = 0;
     if (pn == 0) return;
     const uint8_t* s = work + t * kWorkPerTile + sb;
-    uint32_t counts[kNCat] = {};
-    for (uint32_t i = 0; i < pn; ++i) ++counts[s[i]];
+    uint32_t counts[kNCat];
+    for (int k = 0; k < kNCat; ++k) counts[k] = h.cc[cl][k];
     uint32_t freq[kNCat] = {}, cum[kNCat];
     uint32_t assigned = 0;
     int last = -1;
@@ -1058,10 +1132,12 @@ __global__ void fxv_enc_rans(EncHdr* __restrict__ eh, uint8_t* __restrict__ work
         freq[big] += kRansScale - assigned;
     }
     uint32_t cc = 0;
+    uint64_t rcp[kNCat];  // floor(x / f) = umulhi64(x, ceil(2^64 / f)) for x < 2^32, f >= 2
     for (int k = 0; k < kNCat; ++k) {
         cum[k] = cc;
         cc += freq[k];
         h.freq[cl][k] = freq[k];
+        rcp[k] = freq[k] > 1 ? (~0ull / freq[k]) + 1 : 0;
     }
     uint8_t* buf = work + t * kWorkPerTile + kSymCap + eo;
     const uint32_t cap = 2 * pn + 128;
@@ -1073,7 +1149,8 @@ __global__ void fxv_enc_rans(EncHdr* __restrict__ eh, uint8_t* __restrict__ work
             buf[--ptr] = static_cast<uint8_t>(x & 0xffu);
             x >>= 8;
         }
-        x = ((x / f) << 12) + (x % f) + c;
+        const uint32_t qt = f > 1 ? static_cast<uint32_t>(__umul64hi(x, rcp[sym])) : x;
+        x = (qt << 12) + (x - qt * f) + c;
     };
     auto put4 = [&](uint32_t x) {
         ptr -= 4;
@@ -1248,9 +1325,10 @@ CodecStatus FxvCodec::tables(cudaStream_t s) {
     dev_ = dev;
     // frequency-ascending scan, stable within a shell (dct_block.hpp:67-86), and its inverse
     std::vector<uint32_t> scan(kV);
-    std::vector<uint16_t> rank(kV);
+    std::vector<uint16_t> rank(kV + 48);  // then the first scan position of each shell f = 0..46
     int pos = 0;
-    for (int f = 0; f <= 45; ++f)
+    for (int f = 0; f <= 45; ++f) {
+        rank[kV + f] = static_cast<uint16_t>(pos);
         for (int i = 0; i < kV; ++i) {
             const int z = i >> 8, y = (i >> 4) & 15, x = i & 15;
             if (z + y + x != f) continue;
@@ -1259,9 +1337,11 @@ CodecStatus FxvCodec::tables(cudaStream_t s) {
             rank[i] = static_cast<uint16_t>(pos);
             ++pos;
         }
-    if (cudaMalloc(&scan_, kV * 6) != cudaSuccess) return {8, "cudaMalloc: codec tables"};
+    }
+    rank[kV + 46] = rank[kV + 47] = static_cast<uint16_t>(kV);
+    if (cudaMalloc(&scan_, kV * 6 + 96) != cudaSuccess) return {8, "cudaMalloc: codec tables"};
     cudaMemcpyAsync(scan_, scan.data(), kV * 4, cudaMemcpyHostToDevice, s);
-    cudaMemcpyAsync(static_cast<uint8_t*>(scan_) + kV * 4, rank.data(), kV * 2, cudaMemcpyHostToDevice, s);
+    cudaMemcpyAsync(static_cast<uint8_t*>(scan_) + kV * 4, rank.data(), (kV + 48) * 2, cudaMemcpyHostToDevice, s);
     const cudaError_t e = cudaStreamSynchronize(s);
     return e == cudaSuccess ? CodecStatus{} : cerr("codec tables", e);
 }
@@ -1297,10 +1377,13 @@ CodecStatus FxvCodec::decode(const uint8_t* d_blob, const FxvDecTile* tiles, int
         }
         fxv_dec_rans<<<static_cast<unsigned>(nb), 256, 0, s>>>(d_blob, static_cast<DecHdr*>(hdr_),
                                                                 static_cast<uint8_t*>(syms_));
-        fxv_dec_walk<<<static_cast<unsigned>((nb + kWalkTiles - 1) / kWalkTiles), kWalkTiles,
-                       (kV + kWalkTiles * 257) * 4, s>>>(d_blob, static_cast<DecHdr*>(hdr_),
-                                                         static_cast<const uint8_t*>(syms_), scan, p,
-                                                         static_cast<float2*>(ent_), nb);
+        // one serial walker per tile: few tiles per CTA so that small batches still spread over the SMs
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev_);
+        const int tpc = static_cast<int>(std::min<int64_t>(kWalkTiles, std::max<int64_t>(1, (nb + 4 * sms - 1) / (4 * sms))));
+        fxv_dec_walk<<<static_cast<unsigned>((nb + tpc - 1) / tpc), tpc, (kV + tpc * 257) * 4, s>>>(
+            d_blob, static_cast<DecHdr*>(hdr_), static_cast<const uint8_t*>(syms_), scan, p,
+            static_cast<float2*>(ent_), nb);
         launches_ += 2;
         for (int64_t r0 = 0; r0 < nb; r0 += kMaxReconBatch) {
             const int64_t nr = std::min<int64_t>(kMaxReconBatch, nb - r0);
@@ -1337,6 +1420,7 @@ CodecStatus FxvCodec::encode(const uint8_t* src8, const float* src32, int64_t dz
     if (CodecStatus st = tables(s); st.code) return st;
     const uint32_t* scan = static_cast<const uint32_t*>(scan_);
     const uint16_t* rank = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(scan_) + kV * 4);
+    const uint16_t* shell = rank + kV;
     const int64_t B = std::min<int64_t>(kMaxEncBatch, n);
     if (!grow(elev_, elev_cap_, sizeof(int16_t) * kV * 64 * B) || !grow(ecoef_, ecoef_cap_, sizeof(float) * kV * 64 * B) ||
         !grow(eblk_, eblk_cap_, sizeof(EncBlk) * 64 * B) || !grow(ehdr_, ehdr_cap_, sizeof(EncHdr) * B) ||
@@ -1368,12 +1452,14 @@ CodecStatus FxvCodec::encode(const uint8_t* src8, const float* src32, int64_t dz
         fxv_enc_cluster<<<static_cast<unsigned>(nb), 32, 0, s>>>(eh);
         launches_ += 3;
         if (p.rdoq) {
-            fxv_enc_rdoq<<<static_cast<unsigned>(nb), 64, 0, s>>>(lev, coef, blk, scan, eh, p);
+            fxv_enc_rdoq<<<gq, 128, 0, s>>>(lev, coef, blk, scan, shell, eh, p);
             ++launches_;
         }
-        fxv_enc_emit<<<static_cast<unsigned>(nb), 64, 0, s>>>(lev, blk, scan, eh, work);
+        fxv_enc_count<<<gq, 256, 0, s>>>(lev, blk, scan, eh);
+        fxv_enc_prefix<<<static_cast<unsigned>(nb), 64, 0, s>>>(blk, eh, work);
+        fxv_enc_write<<<gq, 256, 0, s>>>(lev, blk, scan, eh, work);
         fxv_enc_rans<<<static_cast<unsigned>((nb * 8 + 127) / 128), 128, 0, s>>>(eh, work, nb);
-        launches_ += 2;
+        launches_ += 4;
         unsigned long long used = 0;
         for (int attempt = 0; attempt < 2; ++attempt) {
             if (!grow(eout_, eout_cap_, out_want)) return {8, "cudaMalloc: encode output"};

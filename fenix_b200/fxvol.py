@@ -125,3 +125,57 @@ def encode_tiles(tiles: np.ndarray, q: float, hf_exp: float = 0.65, dz_frac: flo
                                       out.ctypes.data, cap, offs.ctypes.data_as(C.POINTER(C.c_uint64)),
                                       lens.ctypes.data_as(C.POINTER(C.c_uint32))))
     return [out[int(o):int(o) + int(n_)].tobytes() for o, n_ in zip(offs, lens)]
+
+
+def _sheets(shape) -> np.ndarray:
+    """A prediction-like u8 volume: four bright planar sheets with a linear falloff, zero elsewhere."""
+    z, y, x = np.meshgrid(*(np.arange(s, dtype=np.int64) for s in shape), indexing="ij")
+    v = np.zeros(shape, np.int64)
+    for k, (a, b, c, d) in enumerate([(3, 2, -4, 40), (2, -3, 1, 90), (1, 1, 1, 300), (5, -1, 2, 700)]):
+        dist = np.abs(z * a + y * b + x * c - d - 37 * k) // (2 + k)
+        v = np.maximum(v, np.maximum(0, 255 - dist * 24))
+    return v.astype(np.uint8)
+
+
+def _bench(argv=None) -> None:
+    """python -m fenix_b200.fxvol bench [--size N] [--reps R] [--q Q] [--device D]: archive write
+    (LOD 0 + pyramid) and LOD-0 read of a synthetic prediction-like N^3 volume, best of R, as JSON."""
+    import argparse
+    import json
+    import os
+    import tempfile
+    import time
+
+    ap = argparse.ArgumentParser(prog="python -m fenix_b200.fxvol bench")
+    ap.add_argument("--size", type=int, default=512)
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--q", type=float, default=32.0)
+    ap.add_argument("--device", type=int, default=0)
+    a = ap.parse_args(argv)
+    vol = _sheets((a.size,) * 3)
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "v.fxvol")
+        tw, tr = [], []
+        for _ in range(a.reps + 1):
+            t0 = time.perf_counter()
+            with VolumeArchive.create(path, vol.shape, a.q) as arc:
+                arc.write_volume_u8(vol, a.device)
+            t1 = time.perf_counter()
+            with VolumeArchive.open(path) as arc:
+                back = arc.read_volume_u8(a.device)
+            tr.append(time.perf_counter() - t1)
+            tw.append(t1 - t0)
+        size = os.path.getsize(path)
+    vox = float(vol.size)
+    print(json.dumps({"size": a.size, "q": a.q, "archive_bytes": size, "encode_gvox_s": vox / min(tw[1:]) / 1e9,
+                      "decode_gvox_s": vox / min(tr[1:]) / 1e9,
+                      "mean_abs_err": float(np.abs(back.astype(np.int32) - vol).mean())}))
+
+
+if __name__ == "__main__":
+    import sys
+
+    if len(sys.argv) > 1 and sys.argv[1] == "bench":
+        _bench(sys.argv[2:])
+    else:
+        print("usage: python -m fenix_b200.fxvol bench [--size N] [--reps R] [--q Q] [--device D]")

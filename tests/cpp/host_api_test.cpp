@@ -2,6 +2,9 @@
 //   host_api_test cpu                   — argument grammar, option checks, views, error mapping
 //   host_api_test gpu <weights> <out>   — predict_surface_window and predict_surface_u8 on a
 //                                         synthetic window; writes both outputs to <out>
+//   host_api_test fxvol <in> <out>      — codec::VolumeArchive: open an archive, check its metadata
+//                                         and rewrite every chunk payload of every LOD to <out>
+#include "fenix_b200/codec/archive.hpp"
 #include "fenix_b200/ml/infer.hpp"
 #include "fenix_b200/ml/tiling.hpp"
 #include "fenix_b200_synth.h"
@@ -144,9 +147,49 @@ static int gpu(const char* weights, const char* outpath) {
     return fails ? 1 : 0;
 }
 
+static int fxvol(const char* in, const char* out) {
+    auto a = codec::VolumeArchive::open(in);
+    CHECK(a.has_value());
+    if (!a) return 1;
+    const Extent3 d = a->dims();
+    const auto prm = a->params();
+    CHECK(a->src_dtype() == codec::DType::u8 && a->nlods() >= 1 && prm.q > 0.0f);
+    auto b = codec::VolumeArchive::create(out, d, prm);
+    CHECK(b.has_value());
+    if (!b) return 1;
+    Extent3 ld = d;
+    int real = 0, zero = 0;
+    for (uint32_t lod = 0; lod < a->nlods(); ++lod) {
+        for (s64 z = 0; z < (ld.z + 63) / 64; ++z)
+            for (s64 y = 0; y < (ld.y + 63) / 64; ++y)
+                for (s64 x = 0; x < (ld.x + 63) / 64; ++x) {
+                    const ChunkCoord c{z, y, x};
+                    const auto cov = a->coverage(lod, c);
+                    if (cov == codec::Coverage::Absent) continue;
+                    auto p = a->chunk_payload(lod, c);
+                    CHECK(p.has_value());
+                    if (!p) continue;
+                    CHECK((cov == codec::Coverage::Real) == !p->empty());
+                    (cov == codec::Coverage::Real ? real : zero)++;
+                    CHECK(b->write_chunk_payload(lod, c, *p).has_value());
+                }
+        ld = {(ld.z + 1) / 2, (ld.y + 1) / 2, (ld.x + 1) / 2};
+    }
+    CHECK(b->set_nlods(a->nlods()).has_value());
+    CHECK(b->close().has_value());
+    CHECK(a->close().has_value());
+    CHECK(real > 0);
+    // a missing file is not_found, a corrupt one decode_error
+    auto m = codec::VolumeArchive::open(std::string(out) + ".missing");
+    CHECK(!m && m.error().code == Errc::not_found);
+    std::printf("%s %d %d\n", fails ? "FAIL" : "ok", real, zero);
+    return fails ? 1 : 0;
+}
+
 int main(int argc, char** argv) {
     if (argc >= 2 && std::string_view(argv[1]) == "cpu") return cpu();
+    if (argc >= 4 && std::string_view(argv[1]) == "fxvol") return fxvol(argv[2], argv[3]);
     if (argc >= 4 && std::string_view(argv[1]) == "gpu") return gpu(argv[2], argv[3]);
-    std::fprintf(stderr, "usage: host_api_test cpu | gpu <weights> <out>\n");
+    std::fprintf(stderr, "usage: host_api_test cpu | gpu <weights> <out> | fxvol <in> <out>\n");
     return 2;
 }

@@ -33,6 +33,14 @@ def test_host_api_cpu(host_api_bin):
     assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
 
 
+def test_host_api_fxvol_rewrite(host_api_bin, tmp_path):
+    gold = ROOT / "tests" / "golden" / "fxvol_small.fxvol"
+    out = tmp_path / "rewrite.fxvol"
+    r = subprocess.run([str(host_api_bin), "fxvol", str(gold), str(out)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.startswith("ok"), r.stdout + r.stderr
+    assert out.read_bytes() == gold.read_bytes()
+
+
 @pytest.mark.gpu
 def test_host_api_window_matches_binding(cuda_torch, host_api_bin, tmp_path):
     w = make_plain_unet(tmp_path / "c1.fxweights", CONFIG1_FEATURES, seed=0)
