@@ -345,7 +345,7 @@ def main():
     conv_tflops = prof["conv_flops"] / (prof["conv_ms"] / 1e3) / 1e12
     peak = 2.0 * bf16_burst if args.precision == "fp8" else bf16_burst
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline and (ROOT / "oracle" / "_ref" / "ref_infer").exists():
+    if world == 1 and not args.no_cpu_baseline and (ROOT / "oracle" / "_ref" / "ref_infer").exists():
         try:
             per_tile, thr, sample = cpu_reference(wpath, P, args.overlap)
             tiles = len(fx.tile_starts(S, P, args.overlap)) ** 3
