@@ -43,8 +43,8 @@ struct SmemCtl {
     uint64_t xready[2][2];  // fold epilogue: row exchange of [half][parity] published by its 4 warps
     uint32_t tmem_base;
     int abort;
-    float colscale[kMaxCols];
-    float bias[kMaxCols];
+    alignas(16) float colscale[kMaxCols];
+    alignas(16) float bias[kMaxCols];
 };
 
 __device__ __forceinline__ void unit_coords(const ConvParams& p, int unit, int& b, int& mu, int& nt) {
@@ -280,7 +280,7 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const int c0 = SPLITC ? half : 0;             // first chunk
     const int rb = SPLITC ? 0 : half, rs = SPLITC ? 1 : 2;
     constexpr bool kAccR = kMy <= 2;         // sum over M blocks in registers, one butterfly per unit
-    constexpr int kGrp = kMy <= 4 ? kMy : 1;  // chunks loaded from TMEM per wait
+    constexpr int kGrp = kMy <= 4 ? kMy : (kMy % 4 == 0 ? 4 : 2);  // chunks loaded from TMEM per wait
     constexpr int kR = kAccR ? kMy : 1;
     const bool e4out = p.out_type == kOpE4M3;
     // prenorm: a per-column scale table, or one scale for all columns (the per-channel part then
@@ -438,6 +438,128 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                 }
             }
         }
+        if (threadIdx.x == 64) {
+            FX_TADD(p, 6);
+            FX_TCNT(p, 8, 1);
+        }
+    }
+}
+
+// Epilogue of the transposed convolution (upsample mode, Cout a power of two): column n of the
+// accumulator is phase n / Cout, channel n % Cout. The warp's chunks are read from TMEM four per
+// wait, the phase / channel of each chunk and its byte offset are computed once per unit, and
+// the per-channel scale and bias (the e4m3 output scale folded in) come from shared memory as
+// float4s. Rows map to input voxels; each chunk goes to the phase's output cell of that voxel.
+template <int NCH, bool SPLITC>
+__device__ void epilogue_up(const ConvParams& p, SmemCtl* ctl, int n_units) {
+    const int lane = threadIdx.x & 31;
+    const int wq = (threadIdx.x >> 5) & 3;
+    const int half = ((threadIdx.x >> 5) - 2) >> 2;
+    const uint32_t tbase = ctl->tmem_base;
+    const uint32_t slot_cols = static_cast<uint32_t>(p.R * p.N_tile);
+    const int Mtot = 128 * p.R;
+    RowDecomp rd;
+    rd.P2 = static_cast<uint32_t>(p.Hp * p.Wp);
+    rd.Wp = static_cast<uint32_t>(p.Wp);
+    rd.mP2 = ~0ull / rd.P2 + 1;
+    rd.mWp = ~0ull / rd.Wp + 1;
+    const uint32_t zmax = static_cast<uint32_t>(p.Dp - 2), ymax = static_cast<uint32_t>(p.Hp - 2),
+                   xmax = static_cast<uint32_t>(p.Wp - 2);
+    constexpr int kMy = SPLITC ? NCH / 2 : NCH;
+    constexpr int kCs = SPLITC ? 2 : 1;
+    const int c0 = SPLITC ? half : 0;
+    const int rb = SPLITC ? 0 : half, rs = SPLITC ? 1 : 2;
+    constexpr int kGrp = kMy <= 4 ? kMy : 4;  // chunks read from TMEM per wait
+    const bool e4out = p.out_type == kOpE4M3;
+    const int lc = __ffs(p.cout) - 1;  // log2(Cout)
+    const int64_t oP2 = static_cast<int64_t>(p.oHp) * p.oWp;
+    uint32_t j = 0;
+    for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
+        int b, mu, nt;
+        unit_coords(p, unit, b, mu, nt);
+        const int aslot = j % p.acc_slots;
+        {
+            FX_T0();
+            if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, kWaitLimitNs)) {
+                set_status(p.status, kStatusTimeoutAcc);
+                ctl->abort = 1;
+                return;
+            }
+            if (threadIdx.x == 64) FX_TADD(p, 5);
+        }
+        tc_fence_after();
+        FX_T0();
+        const int64_t q0 = p.row_begin + static_cast<int64_t>(mu) * Mtot;
+        const int cbase = nt * p.N_tile;
+        int32_t cofs[kMy];  // per chunk: its first channel
+        int32_t boff[kMy];  // per chunk: byte offset of its cell from the voxel's phase-0 cell (< 2 GB)
+#pragma unroll
+        for (int c = 0; c < kMy; ++c) {
+            const int n0 = cbase + (c0 + c * kCs) * 16;
+            const int a = n0 >> lc, co0 = n0 - (a << lc);
+            cofs[c] = co0;
+            const int64_t cell = (a >> 2) * oP2 + ((a >> 1) & 1) * static_cast<int64_t>(p.oWp) + (a & 1);
+            boff[c] = static_cast<int32_t>(cell * 16 + static_cast<int64_t>(co0 / (e4out ? 16 : 8)) * p.out_group_stride);
+        }
+        for (int r = rb; r < p.R; r += rs) {
+            const int64_t row = q0 + r * 128 + wq * 32 + lane;
+            uint32_t z, y, x;
+            rd.split(static_cast<uint32_t>(row), z, y, x);
+            const bool valid = row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 && x <= xmax;
+            const uint32_t taddr =
+                tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + r * p.N_tile;
+            uint8_t* ob = nullptr;
+            if (valid)
+                ob = p.out + static_cast<int64_t>(b) * p.out_batch_stride +
+                     ((static_cast<int64_t>(2 * z - 1) * p.oHp + (2 * y - 1)) * p.oWp + (2 * x - 1)) * 16;
+#pragma unroll
+            for (int g0 = 0; g0 < kMy; g0 += kGrp) {
+                uint32_t raw[kGrp][16];
+#pragma unroll
+                for (int c = 0; c < kGrp; ++c) tmem_ld16_nowait(taddr + (c0 + (g0 + c) * kCs) * 16, raw[c]);
+                tmem_wait();
+#pragma unroll
+                for (int c = 0; c < kGrp; ++c) tmem_regs_ready(raw[c]);
+                if (!valid) continue;
+#pragma unroll
+                for (int c = 0; c < kGrp; ++c) {
+                    const int ci = g0 + c;
+                    const float4* cs4 = reinterpret_cast<const float4*>(ctl->colscale + cofs[ci]);
+                    const float4* bs4 = reinterpret_cast<const float4*>(ctl->bias + cofs[ci]);
+                    float v[16];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 cs = cs4[q], bs = bs4[q];
+                        v[4 * q + 0] = fmaf(__uint_as_float(raw[c][4 * q + 0]), cs.x, bs.x);
+                        v[4 * q + 1] = fmaf(__uint_as_float(raw[c][4 * q + 1]), cs.y, bs.y);
+                        v[4 * q + 2] = fmaf(__uint_as_float(raw[c][4 * q + 2]), cs.z, bs.z);
+                        v[4 * q + 3] = fmaf(__uint_as_float(raw[c][4 * q + 3]), cs.w, bs.w);
+                    }
+                    if (p.amax) {
+                        float mx = 0.f;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(v[i]));
+                        if (e4out) mx /= p.out_qscale;
+                        atomicMax(p.amax, __float_as_uint(mx));
+                    }
+                    uint8_t* o = ob + boff[ci];
+                    if (e4out) {
+                        uint4 w;
+                        w.x = pack_e4m3x4(v[0], v[1], v[2], v[3]);
+                        w.y = pack_e4m3x4(v[4], v[5], v[6], v[7]);
+                        w.z = pack_e4m3x4(v[8], v[9], v[10], v[11]);
+                        w.w = pack_e4m3x4(v[12], v[13], v[14], v[15]);
+                        *reinterpret_cast<uint4*>(o) = w;
+                    } else {
+                        *reinterpret_cast<uint4*>(o) = pack_cell16(v, p.out_type);
+                        *reinterpret_cast<uint4*>(o + p.out_group_stride) = pack_cell16(v + 8, p.out_type);
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl->acce[aslot]));
         if (threadIdx.x == 64) {
             FX_TADD(p, 6);
             FX_TCNT(p, 8, 1);
@@ -705,6 +827,17 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             case 1: epilogue_fold<1, false>(p, ctl, xbuf, n_units); break;
             case 2: sc ? epilogue_fold<2, true>(p, ctl, xbuf, n_units) : epilogue_fold<2, false>(p, ctl, xbuf, n_units); break;
             case 4: sc ? epilogue_fold<4, true>(p, ctl, xbuf, n_units) : epilogue_fold<4, false>(p, ctl, xbuf, n_units); break;
+            default: break;  // rejected on the host (launch_conv_tc)
+        }
+    } else if (p.mode == kModeUpsample && p.cout >= 16 && (p.cout & (p.cout - 1)) == 0 &&
+               (static_cast<int64_t>(p.cout / 8) * p.out_group_stride +
+                static_cast<int64_t>(p.oHp + 1) * p.oWp * 16) < (1ll << 31)) {  // 32-bit chunk offsets
+        const bool sc = p.R == 1;
+        switch (p.N_tile / 16) {
+            case 2: sc ? epilogue_up<2, true>(p, ctl, n_units) : epilogue_up<2, false>(p, ctl, n_units); break;
+            case 4: sc ? epilogue_up<4, true>(p, ctl, n_units) : epilogue_up<4, false>(p, ctl, n_units); break;
+            case 8: sc ? epilogue_up<8, true>(p, ctl, n_units) : epilogue_up<8, false>(p, ctl, n_units); break;
+            case 16: epilogue_up<16, true>(p, ctl, n_units); break;
             default: break;  // rejected on the host (launch_conv_tc)
         }
     } else {
