@@ -41,6 +41,7 @@ struct SmemCtl {
     uint64_t acce[2];
     uint64_t drain;
     uint64_t xready[2][2];  // fold epilogue: row exchange of [half][parity] published by its 4 warps
+    uint64_t bres;          // z-plane fold: the resident weights have landed
     uint32_t tmem_base;
     int abort;
     alignas(16) float colscale[kMaxCols];
@@ -54,16 +55,42 @@ __device__ __forceinline__ void unit_coords(const ConvParams& p, int unit, int& 
     b = t / p.n_units_m;
 }
 
+// First output row of M unit mu. z-plane fold: unit = (group of R planes, 128-row segment of the
+// plane's interior rows), its block r at + r * plane; otherwise R consecutive blocks of rows.
+__device__ __forceinline__ int64_t unit_q0(const ConvParams& p, int mu) {
+    if (p.zfold) {
+        const int64_t P2 = static_cast<int64_t>(p.Hp) * p.Wp;
+        const int zg = mu / p.zseg, seg = mu - zg * p.zseg;
+        const int S = p.R / p.zplanes;
+        return (1 + static_cast<int64_t>(zg) * p.zplanes) * P2 + (p.Wp + 1) + static_cast<int64_t>(seg) * 128 * S;
+    }
+    return p.row_begin + static_cast<int64_t>(mu) * p.block_rows * p.R;
+}
+
 // Producer warp: the whole warp walks the program (warp-uniform control flow); one elected lane
 // issues the bulk copies of every stage of every unit.
 __device__ void producer_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n_units) {
     const bool leader = elect_one();
     uint32_t k = 0;  // global stage counter
-    const int64_t Mtot = static_cast<int64_t>(p.block_rows) * p.R;
+    if (p.zfold) {  // the weights of every tap, once per CTA
+        if (leader) {
+            mbar_arrive_expect_tx(smem_u32(&ctl->bres), static_cast<uint32_t>(p.bres_bytes));
+            bulk_g2s(smem_u32(smem + p.bres_off), p.wpack, static_cast<uint32_t>(p.bres_bytes), smem_u32(&ctl->bres));
+        }
+        __syncwarp();
+        const bool ok = mbar_wait(smem_u32(&ctl->bres), 0u, nullptr, kWaitLimitNs);
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (leader) {
+                set_status(p.status, kStatusTimeoutDrain);
+                ctl->abort = 1;
+            }
+            return;
+        }
+    }
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
         int b, mu, nt;
         unit_coords(p, unit, b, mu, nt);
-        const int64_t q0 = p.row_begin + static_cast<int64_t>(mu) * Mtot;
+        const int64_t q0 = unit_q0(p, mu);
         for (int s = 0; s < p.n_stages; ++s, ++k) {
             const int slot = k % p.n_pipe;
             const uint32_t ph = (k / p.n_pipe) & 1u;
@@ -226,6 +253,124 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
     __syncwarp();
 }
 
+// MMA warp of the z-plane fold: stage j of a unit holds input plane j - 1 relative to the unit's
+// first block plane; each program entry (ky, kx, group pair) and segment is one A tile that feeds
+// block (segment, j - kz) with tap kz for every kz in [max(0, j - Z + 1), min(2, j)] — one
+// collector fill, up to two reuses; the segments alternate, so consecutive MMAs hit different
+// accumulators. The first MMA into a block (kz = 0, first entry) starts its accumulator. The issue
+// stream is the bound of this loop, so the stages are unrolled (Z and S compile-time: each stage's
+// tap range is a constant) and one elected thread issues while the warp waits.
+template <bool F8, int Z>
+__device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n_units) {
+    constexpr int S = 2;
+    const bool leader = elect_one();
+    uint32_t k = 0;
+    uint32_t j = 0;
+    const uint32_t tbase = ctl->tmem_base;
+    const uint32_t ncol = static_cast<uint32_t>(p.N_tile);
+    const uint32_t slot_cols = static_cast<uint32_t>(S * Z) * ncol;
+    const uint32_t smem_base = smem_u32(smem);
+    const uint64_t hi = (static_cast<uint64_t>(128 >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
+    const uint64_t b_lbo = static_cast<uint64_t>((p.N_tile * 16) >> 4) << 16;
+    const uint32_t idesc = instr_desc(128, p.N_tile, p.optype);
+    const uint64_t bres = (hi | b_lbo) + ((smem_base + static_cast<uint32_t>(p.bres_off)) >> 4);
+    const uint64_t kzs = static_cast<uint64_t>(p.zkstride >> 4);
+    const int nent = p.n_mmas;
+    {
+        const bool ok = mbar_wait(smem_u32(&ctl->bres), 0u, &ctl->abort, kWaitLimitNs);
+        if (!__all_sync(0xffffffffu, ok)) {
+            if (leader) {
+                set_status(p.status, kStatusTimeoutFull);
+                ctl->abort = 1;
+            }
+            n_units = 0;  // issue nothing; fall through to the drain
+        }
+    }
+    tc_fence_after();
+    for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
+        const int aslot = j % p.acc_slots;
+        const uint32_t aph = (j / p.acc_slots) & 1u;
+        {
+            FX_T0();
+            const bool ok = mbar_wait(smem_u32(&ctl->acce[aslot]), aph ^ 1u, &ctl->abort, kWaitLimitNs);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (leader) {
+                    set_status(p.status, kStatusTimeoutAccFree);
+                    ctl->abort = 1;
+                }
+                break;
+            }
+            if (leader) FX_TADD(p, 2);
+        }
+        tc_fence_after();
+        const uint32_t dcol0 = tbase + aslot * slot_cols;
+        bool aborted = false;
+#pragma unroll
+        for (int s = 0; s < Z + 2; ++s, ++k) {
+            const int slot = k % p.n_pipe;
+            {
+                FX_T0();
+                const bool ok =
+                    mbar_wait(smem_u32(&ctl->full[slot]), (k / p.n_pipe) & 1u, &ctl->abort, kWaitLimitNs);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    if (leader) {
+                        set_status(p.status, kStatusTimeoutFull);
+                        ctl->abort = 1;
+                    }
+                    aborted = true;
+                    break;
+                }
+                if (leader) FX_TADD(p, 3);
+            }
+            tc_fence_after();
+            FX_T0();
+            const int kz_lo = s - (Z - 1) > 0 ? s - (Z - 1) : 0;  // constants once s is unrolled
+            const int nz = (s < 2 ? s : 2) - kz_lo + 1;
+            if (leader) {
+                const uint64_t ahi = hi + ((smem_base + static_cast<uint32_t>(slot * p.stage_bytes)) >> 4);
+                const uint64_t bbase = bres + static_cast<uint64_t>(kz_lo) * kzs;
+                const uint32_t dbase = dcol0 + static_cast<uint32_t>(s - kz_lo) * ncol;
+                for (int e = 0; e < nent; ++e) {
+                    const ConvMma mm = p.mmas[e];
+                    const uint32_t acc = (kz_lo == 0 && e == 0) ? 0u : 1u;
+                    const uint64_t bb = bbase + mm.b;
+                    const uint64_t a0 = ahi + mm.a;
+#pragma unroll
+                    for (int sg = 0; sg < S; ++sg) {
+                        const uint64_t ad = a0 + static_cast<uint64_t>(sg * 128);
+                        const uint32_t d0 = dbase + static_cast<uint32_t>(sg * Z) * ncol;
+                        if (nz == 3) {
+                            if (F8) mmaz3_f8_if(1u, d0, d0 - ncol, d0 - 2 * ncol, ad, bb, bb + kzs, bb + 2 * kzs, idesc, acc, 1u, 1u);
+                            else mmaz3_f16_if(1u, d0, d0 - ncol, d0 - 2 * ncol, ad, bb, bb + kzs, bb + 2 * kzs, idesc, acc, 1u, 1u);
+                        } else if (nz == 2) {
+                            if (F8) mmaz2_f8_if(1u, d0, d0 - ncol, ad, bb, bb + kzs, idesc, acc, 1u);
+                            else mmaz2_f16_if(1u, d0, d0 - ncol, ad, bb, bb + kzs, idesc, acc, 1u);
+                        } else {
+                            if (F8) mma_f8_if(1u, d0, ad, bb, idesc, acc);
+                            else mma_f16_if(1u, d0, ad, bb, idesc, acc);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->empty[slot]));
+            if (leader) {
+                FX_TADD(p, 4);
+                FX_TCNT(p, 7, nent * S * nz);
+            }
+        }
+        if (aborted) break;
+        mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->accf[aslot]));
+    }
+    mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->drain));
+    if (leader) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+    }
+    __syncwarp();
+}
+
 // Butterfly "transpose-reduce" over 16 channels: on entry each lane holds 16 per-channel values
 // of its row; on exit lane l holds the sum over all 32 lanes of channel (l & 15).
 __device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16], int lane) {
@@ -266,7 +411,8 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const int half = ((threadIdx.x >> 5) - 2) >> 2;   // which of the two warps of the quarter
     const uint32_t tbase = ctl->tmem_base;
     const uint32_t slot_cols = static_cast<uint32_t>(p.R * p.N_tile);
-    const int Mtot = 128 * p.R;
+    const int64_t P2r = static_cast<int64_t>(p.Hp) * p.Wp;
+    const int zpl = p.zfold ? p.zplanes : 1;
     RowDecomp rd;
     rd.P2 = static_cast<uint32_t>(p.Hp * p.Wp);
     rd.Wp = static_cast<uint32_t>(p.Wp);
@@ -304,7 +450,10 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         }
         tc_fence_after();
         FX_T0();
-        const int64_t q0 = p.row_begin + static_cast<int64_t>(mu) * Mtot;
+        const int64_t q0 = unit_q0(p, mu);
+        // z-plane fold: block r owns plane zb + r only (a segment longer than a small plane's
+        // interior reaches into the next plane, whose rows its own block counts)
+        const uint32_t zb = p.zfold ? 1u + static_cast<uint32_t>((mu / p.zseg) * p.zplanes) : 0u;
         const int cbase = nt * p.N_tile;  // first global column of this tile
         float s1[kMy], s2[kMy];
         float r1[kR][16], r2[kR][16];
@@ -315,10 +464,13 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
         for (int r = rb; r < p.R; r += rs) {
-            const int64_t row = q0 + r * 128 + wq * 32 + lane;
+            // M block r: rows q0 + 128 r, or (z-plane fold) segment r / zplanes of plane r % zplanes
+            const int rz = p.zfold ? r % zpl : 0;
+            const int64_t row = q0 + (p.zfold ? (r / zpl) * 128 + rz * P2r : static_cast<int64_t>(r) * 128) + wq * 32 + lane;
             uint32_t z, y, x;
             rd.split(static_cast<uint32_t>(row), z, y, x);
-            const bool valid = row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 && x <= xmax;
+            const bool valid = row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 && x <= xmax &&
+                               (!p.zfold || z == zb + static_cast<uint32_t>(rz));
             const uint32_t taddr =
                 tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + r * p.N_tile;
             // upsample: phase-0 output cell of this input voxel (2z-1, 2y-1, 2x-1 in the padded grid)
@@ -776,6 +928,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             mbar_init(smem_u32(&ctl->acce[i]), kEpiWarps);
         }
         mbar_init(smem_u32(&ctl->drain), 1);
+        mbar_init(smem_u32(&ctl->bres), 1);
         for (int h = 0; h < 2; ++h)
             for (int q = 0; q < 2; ++q) mbar_init(smem_u32(&ctl->xready[h][q]), 4);
         ctl->abort = 0;
@@ -800,6 +953,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
 
     if (warp == 0) {
         producer_loop(p, smem, ctl, n_units);
+    } else if (warp == 1 && p.zfold) {
+        const bool f8 = p.optype == kOpE4M3;
+        if (p.zplanes == 4) f8 ? mma_loop_z<true, 4>(p, smem, ctl, n_units) : mma_loop_z<false, 4>(p, smem, ctl, n_units);
+        else f8 ? mma_loop_z<true, 2>(p, smem, ctl, n_units) : mma_loop_z<false, 2>(p, smem, ctl, n_units);
     } else if (warp == 1 && p.fold) {
         const bool f8 = p.optype == kOpE4M3;
         switch (p.R) {
@@ -888,6 +1045,14 @@ cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cud
         need += conv_tc_fold_bytes(nf);
     } else if (p.block_rows != 128) {
         return cudaErrorInvalidValue;
+    }
+    if (p.zfold) {
+        if (p.fold || p.mode != kModePrenorm || p.n_tiles != 1 || !(p.R == 2 || p.R == 4 || p.R == 8) ||
+            !(p.zplanes == 2 || p.zplanes == 4) || p.R != 2 * p.zplanes || p.zseg <= 0 || p.n_stages != p.zplanes + 2 || p.n_mmas <= 0 || p.bres_off % 128 || p.bres_bytes % 16 ||
+            p.bres_bytes <= 0 || p.zkstride <= 0 || p.zkstride % 16 || static_cast<size_t>(p.bres_off) < need ||
+            p.acc_slots * p.R * p.N_tile > static_cast<int>(p.tmem_cols))
+            return cudaErrorInvalidValue;
+        need = static_cast<size_t>(p.bres_off) + p.bres_bytes;
     }
     if (smem_bytes < need || smem_bytes > 232448) return cudaErrorInvalidValue;
     count_launch();

@@ -45,8 +45,9 @@ Status upload(T*& dst, const std::vector<T>& v, Net* /*unused*/, std::vector<voi
 }  // namespace
 
 size_t DevProgram::smem() const {
-    return static_cast<size_t>(host.n_pipe) * host.stage_bytes + fxk::conv_tc_ctl_bytes() +
-           (fold ? fxk::conv_tc_fold_bytes(N_tile / 3) : 0);
+    const size_t base = static_cast<size_t>(host.n_pipe) * host.stage_bytes + fxk::conv_tc_ctl_bytes() +
+                        (fold ? fxk::conv_tc_fold_bytes(N_tile / 3) : 0);
+    return zfold ? (base + 127) / 128 * 128 + host.bres_bytes : base;
 }
 
 Status cuda_status(cudaError_t e, const char* what) {
@@ -332,6 +333,13 @@ static bool fold_enabled() {
     return v && v[0] == '1';
 }
 
+// z-plane fold (fxk::ConvParams::zfold) for 3x3x3 stride-1 convs of at most 64 output channels
+// whose weights fit in shared memory next to three stages; FENIX_B200_CONV_ZFOLD=0 turns it off.
+static bool zfold_enabled() {
+    const char* v = std::getenv("FENIX_B200_CONV_ZFOLD");
+    return !(v && v[0] == '0');
+}
+
 Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax, int sm_count,
                            std::vector<void*>& allocs_) {
     DevProgram& dp = L.prog[q];
@@ -392,6 +400,12 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
                 for (int ky = 0; ky < 3; ++ky)
                     for (int kx = 0; kx < 3; ++kx)
                         sp.taps.push_back({0, (kz - 1) * P2 + (ky - 1) * Wp + (kx - 1), kz * 9 + ky * 3 + kx, kz});
+            const int64_t bres = 27LL * (sp.G / 2) * L.Cout * 32;
+            if (zfold_enabled() && L.Cout <= 64 && sp.G % 2 == 0 && bres <= 112 * 1024 && gin.D >= 2) {
+                sp.zfold = true;
+                sp.zWp = Wp;
+                sp.zP2 = P2;
+            }
         } else {
             const int64_t Wp = gout.W + 2, P2 = static_cast<int64_t>(gout.H + 2) * Wp;
             for (int kz = 0; kz < 3; ++kz)
@@ -478,6 +492,41 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     }
     // tiling of N and M
     const int N_total = sp.N_total;
+    if (sp.zfold) {  // one N tile; 2 segments x Z planes (Z 4 at N 32, 2 at N 64); 2 TMEM slots
+        const ActGeom& g = gout;
+        const int S = 2, Zp = N_total <= 32 ? 4 : 2, R = S * Zp;
+        const int64_t Wp = g.W + 2, P2 = static_cast<int64_t>(g.H + 2) * Wp;
+        const int zseg = static_cast<int>((P2 - 2 * (Wp + 1) + 128 * S - 1) / (128 * S));
+        sp.N_tile = N_total;
+        sp.R = Zp;
+        sp.zsegs = S;
+        sp.block_rows = 128;
+        Program zp;
+        std::string zerr = build_program(sp, zp);
+        if (zerr.empty()) {
+            dp.host = std::move(zp);
+            dp.R = R;
+            dp.N_tile = N_total;
+            dp.acc_slots = 2;
+            uint32_t cols = 32;
+            while (cols < static_cast<uint32_t>(2 * R * N_total)) cols <<= 1;
+            dp.tmem_cols = cols;
+            dp.zseg = zseg;
+            dp.zplanes = Zp;
+            dp.n_units_m = static_cast<int>((g.D + Zp - 1) / Zp) * zseg;
+            dp.zfold = true;
+            dp.fold = false;
+            dp.block_rows = 128;
+            dp.optype = q;
+            Status zst;
+            if ((zst = upload(dp.wpack, dp.host.wpack, this_net, allocs_)).code) return zst;
+            if ((zst = upload(dp.colscale, colscale, this_net, allocs_)).code) return zst;
+            if ((zst = upload(dp.ratio, ratio, this_net, allocs_)).code) return zst;
+            dp.built = true;
+            return ok();
+        }
+        sp.zfold = false;  // weights do not fit next to three stages: the regular program
+    }
     int N_tile = N_total <= 256 ? N_total : (N_total == 320 ? 320 : 256);
     if (N_total % N_tile) return fail(kUnsupported, L.name + ": output width " + std::to_string(N_total) + " not tileable");
     int R = N_tile <= 32 ? 8 : (N_tile <= 64 ? 4 : (N_tile <= 128 ? 2 : 1));
@@ -731,6 +780,15 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     p.R = dp.R;
     p.block_rows = dp.block_rows;
     p.fold = dp.fold ? 1 : 0;
+    p.zfold = dp.zfold ? 1 : 0;
+    if (dp.zfold) {
+        p.zseg = dp.zseg;
+        p.zplanes = dp.zplanes;
+        p.zkstride = dp.host.zkstride;
+        p.bres_bytes = dp.host.bres_bytes;
+        p.bres_off = static_cast<int32_t>((static_cast<size_t>(dp.host.n_pipe) * dp.host.stage_bytes +
+                                           fxk::conv_tc_ctl_bytes() + 127) / 128 * 128);
+    }
     p.n_units_m = dp.n_units_m;
     p.n_tiles = dp.host.n_tiles;
     p.N_tile = dp.N_tile;

@@ -56,6 +56,9 @@ struct DevProgram {
     ActGeom rowspace;  // output grid (conv) or input grid (transposed conv)
     int optype = 0;    // fxk::OpType of the operands
     bool fold = false;     // x-tap fold (fxk::ConvParams::fold)
+    bool zfold = false;    // z-plane fold (fxk::ConvParams::zfold)
+    int zseg = 0;          // z-plane fold: units per plane
+    int zplanes = 0;       // z-plane fold: planes per unit
     int block_rows = 128;
     bool built = false;
     size_t smem() const;

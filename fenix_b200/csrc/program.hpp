@@ -33,6 +33,12 @@ struct ProgramSpec {
     int block_rows = 128;  // window rows advanced per M block (126 with the x-tap fold)
     bool pair_taps = false;  // G == 1: the two K-halves of one MMA come from two taps
     std::vector<Tap> taps;
+    // z-plane fold (3x3x3 stride 1): the R M blocks of a unit lie one z plane apart, each stage
+    // holds one input plane's window, and its A tiles feed up to three blocks (taps kz = 0, 1, 2);
+    // the weights stay resident in shared memory. zWp / zP2: padded row and plane of the grid.
+    bool zfold = false;
+    int64_t zWp = 0, zP2 = 0;
+    int zsegs = 2;  // z-plane fold: adjacent 128-row segments per unit (R = planes per segment)
     // B value for output column n, input channel ci (0 <= ci < G*cg), tap key
     std::function<float(int n, int ci, int wkey)> wval;
     int smem_total = 212 * 1024;  // stage buffers; the control block takes the rest
@@ -45,6 +51,8 @@ struct Program {
     int64_t wtile_bytes = 0;
     int stage_bytes = 0, stage_a_bytes = 0, n_pipe = 0;
     int n_tiles = 0;
+    int bres_bytes = 0;  // z-plane fold: resident weights (all taps), 0 otherwise
+    int zkstride = 0;    // z-plane fold: bytes between the weight blocks of taps kz and kz + 1
 };
 
 // e4m3 encode with round-to-nearest-even and saturation to +-448 (finite), host side.
@@ -123,8 +131,80 @@ inline fxk::ConvMma pack_mma(int64_t a_off, int64_t lbo, int64_t b_off) {
     return m;
 }
 
+// z-plane fold program (see ProgramSpec::zfold). Stage j = 0 .. R+1 stages input plane
+// z0 + j - 1 of the unit: rows [-(Wp+1), 128 S + Wp + 1) around the unit's S adjacent (y, x)
+// segments, all groups. Its MMA entries are the 9 (ky, kx) shifts x group pairs; the kernel issues
+// each entry for every segment (A + 128 rows per segment) and every kz with 0 <= j - kz < R into
+// block (segment, j - kz), weights (kz, entry) at entry.b + kz * zkstride of the resident region.
+// Returns "" on success.
+inline std::string build_zfold_program(const ProgramSpec& s, Program& pg) {
+    if (s.N_tile != s.N_total || s.N_tile > 256 || s.N_tile % 16) return "zfold: one N tile of at most 256 columns";
+    if (s.G % 2) return "zfold: group count must be even";
+    const int64_t Wp = s.zWp;
+    const int rows = static_cast<int>(128 * s.zsegs + 2 * (Wp + 1));
+    const int bblk = s.N_tile * 32;
+    const int nent = 9 * (s.G / 2);
+    pg.bres_bytes = 3 * nent * bblk;
+    pg.zkstride = nent * bblk;
+    const int sb = rows * s.G * 16;
+    pg.stage_bytes = (sb + 127) / 128 * 128;
+    pg.stage_a_bytes = pg.stage_bytes;
+    const int avail = s.smem_total - pg.bres_bytes;
+    pg.n_pipe = std::min(8, avail / std::max(pg.stage_bytes, 1));
+    if (pg.n_pipe < 3) return "zfold: resident weights leave fewer than 3 stages";
+    pg.n_tiles = 1;
+    pg.stages.clear();
+    pg.mmas.clear();
+    for (int ky = 0; ky < 3; ++ky)
+        for (int kx = 0; kx < 3; ++kx)
+            for (int gp = 0; gp < s.G; gp += 2) {
+                const int e = static_cast<int>(pg.mmas.size());
+                const int64_t a_off = static_cast<int64_t>(gp) * rows * 16 + (ky * Wp + kx) * 16;
+                pg.mmas.push_back(pack_mma(a_off, static_cast<int64_t>(rows) * 16, static_cast<int64_t>(e) * bblk));
+            }
+    for (int j = 0; j < s.R + 2; ++j) {
+        fxk::ConvStage st{};
+        st.src = 0;
+        st.row_off = static_cast<int32_t>((j - 1) * s.zP2 - (Wp + 1));
+        st.rows = rows;
+        st.g0 = 0;
+        st.ng = s.G;
+        st.b_off = 0;
+        st.b_bytes = 0;
+        st.mma_begin = 0;
+        st.mma_count = nent;
+        pg.stages.push_back(st);
+    }
+    for (const auto& m : pg.mmas)
+        if ((m.a & 0xFFFFu) >= 0x4000u || (m.a >> 16) >= 0x4000u || m.b >= 0x4000u) return "zfold: smem offset overflow";
+    // resident weights: [kz][ky][kx][group pair] blocks, each [K half][N_tile][16 B] as in build_program
+    pg.wtile_bytes = pg.bres_bytes;
+    pg.wpack.assign(static_cast<size_t>(pg.bres_bytes), 0);
+    for (int kz = 0; kz < 3; ++kz)
+        for (int e = 0; e < nent; ++e) {
+            const int kyx = e / (s.G / 2), gp = (e % (s.G / 2)) * 2;
+            const int wk = kz * 9 + kyx;  // ky * 3 + kx == kyx
+            uint8_t* blk = pg.wpack.data() + static_cast<size_t>(kz * nent + e) * bblk;
+            for (int h = 0; h < 2; ++h)
+                for (int n = 0; n < s.N_tile; ++n) {
+                    uint8_t* row = blk + (static_cast<size_t>(h) * s.N_tile + n) * 16;
+                    for (int jj = 0; jj < s.cg; ++jj) {
+                        const float v = s.wval(n, (gp + h) * s.cg + jj, wk);
+                        if (s.elem == 2) {
+                            const uint16_t b = s.optype == 2 ? float_to_f16(v) : float_to_bf16(v);
+                            std::memcpy(row + 2 * jj, &b, 2);
+                        } else {
+                            row[jj] = float_to_e4m3(v);
+                        }
+                    }
+                }
+        }
+    return {};
+}
+
 // Returns "" on success.
 inline std::string build_program(const ProgramSpec& s, Program& pg) {
+    if (s.zfold) return build_zfold_program(s, pg);
     if (s.N_tile <= 0 || s.N_tile % 16 || s.N_total % s.N_tile) return "program: bad N tiling";
     if (s.N_tile > 256 && s.N_tile != 320) return "program: N tile > 256 must be 320";
     if (!s.pair_taps && (s.G % 2)) return "program: group count must be even";

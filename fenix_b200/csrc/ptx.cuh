@@ -174,6 +174,46 @@ __device__ __forceinline__ void mma3_f8_if(uint32_t issue, uint32_t d0, uint32_t
     FX_MMA3("f8f6f4");
 }
 #undef FX_MMA3
+// Two or three MMAs sharing one A tile through the A collector, each with its own accumulate flag
+// (z-plane fold: the first MMA into a block starts it).
+#define FX_MMAZ2(KIND)                                                                                          \
+    asm volatile(                                                                                               \
+        "{\n\t.reg .pred p0, p1, q;\n\tsetp.ne.b32 p0, %5, 0;\n\tsetp.ne.b32 p1, %6, 0;\n\t"                  \
+        "setp.ne.b32 q, %7, 0;\n\t"                                                                              \
+        "@q tcgen05.mma.cta_group::1.kind::" KIND ".collector::a::fill [%0], %2, %3, %8, p0;\n\t"              \
+        "@q tcgen05.mma.cta_group::1.kind::" KIND ".collector::a::lastuse [%1], %2, %4, %8, p1;\n\t}"          \
+        ::"r"(d0), "r"(d1), "l"(a_desc), "l"(b0), "l"(b1), "r"(acc0), "r"(acc1), "r"(issue), "r"(idesc)      \
+        : "memory")
+#define FX_MMAZ3(KIND)                                                                                          \
+    asm volatile(                                                                                               \
+        "{\n\t.reg .pred p0, p1, p2, q;\n\tsetp.ne.b32 p0, %7, 0;\n\tsetp.ne.b32 p1, %8, 0;\n\t"            \
+        "setp.ne.b32 p2, %9, 0;\n\tsetp.ne.b32 q, %10, 0;\n\t"                                                 \
+        "@q tcgen05.mma.cta_group::1.kind::" KIND ".collector::a::fill [%0], %3, %4, %11, p0;\n\t"             \
+        "@q tcgen05.mma.cta_group::1.kind::" KIND ".collector::a::use [%1], %3, %5, %11, p1;\n\t"              \
+        "@q tcgen05.mma.cta_group::1.kind::" KIND ".collector::a::lastuse [%2], %3, %6, %11, p2;\n\t}"         \
+        ::"r"(d0), "r"(d1), "r"(d2), "l"(a_desc), "l"(b0), "l"(b1), "l"(b2), "r"(acc0), "r"(acc1), "r"(acc2), \
+        "r"(issue), "r"(idesc)                                                                                  \
+        : "memory")
+__device__ __forceinline__ void mmaz2_f16_if(uint32_t issue, uint32_t d0, uint32_t d1, uint64_t a_desc, uint64_t b0,
+                                             uint64_t b1, uint32_t idesc, uint32_t acc0, uint32_t acc1) {
+    FX_MMAZ2("f16");
+}
+__device__ __forceinline__ void mmaz2_f8_if(uint32_t issue, uint32_t d0, uint32_t d1, uint64_t a_desc, uint64_t b0,
+                                            uint64_t b1, uint32_t idesc, uint32_t acc0, uint32_t acc1) {
+    FX_MMAZ2("f8f6f4");
+}
+__device__ __forceinline__ void mmaz3_f16_if(uint32_t issue, uint32_t d0, uint32_t d1, uint32_t d2, uint64_t a_desc,
+                                             uint64_t b0, uint64_t b1, uint64_t b2, uint32_t idesc, uint32_t acc0,
+                                             uint32_t acc1, uint32_t acc2) {
+    FX_MMAZ3("f16");
+}
+__device__ __forceinline__ void mmaz3_f8_if(uint32_t issue, uint32_t d0, uint32_t d1, uint32_t d2, uint64_t a_desc,
+                                            uint64_t b0, uint64_t b1, uint64_t b2, uint32_t idesc, uint32_t acc0,
+                                            uint32_t acc1, uint32_t acc2) {
+    FX_MMAZ3("f8f6f4");
+}
+#undef FX_MMAZ2
+#undef FX_MMAZ3
 __device__ __forceinline__ void mma_commit_if(uint32_t issue, uint32_t bar) {
     asm volatile(
         "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
