@@ -255,11 +255,15 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
 
 // MMA warp of the z-plane fold: stage j of a unit holds input plane j - 1 relative to the unit's
 // first block plane; each program entry (ky, kx, group pair) and segment is one A tile that feeds
-// block (segment, j - kz) with tap kz for every kz in [max(0, j - Z + 1), min(2, j)] — one
-// collector fill, up to two reuses; the segments alternate, so consecutive MMAs hit different
-// accumulators. The first MMA into a block (kz = 0, first entry) starts its accumulator. The issue
-// stream is the bound of this loop, so the stages are unrolled (Z and S compile-time: each stage's
-// tap range is a constant) and one elected thread issues while the warp waits.
+// block (segment, j - kz) with tap kz for every kz in [kz_lo, kz_hi] = [max(0, j - Z + 1), min(2, j)].
+// Those taps are ONE MMA of N = (kz_hi - kz_lo + 1) N_tile: the resident weights hold the three kz
+// taps of an entry as consecutive rows of B, and the blocks of a segment sit at descending TMEM
+// columns (plane p at (Z - 1 - p) N_tile), so accumulator columns [kz N_tile, (kz + 1) N_tile) of
+// the MMA are plane j - kz's. The first entry of a stage with kz_lo = 0 is split in two: plane j
+// starts its accumulator with tap 0 alone while the planes below keep accumulating. The segments
+// alternate, so consecutive MMAs hit different accumulators. The issue stream is the bound of this
+// loop, so the stages are unrolled (Z and S compile-time: each stage's tap range is a constant) and
+// one elected thread issues while the warp waits.
 template <bool F8, int Z>
 __device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n_units) {
     constexpr int S = 2;
@@ -271,10 +275,14 @@ __device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int
     const uint32_t slot_cols = static_cast<uint32_t>(S * Z) * ncol;
     const uint32_t smem_base = smem_u32(smem);
     const uint64_t hi = (static_cast<uint64_t>(128 >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
-    const uint64_t b_lbo = static_cast<uint64_t>((p.N_tile * 16) >> 4) << 16;
-    const uint32_t idesc = instr_desc(128, p.N_tile, p.optype);
+    // resident weights: per entry [K half][kz 0..2][N_tile rows][16 B]; taps kz_lo.. of one MMA are
+    // consecutive rows of B, so the K-half stride (LBO) spans all three
+    const uint64_t b_lbo = static_cast<uint64_t>((3 * p.zkstride) >> 4) << 16;
+    const uint32_t idesc1 = instr_desc(128, p.N_tile, p.optype);
+    const uint32_t idesc2 = instr_desc(128, 2 * p.N_tile, p.optype);
+    const uint32_t idesc3 = instr_desc(128, 3 * p.N_tile, p.optype);
     const uint64_t bres = (hi | b_lbo) + ((smem_base + static_cast<uint32_t>(p.bres_off)) >> 4);
-    const uint64_t kzs = static_cast<uint64_t>(p.zkstride >> 4);
+    const uint64_t kzs = static_cast<uint64_t>(p.zkstride >> 4);  // rows of tap kz -> kz + 1
     const int nent = p.n_mmas;
     {
         const bool ok = mbar_wait(smem_u32(&ctl->bres), 0u, &ctl->abort, kWaitLimitNs);
@@ -329,26 +337,37 @@ __device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int
             if (leader) {
                 const uint64_t ahi = hi + ((smem_base + static_cast<uint32_t>(slot * p.stage_bytes)) >> 4);
                 const uint64_t bbase = bres + static_cast<uint64_t>(kz_lo) * kzs;
-                const uint32_t dbase = dcol0 + static_cast<uint32_t>(s - kz_lo) * ncol;
-                for (int e = 0; e < nent; ++e) {
+                // plane s - kz_lo of segment 0; planes below it follow at + ncol, + 2 ncol
+                const uint32_t dtop = dcol0 + static_cast<uint32_t>(Z - 1 - (s - kz_lo)) * ncol;
+                const uint32_t idn = nz == 3 ? idesc3 : nz == 2 ? idesc2 : idesc1;
+                int e0 = 0;
+                if (kz_lo == 0) {
+                    // first entry: plane s starts its accumulator with tap kz 0 alone; the planes
+                    // below it (taps 1, 2) keep accumulating
+                    const ConvMma mm = p.mmas[0];
+#pragma unroll
+                    for (int sg = 0; sg < S; ++sg) {
+                        const uint64_t ad = ahi + mm.a + static_cast<uint64_t>(sg * 128);
+                        const uint32_t d0 = dtop + static_cast<uint32_t>(sg * Z) * ncol;
+                        if (F8) mma_f8_if(1u, d0, ad, bbase + mm.b, idesc1, 0u);
+                        else mma_f16_if(1u, d0, ad, bbase + mm.b, idesc1, 0u);
+                        if (nz > 1) {
+                            if (F8) mma_f8_if(1u, d0 + ncol, ad, bbase + mm.b + kzs, nz == 3 ? idesc2 : idesc1, 1u);
+                            else mma_f16_if(1u, d0 + ncol, ad, bbase + mm.b + kzs, nz == 3 ? idesc2 : idesc1, 1u);
+                        }
+                    }
+                    e0 = 1;
+                }
+                for (int e = e0; e < nent; ++e) {
                     const ConvMma mm = p.mmas[e];
-                    const uint32_t acc = (kz_lo == 0 && e == 0) ? 0u : 1u;
                     const uint64_t bb = bbase + mm.b;
                     const uint64_t a0 = ahi + mm.a;
 #pragma unroll
                     for (int sg = 0; sg < S; ++sg) {
                         const uint64_t ad = a0 + static_cast<uint64_t>(sg * 128);
-                        const uint32_t d0 = dbase + static_cast<uint32_t>(sg * Z) * ncol;
-                        if (nz == 3) {
-                            if (F8) mmaz3_f8_if(1u, d0, d0 - ncol, d0 - 2 * ncol, ad, bb, bb + kzs, bb + 2 * kzs, idesc, acc, 1u, 1u);
-                            else mmaz3_f16_if(1u, d0, d0 - ncol, d0 - 2 * ncol, ad, bb, bb + kzs, bb + 2 * kzs, idesc, acc, 1u, 1u);
-                        } else if (nz == 2) {
-                            if (F8) mmaz2_f8_if(1u, d0, d0 - ncol, ad, bb, bb + kzs, idesc, acc, 1u);
-                            else mmaz2_f16_if(1u, d0, d0 - ncol, ad, bb, bb + kzs, idesc, acc, 1u);
-                        } else {
-                            if (F8) mma_f8_if(1u, d0, ad, bb, idesc, acc);
-                            else mma_f16_if(1u, d0, ad, bb, idesc, acc);
-                        }
+                        const uint32_t d0 = dtop + static_cast<uint32_t>(sg * Z) * ncol;
+                        if (F8) mma_f8_if(1u, d0, ad, bb, idn, 1u);
+                        else mma_f16_if(1u, d0, ad, bb, idn, 1u);
                     }
                 }
             }
@@ -356,7 +375,7 @@ __device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int
             mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->empty[slot]));
             if (leader) {
                 FX_TADD(p, 4);
-                FX_TCNT(p, 7, nent * S * nz);
+                FX_TCNT(p, 7, (nent + (kz_lo == 0 && nz > 1 ? 1 : 0)) * S);
             }
         }
         if (aborted) break;
@@ -463,7 +482,61 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         for (int c = 0; c < kR; ++c)
 #pragma unroll
             for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
-        for (int r = rb; r < p.R; r += rs) {
+        // prenorm, one chunk per block: the TMEM reads of kBlk blocks share one wait
+        constexpr int kBlk = 4;
+        int r_first = rb;
+        if constexpr (kMy == 1 && kAccR) {
+            if (prenorm) {
+                for (; r_first + (kBlk - 1) * rs < p.R; r_first += kBlk * rs) {
+                    int64_t rowv[kBlk];
+                    bool validv[kBlk];
+                    uint32_t raw[kBlk][16];
+#pragma unroll
+                    for (int k = 0; k < kBlk; ++k) {
+                        const int r = r_first + k * rs;
+                        const int rz = p.zfold ? r % zpl : 0;
+                        rowv[k] = q0 + (p.zfold ? (r / zpl) * 128 + rz * P2r : static_cast<int64_t>(r) * 128) + wq * 32 + lane;
+                        uint32_t z, y, x;
+                        rd.split(static_cast<uint32_t>(rowv[k]), z, y, x);
+                        validv[k] = rowv[k] < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 &&
+                                    x <= xmax && (!p.zfold || z == zb + static_cast<uint32_t>(rz));
+                        const int rc = p.zfold ? r + zpl - 1 - 2 * rz : r;  // fold: planes at descending columns
+                        tmem_ld16_nowait(tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols +
+                                             rc * p.N_tile + c0 * 16,
+                                         raw[k]);
+                    }
+                    tmem_wait();
+#pragma unroll
+                    for (int k = 0; k < kBlk; ++k) tmem_regs_ready(raw[k]);
+#pragma unroll
+                    for (int k = 0; k < kBlk; ++k) {
+                        // invalid rows (halo, other planes, past the end; their accumulators may hold
+                        // sums over uninitialised memory, NaN included) are selected to zero
+                        float v[16];
+                        if (percol) {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                v[i] = validv[k] ? __uint_as_float(raw[k][i]) * ctl->colscale[cbase + c0 * 16 + i] : 0.f;
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) v[i] = validv[k] ? __uint_as_float(raw[k][i]) * acc_scale : 0.f;
+                        }
+                        if (validv[k]) {
+                            uint8_t* o = p.out + static_cast<int64_t>(b) * p.out_batch_stride + rowv[k] * 16 +
+                                         static_cast<int64_t>((cbase + c0 * 16) / 8) * p.out_group_stride;
+                            *reinterpret_cast<uint4*>(o) = pack_cell_f16_sat(v);
+                            *reinterpret_cast<uint4*>(o + p.out_group_stride) = pack_cell_f16_sat(v + 8);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            r1[0][i] += v[i];
+                            r2[0][i] = fmaf(v[i], v[i], r2[0][i]);
+                        }
+                    }
+                }
+            }
+        }
+        for (int r = r_first; r < p.R; r += rs) {
             // M block r: rows q0 + 128 r, or (z-plane fold) segment r / zplanes of plane r % zplanes
             const int rz = p.zfold ? r % zpl : 0;
             const int64_t row = q0 + (p.zfold ? (r / zpl) * 128 + rz * P2r : static_cast<int64_t>(r) * 128) + wq * 32 + lane;
@@ -471,8 +544,9 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
             rd.split(static_cast<uint32_t>(row), z, y, x);
             const bool valid = row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 && x <= xmax &&
                                (!p.zfold || z == zb + static_cast<uint32_t>(rz));
+            const int rc = p.zfold ? r + zpl - 1 - 2 * rz : r;  // fold: planes at descending columns
             const uint32_t taddr =
-                tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + r * p.N_tile;
+                tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + rc * p.N_tile;
             // upsample: phase-0 output cell of this input voxel (2z-1, 2y-1, 2x-1 in the padded grid)
             uint8_t* ob = nullptr;
             if (!prenorm && valid)
@@ -998,7 +1072,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             default: break;  // rejected on the host (launch_conv_tc)
         }
     } else {
-        const bool sc = p.R == 1;  // one M block per unit: split its chunks between the warp pair
+        // split the chunks between the warp pair for one M block per unit, and for pre-norm tiles of
+        // 32 / 64 columns (one / two chunks per warp and block: statistics summed in registers, the
+        // TMEM reads of several blocks per wait)
+        const bool sc = p.R == 1 || (p.mode == kModePrenorm && p.N_tile <= 64);
         switch (p.N_tile / 16) {
             case 1: epilogue_loop<1, false>(p, ctl, n_units); break;
             case 2: sc ? epilogue_loop<2, true>(p, ctl, n_units) : epilogue_loop<2, false>(p, ctl, n_units); break;
@@ -1049,7 +1126,8 @@ cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cud
     if (p.zfold) {
         if (p.fold || p.mode != kModePrenorm || p.n_tiles != 1 || !(p.R == 2 || p.R == 4 || p.R == 8) ||
             !(p.zplanes == 2 || p.zplanes == 4) || p.R != 2 * p.zplanes || p.zseg <= 0 || p.n_stages != p.zplanes + 2 || p.n_mmas <= 0 || p.bres_off % 128 || p.bres_bytes % 16 ||
-            p.bres_bytes <= 0 || p.zkstride <= 0 || p.zkstride % 16 || static_cast<size_t>(p.bres_off) < need ||
+            p.bres_bytes < 3 * p.n_mmas * p.N_tile * 32 || p.zkstride != p.N_tile * 16 ||
+            p.N_tile * (p.zplanes < 3 ? p.zplanes : 3) > 256 || static_cast<size_t>(p.bres_off) < need ||
             p.acc_slots * p.R * p.N_tile > static_cast<int>(p.tmem_cols))
             return cudaErrorInvalidValue;
         need = static_cast<size_t>(p.bres_off) + p.bres_bytes;

@@ -23,10 +23,11 @@
 // z-plane fold (3x3x3 stride 1): a unit's M blocks are S adjacent 128-row (y, x) segments in
 // `zplanes` consecutive z planes, so output block (segment, r) and tap kz read input plane
 // z0 + r + kz - 1: the A tile of input plane j (shift ky, kx) feeds blocks j, j-1, j-2 of its
-// segment with taps kz = 0, 1, 2 — one A read from shared memory through the collector for up to
-// three MMAs, accumulators unshifted; the S segments keep 2S accumulators independent of each
-// other in flight. Stages are input-plane windows; the 27 taps' weights stay resident in shared
-// memory.
+// segment with taps kz = 0, 1, 2. The three taps' weights are consecutive rows of B and the
+// planes of a segment sit at descending TMEM columns, so that is ONE MMA of N = 3 Cout (fewer at
+// the first and last planes): one A read from shared memory and one issue for up to three
+// accumulators, unshifted. Stages are input-plane windows; the 27 taps' weights stay resident in
+// shared memory.
 //
 // The host compiles each layer into a small "program": a list of pipeline stages (one bulk
 // copy of a window of rows for a range of groups + the matching packed weight block) and, per
@@ -101,7 +102,7 @@ struct ConvParams {
     int32_t zfold;               // 1: z-plane fold — the R blocks of a unit are one z plane apart
     int32_t zseg;                // z-plane fold: units per plane (each S adjacent 128-row segments)
     int32_t zplanes;             // z-plane fold: planes per unit; R = zplanes x S blocks
-    int32_t zkstride;            // z-plane fold: bytes between the resident weights of kz and kz + 1
+    int32_t zkstride;            // z-plane fold: bytes between the resident weight rows of kz and kz + 1
     int32_t bres_off, bres_bytes;  // z-plane fold: resident weights in shared memory (offset, size)
     int32_t n_units_m;           // ceil((row_end - row_begin) / (block_rows R))
     int32_t n_tiles;             // N tiles

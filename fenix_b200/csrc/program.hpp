@@ -134,8 +134,9 @@ inline fxk::ConvMma pack_mma(int64_t a_off, int64_t lbo, int64_t b_off) {
 // z-plane fold program (see ProgramSpec::zfold). Stage j = 0 .. R+1 stages input plane
 // z0 + j - 1 of the unit: rows [-(Wp+1), 128 S + Wp + 1) around the unit's S adjacent (y, x)
 // segments, all groups. Its MMA entries are the 9 (ky, kx) shifts x group pairs; the kernel issues
-// each entry for every segment (A + 128 rows per segment) and every kz with 0 <= j - kz < R into
-// block (segment, j - kz), weights (kz, entry) at entry.b + kz * zkstride of the resident region.
+// each entry for every segment (A + 128 rows per segment), with the taps kz of 0 <= j - kz < R
+// stacked along N into blocks (segment, j - kz); the weights of (entry, kz) start at
+// entry.b + kz * zkstride of the resident region, zkstride = N_tile rows of 16 B.
 // Returns "" on success.
 inline std::string build_zfold_program(const ProgramSpec& s, Program& pg) {
     if (s.N_tile != s.N_total || s.N_tile > 256 || s.N_tile % 16) return "zfold: one N tile of at most 256 columns";
@@ -145,7 +146,7 @@ inline std::string build_zfold_program(const ProgramSpec& s, Program& pg) {
     const int bblk = s.N_tile * 32;
     const int nent = 9 * (s.G / 2);
     pg.bres_bytes = 3 * nent * bblk;
-    pg.zkstride = nent * bblk;
+    pg.zkstride = s.N_tile * 16;  // tap kz -> kz + 1 within an entry's block
     const int sb = rows * s.G * 16;
     pg.stage_bytes = (sb + 127) / 128 * 128;
     pg.stage_a_bytes = pg.stage_bytes;
@@ -160,7 +161,7 @@ inline std::string build_zfold_program(const ProgramSpec& s, Program& pg) {
             for (int gp = 0; gp < s.G; gp += 2) {
                 const int e = static_cast<int>(pg.mmas.size());
                 const int64_t a_off = static_cast<int64_t>(gp) * rows * 16 + (ky * Wp + kx) * 16;
-                pg.mmas.push_back(pack_mma(a_off, static_cast<int64_t>(rows) * 16, static_cast<int64_t>(e) * bblk));
+                pg.mmas.push_back(pack_mma(a_off, static_cast<int64_t>(rows) * 16, static_cast<int64_t>(e) * 3 * bblk));
             }
     for (int j = 0; j < s.R + 2; ++j) {
         fxk::ConvStage st{};
@@ -177,17 +178,18 @@ inline std::string build_zfold_program(const ProgramSpec& s, Program& pg) {
     }
     for (const auto& m : pg.mmas)
         if ((m.a & 0xFFFFu) >= 0x4000u || (m.a >> 16) >= 0x4000u || m.b >= 0x4000u) return "zfold: smem offset overflow";
-    // resident weights: [kz][ky][kx][group pair] blocks, each [K half][N_tile][16 B] as in build_program
+    // resident weights: one block per (ky, kx, group pair) entry, [K half][kz][N_tile][16 B]: the
+    // three kz taps are consecutive B rows, so one MMA of N = k N_tile covers k adjacent taps
     pg.wtile_bytes = pg.bres_bytes;
     pg.wpack.assign(static_cast<size_t>(pg.bres_bytes), 0);
     for (int kz = 0; kz < 3; ++kz)
         for (int e = 0; e < nent; ++e) {
             const int kyx = e / (s.G / 2), gp = (e % (s.G / 2)) * 2;
             const int wk = kz * 9 + kyx;  // ky * 3 + kx == kyx
-            uint8_t* blk = pg.wpack.data() + static_cast<size_t>(kz * nent + e) * bblk;
+            uint8_t* blk = pg.wpack.data() + static_cast<size_t>(e) * 3 * bblk;
             for (int h = 0; h < 2; ++h)
                 for (int n = 0; n < s.N_tile; ++n) {
-                    uint8_t* row = blk + (static_cast<size_t>(h) * s.N_tile + n) * 16;
+                    uint8_t* row = blk + ((static_cast<size_t>(h) * 3 + kz) * s.N_tile + n) * 16;
                     for (int jj = 0; jj < s.cg; ++jj) {
                         const float v = s.wval(n, (gp + h) * s.cg + jj, wk);
                         if (s.elem == 2) {
