@@ -410,6 +410,10 @@ __device__ __forceinline__ float warp_transpose_reduce16(float (&v)[16], int lan
 struct RowDecomp {
     uint64_t mP2, mWp;
     uint32_t P2, Wp;
+    __device__ __forceinline__ void split_plane(uint32_t rem, uint32_t& y, uint32_t& x) const {
+        y = static_cast<uint32_t>(__umul64hi(rem, mWp));
+        x = rem - y * Wp;
+    }
     __device__ __forceinline__ void split(uint32_t row, uint32_t& z, uint32_t& y, uint32_t& x) const {
         z = static_cast<uint32_t>(__umul64hi(row, mP2));
         const uint32_t rem = row - z * P2;
@@ -431,7 +435,10 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const uint32_t tbase = ctl->tmem_base;
     const uint32_t slot_cols = static_cast<uint32_t>(p.R * p.N_tile);
     const int64_t P2r = static_cast<int64_t>(p.Hp) * p.Wp;
-    const int zpl = p.zfold ? p.zplanes : 1;
+    constexpr bool kFold = NCH <= 4;  // the z-plane fold only runs tiles of at most 64 columns
+    const bool zfold = kFold && p.zfold;
+    const int zpl = zfold ? p.zplanes : 1;
+    const int lzp = zpl == 4 ? 2 : (zpl == 2 ? 1 : 0);  // log2(zplanes): 2 or 4 planes per fold unit
     RowDecomp rd;
     rd.P2 = static_cast<uint32_t>(p.Hp * p.Wp);
     rd.Wp = static_cast<uint32_t>(p.Wp);
@@ -472,7 +479,38 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         const int64_t q0 = unit_q0(p, mu);
         // z-plane fold: block r owns plane zb + r only (a segment longer than a small plane's
         // interior reaches into the next plane, whose rows its own block counts)
-        const uint32_t zb = p.zfold ? 1u + static_cast<uint32_t>((mu / p.zseg) * p.zplanes) : 0u;
+        const uint32_t zb = zfold ? 1u + static_cast<uint32_t>((mu / p.zseg) * p.zplanes) : 0u;
+        // Every plane of a fold segment has the same in-plane offset o, so (y, x) and ownership
+        // (o inside the plane) are decided once per segment; a block then only checks its plane.
+        uint32_t zok = 0;  // bit sg: this thread's row of segment sg is an output
+        if (zfold) {
+            const uint32_t o0 = static_cast<uint32_t>(q0 - static_cast<int64_t>(zb) * P2r) + wq * 32 + lane;
+#pragma unroll
+            for (int sg = 0; sg < 2; ++sg) {
+                const uint32_t o = o0 + sg * 128;
+                uint32_t y, x;
+                rd.split_plane(o, y, x);
+                const bool ok = o < rd.P2 && y >= 1 && y <= ymax && x >= 1 && x <= xmax;
+                zok |= (ok ? 1u : 0u) << sg;
+            }
+        }
+        // M block r: its row for this thread, whether that row is an output of this block, and
+        // its TMEM column block (fold: segment r >> lzp, plane r & (zplanes - 1), planes at
+        // descending columns)
+        auto locate = [&](int r, int64_t& row, bool& valid, int& rc) {
+            if (zfold) {
+                const int sg = r >> lzp, rz = r & (zpl - 1);
+                row = q0 + sg * 128 + rz * P2r + wq * 32 + lane;
+                valid = ((zok >> sg) & 1u) && zb + static_cast<uint32_t>(rz) <= zmax;
+                rc = r + zpl - 1 - 2 * rz;
+            } else {
+                row = q0 + static_cast<int64_t>(r) * 128 + wq * 32 + lane;
+                uint32_t z, y, x;
+                rd.split(static_cast<uint32_t>(row), z, y, x);
+                valid = row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 && x <= xmax;
+                rc = r;
+            }
+        };
         const int cbase = nt * p.N_tile;  // first global column of this tile
         float s1[kMy], s2[kMy];
         float r1[kR][16], r2[kR][16];
@@ -493,14 +531,8 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                     uint32_t raw[kBlk][16];
 #pragma unroll
                     for (int k = 0; k < kBlk; ++k) {
-                        const int r = r_first + k * rs;
-                        const int rz = p.zfold ? r % zpl : 0;
-                        rowv[k] = q0 + (p.zfold ? (r / zpl) * 128 + rz * P2r : static_cast<int64_t>(r) * 128) + wq * 32 + lane;
-                        uint32_t z, y, x;
-                        rd.split(static_cast<uint32_t>(rowv[k]), z, y, x);
-                        validv[k] = rowv[k] < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 &&
-                                    x <= xmax && (!p.zfold || z == zb + static_cast<uint32_t>(rz));
-                        const int rc = p.zfold ? r + zpl - 1 - 2 * rz : r;  // fold: planes at descending columns
+                        int rc;
+                        locate(r_first + k * rs, rowv[k], validv[k], rc);
                         tmem_ld16_nowait(tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols +
                                              rc * p.N_tile + c0 * 16,
                                          raw[k]);
@@ -537,21 +569,20 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
             }
         }
         for (int r = r_first; r < p.R; r += rs) {
-            // M block r: rows q0 + 128 r, or (z-plane fold) segment r / zplanes of plane r % zplanes
-            const int rz = p.zfold ? r % zpl : 0;
-            const int64_t row = q0 + (p.zfold ? (r / zpl) * 128 + rz * P2r : static_cast<int64_t>(r) * 128) + wq * 32 + lane;
-            uint32_t z, y, x;
-            rd.split(static_cast<uint32_t>(row), z, y, x);
-            const bool valid = row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 && x <= xmax &&
-                               (!p.zfold || z == zb + static_cast<uint32_t>(rz));
-            const int rc = p.zfold ? r + zpl - 1 - 2 * rz : r;  // fold: planes at descending columns
+            int64_t row;
+            bool valid;
+            int rc;
+            locate(r, row, valid, rc);
             const uint32_t taddr =
                 tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + rc * p.N_tile;
             // upsample: phase-0 output cell of this input voxel (2z-1, 2y-1, 2x-1 in the padded grid)
             uint8_t* ob = nullptr;
-            if (!prenorm && valid)
+            if (!prenorm && valid) {  // upsample runs no fold: the row splits directly
+                uint32_t z, y, x;
+                rd.split(static_cast<uint32_t>(row), z, y, x);
                 ob = p.out + static_cast<int64_t>(b) * p.out_batch_stride +
                      ((static_cast<int64_t>(2 * z - 1) * p.oHp + (2 * y - 1)) * p.oWp + (2 * x - 1)) * 16;
+            }
 #pragma unroll
             for (int g0 = 0; g0 < kMy; g0 += kGrp) {
                 uint32_t raw[kGrp][16];
