@@ -435,7 +435,7 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const uint32_t tbase = ctl->tmem_base;
     const uint32_t slot_cols = static_cast<uint32_t>(p.R * p.N_tile);
     const int64_t P2r = static_cast<int64_t>(p.Hp) * p.Wp;
-    constexpr bool kFold = NCH <= 4;  // the z-plane fold only runs tiles of at most 64 columns
+    constexpr bool kFold = NCH <= 4;  // narrow tiles: the z-plane fold, several M blocks per unit
     const bool zfold = kFold && p.zfold;
     const int zpl = zfold ? p.zplanes : 1;
     const int lzp = zpl == 4 ? 2 : (zpl == 2 ? 1 : 0);  // log2(zplanes): 2 or 4 planes per fold unit
@@ -451,6 +451,9 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     constexpr int kCs = SPLITC ? 2 : 1;           // chunk stride
     const int c0 = SPLITC ? half : 0;             // first chunk
     const int rb = SPLITC ? 0 : half, rs = SPLITC ? 1 : 2;
+    // rs * 128 rows as (lines, voxels) within a padded plane, for the per-block row advance
+    uint32_t sty, stx;
+    rd.split_plane(static_cast<uint32_t>(rs * 128) % rd.P2, sty, stx);
     constexpr bool kAccR = kMy <= 2;         // sum over M blocks in registers, one butterfly per unit
     constexpr int kGrp = kMy <= 4 ? kMy : (kMy % 4 == 0 ? 4 : 2);  // chunks loaded from TMEM per wait
     constexpr int kR = kAccR ? kMy : 1;
@@ -494,21 +497,44 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                 zok |= (ok ? 1u : 0u) << sg;
             }
         }
-        // M block r: its row for this thread, whether that row is an output of this block, and
-        // its TMEM column block (fold: segment r >> lzp, plane r & (zplanes - 1), planes at
-        // descending columns)
+        // Regular tiling of narrow tiles: the blocks are visited in order rb, rb + rs, ..., each
+        // rs * 128 rows after the previous one, so this thread's (z, y, x) advances by a
+        // mixed-radix add.
+        // Rows start at row_begin (plane 1) and row < row_end caps the plane, so only (y, x) are kept.
+        int64_t crow = 0;
+        uint32_t cy = 0, cx = 0;
+        if (kFold && !zfold) {
+            crow = q0 + static_cast<int64_t>(rb) * 128 + wq * 32 + lane;
+            uint32_t cz;
+            rd.split(static_cast<uint32_t>(crow), cz, cy, cx);
+        }
+        // M block r (called once per block, in order): its row for this thread, whether that row is
+        // an output of this block, and its TMEM column block (fold: segment r >> lzp, plane
+        // r & (zplanes - 1), planes at descending columns)
         auto locate = [&](int r, int64_t& row, bool& valid, int& rc) {
             if (zfold) {
                 const int sg = r >> lzp, rz = r & (zpl - 1);
                 row = q0 + sg * 128 + rz * P2r + wq * 32 + lane;
                 valid = ((zok >> sg) & 1u) && zb + static_cast<uint32_t>(rz) <= zmax;
                 rc = r + zpl - 1 - 2 * rz;
-            } else {
+            } else if constexpr (!kFold) {  // wide tiles (one or two blocks per unit): split directly
                 row = q0 + static_cast<int64_t>(r) * 128 + wq * 32 + lane;
                 uint32_t z, y, x;
                 rd.split(static_cast<uint32_t>(row), z, y, x);
                 valid = row < p.row_end && z >= 1 && z <= zmax && y >= 1 && y <= ymax && x >= 1 && x <= xmax;
                 rc = r;
+            } else {
+                row = crow;
+                valid = row >= p.row_begin && row < p.row_end && cy >= 1 && cy <= ymax && cx >= 1 && cx <= xmax;
+                rc = r;
+                crow += static_cast<int64_t>(rs) * 128;
+                cx += stx;
+                if (cx >= rd.Wp) {
+                    cx -= rd.Wp;
+                    ++cy;
+                }
+                cy += sty;
+                if (cy >= static_cast<uint32_t>(p.Hp)) cy -= static_cast<uint32_t>(p.Hp);
             }
         };
         const int cbase = nt * p.N_tile;  // first global column of this tile
