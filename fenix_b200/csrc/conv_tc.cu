@@ -707,14 +707,18 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                     s2[c] = warp_transpose_reduce16(r2[c], lane);
                 }
             }
-            float* dst = p.stats +
-                         ((static_cast<int64_t>(b) * p.n_units_m + mu) * kStatRecsPerUnit + half * 4 + wq) * p.stats_C * 2;
+            // four records per unit when the warp pair splits the chunks (both warps of a lane
+            // quarter fill one record, each its own channels); eight otherwise, a warp's record
+            // holding zeros for the channels it did not handle
+            const bool shared = SPLITC && p.stat_recs == 4;
+            float* dst = p.stats + ((static_cast<int64_t>(b) * p.n_units_m + mu) * p.stat_recs + (shared ? wq : half * 4 + wq)) *
+                                       p.stats_C * 2;
             if (lane < 16) {
 #pragma unroll
                 for (int c = 0; c < kMy; ++c) {
                     const int ch = cbase + (c0 + c * kCs) * 16 + lane;
                     *reinterpret_cast<float2*>(dst + ch * 2) = make_float2(s1[c], s2[c]);
-                    if (SPLITC) {  // the other warp's chunks: zero in this record
+                    if (SPLITC && !shared) {  // the other warp's chunks: zero in this record
                         const int cho = cbase + ((c0 ^ 1) + c * kCs) * 16 + lane;
                         *reinterpret_cast<float2*>(dst + cho * 2) = make_float2(0.f, 0.f);
                     }
@@ -1020,7 +1024,7 @@ __device__ void epilogue_fold(const ConvParams& p, SmemCtl* ctl, float* xbuf, in
             s2[0] = warp_transpose_reduce16(r2[0], lane);
         }
         float* dst = p.stats +
-                     ((static_cast<int64_t>(b) * p.n_units_m + mu) * kStatRecsPerUnit + half * 4 + wq) * p.stats_C * 2;
+                     ((static_cast<int64_t>(b) * p.n_units_m + mu) * p.stat_recs + half * 4 + wq) * p.stats_C * 2;
         if (lane < 16) {
 #pragma unroll
             for (int c = 0; c < kMy; ++c) {
@@ -1132,7 +1136,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         // split the chunks between the warp pair for one M block per unit, and for pre-norm tiles of
         // 32 / 64 columns (one / two chunks per warp and block: statistics summed in registers, the
         // TMEM reads of several blocks per wait)
-        const bool sc = p.R == 1 || (p.mode == kModePrenorm && p.N_tile <= 64);
+        const bool sc = p.R == 1 || (p.mode == kModePrenorm && p.N_tile <= 64);  // (mirrored in launch_conv_tc)
         switch (p.N_tile / 16) {
             case 1: epilogue_loop<1, false>(p, ctl, n_units); break;
             case 2: sc ? epilogue_loop<2, true>(p, ctl, n_units) : epilogue_loop<2, false>(p, ctl, n_units); break;
@@ -1167,6 +1171,11 @@ cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cud
     if (!p.fold && (p.N_tile % 16 || !(nch == 1 || nch == 2 || nch == 4 || nch == 8 || nch == 16 || nch == 20)))
         return cudaErrorInvalidValue;
     if ((p.mode == kModeUpsample ? p.cout : p.stats_C) > kMaxCols) return cudaErrorInvalidValue;
+    // four statistics records per unit only where the epilogue's warp pair splits the chunks
+    if (p.mode == kModePrenorm &&
+        !(p.stat_recs == kStatRecsPerUnit ||
+          (p.stat_recs == kStatRecsPerUnit / 2 && !p.fold && p.N_tile >= 32 && (p.R == 1 || p.N_tile <= 64))))
+        return cudaErrorInvalidValue;
     if (!(p.R == 1 || p.R == 2 || p.R == 4 || p.R == 8) || (p.N_tile > 256 && p.R != 1)) return cudaErrorInvalidValue;
     if (p.n_stages > kMaxStages || p.n_mmas > kMaxMmas) return cudaErrorInvalidValue;
     size_t need = static_cast<size_t>(p.n_pipe) * p.stage_bytes + sizeof(SmemCtl);

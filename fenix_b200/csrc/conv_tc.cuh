@@ -125,8 +125,11 @@ struct ConvParams {
     int32_t cout;            // upsample mode: channels per phase
     int32_t oHp, oWp;        // upsample mode: padded H, W of the output grid
     unsigned* amax;          // upsample mode: max |output| (float bits) when non-null
-    float* stats;            // prenorm mode: [batch][n_units_m][kStatRecsPerUnit][C][2] partial sums
+    float* stats;            // prenorm mode: [batch][n_units_m][stat_recs][C][2] partial sums
     int32_t stats_C;         // channels per stats record (= n_tiles * N_tile)
+    int32_t stat_recs;       // prenorm mode: records per unit, kStatRecsPerUnit or half of it when the
+                             // epilogue's warp pair splits the chunks (N_tile >= 32 and R == 1 or
+                             // N_tile <= 64, no x fold)
     uint32_t* status;
     unsigned long long* trace;  // per-role cycle counters (kernel built with FX_CONV_TRACE), or null
     // The program itself travels in the parameter space: warp-uniform indexed loads of it land in

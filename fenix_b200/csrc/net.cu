@@ -823,7 +823,9 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
         } else {
             L.cur_ratio = nullptr;
         }
-        L.nrec = dp.n_units_m * fxk::kStatRecsPerUnit;
+        p.stat_recs = (!dp.fold && dp.N_tile >= 32 && (dp.R == 1 || dp.N_tile <= 64)) ? fxk::kStatRecsPerUnit / 2
+                                                                                        : fxk::kStatRecsPerUnit;
+        L.nrec = dp.n_units_m * p.stat_recs;
         if (L.nrec > L.nrec_cap) return fail(kInternal, L.name + ": statistics buffer too small");
     }
     const int64_t units = static_cast<int64_t>(nb) * p.n_units_m * p.n_tiles;
