@@ -39,7 +39,7 @@ WEIGHT_SEED, VOLUME_SEED, CALIB_SEED0 = 1, 2, 1000
 # dram__bytes_write.sum from an ncu launch list of `bench.py --size 256 --steps 1 --warmup 3`:
 # 4.563 GB read + 5.933 GB written per forward of 8 tiles). ncu cannot run inside the timed bench,
 # so the captured figure is carried here and re-captured when the conv kernel changes.
-CONV_DRAM_BYTES_PER_TILE = (4.563e9 + 5.933e9) / 8
+CONV_DRAM_BYTES_PER_TILE = 1.2946e9  # ncu launch list of the 256^3 bench: (112.121 + 137.737) GB over 193 tiles
 
 
 def env_int(name, default):
