@@ -431,11 +431,12 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
         const int64_t ogs = gout.gs(), obs = (Cout / 8) * ogs;
         auto* out = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * obs));
         const int64_t rows = static_cast<int64_t>(gout.D) * (gout.H + 2) * (gout.W + 2);
-        const int64_t nrec = ((rows + 125) / 126) * fxk::kStatRecsPerUnit;
+        const int64_t nrec = std::max<int64_t>((rows + 125) / 126, sm_count_of_current()) * fxk::kStatRecsPerUnit;
         L.d_partials = static_cast<float*>(sc.get(sizeof(float) * B * nrec * Cout * 2));
         L.nrec_cap = nrec;
         auto* d_status = static_cast<uint32_t*>(sc.get(sizeof(uint32_t)));
         if (!out || !L.d_partials || !d_status) return set_err(FX_INTERNAL, "cudaMalloc failed");
+        cudaMemsetAsync(L.d_partials, 0, sizeof(float) * B * nrec * Cout * 2, s);  // the epilogue adds into it
         cudaMemsetAsync(out, 0, static_cast<size_t>(B) * obs, s);
         cudaMemsetAsync(d_status, 0, sizeof(uint32_t), s);
         st = fxh::launch_layer(L, q, gin, gout, in, ibs, igs, out, obs, ogs, 0, 1.f, nullptr, B, sm_count_of_current(),

@@ -463,10 +463,56 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const bool percol = p.col_scale != nullptr;
     const float acc_scale = p.acc_scale;
     const int32_t oP2 = p.oHp * p.oWp;  // upsample: padded plane of the output grid
+    // InstanceNorm partial sums accumulate over all units of one (batch item, N tile) run of this
+    // CTA; a run ends in one flush: butterfly, then add into this warp's slot of the CTA's record
+    // [b][blockIdx.x][stat_recs] (records start at zero; the statistics pass clears what it reads).
+    // Four records per CTA when the warp pair splits the chunks (both warps of a lane quarter fill
+    // one record, each its own channels), eight otherwise.
+    float s1[kMy], s2[kMy];
+    float r1[kR][16], r2[kR][16];
+#pragma unroll
+    for (int c = 0; c < kMy; ++c) s1[c] = s2[c] = 0.f;
+#pragma unroll
+    for (int c = 0; c < kR; ++c)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
+    int run_b = -1, run_nt = 0;
+    auto flush = [&]() {
+        if constexpr (kAccR) {
+#pragma unroll
+            for (int c = 0; c < kMy; ++c) {
+                s1[c] = warp_transpose_reduce16(r1[c], lane);
+                s2[c] = warp_transpose_reduce16(r2[c], lane);
+            }
+#pragma unroll
+            for (int c = 0; c < kR; ++c)
+#pragma unroll
+                for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
+        }
+        const bool shared = SPLITC && p.stat_recs == kStatRecsPerUnit / 2;
+        float* dst = p.stats + ((static_cast<int64_t>(run_b) * gridDim.x + blockIdx.x) * p.stat_recs +
+                                (shared ? wq : half * 4 + wq)) *
+                                   p.stats_C * 2;
+        if (lane < 16) {
+#pragma unroll
+            for (int c = 0; c < kMy; ++c) {
+                float2* q = reinterpret_cast<float2*>(dst + (run_nt * p.N_tile + (c0 + c * kCs) * 16 + lane) * 2);
+                const float2 o = *q;
+                *q = make_float2(o.x + s1[c], o.y + s2[c]);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < kMy; ++c) s1[c] = s2[c] = 0.f;
+    };
     uint32_t j = 0;
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
         int b, mu, nt;
         unit_coords(p, unit, b, mu, nt);
+        if (prenorm && (b != run_b || nt != run_nt)) {
+            if (run_b >= 0) flush();
+            run_b = b;
+            run_nt = nt;
+        }
         const int aslot = j % p.acc_slots;
         {
             FX_T0();
@@ -538,14 +584,6 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
             }
         };
         const int cbase = nt * p.N_tile;  // first global column of this tile
-        float s1[kMy], s2[kMy];
-        float r1[kR][16], r2[kR][16];
-#pragma unroll
-        for (int c = 0; c < kMy; ++c) s1[c] = s2[c] = 0.f;
-#pragma unroll
-        for (int c = 0; c < kR; ++c)
-#pragma unroll
-            for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
         // prenorm, one chunk per block: the TMEM reads of kBlk blocks share one wait
         constexpr int kBlk = 4;
         int r_first = rb;
@@ -699,37 +737,12 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&ctl->acce[aslot]));
-        if (prenorm) {
-            if constexpr (kAccR) {
-#pragma unroll
-                for (int c = 0; c < kMy; ++c) {
-                    s1[c] = warp_transpose_reduce16(r1[c], lane);
-                    s2[c] = warp_transpose_reduce16(r2[c], lane);
-                }
-            }
-            // four records per unit when the warp pair splits the chunks (both warps of a lane
-            // quarter fill one record, each its own channels); eight otherwise, a warp's record
-            // holding zeros for the channels it did not handle
-            const bool shared = SPLITC && p.stat_recs == 4;
-            float* dst = p.stats + ((static_cast<int64_t>(b) * p.n_units_m + mu) * p.stat_recs + (shared ? wq : half * 4 + wq)) *
-                                       p.stats_C * 2;
-            if (lane < 16) {
-#pragma unroll
-                for (int c = 0; c < kMy; ++c) {
-                    const int ch = cbase + (c0 + c * kCs) * 16 + lane;
-                    *reinterpret_cast<float2*>(dst + ch * 2) = make_float2(s1[c], s2[c]);
-                    if (SPLITC && !shared) {  // the other warp's chunks: zero in this record
-                        const int cho = cbase + ((c0 ^ 1) + c * kCs) * 16 + lane;
-                        *reinterpret_cast<float2*>(dst + cho * 2) = make_float2(0.f, 0.f);
-                    }
-                }
-            }
-        }
         if (threadIdx.x == 64) {
             FX_TADD(p, 6);
             FX_TCNT(p, 8, 1);
         }
     }
+    if (prenorm && run_b >= 0) flush();
 }
 
 // Epilogue of the transposed convolution (upsample mode, Cout a power of two): column n of the

@@ -125,7 +125,9 @@ struct ConvParams {
     int32_t cout;            // upsample mode: channels per phase
     int32_t oHp, oWp;        // upsample mode: padded H, W of the output grid
     unsigned* amax;          // upsample mode: max |output| (float bits) when non-null
-    float* stats;            // prenorm mode: [batch][n_units_m][stat_recs][C][2] partial sums
+    float* stats;            // prenorm mode: partial sums [batch][gridDim.x][stat_recs][C][2], which
+                             // the epilogue ADDS into (zero before the launch); the x-fold epilogue
+                             // writes [batch][n_units_m][stat_recs][C][2] instead
     int32_t stats_C;         // channels per stats record (= n_tiles * N_tile)
     int32_t stat_recs;       // prenorm mode: records per unit, kStatRecsPerUnit or half of it when the
                              // epilogue's warp pair splits the chunks (N_tile >= 32 and R == 1 or

@@ -147,8 +147,9 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) { return 
 // the S slices in slice order (the result does not depend on block scheduling) and writes
 // ss[B][C][2] = {gamma * rstd, beta - mean * gamma * rstd}. With ratio, the records hold the
 // channel's values divided by ratio[c]: the statistics of the true values are mean * r and
-// var * r^2, and ss is written for the stored values (scale multiplied by r).
-__global__ void __launch_bounds__(256) in_stats_kernel(const float* __restrict__ partials, int nrec, int C, int S,
+// var * r^2, and ss is written for the stored values (scale multiplied by r). Every record read
+// is left at zero: the conv epilogue adds its next partial sums into it.
+__global__ void __launch_bounds__(256) in_stats_kernel(float* __restrict__ partials, int nrec, int C, int S,
                                                        double count, const float* __restrict__ gamma,
                                                        const float* __restrict__ beta,
                                                        const float* __restrict__ ratio, float eps,
@@ -161,13 +162,15 @@ __global__ void __launch_bounds__(256) in_stats_kernel(const float* __restrict__
     const int r1 = static_cast<int>(static_cast<int64_t>(nrec) * (sl + 1) / S);
     double a1 = 0.0, a2 = 0.0;
     if (c < C) {
-        const float2* base = reinterpret_cast<const float2*>(partials) + static_cast<int64_t>(b) * nrec * C + c;
+        float2* base = reinterpret_cast<float2*>(partials) + static_cast<int64_t>(b) * nrec * C + c;
 #pragma unroll 4
         for (int r = r0 + w; r < r1; r += 8) {
-            const float2 v = __ldg(base + static_cast<int64_t>(r) * C);
+            const float2 v = __ldcg(base + static_cast<int64_t>(r) * C);
             a1 += v.x;
             a2 += v.y;
         }
+        // then clear them (the next conv adds into them); apart from the loads so those stay batched
+        for (int r = r0 + w; r < r1; r += 8) base[static_cast<int64_t>(r) * C] = make_float2(0.f, 0.f);
     }
     __shared__ double s1[8][32], s2[8][32];
     s1[w][lane] = a1;
@@ -601,9 +604,11 @@ cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
     return cudaGetLastError();
 }
 
-int in_stats_slices(int nrec) { return nrec < 256 ? 1 : (nrec / 256 < kMaxStatSlices ? nrec / 256 : kMaxStatSlices); }
+// about 64 records per slice (eight per warp, loads batched four deep), at most kMaxStatSlices
+// slices: more slices add blocks but lengthen the last block's serial walk over them
+int in_stats_slices(int nrec) { return nrec < 128 ? 1 : (nrec / 64 < kMaxStatSlices ? nrec / 64 : kMaxStatSlices); }
 
-cudaError_t launch_in_finalize(const float* partials, int B, int nrec, int C, double count, const float* gamma,
+cudaError_t launch_in_finalize(float* partials, int B, int nrec, int C, double count, const float* gamma,
                                const float* beta, const float* ratio, float eps, double* work, unsigned* done,
                                float* ss, cudaStream_t s) {
     if (nrec < 1 || C < 1 || B < 1) return cudaErrorInvalidValue;

@@ -57,9 +57,10 @@ __host__ __device__ inline void tta_source(int m, int P, int a0, int a1, int a2,
 // shift = beta - mean * scale over `count` voxels. work holds B * kMaxStatSlices * C * 2 doubles;
 // done holds B * ceil(C / 32) counters that are zero before the first launch (each launch leaves
 // them zero). Launches sharing work/done must be stream-ordered. ratio (per channel, or null):
-// the records hold each channel's values divided by ratio[c] (see in_stats_kernel).
+// the records hold each channel's values divided by ratio[c] (see in_stats_kernel). The records
+// read are left at zero.
 constexpr int kMaxStatSlices = 128;
-cudaError_t launch_in_finalize(const float* partials, int B, int nrec, int C, double count, const float* gamma,
+cudaError_t launch_in_finalize(float* partials, int B, int nrec, int C, double count, const float* gamma,
                                const float* beta, const float* ratio, float eps, double* work, unsigned* done,
                                float* ss, cudaStream_t s);
 

@@ -572,9 +572,10 @@ Status Net::build_layer(Layer& L, int q) {
     if (L.kind != Layer::kUp && !L.d_partials) {
         const ActGeom g = level(L.lout);
         const int64_t rows = static_cast<int64_t>(g.D) * (g.H + 2) * (g.W + 2);
-        const int64_t nrec_max = ((rows + 125) / 126) * fxk::kStatRecsPerUnit;
+        const int64_t nrec_max = std::max<int64_t>(((rows + 125) / 126), sm_count_) * fxk::kStatRecsPerUnit;
         L.d_partials = static_cast<float*>(dalloc(sizeof(float) * Bmax_ * nrec_max * L.Cout * 2));
         L.nrec_cap = nrec_max;
+        if (L.d_partials) cudaMemset(L.d_partials, 0, sizeof(float) * Bmax_ * nrec_max * L.Cout * 2);
         L.d_ss = static_cast<float*>(dalloc(sizeof(float) * Bmax_ * L.Cout * 2));
         if (!L.d_partials || !L.d_ss) return fail(kInternal, "cudaMalloc: stats buffers");
         if ((st = upload(L.d_gamma, L.gamma, this, allocs_)).code) return st;
@@ -825,17 +826,26 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
         }
         p.stat_recs = (!dp.fold && dp.N_tile >= 32 && (dp.R == 1 || dp.N_tile <= 64)) ? fxk::kStatRecsPerUnit / 2
                                                                                         : fxk::kStatRecsPerUnit;
-        L.nrec = dp.n_units_m * p.stat_recs;
-        if (L.nrec > L.nrec_cap) return fail(kInternal, L.name + ": statistics buffer too small");
     }
     const int64_t units = static_cast<int64_t>(nb) * p.n_units_m * p.n_tiles;
     const int grid = static_cast<int>(std::min<int64_t>(units, sm_count_));
+    if (p.mode == fxk::kModePrenorm) {
+        // x fold: records per unit, each rewritten by every launch; otherwise records per CTA that the
+        // epilogue adds into (zero before the launch: cleared by the statistics pass that reads them,
+        // or here when the previous launch was not followed by one)
+        L.nrec = (dp.fold ? dp.n_units_m : grid) * p.stat_recs;
+        if (L.nrec > L.nrec_cap) return fail(kInternal, L.name + ": statistics buffer too small");
+        if (L.partials_dirty)
+            cudaMemsetAsync(L.d_partials, 0, sizeof(float) * static_cast<size_t>(nb) * L.nrec_cap * L.Cout * 2, s);
+        L.partials_dirty = true;
+    }
     return cuda_status(fxk::launch_conv_tc(p, grid, dp.smem(), s), L.name.c_str());
 }
 
 Status Net::finalize_in(Layer& L, int nb, cudaStream_t s) {
     const ActGeom g = level(L.lout);
     const double count = static_cast<double>(g.D) * g.H * g.W;
+    L.partials_dirty = false;  // the statistics pass leaves the records it reads at zero
     return cuda_status(fxk::launch_in_finalize(L.d_partials, nb, L.nrec, L.Cout, count, L.d_gamma, L.d_beta,
                                                L.cur_ratio, kEps, d_stat_work_, d_stat_done_, L.d_ss, s),
                        "in_finalize");

@@ -79,10 +79,11 @@ struct Layer {
     DevProgram prog[3];               // indexed by fxk::OpType: bf16, e4m3, f16
     float* d_gamma = nullptr;
     float* d_beta = nullptr;
-    float* d_partials = nullptr;      // [Bmax][n_units_m][kStatRecsPerUnit][Cout][2]
+    float* d_partials = nullptr;      // [Bmax][nrec][Cout][2]: per CTA (or per unit for the x fold)
     float* d_ss = nullptr;            // [Bmax][Cout][2]
     int nrec = 0;
     int64_t nrec_cap = 0;             // records per batch item that d_partials holds
+    bool partials_dirty = false;      // a conv wrote d_partials and no statistics pass has cleared it
     const float* cur_ratio = nullptr; // ratio of the last prenorm launch (its statistics' scale)
 };
 
