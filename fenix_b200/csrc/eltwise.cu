@@ -250,8 +250,11 @@ __device__ __forceinline__ void store_dest(const NormDest& d, int b, int gout, i
 // in flight per thread: two voxels per thread and registers for eight CTAs per SM (six for the
 // two-destination form) measured 11% faster than four voxels at three CTAs.
 constexpr int kNormThreads = 256, kNormVox = 2;
-template <int CPT, bool E4>
-__global__ void __launch_bounds__(kNormThreads, E4 ? 8 : 6) norm_act_kernel(const uint8_t* __restrict__ pre,
+// MODE 0: any destinations (store_dest); 1: one plain e4m3 destination (E4 above); 2: an e4m3
+// phase-split destination d0 plus a plain e4m3 d1 (an encoder stage's output: the stride-2 conv's
+// input and the decoder's skip half), both stores resolved at compile time.
+template <int CPT, int MODE>
+__global__ void __launch_bounds__(kNormThreads, MODE == 1 ? 8 : 6) norm_act_kernel(const uint8_t* __restrict__ pre,
                                                                          int64_t pbs, int64_t pgs, GridGeom g,
                                                                          FastDiv fw, int C,
                                                                          const float* __restrict__ ss, float slope,
@@ -304,7 +307,7 @@ __global__ void __launch_bounds__(kNormThreads, E4 ? 8 : 6) norm_act_kernel(cons
             }
         }
         const int64_t row = (static_cast<int64_t>(zp) * Hp + yp[k]) * Wp + xp[k];
-        if constexpr (E4) {
+        if constexpr (MODE == 1) {
             const float qs = d0.qscale;
             uint4 w;
             w.x = pack_e4m3x4(v[0] * qs, v[1] * qs, v[2] * qs, v[3] * qs);
@@ -312,6 +315,22 @@ __global__ void __launch_bounds__(kNormThreads, E4 ? 8 : 6) norm_act_kernel(cons
             w.z = pack_e4m3x4(v[8] * qs, v[9] * qs, v[10] * qs, v[11] * qs);
             w.w = pack_e4m3x4(v[12] * qs, v[13] * qs, v[14] * qs, v[15] * qs);
             *reinterpret_cast<uint4*>(d0.ptr + b * d0.batch_stride + go * d0.group_stride + row * 16) = w;
+        } else if constexpr (MODE == 2) {
+            const float q0 = d0.qscale, q1 = d1.qscale;
+            uint4 w;
+            w.x = pack_e4m3x4(v[0] * q0, v[1] * q0, v[2] * q0, v[3] * q0);
+            w.y = pack_e4m3x4(v[4] * q0, v[5] * q0, v[6] * q0, v[7] * q0);
+            w.z = pack_e4m3x4(v[8] * q0, v[9] * q0, v[10] * q0, v[11] * q0);
+            w.w = pack_e4m3x4(v[12] * q0, v[13] * q0, v[14] * q0, v[15] * q0);
+            const int phi = ((zp & 1) << 2) | ((yp[k] & 1) << 1) | (xp[k] & 1);
+            const int64_t prow = (static_cast<int64_t>(zp >> 1) * d0.pHp + (yp[k] >> 1)) * d0.pWp + (xp[k] >> 1);
+            *reinterpret_cast<uint4*>(d0.ptr + b * d0.batch_stride + go * d0.group_stride + phi * d0.phase_stride +
+                                      prow * 16) = w;
+            w.x = pack_e4m3x4(v[0] * q1, v[1] * q1, v[2] * q1, v[3] * q1);
+            w.y = pack_e4m3x4(v[4] * q1, v[5] * q1, v[6] * q1, v[7] * q1);
+            w.z = pack_e4m3x4(v[8] * q1, v[9] * q1, v[10] * q1, v[11] * q1);
+            w.w = pack_e4m3x4(v[12] * q1, v[13] * q1, v[14] * q1, v[15] * q1);
+            *reinterpret_cast<uint4*>(d1.ptr + b * d1.batch_stride + go * d1.group_stride + row * 16) = w;
         } else {
             store_dest(d0, b, d0.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
             store_dest(d1, b, d1.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
@@ -630,12 +649,20 @@ cudaError_t launch_norm_act(const uint8_t* pre, int64_t pbs, int64_t pgs, GridGe
     const FastDiv fw = make_fastdiv(static_cast<uint32_t>(g.W));
     count_launch();
     const bool e4 = cpt == 16 && d0.ptr && d0.dtype == kOpE4M3 && !d0.phase && !d1.ptr;
+    // one e4m3 phase-split destination and one plain e4m3 destination, in either order (the two
+    // stores are independent): the phase-split one goes first
+    const bool pair = cpt == 16 && d0.ptr && d1.ptr && d0.dtype == kOpE4M3 && d1.dtype == kOpE4M3 &&
+                      (d0.phase != 0) != (d1.phase != 0);
     if (e4)
-        norm_act_kernel<16, true><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+        norm_act_kernel<16, 1><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+    else if (pair && d0.phase)
+        norm_act_kernel<16, 2><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+    else if (pair)
+        norm_act_kernel<16, 2><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d1, d0, amax);
     else if (cpt == 16)
-        norm_act_kernel<16, false><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+        norm_act_kernel<16, 0><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
     else
-        norm_act_kernel<8, false><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+        norm_act_kernel<8, 0><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
     return cudaGetLastError();
 }
 
