@@ -245,14 +245,13 @@ __device__ __forceinline__ void store_dest(const NormDest& d, int b, int gout, i
 // Block = (plane chunk, z, batch x channel group); thread = kNormVox interior voxels of one z
 // plane x CPT channels (one 16-channel e4m3 cell, or one or two 8-channel f16 cells). The cells
 // of all kNormVox voxels are loaded before any is used, for memory-level parallelism.
-// E4 (16 channels, one plain e4m3 destination, no second destination): the common case, with
-// the store reduced to one 16-byte e4m3 cell. The pass is bound by memory latency, not by bytes
-// in flight per thread: two voxels per thread and registers for eight CTAs per SM (six for the
-// two-destination form) measured 11% faster than four voxels at three CTAs.
+// MODE 0: any destinations (store_dest); 1: one plain e4m3 destination, the common case, the
+// store reduced to one 16-byte e4m3 cell; 2: an e4m3 phase-split destination d0 plus a plain e4m3
+// d1 (an encoder stage's output: the stride-2 conv's input and the decoder's skip half), both
+// stores resolved at compile time. The pass is bound by memory latency, not by bytes in flight per
+// thread: two voxels per thread and registers for eight CTAs per SM (six for the two-destination
+// forms) measured 11% faster than four voxels at three CTAs.
 constexpr int kNormThreads = 256, kNormVox = 2;
-// MODE 0: any destinations (store_dest); 1: one plain e4m3 destination (E4 above); 2: an e4m3
-// phase-split destination d0 plus a plain e4m3 d1 (an encoder stage's output: the stride-2 conv's
-// input and the decoder's skip half), both stores resolved at compile time.
 template <int CPT, int MODE>
 __global__ void __launch_bounds__(kNormThreads, MODE == 1 ? 8 : 6) norm_act_kernel(const uint8_t* __restrict__ pre,
                                                                          int64_t pbs, int64_t pgs, GridGeom g,
