@@ -45,7 +45,8 @@ namespace fxk {
 
 constexpr int kConvThreads = 320;  // warp 0 producer, warp 1 MMA issuer, warps 2..9 epilogue
 constexpr int kEpiWarps = 8;        // two per TMEM lane quarter, splitting the M blocks of a unit
-// InstanceNorm partial records written per work unit: one per epilogue warp.
+// InstanceNorm partial records per CTA run (per work unit for the x-fold epilogue): one per
+// epilogue warp, or half of that when the warp pair of a lane quarter shares one.
 constexpr int kStatRecsPerUnit = kEpiWarps;
 constexpr int kMaxSrc = 8;
 
@@ -129,9 +130,9 @@ struct ConvParams {
                              // the epilogue ADDS into (zero before the launch); the x-fold epilogue
                              // writes [batch][n_units_m][stat_recs][C][2] instead
     int32_t stats_C;         // channels per stats record (= n_tiles * N_tile)
-    int32_t stat_recs;       // prenorm mode: records per unit, kStatRecsPerUnit or half of it when the
-                             // epilogue's warp pair splits the chunks (N_tile >= 32 and R == 1 or
-                             // N_tile <= 64, no x fold)
+    int32_t stat_recs;       // prenorm mode: records per CTA (per unit for the x fold): kStatRecsPerUnit,
+                             // or half of it when the epilogue's warp pair splits the chunks
+                             // (N_tile >= 32 and R == 1 or N_tile <= 64, no x fold)
     uint32_t* status;
     unsigned long long* trace;  // per-role cycle counters (kernel built with FX_CONV_TRACE), or null
     // The program itself travels in the parameter space: warp-uniform indexed loads of it land in
