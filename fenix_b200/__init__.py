@@ -102,6 +102,9 @@ def lib():
     _sig(L, "fx_net_calibrate", i32, [vp, u8p, i32])
     _sig(L, "fx_net_act_scales", i32, [vp, f32p, i32])
     _sig(L, "fx_net_set_act_scales", i32, [vp, f32p, i32])
+    _sig(L, "fx_net_set_layer_precision", i32, [vp, C.POINTER(C.c_int), i32])
+    _sig(L, "fx_net_layer_precision", i32, [vp, C.POINTER(C.c_int), C.POINTER(C.c_double), i32])
+    _sig(L, "fx_net_layer_name", C.c_char_p, [vp, i32])
     _sig(L, "fx_net_forward", i32, [vp, vp, i32, vp, i32, i32, vp])
     _sig(L, "fx_predict_volume", i32, [vp, u8p, i64, i64, i64, C.POINTER(InferOpts), f32p, u8p])
     _sig(L, "fx_predict_tiles_dev", i32, [vp, vp, i64, i64, i64, i64, i64, C.POINTER(InferOpts), i64, i64, vp, vp])
@@ -264,6 +267,22 @@ class Net:
         buf = np.zeros(256, dtype=np.float32)
         n = lib().fx_net_act_scales(self._h, buf.ctypes.data_as(C.POINTER(C.c_float)), 256)
         return buf[:n]
+
+    def layers(self) -> list[dict]:
+        """Conv layers in act_scales order: weights prefix, operand precision it runs with and
+        algorithmic FLOPs per tile."""
+        cap = 256
+        q = (C.c_int * cap)()
+        f = (C.c_double * cap)()
+        n = lib().fx_net_layer_precision(self._h, q, f, cap)
+        names = {0: "bf16", 1: "fp8", 2: "f16"}
+        return [{"name": lib().fx_net_layer_name(self._h, i).decode(), "precision": names[q[i]], "flops": f[i]}
+                for i in range(n)]
+
+    def set_layer_precision(self, precisions) -> None:
+        """fp8 nets: per conv layer (act_scales order) "fp8" or the 16-bit type ("f16")."""
+        v = (C.c_int * len(precisions))(*[PRECISIONS[p] for p in precisions])
+        check(lib().fx_net_set_layer_precision(self._h, v, len(precisions)))
 
     def profile(self, enable: bool) -> None:
         check(lib().fx_net_profile(self._h, 1 if enable else 0))

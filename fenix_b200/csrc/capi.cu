@@ -207,6 +207,34 @@ fx_status fx_net_set_act_scales(fx_net* n, const float* scales, int count) {
     });
 }
 
+fx_status fx_net_set_layer_precision(fx_net* n, const int* prec, int count) {
+    return guarded([&]() -> fx_status {
+        if (!n || !prec) return set_err(FX_INVALID_ARGUMENT, "fx_net_set_layer_precision: null argument");
+        // fx_precision -> operand type: FX_PREC_FP8 = e4m3, FX_PREC_BF16 = bf16, FX_PREC_F16 = f16
+        std::vector<int> q(static_cast<size_t>(std::max(count, 0)));
+        for (int i = 0; i < count; ++i)
+            q[i] = prec[i] == FX_PREC_FP8 ? fxk::kOpE4M3 : (prec[i] == FX_PREC_BF16 ? fxk::kOpBF16 : fxk::kOpF16);
+        fxh::Status st = n->net.set_layer_precision(q.data(), count);
+        return st.ok() ? FX_OK : set_err(st);
+    });
+}
+
+int fx_net_layer_precision(const fx_net* n, int* prec, double* flops, int cap) {
+    if (!n) return 0;
+    const auto q = n->net.layer_precision();
+    const auto f = n->net.layer_flops();
+    for (int i = 0; i < cap && i < static_cast<int>(q.size()); ++i) {
+        if (prec) prec[i] = q[i] == fxk::kOpE4M3 ? FX_PREC_FP8 : (q[i] == fxk::kOpBF16 ? FX_PREC_BF16 : FX_PREC_F16);
+        if (flops) flops[i] = f[i];
+    }
+    return static_cast<int>(q.size());
+}
+
+const char* fx_net_layer_name(const fx_net* n, int i) {
+    const fxh::Layer* L = n ? n->net.layer_at(i) : nullptr;
+    return L ? L->name.c_str() : nullptr;
+}
+
 int fx_net_act_scales(const fx_net* n, float* out, int cap) {
     if (!n) return 0;
     auto v = n->net.act_scales();

@@ -855,7 +855,7 @@ Status Net::finalize_in(Layer& L, int nb, cudaStream_t s) {
 // Operand precision of one layer: e4m3 for fp8 nets once calibrated, except the first conv
 // (always bf16) and layers whose input channels do not fill whole e4m3 MMA K-steps (32).
 int Net::layer_q(const Layer& L, bool calib) const {
-    if (prec_ != 1 || calib || L.kind == Layer::kFirst) return t16();
+    if (prec_ != 1 || calib || L.kind == Layer::kFirst || L.keep16) return t16();
     return L.Cin % 32 == 0 ? fxk::kOpE4M3 : t16();
 }
 
@@ -1192,8 +1192,8 @@ Status Net::calibrate(const uint8_t* host_patches, int n) {
     set_scales_from_amax();
     for (auto* v : {&enc_, &up_, &dec_})
         for (Layer& L : *v) {
+            L.prog[1] = DevProgram{};  // scales changed: every e4m3 program is stale
             if (layer_q(L, false) != fxk::kOpE4M3) continue;
-            L.prog[1] = DevProgram{};
             if ((st = build_layer(L, 1)).code) return st;
         }
     calibrated_ = true;
@@ -1213,12 +1213,62 @@ Status Net::set_act_scales(const float* scales, int n) {
         for (Layer& L : *v) L.in_scale = scales[k++];
     for (auto* v : {&enc_, &up_, &dec_})
         for (Layer& L : *v) {
+            L.prog[1] = DevProgram{};  // scales changed: every e4m3 program is stale
             if (layer_q(L, false) != fxk::kOpE4M3) continue;
-            L.prog[1] = DevProgram{};
             if ((st = build_layer(L, 1)).code) return st;
         }
     calibrated_ = true;
     return ok();
+}
+
+Status Net::set_layer_precision(const int* q, int n) {
+    const int total = static_cast<int>(enc_.size() + up_.size() + dec_.size());
+    if (n != total) return fail(kInvalid, "set_layer_precision: expected " + std::to_string(total) + " entries");
+    for (int i = 0; i < n; ++i)
+        if (q[i] != fxk::kOpE4M3 && q[i] != t16())
+            return fail(kInvalid, "set_layer_precision: entries must be fp8 or the net's 16-bit type");
+    if (prec_ != 1) {
+        for (int i = 0; i < n; ++i)
+            if (q[i] == fxk::kOpE4M3) return fail(kInvalid, "set_layer_precision: the net is not fp8");
+        return ok();
+    }
+    cudaSetDevice(dev_);
+    int k = 0;
+    for (auto* v : {&enc_, &up_, &dec_})
+        for (Layer& L : *v) L.keep16 = q[k++] != fxk::kOpE4M3;
+    if (!calibrated_) return ok();  // calibration builds the e4m3 programs
+    Status st;
+    for (auto* v : {&enc_, &up_, &dec_})
+        for (Layer& L : *v)
+            if (layer_q(L, false) == fxk::kOpE4M3 && !L.prog[1].built && (st = build_layer(L, 1)).code) return st;
+    return ok();
+}
+
+std::vector<int> Net::layer_precision() const {
+    std::vector<int> out;
+    for (auto* v : {&enc_, &up_, &dec_})
+        for (const Layer& L : *v) out.push_back(layer_q(L, false));
+    return out;
+}
+
+const Layer* Net::layer_at(int i) const {
+    for (auto* v : {&enc_, &up_, &dec_}) {
+        if (i >= 0 && i < static_cast<int>(v->size())) return &(*v)[i];
+        i -= static_cast<int>(v->size());
+    }
+    return nullptr;
+}
+
+std::vector<double> Net::layer_flops() const {
+    std::vector<double> out;
+    for (auto* v : {&enc_, &up_, &dec_})
+        for (const Layer& L : *v) {
+            const ActGeom gi = level(L.lin), go = level(L.lout);
+            const double vin = static_cast<double>(gi.D) * gi.H * gi.W, vout = static_cast<double>(go.D) * go.H * go.W;
+            const double taps = L.kind == Layer::kProj ? (L.stride == 2 ? 8.0 : 1.0) : 27.0;
+            out.push_back(L.kind == Layer::kUp ? 2.0 * L.Cin * L.Cout * 8.0 * vin : 2.0 * taps * L.Cin * L.Cout * vout);
+        }
+    return out;
 }
 
 std::vector<float> Net::act_scales() const {

@@ -76,6 +76,7 @@ struct Layer {
     std::vector<float> gamma, beta;   // InstanceNorm affine
     std::vector<float> wscale;        // fp8 per-output-channel weight scale (amax / 448)
     float in_scale = 1.f;             // fp8 per-tensor scale of the input activation
+    bool keep16 = false;              // fp8 nets: precision schedule keeps this layer on 16-bit operands
     DevProgram prog[3];               // indexed by fxk::OpType: bf16, e4m3, f16
     float* d_gamma = nullptr;
     float* d_beta = nullptr;
@@ -154,6 +155,15 @@ class Net {
     cudaStream_t stream() const { return stream_; }
     bool calibrated() const { return calibrated_; }
     std::vector<float> act_scales() const;
+    // Precision schedule of an fp8 net, one entry per conv layer in act_scales() order:
+    // fxk::kOpE4M3 (e4m3 where the layer can take it) or the 16-bit type. Layers that cannot run
+    // e4m3 (the first conv, input channels not a multiple of 32) stay 16-bit whatever is asked.
+    Status set_layer_precision(const int* q, int n);
+    // The operand type each conv layer runs with (act_scales() order).
+    std::vector<int> layer_precision() const;
+    // Algorithmic FLOPs (2 x MACs) of one forward of one tile through each conv layer.
+    std::vector<double> layer_flops() const;
+    const Layer* layer_at(int i) const;
 
     // Per-conv-launch device timing with CUDA events on the launching stream (off by default).
     struct ProfileTotals {

@@ -113,6 +113,19 @@ fx_status fx_net_calibrate(fx_net* net, const uint8_t* host_patches, int n);
 int fx_net_act_scales(const fx_net* net, float* out, int cap);
 /* fp8 only: install previously calibrated scales (same order and count) instead of calibrating. */
 fx_status fx_net_set_act_scales(fx_net* net, const float* scales, int count);
+/* Precision schedule of an fp8 net (mixed precision, the per-layer counterpart of the
+ * reference's sensitive-layer notes, docs/design/fp8-conv3d-sm120.md:71-103): one entry per conv
+ * layer in fx_net_act_scales order, FX_PREC_FP8 for e4m3 operands or the net's 16-bit type
+ * (FX_PREC_F16 for fp8 nets) to keep that layer on 16-bit operands. Layers that cannot take e4m3
+ * (the first conv, input channels not a multiple of 32) stay 16-bit. Default: every eligible
+ * layer e4m3. */
+fx_status fx_net_set_layer_precision(fx_net* net, const int* precision, int count);
+/* The operand precision each conv layer runs with (fx_precision values, fx_net_act_scales order)
+ * and, when flops is non-NULL, its algorithmic FLOPs per tile (2 x MACs); returns the count. */
+int fx_net_layer_precision(const fx_net* net, int* precision, double* flops, int cap);
+/* The weights-file prefix of conv layer i (fx_net_act_scales order), e.g.
+ * "decoder.stages.3.convs.0"; NULL when out of range. Valid while the net lives. */
+const char* fx_net_layer_name(const fx_net* net, int i);
 
 /* Forward `nb` device-resident u8 tiles ([nb][P][P][P]) through the net and write the selected
  * class probability ([nb][P][P][P] f32, device). Each tile is z-scored on its own (norm_patch).

@@ -21,6 +21,29 @@ def build() -> Path:
     return LIB
 
 
+class Spiral(C.Structure):
+    _fields_ = [(k, C.c_double) for k in ("pitch", "thickness", "sheet_mean", "sheet_sd", "bg_mean", "bg_sd",
+                                          "blur_sigma", "speckle_sd")]
+
+
+# The synthetic volumes of the benchmark configurations (checker-side copy of the recipe).
+SPIRAL_CONFIG1 = dict(pitch=12, thickness=3, sheet_mean=170, sheet_sd=15, bg_mean=40, bg_sd=10, blur_sigma=1.0,
+                      speckle_sd=0.0)
+SPIRAL_CONFIG3 = dict(SPIRAL_CONFIG1, pitch=16, speckle_sd=8.0)
+
+
+def synth_spiral(shape, seed, params=None, z_begin=0, z_end=None):
+    """The spiral-sheet synthetic CT [z_end - z_begin][dy][dx] u8 (oracle/synth.c)."""
+    dz, dy, dx = shape
+    z_end = dz if z_end is None else z_end
+    p = Spiral(**(params or SPIRAL_CONFIG1))
+    out = np.empty((z_end - z_begin, dy, dx), dtype=np.uint8)
+    if lib().fxo_synth_spiral(out.ctypes.data_as(C.POINTER(C.c_uint8)), dz, dy, dx, C.byref(p), seed, z_begin,
+                              z_end):
+        raise ValueError("fxo_synth_spiral: bad arguments")
+    return out
+
+
 def lib():
     global _lib
     if _lib is None:
@@ -55,6 +78,8 @@ def lib():
         L.fxv_crc32c.argtypes = [vp, C.c_size_t]
         L.fxv_morton3.restype = C.c_uint64
         L.fxv_morton3.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64]
+        L.fxo_synth_spiral.restype = i32
+        L.fxo_synth_spiral.argtypes = [u8p, i64, i64, i64, C.POINTER(Spiral), C.c_uint64, i64, i64]
         _lib = L
     return _lib
 

@@ -8,6 +8,13 @@ Runs only where the reference tree is present (it compiles oracle/_ref from it):
                       + nets::ConvStack through libtorch, fp32, batch 2 so no fp16 round trip) on
                       seeded synthetic volumes with seeded random-init plain UNets: the u8-encoded
                       probability map, exact f32 values at 4096 sampled voxels, and sum / mean.
+  * net128_<case>.npz — the BASELINE configurations at their own 128^3 tile size, with the FULL
+                      probability map (quantised to u16: round(p * 65535), error <= 7.7e-6):
+                      config 1 (one 128^3 tile, 16/32/64/128 net, weight seed 0), config 2 (two
+                      128^3 patches in one batch of 2, 32..320 net, weight seed 1, volume seed 1) and
+                      config 3 (the central 192^3 crop [416, 608)^3 of the 1024^3 seed-2 speckled
+                      volume: 8 tiles at overlap 0.5, so the middle third of every axis is a
+                      blend of two tiles; the benchmark's weight seed 1).
   * resenc_<case>.npz — the same with the reference's own nets::ResEncUNet (residual encoder,
                       optional scSE, plain or task naming) loaded from seeded random-init weights.
   * fxvol_tiles.npz — the reference's encode_tile_dct payloads of the 64^3 chunks of
@@ -44,6 +51,25 @@ CASES = {
     "cfg2_p64": ((32, 64, 128, 256, 320), 1, (64, 64, 64), 1, fx.SPIRAL_CONFIG1, 64, 0.5),
     "cfg3_p64": ((32, 64, 128, 256, 320), 2, (96, 96, 96), 2, fx.SPIRAL_CONFIG3, 64, 0.5),
 }
+
+# name: (features, weight seed, full volume shape, crop origin (None: whole), crop extent, volume
+# seed, spiral params, patch, overlap)
+CASES128 = {
+    "cfg1": ((16, 32, 64, 128), 0, (128, 128, 128), None, None, 0, fx.SPIRAL_CONFIG1, 128, 0.5),
+    "cfg2": ((32, 64, 128, 256, 320), 1, (256, 128, 128), None, None, 1, fx.SPIRAL_CONFIG1, 128, 0.0),
+    "cfg3": ((32, 64, 128, 256, 320), 1, (1024, 1024, 1024), (416, 416, 416), (192, 192, 192), 2, fx.SPIRAL_CONFIG3,
+             128, 0.5),
+}
+
+
+def volume128(name):
+    """The input volume of a net128 case (a crop of the full synthetic where the case has one)."""
+    feats, wseed, full, org, ext, vseed, sp, P, ov = CASES128[name]
+    if org is None:
+        return fx.synth_spiral(full, vseed, sp)
+    slab = fx.synth_spiral(full, vseed, sp, org[0], org[0] + ext[0])
+    return np.ascontiguousarray(slab[:, org[1]:org[1] + ext[1], org[2]:org[2] + ext[2]])
+
 
 # name: (features, blocks, scSE, plain naming, weight seed, volume shape, volume seed, patch, overlap)
 RESENC = {
@@ -95,6 +121,32 @@ def net_case(name):
         ref_threads=np.int64(info["threads"]),
     )
     print(f"net_{name}.npz: shape {shape}, {info}")
+
+
+def net128_case(name):
+    feats, wseed, full, org, ext, vseed, sp, P, ov = CASES128[name]
+    vol = volume128(name)
+    with tempfile.TemporaryDirectory() as td:
+        w = make_plain_unet(Path(td) / "w.fxweights", feats, nconv=2, ncls=2, seed=wseed)
+        prob, info = orc.ref_infer(w, vol, P, ov, batch=2)
+    np.savez_compressed(
+        HERE / f"net128_{name}.npz",
+        prob_u16=np.round(np.clip(prob, 0.0, 1.0).astype(np.float64) * 65535.0).astype(np.uint16),
+        prob_sum=np.float64(prob.astype(np.float64).sum()),
+        features=np.array(feats, dtype=np.int64),
+        weight_seed=np.int64(wseed),
+        full_shape=np.array(full, dtype=np.int64),
+        crop_origin=np.array(org if org else (0, 0, 0), dtype=np.int64),
+        shape=np.array(vol.shape, dtype=np.int64),
+        volume_seed=np.int64(vseed),
+        spiral=np.array([sp[k] for k in ("pitch", "thickness", "sheet_mean", "sheet_sd", "bg_mean", "bg_sd",
+                                         "blur_sigma", "speckle_sd")]),
+        patch=np.int64(P),
+        overlap=np.float64(ov),
+        ref_seconds=np.float64(info["seconds"]),
+        ref_threads=np.int64(info["threads"]),
+    )
+    print(f"net128_{name}.npz: shape {vol.shape}, {info}")
 
 
 def resenc_case(name):
@@ -174,6 +226,9 @@ def main():
     for name in CASES:
         if a.only in (None, name):
             net_case(name)
+    for name in CASES128:
+        if a.only in (None, "net128_" + name):
+            net128_case(name)
     for name in RESENC:
         if a.only in (None, "resenc_" + name):
             resenc_case(name)
