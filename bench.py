@@ -7,10 +7,16 @@ classes + softmax), random Kaiming init (seed 1), fp8 e4m3 operands with per-out
 scales and per-tensor activation scales calibrated on 4 seeded patches; a synthetic 1024^3 u8
 spiral-sheet volume (pitch 16, thickness 3, N(0,8) speckle, seed 2); 128^3 tiles at overlap 0.5
 (3375 tiles) with Gaussian blending, normalised and encoded to u8. One step = one full pass over
-the volume. Multi-GPU: the volume is split into z-slabs by tile ranges (fenix_b200/shard.py), the
-tile-overlap bands are exchanged over NCCL, each GPU finalises the planes it owns.
+the volume. Multi-GPU: the volume is split into z-slabs by tile ranges (fenix_b200/shard.py); each
+owner reads the tile-overlap bands its neighbours accumulated straight from their HBM over NVLink
+(CUDA IPC mappings, an add kernel doing the loads) and finalises the planes it owns. The ranks'
+process group is gloo (host barriers and the timing reduction); nothing goes through NCCL.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fenix|reference] [--precision fp8|f16|bf16]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fenix|reference] [--precision fp8|fp8-all|f16|bf16]
+
+--precision fp8 (the default) is the calibrated mixed schedule: e4m3 operands in the layers the
+calibration picks (fx_net_calibrate_schedule, Dice >= 0.993 against the net's 16-bit forward on the
+4 calibration patches), f16 in the rest; fp8-all puts every layer that can take e4m3 on it.
 
 For N > 1 launch one process per GPU with torch.distributed.run. Rank 0 prints one JSON line.
 """
@@ -35,6 +41,8 @@ sys.path.insert(0, str(ROOT))
 METRIC = "Mvoxels/s fp8 3D-UNet sliding-window inference @1/2/4/8 B200; % tcgen05 peak"
 FEATURES = (32, 64, 128, 256, 320)
 WEIGHT_SEED, VOLUME_SEED, CALIB_SEED0 = 1, 2, 1000
+SCHED_DICE = 0.993  # the fp8 schedule's agreement with the 16-bit forward on the calibration patches
+PARITY_CASE = ROOT / "tests" / "golden" / "net128_cfg3.npz"  # the reference's map of a 192^3 crop
 # DRAM traffic of the 22 conv launches of one fp8 forward, per 128^3 tile (dram__bytes_read.sum +
 # dram__bytes_write.sum from an ncu launch list of `bench.py --size 256 --steps 1 --warmup 3`:
 # 4.563 GB read + 5.933 GB written per forward of 8 tiles). ncu cannot run inside the timed bench,
@@ -240,13 +248,46 @@ def fxvol_measure(vol_u8: np.ndarray, pred_u8: np.ndarray, tmp: str, reps: int =
     return res
 
 
+def precision_report(net, sched):
+    """Which conv layers ran e4m3 and the share of the algorithmic FLOPs they carry."""
+    layers = net.layers()
+    tot = sum(l["flops"] for l in layers)
+    f8 = [l for l in layers if l["precision"] == "fp8"]
+    out = {"fp8_layers": [l["name"] for l in f8], "fp8_flop_share": sum(l["flops"] for l in f8) / tot,
+           "layers": len(layers)}
+    if sched:
+        out.update(sched)
+    return out
+
+
+def parity_check(fx, net, batch, precision):
+    """The benchmark's net, calibration and schedule on the central 192^3 crop of the same volume,
+    against the reference's own CPU inference of that crop (tests/golden/net128_cfg3.npz, every
+    voxel): max |dp| and Dice of the 0.5-thresholded masks, beside the bounds the path is held to."""
+    g = np.load(PARITY_CASE)
+    full, org, shape = (tuple(int(v) for v in g[k]) for k in ("full_shape", "crop_origin", "shape"))
+    slab = fx.synth_spiral(full, int(g["volume_seed"]), fx.SPIRAL_CONFIG3, org[0], org[0] + shape[0])
+    vol = np.ascontiguousarray(slab[:, org[1]:org[1] + shape[1], org[2]:org[2] + shape[2]])
+    prob, _ = net.predict_volume(vol, overlap=float(g["overlap"]), batch=batch, want_u8=False)
+    ref = g["prob_u16"].astype(np.float32) / np.float32(65535.0)
+    e = np.abs(prob - ref)
+    a, b = prob >= 0.5, ref >= 0.5
+    dice = float(2.0 * (a & b).sum() / max(int(a.sum() + b.sum()), 1))
+    bound = 3e-2 if precision == "fp8" else 1e-2
+    return {"case": f"central {shape[0]}^3 crop of the benchmark volume ({len(fx.tile_starts(shape[0], 128, 0.5)) ** 3} "
+                    "tiles), reference = its own CPU inference (libtorch fp32), every voxel",
+            "max_abs": float(e.max()), "mean_abs": float(e.mean()), "dice": dice,
+            "bound_max_abs": bound, "bound_dice": 0.99 if precision == "fp8" else None,
+            "meets_max_abs": bool(e.max() <= bound), "meets_dice": bool(dice >= 0.99)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="fenix", choices=["fenix", "reference"])
-    ap.add_argument("--precision", default="fp8", choices=["fp8", "f16", "bf16"])
+    ap.add_argument("--precision", default="fp8", choices=["fp8", "fp8-all", "f16", "bf16"])
     ap.add_argument("--size", type=int, default=1024)
     ap.add_argument("--patch", type=int, default=128)
     ap.add_argument("--overlap", type=float, default=0.5)
@@ -273,8 +314,8 @@ def main():
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
+        # host plumbing only (barriers, the IPC hand-over, the timing reduction): no NCCL anywhere
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
         group = dist.group.WORLD
 
     def barrier():
@@ -285,10 +326,26 @@ def main():
     shape = (S, S, S)
     tmp = tempfile.mkdtemp(prefix=f"fxbench{rank}_")
     wpath = make_plain_unet(Path(tmp) / "w.fxweights", FEATURES, seed=WEIGHT_SEED)
-    net = fx.Net(wpath, P, max_batch=args.batch, precision=args.precision, device=local)
-    if args.precision == "fp8":
-        calib = np.stack([fx.synth_spiral((P, P, P), CALIB_SEED0 + i, fx.SPIRAL_CONFIG3) for i in range(4)])
-        net.calibrate(calib)
+    fp8 = args.precision.startswith("fp8")
+    net = fx.Net(wpath, P, max_batch=args.batch, precision="fp8" if fp8 else args.precision, device=local)
+    sched = None
+    if fp8:
+        # rank 0 calibrates (scales and schedule) and hands the result to the others, so every slab
+        # is computed by the same network
+        got = [None]
+        if rank == 0:
+            calib = np.stack([fx.synth_spiral((P, P, P), CALIB_SEED0 + i, fx.SPIRAL_CONFIG3) for i in range(4)])
+            net.calibrate(calib)
+            if args.precision == "fp8":
+                d_cal, m_cal = net.calibrate_schedule(calib, min_dice=SCHED_DICE)
+                sched = {"calibration_dice": d_cal, "calibration_max_abs": m_cal, "target_dice": SCHED_DICE}
+            got = [(net.act_scales().tolist(), [l["precision"] for l in net.layers()], sched)]
+        if world > 1:
+            torch.distributed.broadcast_object_list(got, src=0)
+            if rank != 0:
+                scales, precs, sched = got[0]
+                net.set_act_scales(scales)
+                net.set_layer_precision(["fp8" if p == "fp8" else "f16" for p in precs])
     sp = ShardedPredictor(net, shape, args.overlap, args.batch, rank=rank, world=world, group=group)
     me = sp.me
     # this rank's input slab, generated on the host (pinned), and its output planes
@@ -312,7 +369,7 @@ def main():
         barrier()
         ms = ev0.elapsed_time(ev1)
         if world > 1:
-            t = torch.tensor([ms], device="cuda")
+            t = torch.tensor([ms], dtype=torch.float64)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             ms = float(t.item())
         return ms
@@ -331,8 +388,8 @@ def main():
         e2e_path = "fx_predict_volume (C ABI) with pinned host u8 input and u8 output"
     else:
         e2e_step = lambda: sp.run(host_slab=host_slab, host_out=host_out, stream=stream)  # noqa: E731
-        e2e_path = ("fenix_b200.shard.ShardedPredictor over fx_predict_tiles_dev / fx_accum_add / fx_accum_finalize "
-                    "with pinned host input slab and output planes")
+        e2e_path = ("fenix_b200.shard.ShardedPredictor over fx_predict_tiles_dev / fx_accum_add (neighbour bands read "
+                    "over NVLink) / fx_accum_finalize with pinned host input slab and output planes")
     for _ in range(args.warmup):
         dev_step()
     torch.cuda.synchronize()
@@ -356,10 +413,14 @@ def main():
     dev_step()
     net.profile(False)
     prof = net.profile_read()
+    h2d, d2h = sp.h2d_bytes, sp.d2h_bytes
     if world > 1:
-        t = torch.tensor([float(launches)], device="cuda")
+        t = torch.tensor([float(launches), float(h2d), float(d2h)], dtype=torch.float64)
         torch.distributed.all_reduce(t)
-        launches = int(t.item())
+        launches, h2d, d2h = (int(v) for v in t.tolist())
+    parity = None
+    if rank == 0 and S == 1024 and P == 128 and args.overlap == 0.5 and PARITY_CASE.exists():
+        parity = parity_check(fx, net, args.batch, "fp8" if fp8 else args.precision)
     vox = float(S) ** 3
     value = vox * args.steps / (ms / 1e3) / 1e6
     e2e = vox * args.steps / (ms_e2e / 1e3) / 1e6
@@ -367,7 +428,7 @@ def main():
     conv_tflops = prof["conv_flops"] / (prof["conv_ms"] / 1e3) / 1e12
     # the conv launches are timed inside a seconds-long step, so the denominator is the sustained
     # (power-capped) GEMM rate; the burst fraction is reported beside it
-    mult = 2.0 if args.precision == "fp8" else 1.0
+    mult = 2.0 if fp8 else 1.0
     peak, peak_burst = mult * bf16_sus, mult * bf16_burst
     cpu = None
     if world == 1 and not args.no_cpu_baseline and (ROOT / "oracle" / "_ref" / "ref_infer").exists():
@@ -388,33 +449,37 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "Mvoxels/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": {"fp8": "e4m3", "f16": "f16", "bf16": "bf16"}[args.precision],
+            "vs_baseline": None,
+            "dtype": {"fp8": "e4m3 + f16 (calibrated schedule)", "fp8-all": "e4m3", "f16": "f16", "bf16": "bf16"}[args.precision],
             "data": f"synthetic: {S}^3 u8 spiral sheet (pitch 16, thickness 3, N(170,15)/N(40,10), blur 1, N(0,8) "
                     "speckle, seed 2); random-init Kaiming weights (seed 1); fp8 scales calibrated on 4 seeded patches",
             "config": workload_config(args, tiles, world),
             "roofline": {
                 "bound": "tensor", "achieved": conv_tflops, "peak": peak, "unit": "TFLOP/s", "frac": conv_tflops / peak,
-                "traffic": CONV_DRAM_BYTES_PER_TILE if args.precision == "fp8" else None,
+                "traffic": CONV_DRAM_BYTES_PER_TILE if args.precision == "fp8-all" else None,
                 "traffic_unit": "DRAM bytes per 128^3 tile over the 22 conv launches (ncu capture, 256^3 bench)",
                 "algorithmic_flops_per_tile": 945.2e9,
                 "kernel": "conv_tc_kernel (all 22 conv launches of one forward, summed)",
                 "peak_source": (f"2 x {peak_src} bf16 sustained (e4m3 rate is twice bf16 on tcgen05); kernel timed "
-                                "inside a seconds-long step" if args.precision == "fp8"
+                                "inside a seconds-long step" if fp8
                                 else f"{peak_src} bf16 sustained; kernel timed inside a seconds-long step"),
                 "peak_burst": peak_burst, "frac_burst": conv_tflops / peak_burst,
                 "conv_ms_per_step": prof["conv_ms"], "conv_flops_per_step": prof["conv_flops"],
                 "fp8_flop_share": prof["fp8_flops"] / max(prof["conv_flops"], 1.0),
                 "conv_share_of_step": prof["conv_ms"] / (ms / args.steps),
-                "frac_nominal_4500": conv_tflops / (4500.0 if args.precision == "fp8" else 2250.0),
+                "frac_nominal_4500": conv_tflops / (4500.0 if fp8 else 2250.0),
             },
-            "e2e": {"value": e2e, "unit": "Mvoxels/s", "h2d_bytes_per_step": sp.h2d_bytes * world,
-                    "d2h_bytes_per_step": sp.d2h_bytes * world, "path": e2e_path},
+            "precision_schedule": precision_report(net, sched),
+            "parity": parity,
+            "e2e": {"value": e2e, "unit": "Mvoxels/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": e2e_path},
             "cpu_baseline": cpu,
             "fxvol": fxv,
             "clocks": clk,
             "gpu_launches": launches,
         }
         print(json.dumps(line))
+    sp.close()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

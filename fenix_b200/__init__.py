@@ -17,6 +17,7 @@ LIB_PATH = _PKG / "_build" / "libfenix_b200.so"
 _lib = None
 
 FX_OK = 0
+FX_INVALID_ARGUMENT = 1
 STATUS_NAMES = {
     0: "ok",
     1: "invalid_argument",
@@ -105,10 +106,20 @@ def lib():
     _sig(L, "fx_net_set_layer_precision", i32, [vp, C.POINTER(C.c_int), i32])
     _sig(L, "fx_net_layer_precision", i32, [vp, C.POINTER(C.c_int), C.POINTER(C.c_double), i32])
     _sig(L, "fx_net_layer_name", C.c_char_p, [vp, i32])
+    _sig(L, "fx_net_calibrate_schedule", i32, [vp, u8p, i32, C.c_double, C.c_double, C.POINTER(C.c_double),
+                                               C.POINTER(C.c_double)])
+    _sig(L, "fx_shard_plan", i32, [i64, i64, i64, i32, C.c_double, i32, vp])
+    _sig(L, "fx_ipc_buffer_alloc", i32, [i32, C.c_uint64, C.POINTER(vp), vp])
+    _sig(L, "fx_ipc_buffer_free", i32, [i32, vp])
+    _sig(L, "fx_ipc_open", i32, [i32, vp, C.POINTER(vp)])
+    _sig(L, "fx_ipc_close", i32, [i32, vp])
+    _sig(L, "fx_predict_volume_multi", i32, [C.POINTER(vp), i32, u8p, i64, i64, i64, C.POINTER(InferOpts), f32p, u8p])
     _sig(L, "fx_net_forward", i32, [vp, vp, i32, vp, i32, i32, vp])
     _sig(L, "fx_predict_volume", i32, [vp, u8p, i64, i64, i64, C.POINTER(InferOpts), f32p, u8p])
     _sig(L, "fx_predict_tiles_dev", i32, [vp, vp, i64, i64, i64, i64, i64, C.POINTER(InferOpts), i64, i64, vp, vp])
     _sig(L, "fx_accum_add", i32, [vp, vp, i64, vp])
+    _sig(L, "fx_net_device_status", i32, [vp])
+    _sig(L, "fx_selftest_wait_timeout", i32, [i32, C.c_uint64, C.POINTER(C.c_uint32)])
     _sig(L, "fx_tile_starts", i64, [i64, i32, C.c_double, C.POINTER(C.c_int64), i64])
     _sig(L, "fx_gaussian1d", None, [i32, f32p])
     _sig(L, "fx_weight_profile", None, [f32p, i32, C.POINTER(C.c_int64), i64, i64, i64, i64, f32p])
@@ -278,6 +289,15 @@ class Net:
         names = {0: "bf16", 1: "fp8", 2: "f16"}
         return [{"name": lib().fx_net_layer_name(self._h, i).decode(), "precision": names[q[i]], "flops": f[i]}
                 for i in range(n)]
+
+    def calibrate_schedule(self, patches_u8: np.ndarray, min_dice: float = 0.99, max_abs: float = 0.0):
+        """fp8 nets: choose which layers run e4m3 from calibration patches (fx_net_calibrate_schedule);
+        returns (Dice, max |dp|) of the schedule against the net's 16-bit forward."""
+        p = np.ascontiguousarray(patches_u8, dtype=np.uint8)
+        d, m = C.c_double(), C.c_double()
+        check(lib().fx_net_calibrate_schedule(self._h, p.ctypes.data_as(C.POINTER(C.c_uint8)), p.shape[0], min_dice,
+                                              max_abs, C.byref(d), C.byref(m)))
+        return d.value, m.value
 
     def set_layer_precision(self, precisions) -> None:
         """fp8 nets: per conv layer (act_scales order) "fp8" or the 16-bit type ("f16")."""

@@ -108,6 +108,7 @@ fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t 
     cudaStreamSynchronize(s);
     cudaFree(d_w);
     if (e != cudaSuccess) return set_err(cuda_status(e, "accum_finalize"));
+    if ((st = n->net.take_device_status()).code) return set_err(st);  // a bounded wait that gave up
     return FX_OK;
 }
 }  // namespace fxh
@@ -219,6 +220,15 @@ fx_status fx_net_set_layer_precision(fx_net* n, const int* prec, int count) {
     });
 }
 
+fx_status fx_net_calibrate_schedule(fx_net* n, const uint8_t* host_patches, int count, double min_dice, double max_abs,
+                                    double* dice, double* maxabs) {
+    return guarded([&]() -> fx_status {
+        if (!n || !host_patches) return set_err(FX_INVALID_ARGUMENT, "fx_net_calibrate_schedule: null argument");
+        fxh::Status st = n->net.calibrate_schedule(host_patches, count, min_dice, max_abs, dice, maxabs);
+        return st.ok() ? FX_OK : set_err(st);
+    });
+}
+
 int fx_net_layer_precision(const fx_net* n, int* prec, double* flops, int cap) {
     if (!n) return 0;
     const auto q = n->net.layer_precision();
@@ -265,6 +275,7 @@ fx_status fx_net_forward(fx_net* n, const uint8_t* dev_tiles, int nb, float* dev
         cudaFree(d_org);
         if (!st.ok()) return set_err(st);
         if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "forward"));
+        if ((st = n->net.take_device_status()).code) return set_err(st);
         return FX_OK;
     });
 }
@@ -283,6 +294,67 @@ fx_status fx_predict_tiles_dev(fx_net* n, const uint8_t* dev_slab, int64_t slab_
                                               o->channel, o->sigmoid, o->batch, tile_begin, tile_end, dev_acc, s, 0,
                                               -1, o->tta);
         return st.ok() ? FX_OK : set_err(st);
+    });
+}
+
+fx_status fx_net_device_status(fx_net* n) {
+    return guarded([&]() -> fx_status {
+        if (!n) return set_err(FX_INVALID_ARGUMENT, "fx_net_device_status: null net");
+        fxh::Status st = n->net.take_device_status();
+        return st.ok() ? FX_OK : set_err(st);
+    });
+}
+
+fx_status fx_selftest_wait_timeout(int device, uint64_t wait_ns, uint32_t* status_out) {
+    return guarded([&]() -> fx_status {
+        if (!status_out || wait_ns == 0) return set_err(FX_INVALID_ARGUMENT, "fx_selftest_wait_timeout: bad argument");
+        int ndev = 0;
+        if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+            return set_err(FX_INVALID_ARGUMENT, "fx_selftest_wait_timeout: no such device");
+        cudaSetDevice(device);
+        if (!is_sm100()) return set_err(FX_UNSUPPORTED, "fx_selftest_wait_timeout: needs an sm_100 GPU");
+        // one small stride-1 f16 conv (16 -> 128 channels over 8^3: the kernel's regular program)
+        fxh::Layer L;
+        L.name = "selftest";
+        L.kind = fxh::Layer::kConv;
+        L.Cin = 16;
+        L.Cout = 128;
+        L.stride = 1;
+        L.w.assign(static_cast<size_t>(L.Cout) * L.Cin * 27, 0.f);
+        const fxh::ActGeom g{8, 8, 8};
+        std::vector<void*> allocs;
+        struct Free {
+            std::vector<void*>& a;
+            ~Free() {
+                for (void* p : a) cudaFree(p);
+            }
+        } fr{allocs};
+        const int sms = sm_count_of_current();
+        fxh::Status st = fxh::build_layer_program(L, fxk::kOpF16, g, g, 1, sms, allocs);
+        if (!st.ok()) return set_err(st);
+        Scratch sc;
+        const int64_t igs = g.gs(), ibs = (L.Cin / 8) * igs, obs = (L.Cout / 8) * igs;
+        const int64_t nrec = std::max<int64_t>((g.rows() + 125) / 126, sms) * fxk::kStatRecsPerUnit;
+        auto* in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(ibs)));
+        auto* out = static_cast<uint8_t*>(sc.get(static_cast<size_t>(obs)));
+        L.d_partials = static_cast<float*>(sc.get(sizeof(float) * nrec * L.Cout * 2));
+        L.nrec_cap = nrec;
+        auto* d_status = static_cast<uint32_t*>(sc.get(sizeof(uint32_t)));
+        if (!in || !out || !L.d_partials || !d_status) return set_err(FX_INTERNAL, "cudaMalloc failed");
+        cudaStream_t s = nullptr;
+        cudaMemsetAsync(in, 0, static_cast<size_t>(ibs), s);
+        cudaMemsetAsync(L.d_partials, 0, sizeof(float) * nrec * L.Cout * 2, s);
+        cudaMemsetAsync(d_status, 0, sizeof(uint32_t), s);
+        st = fxh::launch_layer(L, fxk::kOpF16, g, g, in, ibs, igs, out, obs, igs, 0, 1.f, nullptr, 1, sms, d_status, s,
+                               true, wait_ns, 1);
+        if (!st.ok()) return set_err(st);
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "fx_selftest_wait_timeout"));
+        uint32_t v = 0;
+        if ((e = cudaMemcpy(&v, d_status, 4, cudaMemcpyDeviceToHost)) != cudaSuccess)
+            return set_err(fxh::cuda_status(e, "fx_selftest_wait_timeout"));
+        *status_out = v;
+        return FX_OK;
     });
 }
 
@@ -376,14 +448,12 @@ fx_status fx_norm_tiles(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t 
         for (int i = 0; i < ntiles; ++i) org[i] = {host_origins[3 * i], host_origins[3 * i + 1], host_origins[3 * i + 2]};
         auto* d_org = static_cast<fxk::TileOrigin*>(sc.get(sizeof(fxk::TileOrigin) * ntiles));
         auto* d_sums = static_cast<unsigned long long*>(sc.get(sizeof(unsigned long long) * 2 * ntiles));
-        const fxh::ActGeom g{patch, patch, patch};
-        auto* d_l0 = static_cast<uint8_t*>(sc.get(static_cast<size_t>(ntiles) * g.gs()));
-        if (!d_org || !d_sums || !d_l0) return set_err(FX_INTERNAL, "cudaMalloc failed");
+        if (!d_org || !d_sums) return set_err(FX_INTERNAL, "cudaMalloc failed");
         cudaMemcpyAsync(d_org, org.data(), sizeof(fxk::TileOrigin) * ntiles, cudaMemcpyHostToDevice, s);
         cudaMemsetAsync(d_sums, 0, sizeof(unsigned long long) * 2 * ntiles, s);
         cudaError_t e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, s);
         if (e == cudaSuccess)
-            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, d_l0, g.gs(), fxk::kOpF16,
+            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, nullptr, 0, 0, fxk::kOpF16,
                                       dev_out, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles"));
@@ -434,11 +504,11 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
         int64_t ibs, igs;
         if (L.kind == fxh::Layer::kFirst) {
             igs = gin.gs();
-            ibs = igs;
+            ibs = 2 * igs;
             in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * ibs));
             if (!in) return set_err(FX_INTERNAL, "cudaMalloc failed");
             cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
-            fxk::launch_pack_first(dev_x, B, D, H, W, in, ibs, q, s);
+            fxk::launch_pack_first(dev_x, B, D, H, W, in, ibs, igs, q, s);
         } else if (stride == 1) {
             igs = gin.gs();
             ibs = (Cin / cg) * igs;
@@ -616,7 +686,7 @@ fx_status fx_norm_tiles_noalloc(const uint8_t* dev_vol, int64_t dz, int64_t dy, 
         if (e == cudaSuccess) e = cudaMemsetAsync(sums, 0, 2 * sizeof(unsigned long long) * ntiles, s);
         if (e == cudaSuccess) e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, org, ntiles, patch, sums, s);
         if (e == cudaSuccess)
-            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, org, ntiles, patch, sums, nullptr, 0, fxk::kOpF16, dev_out,
+            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, org, ntiles, patch, sums, nullptr, 0, 0, fxk::kOpF16, dev_out,
                                       s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles_noalloc"));

@@ -12,6 +12,8 @@ namespace {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate stage wait
 
+__device__ __forceinline__ uint64_t wait_limit(const ConvParams& p) { return p.wait_ns ? p.wait_ns : kWaitLimitNs; }
+
 // Optional cycle accounting per role (build with -DFX_CONV_TRACE; p.trace gets 16 counters):
 // [0] producer waiting for free stages, [1] producer issuing, [2] MMA waiting for drained
 // accumulators, [3] MMA waiting for full stages, [4] MMA issuing, [5] epilogue waiting for
@@ -42,11 +44,18 @@ struct SmemCtl {
     uint64_t drain;
     uint64_t xready[2][2];  // fold epilogue: row exchange of [half][parity] published by its 4 warps
     uint64_t bres;          // z-plane fold: the resident weights have landed
+    uint64_t never;         // failure self-test: a barrier nothing arrives at
     uint32_t tmem_base;
     int abort;
     alignas(16) float colscale[kMaxCols];
     alignas(16) float bias[kMaxCols];
 };
+
+// The barrier the MMA warp waits on for stage k: its full barrier, except in the failure self-test,
+// where the first stage's wait goes to a barrier nothing arrives at.
+__device__ __forceinline__ uint32_t stage_full_bar(const ConvParams& p, SmemCtl* ctl, int slot, uint32_t k) {
+    return (p.stall_first_wait && k == 0) ? smem_u32(&ctl->never) : smem_u32(&ctl->full[slot]);
+}
 
 __device__ __forceinline__ void unit_coords(const ConvParams& p, int unit, int& b, int& mu, int& nt) {
     nt = unit % p.n_tiles;
@@ -78,7 +87,7 @@ __device__ void producer_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, 
             bulk_g2s(smem_u32(smem + p.bres_off), p.wpack, static_cast<uint32_t>(p.bres_bytes), smem_u32(&ctl->bres));
         }
         __syncwarp();
-        const bool ok = mbar_wait(smem_u32(&ctl->bres), 0u, nullptr, kWaitLimitNs);
+        const bool ok = mbar_wait(smem_u32(&ctl->bres), 0u, nullptr, wait_limit(p));
         if (!__all_sync(0xffffffffu, ok)) {
             if (leader) {
                 set_status(p.status, kStatusTimeoutDrain);
@@ -96,7 +105,7 @@ __device__ void producer_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, 
             const uint32_t ph = (k / p.n_pipe) & 1u;
             {
                 FX_T0();
-                const bool ok = mbar_wait(smem_u32(&ctl->empty[slot]), ph ^ 1u, &ctl->abort, kWaitLimitNs);
+                const bool ok = mbar_wait(smem_u32(&ctl->empty[slot]), ph ^ 1u, &ctl->abort, wait_limit(p));
                 if (!__all_sync(0xffffffffu, ok)) {
                     if (leader) {
                         set_status(p.status, kStatusTimeoutEmpty);
@@ -139,7 +148,7 @@ drain:
     const uint32_t n_issued = k;
     for (uint32_t j = (n_issued > static_cast<uint32_t>(p.n_pipe) ? n_issued - p.n_pipe : 0u); j < n_issued; ++j) {
         const int slot = j % p.n_pipe;
-        const bool ok = mbar_wait(smem_u32(&ctl->full[slot]), (j / p.n_pipe) & 1u, nullptr, kWaitLimitNs);
+        const bool ok = mbar_wait(smem_u32(&ctl->full[slot]), (j / p.n_pipe) & 1u, nullptr, wait_limit(p));
         if (!__all_sync(0xffffffffu, ok)) {
             if (leader && !ctl->abort) set_status(p.status, kStatusTimeoutDrain);
             break;
@@ -174,7 +183,7 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
         const uint32_t aph = (j / p.acc_slots) & 1u;
         {
             FX_T0();
-            const bool ok = mbar_wait(smem_u32(&ctl->acce[aslot]), aph ^ 1u, &ctl->abort, kWaitLimitNs);
+            const bool ok = mbar_wait(smem_u32(&ctl->acce[aslot]), aph ^ 1u, &ctl->abort, wait_limit(p));
             if (!__all_sync(0xffffffffu, ok)) {
                 if (leader) {
                     set_status(p.status, kStatusTimeoutAccFree);
@@ -194,7 +203,7 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
             {
                 FX_T0();
                 const bool ok =
-                    mbar_wait(smem_u32(&ctl->full[slot]), (k / p.n_pipe) & 1u, &ctl->abort, kWaitLimitNs);
+                    mbar_wait(stage_full_bar(p, ctl, slot, k), (k / p.n_pipe) & 1u, &ctl->abort, wait_limit(p));
                 if (!__all_sync(0xffffffffu, ok)) {
                     if (leader) {
                         set_status(p.status, kStatusTimeoutFull);
@@ -247,7 +256,7 @@ __device__ void mma_loop(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n
     mma_commit_if(leader, smem_u32(&ctl->drain));
     if (leader) {
         const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < wait_limit(p)) {
         }
     }
     __syncwarp();
@@ -285,7 +294,7 @@ __device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int
     const uint64_t kzs = static_cast<uint64_t>(p.zkstride >> 4);  // rows of tap kz -> kz + 1
     const int nent = p.n_mmas;
     {
-        const bool ok = mbar_wait(smem_u32(&ctl->bres), 0u, &ctl->abort, kWaitLimitNs);
+        const bool ok = mbar_wait(smem_u32(&ctl->bres), 0u, &ctl->abort, wait_limit(p));
         if (!__all_sync(0xffffffffu, ok)) {
             if (leader) {
                 set_status(p.status, kStatusTimeoutFull);
@@ -300,7 +309,7 @@ __device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int
         const uint32_t aph = (j / p.acc_slots) & 1u;
         {
             FX_T0();
-            const bool ok = mbar_wait(smem_u32(&ctl->acce[aslot]), aph ^ 1u, &ctl->abort, kWaitLimitNs);
+            const bool ok = mbar_wait(smem_u32(&ctl->acce[aslot]), aph ^ 1u, &ctl->abort, wait_limit(p));
             if (!__all_sync(0xffffffffu, ok)) {
                 if (leader) {
                     set_status(p.status, kStatusTimeoutAccFree);
@@ -319,7 +328,7 @@ __device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int
             {
                 FX_T0();
                 const bool ok =
-                    mbar_wait(smem_u32(&ctl->full[slot]), (k / p.n_pipe) & 1u, &ctl->abort, kWaitLimitNs);
+                    mbar_wait(stage_full_bar(p, ctl, slot, k), (k / p.n_pipe) & 1u, &ctl->abort, wait_limit(p));
                 if (!__all_sync(0xffffffffu, ok)) {
                     if (leader) {
                         set_status(p.status, kStatusTimeoutFull);
@@ -384,7 +393,7 @@ __device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int
     mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->drain));
     if (leader) {
         const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < wait_limit(p)) {
         }
     }
     __syncwarp();
@@ -516,7 +525,7 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
         const int aslot = j % p.acc_slots;
         {
             FX_T0();
-            if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, kWaitLimitNs)) {
+            if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, wait_limit(p))) {
                 set_status(p.status, kStatusTimeoutAcc);
                 ctl->abort = 1;
                 return;
@@ -780,7 +789,7 @@ __device__ void epilogue_up(const ConvParams& p, SmemCtl* ctl, int n_units) {
         const int aslot = j % p.acc_slots;
         {
             FX_T0();
-            if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, kWaitLimitNs)) {
+            if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, wait_limit(p))) {
                 set_status(p.status, kStatusTimeoutAcc);
                 ctl->abort = 1;
                 return;
@@ -909,7 +918,7 @@ __device__ void epilogue_fold(const ConvParams& p, SmemCtl* ctl, float* xbuf, in
         const int aslot = j % p.acc_slots;
         {
             FX_T0();
-            if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, kWaitLimitNs)) {
+            if (!mbar_wait(smem_u32(&ctl->accf[aslot]), (j / p.acc_slots) & 1u, &ctl->abort, wait_limit(p))) {
                 set_status(p.status, kStatusTimeoutAcc);
                 ctl->abort = 1;
                 return;
@@ -965,7 +974,7 @@ __device__ void epilogue_fold(const ConvParams& p, SmemCtl* ctl, float* xbuf, in
             }
             __syncwarp();  // lane 1's publish is ordered before lane 0's arrive
             if (lane == 0) mbar_arrive(smem_u32(&ctl->xready[half][par]));
-            if (!mbar_wait(smem_u32(&ctl->xready[half][par]), xph[par], &ctl->abort, kWaitLimitNs)) {
+            if (!mbar_wait(smem_u32(&ctl->xready[half][par]), xph[par], &ctl->abort, wait_limit(p))) {
                 set_status(p.status, kStatusTimeoutExchange);
                 ctl->abort = 1;
                 return;
@@ -1077,6 +1086,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         }
         mbar_init(smem_u32(&ctl->drain), 1);
         mbar_init(smem_u32(&ctl->bres), 1);
+        mbar_init(smem_u32(&ctl->never), 1);
         for (int h = 0; h < 2; ++h)
             for (int q = 0; q < 2; ++q) mbar_init(smem_u32(&ctl->xready[h][q]), 4);
         ctl->abort = 0;
@@ -1098,8 +1108,12 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
     __syncthreads();
     tc_fence_after();
     (void)lane;
-
-    if (warp == 0) {
+    // the allocation must lie inside the columns asked for (lane field 0, column + width <= 512)
+    const uint32_t tb = ctl->tmem_base;
+    const bool tmem_ok = (tb >> 16) == 0u && (tb & 0xFFFFu) + p.tmem_cols <= 512u;
+    if (!tmem_ok) {
+        if (threadIdx.x == 0) set_status(p.status, kStatusBadTmem);
+    } else if (warp == 0) {
         producer_loop(p, smem, ctl, n_units);
     } else if (warp == 1 && p.zfold) {
         const bool f8 = p.optype == kOpE4M3;

@@ -134,6 +134,10 @@ struct ConvParams {
                              // or half of it when the epilogue's warp pair splits the chunks
                              // (N_tile >= 32 and R == 1 or N_tile <= 64, no x fold)
     uint32_t* status;
+    uint64_t wait_ns;            // limit of every barrier wait in ns; 0 = the default (2 s)
+    int32_t stall_first_wait;    // failure self-test only (fx_selftest_wait_timeout): the MMA warp's
+                                 // first stage wait is on a barrier nothing arrives at, so it times
+                                 // out and the launch ends with kStatusTimeoutFull
     unsigned long long* trace;  // per-role cycle counters (kernel built with FX_CONV_TRACE), or null
     // The program itself travels in the parameter space: warp-uniform indexed loads of it land in
     // uniform registers, so issuing an MMA costs a few uniform adds.

@@ -85,8 +85,8 @@ __device__ __forceinline__ void build_lut(float* lut, unsigned long long S, unsi
 __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, int64_t dy, int64_t dx,
                                  const TileOrigin* __restrict__ tiles, int P,
                                  const unsigned long long* __restrict__ sums, uint8_t* __restrict__ l0,
-                                 int64_t l0_batch_stride, int l0_type, float* __restrict__ f32_out,
-                                 const uint8_t* __restrict__ tta) {
+                                 int64_t l0_batch_stride, int64_t l0_group_stride, int l0_type,
+                                 float* __restrict__ f32_out, const uint8_t* __restrict__ tta) {
     const int b = blockIdx.y;
     __shared__ float lut[256];
     const int64_t n = static_cast<int64_t>(P) * P * P;
@@ -120,8 +120,11 @@ __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, in
         }
         const int64_t row = (static_cast<int64_t>(z + 1) * Pp + (y + 1)) * Pp + (x + 1);
         if (l0) {
-            const float cell[8] = {v[0], v[1], v[2], 0.f, 0.f, 0.f, 0.f, 0.f};
-            *reinterpret_cast<uint4*>(l0 + b * l0_batch_stride + row * 16) = pack_cell16(cell, l0_type);
+            uint4 c0, c1;
+            first_layer_cells(v, l0_type, c0, c1);
+            uint8_t* o = l0 + b * l0_batch_stride + row * 16;
+            *reinterpret_cast<uint4*>(o) = c0;
+            *reinterpret_cast<uint4*>(o + l0_group_stride) = c1;
         }
         if (f32_out) f32_out[b * n + i] = v[1];
     }
@@ -593,6 +596,12 @@ __global__ void accum_add_kernel(float* __restrict__ dst, const float* __restric
         dst[i] += src[i];
 }
 
+__global__ void accum_add_scalar_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        dst[i] += src[i];
+}
+
 int grid_for(int64_t n, int threads) {
     int64_t g = (n + threads - 1) / threads;
     if (g > 148 * 16) g = 148 * 16;
@@ -613,12 +622,12 @@ cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
 
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
                              int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
-                             int l0_type, float* f32_out, cudaStream_t s, const uint8_t* tta) {
+                             int64_t l0_group_stride, int l0_type, float* f32_out, cudaStream_t s, const uint8_t* tta) {
     const int64_t lines = static_cast<int64_t>(P) * P;
     const int gx = grid_for(lines, (kEwThreads / 32) * 2);  // two lines per warp
     count_launch();
     tile_norm_kernel<<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums, l0, l0_batch_stride,
-                                                             l0_type, f32_out, tta);
+                                                             l0_group_stride, l0_type, f32_out, tta);
     return cudaGetLastError();
 }
 
@@ -732,11 +741,51 @@ cudaError_t launch_accum_finalize(const float* acc, int64_t dz, int64_t dy, int6
 
 cudaError_t launch_zero(void* p, size_t bytes, cudaStream_t s) { return cudaMemsetAsync(p, 0, bytes, s); }
 
+// Agreement of two probability maps: stats[0] += #(a >= 0.5), stats[1] += #(b >= 0.5),
+// stats[2] += #(both), and max |a - b| into *maxabs (float bits, both non-negative floats compare as
+// unsigned). Used to choose an fp8 net's precision schedule against its 16-bit forward.
+__global__ void prob_compare_kernel(const float* __restrict__ a, const float* __restrict__ b, int64_t n,
+                                    unsigned long long* stats, unsigned* maxabs) {
+    unsigned long long ca = 0, cb = 0, cab = 0;
+    float m = 0.f;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float x = a[i], y = b[i];
+        const bool pa = x >= 0.5f, pb = y >= 0.5f;
+        ca += pa;
+        cb += pb;
+        cab += pa && pb;
+        m = fmaxf(m, fabsf(x - y));
+    }
+    for (int o = 16; o; o >>= 1) {
+        ca += __shfl_xor_sync(0xffffffffu, ca, o);
+        cb += __shfl_xor_sync(0xffffffffu, cb, o);
+        cab += __shfl_xor_sync(0xffffffffu, cab, o);
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+        atomicAdd(stats, ca);
+        atomicAdd(stats + 1, cb);
+        atomicAdd(stats + 2, cab);
+        atomicMax(maxabs, __float_as_uint(m));
+    }
+}
+
+cudaError_t launch_prob_compare(const float* a, const float* b, int64_t n, unsigned long long* stats,
+                                unsigned* maxabs, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    count_launch();
+    prob_compare_kernel<<<grid_for(n, kEwThreads), kEwThreads, 0, s>>>(a, b, n, stats, maxabs);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_accum_add(float* dst, const float* src, int64_t n, cudaStream_t s) {
     if (n <= 0) return cudaSuccess;
-    if ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) return cudaErrorMisalignedAddress;
     count_launch();
-    accum_add_kernel<<<grid_for(n / 4 + 1, kEwThreads), kEwThreads, 0, s>>>(dst, src, n);
+    if ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15)  // e.g. an odd plane size
+        accum_add_scalar_kernel<<<grid_for(n, kEwThreads), kEwThreads, 0, s>>>(dst, src, n);
+    else
+        accum_add_kernel<<<grid_for(n / 4 + 1, kEwThreads), kEwThreads, 0, s>>>(dst, src, n);
     return cudaGetLastError();
 }
 

@@ -27,12 +27,14 @@ cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
 // z-scored values at x-1, x, x+1 (zero outside the tile) as 16-bit floats, then five zeros. The z-score
 // goes through a 256-entry table built with the reference's double-precision expression, so
 // the normalised value of each u8 level is the same float the reference computes.
-// `l0_type` is the first conv's operand type (kOpBF16 or kOpF16); l0 may be null.
+// `l0_type` is the first conv's operand type (kOpBF16 or kOpF16); l0 (may be null) receives its
+// two input groups, l0_group_stride bytes apart (first_layer_cells: the value as hi + lo terms).
 // tta (one byte per tile, or null): octahedral test-time-augmentation member of each tile; the
 // tile is written in that member's frame (see tta_source).
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
                              int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
-                             int l0_type, float* f32_out, cudaStream_t s, const uint8_t* tta = nullptr);
+                             int64_t l0_group_stride, int l0_type, float* f32_out, cudaStream_t s,
+                             const uint8_t* tta = nullptr);
 
 // Octahedral TTA (src/ml/infer.hpp:346, 393-441): member m of the first N of 48 uses the axis
 // permutation perms[m / 8] and flips the transformed frame's axes in the bits of m % 8 (bit 0 z,
@@ -157,5 +159,7 @@ cudaError_t launch_accum_finalize(const float* acc, int64_t dz, int64_t dy, int6
 cudaError_t launch_zero(void* p, size_t bytes, cudaStream_t s);
 // dst[i] += src[i] (f32, n elements): folds another rank's accumulator band into this one.
 cudaError_t launch_accum_add(float* dst, const float* src, int64_t n, cudaStream_t s);
+cudaError_t launch_prob_compare(const float* a, const float* b, int64_t n, unsigned long long* stats,
+                                unsigned* maxabs, cudaStream_t s);
 
 }  // namespace fxk

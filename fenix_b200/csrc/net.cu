@@ -373,15 +373,25 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     dp.acc_scale = 1.f;
     bool fold = false;
     if (L.kind == Layer::kFirst) {
+        // One input channel: a cell carries the three x taps of a voxel, and the value is split into
+        // two 16-bit terms (first_layer_cells): group 0 = [hi x3, lo x3] times the 16-bit weights,
+        // group 1 = [hi x3] times the weights' rounding residues, so the first conv sees its input
+        // and weights to about twice the 16-bit precision. One MMA (K = both groups) per (kz, ky).
         if (fp8) return fail(kInternal, "first layer runs with 16-bit operands");
-        sp.G = 1;
-        sp.pair_taps = true;
+        sp.G = 2;
         const ActGeom g = gout;
         const int64_t Wp = g.W + 2, P2 = static_cast<int64_t>(g.H + 2) * Wp;
         for (int kz = 0; kz < 3; ++kz)
             for (int ky = 0; ky < 3; ++ky) sp.taps.push_back({0, (kz - 1) * P2 + (ky - 1) * Wp, kz * 3 + ky, kz});
         const Layer* Lp = &L;
-        sp.wval = [Lp](int n, int j, int wk) { return j < 3 ? Lp->w[static_cast<size_t>(n) * 27 + wk * 3 + j] : 0.f; };
+        const int q16 = q;
+        sp.wval = [Lp, q16](int n, int ci, int wk) {
+            const int grp = ci / 8, j = ci % 8;
+            const int kx = grp == 0 ? (j < 3 ? j : (j < 6 ? j - 3 : -1)) : (j < 3 ? j : -1);
+            if (kx < 0) return 0.f;
+            const float w = Lp->w[static_cast<size_t>(n) * 27 + wk * 3 + kx];
+            return grp == 0 ? w : w - round16_host(w, q16);
+        };
         sp.N_total = L.Cout;
         dp.rowspace = gout;
     } else if (L.kind == Layer::kConv) {
@@ -586,9 +596,10 @@ Status Net::build_layer(Layer& L, int q) {
 
 Status Net::alloc() {
     const ActGeom g0 = level(0);
-    l0_ = static_cast<uint8_t*>(dalloc(static_cast<size_t>(Bmax_) * g0.gs()));
+    // the first conv's input: two 16-bit groups per voxel (the value as hi + lo, first_layer_cells)
+    l0_ = static_cast<uint8_t*>(dalloc(static_cast<size_t>(Bmax_) * 2 * g0.gs()));
     if (!l0_) return fail(kInternal, "cudaMalloc: first-layer input");
-    cudaMemset(l0_, 0, static_cast<size_t>(Bmax_) * g0.gs());
+    cudaMemset(l0_, 0, static_cast<size_t>(Bmax_) * 2 * g0.gs());
     pn_.assign(S_, nullptr);
     act_.assign(S_, nullptr);
     cat_.assign(S_, nullptr);
@@ -684,6 +695,11 @@ Status Net::create(const std::string& path, int patch, int max_batch, int precis
     std::string err = load_fxweights(path, wm);
     if (!err.empty()) return fail(err.find("open") != std::string::npos ? kIo : kDecode, err);
     if ((st = parse(wm)).code) return st;
+    {
+        int k = 0;
+        for (auto* v : {&enc_, &up_, &dec_})
+            for (Layer& L : *v) L.idx = k++;
+    }
     const int div = 1 << (S_ - 1);
     if (P_ % div) return fail(kInvalid, "patch must be divisible by " + std::to_string(div));
     for (int s = 0; s < S_; ++s)
@@ -711,6 +727,7 @@ Status Net::run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int6
         const double taps = L.kind == Layer::kProj ? (L.stride == 2 ? 8.0 : 1.0) : 27.0;
         ev.flops = L.kind == Layer::kUp ? 2.0 * L.Cin * L.Cout * 8.0 * vin * nb : 2.0 * taps * L.Cin * L.Cout * vout * nb;
         ev.optype = q;
+        ev.layer = L.idx;
         cudaEventCreate(&ev.a);
         cudaEventCreate(&ev.b);
         cudaEventRecord(ev.a, s);
@@ -726,8 +743,9 @@ Status Net::run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int6
 
 void Net::profile(bool on) { profile_ = on; }
 
-Status Net::profile_read(ProfileTotals& out, double* per, int cap) {
+Status Net::profile_read(ProfileTotals& out, double* per, int cap, std::vector<double>* per_layer) {
     out = ProfileTotals{};
+    if (per_layer) per_layer->assign(enc_.size() + up_.size() + dec_.size(), 0.0);
     int k = 0;
     for (ProfEv& e : prof_) {
         cudaError_t err = cudaEventSynchronize(e.b);
@@ -742,6 +760,7 @@ Status Net::profile_read(ProfileTotals& out, double* per, int cap) {
             per[2 * k] = ms;
             per[2 * k + 1] = e.flops;
         }
+        if (per_layer && e.layer >= 0 && e.layer < static_cast<int>(per_layer->size())) (*per_layer)[e.layer] += ms;
         ++k;
         cudaEventDestroy(e.a);
         cudaEventDestroy(e.b);
@@ -752,7 +771,8 @@ Status Net::profile_read(ProfileTotals& out, double* per, int cap) {
 
 Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
                     uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax,
-                    int nb, int sm_count_, uint32_t* d_status_, cudaStream_t s, bool per_column) {
+                    int nb, int sm_count_, uint32_t* d_status_, cudaStream_t s, bool per_column, uint64_t wait_ns,
+                    int stall_first_wait) {
     DevProgram& dp = L.prog[q];
     if (!dp.built) return fail(kInternal, L.name + ": program not built");
     static thread_local fxk::ConvParams p;  // ~22 KB: kept off the stack
@@ -803,6 +823,8 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     p.out_batch_stride = out_bs;
     p.out_group_stride = out_gs;
     p.status = d_status_;
+    p.wait_ns = wait_ns;
+    p.stall_first_wait = stall_first_wait;
     p.trace = g_conv_trace;
     if (L.kind == Layer::kUp) {
         p.mode = fxk::kModeUpsample;
@@ -868,7 +890,7 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
     const ActGeom g0 = level(0);
     if ((st = cuda_status(cudaMemsetAsync(d_sums_, 0, sizeof(unsigned long long) * 2 * nb, s), "memset")).code) return st;
     if ((st = cuda_status(fxk::launch_tile_sums(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, s), "tile_sums")).code) return st;
-    if ((st = cuda_status(fxk::launch_tile_norm(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, l0_, g0.gs(), t16(), nullptr,
+    if ((st = cuda_status(fxk::launch_tile_norm(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, l0_, 2 * g0.gs(), g0.gs(), t16(), nullptr,
                                                 s, d_tta),
                           "tile_norm"))
             .code)
@@ -928,7 +950,7 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
             d.qscale = 1.f;
             return d;
         };
-        if ((st = run_conv(enc_[0], qof(stem), l0_, g0.gs(), g0.gs(), pn_[0], pn0, g0l.gs(), 0, 1.f, nullptr, nb, s)).code)
+        if ((st = run_conv(enc_[0], qof(stem), l0_, 2 * g0.gs(), g0.gs(), pn_[0], pn0, g0l.gs(), 0, 1.f, nullptr, nb, s)).code)
             return st;
         if ((st = norm(enc_[0], dest(act_[0], 0, F_[0], 0, enc_[blocks_[0].c1]), f16dest(xf_[0], 0, F_[0]),
                        blocks_[0].slot_x))
@@ -1032,7 +1054,7 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
                 int64_t ibs, igs;
                 if (L.kind == Layer::kFirst) {
                     in = l0_;
-                    ibs = g0.gs();
+                    ibs = 2 * g0.gs();
                     igs = g0.gs();
                 } else if (i == 0) {  // stride 2: phase-split copy of the previous stage's output
                     in = ph_[lv - 1];
@@ -1181,9 +1203,7 @@ Status Net::calibrate(const uint8_t* host_patches, int n) {
             .code)
         return st;
     if ((st = cuda_status(cudaStreamSynchronize(stream_), "calibration forward")).code) return st;
-    uint32_t status = 0;
-    cudaMemcpy(&status, d_status_, 4, cudaMemcpyDeviceToHost);
-    if (status) return fail(kInternal, "calibration: device status " + std::to_string(status));
+    if ((st = take_device_status()).code) return fail(st.code, "calibration: " + st.msg);
     for (size_t k = 0; k < bits.size(); ++k) {
         float f;
         std::memcpy(&f, &bits[k], 4);
@@ -1244,11 +1264,140 @@ Status Net::set_layer_precision(const int* q, int n) {
     return ok();
 }
 
+Status Net::calibrate_schedule(const uint8_t* host_patches, int n, double min_dice, double max_abs, double* dice_out,
+                               double* maxabs_out) {
+    if (prec_ != 1) return fail(kInvalid, "calibrate_schedule: net is not fp8");
+    if (n < 1 || !host_patches) return fail(kInvalid, "calibrate_schedule: need at least one patch");
+    if (!(min_dice >= 0.0 && min_dice <= 1.0)) return fail(kInvalid, "calibrate_schedule: min_dice must be in [0, 1]");
+    Status st;
+    if (!calibrated_ && (st = calibrate(host_patches, n)).code) return st;
+    cudaSetDevice(dev_);
+    const size_t pv = static_cast<size_t>(P_) * P_ * P_;
+    auto* d_vol = static_cast<uint8_t*>(dalloc(pv * n));
+    auto* d_ref = static_cast<float*>(dalloc(sizeof(float) * pv * n));
+    auto* d_cur = static_cast<float*>(dalloc(sizeof(float) * pv * n));
+    auto* d_cmp = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * 4));
+    auto* d_org = static_cast<fxk::TileOrigin*>(dalloc(sizeof(fxk::TileOrigin) * Bmax_));
+    if (!d_vol || !d_ref || !d_cur || !d_cmp || !d_org) return fail(kInternal, "cudaMalloc: schedule search buffers");
+    std::vector<fxk::TileOrigin> org(Bmax_);
+    for (int b = 0; b < Bmax_; ++b) org[b] = {static_cast<int64_t>(b) * P_, 0, 0};
+    cudaMemcpyAsync(d_org, org.data(), sizeof(fxk::TileOrigin) * Bmax_, cudaMemcpyHostToDevice, stream_);
+    cudaMemcpyAsync(d_vol, host_patches, pv * n, cudaMemcpyHostToDevice, stream_);
+    const int nl = static_cast<int>(enc_.size() + up_.size() + dec_.size());
+    std::vector<int> elig;
+    for (int k = 0; k < nl; ++k) {
+        Layer& L = const_cast<Layer&>(*layer_at(k));
+        const bool saved = L.keep16;
+        L.keep16 = false;
+        if (layer_q(L, false) == fxk::kOpE4M3) elig.push_back(k);
+        L.keep16 = saved;
+    }
+    const int sig = ncls_ == 1 ? 1 : 0;
+    // every tile of the calibration set through the net with schedule q8 (1 = e4m3), probabilities into out
+    auto run = [&](const std::vector<char>& q8, float* out) -> Status {
+        std::vector<int> q(nl, t16());
+        for (int k = 0; k < nl; ++k)
+            if (q8[k]) q[k] = fxk::kOpE4M3;
+        Status r = set_layer_precision(q.data(), nl);
+        if (!r.ok()) return r;
+        for (int i0 = 0; i0 < n; i0 += Bmax_) {
+            const int nb = std::min(Bmax_, n - i0);
+            if ((r = forward(d_vol + pv * i0, static_cast<int64_t>(nb) * P_, P_, P_, d_org, nb, 1, sig, nullptr,
+                             out + pv * i0, false, stream_))
+                    .code)
+                return r;
+        }
+        return take_device_status();
+    };
+    // Dice of the 0.5-thresholded masks and max |dp| of d_cur against d_ref
+    auto compare = [&](double& dice, double& mx) -> Status {
+        cudaMemsetAsync(d_cmp, 0, sizeof(unsigned long long) * 4, stream_);
+        Status r = cuda_status(fxk::launch_prob_compare(d_ref, d_cur, static_cast<int64_t>(pv) * n, d_cmp,
+                                                        reinterpret_cast<unsigned*>(d_cmp + 3), stream_),
+                               "prob_compare");
+        if (!r.ok()) return r;
+        unsigned long long h[4] = {0, 0, 0, 0};
+        if ((r = cuda_status(cudaMemcpyAsync(h, d_cmp, sizeof h, cudaMemcpyDeviceToHost, stream_), "D2H")).code) return r;
+        if ((r = cuda_status(cudaStreamSynchronize(stream_), "compare")).code) return r;
+        dice = h[0] + h[1] == 0 ? 1.0 : 2.0 * static_cast<double>(h[2]) / static_cast<double>(h[0] + h[1]);
+        float f;
+        const unsigned bits = static_cast<unsigned>(h[3]);
+        std::memcpy(&f, &bits, 4);
+        mx = f;
+        return ok();
+    };
+    std::vector<char> none(nl, 0), all(nl, 0);
+    for (int k : elig) all[k] = 1;
+    // conv time per layer on each operand type (one profiled pass each), and the 16-bit yardstick
+    const bool was_profiling = profile_;
+    std::vector<double> t16, t8;
+    profile_ = true;
+    st = run(all, d_cur);
+    if (st.ok()) {
+        ProfileTotals tot;
+        st = profile_read(tot, nullptr, 0, &t8);
+    }
+    if (st.ok()) st = run(none, d_ref);
+    if (st.ok()) {
+        ProfileTotals tot;
+        st = profile_read(tot, nullptr, 0, &t16);
+    }
+    profile_ = was_profiling;
+    if (!st.ok()) return st;
+    struct Cand {
+        int k;
+        double loss2, mx, gain;
+    };
+    std::vector<Cand> cands;
+    for (int k : elig) {
+        std::vector<char> q(nl, 0);
+        q[k] = 1;
+        double d = 1.0, mx = 0.0;
+        if ((st = run(q, d_cur)).code || (st = compare(d, mx)).code) return st;
+        const double loss = std::max(1.0 - d, 1e-7);
+        cands.push_back({k, loss * loss, mx, t16[k] - t8[k]});
+    }
+    std::sort(cands.begin(), cands.end(), [](const Cand& a, const Cand& b) { return a.gain / a.loss2 > b.gain / b.loss2; });
+    const double budget = (1.0 - min_dice) * (1.0 - min_dice);
+    std::vector<char> cur(nl, 0);
+    std::vector<int> taken;
+    double used = 0.0;
+    for (const Cand& c : cands) {
+        if (c.gain <= 0.0 || (max_abs > 0.0 && c.mx > max_abs) || used + c.loss2 > budget) continue;
+        cur[c.k] = 1;
+        used += c.loss2;
+        taken.push_back(c.k);
+    }
+    double dice = 1.0, mx = 0.0;
+    for (;;) {
+        if ((st = run(cur, d_cur)).code || (st = compare(dice, mx)).code) return st;
+        if ((dice >= min_dice && (max_abs <= 0.0 || mx <= max_abs)) || taken.empty()) break;
+        cur[taken.back()] = 0;
+        taken.pop_back();
+    }
+    if (dice_out) *dice_out = dice;
+    if (maxabs_out) *maxabs_out = mx;
+    return ok();
+}
+
 std::vector<int> Net::layer_precision() const {
     std::vector<int> out;
     for (auto* v : {&enc_, &up_, &dec_})
         for (const Layer& L : *v) out.push_back(layer_q(L, false));
     return out;
+}
+
+Status Net::take_device_status() {
+    cudaSetDevice(dev_);
+    Status st = cuda_status(cudaStreamSynchronize(stream_), "stream");
+    if (!st.ok()) return st;
+    uint32_t v = 0;
+    if ((st = cuda_status(cudaMemcpy(&v, d_status_, 4, cudaMemcpyDeviceToHost), "D2H status")).code) return st;
+    if (!v) return ok();
+    cudaMemset(d_status_, 0, 4);
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "device status 0x%x: a kernel's bounded wait timed out", v);
+    return fail(kInternal, buf);
 }
 
 const Layer* Net::layer_at(int i) const {

@@ -77,6 +77,7 @@ struct Layer {
     std::vector<float> wscale;        // fp8 per-output-channel weight scale (amax / 448)
     float in_scale = 1.f;             // fp8 per-tensor scale of the input activation
     bool keep16 = false;              // fp8 nets: precision schedule keeps this layer on 16-bit operands
+    int idx = -1;                     // position in act_scales() order
     DevProgram prog[3];               // indexed by fxk::OpType: bf16, e4m3, f16
     float* d_gamma = nullptr;
     float* d_beta = nullptr;
@@ -98,7 +99,8 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
 // callers that read them); otherwise by one factor, with the per-channel part in L.cur_ratio.
 Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs,
                     uint8_t* out_ptr, int64_t out_bs, int64_t out_gs, int out_type, float out_qscale, unsigned* amax,
-                    int nb, int sm_count, uint32_t* d_status, cudaStream_t s, bool per_column = false);
+                    int nb, int sm_count, uint32_t* d_status, cudaStream_t s, bool per_column = false,
+                    uint64_t wait_ns = 0, int stall_first_wait = 0);
 
 // One BasicBlockD of a residual encoder (src/ml/nets/resenc_unet.hpp:103-135): indices into the
 // net's encoder layers, the skip path and the scSE parameters.
@@ -159,11 +161,24 @@ class Net {
     // fxk::kOpE4M3 (e4m3 where the layer can take it) or the 16-bit type. Layers that cannot run
     // e4m3 (the first conv, input channels not a multiple of 32) stay 16-bit whatever is asked.
     Status set_layer_precision(const int* q, int n);
+    // Choose the precision schedule on n host calibration patches ([n][P][P][P] u8): the net's
+    // 16-bit forward is the yardstick; every e4m3-capable layer is tried alone on e4m3 (agreement of
+    // the 0.5-thresholded masks as Dice, and max |dp|), its conv time is measured on both operand
+    // types, and layers are taken greedily by time saved per unit of squared Dice loss while the
+    // summed squared losses stay within (1 - min_dice)^2 and each layer's max |dp| within max_abs
+    // (<= 0: no bound). The chosen schedule is then run and layers are given back (last taken first)
+    // until it meets both bounds. Calibrates the scales first if needed. Reports the schedule's Dice
+    // and max |dp| against the 16-bit forward.
+    Status calibrate_schedule(const uint8_t* host_patches, int n, double min_dice, double max_abs, double* dice,
+                              double* maxabs);
     // The operand type each conv layer runs with (act_scales() order).
     std::vector<int> layer_precision() const;
     // Algorithmic FLOPs (2 x MACs) of one forward of one tile through each conv layer.
     std::vector<double> layer_flops() const;
     const Layer* layer_at(int i) const;
+    // The device status word the kernels set on a bounded-wait timeout (0 = none); synchronises the
+    // net's stream, then clears the word.
+    Status take_device_status();
 
     // Per-conv-launch device timing with CUDA events on the launching stream (off by default).
     struct ProfileTotals {
@@ -172,13 +187,14 @@ class Net {
     };
     void profile(bool on);
     // synchronises the recorded events; per-launch (ms, flops) pairs into `per` (up to cap)
-    Status profile_read(ProfileTotals& out, double* per = nullptr, int cap = 0);
+    Status profile_read(ProfileTotals& out, double* per = nullptr, int cap = 0, std::vector<double>* per_layer = nullptr);
 
   private:
     struct ProfEv {
         cudaEvent_t a, b;
         double flops;
         int optype;
+        int layer;
     };
     bool profile_ = false;
     std::vector<ProfEv> prof_;

@@ -62,7 +62,7 @@ __global__ void pack_kernel(const float* __restrict__ x, int B, int C, int D, in
 }
 
 __global__ void pack_first_kernel(const float* __restrict__ x, int B, int D, int H, int W, uint8_t* out, int64_t bs,
-                                  int dtype) {
+                                  int64_t gs, int dtype) {
     const int64_t vox = static_cast<int64_t>(D) * H * W;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vox * B;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -72,13 +72,12 @@ __global__ void pack_first_kernel(const float* __restrict__ x, int B, int D, int
         const int yy = static_cast<int>((v / W) % H);
         const int zz = static_cast<int>(v / (static_cast<int64_t>(W) * H));
         const float* row = x + static_cast<int64_t>(b) * vox + (static_cast<int64_t>(zz) * H + yy) * W;
-        const float a = xx > 0 ? row[xx - 1] : 0.f;
-        const float c = row[xx];
-        const float d = xx + 1 < W ? row[xx + 1] : 0.f;
-        const float cell[8] = {a, c, d, 0.f, 0.f, 0.f, 0.f, 0.f};
-        const uint4 w = pack_cell16(cell, dtype);
+        const float taps[3] = {xx > 0 ? row[xx - 1] : 0.f, row[xx], xx + 1 < W ? row[xx + 1] : 0.f};
+        uint4 c0, c1;
+        first_layer_cells(taps, dtype, c0, c1);
         const int64_t r = ((static_cast<int64_t>(zz + 1) * (H + 2) + (yy + 1)) * (W + 2) + (xx + 1));
-        *reinterpret_cast<uint4*>(out + b * bs + r * 16) = w;
+        *reinterpret_cast<uint4*>(out + b * bs + r * 16) = c0;
+        *reinterpret_cast<uint4*>(out + b * bs + gs + r * 16) = c1;
     }
 }
 
@@ -133,11 +132,11 @@ cudaError_t launch_pack(const float* x, int B, int C, int D, int H, int W, uint8
     return cudaGetLastError();
 }
 
-cudaError_t launch_pack_first(const float* x, int B, int D, int H, int W, uint8_t* out, int64_t bs, int dtype,
-                              cudaStream_t s) {
+cudaError_t launch_pack_first(const float* x, int B, int D, int H, int W, uint8_t* out, int64_t bs, int64_t gs,
+                              int dtype, cudaStream_t s) {
     const int64_t total = static_cast<int64_t>(D) * H * W * B;
     count_launch();
-    pack_first_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, B, D, H, W, out, bs, dtype);
+    pack_first_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, B, D, H, W, out, bs, gs, dtype);
     return cudaGetLastError();
 }
 

@@ -13,9 +13,10 @@ namespace fxk {
 cudaError_t launch_pack(const float* x, int B, int C, int D, int H, int W, uint8_t* out, int64_t batch_stride,
                         int64_t group_stride, int dtype, float qscale, int phase, int pHp, int pWp,
                         int64_t phase_stride, cudaStream_t s);
-// f32 [B][1][D][H][W] -> the first layer's x-folded 16-bit cells (x-1, x, x+1, 0...).
+// f32 [B][1][D][H][W] -> the first layer's two x-folded 16-bit groups (first_layer_cells),
+// group_stride bytes apart.
 cudaError_t launch_pack_first(const float* x, int B, int D, int H, int W, uint8_t* out, int64_t batch_stride,
-                              int dtype, cudaStream_t s);
+                              int64_t group_stride, int dtype, cudaStream_t s);
 // padded group planes of OpType `dtype` -> f32 [B][C][D][H][W] (e4m3 values times `scale`).
 cudaError_t launch_unpack(const uint8_t* in, int64_t batch_stride, int64_t group_stride, int dtype, float scale, int B,
                           int C, int D, int H, int W, float* y, cudaStream_t s);

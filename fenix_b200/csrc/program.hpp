@@ -31,7 +31,6 @@ struct ProgramSpec {
     int N_tile = 0;    // columns per work unit
     int R = 1;         // M blocks per unit
     int block_rows = 128;  // window rows advanced per M block (126 with the x-tap fold)
-    bool pair_taps = false;  // G == 1: the two K-halves of one MMA come from two taps
     std::vector<Tap> taps;
     // z-plane fold (3x3x3 stride 1): the R M blocks of a unit lie one z plane apart, each stage
     // holds one input plane's window, and its A tiles feed up to three blocks (taps kz = 0, 1, 2);
@@ -123,6 +122,21 @@ inline uint16_t float_to_bf16(float f) {
     return static_cast<uint16_t>(u >> 16);
 }
 
+// v rounded to the 16-bit operand type q (2 f16, else bf16), as the packer rounds it.
+inline float round16_host(float v, int q) {
+    uint32_t u;
+    if (q == 2) {
+        const uint16_t h = float_to_f16(v);
+        const uint32_t e = (h >> 10) & 0x1fu, m = h & 0x3ffu;
+        const float a = e == 0 ? std::ldexp(static_cast<float>(m), -24) : std::ldexp(1.f + m / 1024.f, static_cast<int>(e) - 15);
+        return (h & 0x8000u) ? -a : a;
+    }
+    u = static_cast<uint32_t>(float_to_bf16(v)) << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
 // A / B smem offsets of one MMA packed into descriptor low words (see fxk::ConvMma).
 inline fxk::ConvMma pack_mma(int64_t a_off, int64_t lbo, int64_t b_off) {
     fxk::ConvMma m{};
@@ -209,7 +223,7 @@ inline std::string build_program(const ProgramSpec& s, Program& pg) {
     if (s.zfold) return build_zfold_program(s, pg);
     if (s.N_tile <= 0 || s.N_tile % 16 || s.N_total % s.N_tile) return "program: bad N tiling";
     if (s.N_tile > 256 && s.N_tile != 320) return "program: N tile > 256 must be 320";
-    if (!s.pair_taps && (s.G % 2)) return "program: group count must be even";
+    if (s.G % 2) return "program: group count must be even";
     const int Mtot = s.block_rows * (s.R - 1) + 128;  // rows spanned by a unit's M blocks
     // windows
     std::map<int, std::vector<Tap>> win;
@@ -237,17 +251,15 @@ inline std::string build_program(const ProgramSpec& s, Program& pg) {
     // groups per stage: largest that keeps >= 3 stages in the smem budget (>= 2 as a fallback)
     const int bblk = s.N_tile * 32;  // bytes of one MMA's B block
     auto stage_bytes_for = [&](int gc) {
-        const int nm = s.pair_taps ? (max_taps + 1) / 2 : max_taps * (gc / 2);
+        const int nm = max_taps * (gc / 2);
         return max_rows * gc * 16 + nm * bblk;
     };
-    int gc = s.pair_taps ? 1 : 2;
-    if (!s.pair_taps) {
-        for (int c = s.G; c >= 2; c -= 2)
-            if (stage_bytes_for(c) * 3 <= s.smem_total) {
-                gc = c;
-                break;
-            }
-    }
+    int gc = 2;
+    for (int c = s.G; c >= 2; c -= 2)
+        if (stage_bytes_for(c) * 3 <= s.smem_total) {
+            gc = c;
+            break;
+        }
     int sb = stage_bytes_for(gc);
     int n_pipe = std::min(8, s.smem_total / sb);
     if (n_pipe < 2) return "program: stage does not fit in shared memory (" + std::to_string(sb) + " bytes)";
@@ -279,25 +291,13 @@ inline std::string build_program(const ProgramSpec& s, Program& pg) {
             st.b_off = boff;
             st.mma_begin = static_cast<int32_t>(pg.mmas.size());
             int32_t local_b = 0;
-            if (s.pair_taps) {
-                for (size_t i = 0; i < w.taps.size(); i += 2) {
-                    const Tap& a = w.taps[i];
-                    const bool two = i + 1 < w.taps.size();
-                    const int64_t a_off = (a.off - w.lo) * 16;
-                    const int64_t lbo = two ? (w.taps[i + 1].off - a.off) * 16 : 0;
-                    pg.mmas.push_back(pack_mma(a_off, lbo, local_b));
-                    brecs.push_back({a.wkey, two ? w.taps[i + 1].wkey : -1, 0, 0});
+            for (const Tap& t : w.taps)
+                for (int gp = g0; gp < g0 + ng; gp += 2) {
+                    const int64_t a_off = static_cast<int64_t>(gp - g0) * rows * 16 + (t.off - w.lo) * 16;
+                    pg.mmas.push_back(pack_mma(a_off, static_cast<int64_t>(rows) * 16, local_b));
+                    brecs.push_back({t.wkey, t.wkey, gp, gp + 1});
                     local_b += bblk;
                 }
-            } else {
-                for (const Tap& t : w.taps)
-                    for (int gp = g0; gp < g0 + ng; gp += 2) {
-                        const int64_t a_off = static_cast<int64_t>(gp - g0) * rows * 16 + (t.off - w.lo) * 16;
-                        pg.mmas.push_back(pack_mma(a_off, static_cast<int64_t>(rows) * 16, local_b));
-                        brecs.push_back({t.wkey, t.wkey, gp, gp + 1});
-                        local_b += bblk;
-                    }
-            }
             st.mma_count = static_cast<int32_t>(pg.mmas.size()) - st.mma_begin;
             st.b_bytes = local_b;
             boff += local_b;

@@ -24,7 +24,7 @@ enum : uint32_t {
     kStatusTimeoutAccFree = 0x400, // MMA issuer waited too long for a drained accumulator
     kStatusTimeoutDrain = 0x500,   // final drain of in-flight copies timed out
     kStatusTimeoutExchange = 0x600, // fold epilogue waited too long for the row exchange
-    kStatusBadTmem = 0x600,        // TMEM allocation returned an unexpected address
+    kStatusBadTmem = 0x700,        // TMEM allocation returned an address outside the columns asked for
 };
 
 __device__ __forceinline__ void set_status(uint32_t* st, uint32_t code) {
@@ -329,6 +329,27 @@ __device__ __forceinline__ uint4 pack_cell16(const float* v, int optype) {
         w.w = pack_bf16x2(v[6], v[7]);
     }
     return w;
+}
+// v rounded to the 16-bit operand type (round to nearest; f16 saturated as pack_f16x2 does).
+__device__ __forceinline__ float round16(float v, int optype) {
+    if (optype == kOpF16) return __half2float(__float2half_rn(fminf(fmaxf(v, -65504.f), 65504.f)));
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+// The first conv's input cells for the three x taps v[0..2] (x - 1, x, x + 1) as two 16-bit terms,
+// hi = round16(v) and lo = round16(v - hi) (v - hi is exact in f32), so hi + lo carries v to about
+// twice the type's precision: cell 0 = [hi x3, lo x3, 0, 0] (multiplied by the 16-bit weights),
+// cell 1 = [hi x3, 0 x5] (multiplied by the weights' rounding residues).
+__device__ __forceinline__ void first_layer_cells(const float (&v)[3], int optype, uint4& c0, uint4& c1) {
+    float hi[3], lo[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        hi[k] = round16(v[k], optype);
+        lo[k] = v[k] - hi[k];
+    }
+    const float a[8] = {hi[0], hi[1], hi[2], lo[0], lo[1], lo[2], 0.f, 0.f};
+    const float b[8] = {hi[0], hi[1], hi[2], 0.f, 0.f, 0.f, 0.f, 0.f};
+    c0 = pack_cell16(a, optype);
+    c1 = pack_cell16(b, optype);
 }
 // Eight floats -> one 16-byte cell of f16, round to nearest, saturated to +-65504 (one
 // cvt.rn.satfinite.f16x2.f32 per pair; the first value of a pair lands in the low half).

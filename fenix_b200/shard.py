@@ -1,14 +1,18 @@
-"""Multi-GPU sliding-window inference over one volume: z-slab sharding with a band exchange.
+"""Multi-GPU sliding-window inference over one volume: z-slab sharding without a collective.
 
 One process per GPU. The z-major tile list of the whole volume (the global grid of the
 reference's predict-scroll, src/ml/inference.cpp:1282-1372) is split into contiguous, near-equal
-ranges, one per rank, so tile coordinates and blend weights are those of a one-GPU run. Each rank
-holds only the input z-slab its tiles read and an f32 accumulator over the same planes. Planes
-are owned by exactly one rank (a partition of [0, D)); after its tiles are blended, each rank sends
-the accumulator planes it computed for planes that another rank owns (the tile-overlap halo bands,
-at most one tile deep) over NCCL point-to-point, the owner adds them (fx_accum_add) and finalises its
-owned planes to probability / u8 on its own GPU (fx_accum_finalize). torch provides device memory,
-streams and the process group; every compute step is a libfenix_b200 kernel.
+ranges, one per rank (fx_shard_plan), so tile coordinates and blend weights are those of a one-GPU
+run. Each rank holds only the input z-slab its tiles read and an f32 accumulator window over the
+same planes. Planes are owned by exactly one rank (a partition of [0, D)). After every rank has
+blended its tiles, each owner folds in the bands its neighbours accumulated for its planes (at most
+one tile deep) with fx_accum_add reading the neighbour's accumulator straight from its HBM over
+NVLink, through a CUDA IPC mapping handed over once at set-up, and finalises its owned planes to u8
+on its own GPU (fx_accum_finalize). The host only orders the steps: two barriers per pass on a
+host (gloo) process group. No NCCL, no collective on the data path. torch provides device memory,
+streams and the host process group; every compute step is a libfenix_b200 kernel.
+
+The same scheme runs in one process with one thread per GPU as fx_predict_volume_multi.
 """
 from __future__ import annotations
 
@@ -18,6 +22,10 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import InferOpts, check, gaussian1d, lib, tile_starts, weight_profile
+
+
+class _Shard(C.Structure):
+    _fields_ = [(k, C.c_int64) for k in ("tile_begin", "tile_end", "z_lo", "z_hi", "own_lo", "own_hi")]
 
 
 @dataclass
@@ -32,23 +40,12 @@ class RankPlan:
 
 
 def plan(shape, patch: int, overlap: float, world: int) -> list[RankPlan]:
+    """The library's shard plan (fx_shard_plan)."""
     D, H, W = shape
-    zs, ys, xs = tile_starts(D, patch, overlap), tile_starts(H, patch, overlap), tile_starts(W, patch, overlap)
-    per_row = len(ys) * len(xs)
-    T = len(zs) * per_row
-    out = []
-    for r in range(world):
-        t0, t1 = T * r // world, T * (r + 1) // world
-        if t1 <= t0:  # more ranks than tiles: an empty rank keeps an empty slab
-            out.append(RankPlan(r, t0, t0, 0, 0, 0, 0))
-            continue
-        iz0, iz1 = t0 // per_row, (t1 - 1) // per_row
-        out.append(RankPlan(r, t0, t1, int(zs[iz0]), int(min(zs[iz1] + patch, D)), 0, 0))
-    live = [p for p in out if p.tile_end > p.tile_begin]
-    for i, p in enumerate(live):
-        p.own_lo = 0 if i == 0 else p.z_lo
-        p.own_hi = D if i == len(live) - 1 else live[i + 1].z_lo
-    return out
+    buf = (_Shard * world)()
+    if lib().fx_shard_plan(D, H, W, patch, overlap, world, buf) != world:
+        raise ValueError("fx_shard_plan: bad arguments")
+    return [RankPlan(r, *(int(getattr(buf[r], k)) for k, _ in _Shard._fields_)) for r in range(world)]
 
 
 def exchanges(plans: list[RankPlan]):
@@ -56,7 +53,7 @@ def exchanges(plans: list[RankPlan]):
     ex = []
     for a in plans:
         for b in plans:
-            if a.rank == b.rank:
+            if a.rank == b.rank or a.tile_end <= a.tile_begin or b.tile_end <= b.tile_begin:
                 continue
             z0, z1 = max(a.z_lo, b.own_lo), min(a.z_hi, b.own_hi)
             if z1 > z0:
@@ -64,24 +61,30 @@ def exchanges(plans: list[RankPlan]):
     return ex
 
 
-def exchange_bands(acc, z_lo: int, send, recv, group, add) -> None:
-    """Send this rank's accumulator planes that other ranks own, receive the bands it owns and
-    fold them in with add(dst_view, src). acc holds planes [z_lo, z_lo + len(acc)); send is a list
-    of (dst, z0, z1), recv of (src, z0, z1, buffer). Works for any torch device the process group
-    supports (NCCL on GPUs, gloo on CPU tensors)."""
-    import torch.distributed as dist
+def fold_bands(me: RankPlan, plans: list[RankPlan], recv, barrier, fold) -> None:
+    """The host protocol of a pass once this rank's tiles are blended: wait until every rank's bands
+    are complete, fold each band this rank owns (fold(src, dst_offset_planes, src_offset_planes,
+    planes)), then wait until every rank has read what it needs, so no accumulator is cleared or
+    freed while a neighbour still reads it."""
+    barrier()
+    for src, z0, z1 in recv:
+        fold(src, z0 - me.z_lo, z0 - plans[src].z_lo, z1 - z0)
+    barrier()
 
-    ops = [dist.P2POp(dist.isend, acc[z0 - z_lo:z1 - z_lo].contiguous(), dst, group=group) for dst, z0, z1 in send]
-    ops += [dist.P2POp(dist.irecv, buf, src, group=group) for src, z0, z1, buf in recv]
-    if ops:
-        for w in dist.batch_isend_irecv(ops):
-            w.wait()
-    for src, z0, z1, buf in recv:
-        add(acc[z0 - z_lo:z1 - z_lo], buf)
+
+class _DevArray:
+    """A raw device allocation seen by torch through __cuda_array_interface__ (no copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
 
 
 class ShardedPredictor:
-    """Runs one rank's share of a sliding-window prediction of a (D, H, W) u8 volume."""
+    """Runs one rank's share of a sliding-window prediction of a (D, H, W) u8 volume.
+
+    group: a host (gloo) process group over the ranks, used for the IPC hand-over at set-up and the
+    two barriers of each pass; None when world == 1."""
 
     def __init__(self, net, shape, overlap: float, batch: int, rank: int = 0, world: int = 1, group=None,
                  channel: int = 1, sigmoid: int = 0):
@@ -98,14 +101,30 @@ class ShardedPredictor:
         self.me = self.plans[rank]
         self.ex = exchanges(self.plans)
         D, H, W = self.shape
-        dev = torch.device("cuda", torch.cuda.current_device())
+        self.plane = H * W
+        self.dev_index = int(net.device)
+        dev = torch.device("cuda", self.dev_index)
         nz = max(self.me.z_hi - self.me.z_lo, 1)
         self.slab = torch.zeros((nz, H, W), dtype=torch.uint8, device=dev)
-        self.acc = torch.zeros((nz, H, W), dtype=torch.float32, device=dev)
+        # the accumulator window: a buffer the neighbours map to read their bands
+        L = lib()
+        ptr, handle = C.c_void_p(), (C.c_uint8 * 64)()
+        check(L.fx_ipc_buffer_alloc(self.dev_index, nz * self.plane * 4, C.byref(ptr), handle))
+        self._acc_ptr = ptr.value
+        self.acc = torch.as_tensor(_DevArray(self._acc_ptr, (nz, H, W), "<f4"), device=dev)
         self.u8 = torch.zeros((max(self.me.own_hi - self.me.own_lo, 1), H, W), dtype=torch.uint8, device=dev)
-        self.recv = [(src, z0, z1, torch.empty((z1 - z0, H, W), dtype=torch.float32, device=dev))
-                     for (src, dst, z0, z1) in self.ex if dst == rank]
-        self.send = [(dst, z0, z1) for (src, dst, z0, z1) in self.ex if src == rank]
+        self.recv = [(src, z0, z1) for (src, dst, z0, z1) in self.ex if dst == rank]
+        self.peers = {}
+        if world > 1:
+            import torch.distributed as dist
+
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            for src in sorted({s for s, _, _ in self.recv}):
+                p = C.c_void_p()
+                h = (C.c_uint8 * 64).from_buffer_copy(handles[src])
+                check(L.fx_ipc_open(self.dev_index, h, C.byref(p)))
+                self.peers[src] = p.value
         self.stream = torch.cuda.Stream(device=dev)  # default stream for run(); never the null stream
         g = gaussian1d(net.patch)
         prof = [weight_profile(g, net.patch, tile_starts(n, net.patch, overlap), 0, n, n) for n in self.shape]
@@ -113,14 +132,24 @@ class ShardedPredictor:
 
     @property
     def h2d_bytes(self) -> int:
-        return int(self.slab.numel())
+        return int(max(self.me.z_hi - self.me.z_lo, 0) * self.plane)
 
     @property
     def d2h_bytes(self) -> int:
-        return int((self.me.own_hi - self.me.own_lo) * self.shape[1] * self.shape[2])
+        return int((self.me.own_hi - self.me.own_lo) * self.plane)
+
+    @property
+    def band_bytes(self) -> int:
+        """Accumulator bytes this rank reads from its neighbours per pass (over NVLink)."""
+        return int(sum((z1 - z0) * self.plane * 4 for _, z0, z1 in self.recv))
+
+    def _barrier(self):
+        if self.world > 1:
+            self.torch.distributed.barrier(group=self.group)
 
     def run(self, host_slab=None, host_out=None, stream=None) -> None:
-        """One full pass: [H2D slab] -> tiles -> band exchange -> finalise owned planes [-> D2H]."""
+        """One full pass: [H2D slab] -> tiles -> barrier -> fold the neighbours' bands over NVLink ->
+        barrier -> finalise owned planes [-> D2H]."""
         torch = self.torch
         L = lib()
         s = self.stream if stream is None else stream
@@ -129,22 +158,45 @@ class ShardedPredictor:
             raise ValueError("ShardedPredictor.run needs a non-null CUDA stream")
         me = self.me
         D, H, W = self.shape
+        live = me.tile_end > me.tile_begin
         with torch.cuda.stream(s):
-            if host_slab is not None:
+            if host_slab is not None and live:
                 self.slab.copy_(host_slab, non_blocking=True)
             self.acc.zero_()
-            if me.tile_end > me.tile_begin:
+            if live:
                 self.net.predict_tiles_dev(self.slab.data_ptr(), tuple(self.slab.shape), me.z_lo, D, self.overlap,
                                            self.batch, me.tile_begin, me.tile_end, self.acc.data_ptr(),
                                            channel=self.channel, sigmoid=self.sigmoid, stream=sp)
-            if self.world > 1 and self.ex:
-                exchange_bands(self.acc, me.z_lo, self.send, self.recv, self.group,
-                               lambda dst, src: check(L.fx_accum_add(dst.data_ptr(), src.data_ptr(), src.numel(), sp)))
-            n_own = me.own_hi - me.own_lo
-            if n_own > 0:
+        if self.world > 1:
+            s.synchronize()
+            check(L.fx_net_device_status(self.net.handle))
+            pb = self.plane * 4
+
+            def fold(src, dz0, sz0, nzb):
+                check(L.fx_accum_add(self._acc_ptr + dz0 * pb, self.peers[src] + sz0 * pb, nzb * self.plane, sp))
+
+            fold_bands(me, self.plans, self.recv, self._barrier, fold)
+            s.synchronize()
+        n_own = me.own_hi - me.own_lo
+        if n_own > 0:
+            with torch.cuda.stream(s):
                 # Wz is indexed by slab-local z: start the profile at plane z_lo
-                check(L.fx_accum_finalize(self.acc.data_ptr(), me.z_hi - me.z_lo, H, W, me.own_lo - me.z_lo,
+                check(L.fx_accum_finalize(self._acc_ptr, me.z_hi - me.z_lo, H, W, me.own_lo - me.z_lo,
                                           me.own_hi - me.z_lo, self.wz.data_ptr() + 4 * me.z_lo,
                                           self.wy.data_ptr(), self.wx.data_ptr(), None, self.u8.data_ptr(), sp))
                 if host_out is not None:
                     host_out[:n_own].copy_(self.u8[:n_own], non_blocking=True)
+
+    def close(self) -> None:
+        """Unmap the neighbours' buffers, wait until every rank has, then free this rank's."""
+        L = lib()
+        if getattr(self, "_acc_ptr", None) is None:
+            return
+        self.torch.cuda.synchronize(self.dev_index)
+        for p in self.peers.values():
+            check(L.fx_ipc_close(self.dev_index, p))
+        self.peers = {}
+        self._barrier()
+        self.acc = None
+        check(L.fx_ipc_buffer_free(self.dev_index, self._acc_ptr))
+        self._acc_ptr = None

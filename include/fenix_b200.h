@@ -120,6 +120,17 @@ fx_status fx_net_set_act_scales(fx_net* net, const float* scales, int count);
  * (the first conv, input channels not a multiple of 32) stay 16-bit. Default: every eligible
  * layer e4m3. */
 fx_status fx_net_set_layer_precision(fx_net* net, const int* precision, int count);
+/* Calibrated precision schedule of an fp8 net from n host patches ([n][P][P][P] u8): calibrates the
+ * scales if needed, then measures, against the net's own 16-bit forward of the patches, what e4m3
+ * operands in each layer alone cost (Dice of the 0.5-thresholded masks, max |dp|) and save (conv
+ * time of both operand types, CUDA events), takes layers greedily by time saved per unit of squared
+ * Dice loss while the summed squared losses stay within (1 - min_dice)^2 and no layer alone moves a
+ * probability by more than max_abs (<= 0: unbounded), runs the result and gives layers back until it
+ * meets both bounds. dice / maxabs (either may be NULL) receive the schedule's agreement with the
+ * 16-bit forward. The reference's fp8 notes keep their sensitive layers in 16-bit by hand
+ * (docs/design/fp8-conv3d-sm120.md:71-103); this measures the sensitivity instead. */
+fx_status fx_net_calibrate_schedule(fx_net* net, const uint8_t* host_patches, int n, double min_dice, double max_abs,
+                                    double* dice, double* maxabs);
 /* The operand precision each conv layer runs with (fx_precision values, fx_net_act_scales order)
  * and, when flops is non-NULL, its algorithmic FLOPs per tile (2 x MACs); returns the count. */
 int fx_net_layer_precision(const fx_net* net, int* precision, double* flops, int cap);
@@ -147,9 +158,52 @@ fx_status fx_predict_volume(fx_net* net, const uint8_t* host_vol, int64_t dz, in
 fx_status fx_predict_tiles_dev(fx_net* net, const uint8_t* dev_slab, int64_t slab_dz, int64_t dy, int64_t dx,
                                int64_t z_origin, int64_t full_dz, const fx_infer_opts* opts, int64_t tile_begin,
                                int64_t tile_end, float* dev_acc, void* stream);
-/* dev_dst[i] += dev_src[i] over n f32 values (both 16-byte aligned): folds the band another GPU
- * accumulated for planes this GPU owns into its own accumulator. */
+/* The device status word of the net's kernels: FX_OK, or FX_INTERNAL with the code in the message
+ * when a kernel's bounded wait gave up (the kernel then returns early instead of hanging, and its
+ * outputs are undefined). Synchronises the net's stream and clears the word; call it after the
+ * stream given to fx_predict_tiles_dev is synchronised. fx_predict_volume and fx_net_forward check
+ * it themselves. The reference's counterpart is the worker error path (src/ml/infer.hpp:675-808). */
+fx_status fx_net_device_status(fx_net* net);
+/* Failure-detection self-test: one small conv launch whose MMA warp waits on a barrier that nothing
+ * arrives at, with every wait bounded by wait_ns. The launch ends by itself after about wait_ns and
+ * *status_out receives the kernel's status word, the code of the first wait that gave up (0x100: the
+ * MMA warp's stage wait, 0x300: the epilogue's accumulator wait); the context stays usable. No reference counterpart (the reference has no device code). */
+fx_status fx_selftest_wait_timeout(int device, uint64_t wait_ns, uint32_t* status_out);
+/* dev_dst[i] += dev_src[i] over n f32 values: folds the band another GPU accumulated for planes
+ * this GPU owns into its own accumulator. dev_src may be another GPU's memory (a peer pointer or an
+ * IPC mapping): the kernel then reads it over NVLink. 16-byte aligned pointers take the vector path. */
 fx_status fx_accum_add(float* dev_dst, const float* dev_src, int64_t n, void* stream);
+
+/* ---- several GPUs, no collective (z-slab sharding) ----
+ * The reference runs one replica per GPU on worker threads over one global tile grid
+ * (src/ml/inference.cpp:1129-1188, 1402-1586). Here the z-major tile list of the volume's grid is
+ * split into contiguous near-equal ranges, one per GPU; shard r reads input planes [z_lo, z_hi)
+ * (every plane its tiles touch), accumulates over the same planes and finalises the planes it owns,
+ * [own_lo, own_hi) (a partition of [0, dz)). A shard with no tiles has tile_begin == tile_end. */
+typedef struct fx_shard {
+    int64_t tile_begin, tile_end;
+    int64_t z_lo, z_hi;
+    int64_t own_lo, own_hi;
+} fx_shard;
+/* Writes nshards plans to out (when non-NULL); returns nshards, or 0 on bad arguments. */
+int fx_shard_plan(int64_t dz, int64_t dy, int64_t dx, int patch, double overlap, int nshards, fx_shard* out);
+/* fx_predict_volume over n nets (normally one per device; nets may share a device), one host thread
+ * per net: each uploads its
+ * input slab, blends its tile range into its own accumulator window, then (after every device has
+ * finished) adds the bands its neighbours accumulated for its owned planes, read from their HBM over
+ * NVLink by an add kernel (staged with a peer copy where the devices cannot map each other), and
+ * finalises and downloads its owned planes. Same outputs as fx_predict_volume. */
+fx_status fx_predict_volume_multi(fx_net* const* nets, int n, const uint8_t* host_vol, int64_t dz, int64_t dy,
+                                  int64_t dx, const fx_infer_opts* opts, float* host_prob, uint8_t* host_u8);
+
+/* Device buffers another process can map: with one process per GPU, a shard's accumulator window is
+ * allocated here and its CUDA IPC handle (64 bytes) handed to the neighbours through the host, which
+ * map it (fx_ipc_open) and fold the bands they own with fx_accum_add reading it over NVLink. The
+ * buffer's owner frees it only after every mapping of it is closed. */
+fx_status fx_ipc_buffer_alloc(int device, uint64_t bytes, void** dev_ptr, void* handle);
+fx_status fx_ipc_buffer_free(int device, void* dev_ptr);
+fx_status fx_ipc_open(int device, const void* handle, void** dev_ptr);
+fx_status fx_ipc_close(int device, void* dev_ptr);
 
 /* Device timing of the tensor-core convolutions: with profiling enabled every conv launch of
  * this net is bracketed by CUDA events on its stream; fx_net_profile_read synchronises them and

@@ -92,7 +92,8 @@ def forward(params: dict, x: torch.Tensor, types: dict | None = None, scales: di
 def gpu_types(features, precision: str, nconv: int = 2) -> dict:
     """Operand type of every layer in the library's nets: 16-bit layers are 'bf16' for bf16 nets
     and 'f16' otherwise; fp8 nets use e4m3 except the first conv and convs whose input channel
-    count is not a multiple of 32."""
+    count is not a multiple of 32. The first conv splits its operands into two 16-bit terms, which
+    is modelled as fp32 operands."""
     S = len(features)
     t16 = "bf16" if precision == "bf16" else "f16"
     types = {}
@@ -109,4 +110,5 @@ def gpu_types(features, precision: str, nconv: int = 2) -> dict:
             cin[f"d{t}{i}"] = 2 * features[lv] if i == 0 else features[lv]
     for k, c in cin.items():
         types[k] = "e4m3" if (precision == "fp8" and k != "e00" and c % 32 == 0) else t16
+    types["e00"] = "f32"  # the first conv carries its input and weights as hi + lo 16-bit terms
     return types

@@ -61,7 +61,7 @@ CONV_CASES = [
     (1, 128, 256, (8, 8, 8), 1),
     (1, 256, 320, (4, 4, 4), 2),
     (1, 320, 320, (4, 4, 4), 1),
-    (1, 1, 32, (16, 12, 20), 1),  # the 1-channel first layer (x-folded taps)
+    (1, 1, 32, (16, 12, 20), 1),  # the 1-channel first layer (x-folded taps, hi + lo split)
     (1, 32, 32, (3, 5, 7), 1),     # fewer rows than one M block
     (2, 32, 16, (20, 14, 30), 1),
     (1, 64, 32, (24, 20, 18), 1),
@@ -93,7 +93,9 @@ def test_conv3d_16bit(cuda_torch, fold_mode, B, Cin, Cout, dims, stride, kind):
     D, H, W = dims
     x = torch.randn(B, Cin, D, H, W, generator=g)
     w = torch.randn(Cout, Cin, 3, 3, 3, generator=g) * (2.0 / (27 * Cin)) ** 0.5
-    ref = F.conv3d(_q16(x, kind), _q16(w, kind), stride=stride, padding=1)
+    # the 1-channel first layer carries input and weights as hi + lo 16-bit terms (about fp32)
+    xq, wq = (x, w) if Cin == 1 else (_q16(x, kind), _q16(w, kind))
+    ref = F.conv3d(xq, wq, stride=stride, padding=1)
     xd, wd = x.cuda(), w.cuda()
     y = torch.zeros_like(ref, device="cuda")
     st = torch.zeros(B, Cout, 2, device="cuda")

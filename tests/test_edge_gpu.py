@@ -72,3 +72,38 @@ def test_abi_argument_checks(cuda_torch, tmp_path):
     assert L.fx_predict_volume(net.handle, vp, 8, 8, 8, C.byref(odd), None, op) == 1
     assert L.fx_last_error()  # every failure leaves a message
     net.close()
+
+
+@pytest.mark.parametrize("bias1,channel,sigmoid,want", [
+    (np.inf, 1, 0, 0.0),    # softmax over [finite, +inf] = [0, nan] -> nan_to_num -> 0
+    (np.inf, 0, 0, 0.0),    # the other channel: 0 / nan -> 0
+    (-np.inf, 1, 0, 0.0),   # exp(-inf) = 0
+    (-np.inf, 0, 0, 1.0),
+    (np.nan, 1, 0, 0.0),    # NaN logits everywhere -> 0
+    (np.inf, 0, 1, 1.0),    # sigmoid(+inf) = 1
+    (np.nan, 0, 1, 0.0),
+])
+def test_head_scrubs_nan_and_inf(cuda_torch, tmp_path, bias1, channel, sigmoid, want):
+    """A non-finite head bias makes every logit of that class non-finite; the fused head kernel
+    scrubs the probability as the reference's nan_to_num(nan=0, posinf=1, neginf=0) does
+    (src/ml/infer.hpp:760-767), and the oracle gives the same bytes."""
+    from fenix_b200.weights import plain_unet_params, write_fxweights
+
+    ncls = 1 if sigmoid else 2
+    prm = plain_unet_params(FEATS, ncls=ncls, seed=7)
+    key = f"decoder.seg_layers.{len(FEATS) - 2}.bias"
+    prm[key] = prm[key].copy()
+    prm[key][-1 if not sigmoid else 0] = bias1
+    w = tmp_path / "nan.fxweights"
+    write_fxweights(w, prm)
+    vol = fx.synth_spiral((72, 64, 80), 11, fx.SPIRAL_CONFIG1)
+    net = fx.Net(w, 64, max_batch=2, precision="f16")
+    prob, u8 = net.predict_volume(vol, overlap=0.5, batch=2, channel=channel, sigmoid=sigmoid)
+    net.close()
+    assert np.isfinite(prob).all()
+    # a constant tile probability survives the blend up to the rounding of the weight sums
+    assert float(np.abs(prob - np.float32(want)).max()) <= 1e-6, (prob.min(), prob.max())
+    oracle = orc.Net(w).predict_surface(vol, 64, 0.5, channel=channel, sigmoid=sigmoid)
+    assert float(np.abs(prob - oracle).max()) <= 1e-6
+    assert np.array_equal(u8, orc.prob_to_u8(oracle))
+    assert np.all(u8 == np.uint8(round(want * 255)))

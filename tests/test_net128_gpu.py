@@ -98,3 +98,27 @@ def test_fp8_all_layers_distance_reported(cuda_torch, tmp_path, name):
     print(f"net128 {name} fp8 all layers: max-abs {mx:.3e} mean {mean:.3e} Dice {d:.5f}")
     assert d >= 0.9
     net.close()
+
+
+SCHED_DICE = 0.993  # the schedule's target agreement with the 16-bit forward on the calibration patches
+
+
+@pytest.mark.parametrize("name", ["cfg2", "cfg3"])
+def test_fp8_calibrated_schedule(cuda_torch, tmp_path, name):
+    """The calibrated mixed schedule (fx_net_calibrate_schedule on the benchmark's calibration
+    patches) against the reference's full map: Dice >= 0.99 on the 0.5-thresholded mask, with
+    part of the convolution work on e4m3 operands."""
+    g, w, vol, sp, ref = load(name, tmp_path)
+    P = int(g["patch"])
+    net = fx.Net(w, P, max_batch=4, precision="fp8")
+    d_cal, m_cal = net.calibrate_schedule(calib_patches(P, sp), min_dice=SCHED_DICE)
+    layers = net.layers()
+    f8 = [l["name"] for l in layers if l["precision"] == "fp8"]
+    share = sum(l["flops"] for l in layers if l["precision"] == "fp8") / sum(l["flops"] for l in layers)
+    prob, _ = net.predict_volume(vol, overlap=float(g["overlap"]), batch=4)
+    mx, mean, d = metrics(prob, ref)
+    print(f"net128 {name} fp8 schedule: {len(f8)} e4m3 layers ({share:.1%} of conv FLOPs) {f8}; calibration "
+          f"Dice {d_cal:.5f} max {m_cal:.3e}; vs reference max-abs {mx:.3e} mean {mean:.3e} Dice {d:.5f}")
+    assert d_cal >= SCHED_DICE
+    assert d >= DICE_MIN
+    net.close()

@@ -1,5 +1,7 @@
-"""z-slab sharding (fenix_b200/shard.py) on the CPU: the rank plan, and the band exchange between
-two gloo ranks against the one-process blend of the same tiles."""
+"""z-slab sharding (fenix_b200/shard.py, fx_shard_plan) on the CPU: the rank plan, and the band fold
+protocol of one pass between gloo ranks against the one-process blend of the same tiles. On the GPU
+a neighbour's accumulator is read through a CUDA IPC mapping; here each rank's accumulator is a
+memory-mapped file its neighbours read, with the same plan, exchanges and barriers."""
 import os
 import tempfile
 
@@ -7,7 +9,7 @@ import numpy as np
 import pytest
 
 import fenix_b200 as fx
-from fenix_b200.shard import exchange_bands, exchanges, plan
+from fenix_b200.shard import exchanges, fold_bands, plan
 
 
 def tile_grid(shape, P, ov):
@@ -82,7 +84,6 @@ CASE = ((150, 40, 36), 32, 0.5)
 
 
 def _rank(rank, world, port, outdir):
-    import torch
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -91,13 +92,19 @@ def _rank(rank, world, port, outdir):
         shape, P, ov = CASE
         plans = plan(shape, P, ov, world)
         me = plans[rank]
-        ex = exchanges(plans)
-        acc = torch.from_numpy(blend(shape, P, ov, range(me.tile_begin, me.tile_end), me.z_lo, me.z_hi))
-        send = [(d, z0, z1) for s, d, z0, z1 in ex if s == rank]
-        recv = [(s, z0, z1, torch.empty((z1 - z0,) + shape[1:], dtype=torch.float32))
-                for s, d, z0, z1 in ex if d == rank]
-        exchange_bands(acc, me.z_lo, send, recv, None, lambda dst, src: dst.add_(src))
-        own = finalize(acc.numpy(), shape, P, ov, me.z_lo)[me.own_lo - me.z_lo:me.own_hi - me.z_lo]
+        recv = [(s, z0, z1) for s, d, z0, z1 in exchanges(plans) if d == rank]
+        nz = max(me.z_hi - me.z_lo, 1)
+        acc = np.lib.format.open_memmap(os.path.join(outdir, f"acc{rank}.npy"), mode="w+", dtype=np.float32,
+                                        shape=(nz,) + shape[1:])
+        acc[:me.z_hi - me.z_lo] = blend(shape, P, ov, range(me.tile_begin, me.tile_end), me.z_lo, me.z_hi)
+        acc.flush()
+
+        def fold(src, dz0, sz0, n):
+            peer = np.load(os.path.join(outdir, f"acc{src}.npy"), mmap_mode="r")
+            acc[dz0:dz0 + n] += peer[sz0:sz0 + n]
+
+        fold_bands(me, plans, recv, dist.barrier, fold)
+        own = finalize(np.asarray(acc[:me.z_hi - me.z_lo]), shape, P, ov, me.z_lo)[me.own_lo - me.z_lo:me.own_hi - me.z_lo]
         np.save(os.path.join(outdir, f"r{rank}.npy"), own)
         dist.barrier()
     finally:
@@ -105,7 +112,7 @@ def _rank(rank, world, port, outdir):
 
 
 @pytest.mark.parametrize("world", [2, 3])
-def test_gloo_band_exchange_matches_single_process(world):
+def test_gloo_band_fold_matches_single_process(world):
     import socket
 
     import torch.multiprocessing as mp
