@@ -41,8 +41,13 @@ class FxError(RuntimeError):
         self.code = code
 
 
+TileFilter = C.CFUNCTYPE(C.c_int, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_void_p)
+NORMS = {"zscore": 0, "pct_minmax": 1, "unit255": 2}
+
+
 class InferOpts(C.Structure):
-    """fx_infer_opts (mirrors the reference's ml::InferOptions subset)."""
+    """fx_infer_opts (mirrors the reference's ml::InferOptions): fields after tta default to zero =
+    zscore, every tile, no crop, no filter."""
 
     _fields_ = [
         ("patch", C.c_int),
@@ -51,6 +56,12 @@ class InferOpts(C.Structure):
         ("sigmoid", C.c_int),
         ("batch", C.c_int),
         ("tta", C.c_int),
+        ("norm", C.c_int),
+        ("skip_constant", C.c_int),
+        ("core_org", C.c_int64 * 3),
+        ("core_ext", C.c_int64 * 3),
+        ("tile_filter", TileFilter),
+        ("tile_filter_user", C.c_void_p),
     ]
 
 
@@ -124,6 +135,7 @@ def lib():
     _sig(L, "fx_gaussian1d", None, [i32, f32p])
     _sig(L, "fx_weight_profile", None, [f32p, i32, C.POINTER(C.c_int64), i64, i64, i64, i64, f32p])
     _sig(L, "fx_norm_tiles", i32, [vp, i64, i64, i64, C.POINTER(C.c_int64), i32, i32, vp, vp])
+    _sig(L, "fx_norm_tiles_mode", i32, [vp, i64, i64, i64, C.POINTER(C.c_int64), i32, i32, i32, vp, vp])
     _sig(L, "fx_norm_tiles_noalloc", i32, [vp, i64, i64, i64, C.POINTER(C.c_int64), i32, i32, vp, vp])
     i64p = C.POINTER(C.c_int64)
     _sig(L, "fx_gaccum_create", i32, [i64p, i64p, i32, C.c_double, i64, i32, C.POINTER(vp)])
@@ -142,6 +154,7 @@ def lib():
     _sig(L, "fx_net_profile_read", i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_double),
                                          C.POINTER(C.c_int64), C.POINTER(C.c_double), i32])
     _sig(L, "fx_kernel_launches", C.c_ulonglong, [])
+    _sig(L, "fx_tc_peak", i32, [i32, i32, C.c_double, i32, C.POINTER(C.c_double), C.POINTER(C.c_double)])
     _sig(L, "fx_synth_spiral", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
     u64p, u32p = C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)
     _sig(L, "fx_fxvol_open", i32, [C.c_char_p, C.POINTER(vp)])
@@ -218,6 +231,13 @@ def synth_spiral(shape, seed: int, params: dict | None = None, z_begin: int = 0,
 def kernel_launches() -> int:
     """Kernel launches issued by libfenix_b200 in this process."""
     return int(lib().fx_kernel_launches())
+
+
+def tc_peak(precision: str = "fp8", ms_per_run: float = 50.0, runs: int = 10, device: int = 0):
+    """Measured dense tensor rate (TFLOP/s) of this library's MMA-loop kernel: (best, mean) over runs."""
+    b, m = C.c_double(), C.c_double()
+    check(lib().fx_tc_peak(device, PRECISIONS[precision], ms_per_run, runs, C.byref(b), C.byref(m)))
+    return b.value, m.value
 
 
 def device_count() -> int:
@@ -322,12 +342,24 @@ class Net:
         check(lib().fx_net_forward(self._h, dev_tiles_ptr, nb, dev_prob_ptr, channel, sigmoid, stream))
 
     def predict_volume(self, vol_u8: np.ndarray, overlap: float = 0.5, batch: int = 1, channel: int = 1,
-                       sigmoid: int = 0, want_prob: bool = True, want_u8: bool = True, tta: int = 0):
+                       sigmoid: int = 0, want_prob: bool = True, want_u8: bool = True, tta: int = 0,
+                       norm: str = "zscore", skip_constant: bool = False, core=None, tile_filter=None):
+        """core = (z, y, x, dz, dy, dx) output crop (extents <= 0: to the end); tile_filter =
+        callable(z0, y0, x0, patch) -> bool. Outputs have the crop's dims when cropped."""
         v = np.ascontiguousarray(vol_u8, dtype=np.uint8)
         dz, dy, dx = v.shape
-        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch, tta)
-        prob = np.zeros(v.shape, dtype=np.float32) if want_prob else None
-        u8 = np.zeros(v.shape, dtype=np.uint8) if want_u8 else None
+        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch, tta, NORMS[norm], 1 if skip_constant else 0)
+        out_shape = v.shape
+        if core is not None:
+            opts.core_org[:] = list(core[:3])
+            opts.core_ext[:] = list(core[3:])
+            out_shape = tuple(min(e, n - o) if e > 0 else n - o
+                              for o, e, n in zip((min(max(c, 0), n) for c, n in zip(core[:3], v.shape)), core[3:], v.shape))
+        if tile_filter is not None:
+            cb = TileFilter(lambda z0, y0, x0, p, _u: 1 if tile_filter(z0, y0, x0, p) else 0)
+            opts.tile_filter = cb
+        prob = np.zeros(out_shape, dtype=np.float32) if want_prob else None
+        u8 = np.zeros(out_shape, dtype=np.uint8) if want_u8 else None
         check(
             lib().fx_predict_volume(
                 self._h,

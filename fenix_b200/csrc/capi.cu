@@ -80,31 +80,60 @@ fx_status abi_exception() {
         return set_err(FX_INTERNAL, "internal error");
     }
 }
+// ml::InferOptions fields beyond the tile grid, as the driver's per-call options.
+RunOpts run_opts(const fx_infer_opts* o) {
+    RunOpts r;
+    r.norm = o->norm;
+    r.skip_constant = o->skip_constant != 0;
+    r.filter = o->tile_filter;
+    r.filter_user = o->tile_filter_user;
+    for (int a = 0; a < 3; ++a) {
+        r.core_org[a] = o->core_org[a];
+        r.core_ext[a] = o->core_ext[a];
+    }
+    return r;
+}
+
+// The output crop of opts over an input of dims d (src/ml/infer.hpp:462-472): origin clamped into
+// the input, extent (<= 0: to the end) clamped to it.
+void crop_box(const fx_infer_opts* o, const int64_t d[3], int64_t co[3], int64_t ce[3]) {
+    for (int a = 0; a < 3; ++a) {
+        co[a] = std::clamp<int64_t>(o->core_org[a], 0, d[a]);
+        ce[a] = o->core_ext[a] <= 0 ? d[a] - co[a] : std::min(o->core_ext[a], d[a] - co[a]);
+    }
+}
+
 // The device part of fx_predict_volume (src/ml/infer.hpp:456-864 + inference.cpp:343-351): d_vol
-// (resident, dims dz, dy, dx) -> Gaussian blend in d_acc -> normalised probability in d_prob
-// (may alias d_acc) and/or u8 in d_u8. Stream-ordered on the net's stream; no final sync.
+// (resident, dims dz, dy, dx) -> Gaussian blend in d_acc (the crop's dims) -> normalised probability
+// in d_prob (may alias d_acc) and/or u8 in d_u8. Runs on the net's stream and synchronises it.
 fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx,
                            const fx_infer_opts* o, float* d_acc, float* d_prob, uint8_t* d_u8) {
     cudaStream_t s = n->net.stream();
-    const size_t nv = static_cast<size_t>(dz) * dy * dx;
+    const int64_t d[3] = {dz, dy, dx};
+    int64_t co[3], ce[3];
+    crop_box(o, d, co, ce);
+    if (ce[0] < 1 || ce[1] < 1 || ce[2] < 1) return set_err(FX_INVALID_ARGUMENT, "predict: empty output crop");
+    const size_t nv = static_cast<size_t>(ce[0]) * ce[1] * ce[2];
     cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
     Status st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, o->patch, o->overlap, o->channel, o->sigmoid, o->batch,
-                                     0, -1, d_acc, s, 0, -1, o->tta);
+                                     0, -1, d_acc, s, co[0], ce[0], o->tta, run_opts(o));
     if (!st.ok()) return set_err(st);
     const int P = o->patch;
     const auto g = fenix::ml::gaussian1d(P);
-    const auto zs = fenix::ml::tile_starts(dz, P, o->overlap), ys = fenix::ml::tile_starts(dy, P, o->overlap),
-               xs = fenix::ml::tile_starts(dx, P, o->overlap);
-    const auto Wz = fenix::ml::weight_profile(g, zs, 0, dz, dz, P), Wy = fenix::ml::weight_profile(g, ys, 0, dy, dy, P),
-               Wx = fenix::ml::weight_profile(g, xs, 0, dx, dx, P);
-    std::vector<float> w(static_cast<size_t>(dz + dy + dx));
-    std::copy(Wz.begin(), Wz.end(), w.begin());
-    std::copy(Wy.begin(), Wy.end(), w.begin() + dz);
-    std::copy(Wx.begin(), Wx.end(), w.begin() + dz + dy);
+    std::vector<float> w(static_cast<size_t>(ce[0] + ce[1] + ce[2]));
+    size_t at = 0;
+    for (int a = 0; a < 3; ++a) {
+        // the factorised weight over the crop's span of each axis (src/ml/infer.hpp:499-509)
+        const auto starts = fenix::ml::tile_starts(d[a], P, o->overlap);
+        const auto W = fenix::ml::weight_profile(g, starts, co[a], ce[a], d[a], P);
+        std::copy(W.begin(), W.end(), w.begin() + static_cast<std::ptrdiff_t>(at));
+        at += static_cast<size_t>(ce[a]);
+    }
     float* d_w = nullptr;
     if (cudaMalloc(&d_w, sizeof(float) * w.size()) != cudaSuccess) return set_err(FX_INTERNAL, "cudaMalloc: weight profiles");
     cudaMemcpyAsync(d_w, w.data(), sizeof(float) * w.size(), cudaMemcpyHostToDevice, s);
-    cudaError_t e = fxk::launch_accum_finalize(d_acc, dz, dy, dx, 0, dz, d_w, d_w + dz, d_w + dz + dy, d_prob, d_u8, s);
+    cudaError_t e = fxk::launch_accum_finalize(d_acc, ce[0], ce[1], ce[2], 0, ce[0], d_w, d_w + ce[0],
+                                               d_w + ce[0] + ce[1], d_prob, d_u8, s);
     cudaStreamSynchronize(s);
     cudaFree(d_w);
     if (e != cudaSuccess) return set_err(cuda_status(e, "accum_finalize"));
@@ -290,9 +319,13 @@ fx_status fx_predict_tiles_dev(fx_net* n, const uint8_t* dev_slab, int64_t slab_
         if (o->patch % 64 != 0) return set_err(FX_INVALID_ARGUMENT, "patch must be divisible by 64");
         cudaSetDevice(n->net.device());
         cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : n->net.stream();
+        fxh::RunOpts ro = fxh::run_opts(o);
+        if (ro.core_org[0] || ro.core_org[1] || ro.core_org[2] || ro.core_ext[0] > 0 || ro.core_ext[1] > 0 ||
+            ro.core_ext[2] > 0)
+            return set_err(FX_UNSUPPORTED, "fx_predict_tiles_dev: output crops are taken by fx_predict_volume only");
         fxh::Status st = n->net.predict_tiles(dev_slab, slab_dz, dy, dx, z_origin, full_dz, o->patch, o->overlap,
                                               o->channel, o->sigmoid, o->batch, tile_begin, tile_end, dev_acc, s, 0,
-                                              -1, o->tta);
+                                              -1, o->tta, ro);
         return st.ok() ? FX_OK : set_err(st);
     });
 }
@@ -376,17 +409,23 @@ fx_status fx_predict_volume(fx_net* n, const uint8_t* host_vol, int64_t dz, int6
         cudaSetDevice(n->net.device());
         cudaStream_t s = n->net.stream();
         const size_t nv = static_cast<size_t>(dz) * dy * dx;
+        const int64_t d[3] = {dz, dy, dx};
+        int64_t co[3], ce[3];
+        fxh::crop_box(o, d, co, ce);
+        const size_t no = static_cast<size_t>(std::max<int64_t>(ce[0], 0)) * std::max<int64_t>(ce[1], 0) *
+                          std::max<int64_t>(ce[2], 0);  // output voxels
         uint8_t *d_vol = nullptr, *d_u8 = nullptr;
         float* d_acc = nullptr;
-        fxh::Status st = n->net.workspace(nv, nv * sizeof(float), host_u8 ? nv : 0, &d_vol, &d_acc, &d_u8);
+        fxh::Status st = n->net.workspace(nv, std::max<size_t>(no, 1) * sizeof(float), host_u8 ? std::max<size_t>(no, 1) : 0,
+                                          &d_vol, &d_acc, &d_u8);
         if (!st.ok()) return set_err(st);
         cudaMemcpyAsync(d_vol, host_vol, nv, cudaMemcpyHostToDevice, s);
         // the normalised probability overwrites the accumulator in place
         float* d_prob = host_prob ? d_acc : nullptr;
         if (fx_status r = fxh::predict_resident(n, d_vol, dz, dy, dx, o, d_acc, d_prob, host_u8 ? d_u8 : nullptr))
             return r;
-        if (host_prob) cudaMemcpyAsync(host_prob, d_prob, nv * sizeof(float), cudaMemcpyDeviceToHost, s);
-        if (host_u8) cudaMemcpyAsync(host_u8, d_u8, nv, cudaMemcpyDeviceToHost, s);
+        if (host_prob) cudaMemcpyAsync(host_prob, d_prob, no * sizeof(float), cudaMemcpyDeviceToHost, s);
+        if (host_u8) cudaMemcpyAsync(host_u8, d_u8, no, cudaMemcpyDeviceToHost, s);
         cudaError_t e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "predict_volume"));
         return FX_OK;
@@ -457,6 +496,34 @@ fx_status fx_norm_tiles(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t 
                                       dev_out, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles"));
+    });
+}
+
+fx_status fx_norm_tiles_mode(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx, const int64_t* host_origins,
+                             int ntiles, int patch, int norm, float* dev_out, void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!dev_vol || !host_origins || !dev_out || ntiles < 1 || ntiles > 65535 || patch < 1 || norm < 0 || norm > 2)
+            return set_err(FX_INVALID_ARGUMENT, "fx_norm_tiles_mode: bad argument");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        Scratch sc;
+        std::vector<fxk::TileOrigin> org(ntiles);
+        for (int i = 0; i < ntiles; ++i) org[i] = {host_origins[3 * i], host_origins[3 * i + 1], host_origins[3 * i + 2]};
+        auto* d_org = static_cast<fxk::TileOrigin*>(sc.get(sizeof(fxk::TileOrigin) * ntiles));
+        auto* d_sums = static_cast<unsigned long long*>(sc.get(sizeof(unsigned long long) * 2 * ntiles));
+        auto* d_hist = static_cast<unsigned*>(sc.get(sizeof(unsigned) * 256 * ntiles));
+        auto* d_lut = static_cast<float*>(sc.get(sizeof(float) * 256 * ntiles));
+        if (!d_org || !d_sums || !d_hist || !d_lut) return set_err(FX_INTERNAL, "cudaMalloc failed");
+        cudaMemcpyAsync(d_org, org.data(), sizeof(fxk::TileOrigin) * ntiles, cudaMemcpyHostToDevice, s);
+        cudaMemsetAsync(d_sums, 0, sizeof(unsigned long long) * 2 * ntiles, s);
+        cudaMemsetAsync(d_hist, 0, sizeof(unsigned) * 256 * ntiles, s);
+        cudaError_t e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, s, d_hist);
+        const int64_t n = static_cast<int64_t>(patch) * patch * patch;
+        if (e == cudaSuccess) e = fxk::launch_tile_lut(d_sums, d_hist, ntiles, n, norm, d_lut, nullptr, s);
+        if (e == cudaSuccess)
+            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, nullptr, 0, 0, fxk::kOpF16,
+                                      dev_out, s, nullptr, d_lut);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles_mode"));
     });
 }
 

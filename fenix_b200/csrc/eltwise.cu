@@ -27,9 +27,16 @@ __device__ __forceinline__ uint8_t vol_at(const uint8_t* vol, int64_t dz, int64_
 
 // Exact integer sum and sum of squares of a tile's u8 voxels (edge tiles clamp to the volume).
 // A warp walks whole (z, y) lines of the tile, lanes across x: one 32-bit division per line.
+template <bool HIST>
 __global__ void tile_sums_kernel(const uint8_t* __restrict__ vol, int64_t dz, int64_t dy, int64_t dx,
-                                 const TileOrigin* __restrict__ tiles, int P, unsigned long long* sums) {
+                                 const TileOrigin* __restrict__ tiles, int P, unsigned long long* sums,
+                                 unsigned* __restrict__ hist) {
     const int b = blockIdx.y;
+    __shared__ unsigned h[HIST ? 256 : 1];
+    if (HIST) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) h[i] = 0u;
+        __syncthreads();
+    }
     const TileOrigin t = tiles[b];
     const bool inside = t.z0 + P <= dz && t.y0 + P <= dy && t.x0 + P <= dx;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -45,6 +52,7 @@ __global__ void tile_sums_kernel(const uint8_t* __restrict__ vol, int64_t dz, in
             const uint32_t v = inside ? __ldg(src + x) : vol_at(vol, dz, dy, dx, t.z0 + z, t.y0 + y, t.x0 + x);
             a1 += v;
             a2 += v * v;
+            if (HIST) atomicAdd(&h[v], 1u);
         }
         s1 += a1;
         s2 += a2;
@@ -68,6 +76,11 @@ __global__ void tile_sums_kernel(const uint8_t* __restrict__ vol, int64_t dz, in
         atomicAdd(&sums[2 * b], a);
         atomicAdd(&sums[2 * b + 1], c);
     }
+    if (HIST) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < 256; i += blockDim.x)
+            if (h[i]) atomicAdd(hist + static_cast<int64_t>(b) * 256 + i, h[i]);
+    }
 }
 
 // Per-tile z-score table: lut[v] = (float)((v - mean) / sd) with mean = S/n and
@@ -82,15 +95,90 @@ __device__ __forceinline__ void build_lut(float* lut, unsigned long long S, unsi
         lut[v] = static_cast<float>(__ddiv_rn(__dsub_rn(static_cast<double>(v), mean), sd));
 }
 
+// Per-tile normalisation table of the u8 levels, one block of 256 threads per tile
+// (src/ml/infer.hpp:350-385, norm_patch):
+//  zscore   lut[v] = (float)((v - mean) / sd) from the exact sums (build_lut);
+//  unit255  lut[v] = (float)v * (1 / 255) in f32;
+//  pct_minmax  the reference's percentile bounds (infer.hpp:107-134): a 1024-bin histogram over
+//    [min, max] of the tile, whose bin of each u8 level is (x - min) * ((1024 - 1) / (max - min)) in
+//    f32, cut at the 0.5 / 99.5 percent counts, then lut[v] = clamp((v - lo) / (hi - lo), 0, 1) with
+//    the reciprocal taken first as the reference does. The u8 histogram gives every bin count
+//    exactly, so the table equals the per-voxel computation.
+// const_flag[b] (when non-null) = 1 for a tile whose voxels all hold one value.
+__global__ void tile_lut_kernel(const unsigned long long* __restrict__ sums, const unsigned* __restrict__ hist,
+                                int64_t n, int norm, float* __restrict__ luts, uint8_t* __restrict__ const_flag) {
+    const int b = blockIdx.x;
+    float* lut = luts + static_cast<int64_t>(b) * 256;
+    const unsigned long long S = sums[2 * b], Q = sums[2 * b + 1];
+    if (const_flag && threadIdx.x == 0) {
+        // constant <=> n Q == S^2 (128-bit products)
+        const unsigned long long un = static_cast<unsigned long long>(n);
+        const bool c = __umul64hi(un, Q) == __umul64hi(S, S) && un * Q == S * S;
+        const_flag[b] = c ? 1 : 0;
+    }
+    if (norm == 0) {
+        build_lut(lut, S, Q, n);
+        return;
+    }
+    if (norm == 2) {
+        lut[threadIdx.x] = __fmul_rn(static_cast<float>(threadIdx.x), 1.0f / 255.0f);
+        return;
+    }
+    __shared__ float s_lo, s_inv;
+    if (threadIdx.x == 0) {
+        const unsigned* hc = hist + static_cast<int64_t>(b) * 256;
+        int vmin = 255, vmax = 0;
+        for (int v = 0; v < 256; ++v)
+            if (hc[v]) {
+                vmin = min(vmin, v);
+                vmax = max(vmax, v);
+            }
+        const float mn = static_cast<float>(vmin), mx = static_cast<float>(vmax);
+        float lo, hi;
+        if (mx <= mn) {
+            lo = mn;
+            hi = __fadd_rn(mn, 1.0f);
+        } else {
+            const float inv = __fdiv_rn(1023.0f, __fsub_rn(mx, mn));
+            const long long tlo = static_cast<long long>(0.5 / 100.0 * static_cast<double>(n));
+            const long long thi = static_cast<long long>(99.5 / 100.0 * static_cast<double>(n));
+            // cumulative count over the 1024 bins: the u8 levels land in non-decreasing bins
+            long long c = 0;
+            int blo = 0, bhi = 1023, v = vmin;
+            for (int bin = 0; bin < 1024; ++bin) {
+                while (v <= vmax && static_cast<int>(__fmul_rn(__fsub_rn(static_cast<float>(v), mn), inv)) == bin) {
+                    c += hc[v];
+                    ++v;
+                }
+                if (c <= tlo) blo = bin;
+                if (c < thi) bhi = bin;
+            }
+            lo = __fadd_rn(mn, __fdiv_rn(static_cast<float>(blo), inv));
+            hi = __fadd_rn(mn, __fdiv_rn(static_cast<float>(bhi + 1), inv));
+            if (hi <= lo) hi = __fadd_rn(lo, 1.0f);
+        }
+        s_lo = lo;
+        s_inv = __fdiv_rn(1.0f, __fsub_rn(hi, lo));
+    }
+    __syncthreads();
+    const float r = __fmul_rn(__fsub_rn(static_cast<float>(threadIdx.x), s_lo), s_inv);
+    lut[threadIdx.x] = fminf(fmaxf(r, 0.0f), 1.0f);
+}
+
 __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, int64_t dy, int64_t dx,
                                  const TileOrigin* __restrict__ tiles, int P,
-                                 const unsigned long long* __restrict__ sums, uint8_t* __restrict__ l0,
+                                 const unsigned long long* __restrict__ sums, const float* __restrict__ luts,
+                                 uint8_t* __restrict__ l0,
                                  int64_t l0_batch_stride, int64_t l0_group_stride, int l0_type,
                                  float* __restrict__ f32_out, const uint8_t* __restrict__ tta) {
     const int b = blockIdx.y;
     __shared__ float lut[256];
     const int64_t n = static_cast<int64_t>(P) * P * P;
-    build_lut(lut, sums[2 * b], sums[2 * b + 1], n);
+    if (luts) {
+        for (int v = threadIdx.x; v < 256; v += blockDim.x) lut[v] = luts[static_cast<int64_t>(b) * 256 + v];
+    } else {
+        build_lut(lut, sums[2 * b], sums[2 * b + 1], n);
+    }
     __syncthreads();
     const TileOrigin t = tiles[b];
     const int Pp = P + 2;
@@ -520,11 +608,15 @@ __global__ void __launch_bounds__(kEwThreads) head_blend_kernel(HeadParams h, Fa
         const int z = sz, y = sy, x = sx;
         const int64_t oz = t.z0 + z, oy = t.y0 + y, ox = t.x0 + x;
         const int64_t az = oz + h.acc_z_shift;
-        if (oz < h.dz && oy < h.dy && ox < h.dx && az >= 0 && az < h.acc_dz) {
+        const bool crop = h.acc_dy > 0;
+        const int64_t ay = crop ? oy + h.acc_y_shift : oy, ax = crop ? ox + h.acc_x_shift : ox;
+        const int64_t ady = crop ? h.acc_dy : h.dy, adx = crop ? h.acc_dx : h.dx;
+        if (oz < h.dz && oy < h.dy && ox < h.dx && az >= 0 && az < h.acc_dz && ay >= 0 && ay < ady && ax >= 0 &&
+            ax < adx) {
             // (gz*gy)*gx*p in the reference's order (src/ml/infer.hpp:631-653)
             const float wzy = __fmul_rn(__ldg(h.gauss + z), __ldg(h.gauss + y));
             const float c = __fmul_rn(__fmul_rn(wzy, __ldg(h.gauss + x)), p);
-            atomicAdd(h.acc + (az * h.dy + oy) * h.dx + ox, c);
+            atomicAdd(h.acc + (az * ady + ay) * adx + ax, c);
         }
     }
 }
@@ -612,22 +704,35 @@ int grid_for(int64_t n, int threads) {
 }  // namespace
 
 cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
-                             int ntiles, int P, unsigned long long* sums, cudaStream_t s) {
+                             int ntiles, int P, unsigned long long* sums, cudaStream_t s, unsigned* hist) {
+    if (ntiles < 1 || ntiles > 65535) return cudaErrorInvalidValue;
     const int64_t lines = static_cast<int64_t>(P) * P;
     const int gx = grid_for(lines, (kEwThreads / 32) * 4);  // four lines per warp
     count_launch();
-    tile_sums_kernel<<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums);
+    if (hist)
+        tile_sums_kernel<true><<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums, hist);
+    else
+        tile_sums_kernel<false><<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tile_lut(const unsigned long long* sums, const unsigned* hist, int ntiles, int64_t n, int norm,
+                            float* luts, uint8_t* const_flag, cudaStream_t s) {
+    if (ntiles < 1 || norm < 0 || norm > 2 || (norm == 1 && !hist)) return cudaErrorInvalidValue;
+    count_launch();
+    tile_lut_kernel<<<ntiles, 256, 0, s>>>(sums, hist, n, norm, luts, const_flag);
     return cudaGetLastError();
 }
 
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
                              int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
-                             int64_t l0_group_stride, int l0_type, float* f32_out, cudaStream_t s, const uint8_t* tta) {
+                             int64_t l0_group_stride, int l0_type, float* f32_out, cudaStream_t s, const uint8_t* tta,
+                             const float* luts) {
     const int64_t lines = static_cast<int64_t>(P) * P;
     const int gx = grid_for(lines, (kEwThreads / 32) * 2);  // two lines per warp
     count_launch();
-    tile_norm_kernel<<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums, l0, l0_batch_stride,
-                                                             l0_group_stride, l0_type, f32_out, tta);
+    tile_norm_kernel<<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums, luts, l0,
+                                                             l0_batch_stride, l0_group_stride, l0_type, f32_out, tta);
     return cudaGetLastError();
 }
 

@@ -20,13 +20,20 @@ struct TileOrigin {
 
 // ---- tiler ----------------------------------------------------------------------------------
 // Integer sum and sum of squares of every tile's P^3 u8 voxels (edge-clamped reads), into
-// sums[2*b + {0,1}] (exact; the caller zeroes `sums`).
+// sums[2*b + {0,1}] (exact; the caller zeroes `sums`), and with `hist` the count of each u8 level
+// per tile, hist[256*b + v] (caller-zeroed).
 cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
-                             int ntiles, int P, unsigned long long* sums, cudaStream_t s);
-// Writes the first conv's input for every tile: each interior voxel's 16-byte cell holds the
-// z-scored values at x-1, x, x+1 (zero outside the tile) as 16-bit floats, then five zeros. The z-score
-// goes through a 256-entry table built with the reference's double-precision expression, so
-// the normalised value of each u8 level is the same float the reference computes.
+                             int ntiles, int P, unsigned long long* sums, cudaStream_t s, unsigned* hist = nullptr);
+// Per-tile normalisation table of the 256 u8 levels, luts[256*b + v], for norm 0 zscore (from the
+// sums), 1 pct_minmax (from the histogram), 2 unit255 (src/ml/infer.hpp:107-134, 350-385); with
+// const_flag, 1 for each tile whose voxels all hold one value.
+cudaError_t launch_tile_lut(const unsigned long long* sums, const unsigned* hist, int ntiles, int64_t n, int norm,
+                            float* luts, uint8_t* const_flag, cudaStream_t s);
+// Writes the first conv's input for every tile: the normalised values at x-1, x, x+1 (zero outside
+// the tile). Normalisation goes through a 256-entry table per tile: luts[256*b ..] when given
+// (launch_tile_lut), else the z-score table built here from `sums` with the reference's
+// double-precision expression, so the normalised value of each u8 level is the same float the
+// reference computes.
 // `l0_type` is the first conv's operand type (kOpBF16 or kOpF16); l0 (may be null) receives its
 // two input groups, l0_group_stride bytes apart (first_layer_cells: the value as hi + lo terms).
 // tta (one byte per tile, or null): octahedral test-time-augmentation member of each tile; the
@@ -34,7 +41,7 @@ cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
                              int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
                              int64_t l0_group_stride, int l0_type, float* f32_out, cudaStream_t s,
-                             const uint8_t* tta = nullptr);
+                             const uint8_t* tta = nullptr, const float* luts = nullptr);
 
 // Octahedral TTA (src/ml/infer.hpp:346, 393-441): member m of the first N of 48 uses the axis
 // permutation perms[m / 8] and flips the transformed frame's axes in the bits of m % 8 (bit 0 z,
@@ -138,6 +145,9 @@ struct HeadParams {
     // accumulator plane of volume plane z is z + acc_z_shift; planes outside [0, acc_dz) are not
     // written (a sliding window over a longer volume). acc_dz = dz, shift 0: the whole volume.
     int64_t acc_z_shift, acc_dz;
+    // the same along y and x (an output crop): accumulator row y + acc_y_shift of acc_dy rows, column
+    // x + acc_x_shift of acc_dx; acc_dy / acc_dx <= 0 mean the volume's dy / dx with shift 0
+    int64_t acc_y_shift, acc_dy, acc_x_shift, acc_dx;
     float* prob;         // [B][P^3] or null
 };
 cudaError_t launch_head_blend(const HeadParams& h, cudaStream_t s);

@@ -224,7 +224,7 @@ fx_status fx_gaccum_predict_row(fx_gaccum* a, fx_net* net, int64_t zi, const uin
     fxh::Status st = net->net.predict_tiles(a->d_slab, z_hi - z_lo, a->ext[1], a->ext[2], z_lo, a->ext[0], opts->patch,
                                             opts->overlap, opts->channel, opts->sigmoid, opts->batch, zi * per_row,
                                             (zi + 1) * per_row, a->win[a->cur], a->stream, a->wz0, a->win_planes,
-                                            opts->tta);
+                                            opts->tta, fxh::run_opts(opts));
     if (!st.ok()) return abi_error(st.code, st.msg);
     e = cudaStreamSynchronize(a->stream);
     return e == cudaSuccess ? FX_OK : cuda_err(e, "fx_gaccum_predict_row");

@@ -163,6 +163,10 @@ fx_status fx_predict_volume_multi(fx_net* const* nets, int n, const uint8_t* hos
                 if (nets[j] == nets[i]) return fxh::abi_error(FX_INVALID_ARGUMENT, "fx_predict_volume_multi: a net twice");
         }
         if (n == 1) return fx_predict_volume(nets[0], host_vol, dz, dy, dx, o, host_prob, host_u8);
+        const fxh::RunOpts ro = fxh::run_opts(o);
+        if (ro.core_org[0] || ro.core_org[1] || ro.core_org[2] || ro.core_ext[0] > 0 || ro.core_ext[1] > 0 ||
+            ro.core_ext[2] > 0)
+            return fxh::abi_error(FX_UNSUPPORTED, "fx_predict_volume_multi: output crops are taken by fx_predict_volume only");
         const auto plan = fxh::shard_plan(dz, dy, dx, o->patch, o->overlap, n);
         const auto ex = exchanges(plan);
         // peer access between every pair of devices that can reach each other (NVLink / NVSwitch)
@@ -221,7 +225,7 @@ fx_status fx_predict_volume_multi(fx_net* const* nets, int n, const uint8_t* hos
                 cudaMemcpyAsync(d_vol, host_vol + p.z_lo * plane, static_cast<size_t>(nz * plane), cudaMemcpyHostToDevice, s);
                 cudaMemsetAsync(accs[r], 0, static_cast<size_t>(nz * plane) * 4, s);
                 if ((out = net.predict_tiles(d_vol, nz, dy, dx, p.z_lo, dz, P, o->overlap, o->channel, o->sigmoid,
-                                             o->batch, p.tile_begin, p.tile_end, accs[r], s, 0, -1, o->tta))
+                                             o->batch, p.tile_begin, p.tile_end, accs[r], s, 0, -1, o->tta, ro))
                         .code)
                     return;
                 out = net.take_device_status();  // synchronises the stream: this GPU's blend is complete

@@ -656,6 +656,9 @@ Status Net::alloc() {
     }
     nslots_ = std::max(nslots_, 5 * S_);
     d_sums_ = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * 2 * Bmax_));
+    d_hist_ = static_cast<unsigned*>(dalloc(sizeof(unsigned) * 256 * Bmax_));
+    d_luts_ = static_cast<float*>(dalloc(sizeof(float) * 256 * Bmax_));
+    if (!d_hist_ || !d_luts_) return fail(kInternal, "cudaMalloc: normalisation tables");
     d_amax_ = static_cast<unsigned*>(dalloc(sizeof(unsigned) * nslots_));
     d_status_ = static_cast<uint32_t*>(dalloc(sizeof(uint32_t)));
     const int cmax = *std::max_element(F_.begin(), F_.end());
@@ -889,9 +892,17 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
     Status st;
     const ActGeom g0 = level(0);
     if ((st = cuda_status(cudaMemsetAsync(d_sums_, 0, sizeof(unsigned long long) * 2 * nb, s), "memset")).code) return st;
-    if ((st = cuda_status(fxk::launch_tile_sums(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, s), "tile_sums")).code) return st;
+    if (norm_ == 1 && (st = cuda_status(cudaMemsetAsync(d_hist_, 0, sizeof(unsigned) * 256 * nb, s), "memset")).code)
+        return st;
+    if ((st = cuda_status(fxk::launch_tile_sums(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, s, norm_ == 1 ? d_hist_ : nullptr),
+                          "tile_sums"))
+            .code)
+        return st;
+    const int64_t pvox = static_cast<int64_t>(P_) * P_ * P_;
+    if ((st = cuda_status(fxk::launch_tile_lut(d_sums_, d_hist_, nb, pvox, norm_, d_luts_, nullptr, s), "tile_lut")).code)
+        return st;
     if ((st = cuda_status(fxk::launch_tile_norm(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, l0_, 2 * g0.gs(), g0.gs(), t16(), nullptr,
-                                                s, d_tta),
+                                                s, d_tta, d_luts_),
                           "tile_norm"))
             .code)
         return st;
@@ -1129,6 +1140,10 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
                 h.dx = dx;
                 h.acc_z_shift = acc_z_shift;
                 h.acc_dz = acc_dz < 0 ? dz : acc_dz;
+                h.acc_y_shift = acc_y_shift_;
+                h.acc_dy = acc_dy_;
+                h.acc_x_shift = acc_x_shift_;
+                h.acc_dx = acc_dx_;
                 h.prob = prob;
                 if ((st = cuda_status(fxk::launch_head_blend(h, s), "head_blend")).code) return st;
             }
@@ -1458,8 +1473,9 @@ Status Net::workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint
 Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
                           int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
                           int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin, int64_t acc_dz,
-                          int tta) {
+                          int tta, const RunOpts& ro) {
     if (patch != P_) return fail(kInvalid, "predict: patch differs from the net's patch");
+    if (ro.norm < 0 || ro.norm > 2) return fail(kInvalid, "predict: norm must be zscore, pct_minmax or unit255");
     if (batch < 1) batch = 1;
     batch = std::min(batch, Bmax_);
     if (full_dz <= 0) full_dz = dz;
@@ -1469,23 +1485,75 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
     if (tile_end < 0 || tile_end > total) tile_end = total;
     if (tile_begin < 0) tile_begin = 0;
     if (tile_begin >= tile_end) return ok();
+    // the output crop (src/ml/infer.hpp:462-472): origin clamped into the volume, extent to its end
+    const int64_t dims[3] = {full_dz, dy, dx};
+    int64_t co[3], ce[3];
+    bool cropped = false;
+    for (int a = 0; a < 3; ++a) {
+        co[a] = std::clamp<int64_t>(ro.core_org[a], 0, dims[a]);
+        ce[a] = ro.core_ext[a] <= 0 ? dims[a] - co[a] : std::min(ro.core_ext[a], dims[a] - co[a]);
+        cropped |= co[a] != 0 || ce[a] != dims[a];
+    }
     // TTA: every tile once per member (src/ml/infer.hpp:554)
     const int ne = tta <= 1 ? 1 : std::min(tta, fxk::kTtaMaxMembers);
-    std::vector<fxk::TileOrigin> tiles;
-    std::vector<uint8_t> members;
-    tiles.reserve(static_cast<size_t>(tile_end - tile_begin) * ne);
+    std::vector<fxk::TileOrigin> cand;  // slab-local origins of the tiles that run
     for (int64_t i = tile_begin; i < tile_end; ++i) {
         const int64_t xi = i % static_cast<int64_t>(xs.size());
         const int64_t yi = (i / static_cast<int64_t>(xs.size())) % static_cast<int64_t>(ys.size());
         const int64_t zi = i / (static_cast<int64_t>(xs.size()) * ys.size());
-        const int64_t zl = zs[zi] - z_origin;  // slab-local
+        const int64_t z0 = zs[zi], y0 = ys[yi], x0 = xs[xi];
+        // a tile that does not reach the core contributes nothing (src/ml/infer.hpp:532-543)
+        if (cropped && !(z0 < co[0] + ce[0] && z0 + P_ > co[0] && y0 < co[1] + ce[1] && y0 + P_ > co[1] &&
+                         x0 < co[2] + ce[2] && x0 + P_ > co[2]))
+            continue;
+        if (ro.filter && !ro.filter(z0, y0, x0, P_, ro.filter_user)) continue;
+        const int64_t zl = z0 - z_origin;  // slab-local
         if (zl < 0 || (zl + P_ > dz && full_dz >= P_))
             return fail(kInvalid, "predict: tile " + std::to_string(i) + " is outside the z-slab");
+        cand.push_back({zl, y0, x0});
+    }
+    if (ro.skip_constant && !cand.empty()) {
+        // tiles whose input voxels all hold one value are not run (src/ml/inference.cpp:1487-1496,
+        // 1885-1900): exact Σ / Σ² per tile on the device, n Σ² == (Σ)² <=> constant
+        const size_t nc = cand.size();
+        auto* d_org = static_cast<fxk::TileOrigin*>(dalloc(sizeof(fxk::TileOrigin) * nc));
+        auto* d_s = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * 2 * nc));
+        auto* d_lut = static_cast<float*>(dalloc(sizeof(float) * 256 * nc));
+        auto* d_flag = static_cast<uint8_t*>(dalloc(nc));
+        if (!d_org || !d_s || !d_lut || !d_flag) return fail(kInternal, "cudaMalloc: constant-tile check");
+        std::vector<uint8_t> flag(nc, 0);
+        Status st = cuda_status(cudaMemcpyAsync(d_org, cand.data(), sizeof(fxk::TileOrigin) * nc, cudaMemcpyHostToDevice, s),
+                                "H2D tiles");
+        if (st.ok()) st = cuda_status(cudaMemsetAsync(d_s, 0, sizeof(unsigned long long) * 2 * nc, s), "memset");
+        for (size_t i0 = 0; st.ok() && i0 < nc; i0 += 65535) {
+            const int n = static_cast<int>(std::min<size_t>(65535, nc - i0));
+            st = cuda_status(fxk::launch_tile_sums(d_vol, dz, dy, dx, d_org + i0, n, P_, d_s + 2 * i0, s), "tile_sums");
+            if (st.ok())
+                st = cuda_status(fxk::launch_tile_lut(d_s + 2 * i0, nullptr, n, static_cast<int64_t>(P_) * P_ * P_, 2,
+                                                      d_lut + 256 * i0, d_flag + i0, s),
+                                 "tile_lut");
+        }
+        if (st.ok()) st = cuda_status(cudaMemcpyAsync(flag.data(), d_flag, nc, cudaMemcpyDeviceToHost, s), "D2H flags");
+        if (st.ok()) st = cuda_status(cudaStreamSynchronize(s), "constant-tile check");
+        for (void* p : {static_cast<void*>(d_org), static_cast<void*>(d_s), static_cast<void*>(d_lut), static_cast<void*>(d_flag)}) {
+            cudaFree(p);
+            allocs_.erase(std::remove(allocs_.begin(), allocs_.end(), p), allocs_.end());
+        }
+        if (!st.ok()) return st;
+        size_t k = 0;
+        for (size_t i = 0; i < nc; ++i)
+            if (!flag[i]) cand[k++] = cand[i];
+        cand.resize(k);
+    }
+    std::vector<fxk::TileOrigin> tiles;
+    std::vector<uint8_t> members;
+    tiles.reserve(cand.size() * ne);
+    for (const auto& t : cand)
         for (int m = 0; m < ne; ++m) {
-            tiles.push_back({zl, ys[yi], xs[xi]});
+            tiles.push_back(t);
             members.push_back(static_cast<uint8_t>(m));
         }
-    }
+    if (tiles.empty()) return ok();
     if (static_cast<int64_t>(tiles.size()) > d_tiles_cap_) {
         void* p = dalloc(sizeof(fxk::TileOrigin) * tiles.size());
         void* q = dalloc(tiles.size());
@@ -1502,6 +1570,12 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
                                     "H2D tta"))
                       .code)
         return st;
+    // the accumulator window along y and x (the crop) for the head kernel
+    norm_ = ro.norm;
+    acc_y_shift_ = cropped ? -co[1] : 0;
+    acc_dy_ = cropped ? ce[1] : 0;
+    acc_x_shift_ = cropped ? -co[2] : 0;
+    acc_dx_ = cropped ? ce[2] : 0;
     for (size_t i0 = 0; i0 < tiles.size(); i0 += batch) {
         const int nb = static_cast<int>(std::min<size_t>(batch, tiles.size() - i0));
         // accumulator window: acc plane 0 is volume plane acc_z_origin (default: the slab's origin)
@@ -1509,9 +1583,10 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
         if ((st = forward(d_vol, dz, dy, dx, d_tiles_ + i0, nb, channel, sigmoid, d_acc, nullptr, false, s, shift,
                           acc_dz, ne > 1 ? d_tta_ + i0 : nullptr, 1.f / static_cast<float>(ne)))
                 .code)
-            return st;
+            break;
     }
-    return ok();
+    acc_y_shift_ = acc_dy_ = acc_x_shift_ = acc_dx_ = 0;
+    return st;
 }
 
 }  // namespace fxh

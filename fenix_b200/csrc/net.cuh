@@ -119,6 +119,21 @@ struct ResBlock {
     int slot_x = 0, slot_h = 0;       // calibration amax slots of the block input / conv2 input
 };
 
+// Options of one sliding-window call beyond the tile grid (ml::InferOptions fields,
+// src/ml/infer.hpp:38-103): the per-tile normalisation, the output crop, the constant-input tile
+// skip and a caller's tile filter.
+struct RunOpts {
+    int norm = 0;               // 0 zscore, 1 pct_minmax, 2 unit255
+    bool skip_constant = false; // tiles whose input voxels all hold one value are not run
+    int (*filter)(int64_t z0, int64_t y0, int64_t x0, int64_t patch, void* user) = nullptr;
+    void* filter_user = nullptr;
+    // output crop in volume coordinates (core_ext <= 0: to the end of the volume). Tiles that do not
+    // reach the core are not run; the accumulator covers the core along y and x (its z window is
+    // predict_tiles' acc_z_origin / acc_dz).
+    int64_t core_org[3] = {0, 0, 0};
+    int64_t core_ext[3] = {0, 0, 0};
+};
+
 class Net {
   public:
     ~Net();
@@ -143,7 +158,9 @@ class Net {
     Status predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
                          int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
                          int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin = 0,
-                         int64_t acc_dz = -1, int tta = 0);
+                         int64_t acc_dz = -1, int tta = 0, const RunOpts& ro = RunOpts{});
+    // The normalisation forwards use (0 zscore, 1 pct_minmax, 2 unit255); calibration uses it too.
+    void set_norm(int norm) { norm_ = norm; }
     // Device workspace for whole-volume calls: grown on demand, kept for the net's lifetime.
     Status workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint8_t** vol, float** acc, uint8_t** out);
 
@@ -230,6 +247,11 @@ class Net {
     uint8_t* l0_ = nullptr;
     std::vector<uint8_t*> pn_, act_, cat_, ph_;
     unsigned long long* d_sums_ = nullptr;
+    unsigned* d_hist_ = nullptr;  // [Bmax][256] u8 level counts (pct_minmax)
+    float* d_luts_ = nullptr;     // [Bmax][256] per-tile normalisation tables
+    int norm_ = 0;
+    // accumulator window along y and x of the current sliding-window call (acc_dy_ <= 0: the volume)
+    int64_t acc_y_shift_ = 0, acc_dy_ = 0, acc_x_shift_ = 0, acc_dx_ = 0;
     unsigned* d_amax_ = nullptr;  // calibration amax slots
     double* d_stat_work_ = nullptr;  // InstanceNorm slice sums [Bmax][kMaxStatSlices][Cmax][2]
     unsigned* d_stat_done_ = nullptr;  // slice counters [Bmax][Cmax / 32], zero between launches
@@ -256,6 +278,9 @@ struct fx_net {
 };
 
 namespace fxh {
+// fx_infer_opts -> the driver's per-call options, and the output crop box it asks for (capi.cu).
+RunOpts run_opts(const fx_infer_opts* o);
+void crop_box(const fx_infer_opts* o, const int64_t d[3], int64_t co[3], int64_t ce[3]);
 // fx_predict_volume's device part (capi.cu), shared with the .fxvol entry points.
 fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx,
                            const fx_infer_opts* o, float* d_acc, float* d_prob, uint8_t* d_u8);

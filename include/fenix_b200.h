@@ -67,7 +67,15 @@ typedef enum fx_status {
  * whose input channels are not a multiple of 32 use f16. */
 typedef enum fx_precision { FX_PREC_BF16 = 0, FX_PREC_FP8 = 1, FX_PREC_F16 = 2 } fx_precision;
 
-/* Mirrors ml::InferOptions (src/ml/infer.hpp:38-103), the subset this path implements. */
+/* Per-tile normalisation of the u8 input (src/ml/infer.hpp:107-134, 350-385 norm_patch). */
+typedef enum fx_norm { FX_NORM_ZSCORE = 0, FX_NORM_PCT_MINMAX = 1, FX_NORM_UNIT255 = 2 } fx_norm;
+
+/* A caller's tile filter (InferOptions::tile_filter, src/ml/infer.hpp:102): nonzero = run the
+ * tile at (z0, y0, x0) of side `patch` (input coordinates). Called on the calling thread. */
+typedef int (*fx_tile_filter_fn)(int64_t z0, int64_t y0, int64_t x0, int64_t patch, void* user);
+
+/* Mirrors ml::InferOptions (src/ml/infer.hpp:38-103), the fields this path implements. A
+ * zero-initialised struct past `tta` means: zscore, every tile, no crop, no filter. */
 typedef struct fx_infer_opts {
     int patch;      /* tile side P, divisible by 2^(stages-1) */
     double overlap; /* step = (int64)(P * (1 - overlap)) */
@@ -76,6 +84,15 @@ typedef struct fx_infer_opts {
     int batch;      /* tiles per forward, <= the net's max batch */
     int tta;        /* octahedral test-time augmentation: <= 1 off, else the first min(tta, 48)
                        symmetries, averaged (src/ml/infer.hpp:393-441); each costs a forward */
+    int norm;       /* fx_norm */
+    int skip_constant; /* 1: tiles whose input voxels all hold one value are not run, they add nothing
+                          to the blend (predict-scroll's rule, src/ml/inference.cpp:1487-1496, 1885-1900) */
+    int64_t core_org[3]; /* output crop (InferOptions::core_org / core_ext, src/ml/infer.hpp:69-76):
+                            tiles still read the whole input, a tile that does not reach the core is not
+                            run, and the outputs cover only [core_org, core_org + core_ext) */
+    int64_t core_ext[3]; /* <= 0 along an axis: to the end of the input */
+    fx_tile_filter_fn tile_filter; /* NULL: every tile */
+    void* tile_filter_user;
 } fx_infer_opts;
 
 typedef struct fx_net fx_net;
@@ -145,7 +162,8 @@ fx_status fx_net_forward(fx_net* net, const uint8_t* dev_tiles, int nb, float* d
                          void* stream);
 
 /* Sliding-window prediction over a host-resident dense u8 volume [dz][dy][dx] (ZYX, x fastest).
- * Outputs (either may be NULL): the normalised probability (f32) and its u8 encoding. */
+ * Outputs (either may be NULL): the normalised probability (f32) and its u8 encoding, both with the
+ * crop's dims when opts has an output crop (else the input's). */
 fx_status fx_predict_volume(fx_net* net, const uint8_t* host_vol, int64_t dz, int64_t dy, int64_t dx,
                             const fx_infer_opts* opts, float* host_prob, uint8_t* host_u8);
 
@@ -213,6 +231,13 @@ fx_status fx_ipc_close(int device, void* dev_ptr);
 fx_status fx_net_profile(fx_net* net, int enable);
 fx_status fx_net_profile_read(fx_net* net, double* conv_ms, double* conv_flops, double* fp8_flops,
                               int64_t* conv_launches, double* per_launch, int cap);
+/* The dense tcgen05 tensor rate of `device`, measured with this library's own kernel: one CTA per SM
+ * issuing M = 128, N = 256 MMAs back to back on shared-memory-resident operands (kind::f8f6f4 e4m3
+ * for FX_PREC_FP8, kind::f16 for bf16 / f16) into TMEM. `runs` launches of about ms_per_run each:
+ * *best_tflops = the fastest (the burst rate), *mean_tflops (may be NULL) = their mean; a single long
+ * run gives the sustained, power-capped rate. No reference counterpart (the reference measures
+ * none). */
+fx_status fx_tc_peak(int device, int precision, double ms_per_run, int runs, double* best_tflops, double* mean_tflops);
 /* Kernel launches issued by this library since the process started. */
 unsigned long long fx_kernel_launches(void);
 /* Device buffer of 16 u64 cycle counters that conv launches add to when the library is built
@@ -264,6 +289,10 @@ void fx_weight_profile(const float* g, int patch, const int64_t* starts, int64_t
 /* z-score `ntiles` tiles at the given origins of a device u8 volume into f32 [ntiles][P^3]. */
 fx_status fx_norm_tiles(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx, const int64_t* host_origins,
                         int ntiles, int patch, float* dev_out, void* stream);
+/* fx_norm_tiles with any of the reference's patch normalisations (fx_norm: zscore, pct_minmax,
+ * unit255; src/ml/infer.hpp:107-134, 350-385): the dense u8 filler + detail::norm_patch. */
+fx_status fx_norm_tiles_mode(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx, const int64_t* host_origins,
+                             int ntiles, int patch, int norm, float* dev_out, void* stream);
 /* fx_norm_tiles without any device allocation. No reference counterpart: the reference
  * allocates its patch buffers per call. This one keeps its scratch (tile origins and the
  * per-tile exact sums) in a static 160 KiB __device__ array, so it serves callers that must not

@@ -12,18 +12,23 @@
 //   - the predict-surface stage argument grammar (src/ml/inference.cpp:369-420),
 //   - ml::GlobalAccum, the global-grid accumulator with its z-sweep finalize and resume floor
 //     (src/ml/global_accum.hpp:37-198), kept on the device.
+//   - ml::predict_surface_filled with a caller's filler (src/ml/infer.hpp:452-458),
+//   - InferOptions' normalisations (zscore / pct_minmax / unit255), output core crop and tile filter
+//     (src/ml/infer.hpp:38-134, 462-472, 532-543),
 // Every computation runs on the GPU through the extern "C" ABI of fenix_b200.h. Options the device
-// path does not implement (non-zscore normalisation, core crops, multi-scale, rotation / noise /
-// offset TTA, checkpoints, tile filters) return Errc::unsupported; there is no CPU fallback.
+// path does not implement (multi-scale, rotation / noise / offset TTA, checkpoints) return
+// Errc::unsupported; there is no CPU fallback.
 #pragma once
 
 #include "fenix_b200.h"
+#include "fenix_b200/ml/tiling.hpp"
 
 #include <algorithm>
 #include <charconv>
 #include <cstdint>
 #include <cstring>
 #include <expected>
+#include <functional>
 #include <memory>
 #include <mutex>
 #include <span>
@@ -134,20 +139,70 @@ struct InferOptions {
     bool sigmoid = false;  // 1-class head -> sigmoid
     Norm norm = Norm::zscore;
     int tta = 0;  // <= 1: off; else the first min(tta, 48) octahedral symmetries, averaged
+    // Output crop: the returned volume covers only [core_org, core_org + core_ext) of the input;
+    // tiles still read the whole input, a tile that does not reach the core is not run. A negative
+    // extent component = to the end of the input (the default: no crop).
     Index3 core_org{0, 0, 0};
-    Extent3 core_ext{-1, -1, -1};  // whole input
+    Extent3 core_ext{-1, -1, -1};
     int batch = 3;                 // tiles per forward
+    // A tile (origin z0, y0, x0, side patch) runs only if this returns true (src/ml/infer.hpp:102);
+    // called on the calling thread while the tile list is built. Empty = every tile.
+    std::function<bool(s64 z0, s64 y0, s64 x0, s64 patch)> tile_filter{};
+    // Tiles whose input voxels all hold one value are not run (they add nothing to the blend) —
+    // predict-scroll's constant-input filter (src/ml/inference.cpp:1487-1496, 1885-1900), evaluated
+    // on the device.
+    bool skip_constant = false;
 };
 
-// The options as the ABI struct, or unsupported/invalid_argument for what this path lacks.
+namespace detail {
+inline int tile_filter_trampoline(int64_t z0, int64_t y0, int64_t x0, int64_t p, void* user) {
+    const auto* f = static_cast<const std::function<bool(s64, s64, s64, s64)>*>(user);
+    try {
+        return (*f)(z0, y0, x0, p) ? 1 : 0;
+    } catch (...) {
+        return 1;  // a filter that fails keeps its tile
+    }
+}
+}  // namespace detail
+
+// The options as the ABI struct, or invalid_argument for what cannot hold. The struct refers to
+// o.tile_filter: keep `o` alive while it is in use.
 [[nodiscard]] inline Expected<fx_infer_opts> to_fx(const InferOptions& o) {
-    if (o.norm != Norm::zscore) return err(Errc::unsupported, "InferOptions: only zscore normalisation is implemented");
-    if (o.core_ext.z >= 0 || o.core_ext.y >= 0 || o.core_ext.x >= 0)
-        return err(Errc::unsupported, "InferOptions: core crops are not implemented on the B200 path");
     if (o.patch < 1 || o.batch < 1 || !(o.overlap >= 0.0 && o.overlap < 1.0))
         return err(Errc::invalid_argument, "InferOptions: bad patch, batch or overlap");
     if (o.channel < 0 || o.channel > 1) return err(Errc::invalid_argument, "InferOptions: channel must be 0 or 1");
-    return fx_infer_opts{o.patch, o.overlap, o.channel, o.sigmoid ? 1 : 0, o.batch, o.tta};
+    fx_infer_opts f{};
+    f.patch = o.patch;
+    f.overlap = o.overlap;
+    f.channel = o.channel;
+    f.sigmoid = o.sigmoid ? 1 : 0;
+    f.batch = o.batch;
+    f.tta = o.tta;
+    f.norm = o.norm == Norm::pct_minmax ? FX_NORM_PCT_MINMAX : (o.norm == Norm::unit255 ? FX_NORM_UNIT255 : FX_NORM_ZSCORE);
+    f.skip_constant = o.skip_constant ? 1 : 0;
+    f.core_org[0] = o.core_org.z;
+    f.core_org[1] = o.core_org.y;
+    f.core_org[2] = o.core_org.x;
+    if (o.core_ext.z == 0 || o.core_ext.y == 0 || o.core_ext.x == 0)
+        return err(Errc::invalid_argument, "InferOptions: an empty output crop");
+    // "to the end" is a negative component here and a non-positive one in the ABI
+    f.core_ext[0] = std::max<s64>(o.core_ext.z, 0);
+    f.core_ext[1] = std::max<s64>(o.core_ext.y, 0);
+    f.core_ext[2] = std::max<s64>(o.core_ext.x, 0);
+    if (o.tile_filter) {
+        f.tile_filter = &detail::tile_filter_trampoline;
+        f.tile_filter_user = const_cast<std::function<bool(s64, s64, s64, s64)>*>(&o.tile_filter);
+    }
+    return f;
+}
+
+// The output dims of a prediction over an input of dims d with opt's crop (src/ml/infer.hpp:462-472).
+[[nodiscard]] inline Extent3 output_dims(Extent3 d, const InferOptions& o) {
+    auto ax = [](s64 org, s64 ext, s64 n) {
+        const s64 c = std::clamp<s64>(org, 0, n);
+        return ext < 0 ? n - c : std::min(ext, n - c);
+    };
+    return {ax(o.core_org.z, o.core_ext.z, d.z), ax(o.core_org.y, o.core_ext.y, d.y), ax(o.core_org.x, o.core_ext.x, d.x)};
 }
 
 // One net on one device (the operator concept of the reference's TrtNet / AotiNet).
@@ -240,7 +295,7 @@ inline Expected<void> run(VolumeView<const u8> in, B200Net& net, const InferOpti
 // normalise by the factorised weight (same dims as the input).
 [[nodiscard]] inline Expected<Volume<f32>> predict_surface(VolumeView<const u8> in, B200Net& net,
                                                            const InferOptions& opt = {}) {
-    Volume<f32> out(in.dims());
+    Volume<f32> out(output_dims(in.dims(), opt));
     if (auto r = detail::run(in, net, opt, out.data(), nullptr); !r) return std::unexpected(r.error());
     return out;
 }
@@ -248,9 +303,41 @@ inline Expected<void> run(VolumeView<const u8> in, B200Net& net, const InferOpti
 // The same, encoded (u8)(clamp(p, 0, 1) * 255 + 0.5).
 [[nodiscard]] inline Expected<Volume<u8>> predict_surface_u8(VolumeView<const u8> in, B200Net& net,
                                                              const InferOptions& opt = {}) {
-    Volume<u8> out(in.dims());
+    Volume<u8> out(output_dims(in.dims(), opt));
     if (auto r = detail::run(in, net, opt, nullptr, out.data()); !r) return std::unexpected(r.error());
     return out;
+}
+
+// predict_surface_filled (src/ml/infer.hpp:452-458): the input comes from a caller's filler,
+// fill(z0, y0, x0, P, float* out) writing the P^3 patch at that origin (out of the volume it must
+// clamp, as the reference's fillers do). The device path normalises u8 levels exactly, so every
+// filled value must be an integer in [0, 255] (the reference's u8 sources); anything else is
+// Errc::unsupported. The patches are gathered into a dense u8 volume of dims d on the host, which
+// is then predicted on the device like predict_surface.
+template <class Filler>
+[[nodiscard]] inline Expected<Volume<f32>> predict_surface_filled(Extent3 d, Filler&& fill, B200Net& net,
+                                                                  const InferOptions& opt = {}) {
+    if (opt.patch % 64 != 0) return err(Errc::invalid_argument, "patch must be divisible by 64");
+    if (d.z < 1 || d.y < 1 || d.x < 1) return err(Errc::invalid_argument, "predict_surface_filled: empty volume");
+    const int P = opt.patch;
+    Volume<u8> vol(d);
+    std::vector<float> patch(static_cast<std::size_t>(P) * P * P);
+    const std::vector<s64> zs = fenix::ml::tile_starts(d.z, P, opt.overlap), ys = fenix::ml::tile_starts(d.y, P, opt.overlap),
+                           xs = fenix::ml::tile_starts(d.x, P, opt.overlap);
+    for (s64 z0 : zs)
+        for (s64 y0 : ys)
+            for (s64 x0 : xs) {
+                fill(z0, y0, x0, P, patch.data());
+                for (s64 z = 0; z < P && z0 + z < d.z; ++z)
+                    for (s64 y = 0; y < P && y0 + y < d.y; ++y)
+                        for (s64 x = 0; x < P && x0 + x < d.x; ++x) {
+                            const float v = patch[static_cast<std::size_t>((z * P + y) * P + x)];
+                            if (!(v >= 0.0f && v <= 255.0f) || v != static_cast<float>(static_cast<int>(v)))
+                                return err(Errc::unsupported, "predict_surface_filled: filled values must be u8 levels");
+                            vol.view()(z0 + z, y0 + y, x0 + x) = static_cast<u8>(v);
+                        }
+            }
+    return predict_surface(static_cast<const Volume<u8>&>(vol).view(), net, opt);
 }
 
 // One resident u8 window -> u8 sheet probability, same dims: patch 128, overlap 0.25, f16,

@@ -153,9 +153,10 @@ def prob_to_u8(p):
     return out
 
 
-def ref_infer(weights, vol, P, overlap, batch=1, threads=None, out_path=None):
-    """Run the reference's own CPU predict_surface_filled (oracle/_ref/ref_infer). Returns
-    (prob or None, info dict)."""
+def ref_infer(weights, vol, P, overlap, batch=1, threads=None, out_path=None, **opts):
+    """Run the reference's own CPU predict_surface_filled (oracle/_ref/ref_infer). opts become its
+    key=value options (tta, norm, channel, sigmoid, core=(z, y, x, dz, dy, dx), skipconst). Returns
+    (prob, info dict); prob has the output's dims (the core's when cropped)."""
     import json
     import tempfile
 
@@ -170,9 +171,11 @@ def ref_infer(weights, vol, P, overlap, batch=1, threads=None, out_path=None):
         cmd = [str(exe), str(weights), str(vp), *map(str, v.shape), str(P), str(overlap), str(batch), str(op)]
         if threads:
             cmd.append(str(threads))
+        for k, val in opts.items():
+            cmd.append(f"{k}={','.join(map(str, val)) if isinstance(val, (tuple, list)) else val}")
         r = subprocess.run(cmd, capture_output=True, text=True, check=True)
         info = json.loads(r.stdout.strip().splitlines()[-1])
-        prob = np.fromfile(op, dtype=np.float32).reshape(v.shape)
+        prob = np.fromfile(op, dtype=np.float32).reshape(tuple(info.get("dims", v.shape)))
     return prob, info
 
 

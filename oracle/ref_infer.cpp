@@ -12,8 +12,12 @@
 // CPU), fed by a dense u8 filler with edge clamp as run_predict_core uses
 // (src/ml/inference.cpp:309-321).
 //
-// usage: ref_infer <w.fxweights> <vol.u8> dz dy dx patch overlap batch <out.f32|-> [threads]
-// prints one JSON line: {"seconds": ..., "threads": ..., "tiles": ...}
+// usage: ref_infer <w.fxweights> <vol.u8> dz dy dx patch overlap batch <out.f32|-> [threads] [key=value ...]
+//   keys (InferOptions fields, src/ml/infer.hpp:38-103): tta=N, norm=zscore|pct_minmax|unit255,
+//   channel=N, sigmoid=0|1, core=z,y,x,dz,dy,dx (output crop), skipconst=1 (the constant-input tile
+//   filter of predict-scroll's region mode, src/ml/inference.cpp:1885-1900)
+// prints one JSON line: {"seconds": ..., "threads": ..., "tiles": ..., "dims": [z, y, x]} and writes the
+// f32 probability volume (the core's dims when cropped).
 #include "ml/infer.hpp"
 #include "ml/weights.hpp"
 
@@ -100,7 +104,7 @@ TORCH_MODULE(Plain);
 
 // Run the reference's predict_surface_filled with `net` on the volume file and write the result.
 template <class Net>
-int run(Net& net, char** argv, Extent3 d, const std::string& vpath, const std::string& opath) {
+int run(Net& net, int argc, char** argv, Extent3 d, const std::string& vpath, const std::string& opath) {
     Volume<u8> vol(d);
     {
         std::FILE* fp = std::fopen(vpath.c_str(), "rb");
@@ -116,6 +120,33 @@ int run(Net& net, char** argv, Extent3 d, const std::string& vpath, const std::s
     opt.batch = std::atoi(argv[8]);
     opt.half = false;  // fp32 on the CPU
     const VolumeView<const u8> uv = vol.view();
+    for (int i = 10; i < argc; ++i) {
+        const std::string a = argv[i];
+        const auto eq = a.find('=');
+        if (eq == std::string::npos) continue;  // the positional thread count
+        const std::string k = a.substr(0, eq), v = a.substr(eq + 1);
+        if (k == "tta") opt.tta = std::atoi(v.c_str());
+        else if (k == "channel") opt.channel = std::atoi(v.c_str());
+        else if (k == "sigmoid") opt.sigmoid = std::atoi(v.c_str()) != 0;
+        else if (k == "norm") opt.norm = v == "pct_minmax" ? ml::Norm::pct_minmax : (v == "unit255" ? ml::Norm::unit255 : ml::Norm::zscore);
+        else if (k == "core") {
+            long long c[6] = {0, 0, 0, -1, -1, -1};
+            std::sscanf(v.c_str(), "%lld,%lld,%lld,%lld,%lld,%lld", &c[0], &c[1], &c[2], &c[3], &c[4], &c[5]);
+            opt.core_org = {c[0], c[1], c[2]};
+            opt.core_ext = {c[3], c[4], c[5]};
+        } else if (k == "skipconst" && v == "1") {
+            opt.tile_filter = [uv](s64 z0, s64 y0, s64 x0, s64 P) {
+                const Extent3 dd = uv.dims();
+                const s64 z1 = std::min(dd.z, z0 + P), y1 = std::min(dd.y, y0 + P), x1 = std::min(dd.x, x0 + P);
+                const u8 first = uv(std::min(z0, dd.z - 1), std::min(y0, dd.y - 1), std::min(x0, dd.x - 1));
+                for (s64 z = z0; z < z1; ++z)
+                    for (s64 y = y0; y < y1; ++y)
+                        for (s64 x = x0; x < x1; ++x)
+                            if (uv(z, y, x) != first) return true;
+                return false;
+            };
+        }
+    }
     const auto t0 = std::chrono::steady_clock::now();
     auto prob = ml::predict_surface_filled(
         d,
@@ -133,16 +164,19 @@ int run(Net& net, char** argv, Extent3 d, const std::string& vpath, const std::s
         std::fprintf(stderr, "predict: %s\n", prob.error().message.c_str());
         return 1;
     }
+    const Extent3 od = prob->dims();
     if (opath != "-") {
         std::FILE* fp = std::fopen(opath.c_str(), "wb");
         if (!fp) return 1;
-        std::fwrite(prob->data(), sizeof(float), static_cast<size_t>(d.count()), fp);
+        std::fwrite(prob->data(), sizeof(float), static_cast<size_t>(od.count()), fp);
         std::fclose(fp);
     }
     const long tiles = static_cast<long>(ml::tile_starts(d.z, opt.patch, opt.overlap).size() *
                                          ml::tile_starts(d.y, opt.patch, opt.overlap).size() *
                                          ml::tile_starts(d.x, opt.patch, opt.overlap).size());
-    std::printf("{\"seconds\": %.6f, \"threads\": %d, \"tiles\": %ld}\n", dt, torch::get_num_threads(), tiles);
+    std::printf("{\"seconds\": %.6f, \"threads\": %d, \"tiles\": %ld, \"dims\": [%lld, %lld, %lld]}\n", dt,
+                torch::get_num_threads(), tiles, static_cast<long long>(od.z), static_cast<long long>(od.y),
+                static_cast<long long>(od.x));
     return 0;
 }
 
@@ -153,7 +187,7 @@ int main(int argc, char** argv) {
     }
     const std::string wpath = argv[1], vpath = argv[2], opath = argv[9];
     const Extent3 d{std::atoll(argv[3]), std::atoll(argv[4]), std::atoll(argv[5])};
-    if (argc > 10) torch::set_num_threads(std::atoi(argv[10]));
+    if (argc > 10 && std::string(argv[10]).find('=') == std::string::npos) torch::set_num_threads(std::atoi(argv[10]));
     auto wm = ml::load_fxweights(wpath);
     if (!wm) {
         std::fprintf(stderr, "load_fxweights: %s\n", wm.error().message.c_str());
@@ -188,7 +222,7 @@ int main(int argc, char** argv) {
             std::fprintf(stderr, "weights missing %s\n", miss[0].c_str());
             return 1;
         }
-        return run(rnet, argv, d, vpath, opath);
+        return run(rnet, argc, argv, d, vpath, opath);
     }
     std::vector<int> f;
     int nconv = 0;
@@ -207,5 +241,5 @@ int main(int argc, char** argv) {
         std::fprintf(stderr, "weights missing %s\n", missing[0].c_str());
         return 1;
     }
-    return run(net, argv, d, vpath, opath);
+    return run(net, argc, argv, d, vpath, opath);
 }

@@ -4,11 +4,16 @@
 //                                         synthetic window; writes both outputs to <out>
 //   host_api_test fxvol <in> <out>      — codec::VolumeArchive: open an archive, check its metadata
 //                                         and rewrite every chunk payload of every LOD to <out>
+//   host_api_test stages <weights> <dir> — the predict-surface / predict-scroll stages through the
+//                                         registry on an archive written in <dir>, against
+//                                         predict_surface_u8; predict_surface_filled, crops, filters
 #include "fenix_b200/codec/archive.hpp"
 #include "fenix_b200/ml/infer.hpp"
+#include "fenix_b200/ml/ml_api.hpp"
 #include "fenix_b200/ml/tiling.hpp"
 #include "fenix_b200_synth.h"
 
+#include <cmath>
 #include <cstdio>
 #include <fstream>
 #include <vector>
@@ -52,10 +57,22 @@ static int cpu() {
     {
         ml::InferOptions o;
         o.norm = ml::Norm::pct_minmax;
-        CHECK(ml::to_fx(o).error().code == Errc::unsupported);
+        CHECK(ml::to_fx(o) && ml::to_fx(o)->norm == FX_NORM_PCT_MINMAX);
         o = {};
-        o.core_ext = {64, 64, 64};
-        CHECK(ml::to_fx(o).error().code == Errc::unsupported);
+        o.core_org = {8, 0, 4};
+        o.core_ext = {64, -1, 32};
+        auto c = ml::to_fx(o);
+        CHECK(c && c->core_org[0] == 8 && c->core_org[2] == 4 && c->core_ext[0] == 64 && c->core_ext[1] == 0 &&
+              c->core_ext[2] == 32);
+        CHECK(ml::output_dims({100, 90, 80}, o) == (Extent3{64, 90, 32}));
+        o.core_ext = {0, -1, -1};
+        CHECK(ml::to_fx(o).error().code == Errc::invalid_argument);
+        o = {};
+        int seen = 0;
+        o.tile_filter = [&](s64 z0, s64, s64, s64 P) { return ++seen, z0 + P > 100; };
+        auto fo = ml::to_fx(o);
+        CHECK(fo && fo->tile_filter && fo->tile_filter(64, 0, 0, 64, fo->tile_filter_user) == 1 &&
+              fo->tile_filter(0, 0, 0, 64, fo->tile_filter_user) == 0 && seen == 2);
         o = {};
         o.overlap = 1.0;
         CHECK(ml::to_fx(o).error().code == Errc::invalid_argument);
@@ -89,6 +106,162 @@ static int cpu() {
     {  // the grid origin must be 64-aligned (checked before any device work)
         auto g = ml::GlobalAccum::create({32, 0, 0}, {128, 64, 64}, 64, 0.5);
         CHECK(!g && g.error().code == Errc::invalid_argument);
+    }
+    {  // the stage registry (src/core/core.hpp:68-108) holds the ML stages, idempotent by name
+        CHECK(find_stage("predict-surface") && find_stage("predict-scroll") && find_stage("predict-ink"));
+        CHECK(!find_stage("no-such-stage"));
+        const std::size_t n = registry().size();
+        register_stage(Stage{"predict-surface", "again", nullptr});
+        CHECK(registry().size() == n);
+        Context ctx;
+        std::vector<std::string_view> a{"x"};
+        auto r = find_stage("predict-ink")->run(a, ctx);
+        CHECK(!r && r.error().code == Errc::unsupported);
+        std::vector<std::string_view> z{"s3://bucket/scroll.zarr", "0", "w.fxweights", "out.fxvol"};
+        r = find_stage("predict-scroll")->run(z, ctx);
+        CHECK(!r && r.error().code == Errc::unsupported);
+        std::vector<std::string_view> b{"ct.fxvol", "0", "w.fxweights", "out.fxvol", "bogus=1"};
+        r = find_stage("predict-scroll")->run(b, ctx);
+        CHECK(!r && r.error().code == Errc::invalid_argument);
+        std::vector<std::string_view> m{"ct.fxvol", "0", "w.fxweights", "out.fxvol", "mode=region"};
+        r = find_stage("predict-scroll")->run(m, ctx);
+        CHECK(!r && r.error().code == Errc::unsupported);
+        std::vector<std::string_view> u{"ct.fxvol"};
+        r = find_stage("predict-surface")->run(u, ctx);
+        CHECK(!r && r.error().code == Errc::invalid_argument);
+    }
+    std::printf("%s\n", fails ? "FAIL" : "ok");
+    return fails ? 1 : 0;
+}
+
+// The stages over archives against the in-memory API on the same volume and net.
+static int stages(const char* weights, const char* dir) {
+    const Extent3 d{160, 96, 120};
+    std::vector<u8> vol(static_cast<std::size_t>(d.count()));
+    fx_spiral_params sp{12.0, 3.0, 170.0, 15.0, 40.0, 10.0, 1.0, 0.0};
+    if (fx_synth_spiral(vol.data(), d.z, d.y, d.x, &sp, 9, 0, d.z) != 0) return 2;
+    VolumeView<const u8> in(vol.data(), d);
+    const std::string ip = std::string(dir) + "/in.fxvol", op = std::string(dir) + "/surf.fxvol",
+                      sp2 = std::string(dir) + "/scroll.fxvol";
+    {
+        auto a = codec::VolumeArchive::create(ip, d, {8.0f});
+        if (!a || !a->write_volume(in) || !a->close()) return 3;
+    }
+    auto src = codec::VolumeArchive::open(ip);
+    if (!src) return 4;
+    auto dec = src->read_volume_u8();  // what the stages see (the codec is lossy)
+    if (!dec) return 5;
+    const VolumeView<const u8> dv = static_cast<const Volume<u8>&>(*dec).view();
+    Context ctx;
+    {  // predict-surface: patch 64, overlap 0.5, no tta, batch 2
+        std::vector<std::string_view> a{ip, weights, op, "64", "0.5", "0", "2"};
+        auto r = find_stage("predict-surface")->run(a, ctx);
+        if (!r) {
+            std::fprintf(stderr, "predict-surface: %s\n", r.error().message.c_str());
+            return 6;
+        }
+    }
+    auto net = ml::B200Net::load(weights, 64, 2);
+    if (!net) return 7;
+    ml::InferOptions o;
+    o.patch = 64;
+    o.overlap = 0.5;
+    o.batch = 2;
+    auto want = ml::predict_surface_u8(dv, *net, o);
+    if (!want) return 8;
+    auto q32 = [&](const Volume<u8>& v) {  // what a q = 32 archive of v decodes to
+        const std::string t = std::string(dir) + "/tmp.fxvol";
+        auto a = codec::VolumeArchive::create(t, v.dims(), {32.0f});
+        if (!a || !a->write_volume(v.view()) || !a->close()) return Volume<u8>{};
+        auto b = codec::VolumeArchive::open(t);
+        auto r = b ? b->read_volume_u8() : Expected<Volume<u8>>(std::unexpected(Error{}));
+        return r ? std::move(*r) : Volume<u8>{};
+    };
+    auto got = codec::VolumeArchive::open(op);
+    auto gv = got ? got->read_volume_u8() : Expected<Volume<u8>>(std::unexpected(Error{}));
+    const Volume<u8> wq = q32(*want);
+    CHECK(gv && wq.data() && std::memcmp(gv->data(), wq.data(), vol.size()) == 0);
+    {  // predict-scroll over the same archive, global grid, no tta: the same tiles and blend
+        std::vector<std::string_view> a{ip, "0", weights, sp2, "tta=0", "batch=2", "patch=64", "overlap=0.5"};
+        auto r = find_stage("predict-scroll")->run(a, ctx);
+        if (!r) {
+            std::fprintf(stderr, "predict-scroll: %s\n", r.error().message.c_str());
+            return 9;
+        }
+        auto s2 = codec::VolumeArchive::open(sp2);
+        auto sv = s2 ? s2->read_volume_u8() : Expected<Volume<u8>>(std::unexpected(Error{}));
+        CHECK(sv.has_value());
+        if (sv) {
+            // predict-scroll writes each finalised chunk with the voxels past the volume at 0 (the
+            // GlobalAccum sink), predict-surface's write_volume replicates the edge: encode the
+            // in-memory prediction's chunks the scroll's way and compare the decoded results
+            const s64 T = 64, ncz = (d.z + T - 1) / T, ncy = (d.y + T - 1) / T, ncx = (d.x + T - 1) / T;
+            const std::size_t n = static_cast<std::size_t>(ncz * ncy * ncx), cv = static_cast<std::size_t>(T * T * T);
+            std::vector<u8> ch(n * cv, 0), enc(n * (cv + 4096)), dec(n * cv);
+            std::vector<uint64_t> offs(n);
+            std::vector<uint32_t> lens(n);
+            for (s64 k = 0; k < static_cast<s64>(n); ++k) {
+                const s64 cz = k / (ncy * ncx), cy = (k / ncx) % ncy, cx = k % ncx;
+                for (s64 z = 0; z < T && cz * T + z < d.z; ++z)
+                    for (s64 y = 0; y < T && cy * T + y < d.y; ++y)
+                        for (s64 x = 0; x < T && cx * T + x < d.x; ++x)
+                            ch[k * cv + (z * T + y) * T + x] = want->data()[((cz * T + z) * d.y + cy * T + y) * d.x + cx * T + x];
+            }
+            CHECK(fx_fxvol_encode_tiles(ch.data(), nullptr, static_cast<int64_t>(n), 32.0f, 0.65f, 0.80f, 0, enc.data(), enc.size(),
+                                        offs.data(), lens.data()) == FX_OK);
+            CHECK(fx_fxvol_decode_tiles(enc.data(), enc.size(), offs.data(), lens.data(), static_cast<int64_t>(n), 32.0f,
+                                        0.65f, 0.80f, 0, dec.data(), nullptr) == FX_OK);
+            std::size_t far = 0;
+            double sum = 0;
+            for (s64 z = 0; z < d.z; ++z)
+                for (s64 y = 0; y < d.y; ++y)
+                    for (s64 x = 0; x < d.x; ++x) {
+                        const s64 k = ((z / T) * ncy + y / T) * ncx + x / T;
+                        const int w0 = dec[k * cv + ((z % T) * T + y % T) * T + x % T];
+                        const int dd = std::abs(int(sv->data()[(z * d.y + y) * d.x + x]) - w0);
+                        sum += dd;
+                        far += dd > 8;
+                    }
+            std::fprintf(stderr, "predict-scroll vs predict_surface (decoded q32): mean |d| %.4f, %zu voxels > 8\n",
+                         sum / static_cast<double>(vol.size()), far);
+            CHECK(sum / static_cast<double>(vol.size()) <= 0.25 && far * 1000 <= vol.size());
+        }
+    }
+    {  // predict_surface_filled with a clamped filler = predict_surface on the dense view
+        auto f = ml::predict_surface_filled(
+            d,
+            [&](s64 z0, s64 y0, s64 x0, int P, float* out) {
+                for (s64 z = 0; z < P; ++z)
+                    for (s64 y = 0; y < P; ++y)
+                        for (s64 x = 0; x < P; ++x)
+                            out[(z * P + y) * P + x] = in(std::min(z0 + z, d.z - 1), std::min(y0 + y, d.y - 1), std::min(x0 + x, d.x - 1));
+            },
+            *net, o);
+        auto p = ml::predict_surface(in, *net, o);
+        CHECK(f && p);
+        if (f && p) {
+            float worst = 0;
+            for (std::size_t i = 0; i < vol.size(); ++i) worst = std::max(worst, std::fabs(f->data()[i] - p->data()[i]));
+            CHECK(worst <= 1e-5f);
+        }
+        auto bad = ml::predict_surface_filled(d, [](s64, s64, s64, int P, float* out) { std::fill(out, out + P * P * P, 0.5f); }, *net, o);
+        CHECK(!bad && bad.error().code == Errc::unsupported);
+    }
+    {  // output crop + tile filter through the header: the crop's dims, filtered tiles add nothing
+        ml::InferOptions c = o;
+        c.core_org = {32, 16, 8};
+        c.core_ext = {64, 48, -1};
+        auto p = ml::predict_surface(in, *net, c);
+        CHECK(p && p->dims() == (Extent3{64, 48, 112}));
+        ml::InferOptions t = o;
+        t.tile_filter = [](s64 z0, s64, s64, s64) { return z0 >= 64; };
+        auto q = ml::predict_surface(in, *net, t);
+        CHECK(q.has_value());
+        if (q) {  // planes below 32 are covered only by tiles starting at z 0: all zero
+            bool zero = true;
+            for (s64 i = 0; i < 32 * d.y * d.x; ++i) zero &= q->data()[i] == 0.0f;
+            CHECK(zero);
+        }
     }
     std::printf("%s\n", fails ? "FAIL" : "ok");
     return fails ? 1 : 0;
@@ -190,6 +363,7 @@ int main(int argc, char** argv) {
     if (argc >= 2 && std::string_view(argv[1]) == "cpu") return cpu();
     if (argc >= 4 && std::string_view(argv[1]) == "fxvol") return fxvol(argv[2], argv[3]);
     if (argc >= 4 && std::string_view(argv[1]) == "gpu") return gpu(argv[2], argv[3]);
+    if (argc >= 4 && std::string_view(argv[1]) == "stages") return stages(argv[2], argv[3]);
     std::fprintf(stderr, "usage: host_api_test cpu | gpu <weights> <out> | fxvol <in> <out>\n");
     return 2;
 }

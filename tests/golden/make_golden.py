@@ -15,6 +15,10 @@ Runs only where the reference tree is present (it compiles oracle/_ref from it):
                       config 3 (the central 192^3 crop [416, 608)^3 of the 1024^3 seed-2 speckled
                       volume: 8 tiles at overlap 0.5, so the middle third of every axis is a
                       blend of two tiles; the benchmark's weight seed 1).
+  * feat_<case>.npz — InferOptions features through the reference's own predict_surface_filled on small
+                      volumes (full maps as u16): octahedral TTA (tta_infer_dev), pct_minmax and
+                      unit255 normalisation (norm_patch), the output core crop, the constant-input
+                      tile filter of predict-scroll, and a one-class sigmoid head.
   * resenc_<case>.npz — the same with the reference's own nets::ResEncUNet (residual encoder,
                       optional scSE, plain or task naming) loaded from seeded random-init weights.
   * fxvol_tiles.npz — the reference's encode_tile_dct payloads of the 64^3 chunks of
@@ -69,6 +73,28 @@ def volume128(name):
         return fx.synth_spiral(full, vseed, sp)
     slab = fx.synth_spiral(full, vseed, sp, org[0], org[0] + ext[0])
     return np.ascontiguousarray(slab[:, org[1]:org[1] + ext[1], org[2]:org[2] + ext[2]])
+
+
+# name: (features, ncls, weight seed, volume shape, volume seed, patch, overlap, reference options)
+FEATS = {
+    "tta8": ((16, 32, 64, 128), 2, 3, (96, 80, 72), 21, 64, 0.5, {"tta": 8}),
+    "tta48": ((16, 32, 64), 2, 4, (64, 64, 64), 22, 64, 0.5, {"tta": 48}),
+    "pct": ((16, 32, 64, 128), 2, 5, (96, 80, 72), 23, 64, 0.5, {"norm": "pct_minmax"}),
+    "unit255": ((16, 32, 64, 128), 2, 6, (96, 80, 72), 24, 64, 0.5, {"norm": "unit255"}),
+    "core": ((16, 32, 64, 128), 2, 7, (96, 80, 72), 25, 64, 0.5, {"core": (16, 8, 4, 48, 40, 44)}),
+    "skipconst": ((16, 32, 64, 128), 2, 8, (128, 64, 96), 26, 64, 0.5, {"skipconst": 1}),
+    "sigmoid": ((16, 32, 64, 128), 1, 9, (96, 80, 72), 27, 64, 0.5, {"sigmoid": 1}),
+}
+
+
+def feat_volume(name):
+    """The input volume of a feat case: the spiral synthetic (planes [0, 72) held at one value for
+    the constant-tile case)."""
+    feats, ncls, wseed, shape, vseed, P, ov, ropt = FEATS[name]
+    vol = fx.synth_spiral(shape, vseed, fx.SPIRAL_CONFIG1)
+    if name == "skipconst":
+        vol[:72] = 40
+    return vol
 
 
 # name: (features, blocks, scSE, plain naming, weight seed, volume shape, volume seed, patch, overlap)
@@ -147,6 +173,22 @@ def net128_case(name):
         ref_threads=np.int64(info["threads"]),
     )
     print(f"net128_{name}.npz: shape {vol.shape}, {info}")
+
+
+def feat_case(name):
+    feats, ncls, wseed, shape, vseed, P, ov, ropt = FEATS[name]
+    vol = feat_volume(name)
+    with tempfile.TemporaryDirectory() as td:
+        w = make_plain_unet(Path(td) / "w.fxweights", feats, nconv=2, ncls=ncls, seed=wseed)
+        prob, info = orc.ref_infer(w, vol, P, ov, batch=2, **ropt)
+    np.savez_compressed(
+        HERE / f"feat_{name}.npz",
+        prob_u16=np.round(np.clip(prob, 0.0, 1.0).astype(np.float64) * 65535.0).astype(np.uint16),
+        features=np.array(feats, dtype=np.int64), ncls=np.int64(ncls), weight_seed=np.int64(wseed),
+        shape=np.array(shape, dtype=np.int64), volume_seed=np.int64(vseed), patch=np.int64(P),
+        overlap=np.float64(ov), options=np.array(repr(ropt)),
+    )
+    print(f"feat_{name}.npz: {prob.shape}, {info}")
 
 
 def resenc_case(name):
@@ -229,6 +271,9 @@ def main():
     for name in CASES128:
         if a.only in (None, "net128_" + name):
             net128_case(name)
+    for name in FEATS:
+        if a.only in (None, "feat_" + name):
+            feat_case(name)
     for name in RESENC:
         if a.only in (None, "resenc_" + name):
             resenc_case(name)

@@ -1,6 +1,8 @@
-"""The header-only C++ host API (include/fenix_b200/ml/infer.hpp), compiled with g++ -std=c++23
-against the library: argument grammar and error mapping on the CPU, predict_surface_window and
-predict_surface_u8 on the GPU against the same path called through the Python binding."""
+"""The header-only C++ host API (include/fenix_b200/ml/infer.hpp, ml_api.hpp), compiled with g++
+-std=c++23 against the library: argument grammar, options, the stage registry and error mapping on
+the CPU; predict_surface_window and predict_surface_u8 on the GPU against the same path called
+through the Python binding; the predict-surface / predict-scroll stages over archives,
+predict_surface_filled, output crops and tile filters on the GPU."""
 import subprocess
 from pathlib import Path
 
@@ -60,3 +62,11 @@ def test_host_api_window_matches_binding(cuda_torch, host_api_bin, tmp_path):
     # InstanceNorm statistics: equal within the f16 path's tolerance (u8 steps of 1/255)
     d = np.abs(u8_b2.astype(int) - want.astype(int))
     assert d.max() <= 4 and d.mean() < 0.05
+
+
+@pytest.mark.gpu
+def test_host_api_stages(cuda_torch, host_api_bin, tmp_path):
+    w = make_plain_unet(tmp_path / "c1.fxweights", CONFIG1_FEATURES, seed=0)
+    r = subprocess.run([str(host_api_bin), "stages", str(w), str(tmp_path)], capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
