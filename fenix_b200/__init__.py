@@ -62,7 +62,21 @@ class InferOpts(C.Structure):
         ("core_ext", C.c_int64 * 3),
         ("tile_filter", TileFilter),
         ("tile_filter_user", C.c_void_p),
+        ("tile", C.c_int * 3),
     ]
+
+
+class PapyrusParams(C.Structure):
+    """fx_papyrus_params (include/fenix_b200_synth.h)."""
+
+    _fields_ = [(k, C.c_double) for k in ("sigma_z", "sigma_y", "sigma_x", "mean", "sd", "ink_sigma", "ink_fraction",
+                                          "ink_delta")]
+
+
+# The layer-stack workload's papyrus: fibre texture sigma (4, 1, 1) around 110 +- 20, ink blobs
+# (2D sigma 6) on 5% of the (y, x) columns, +25.
+PAPYRUS_INK = dict(sigma_z=4.0, sigma_y=1.0, sigma_x=1.0, mean=110.0, sd=20.0, ink_sigma=6.0, ink_fraction=0.05,
+                   ink_delta=25.0)
 
 
 class SpiralParams(C.Structure):
@@ -108,6 +122,8 @@ def lib():
     _sig(L, "fx_net_create", i32, [C.c_char_p, i32, i32, i32, i32, C.POINTER(vp)])
     _sig(L, "fx_net_destroy", None, [vp])
     _sig(L, "fx_net_patch", i32, [vp])
+    _sig(L, "fx_net_create_tiled", i32, [C.c_char_p, C.POINTER(i32), i32, i32, i32, C.POINTER(vp)])
+    _sig(L, "fx_net_tile", i32, [vp, C.POINTER(i32), C.POINTER(i32), i32])
     _sig(L, "fx_net_max_batch", i32, [vp])
     _sig(L, "fx_net_classes", i32, [vp])
     _sig(L, "fx_net_features", i32, [vp, C.POINTER(C.c_int), i32])
@@ -156,6 +172,7 @@ def lib():
     _sig(L, "fx_kernel_launches", C.c_ulonglong, [])
     _sig(L, "fx_tc_peak", i32, [i32, i32, C.c_double, i32, C.POINTER(C.c_double), C.POINTER(C.c_double)])
     _sig(L, "fx_synth_spiral", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
+    _sig(L, "fx_synth_papyrus", i32, [u8p, u8p, i64, i64, i64, C.POINTER(PapyrusParams), C.c_uint64, i64])
     u64p, u32p = C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)
     _sig(L, "fx_fxvol_open", i32, [C.c_char_p, C.POINTER(vp)])
     _sig(L, "fx_fxvol_create", i32, [C.c_char_p, i64, i64, i64, C.c_float, i32, C.POINTER(vp)])
@@ -228,6 +245,21 @@ def synth_spiral(shape, seed: int, params: dict | None = None, z_begin: int = 0,
     return out
 
 
+def synth_papyrus(shape, seed: int, stack: int = 0, params: dict | None = None, want_ink: bool = False):
+    """Papyrus layer stack [dz][dy][dx] u8 number `stack` of a seeded series (fx_synth_papyrus);
+    with want_ink, also its [dy][dx] ink mask."""
+    dz, dy, dx = shape
+    p = PapyrusParams(**(params or PAPYRUS_INK))
+    out = np.empty((dz, dy, dx), dtype=np.uint8)
+    ink = np.empty((dy, dx), dtype=np.uint8) if want_ink else None
+    rc = lib().fx_synth_papyrus(out.ctypes.data_as(C.POINTER(C.c_uint8)),
+                                ink.ctypes.data_as(C.POINTER(C.c_uint8)) if want_ink else None, dz, dy, dx,
+                                C.byref(p), seed, stack)
+    if rc != 0:
+        raise ValueError("fx_synth_papyrus: bad arguments")
+    return (out, ink) if want_ink else out
+
+
 def kernel_launches() -> int:
     """Kernel launches issued by libfenix_b200 in this process."""
     return int(lib().fx_kernel_launches())
@@ -246,17 +278,39 @@ def device_count() -> int:
 
 # ---- nets ----------------------------------------------------------------------------------
 class Net:
-    """A UNet on one GPU (fx_net). ``precision`` is "f16", "bf16" or "fp8"."""
+    """A UNet on one GPU (fx_net). ``precision`` is "f16", "bf16" or "fp8". ``patch`` is the side of
+    a cubic tile, or a (z, y, x) tile (fx_net_create_tiled); ``self.patch`` is None for a non-cubic
+    tile and ``self.tile`` always holds the three extents."""
 
-    def __init__(self, weights_path: str, patch: int, max_batch: int = 1, precision: str = "bf16", device: int = 0):
+    def __init__(self, weights_path: str, patch, max_batch: int = 1, precision: str = "bf16", device: int = 0):
         L = lib()
         h = C.c_void_p()
         prec = PRECISIONS[precision]
-        check(L.fx_net_create(str(weights_path).encode(), patch, max_batch, prec, device, C.byref(h)))
+        tile = (int(patch),) * 3 if np.isscalar(patch) else tuple(int(v) for v in patch)
+        if len(tile) != 3:
+            raise ValueError("patch: an int or a (z, y, x) triple")
+        if tile[0] == tile[1] == tile[2]:
+            check(L.fx_net_create(str(weights_path).encode(), tile[0], max_batch, prec, device, C.byref(h)))
+        else:
+            check(L.fx_net_create_tiled(str(weights_path).encode(), (C.c_int * 3)(*tile), max_batch, prec, device,
+                                        C.byref(h)))
         self._h = h
-        self.patch = patch
+        self.tile = tile
+        self.patch = tile[0] if tile[0] == tile[1] == tile[2] else None
         self.precision = precision
         self.device = device
+
+    def stage_masks(self) -> list[int]:
+        """Per stage, the axes its strided conv halves (bit 2 z, bit 1 y, bit 0 x; stage 0: 0)."""
+        m = (C.c_int * 16)()
+        n = lib().fx_net_tile(self._h, None, m, 16)
+        return list(m[:n])
+
+    def _opts(self, overlap, channel, sigmoid, batch, tta, norm=0, skip=0):
+        opts = InferOpts(self.patch or 0, overlap, channel, sigmoid, batch, tta, norm, skip)
+        if self.patch is None:
+            opts.tile[:] = list(self.tile)
+        return opts
 
     def close(self):
         if getattr(self, "_h", None):
@@ -348,7 +402,7 @@ class Net:
         callable(z0, y0, x0, patch) -> bool. Outputs have the crop's dims when cropped."""
         v = np.ascontiguousarray(vol_u8, dtype=np.uint8)
         dz, dy, dx = v.shape
-        opts = InferOpts(self.patch, overlap, channel, sigmoid, batch, tta, NORMS[norm], 1 if skip_constant else 0)
+        opts = self._opts(overlap, channel, sigmoid, batch, tta, NORMS[norm], 1 if skip_constant else 0)
         out_shape = v.shape
         if core is not None:
             opts.core_org[:] = list(core[:3])

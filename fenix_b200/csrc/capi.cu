@@ -80,6 +80,20 @@ fx_status abi_exception() {
         return set_err(FX_INTERNAL, "internal error");
     }
 }
+// The tile of a call: opts.tile when set (all three positive), else the cube of side opts.patch,
+// which must be divisible by 64 as in the reference (src/ml/infer.hpp:459).
+fx_status opts_tile(const fx_infer_opts* o, fxk::TileDims* t) {
+    if (o->tile[0] == 0 && o->tile[1] == 0 && o->tile[2] == 0) {
+        if (o->patch <= 0 || o->patch % 64 != 0) return set_err(FX_INVALID_ARGUMENT, "patch must be divisible by 64");
+        *t = {o->patch, o->patch, o->patch};
+        return FX_OK;
+    }
+    if (o->tile[0] <= 0 || o->tile[1] <= 0 || o->tile[2] <= 0)
+        return set_err(FX_INVALID_ARGUMENT, "tile: all three extents must be positive");
+    *t = {o->tile[0], o->tile[1], o->tile[2]};
+    return FX_OK;
+}
+
 // ml::InferOptions fields beyond the tile grid, as the driver's per-call options.
 RunOpts run_opts(const fx_infer_opts* o) {
     RunOpts r;
@@ -115,17 +129,19 @@ fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t 
     if (ce[0] < 1 || ce[1] < 1 || ce[2] < 1) return set_err(FX_INVALID_ARGUMENT, "predict: empty output crop");
     const size_t nv = static_cast<size_t>(ce[0]) * ce[1] * ce[2];
     cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
-    Status st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, o->patch, o->overlap, o->channel, o->sigmoid, o->batch,
-                                     0, -1, d_acc, s, co[0], ce[0], o->tta, run_opts(o));
+    fxk::TileDims tl{};
+    if (fx_status r = opts_tile(o, &tl)) return r;
+    Status st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, tl, o->overlap, o->channel, o->sigmoid, o->batch, 0, -1,
+                                     d_acc, s, co[0], ce[0], o->tta, run_opts(o));
     if (!st.ok()) return set_err(st);
-    const int P = o->patch;
-    const auto g = fenix::ml::gaussian1d(P);
+    const int T[3] = {tl.z, tl.y, tl.x};
     std::vector<float> w(static_cast<size_t>(ce[0] + ce[1] + ce[2]));
     size_t at = 0;
     for (int a = 0; a < 3; ++a) {
         // the factorised weight over the crop's span of each axis (src/ml/infer.hpp:499-509)
-        const auto starts = fenix::ml::tile_starts(d[a], P, o->overlap);
-        const auto W = fenix::ml::weight_profile(g, starts, co[a], ce[a], d[a], P);
+        const auto g = fenix::ml::gaussian1d(T[a]);
+        const auto starts = fenix::ml::tile_starts(d[a], T[a], o->overlap);
+        const auto W = fenix::ml::weight_profile(g, starts, co[a], ce[a], d[a], T[a]);
         std::copy(W.begin(), W.end(), w.begin() + static_cast<std::ptrdiff_t>(at));
         at += static_cast<size_t>(ce[a]);
     }
@@ -202,7 +218,21 @@ fx_status fx_net_create(const char* path, int patch, int max_batch, fx_precision
         if (!path || !out) return set_err(FX_INVALID_ARGUMENT, "fx_net_create: null argument");
         *out = nullptr;
         auto h = std::make_unique<fx_net>();
-        fxh::Status st = h->net.create(path, patch, max_batch, static_cast<int>(precision), device);
+        const int t[3] = {patch, patch, patch};
+        fxh::Status st = h->net.create(path, t, max_batch, static_cast<int>(precision), device);
+        if (!st.ok()) return set_err(st);
+        *out = h.release();
+        return FX_OK;
+    });
+}
+
+fx_status fx_net_create_tiled(const char* path, const int tile[3], int max_batch, fx_precision precision, int device,
+                              fx_net** out) {
+    return guarded([&]() -> fx_status {
+        if (!path || !tile || !out) return set_err(FX_INVALID_ARGUMENT, "fx_net_create_tiled: null argument");
+        *out = nullptr;
+        auto h = std::make_unique<fx_net>();
+        fxh::Status st = h->net.create(path, tile, max_batch, static_cast<int>(precision), device);
         if (!st.ok()) return set_err(st);
         *out = h.release();
         return FX_OK;
@@ -212,6 +242,18 @@ fx_status fx_net_create(const char* path, int patch, int max_batch, fx_precision
 void fx_net_destroy(fx_net* net) { delete net; }
 
 int fx_net_patch(const fx_net* n) { return n ? n->net.patch() : 0; }
+int fx_net_tile(const fx_net* n, int tile[3], int* masks, int cap) {
+    if (!n) return 0;
+    const fxk::TileDims t = n->net.tile();
+    if (tile) {
+        tile[0] = t.z;
+        tile[1] = t.y;
+        tile[2] = t.x;
+    }
+    const auto& m = n->net.stage_masks();
+    for (int i = 0; masks && i < cap && i < static_cast<int>(m.size()); ++i) masks[i] = m[i];
+    return static_cast<int>(m.size());
+}
 int fx_net_max_batch(const fx_net* n) { return n ? n->net.max_batch() : 0; }
 int fx_net_classes(const fx_net* n) { return n ? n->net.classes() : 0; }
 int fx_net_features(const fx_net* n, int* out, int cap) {
@@ -287,18 +329,18 @@ fx_status fx_net_forward(fx_net* n, const uint8_t* dev_tiles, int nb, float* dev
         if (!n || !dev_tiles || !dev_prob) return set_err(FX_INVALID_ARGUMENT, "fx_net_forward: null argument");
         cudaSetDevice(n->net.device());
         cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : n->net.stream();
-        const int P = n->net.patch();
+        const fxk::TileDims t = n->net.tile();
         if (nb < 1 || nb > n->net.max_batch()) return set_err(FX_INVALID_ARGUMENT, "fx_net_forward: batch out of range");
         if (!sigmoid && (channel < 0 || channel >= n->net.classes()))
             return set_err(FX_INVALID_ARGUMENT, "fx_net_forward: channel out of range");
-        // The nb tiles are stacked along z: tile b is the volume's z-range [b P, (b+1) P).
+        // The nb tiles are stacked along z: tile b is the volume's z-range [b tz, (b+1) tz).
         std::vector<fxk::TileOrigin> org(nb);
-        for (int b = 0; b < nb; ++b) org[b] = {static_cast<int64_t>(b) * P, 0, 0};
+        for (int b = 0; b < nb; ++b) org[b] = {static_cast<int64_t>(b) * t.z, 0, 0};
         fxk::TileOrigin* d_org = nullptr;
         if (cudaMalloc(&d_org, sizeof(fxk::TileOrigin) * nb) != cudaSuccess)
             return set_err(FX_INTERNAL, "cudaMalloc failed");
         cudaMemcpyAsync(d_org, org.data(), sizeof(fxk::TileOrigin) * nb, cudaMemcpyHostToDevice, s);
-        fxh::Status st = n->net.forward(dev_tiles, static_cast<int64_t>(nb) * P, P, P, d_org, nb, channel, sigmoid,
+        fxh::Status st = n->net.forward(dev_tiles, static_cast<int64_t>(nb) * t.z, t.y, t.x, d_org, nb, channel, sigmoid,
                                         nullptr, dev_prob, false, s);
         cudaError_t e = cudaStreamSynchronize(s);
         cudaFree(d_org);
@@ -316,14 +358,15 @@ fx_status fx_predict_tiles_dev(fx_net* n, const uint8_t* dev_slab, int64_t slab_
         if (!n || !dev_slab || !o || !dev_acc) return set_err(FX_INVALID_ARGUMENT, "fx_predict_tiles_dev: null argument");
         if (slab_dz < 1 || dy < 1 || dx < 1 || full_dz < slab_dz || z_origin < 0 || z_origin + slab_dz > full_dz)
             return set_err(FX_INVALID_ARGUMENT, "fx_predict_tiles_dev: bad slab geometry");
-        if (o->patch % 64 != 0) return set_err(FX_INVALID_ARGUMENT, "patch must be divisible by 64");
+        fxk::TileDims tl{};
+        if (fx_status r = fxh::opts_tile(o, &tl)) return r;
         cudaSetDevice(n->net.device());
         cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : n->net.stream();
         fxh::RunOpts ro = fxh::run_opts(o);
         if (ro.core_org[0] || ro.core_org[1] || ro.core_org[2] || ro.core_ext[0] > 0 || ro.core_ext[1] > 0 ||
             ro.core_ext[2] > 0)
             return set_err(FX_UNSUPPORTED, "fx_predict_tiles_dev: output crops are taken by fx_predict_volume only");
-        fxh::Status st = n->net.predict_tiles(dev_slab, slab_dz, dy, dx, z_origin, full_dz, o->patch, o->overlap,
+        fxh::Status st = n->net.predict_tiles(dev_slab, slab_dz, dy, dx, z_origin, full_dz, tl, o->overlap,
                                               o->channel, o->sigmoid, o->batch, tile_begin, tile_end, dev_acc, s, 0,
                                               -1, o->tta, ro);
         return st.ok() ? FX_OK : set_err(st);
@@ -404,8 +447,8 @@ fx_status fx_predict_volume(fx_net* n, const uint8_t* host_vol, int64_t dz, int6
     return guarded([&]() -> fx_status {
         if (!n || !host_vol || !o) return set_err(FX_INVALID_ARGUMENT, "fx_predict_volume: null argument");
         if (dz < 1 || dy < 1 || dx < 1) return set_err(FX_INVALID_ARGUMENT, "fx_predict_volume: empty volume");
-        if (o->patch % 64 != 0)  // the reference's own check (src/ml/infer.hpp:459)
-            return set_err(FX_INVALID_ARGUMENT, "patch must be divisible by 64");
+        fxk::TileDims tl{};  // the reference's patch % 64 check (src/ml/infer.hpp:459) for cubes
+        if (fx_status r = fxh::opts_tile(o, &tl)) return r;
         cudaSetDevice(n->net.device());
         cudaStream_t s = n->net.stream();
         const size_t nv = static_cast<size_t>(dz) * dy * dx;
@@ -490,9 +533,9 @@ fx_status fx_norm_tiles(const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t 
         if (!d_org || !d_sums) return set_err(FX_INTERNAL, "cudaMalloc failed");
         cudaMemcpyAsync(d_org, org.data(), sizeof(fxk::TileOrigin) * ntiles, cudaMemcpyHostToDevice, s);
         cudaMemsetAsync(d_sums, 0, sizeof(unsigned long long) * 2 * ntiles, s);
-        cudaError_t e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, s);
+        cudaError_t e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, d_org, ntiles, fxk::TileDims{patch, patch, patch}, d_sums, s);
         if (e == cudaSuccess)
-            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, nullptr, 0, 0, fxk::kOpF16,
+            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, fxk::TileDims{patch, patch, patch}, d_sums, nullptr, 0, 0, fxk::kOpF16,
                                       dev_out, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles"));
@@ -516,11 +559,11 @@ fx_status fx_norm_tiles_mode(const uint8_t* dev_vol, int64_t dz, int64_t dy, int
         cudaMemcpyAsync(d_org, org.data(), sizeof(fxk::TileOrigin) * ntiles, cudaMemcpyHostToDevice, s);
         cudaMemsetAsync(d_sums, 0, sizeof(unsigned long long) * 2 * ntiles, s);
         cudaMemsetAsync(d_hist, 0, sizeof(unsigned) * 256 * ntiles, s);
-        cudaError_t e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, s, d_hist);
+        cudaError_t e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, d_org, ntiles, fxk::TileDims{patch, patch, patch}, d_sums, s, d_hist);
         const int64_t n = static_cast<int64_t>(patch) * patch * patch;
         if (e == cudaSuccess) e = fxk::launch_tile_lut(d_sums, d_hist, ntiles, n, norm, d_lut, nullptr, s);
         if (e == cudaSuccess)
-            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, patch, d_sums, nullptr, 0, 0, fxk::kOpF16,
+            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, d_org, ntiles, fxk::TileDims{patch, patch, patch}, d_sums, nullptr, 0, 0, fxk::kOpF16,
                                       dev_out, s, nullptr, d_lut);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles_mode"));
@@ -548,6 +591,7 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
         L.Cin = Cin;
         L.Cout = Cout;
         L.stride = stride;
+        L.smask = stride == 2 ? 7 : 0;
         L.w.resize(static_cast<size_t>(Cout) * Cin * 27);
         cudaMemcpyAsync(L.w.data(), dev_w, L.w.size() * sizeof(float), cudaMemcpyDeviceToHost, s);
         cudaStreamSynchronize(s);
@@ -590,7 +634,7 @@ fx_status fx_conv3d(const float* dev_x, int B, int Cin, int D, int H, int W, con
             in = static_cast<uint8_t*>(sc.get(static_cast<size_t>(B) * ibs));
             if (!in) return set_err(FX_INTERNAL, "cudaMalloc failed");
             cudaMemsetAsync(in, 0, static_cast<size_t>(B) * ibs, s);
-            fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, fp8 ? 1.f / L.in_scale : 1.f, 1, gout.H + 2,
+            fxk::launch_pack(dev_x, B, Cin, D, H, W, in, ibs, igs, q, fp8 ? 1.f / L.in_scale : 1.f, 7, gout.H + 2,
                              gout.W + 2, ps, s);
         }
         const int64_t ogs = gout.gs(), obs = (Cout / 8) * ogs;
@@ -656,6 +700,7 @@ fx_status fx_conv_transpose2(const float* dev_x, int B, int Cin, int D, int H, i
         L.Cin = Cin;
         L.Cout = Cout;
         L.stride = 2;
+        L.smask = 7;
         L.w.resize(static_cast<size_t>(Cin) * Cout * 8);
         L.b.resize(Cout);
         cudaMemcpyAsync(L.w.data(), dev_w, L.w.size() * sizeof(float), cudaMemcpyDeviceToHost, s);
@@ -751,9 +796,9 @@ fx_status fx_norm_tiles_noalloc(const uint8_t* dev_vol, int64_t dz, int64_t dy, 
         e = cudaMemcpyAsync(org, host_origins, sizeof(fxk::TileOrigin) * ntiles, cudaMemcpyHostToDevice, s);
         // the sums are accumulated with atomics: they start at zero on every call
         if (e == cudaSuccess) e = cudaMemsetAsync(sums, 0, 2 * sizeof(unsigned long long) * ntiles, s);
-        if (e == cudaSuccess) e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, org, ntiles, patch, sums, s);
+        if (e == cudaSuccess) e = fxk::launch_tile_sums(dev_vol, dz, dy, dx, org, ntiles, fxk::TileDims{patch, patch, patch}, sums, s);
         if (e == cudaSuccess)
-            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, org, ntiles, patch, sums, nullptr, 0, 0, fxk::kOpF16, dev_out,
+            e = fxk::launch_tile_norm(dev_vol, dz, dy, dx, org, ntiles, fxk::TileDims{patch, patch, patch}, sums, nullptr, 0, 0, fxk::kOpF16, dev_out,
                                       s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
         return e == cudaSuccess ? FX_OK : set_err(fxh::cuda_status(e, "fx_norm_tiles_noalloc"));

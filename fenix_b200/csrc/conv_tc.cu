@@ -472,6 +472,10 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const bool percol = p.col_scale != nullptr;
     const float acc_scale = p.acc_scale;
     const int32_t oP2 = p.oHp * p.oWp;  // upsample: padded plane of the output grid
+    // upsample: factor along each axis and the bit of a phase index that holds each axis's parity
+    const int um = p.up_mask;
+    const int uz = (um & 4) ? 2 : 1, uy = (um & 2) ? 2 : 1, ux = (um & 1) ? 2 : 1;
+    const int bx = 0, by = (um & 1) ? 1 : 0, bz = by + ((um & 2) ? 1 : 0);
     // InstanceNorm partial sums accumulate over all units of one (batch item, N tile) run of this
     // CTA; a run ends in one flush: butterfly, then add into this warp's slot of the CTA's record
     // [b][blockIdx.x][stat_recs] (records start at zero; the statistics pass clears what it reads).
@@ -648,13 +652,14 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
             locate(r, row, valid, rc);
             const uint32_t taddr =
                 tbase + (static_cast<uint32_t>(wq * 32) << 16) + aslot * slot_cols + rc * p.N_tile;
-            // upsample: phase-0 output cell of this input voxel (2z-1, 2y-1, 2x-1 in the padded grid)
+            // upsample: phase-0 output cell of this input voxel (u (z - 1) + 1 per axis in the padded grid)
             uint8_t* ob = nullptr;
             if (!prenorm && valid) {  // upsample runs no fold: the row splits directly
                 uint32_t z, y, x;
                 rd.split(static_cast<uint32_t>(row), z, y, x);
                 ob = p.out + static_cast<int64_t>(b) * p.out_batch_stride +
-                     ((static_cast<int64_t>(2 * z - 1) * p.oHp + (2 * y - 1)) * p.oWp + (2 * x - 1)) * 16;
+                     ((static_cast<int64_t>(uz * (z - 1) + 1) * p.oHp + (uy * (y - 1) + 1)) * p.oWp +
+                      (ux * (x - 1) + 1)) * 16;
             }
 #pragma unroll
             for (int g0 = 0; g0 < kMy; g0 += kGrp) {
@@ -723,7 +728,8 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
                             if (e4out) mx /= p.out_qscale;
                             atomicMax(p.amax, __float_as_uint(mx));
                         }
-                        const int az = a >> 2, ay = (a >> 1) & 1, ax = a & 1;
+                        const int az = uz == 2 ? (a >> bz) & 1 : 0, ay = uy == 2 ? (a >> by) & 1 : 0,
+                                  ax = ux == 2 ? (a >> bx) & 1 : 0;
                         uint8_t* o = ob + static_cast<int64_t>(az * oP2 + ay * p.oWp + ax) * 16;
                         if (e4out) {
                             uint4 w;
@@ -782,6 +788,10 @@ __device__ void epilogue_up(const ConvParams& p, SmemCtl* ctl, int n_units) {
     const bool e4out = p.out_type == kOpE4M3;
     const int lc = __ffs(p.cout) - 1;  // log2(Cout)
     const int64_t oP2 = static_cast<int64_t>(p.oHp) * p.oWp;
+    // factor along each axis and the bit of a phase index that holds each axis's parity
+    const int um = p.up_mask;
+    const int uz = (um & 4) ? 2 : 1, uy = (um & 2) ? 2 : 1, ux = (um & 1) ? 2 : 1;
+    const int bx = 0, by = (um & 1) ? 1 : 0, bz = by + ((um & 2) ? 1 : 0);
     uint32_t j = 0;
     for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, ++j) {
         int b, mu, nt;
@@ -807,7 +817,8 @@ __device__ void epilogue_up(const ConvParams& p, SmemCtl* ctl, int n_units) {
             const int n0 = cbase + (c0 + c * kCs) * 16;
             const int a = n0 >> lc, co0 = n0 - (a << lc);
             cofs[c] = co0;
-            const int64_t cell = (a >> 2) * oP2 + ((a >> 1) & 1) * static_cast<int64_t>(p.oWp) + (a & 1);
+            const int dz = uz == 2 ? (a >> bz) & 1 : 0, dy = uy == 2 ? (a >> by) & 1 : 0, dx = ux == 2 ? (a >> bx) & 1 : 0;
+            const int64_t cell = dz * oP2 + dy * static_cast<int64_t>(p.oWp) + dx;
             boff[c] = static_cast<int32_t>(cell * 16 + static_cast<int64_t>(co0 / (e4out ? 16 : 8)) * p.out_group_stride);
         }
         for (int r = rb; r < p.R; r += rs) {
@@ -820,7 +831,8 @@ __device__ void epilogue_up(const ConvParams& p, SmemCtl* ctl, int n_units) {
             uint8_t* ob = nullptr;
             if (valid)
                 ob = p.out + static_cast<int64_t>(b) * p.out_batch_stride +
-                     ((static_cast<int64_t>(2 * z - 1) * p.oHp + (2 * y - 1)) * p.oWp + (2 * x - 1)) * 16;
+                     ((static_cast<int64_t>(uz * (z - 1) + 1) * p.oHp + (uy * (y - 1) + 1)) * p.oWp +
+                      (ux * (x - 1) + 1)) * 16;
 #pragma unroll
             for (int g0 = 0; g0 < kMy; g0 += kGrp) {
                 uint32_t raw[kGrp][16];

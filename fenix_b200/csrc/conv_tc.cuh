@@ -122,6 +122,8 @@ struct ConvParams {
     uint8_t* out;            // output tensor, group 0 of the written channel slice, batch 0
     int64_t out_batch_stride, out_group_stride;  // bytes
     int32_t out_type;        // upsample mode: OpType of the written cells (e4m3 scaled by out_qscale)
+    int32_t up_mask;         // upsample mode: the axes doubled (bit 2 z, bit 1 y, bit 0 x); the output
+                             // phases (N_tile / cout of them) enumerate their parities in z, y, x order
     float out_qscale;
     int32_t cout;            // upsample mode: channels per phase
     int32_t oHp, oWp;        // upsample mode: padded H, W of the output grid

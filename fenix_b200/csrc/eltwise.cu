@@ -29,7 +29,7 @@ __device__ __forceinline__ uint8_t vol_at(const uint8_t* vol, int64_t dz, int64_
 // A warp walks whole (z, y) lines of the tile, lanes across x: one 32-bit division per line.
 template <bool HIST>
 __global__ void tile_sums_kernel(const uint8_t* __restrict__ vol, int64_t dz, int64_t dy, int64_t dx,
-                                 const TileOrigin* __restrict__ tiles, int P, unsigned long long* sums,
+                                 const TileOrigin* __restrict__ tiles, TileDims P, unsigned long long* sums,
                                  unsigned* __restrict__ hist) {
     const int b = blockIdx.y;
     __shared__ unsigned h[HIST ? 256 : 1];
@@ -38,17 +38,17 @@ __global__ void tile_sums_kernel(const uint8_t* __restrict__ vol, int64_t dz, in
         __syncthreads();
     }
     const TileOrigin t = tiles[b];
-    const bool inside = t.z0 + P <= dz && t.y0 + P <= dy && t.x0 + P <= dx;
+    const bool inside = t.z0 + P.z <= dz && t.y0 + P.y <= dy && t.x0 + P.x <= dx;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     constexpr int kWarps = kEwThreads / 32;
     unsigned long long s1 = 0, s2 = 0;
-    const uint32_t lines = static_cast<uint32_t>(P) * P;
+    const uint32_t lines = static_cast<uint32_t>(P.z) * P.y;
     for (uint32_t line = blockIdx.x * kWarps + w; line < lines; line += gridDim.x * kWarps) {
-        const int z = static_cast<int>(line / static_cast<uint32_t>(P));
-        const int y = static_cast<int>(line - static_cast<uint32_t>(z) * P);
+        const int z = static_cast<int>(line / static_cast<uint32_t>(P.y));
+        const int y = static_cast<int>(line - static_cast<uint32_t>(z) * P.y);
         const uint8_t* src = vol + ((t.z0 + z) * dy + (t.y0 + y)) * dx + t.x0;
-        uint32_t a1 = 0, a2 = 0;  // one line: at most P * 255^2 < 2^32 for P <= 66051
-        for (int x = lane; x < P; x += 32) {
+        uint32_t a1 = 0, a2 = 0;  // one line: at most P.x * 255^2 < 2^32 for P.x <= 66051
+        for (int x = lane; x < P.x; x += 32) {
             const uint32_t v = inside ? __ldg(src + x) : vol_at(vol, dz, dy, dx, t.z0 + z, t.y0 + y, t.x0 + x);
             a1 += v;
             a2 += v * v;
@@ -166,14 +166,14 @@ __global__ void tile_lut_kernel(const unsigned long long* __restrict__ sums, con
 }
 
 __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, int64_t dy, int64_t dx,
-                                 const TileOrigin* __restrict__ tiles, int P,
+                                 const TileOrigin* __restrict__ tiles, TileDims P,
                                  const unsigned long long* __restrict__ sums, const float* __restrict__ luts,
                                  uint8_t* __restrict__ l0,
                                  int64_t l0_batch_stride, int64_t l0_group_stride, int l0_type,
                                  float* __restrict__ f32_out, const uint8_t* __restrict__ tta) {
     const int b = blockIdx.y;
     __shared__ float lut[256];
-    const int64_t n = static_cast<int64_t>(P) * P * P;
+    const int64_t n = P.count();
     if (luts) {
         for (int v = threadIdx.x; v < 256; v += blockDim.x) lut[v] = luts[static_cast<int64_t>(b) * 256 + v];
     } else {
@@ -181,32 +181,32 @@ __global__ void tile_norm_kernel(const uint8_t* __restrict__ vol, int64_t dz, in
     }
     __syncthreads();
     const TileOrigin t = tiles[b];
-    const int Pp = P + 2;
-    const bool inside = t.z0 + P <= dz && t.y0 + P <= dy && t.x0 + P <= dx;
+    const int Hp = P.y + 2, Wp = P.x + 2;
+    const bool inside = t.z0 + P.z <= dz && t.y0 + P.y <= dy && t.x0 + P.x <= dx;
     // a warp walks whole (z, y) lines, lanes across x: one 32-bit division per line
     const int lane = threadIdx.x & 31;
     constexpr int kWarps = kEwThreads / 32;
-    const uint32_t lines = static_cast<uint32_t>(P) * P;
+    const uint32_t lines = static_cast<uint32_t>(P.z) * P.y;
     for (uint32_t line = blockIdx.x * kWarps + (threadIdx.x >> 5); line < lines; line += gridDim.x * kWarps)
-    for (int x = lane; x < P; x += 32) {
-        const int z = static_cast<int>(line / static_cast<uint32_t>(P));
-        const int y = static_cast<int>(line - static_cast<uint32_t>(z) * P);
-        const int64_t i = static_cast<int64_t>(line) * P + x;
+    for (int x = lane; x < P.x; x += 32) {
+        const int z = static_cast<int>(line / static_cast<uint32_t>(P.y));
+        const int y = static_cast<int>(line - static_cast<uint32_t>(z) * P.y);
+        const int64_t i = static_cast<int64_t>(line) * P.x + x;
         float v[3];
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
             const int xx = x - 1 + k;
-            if (xx < 0 || xx >= P) {
+            if (xx < 0 || xx >= P.x) {
                 v[k] = 0.f;
             } else {
-                int sz = z, sy = y, sx = xx;  // source voxel of this member's frame voxel
-                if (tta) tta_source(tta[b], P, z, y, xx, sz, sy, sx);
+                int sz = z, sy = y, sx = xx;  // source voxel of this member's frame voxel (cubic tiles)
+                if (tta) tta_source(tta[b], P.x, z, y, xx, sz, sy, sx);
                 const uint8_t u = inside ? __ldg(vol + ((t.z0 + sz) * dy + (t.y0 + sy)) * dx + (t.x0 + sx))
                                          : vol_at(vol, dz, dy, dx, t.z0 + sz, t.y0 + sy, t.x0 + sx);
                 v[k] = lut[u];
             }
         }
-        const int64_t row = (static_cast<int64_t>(z + 1) * Pp + (y + 1)) * Pp + (x + 1);
+        const int64_t row = (static_cast<int64_t>(z + 1) * Hp + (y + 1)) * Wp + (x + 1);
         if (l0) {
             uint4 c0, c1;
             first_layer_cells(v, l0_type, c0, c1);
@@ -312,9 +312,7 @@ __device__ __forceinline__ void store_dest(const NormDest& d, int b, int gout, i
     if (!d.ptr) return;
     int64_t off;
     if (d.phase) {
-        const int phi = ((zp & 1) << 2) | ((yp & 1) << 1) | (xp & 1);
-        const int64_t prow = (static_cast<int64_t>(zp >> 1) * d.pHp + (yp >> 1)) * d.pWp + (xp >> 1);
-        off = phi * d.phase_stride + prow * 16;
+        off = phase_cell_offset(d.phase, zp, yp, xp, d.pHp, d.pWp, d.phase_stride);
     } else {
         off = row * 16;
     }
@@ -412,10 +410,8 @@ __global__ void __launch_bounds__(kNormThreads, MODE == 1 ? 8 : 6) norm_act_kern
             w.y = pack_e4m3x4(v[4] * q0, v[5] * q0, v[6] * q0, v[7] * q0);
             w.z = pack_e4m3x4(v[8] * q0, v[9] * q0, v[10] * q0, v[11] * q0);
             w.w = pack_e4m3x4(v[12] * q0, v[13] * q0, v[14] * q0, v[15] * q0);
-            const int phi = ((zp & 1) << 2) | ((yp[k] & 1) << 1) | (xp[k] & 1);
-            const int64_t prow = (static_cast<int64_t>(zp >> 1) * d0.pHp + (yp[k] >> 1)) * d0.pWp + (xp[k] >> 1);
-            *reinterpret_cast<uint4*>(d0.ptr + b * d0.batch_stride + go * d0.group_stride + phi * d0.phase_stride +
-                                      prow * 16) = w;
+            *reinterpret_cast<uint4*>(d0.ptr + b * d0.batch_stride + go * d0.group_stride +
+                                      phase_cell_offset(d0.phase, zp, yp[k], xp[k], d0.pHp, d0.pWp, d0.phase_stride)) = w;
             w.x = pack_e4m3x4(v[0] * q1, v[1] * q1, v[2] * q1, v[3] * q1);
             w.y = pack_e4m3x4(v[4] * q1, v[5] * q1, v[6] * q1, v[7] * q1);
             w.z = pack_e4m3x4(v[8] * q1, v[9] * q1, v[10] * q1, v[11] * q1);
@@ -553,18 +549,18 @@ __constant__ float c_head_b[2];
 // Block = (plane chunk, z, batch item); thread = one voxel. Scale/shift of the batch item's C
 // channels sit in shared memory, the head weights in constant memory.
 __global__ void __launch_bounds__(kEwThreads) head_blend_kernel(HeadParams h, FastDiv fp) {
-    const int P = h.P, Pp = P + 2;
+    const int Hp = h.Py + 2, Wp = h.Px + 2;
     const int b = blockIdx.z, z = blockIdx.y;
     __shared__ float2 s_ss[64];
     if (threadIdx.x < h.C)
         s_ss[threadIdx.x] = __ldg(reinterpret_cast<const float2*>(h.ss) + static_cast<int64_t>(b) * h.C + threadIdx.x);
     __syncthreads();
     const uint32_t i = blockIdx.x * kEwThreads + threadIdx.x;
-    if (i >= static_cast<uint32_t>(P) * P) return;
+    if (i >= static_cast<uint32_t>(h.Py) * h.Px) return;
     const int y = static_cast<int>(fdiv(i, fp));
-    const int x = static_cast<int>(i - static_cast<uint32_t>(y) * P);
+    const int x = static_cast<int>(i - static_cast<uint32_t>(y) * h.Px);
     const int G = h.C / 8;
-    const int64_t row = (static_cast<int64_t>(z + 1) * Pp + (y + 1)) * Pp + (x + 1);
+    const int64_t row = (static_cast<int64_t>(z + 1) * Hp + (y + 1)) * Wp + (x + 1);
     const uint8_t* pb = h.pre + b * h.pre_batch_stride + row * 16;
     uint4 cells[8];
 #pragma unroll
@@ -596,13 +592,13 @@ __global__ void __launch_bounds__(kEwThreads) head_blend_kernel(HeadParams h, Fa
     }
     if (isnan(p)) p = 0.f;
     else if (isinf(p)) p = p > 0.f ? 1.f : 0.f;
-    const int64_t n = static_cast<int64_t>(P) * P * P;
-    int sz = z, sy = y, sx = x;  // tile voxel this output belongs to (its TTA member's source)
+    const int64_t n = static_cast<int64_t>(h.Pz) * h.Py * h.Px;
+    int sz = z, sy = y, sx = x;  // tile voxel this output belongs to (its TTA member's source; cubes)
     if (h.tta) {
-        tta_source(h.tta[b], P, z, y, x, sz, sy, sx);
+        tta_source(h.tta[b], h.Px, z, y, x, sz, sy, sx);
         p *= h.tta_scale;
     }
-    if (h.prob) h.prob[b * n + (static_cast<int64_t>(sz) * P + sy) * P + sx] = p;
+    if (h.prob) h.prob[b * n + (static_cast<int64_t>(sz) * h.Py + sy) * h.Px + sx] = p;
     if (h.acc) {
         const TileOrigin t = h.tiles[b];
         const int z = sz, y = sy, x = sx;
@@ -614,8 +610,8 @@ __global__ void __launch_bounds__(kEwThreads) head_blend_kernel(HeadParams h, Fa
         if (oz < h.dz && oy < h.dy && ox < h.dx && az >= 0 && az < h.acc_dz && ay >= 0 && ay < ady && ax >= 0 &&
             ax < adx) {
             // (gz*gy)*gx*p in the reference's order (src/ml/infer.hpp:631-653)
-            const float wzy = __fmul_rn(__ldg(h.gauss + z), __ldg(h.gauss + y));
-            const float c = __fmul_rn(__fmul_rn(wzy, __ldg(h.gauss + x)), p);
+            const float wzy = __fmul_rn(__ldg(h.gz + z), __ldg(h.gy + y));
+            const float c = __fmul_rn(__fmul_rn(wzy, __ldg(h.gx + x)), p);
             atomicAdd(h.acc + (az * ady + ay) * adx + ax, c);
         }
     }
@@ -704,9 +700,9 @@ int grid_for(int64_t n, int threads) {
 }  // namespace
 
 cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
-                             int ntiles, int P, unsigned long long* sums, cudaStream_t s, unsigned* hist) {
-    if (ntiles < 1 || ntiles > 65535) return cudaErrorInvalidValue;
-    const int64_t lines = static_cast<int64_t>(P) * P;
+                             int ntiles, TileDims P, unsigned long long* sums, cudaStream_t s, unsigned* hist) {
+    if (ntiles < 1 || ntiles > 65535 || P.z < 1 || P.y < 1 || P.x < 1) return cudaErrorInvalidValue;
+    const int64_t lines = static_cast<int64_t>(P.z) * P.y;
     const int gx = grid_for(lines, (kEwThreads / 32) * 4);  // four lines per warp
     count_launch();
     if (hist)
@@ -725,10 +721,12 @@ cudaError_t launch_tile_lut(const unsigned long long* sums, const unsigned* hist
 }
 
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
-                             int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
+                             int ntiles, TileDims P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
                              int64_t l0_group_stride, int l0_type, float* f32_out, cudaStream_t s, const uint8_t* tta,
                              const float* luts) {
-    const int64_t lines = static_cast<int64_t>(P) * P;
+    if (ntiles < 1 || ntiles > 65535 || P.z < 1 || P.y < 1 || P.x < 1) return cudaErrorInvalidValue;
+    if (tta && !(P.z == P.y && P.y == P.x)) return cudaErrorInvalidValue;  // the symmetries permute axes
+    const int64_t lines = static_cast<int64_t>(P.z) * P.y;
     const int gx = grid_for(lines, (kEwThreads / 32) * 2);  // two lines per warp
     count_launch();
     tile_norm_kernel<<<dim3(gx, ntiles), kEwThreads, 0, s>>>(vol, dz, dy, dx, tiles, P, sums, luts, l0,
@@ -809,16 +807,18 @@ cudaError_t launch_avgpool2_f16(const uint8_t* src, int64_t src_bs, int64_t src_
 }
 
 cudaError_t launch_head_blend(const HeadParams& h, cudaStream_t s) {
-    if (h.ncls < 1 || h.ncls > 2 || h.C > 64 || h.C % 8 || h.P > 46340 || h.B > 65535) return cudaErrorInvalidValue;
+    if (h.ncls < 1 || h.ncls > 2 || h.C > 64 || h.C % 8 || h.B > 65535 || h.Pz < 1 || h.Pz > 65535 ||
+        static_cast<int64_t>(h.Py) * h.Px >= (1ll << 31) || (h.tta && !(h.Pz == h.Py && h.Py == h.Px)))
+        return cudaErrorInvalidValue;
     cudaError_t e = cudaMemcpyToSymbolAsync(c_head_w, h.wh, sizeof(float) * h.ncls * h.C, 0,
                                             cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return e;
     e = cudaMemcpyToSymbolAsync(c_head_b, h.bh, sizeof(float) * h.ncls, 0, cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return e;
-    const uint32_t PP = static_cast<uint32_t>(h.P) * h.P;
+    const uint32_t PP = static_cast<uint32_t>(h.Py) * h.Px;
     count_launch();
-    head_blend_kernel<<<dim3((PP + kEwThreads - 1) / kEwThreads, h.P, h.B), kEwThreads, 0, s>>>(
-        h, make_fastdiv(static_cast<uint32_t>(h.P)));
+    head_blend_kernel<<<dim3((PP + kEwThreads - 1) / kEwThreads, h.Pz, h.B), kEwThreads, 0, s>>>(
+        h, make_fastdiv(static_cast<uint32_t>(h.Px)));
     return cudaGetLastError();
 }
 

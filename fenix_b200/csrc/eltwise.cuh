@@ -18,12 +18,18 @@ struct TileOrigin {
     int64_t z0, y0, x0;
 };
 
+// Extents of one tile along z, y, x (the surface nets use cubes; the layer-stack ink net 64 x 256 x 256).
+struct TileDims {
+    int32_t z, y, x;
+    __host__ __device__ int64_t count() const { return static_cast<int64_t>(z) * y * x; }
+};
+
 // ---- tiler ----------------------------------------------------------------------------------
 // Integer sum and sum of squares of every tile's P^3 u8 voxels (edge-clamped reads), into
 // sums[2*b + {0,1}] (exact; the caller zeroes `sums`), and with `hist` the count of each u8 level
 // per tile, hist[256*b + v] (caller-zeroed).
 cudaError_t launch_tile_sums(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
-                             int ntiles, int P, unsigned long long* sums, cudaStream_t s, unsigned* hist = nullptr);
+                             int ntiles, TileDims P, unsigned long long* sums, cudaStream_t s, unsigned* hist = nullptr);
 // Per-tile normalisation table of the 256 u8 levels, luts[256*b + v], for norm 0 zscore (from the
 // sums), 1 pct_minmax (from the histogram), 2 unit255 (src/ml/infer.hpp:107-134, 350-385); with
 // const_flag, 1 for each tile whose voxels all hold one value.
@@ -39,7 +45,7 @@ cudaError_t launch_tile_lut(const unsigned long long* sums, const unsigned* hist
 // tta (one byte per tile, or null): octahedral test-time-augmentation member of each tile; the
 // tile is written in that member's frame (see tta_source).
 cudaError_t launch_tile_norm(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, const TileOrigin* tiles,
-                             int ntiles, int P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
+                             int ntiles, TileDims P, const unsigned long long* sums, uint8_t* l0, int64_t l0_batch_stride,
                              int64_t l0_group_stride, int l0_type, float* f32_out, cudaStream_t s,
                              const uint8_t* tta = nullptr, const float* luts = nullptr);
 
@@ -79,7 +85,8 @@ struct NormDest {
     int64_t group_stride;  // bytes
     int32_t dtype;         // OpType of the written cells (e4m3 values are y * qscale)
     float qscale;
-    int32_t phase;         // 1: write the stride-2 phase-split copy (8 parity sub-volumes)
+    int32_t phase;         // != 0: write the stride-2 phase-split copy over the axes of this mask
+                           // (bit 2 z, bit 1 y, bit 0 x; one parity sub-volume per phase)
     int32_t pHp, pWp;      // phase sub-volume padded H, W (= output grid of the stride-2 conv)
     int64_t phase_stride;  // bytes between parity sub-volumes
 };
@@ -131,12 +138,14 @@ cudaError_t launch_avgpool2_f16(const uint8_t* src, int64_t src_bs, int64_t src_
 struct HeadParams {
     const uint8_t* pre;
     int64_t pre_batch_stride, pre_group_stride;
-    int32_t P, C, B, ncls, channel, sigmoid;
+    int32_t Pz, Py, Px, C, B, ncls, channel, sigmoid;  // tile extents; TTA members need a cube
     const float* ss;     // [B][C][2]
     float slope;
     const float* wh;     // [ncls][C]
     const float* bh;     // [ncls]
-    const float* gauss;  // [P] gaussian1d(P)
+    const float* gz;     // gaussian1d(Pz), gaussian1d(Py), gaussian1d(Px)
+    const float* gy;
+    const float* gx;
     const TileOrigin* tiles;
     const uint8_t* tta;  // TTA member of each tile (null: none); the output at a goes to tta_source(a)
     float tta_scale;     // 1 / members (the blend adds the members' mean)

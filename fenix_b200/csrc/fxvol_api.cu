@@ -434,6 +434,8 @@ fx_status fx_predict_fxvol(fx_net* net, const char* in_path, const char* out_pat
     return guarded([&]() -> fx_status {
         if (!net || !in_path || !out_path || !o) return abi_error(FX_INVALID_ARGUMENT, "fx_predict_fxvol: null argument");
         if (o->patch % 64 != 0) return abi_error(FX_INVALID_ARGUMENT, "patch must be divisible by 64");
+        if (o->tile[0] || o->tile[1] || o->tile[2])
+            return abi_error(FX_UNSUPPORTED, "fx_predict_fxvol: cubic tiles only (opts.tile must be 0)");
         for (int a = 0; a < 3; ++a)
             if (o->core_org[a] || o->core_ext[a] > 0)
                 return abi_error(FX_UNSUPPORTED, "fx_predict_fxvol: the prediction archive covers the whole input (no crop)");

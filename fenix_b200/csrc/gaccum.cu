@@ -206,6 +206,8 @@ fx_status fx_gaccum_predict_row(fx_gaccum* a, fx_net* net, int64_t zi, const uin
     FX_ABI_TRY
     if (!a || !net || !host_planes || !opts || zi < 0 || zi >= static_cast<int64_t>(a->zs.size()))
         return abi_error(FX_INVALID_ARGUMENT, "fx_gaccum_predict_row: bad argument");
+    if (opts->tile[0] || opts->tile[1] || opts->tile[2])
+        return abi_error(FX_UNSUPPORTED, "fx_gaccum_predict_row: cubic tiles only (opts.tile must be 0)");
     if (opts->patch != a->P || opts->overlap != a->overlap)
         return abi_error(FX_INVALID_ARGUMENT, "fx_gaccum_predict_row: patch / overlap differ from the accumulator's");
     cudaSetDevice(a->dev);
@@ -221,8 +223,8 @@ fx_status fx_gaccum_predict_row(fx_gaccum* a, fx_net* net, int64_t zi, const uin
     cudaError_t e = cudaMemcpyAsync(a->d_slab, host_planes, slab, cudaMemcpyHostToDevice, a->stream);
     if (e != cudaSuccess) return cuda_err(e, "fx_gaccum_predict_row: H2D");
     const int64_t per_row = static_cast<int64_t>(a->ys.size()) * static_cast<int64_t>(a->xs.size());
-    fxh::Status st = net->net.predict_tiles(a->d_slab, z_hi - z_lo, a->ext[1], a->ext[2], z_lo, a->ext[0], opts->patch,
-                                            opts->overlap, opts->channel, opts->sigmoid, opts->batch, zi * per_row,
+    fxh::Status st = net->net.predict_tiles(a->d_slab, z_hi - z_lo, a->ext[1], a->ext[2], z_lo, a->ext[0],
+                                            fxk::TileDims{a->P, a->P, a->P}, opts->overlap, opts->channel, opts->sigmoid, opts->batch, zi * per_row,
                                             (zi + 1) * per_row, a->win[a->cur], a->stream, a->wz0, a->win_planes,
                                             opts->tta, fxh::run_opts(opts));
     if (!st.ok()) return abi_error(st.code, st.msg);

@@ -155,6 +155,8 @@ fx_status fx_predict_volume_multi(fx_net* const* nets, int n, const uint8_t* hos
         if (!nets || n < 1 || !host_vol || !o) return fxh::abi_error(FX_INVALID_ARGUMENT, "fx_predict_volume_multi: null argument");
         if (dz < 1 || dy < 1 || dx < 1) return fxh::abi_error(FX_INVALID_ARGUMENT, "fx_predict_volume_multi: empty volume");
         if (o->patch % 64 != 0) return fxh::abi_error(FX_INVALID_ARGUMENT, "patch must be divisible by 64");
+        if (o->tile[0] || o->tile[1] || o->tile[2])  // z-slab sharding plans cubic tiles
+            return fxh::abi_error(FX_UNSUPPORTED, "fx_predict_volume_multi: cubic tiles only (opts.tile must be 0)");
         for (int i = 0; i < n; ++i) {
             if (!nets[i]) return fxh::abi_error(FX_INVALID_ARGUMENT, "fx_predict_volume_multi: null net");
             if (nets[i]->net.patch() != o->patch)
@@ -224,7 +226,7 @@ fx_status fx_predict_volume_multi(fx_net* const* nets, int n, const uint8_t* hos
                     return;
                 cudaMemcpyAsync(d_vol, host_vol + p.z_lo * plane, static_cast<size_t>(nz * plane), cudaMemcpyHostToDevice, s);
                 cudaMemsetAsync(accs[r], 0, static_cast<size_t>(nz * plane) * 4, s);
-                if ((out = net.predict_tiles(d_vol, nz, dy, dx, p.z_lo, dz, P, o->overlap, o->channel, o->sigmoid,
+                if ((out = net.predict_tiles(d_vol, nz, dy, dx, p.z_lo, dz, fxk::TileDims{P, P, P}, o->overlap, o->channel, o->sigmoid,
                                              o->batch, p.tile_begin, p.tile_end, accs[r], s, 0, -1, o->tta, ro))
                         .code)
                     return;

@@ -95,6 +95,22 @@ Status Net::parse(const WeightMap& wm) {
     while (get("encoder.stages.0.convs." + std::to_string(nconv_) + ".conv.weight")) ++nconv_;
     if (nconv_ < 1) return fail(kDecode, "fxweights: no convs in encoder stage 0");
     F_.clear();
+    // the axes each stage halves, read from the transposed conv that undoes it: its kernel is 2 along
+    // the halved axes and 1 along the others (nnU-Net's per-stage strides, e.g. (1, 2, 2))
+    smask_.assign(S_, 0);
+    for (int s = 1; s < S_; ++s) {
+        const std::string tp = "decoder.transpconvs." + std::to_string(S_ - 1 - s);
+        const HostTensor* w = get(tp + ".weight");
+        if (!w || w->shape.size() != 5) return fail(kDecode, "fxweights: missing or malformed " + tp + ".weight");
+        int m = 0;
+        for (int a = 0; a < 3; ++a) {
+            const int64_t k = w->shape[2 + a];
+            if (k != 1 && k != 2) return fail(kUnsupported, "fxweights: " + tp + " kernel must be 1 or 2 along each axis");
+            if (k == 2) m |= 4 >> a;
+        }
+        if (!m) return fail(kUnsupported, "fxweights: " + tp + " does not upsample");
+        smask_[s] = m;
+    }
     auto conv_layer = [&](const std::string& pre, Layer& L) -> Status {
         const HostTensor* w = get(pre + ".conv.weight");
         const HostTensor* g = get(pre + ".norm.weight");
@@ -119,6 +135,7 @@ Status Net::parse(const WeightMap& wm) {
             if (!st.ok()) return st;
             if (L.Cin != (i == 0 ? prev : L.Cout)) return fail(kDecode, "fxweights: channel mismatch at " + L.name);
             L.stride = (i == 0 && s > 0) ? 2 : 1;
+            L.smask = (i == 0 && s > 0) ? smask_[s] : 0;
             L.kind = (s == 0 && i == 0) ? Layer::kFirst : Layer::kConv;
             L.lin = (i == 0 && s > 0) ? s - 1 : s;
             L.lout = s;
@@ -134,9 +151,7 @@ Status Net::parse(const WeightMap& wm) {
         const HostTensor* w = get(tp + ".weight");
         const HostTensor* b = get(tp + ".bias");
         if (!w || !b) return fail(kDecode, "fxweights: missing " + tp + ".{weight,bias}");
-        if (w->shape.size() != 5 || w->shape[2] != 2 || w->shape[3] != 2 || w->shape[4] != 2)
-            return fail(kUnsupported, "fxweights: " + tp + " must be a 2x2x2 transposed conv");
-        Layer& U = up_[lvl];
+        Layer& U = up_[lvl];  // kernel shape already checked against the stage's mask above
         U.kind = Layer::kUp;
         U.name = tp;
         U.Cin = static_cast<int>(w->shape[0]);
@@ -145,6 +160,7 @@ Status Net::parse(const WeightMap& wm) {
         U.w = w->data;
         U.b = b->data;
         U.stride = 2;
+        U.smask = smask_[lvl + 1];
         U.lin = lvl + 1;
         U.lout = lvl;
         for (int i = 0; i < nconv_; ++i) {
@@ -193,6 +209,7 @@ Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std:
     };
     resenc_ = true;
     enc_.clear();
+    smask_.clear();
     blocks_.clear();
     F_.clear();
     Layer stem;
@@ -225,6 +242,7 @@ Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std:
                 return fail(kDecode, "fxweights: channel mismatch at " + pre);
             c1.kind = c2.kind = Layer::kConv;
             c1.stride = K.stride;
+            c1.smask = K.stride == 2 ? 7 : 0;
             c2.stride = 1;
             c1.lin = K.stride == 2 ? s - 1 : s;
             c1.lout = c2.lin = c2.lout = s;
@@ -238,6 +256,7 @@ Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std:
                 if ((st = conv_layer(pj, pl, 1)).code) return st;
                 pl.kind = Layer::kProj;
                 pl.stride = K.stride;
+                pl.smask = K.stride == 2 ? 7 : 0;
                 pl.lin = c1.lin;
                 pl.lout = s;
                 K.proj = static_cast<int>(enc_.size());
@@ -278,6 +297,7 @@ Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std:
             prev = c1.Cout;
         }
         F_.push_back(prev);
+        smask_.push_back(s > 0 ? 7 : 0);
     }
     nslots_ = slot + 1;  // + the last stage's output (the first transposed conv's input)
     // decoder: transpconvs, one or more convs per stage, seg_layers (as the plain decoder)
@@ -292,7 +312,7 @@ Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std:
         const HostTensor* w = get(tp + ".weight");
         const HostTensor* b = get(tp + ".bias");
         if (!w || !b) return fail(kDecode, "fxweights: missing " + tp + ".{weight,bias}");
-        Layer& U = up_[lvl];
+        Layer& U = up_[lvl];  // kernel shape already checked against the stage's mask above
         U.kind = Layer::kUp;
         U.name = tp;
         U.Cin = static_cast<int>(w->shape[0]);
@@ -301,6 +321,7 @@ Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std:
         U.w = w->data;
         U.b = b->data;
         U.stride = 2;
+        U.smask = 7;
         U.lin = lvl + 1;
         U.lout = lvl;
         for (int i = 0; i < nconv_; ++i) {
@@ -356,8 +377,10 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
         if (L.kind == Layer::kUp) {
             for (int co = 0; co < L.Cout; ++co) {
                 float m = 0.f;
+                const int nph = 1 << __builtin_popcount(static_cast<unsigned>(L.smask));
                 for (int ci = 0; ci < L.Cin; ++ci)
-                    for (int a = 0; a < 8; ++a) m = std::max(m, std::fabs(L.w[(static_cast<size_t>(ci) * L.Cout + co) * 8 + a]));
+                    for (int a = 0; a < nph; ++a)
+                        m = std::max(m, std::fabs(L.w[(static_cast<size_t>(ci) * L.Cout + co) * nph + a]));
                 L.wscale[co] = std::max(m, 1e-8f) / kE4M3Max;
             }
         } else {
@@ -417,13 +440,28 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
                 sp.zP2 = P2;
             }
         } else {
+            // stride 2 along the axes of smask: the input is the phase-split copy (one sub-volume per
+            // parity of the halved axes, each on the output grid); a tap on a halved axis picks the
+            // phase of its parity and shifts by k / 2 - 1, on a full axis it shifts by k - 1
             const int64_t Wp = gout.W + 2, P2 = static_cast<int64_t>(gout.H + 2) * Wp;
+            const int m = L.smask;
             for (int kz = 0; kz < 3; ++kz)
                 for (int ky = 0; ky < 3; ++ky)
                     for (int kx = 0; kx < 3; ++kx) {
-                        const int phi = ((kz & 1) << 2) | ((ky & 1) << 1) | (kx & 1);
-                        const int64_t off = (kz / 2 - 1) * P2 + (ky / 2 - 1) * Wp + (kx / 2 - 1);
-                        sp.taps.push_back({phi, off, kz * 9 + ky * 3 + kx, phi * 2 + kz / 2});
+                        int phi = 0;
+                        int64_t off = 0;
+                        const int k[3] = {kz, ky, kx};
+                        const int64_t step[3] = {P2, Wp, 1};
+                        for (int a = 0; a < 3; ++a) {
+                            if (m & (4 >> a)) {
+                                phi = (phi << 1) | (k[a] & 1);
+                                off += (k[a] / 2 - 1) * step[a];
+                            } else {
+                                off += (k[a] - 1) * step[a];
+                            }
+                        }
+                        const int zkey = (m & 4) ? kz / 2 : kz;  // taps of one z shift share a window
+                        sp.taps.push_back({phi, off, kz * 9 + ky * 3 + kx, phi * 3 + zkey});
                     }
         }
         const Layer* Lp = &L;
@@ -487,13 +525,16 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
         sp.taps.push_back({0, 0, 0, 0});
         const Layer* Lp = &L;
         const bool f8 = fp8;
-        sp.wval = [Lp, f8](int n, int ci, int) {
+        // one output phase per kernel position: weights [Cin][Cout][kz][ky][kx], 2 along the axes of
+        // smask and 1 along the others, so the positions are the phases in z, y, x bit order
+        const int nph = 1 << __builtin_popcount(static_cast<unsigned>(L.smask));
+        sp.wval = [Lp, f8, nph](int n, int ci, int) {
             if (ci >= Lp->Cin) return 0.f;
             const int co = n % Lp->Cout, a = n / Lp->Cout;
-            const float v = Lp->w[(static_cast<size_t>(ci) * Lp->Cout + co) * 8 + a];
+            const float v = Lp->w[(static_cast<size_t>(ci) * Lp->Cout + co) * nph + a];
             return f8 ? v / Lp->wscale[co] : v;
         };
-        sp.N_total = 8 * L.Cout;
+        sp.N_total = nph * L.Cout;
         dp.rowspace = gin;
         if (fp8) {
             colscale.resize(L.Cout);
@@ -614,7 +655,8 @@ Status Net::alloc() {
         if (s < S_ - 1) {
             cat_[s] = static_cast<uint8_t*>(dalloc(2 * bytes));
             const ActGeom gn = level(s + 1);
-            const size_t pbytes = static_cast<size_t>(Bmax_) * (F_[s] / 8) * 8 * gn.gs();
+            const int nph = 1 << __builtin_popcount(static_cast<unsigned>(smask_[s + 1]));
+            const size_t pbytes = static_cast<size_t>(Bmax_) * (F_[s] / 8) * nph * gn.gs();
             ph_[s] = static_cast<uint8_t*>(dalloc(pbytes));
             if (!cat_[s] || !ph_[s]) return fail(kInternal, "cudaMalloc: skip buffers");
             cudaMemset(cat_[s], 0, 2 * bytes);
@@ -669,7 +711,9 @@ Status Net::alloc() {
         return fail(kInternal, "cudaMalloc: control buffers");
     cudaMemset(d_status_, 0, sizeof(uint32_t));
     cudaMemset(d_stat_done_, 0, sizeof(unsigned) * ndone);
-    std::vector<float> g = gaussian1d(P_);
+    std::vector<float> g = gaussian1d(tz_), gy = gaussian1d(ty_), gx = gaussian1d(tx_);
+    g.insert(g.end(), gy.begin(), gy.end());
+    g.insert(g.end(), gx.begin(), gx.end());
     Status st = upload(d_gauss_, g, this, allocs_);
     if (!st.ok()) return st;
     if ((st = upload(d_head_w_, head_w_, this, allocs_)).code) return st;
@@ -677,12 +721,14 @@ Status Net::alloc() {
     return cuda_status(cudaDeviceSynchronize(), "allocation");
 }
 
-Status Net::create(const std::string& path, int patch, int max_batch, int precision, int device) {
-    P_ = patch;
+Status Net::create(const std::string& path, const int tile[3], int max_batch, int precision, int device) {
+    tz_ = tile[0];
+    ty_ = tile[1];
+    tx_ = tile[2];
     Bmax_ = max_batch;
     prec_ = precision;
     dev_ = device;
-    if (patch <= 0 || max_batch <= 0) return fail(kInvalid, "net: patch and max_batch must be positive");
+    if (tz_ <= 0 || ty_ <= 0 || tx_ <= 0 || max_batch <= 0) return fail(kInvalid, "net: tile and max_batch must be positive");
     if (precision < 0 || precision > 2) return fail(kInvalid, "net: precision must be bf16 (0), fp8 (1) or f16 (2)");
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
@@ -703,8 +749,17 @@ Status Net::create(const std::string& path, int patch, int max_batch, int precis
         for (auto* v : {&enc_, &up_, &dec_})
             for (Layer& L : *v) L.idx = k++;
     }
-    const int div = 1 << (S_ - 1);
-    if (P_ % div) return fail(kInvalid, "patch must be divisible by " + std::to_string(div));
+    // the grid of every level: each stage halves the axes of its mask, which must divide evenly
+    lv_.assign(S_, ActGeom{});
+    lv_[0] = {tz_, ty_, tx_};
+    for (int lvl = 1; lvl < S_; ++lvl) {
+        const ActGeom& a = lv_[lvl - 1];
+        const int m = smask_[lvl];
+        if (((m & 4) && a.D % 2) || ((m & 2) && a.H % 2) || ((m & 1) && a.W % 2))
+            return fail(kInvalid, "tile (" + std::to_string(tz_) + ", " + std::to_string(ty_) + ", " + std::to_string(tx_) +
+                                      ") does not halve evenly through the net's " + std::to_string(S_) + " stages");
+        lv_[lvl] = {(m & 4) ? a.D / 2 : a.D, (m & 2) ? a.H / 2 : a.H, (m & 1) ? a.W / 2 : a.W};
+    }
     for (int s = 0; s < S_; ++s)
         if (F_[s] % 16) return fail(kUnsupported, "net: stage features must be multiples of 16");
     if (F_[0] > 64) return fail(kUnsupported, "net: first stage wider than 64 channels");
@@ -728,7 +783,8 @@ Status Net::run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int6
         // algorithmic FLOPs = 2 x MACs: conv 27 Cin Cout Vout, transposed conv Cin Cout Vout
         // (a strided projection counts its AvgPool as 8 taps of the conv it runs as)
         const double taps = L.kind == Layer::kProj ? (L.stride == 2 ? 8.0 : 1.0) : 27.0;
-        ev.flops = L.kind == Layer::kUp ? 2.0 * L.Cin * L.Cout * 8.0 * vin * nb : 2.0 * taps * L.Cin * L.Cout * vout * nb;
+        const double nph = static_cast<double>(1 << __builtin_popcount(static_cast<unsigned>(L.smask)));
+        ev.flops = L.kind == Layer::kUp ? 2.0 * L.Cin * L.Cout * nph * vin * nb : 2.0 * taps * L.Cin * L.Cout * vout * nb;
         ev.optype = q;
         ev.layer = L.idx;
         cudaEventCreate(&ev.a);
@@ -783,7 +839,8 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     const ActGeom& rs = dp.rowspace;
     if ((L.kind == Layer::kConv || L.kind == Layer::kProj) && L.stride == 2) {
         const int64_t ps = gout.gs();
-        for (int phi = 0; phi < 8; ++phi) p.src[phi] = {in_ptr + phi * ps, in_bs, in_gs, gout.rows()};
+        const int nph = 1 << __builtin_popcount(static_cast<unsigned>(L.smask));
+        for (int phi = 0; phi < nph; ++phi) p.src[phi] = {in_ptr + phi * ps, in_bs, in_gs, gout.rows()};
     } else {
         p.src[0] = {in_ptr, in_bs, in_gs, gin.rows()};
     }
@@ -831,6 +888,7 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     p.trace = g_conv_trace;
     if (L.kind == Layer::kUp) {
         p.mode = fxk::kModeUpsample;
+        p.up_mask = L.smask;
         p.bias = dp.bias;
         p.out_type = out_type;
         p.out_qscale = out_qscale;
@@ -894,14 +952,14 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
     if ((st = cuda_status(cudaMemsetAsync(d_sums_, 0, sizeof(unsigned long long) * 2 * nb, s), "memset")).code) return st;
     if (norm_ == 1 && (st = cuda_status(cudaMemsetAsync(d_hist_, 0, sizeof(unsigned) * 256 * nb, s), "memset")).code)
         return st;
-    if ((st = cuda_status(fxk::launch_tile_sums(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, s, norm_ == 1 ? d_hist_ : nullptr),
+    if ((st = cuda_status(fxk::launch_tile_sums(vol, dz, dy, dx, d_tiles, nb, tile(), d_sums_, s, norm_ == 1 ? d_hist_ : nullptr),
                           "tile_sums"))
             .code)
         return st;
-    const int64_t pvox = static_cast<int64_t>(P_) * P_ * P_;
+    const int64_t pvox = tile().count();
     if ((st = cuda_status(fxk::launch_tile_lut(d_sums_, d_hist_, nb, pvox, norm_, d_luts_, nullptr, s), "tile_lut")).code)
         return st;
-    if ((st = cuda_status(fxk::launch_tile_norm(vol, dz, dy, dx, d_tiles, nb, P_, d_sums_, l0_, 2 * g0.gs(), g0.gs(), t16(), nullptr,
+    if ((st = cuda_status(fxk::launch_tile_norm(vol, dz, dy, dx, d_tiles, nb, tile(), d_sums_, l0_, 2 * g0.gs(), g0.gs(), t16(), nullptr,
                                                 s, d_tta, d_luts_),
                           "tile_norm"))
             .code)
@@ -927,11 +985,11 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
         fxk::NormDest d{};
         const ActGeom gn = level(lvl + 1);
         d.ptr = ph_[lvl];
-        d.phase = 1;
+        d.phase = smask_[lvl + 1];
         d.pHp = gn.H + 2;
         d.pWp = gn.W + 2;
         d.phase_stride = gn.gs();
-        d.group_stride = 8 * gn.gs();
+        d.group_stride = (1 << __builtin_popcount(static_cast<unsigned>(smask_[lvl + 1]))) * gn.gs();
         d.batch_stride = static_cast<int64_t>(F_[lvl] / cgof(q)) * d.group_stride;
         d.dtype = q;
         d.qscale = q == fxk::kOpE4M3 ? 1.f / cons.in_scale : 1.f;
@@ -980,7 +1038,7 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
             int64_t ibs, igs;
             if (K.stride == 2) {
                 in1 = ph_[lv - 1];
-                igs = 8 * g.gs();
+                igs = (1 << __builtin_popcount(static_cast<unsigned>(smask_[lv]))) * g.gs();
                 ibs = static_cast<int64_t>(L1.Cin / cgof(q1)) * igs;
             } else {
                 in1 = act_[lv];
@@ -1069,7 +1127,7 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
                     igs = g0.gs();
                 } else if (i == 0) {  // stride 2: phase-split copy of the previous stage's output
                     in = ph_[lv - 1];
-                    igs = 8 * g.gs();
+                    igs = (1 << __builtin_popcount(static_cast<unsigned>(smask_[lv]))) * g.gs();
                     ibs = static_cast<int64_t>(F_[lv - 1] / cgof(q)) * igs;
                 } else {
                     in = act_[lv];
@@ -1120,7 +1178,9 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
                 h.pre = pn_[0];
                 h.pre_batch_stride = pn_bs;
                 h.pre_group_stride = g.gs();
-                h.P = P_;
+                h.Pz = tz_;
+                h.Py = ty_;
+                h.Px = tx_;
                 h.C = F_[0];
                 h.B = nb;
                 h.ncls = ncls_;
@@ -1130,7 +1190,9 @@ Status Net::forward(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, cons
                 h.slope = kSlope;
                 h.wh = d_head_w_;
                 h.bh = d_head_b_;
-                h.gauss = d_gauss_;
+                h.gz = d_gauss_;
+                h.gy = d_gauss_ + tz_;
+                h.gx = d_gauss_ + tz_ + ty_;
                 h.tiles = d_tiles;
                 h.tta = d_tta;
                 h.tta_scale = tta_scale;
@@ -1191,11 +1253,11 @@ Status Net::calibrate(const uint8_t* host_patches, int n) {
     if (prec_ != 1) return fail(kInvalid, "calibrate: net is not fp8");
     if (n < 1) return fail(kInvalid, "calibrate: need at least one patch");
     cudaSetDevice(dev_);
-    const size_t pv = static_cast<size_t>(P_) * P_ * P_;
+    const size_t pv = static_cast<size_t>(tile().count());
     uint8_t* d_vol = static_cast<uint8_t*>(dalloc(pv * Bmax_));
     if (!d_vol) return fail(kInternal, "cudaMalloc: calibration patches");
     std::vector<fxk::TileOrigin> org(Bmax_);
-    for (int b = 0; b < Bmax_; ++b) org[b] = {static_cast<int64_t>(b) * P_, 0, 0};
+    for (int b = 0; b < Bmax_; ++b) org[b] = {static_cast<int64_t>(b) * tz_, 0, 0};
     fxk::TileOrigin* d_org = nullptr;
     Status st = upload(d_org, org, this, allocs_);
     if (!st.ok()) return st;
@@ -1206,7 +1268,7 @@ Status Net::calibrate(const uint8_t* host_patches, int n) {
                               "H2D calibration"))
                 .code)
             return st;
-        if ((st = forward(d_vol, static_cast<int64_t>(nb) * P_, P_, P_, d_org, nb, 1, 0, nullptr, nullptr, true,
+        if ((st = forward(d_vol, static_cast<int64_t>(nb) * tz_, ty_, tx_, d_org, nb, 1, 0, nullptr, nullptr, true,
                           stream_))
                 .code)
             return st;
@@ -1287,7 +1349,7 @@ Status Net::calibrate_schedule(const uint8_t* host_patches, int n, double min_di
     Status st;
     if (!calibrated_ && (st = calibrate(host_patches, n)).code) return st;
     cudaSetDevice(dev_);
-    const size_t pv = static_cast<size_t>(P_) * P_ * P_;
+    const size_t pv = static_cast<size_t>(tile().count());
     auto* d_vol = static_cast<uint8_t*>(dalloc(pv * n));
     auto* d_ref = static_cast<float*>(dalloc(sizeof(float) * pv * n));
     auto* d_cur = static_cast<float*>(dalloc(sizeof(float) * pv * n));
@@ -1295,7 +1357,7 @@ Status Net::calibrate_schedule(const uint8_t* host_patches, int n, double min_di
     auto* d_org = static_cast<fxk::TileOrigin*>(dalloc(sizeof(fxk::TileOrigin) * Bmax_));
     if (!d_vol || !d_ref || !d_cur || !d_cmp || !d_org) return fail(kInternal, "cudaMalloc: schedule search buffers");
     std::vector<fxk::TileOrigin> org(Bmax_);
-    for (int b = 0; b < Bmax_; ++b) org[b] = {static_cast<int64_t>(b) * P_, 0, 0};
+    for (int b = 0; b < Bmax_; ++b) org[b] = {static_cast<int64_t>(b) * tz_, 0, 0};
     cudaMemcpyAsync(d_org, org.data(), sizeof(fxk::TileOrigin) * Bmax_, cudaMemcpyHostToDevice, stream_);
     cudaMemcpyAsync(d_vol, host_patches, pv * n, cudaMemcpyHostToDevice, stream_);
     const int nl = static_cast<int>(enc_.size() + up_.size() + dec_.size());
@@ -1317,7 +1379,7 @@ Status Net::calibrate_schedule(const uint8_t* host_patches, int n, double min_di
         if (!r.ok()) return r;
         for (int i0 = 0; i0 < n; i0 += Bmax_) {
             const int nb = std::min(Bmax_, n - i0);
-            if ((r = forward(d_vol + pv * i0, static_cast<int64_t>(nb) * P_, P_, P_, d_org, nb, 1, sig, nullptr,
+            if ((r = forward(d_vol + pv * i0, static_cast<int64_t>(nb) * tz_, ty_, tx_, d_org, nb, 1, sig, nullptr,
                              out + pv * i0, false, stream_))
                     .code)
                 return r;
@@ -1430,7 +1492,8 @@ std::vector<double> Net::layer_flops() const {
             const ActGeom gi = level(L.lin), go = level(L.lout);
             const double vin = static_cast<double>(gi.D) * gi.H * gi.W, vout = static_cast<double>(go.D) * go.H * go.W;
             const double taps = L.kind == Layer::kProj ? (L.stride == 2 ? 8.0 : 1.0) : 27.0;
-            out.push_back(L.kind == Layer::kUp ? 2.0 * L.Cin * L.Cout * 8.0 * vin : 2.0 * taps * L.Cin * L.Cout * vout);
+            const double nph = static_cast<double>(1 << __builtin_popcount(static_cast<unsigned>(L.smask)));
+            out.push_back(L.kind == Layer::kUp ? 2.0 * L.Cin * L.Cout * nph * vin : 2.0 * taps * L.Cin * L.Cout * vout);
         }
     return out;
 }
@@ -1471,16 +1534,17 @@ Status Net::workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint
 }
 
 Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
-                          int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
+                          fxk::TileDims tl, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
                           int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin, int64_t acc_dz,
                           int tta, const RunOpts& ro) {
-    if (patch != P_) return fail(kInvalid, "predict: patch differs from the net's patch");
+    if (tl.z != tz_ || tl.y != ty_ || tl.x != tx_) return fail(kInvalid, "predict: tile differs from the net's tile");
+    if (tta > 1 && !patch()) return fail(kUnsupported, "predict: TTA members permute axes and need a cubic tile");
     if (ro.norm < 0 || ro.norm > 2) return fail(kInvalid, "predict: norm must be zscore, pct_minmax or unit255");
     if (batch < 1) batch = 1;
     batch = std::min(batch, Bmax_);
     if (full_dz <= 0) full_dz = dz;
-    const auto zs = tile_starts(full_dz, P_, overlap), ys = tile_starts(dy, P_, overlap),
-               xs = tile_starts(dx, P_, overlap);
+    const auto zs = tile_starts(full_dz, tz_, overlap), ys = tile_starts(dy, ty_, overlap),
+               xs = tile_starts(dx, tx_, overlap);
     const int64_t total = static_cast<int64_t>(zs.size()) * ys.size() * xs.size();
     if (tile_end < 0 || tile_end > total) tile_end = total;
     if (tile_begin < 0) tile_begin = 0;
@@ -1503,12 +1567,12 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
         const int64_t zi = i / (static_cast<int64_t>(xs.size()) * ys.size());
         const int64_t z0 = zs[zi], y0 = ys[yi], x0 = xs[xi];
         // a tile that does not reach the core contributes nothing (src/ml/infer.hpp:532-543)
-        if (cropped && !(z0 < co[0] + ce[0] && z0 + P_ > co[0] && y0 < co[1] + ce[1] && y0 + P_ > co[1] &&
-                         x0 < co[2] + ce[2] && x0 + P_ > co[2]))
+        if (cropped && !(z0 < co[0] + ce[0] && z0 + tz_ > co[0] && y0 < co[1] + ce[1] && y0 + ty_ > co[1] &&
+                         x0 < co[2] + ce[2] && x0 + tx_ > co[2]))
             continue;
-        if (ro.filter && !ro.filter(z0, y0, x0, P_, ro.filter_user)) continue;
+        if (ro.filter && !ro.filter(z0, y0, x0, tz_, ro.filter_user)) continue;
         const int64_t zl = z0 - z_origin;  // slab-local
-        if (zl < 0 || (zl + P_ > dz && full_dz >= P_))
+        if (zl < 0 || (zl + tz_ > dz && full_dz >= tz_))
             return fail(kInvalid, "predict: tile " + std::to_string(i) + " is outside the z-slab");
         cand.push_back({zl, y0, x0});
     }
@@ -1527,9 +1591,9 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
         if (st.ok()) st = cuda_status(cudaMemsetAsync(d_s, 0, sizeof(unsigned long long) * 2 * nc, s), "memset");
         for (size_t i0 = 0; st.ok() && i0 < nc; i0 += 65535) {
             const int n = static_cast<int>(std::min<size_t>(65535, nc - i0));
-            st = cuda_status(fxk::launch_tile_sums(d_vol, dz, dy, dx, d_org + i0, n, P_, d_s + 2 * i0, s), "tile_sums");
+            st = cuda_status(fxk::launch_tile_sums(d_vol, dz, dy, dx, d_org + i0, n, tile(), d_s + 2 * i0, s), "tile_sums");
             if (st.ok())
-                st = cuda_status(fxk::launch_tile_lut(d_s + 2 * i0, nullptr, n, static_cast<int64_t>(P_) * P_ * P_, 2,
+                st = cuda_status(fxk::launch_tile_lut(d_s + 2 * i0, nullptr, n, tile().count(), 2,
                                                       d_lut + 256 * i0, d_flag + i0, s),
                                  "tile_lut");
         }

@@ -70,6 +70,10 @@ struct Layer {
     enum Kind { kConv, kFirst, kUp, kProj } kind = kConv;
     std::string name;
     int Cin = 0, Cout = 0, stride = 1;
+    // strided convs and transposed convs: the axes with factor 2 (bit 2 z, bit 1 y, bit 0 x). The
+    // surface nets halve every axis (7); the layer-stack (ink) net halves y and x only in its
+    // first strided stages (3).
+    int smask = 0;
     int lin = 0, lout = 0;            // resolution levels of input and output
     std::vector<float> w;             // conv: [Cout][Cin][27]; up: [Cin][Cout][8]
     std::vector<float> b;             // up: bias (conv biases cancel inside InstanceNorm)
@@ -137,7 +141,8 @@ struct RunOpts {
 class Net {
   public:
     ~Net();
-    Status create(const std::string& path, int patch, int max_batch, int precision, int device);
+    // tile = (z, y, x) extents of one tile; a cube for the surface nets
+    Status create(const std::string& path, const int tile[3], int max_batch, int precision, int device);
     Status calibrate(const uint8_t* host_patches, int n);
     // Install per-layer input scales (act_scales() order) and build the e4m3 programs.
     Status set_act_scales(const float* scales, int n);
@@ -156,7 +161,7 @@ class Net {
     // With acc_dz >= 0, d_acc is a window of acc_dz planes starting at volume plane acc_z_origin
     // (contributions outside it are dropped), independent of the input slab.
     Status predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
-                         int patch, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
+                         fxk::TileDims tile, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
                          int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin = 0,
                          int64_t acc_dz = -1, int tta = 0, const RunOpts& ro = RunOpts{});
     // The normalisation forwards use (0 zscore, 1 pct_minmax, 2 unit255); calibration uses it too.
@@ -164,7 +169,10 @@ class Net {
     // Device workspace for whole-volume calls: grown on demand, kept for the net's lifetime.
     Status workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint8_t** vol, float** acc, uint8_t** out);
 
-    int patch() const { return P_; }
+    // the side of a cubic tile, 0 for an anisotropic one
+    int patch() const { return tz_ == ty_ && ty_ == tx_ ? tz_ : 0; }
+    fxk::TileDims tile() const { return {tz_, ty_, tx_}; }
+    const std::vector<int>& stage_masks() const { return smask_; }
     int max_batch() const { return Bmax_; }
     int classes() const { return ncls_; }
     const std::vector<int>& features() const { return F_; }
@@ -225,10 +233,13 @@ class Net {
     Status finalize_in(Layer& L, int nb, cudaStream_t s);
     Status set_scales_from_amax();
     int layer_q(const Layer& L, bool calib) const;
-    ActGeom level(int s) const { return {P_ >> s, P_ >> s, P_ >> s}; }
+    ActGeom level(int s) const { return lv_[static_cast<size_t>(s)]; }
     void* dalloc(size_t bytes);
 
-    int P_ = 0, Bmax_ = 0, ncls_ = 2, prec_ = 0, dev_ = 0, S_ = 0, nconv_ = 2, sm_count_ = 148;
+    int tz_ = 0, ty_ = 0, tx_ = 0;  // tile extents
+    int Bmax_ = 0, ncls_ = 2, prec_ = 0, dev_ = 0, S_ = 0, nconv_ = 2, sm_count_ = 148;
+    std::vector<int> smask_;        // per stage: the axes its first conv halves (stage 0: none)
+    std::vector<ActGeom> lv_;       // grid of each resolution level
     std::vector<int> F_;
     std::vector<Layer> enc_;  // S * nconv, stage-major
     std::vector<Layer> up_;   // S-1, index = level
@@ -256,7 +267,7 @@ class Net {
     double* d_stat_work_ = nullptr;  // InstanceNorm slice sums [Bmax][kMaxStatSlices][Cmax][2]
     unsigned* d_stat_done_ = nullptr;  // slice counters [Bmax][Cmax / 32], zero between launches
     std::vector<float> amax_;
-    float* d_gauss_ = nullptr;
+    float* d_gauss_ = nullptr;  // gaussian1d(tz), gaussian1d(ty), gaussian1d(tx) back to back
     uint32_t* d_status_ = nullptr;
     fxk::TileOrigin* d_tiles_ = nullptr;
     uint8_t* d_tta_ = nullptr;  // TTA member of each entry of d_tiles_
@@ -280,6 +291,8 @@ struct fx_net {
 namespace fxh {
 // fx_infer_opts -> the driver's per-call options, and the output crop box it asks for (capi.cu).
 RunOpts run_opts(const fx_infer_opts* o);
+// The call's tile: opts.tile, or the cube of side opts.patch (divisible by 64); sets the error on failure.
+fx_status opts_tile(const fx_infer_opts* o, fxk::TileDims* t);
 void crop_box(const fx_infer_opts* o, const int64_t d[3], int64_t co[3], int64_t ce[3]);
 // fx_predict_volume's device part (capi.cu), shared with the .fxvol entry points.
 fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx,

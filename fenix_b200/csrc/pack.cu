@@ -43,8 +43,7 @@ __global__ void pack_kernel(const float* __restrict__ x, int B, int C, int D, in
         const int zp = zz + 1, yp = yy + 1, xp = xx + 1;
         int64_t off;
         if (phase) {
-            const int phi = ((zp & 1) << 2) | ((yp & 1) << 1) | (xp & 1);
-            off = phi * ps + ((static_cast<int64_t>(zp >> 1) * pHp + (yp >> 1)) * pWp + (xp >> 1)) * 16;
+            off = phase_cell_offset(phase, zp, yp, xp, pHp, pWp, ps);
         } else {
             off = ((static_cast<int64_t>(zp) * (H + 2) + yp) * (W + 2) + xp) * 16;
         }

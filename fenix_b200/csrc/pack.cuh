@@ -8,8 +8,8 @@
 namespace fxk {
 
 // f32 [B][C][D][H][W] -> padded group planes of OpType `dtype` (e4m3 values are x*qscale). With
-// `phase`, writes the stride-2 phase-split copy (sub-volume padded dims pHp x pWp,
-// `phase_stride` bytes apart). Channels >= C inside the last group are written as zero.
+// `phase` != 0, writes the stride-2 phase-split copy over the axes of that mask (bit 2 z, bit 1 y,
+// bit 0 x; sub-volume padded dims pHp x pWp, `phase_stride` bytes apart). Channels >= C inside the last group are written as zero.
 cudaError_t launch_pack(const float* x, int B, int C, int D, int H, int W, uint8_t* out, int64_t batch_stride,
                         int64_t group_stride, int dtype, float qscale, int phase, int pHp, int pWp,
                         int64_t phase_stride, cudaStream_t s);

@@ -330,6 +330,26 @@ __device__ __forceinline__ uint4 pack_cell16(const float* v, int optype) {
     }
     return w;
 }
+// Byte offset of padded voxel (zp, yp, xp)'s cell in a stride-2 conv's phase-split copy: one
+// sub-volume per parity of the axes in mask m (bit 2 z, bit 1 y, bit 0 x), phase index = those
+// parities in z, y, x order, each sub-volume padded pHp x pWp rows (the conv's output grid + 2)
+// and ps bytes apart; a halved axis indexes by p >> 1, a full one by p.
+__device__ __forceinline__ int64_t phase_cell_offset(int m, int zp, int yp, int xp, int pHp, int pWp, int64_t ps) {
+    int phi = 0;
+    if (m & 4) {
+        phi = zp & 1;
+        zp >>= 1;
+    }
+    if (m & 2) {
+        phi = (phi << 1) | (yp & 1);
+        yp >>= 1;
+    }
+    if (m & 1) {
+        phi = (phi << 1) | (xp & 1);
+        xp >>= 1;
+    }
+    return phi * ps + ((static_cast<int64_t>(zp) * pHp + yp) * pWp + xp) * 16;
+}
 // v rounded to the 16-bit operand type (round to nearest; f16 saturated as pack_f16x2 does).
 __device__ __forceinline__ float round16(float v, int optype) {
     if (optype == kOpF16) return __half2float(__float2half_rn(fminf(fmaxf(v, -65504.f), 65504.f)));

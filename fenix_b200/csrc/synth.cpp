@@ -151,3 +151,86 @@ extern "C" int fx_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx,
     }
     return 0;
 }
+
+namespace {
+// Normalised Gaussian weights exp(-i^2 / 2 sigma^2), i in [-r, r], r = ceil(3 sigma) (r = 0: {1}).
+std::vector<float> gauss_taps(double sigma) {
+    const int r = sigma > 0 ? static_cast<int>(std::ceil(3.0 * sigma)) : 0;
+    std::vector<float> k(2 * r + 1, 1.f);
+    if (!r) return k;
+    double s = 0;
+    for (int i = -r; i <= r; ++i) s += std::exp(-0.5 * i * i / (sigma * sigma));
+    for (int i = -r; i <= r; ++i) k[i + r] = static_cast<float>(std::exp(-0.5 * i * i / (sigma * sigma)) / s);
+    return k;
+}
+
+double sum_sq(const std::vector<float>& k) {
+    double s = 0;
+    for (float v : k) s += static_cast<double>(v) * v;
+    return s;
+}
+
+// One separable pass over rows of n elements spaced `step` apart: dst[i] = sum_j k[j] src[clamp(i + j - r)].
+void filter_line(const float* src, float* dst, int64_t n, int64_t step, const std::vector<float>& k) {
+    const int r = static_cast<int>(k.size() / 2);
+    for (int64_t i = 0; i < n; ++i) {
+        float s = 0.f;
+        for (int j = -r; j <= r; ++j) s += k[j + r] * src[std::clamp<int64_t>(i + j, 0, n - 1) * step];
+        dst[i * step] = s;
+    }
+}
+}  // namespace
+
+extern "C" int fx_synth_papyrus(uint8_t* out, uint8_t* ink, int64_t dz, int64_t dy, int64_t dx,
+                                const fx_papyrus_params* prm, uint64_t seed, int64_t stack) {
+    if (!out || !prm || dz < 1 || dy < 1 || dx < 1 || stack < 0 || prm->sigma_z < 0 || prm->sigma_y < 0 ||
+        prm->sigma_x < 0 || prm->ink_sigma < 0 || !(prm->ink_fraction >= 0 && prm->ink_fraction <= 1))
+        return 1;
+    const auto kz = gauss_taps(prm->sigma_z), ky = gauss_taps(prm->sigma_y), kx = gauss_taps(prm->sigma_x);
+    const auto ki = gauss_taps(prm->ink_sigma);
+    const int64_t plane = dy * dx, n = dz * plane;
+    std::vector<float> a(static_cast<size_t>(n)), b(static_cast<size_t>(n));
+    // texture noise, then x and y passes per layer
+    parallel_rows(dz, [&](int64_t z) {
+        float* p = a.data() + z * plane;
+        float* q = b.data() + z * plane;
+        for (int64_t y = 0; y < dy; ++y) {
+            Pcg rng(seed ^ 0x5EED0F1B4E5ull, static_cast<uint64_t>((stack * dz + z) * dy + y) + 0x2545F4914F6CDD1Dull);
+            for (int64_t x = 0; x < dx; ++x) p[y * dx + x] = rng.normal();
+        }
+        for (int64_t y = 0; y < dy; ++y) filter_line(p + y * dx, q + y * dx, dx, 1, kx);
+        for (int64_t x = 0; x < dx; ++x) filter_line(q + x, p + x, dy, dx, ky);
+    });
+    // z pass
+    parallel_rows(dy, [&](int64_t y) {
+        for (int64_t x = 0; x < dx; ++x) filter_line(a.data() + y * dx + x, b.data() + y * dx + x, dz, plane, kz);
+    });
+    // ink plane: noise, 2D filter, the top floor(fraction * dy * dx) columns
+    std::vector<float> f(static_cast<size_t>(plane)), g(static_cast<size_t>(plane));
+    for (int64_t y = 0; y < dy; ++y) {
+        Pcg rng(seed ^ 0x1A4B1075ull, static_cast<uint64_t>(stack * dy + y) + 0x9E3779B97F4A7C15ull);
+        for (int64_t x = 0; x < dx; ++x) f[y * dx + x] = rng.normal();
+    }
+    for (int64_t y = 0; y < dy; ++y) filter_line(f.data() + y * dx, g.data() + y * dx, dx, 1, ki);
+    for (int64_t x = 0; x < dx; ++x) filter_line(g.data() + x, f.data() + x, dy, dx, ki);
+    const int64_t kink = static_cast<int64_t>(std::floor(prm->ink_fraction * static_cast<double>(plane)));
+    std::vector<uint8_t> mask(static_cast<size_t>(plane), 0);
+    if (kink > 0) {
+        std::vector<float> srt(f);
+        std::nth_element(srt.begin(), srt.begin() + (kink - 1), srt.end(), std::greater<float>());
+        const float thr = srt[static_cast<size_t>(kink - 1)];
+        for (int64_t i = 0; i < plane; ++i) mask[i] = f[i] >= thr ? 1 : 0;
+    }
+    if (ink) std::copy(mask.begin(), mask.end(), ink);
+    const float scale = static_cast<float>(prm->sd / std::sqrt(sum_sq(kz) * sum_sq(ky) * sum_sq(kx)));
+    const float mean = static_cast<float>(prm->mean), delta = static_cast<float>(prm->ink_delta);
+    parallel_rows(dz, [&](int64_t z) {
+        for (int64_t i = 0; i < plane; ++i) {
+            float s = mean + scale * b[z * plane + i];
+            if (mask[i]) s += delta;
+            s = std::min(255.f, std::max(0.f, s));
+            out[z * plane + i] = static_cast<uint8_t>(std::floor(s + 0.5f));
+        }
+    });
+    return 0;
+}

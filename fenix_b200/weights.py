@@ -18,9 +18,14 @@ from pathlib import Path
 
 import numpy as np
 
-# BASELINE networks (features per stage)
+# Benchmark networks (features per stage)
 CONFIG1_FEATURES = (16, 32, 64, 128)           # 4-stage, 2 classes
 CONFIG2_FEATURES = (32, 64, 128, 256, 320)     # 5-stage nnU-Net style, 2 classes
+# The layer-stack (wide-ink) net: 4 stages, 1 class + sigmoid, the first two strided stages halve y
+# and x only (stride (1, 2, 2)), the last halves all three axes; 64 x 256 x 256 tiles
+INK_FEATURES = (64, 128, 256, 512)
+INK_STRIDES = ((1, 1, 1), (1, 2, 2), (1, 2, 2), (2, 2, 2))
+INK_TILE = (64, 256, 256)
 
 
 def write_fxweights(path: str | Path, tensors: dict[str, np.ndarray]) -> None:
@@ -75,8 +80,10 @@ def read_fxweights(path: str | Path) -> dict[str, np.ndarray]:
     return out
 
 
-def plain_unet_params(features, nconv: int = 2, ncls: int = 2, seed: int = 0) -> dict[str, np.ndarray]:
-    """Seeded random init of the plain UNet.
+def plain_unet_params(features, nconv: int = 2, ncls: int = 2, seed: int = 0, strides=None) -> dict[str, np.ndarray]:
+    """Seeded random init of the plain UNet. ``strides`` = per stage (z, y, x) stride of its first
+    conv, each 1 or 2 (stage 0: (1, 1, 1)); None = 2 on every axis after stage 0. A stage's
+    transposed conv has kernel = stride = that stage's stride, as nnU-Net builds it.
 
     Conv and transposed-conv weights are Kaiming-normal (torch.nn.init.kaiming_normal_ with
     a=1e-2, fan_in, leaky_relu gain, the nnU-Net convention) drawn from torch's CPU generator
@@ -98,6 +105,11 @@ def plain_unet_params(features, nconv: int = 2, ncls: int = 2, seed: int = 0) ->
 
     P: dict[str, np.ndarray] = {}
     S = len(features)
+    if strides is None:
+        strides = [(1, 1, 1)] + [(2, 2, 2)] * (S - 1)
+    strides = [tuple(int(v) for v in st) for st in strides]
+    if len(strides) != S or strides[0] != (1, 1, 1) or any(v not in (1, 2) for st in strides for v in st):
+        raise ValueError("strides: one (z, y, x) triple of 1 / 2 per stage, stage 0 = (1, 1, 1)")
     prev = 1
     for s in range(S):
         for i in range(nconv):
@@ -111,8 +123,9 @@ def plain_unet_params(features, nconv: int = 2, ncls: int = 2, seed: int = 0) ->
         prev = features[s]
     for t in range(S - 1):
         below, skipc = features[S - 1 - t], features[S - 2 - t]
-        # torch computes a ConvTranspose3d weight's fan_in from dim 1: Cout * 8
-        P[f"decoder.transpconvs.{t}.weight"] = kaiming((below, skipc, 2, 2, 2), skipc * 8)
+        # torch computes a ConvTranspose3d weight's fan_in from dim 1: Cout * prod(kernel)
+        k = strides[S - 1 - t]
+        P[f"decoder.transpconvs.{t}.weight"] = kaiming((below, skipc) + k, skipc * k[0] * k[1] * k[2])
         P[f"decoder.transpconvs.{t}.bias"] = small(skipc)
         for i in range(nconv):
             cin = 2 * skipc if i == 0 else skipc
@@ -126,8 +139,8 @@ def plain_unet_params(features, nconv: int = 2, ncls: int = 2, seed: int = 0) ->
     return P
 
 
-def make_plain_unet(path: str | Path, features, nconv: int = 2, ncls: int = 2, seed: int = 0) -> Path:
-    write_fxweights(path, plain_unet_params(features, nconv, ncls, seed))
+def make_plain_unet(path: str | Path, features, nconv: int = 2, ncls: int = 2, seed: int = 0, strides=None) -> Path:
+    write_fxweights(path, plain_unet_params(features, nconv, ncls, seed, strides))
     return Path(path)
 
 

@@ -93,6 +93,12 @@ typedef struct fx_infer_opts {
     int64_t core_ext[3]; /* <= 0 along an axis: to the end of the input */
     fx_tile_filter_fn tile_filter; /* NULL: every tile */
     void* tile_filter_user;
+    int tile[3]; /* per-axis tile (z, y, x) for nets built by fx_net_create_tiled; all 0: the cube of
+                    side `patch`, which then must be divisible by 64 as in the reference
+                    (src/ml/infer.hpp:459). The reference tiles cubes only; an anisotropic tile is
+                    the layer-stack (wide-ink) workload's 64 x 256 x 256, stepped per axis by
+                    (int64)(tile[a] * (1 - overlap)) with a Gaussian of sigma tile[a] / 8 per axis.
+                    The tile filter's `patch` argument is then tile[0]. TTA needs a cube. */
 } fx_infer_opts;
 
 typedef struct fx_net fx_net;
@@ -114,9 +120,18 @@ int fx_device_count(void);
  *                     task_decoders.<task>.* (BasicBlockD with AvgPool + 1x1 projection skips, scSE). */
 fx_status fx_net_create(const char* fxweights_path, int patch, int max_batch, fx_precision precision, int device,
                         fx_net** out);
+/* The same for a tile of tile[0] x tile[1] x tile[2] (z, y, x) voxels. A stage downsamples only the
+ * axes its stride-2 conv strides (read from the decoder's transposed-conv kernel shape, e.g.
+ * (1, 2, 2) for a y/x-only stage); every level's extent must halve evenly. No reference
+ * counterpart: the reference's predict path tiles cubes (src/ml/infer.hpp:39, 459). */
+fx_status fx_net_create_tiled(const char* fxweights_path, const int tile[3], int max_batch, fx_precision precision,
+                              int device, fx_net** out);
 void fx_net_destroy(fx_net* net);
-/* Static net shape, like TrtNet's batch()/patch()/classes(). */
+/* Static net shape, like TrtNet's batch()/patch()/classes(). fx_net_patch is 0 for a non-cubic tile;
+ * fx_net_tile writes (z, y, x) and the per-stage stride masks (bit 2 z, bit 1 y, bit 0 x; stage 0's
+ * is 0) into masks[0..cap) when masks is not NULL, returning the stage count. */
 int fx_net_patch(const fx_net* net);
+int fx_net_tile(const fx_net* net, int tile[3], int* masks, int cap);
 int fx_net_max_batch(const fx_net* net);
 int fx_net_classes(const fx_net* net);
 int fx_net_features(const fx_net* net, int* out, int cap); /* returns the stage count */

@@ -59,27 +59,33 @@ void fxo_weight_profile(const float* g, int patch, const int64_t* starts, int64_
 /* ---- patch fill + z-score: src/ml/inference.cpp:309-321, src/ml/infer.hpp:350-385 ----------- */
 static int64_t clampi(int64_t v, int64_t lo, int64_t hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
-void fxo_fill_patch_u8(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, int64_t z0, int64_t y0, int64_t x0,
-                       int P, float* out) {
+void fxo_fill_tile_u8(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, int64_t z0, int64_t y0, int64_t x0,
+                      int tz, int ty, int tx, float* out) {
 #pragma omp parallel for
-    for (int z = 0; z < P; ++z)
-        for (int y = 0; y < P; ++y)
-            for (int x = 0; x < P; ++x) {
+    for (int z = 0; z < tz; ++z)
+        for (int y = 0; y < ty; ++y)
+            for (int x = 0; x < tx; ++x) {
                 const int64_t zz = clampi(z0 + z, 0, dz - 1), yy = clampi(y0 + y, 0, dy - 1),
                               xx = clampi(x0 + x, 0, dx - 1);
-                out[((int64_t)z * P + y) * P + x] = (float)vol[(zz * dy + yy) * dx + xx];
+                out[((int64_t)z * ty + y) * tx + x] = (float)vol[(zz * dy + yy) * dx + xx];
             }
 }
 
-void fxo_norm_patch_zscore(float* x, int P) {
-    const int64_t PN = (int64_t)P * P * P;
-    double* psum = (double*)calloc((size_t)P, sizeof(double));
-    double* psq = (double*)calloc((size_t)P, sizeof(double));
+void fxo_fill_patch_u8(const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, int64_t z0, int64_t y0, int64_t x0,
+                       int P, float* out) {
+    fxo_fill_tile_u8(vol, dz, dy, dx, z0, y0, x0, P, P, P, out);
+}
+
+void fxo_norm_tile_zscore(float* x, int tz, int ty, int tx) {
+    const int64_t PN = (int64_t)tz * ty * tx;
+    const int64_t pl = (int64_t)ty * tx;
+    double* psum = (double*)calloc((size_t)tz, sizeof(double));
+    double* psq = (double*)calloc((size_t)tz, sizeof(double));
 #pragma omp parallel for
-    for (int z = 0; z < P; ++z) {
+    for (int z = 0; z < tz; ++z) {
         double ls = 0.0, lq = 0.0;
-        const float* row = x + (int64_t)z * P * P;
-        for (int i = 0; i < P * P; ++i) {
+        const float* row = x + (int64_t)z * pl;
+        for (int64_t i = 0; i < pl; ++i) {
             const double v = row[i];
             ls += v;
             lq += v * v;
@@ -88,7 +94,7 @@ void fxo_norm_patch_zscore(float* x, int P) {
         psq[z] = lq;
     }
     double sum = 0.0, sq = 0.0;
-    for (int z = 0; z < P; ++z) {
+    for (int z = 0; z < tz; ++z) {
         sum += psum[z];
         sq += psq[z];
     }
@@ -103,10 +109,12 @@ void fxo_norm_patch_zscore(float* x, int P) {
     for (int64_t i = 0; i < PN; ++i) x[i] = (float)((x[i] - mean) / sd);
 }
 
-/* ---- conv3d 3x3x3, zero padding 1, stride 1|2 (torch.nn.Conv3d semantics) ------------------- */
-void fxo_conv3d(const float* x, int B, int Cin, int D, int H, int W, const float* w, const float* bias, int Cout,
-                int stride, float* y) {
-    const int Do = (D + 2 - 3) / stride + 1, Ho = (H + 2 - 3) / stride + 1, Wo = (W + 2 - 3) / stride + 1;
+void fxo_norm_patch_zscore(float* x, int P) { fxo_norm_tile_zscore(x, P, P, P); }
+
+/* ---- conv3d 3x3x3, zero padding 1, stride 1|2 per axis (torch.nn.Conv3d semantics) -------- */
+void fxo_conv3d_s(const float* x, int B, int Cin, int D, int H, int W, const float* w, const float* bias, int Cout,
+                  int sz, int sy, int sx, float* y) {
+    const int Do = (D + 2 - 3) / sz + 1, Ho = (H + 2 - 3) / sy + 1, Wo = (W + 2 - 3) / sx + 1;
     const int64_t vin = (int64_t)D * H * W, vout = (int64_t)Do * Ho * Wo;
 #pragma omp parallel for collapse(2) schedule(dynamic)
     for (int b = 0; b < B; ++b)
@@ -121,20 +129,20 @@ void fxo_conv3d(const float* x, int B, int Cin, int D, int H, int W, const float
                         for (int kx = 0; kx < 3; ++kx) {
                             const float wv = w[(((int64_t)co * Cin + ci) * 3 + kz) * 9 + ky * 3 + kx];
                             for (int zo = 0; zo < Do; ++zo) {
-                                const int zi = zo * stride - 1 + kz;
+                                const int zi = zo * sz - 1 + kz;
                                 if (zi < 0 || zi >= D) continue;
                                 for (int yo_ = 0; yo_ < Ho; ++yo_) {
-                                    const int yi = yo_ * stride - 1 + ky;
+                                    const int yi = yo_ * sy - 1 + ky;
                                     if (yi < 0 || yi >= H) continue;
                                     const float* xr = xi + ((int64_t)zi * H + yi) * W;
                                     float* yr = yo + ((int64_t)zo * Ho + yo_) * Wo;
-                                    if (stride == 1) {
+                                    if (sx == 1) {
                                         const int lo = kx == 0 ? 1 : 0, hi = kx == 2 ? Wo - 1 : Wo;
                                         const float* xs = xr + kx - 1;
                                         for (int xo = lo; xo < hi; ++xo) yr[xo] += wv * xs[xo];
                                     } else {
                                         for (int xo = 0; xo < Wo; ++xo) {
-                                            const int xx = xo * 2 - 1 + kx;
+                                            const int xx = xo * sx - 1 + kx;
                                             if (xx >= 0 && xx < W) yr[xo] += wv * xr[xx];
                                         }
                                     }
@@ -145,6 +153,11 @@ void fxo_conv3d(const float* x, int B, int Cin, int D, int H, int W, const float
             if (bv != 0.0f)
                 for (int64_t i = 0; i < vout; ++i) yo[i] += bv;
         }
+}
+
+void fxo_conv3d(const float* x, int B, int Cin, int D, int H, int W, const float* w, const float* bias, int Cout,
+                int stride, float* y) {
+    fxo_conv3d_s(x, B, Cin, D, H, W, w, bias, Cout, stride, stride, stride, y);
 }
 
 /* ---- InstanceNorm3d(affine, eps) + LeakyReLU: resenc_unet.hpp:35-52 ------------------------- */
@@ -174,11 +187,12 @@ void fxo_instance_norm_act(float* x, int B, int C, int64_t S, const float* gamma
         }
 }
 
-/* ---- ConvTranspose3d(k=2, s=2) with bias: resenc_unet.hpp:211 ---------------------------- */
-void fxo_conv_transpose2(const float* x, int B, int Cin, int D, int H, int W, const float* w, const float* bias,
-                         int Cout, float* y) {
+/* ---- ConvTranspose3d(kernel = stride = (kz, ky, kx), each 1 or 2) with bias: resenc_unet.hpp:211
+ * (kernel 2, stride 2 there; nnU-Net sets both to the stage's per-axis pooling kernel) --------- */
+void fxo_conv_transpose_s(const float* x, int B, int Cin, int D, int H, int W, const float* w, const float* bias,
+                          int Cout, int kz, int ky, int kx, float* y) {
     const int64_t vin = (int64_t)D * H * W;
-    const int Do = 2 * D, Ho = 2 * H, Wo = 2 * W;
+    const int Do = kz * D, Ho = ky * H, Wo = kx * W, nk = kz * ky * kx;
     const int64_t vout = (int64_t)Do * Ho * Wo;
 #pragma omp parallel for collapse(2) schedule(dynamic)
     for (int b = 0; b < B; ++b)
@@ -187,22 +201,26 @@ void fxo_conv_transpose2(const float* x, int B, int Cin, int D, int H, int W, co
             for (int64_t i = 0; i < vout; ++i) yo[i] = bias ? bias[co] : 0.0f;
             for (int ci = 0; ci < Cin; ++ci) {
                 const float* xi = x + ((int64_t)b * Cin + ci) * vin;
-                const float* wk = w + ((int64_t)ci * Cout + co) * 8;
+                const float* wk = w + ((int64_t)ci * Cout + co) * nk;
                 for (int z = 0; z < D; ++z)
                     for (int yy = 0; yy < H; ++yy) {
                         const float* xr = xi + ((int64_t)z * H + yy) * W;
-                        for (int a = 0; a < 4; ++a) {
-                            const int az = a >> 1, ay = a & 1;
-                            float* yr = yo + ((int64_t)(2 * z + az) * Ho + (2 * yy + ay)) * Wo;
-                            const float w0 = wk[az * 4 + ay * 2 + 0], w1 = wk[az * 4 + ay * 2 + 1];
-                            for (int xx = 0; xx < W; ++xx) {
-                                yr[2 * xx] += w0 * xr[xx];
-                                yr[2 * xx + 1] += w1 * xr[xx];
+                        for (int az = 0; az < kz; ++az)
+                            for (int ay = 0; ay < ky; ++ay) {
+                                float* yr = yo + ((int64_t)(kz * z + az) * Ho + (ky * yy + ay)) * Wo;
+                                for (int ax = 0; ax < kx; ++ax) {
+                                    const float wv = wk[(az * ky + ay) * kx + ax];
+                                    for (int xx = 0; xx < W; ++xx) yr[kx * xx + ax] += wv * xr[xx];
+                                }
                             }
-                        }
                     }
             }
         }
+}
+
+void fxo_conv_transpose2(const float* x, int B, int Cin, int D, int H, int W, const float* w, const float* bias,
+                         int Cout, float* y) {
+    fxo_conv_transpose_s(x, B, Cin, D, H, W, w, bias, Cout, 2, 2, 2, y);
 }
 
 /* ---- 1x1x1 head + softmax channel select / sigmoid + nan_to_num: infer.hpp:760-767 -------- */
@@ -251,6 +269,7 @@ struct fxo_net {
     int nt;
     int S, nconv, ncls;
     int F[16];
+    int st[16][3]; /* per stage: stride (z, y, x) of its first conv = kernel of the transposed conv undoing it */
 };
 
 static const fxo_tensor* find_t(const fxo_net* n, const char* name) {
@@ -360,6 +379,16 @@ fxo_net* fxo_net_load(const char* path) {
         const fxo_tensor* h = find_t(n, nm);
         if (n->S < 2 || n->nconv < 1 || !h) goto bad;
         n->ncls = (int)h->shape[0];
+        n->st[0][0] = n->st[0][1] = n->st[0][2] = 1;
+        for (int s = 1; s < n->S; ++s) {
+            snprintf(nm, sizeof nm, "decoder.transpconvs.%d.weight", n->S - 1 - s);
+            const fxo_tensor* tp = find_t(n, nm);
+            if (!tp || tp->ndim != 5) goto bad;
+            for (int a = 0; a < 3; ++a) {
+                if (tp->shape[2 + a] != 1 && tp->shape[2 + a] != 2) goto bad;
+                n->st[s][a] = (int)tp->shape[2 + a];
+            }
+        }
     }
     return n;
 bad:
@@ -377,39 +406,55 @@ static const float* W_(const fxo_net* n, const char* fmt, int a, int b) {
     return t ? t->data : NULL;
 }
 
-/* ConvNormAct: conv(k3, pad 1, stride, bias) -> InstanceNorm3d(affine, eps 1e-5) -> LeakyReLU(0.01) */
+/* ConvNormAct: conv(k3, pad 1, stride, bias) -> InstanceNorm3d(affine, eps 1e-5) -> LeakyReLU(0.01);
+ * g = the input extents (z, y, x), replaced by the output's */
 static float* conv_norm_act(const fxo_net* n, const char* pre, int idx, int i, const float* x, int B, int Cin,
-                            int D, int stride, int Cout) {
+                            int g[3], const int stride[3], int Cout) {
     char fw[256], fb[256], fg[256], fbt[256];
     snprintf(fw, sizeof fw, "%s.%%d.convs.%%d.conv.weight", pre);
     snprintf(fb, sizeof fb, "%s.%%d.convs.%%d.conv.bias", pre);
     snprintf(fg, sizeof fg, "%s.%%d.convs.%%d.norm.weight", pre);
     snprintf(fbt, sizeof fbt, "%s.%%d.convs.%%d.norm.bias", pre);
-    const int Do = D / stride;
-    const int64_t S = (int64_t)Do * Do * Do;
+    const int o[3] = {g[0] / stride[0], g[1] / stride[1], g[2] / stride[2]};
+    const int64_t S = (int64_t)o[0] * o[1] * o[2];
     float* y = (float*)malloc(sizeof(float) * (size_t)(B * (int64_t)Cout * S));
-    fxo_conv3d(x, B, Cin, D, D, D, W_(n, fw, idx, i), W_(n, fb, idx, i), Cout, stride, y);
+    fxo_conv3d_s(x, B, Cin, g[0], g[1], g[2], W_(n, fw, idx, i), W_(n, fb, idx, i), Cout, stride[0], stride[1], stride[2],
+                 y);
     fxo_instance_norm_act(y, B, Cout, S, W_(n, fg, idx, i), W_(n, fbt, idx, i), 1e-5f, 1, 0.01f);
+    for (int a = 0; a < 3; ++a) g[a] = o[a];
     return y;
 }
 
-int fxo_net_forward(const fxo_net* n, const float* x, int B, int P, int channel, int sigmoid, float* prob) {
+int fxo_net_tile_ok(const fxo_net* n, int tz, int ty, int tx) {
+    int g[3] = {tz, ty, tx};
+    if (tz < 1 || ty < 1 || tx < 1) return 0;
+    for (int s = 1; s < n->S; ++s)
+        for (int a = 0; a < 3; ++a) {
+            if (g[a] % n->st[s][a]) return 0;
+            g[a] /= n->st[s][a];
+        }
+    return 1;
+}
+
+int fxo_net_forward_tiled(const fxo_net* n, const float* x, int B, int tz, int ty, int tx, int channel, int sigmoid,
+                          float* prob) {
+    if (!fxo_net_tile_ok(n, tz, ty, tx)) return 1;
     const int S = n->S;
+    static const int one[3] = {1, 1, 1};
     float* skips[16] = {0};
-    float* cur = (float*)malloc(sizeof(float) * (size_t)B * P * P * P);
-    memcpy(cur, x, sizeof(float) * (size_t)B * P * P * P);
-    int C = 1, D = P;
-    /* encoder: ConvStack(prev, F[s], 3, s ? 2 : 1, nconv) per stage */
+    const int64_t v0 = (int64_t)tz * ty * tx;
+    float* cur = (float*)malloc(sizeof(float) * (size_t)(B * v0));
+    memcpy(cur, x, sizeof(float) * (size_t)(B * v0));
+    int C = 1, g[3] = {tz, ty, tx};
+    /* encoder: ConvStack(prev, F[s], 3, stride[s], nconv) per stage */
     for (int s = 0; s < S; ++s)
         for (int i = 0; i < n->nconv; ++i) {
-            const int stride = (i == 0 && s > 0) ? 2 : 1;
-            float* y = conv_norm_act(n, "encoder.stages", s, i, cur, B, C, D, stride, n->F[s]);
+            float* y = conv_norm_act(n, "encoder.stages", s, i, cur, B, C, g, i == 0 ? n->st[s] : one, n->F[s]);
             free(cur);
             cur = y;
             C = n->F[s];
-            D /= stride;
             if (i == n->nconv - 1) {
-                const int64_t sz = (int64_t)B * C * D * D * D;
+                const int64_t sz = (int64_t)B * C * g[0] * g[1] * g[2];
                 skips[s] = (float*)malloc(sizeof(float) * (size_t)sz);
                 memcpy(skips[s], cur, sizeof(float) * (size_t)sz);
             }
@@ -417,11 +462,12 @@ int fxo_net_forward(const fxo_net* n, const float* x, int B, int P, int channel,
     /* decoder: transpconv -> cat(up, skip) -> ConvStack(2 F, F, 3, 1, nconv) (resenc_unet.hpp:227-237) */
     for (int t = 0; t < S - 1; ++t) {
         const int lvl = S - 2 - t, F = n->F[lvl];
-        const int Dn = D * 2;
-        const int64_t S3 = (int64_t)Dn * Dn * Dn;
+        const int* k = n->st[lvl + 1];
+        const int gn[3] = {g[0] * k[0], g[1] * k[1], g[2] * k[2]};
+        const int64_t S3 = (int64_t)gn[0] * gn[1] * gn[2];
         float* up = (float*)malloc(sizeof(float) * (size_t)(B * (int64_t)F * S3));
-        fxo_conv_transpose2(cur, B, C, D, D, D, W_(n, "decoder.transpconvs.%d.weight", t, 0),
-                            W_(n, "decoder.transpconvs.%d.bias", t, 0), F, up);
+        fxo_conv_transpose_s(cur, B, C, g[0], g[1], g[2], W_(n, "decoder.transpconvs.%d.weight", t, 0),
+                             W_(n, "decoder.transpconvs.%d.bias", t, 0), F, k[0], k[1], k[2], up);
         float* cat = (float*)malloc(sizeof(float) * (size_t)(B * (int64_t)2 * F * S3));
         for (int b = 0; b < B; ++b) {
             memcpy(cat + (int64_t)b * 2 * F * S3, up + (int64_t)b * F * S3, sizeof(float) * (size_t)(F * S3));
@@ -432,15 +478,15 @@ int fxo_net_forward(const fxo_net* n, const float* x, int B, int P, int channel,
         free(cur);
         cur = cat;
         C = 2 * F;
-        D = Dn;
+        for (int a = 0; a < 3; ++a) g[a] = gn[a];
         for (int i = 0; i < n->nconv; ++i) {
-            float* y = conv_norm_act(n, "decoder.stages", t, i, cur, B, C, D, 1, F);
+            float* y = conv_norm_act(n, "decoder.stages", t, i, cur, B, C, g, one, F);
             free(cur);
             cur = y;
             C = F;
         }
     }
-    const int64_t S3 = (int64_t)D * D * D;
+    const int64_t S3 = (int64_t)g[0] * g[1] * g[2];
     fxo_head(cur, B, C, S3, W_(n, "decoder.seg_layers.%d.weight", S - 2, 0), W_(n, "decoder.seg_layers.%d.bias", S - 2, 0),
              n->ncls, channel, sigmoid, prob);
     free(cur);
@@ -448,23 +494,32 @@ int fxo_net_forward(const fxo_net* n, const float* x, int B, int P, int channel,
     return 0;
 }
 
-/* ---- sliding window: src/ml/infer.hpp:456-864 (tta off, no crop, no checkpoint) ------------ */
-int fxo_predict_surface(const fxo_net* n, const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, int P,
-                        double overlap, int channel, int sigmoid, float* prob) {
-    if (P % 64 != 0) return 1;
+int fxo_net_forward(const fxo_net* n, const float* x, int B, int P, int channel, int sigmoid, float* prob) {
+    return fxo_net_forward_tiled(n, x, B, P, P, P, channel, sigmoid, prob);
+}
+
+/* ---- sliding window: src/ml/infer.hpp:456-864 (tta off, no crop, no checkpoint), per axis:
+ * tile starts, Gaussian (sigma = tile / 8) and weight profile of each axis from its own extent -- */
+int fxo_predict_tiled(const fxo_net* n, const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, int tz, int ty,
+                      int tx, double overlap, int channel, int sigmoid, float* prob) {
+    if (!fxo_net_tile_ok(n, tz, ty, tx)) return 1;
     int64_t zs[4096], ys[4096], xs[4096];
-    const int64_t nz = fxo_tile_starts(dz, P, overlap, zs, 4096), ny = fxo_tile_starts(dy, P, overlap, ys, 4096),
-                  nx = fxo_tile_starts(dx, P, overlap, xs, 4096);
+    const int64_t nz = fxo_tile_starts(dz, tz, overlap, zs, 4096), ny = fxo_tile_starts(dy, ty, overlap, ys, 4096),
+                  nx = fxo_tile_starts(dx, tx, overlap, xs, 4096);
     if (nz > 4096 || ny > 4096 || nx > 4096) return 1;
-    float* g = (float*)malloc(sizeof(float) * (size_t)P);
-    fxo_gaussian1d(P, g);
+    float* gz = (float*)malloc(sizeof(float) * (size_t)tz);
+    float* gy = (float*)malloc(sizeof(float) * (size_t)ty);
+    float* gx = (float*)malloc(sizeof(float) * (size_t)tx);
+    fxo_gaussian1d(tz, gz);
+    fxo_gaussian1d(ty, gy);
+    fxo_gaussian1d(tx, gx);
     float* Wz = (float*)malloc(sizeof(float) * (size_t)dz);
     float* Wy = (float*)malloc(sizeof(float) * (size_t)dy);
     float* Wx = (float*)malloc(sizeof(float) * (size_t)dx);
-    fxo_weight_profile(g, P, zs, nz, 0, dz, dz, Wz);
-    fxo_weight_profile(g, P, ys, ny, 0, dy, dy, Wy);
-    fxo_weight_profile(g, P, xs, nx, 0, dx, dx, Wx);
-    const int64_t PN = (int64_t)P * P * P;
+    fxo_weight_profile(gz, tz, zs, nz, 0, dz, dz, Wz);
+    fxo_weight_profile(gy, ty, ys, ny, 0, dy, dy, Wy);
+    fxo_weight_profile(gx, tx, xs, nx, 0, dx, dx, Wx);
+    const int64_t PN = (int64_t)tz * ty * tx;
     float* patch = (float*)malloc(sizeof(float) * (size_t)PN);
     float* sp = (float*)malloc(sizeof(float) * (size_t)PN);
     memset(prob, 0, sizeof(float) * (size_t)(dz * dy * dx));
@@ -472,22 +527,22 @@ int fxo_predict_surface(const fxo_net* n, const uint8_t* vol, int64_t dz, int64_
         for (int64_t iy = 0; iy < ny; ++iy)
             for (int64_t ix = 0; ix < nx; ++ix) {
                 const int64_t z0 = zs[iz], y0 = ys[iy], x0 = xs[ix];
-                fxo_fill_patch_u8(vol, dz, dy, dx, z0, y0, x0, P, patch);
-                fxo_norm_patch_zscore(patch, P);
-                fxo_net_forward(n, patch, 1, P, channel, sigmoid, sp);
+                fxo_fill_tile_u8(vol, dz, dy, dx, z0, y0, x0, tz, ty, tx, patch);
+                fxo_norm_tile_zscore(patch, tz, ty, tx);
+                fxo_net_forward_tiled(n, patch, 1, tz, ty, tx, channel, sigmoid, sp);
                 /* scatter: prob += (gz*gy)*gx*p over the in-volume part (infer.hpp:631-653) */
 #pragma omp parallel for
-                for (int z = 0; z < P; ++z) {
+                for (int z = 0; z < tz; ++z) {
                     const int64_t oz = z0 + z;
                     if (oz >= dz) continue;
-                    for (int y = 0; y < P; ++y) {
+                    for (int y = 0; y < ty; ++y) {
                         const int64_t oy = y0 + y;
                         if (oy >= dy) break;
-                        const float wzy = g[z] * g[y];
-                        for (int x = 0; x < P; ++x) {
+                        const float wzy = gz[z] * gy[y];
+                        for (int x = 0; x < tx; ++x) {
                             const int64_t ox = x0 + x;
                             if (ox >= dx) break;
-                            prob[(oz * dy + oy) * dx + ox] += wzy * g[x] * sp[((int64_t)z * P + y) * P + x];
+                            prob[(oz * dy + oy) * dx + ox] += wzy * gx[x] * sp[((int64_t)z * ty + y) * tx + x];
                         }
                     }
                 }
@@ -502,13 +557,21 @@ int fxo_predict_surface(const fxo_net* n, const uint8_t* vol, int64_t dz, int64_
                 if (w > 0.0f) prob[(z * dy + y) * dx + x] /= w;
             }
         }
-    free(g);
+    free(gz);
+    free(gy);
+    free(gx);
     free(Wz);
     free(Wy);
     free(Wx);
     free(patch);
     free(sp);
     return 0;
+}
+
+int fxo_predict_surface(const fxo_net* n, const uint8_t* vol, int64_t dz, int64_t dy, int64_t dx, int P,
+                        double overlap, int channel, int sigmoid, float* prob) {
+    if (P % 64 != 0) return 1;
+    return fxo_predict_tiled(n, vol, dz, dy, dx, P, P, P, overlap, channel, sigmoid, prob);
 }
 
 /* u8 = (u8)(clamp(p, 0, 1) * 255 + 0.5): src/ml/inference.cpp:343-351 */

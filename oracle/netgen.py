@@ -18,7 +18,10 @@ from pathlib import Path
 import numpy as np
 
 
-def plain_unet(features, nconv=2, ncls=2, seed=0):
+def plain_unet(features, nconv=2, ncls=2, seed=0, strides=None):
+    """strides: per stage (z, y, x) stride of its first conv (stage 0 (1, 1, 1)); None = 2 on every
+    axis after stage 0. The transposed conv undoing a stage has kernel = stride (nnU-Net's
+    get_network_from_plans: transpconv_op(..., pool_op_kernel_sizes[s], stride=pool_op_kernel_sizes[s]))."""
     import torch
 
     g = torch.Generator().manual_seed(int(seed))
@@ -29,6 +32,7 @@ def plain_unet(features, nconv=2, ncls=2, seed=0):
         return (base + sd * torch.randn(*shape, generator=g)).numpy()
 
     S = len(features)
+    strides = [(1, 1, 1)] + [(2, 2, 2)] * (S - 1) if strides is None else [tuple(st) for st in strides]
     cin = 1
     for s in range(S):
         for i in range(nconv):
@@ -41,7 +45,8 @@ def plain_unet(features, nconv=2, ncls=2, seed=0):
         cin = features[s]
     for t in range(S - 1):
         below, skipc = features[S - 1 - t], features[S - 2 - t]
-        out[f"decoder.transpconvs.{t}.weight"] = normal((below, skipc, 2, 2, 2), gain / (skipc * 8) ** 0.5)
+        k = strides[S - 1 - t]
+        out[f"decoder.transpconvs.{t}.weight"] = normal((below, skipc) + k, gain / (skipc * k[0] * k[1] * k[2]) ** 0.5)
         out[f"decoder.transpconvs.{t}.bias"] = normal((skipc,), 0.1)
         for i in range(nconv):
             c_in = 2 * skipc if i == 0 else skipc
@@ -74,5 +79,5 @@ def write_fxweights(path, tensors):
     return Path(path)
 
 
-def make_plain_unet(path, features, nconv=2, ncls=2, seed=0):
-    return write_fxweights(path, plain_unet(features, nconv, ncls, seed))
+def make_plain_unet(path, features, nconv=2, ncls=2, seed=0, strides=None):
+    return write_fxweights(path, plain_unet(features, nconv, ncls, seed, strides))

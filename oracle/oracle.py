@@ -32,6 +32,28 @@ SPIRAL_CONFIG1 = dict(pitch=12, thickness=3, sheet_mean=170, sheet_sd=15, bg_mea
 SPIRAL_CONFIG3 = dict(SPIRAL_CONFIG1, pitch=16, speckle_sd=8.0)
 
 
+class Papyrus(C.Structure):
+    _fields_ = [(k, C.c_double) for k in ("sigma_z", "sigma_y", "sigma_x", "mean", "sd", "ink_sigma", "ink_fraction",
+                                          "ink_delta")]
+
+
+# The layer-stack workload's papyrus with ink (checker-side copy of the recipe).
+PAPYRUS_INK = dict(sigma_z=4.0, sigma_y=1.0, sigma_x=1.0, mean=110.0, sd=20.0, ink_sigma=6.0, ink_fraction=0.05,
+                   ink_delta=25.0)
+
+
+def synth_papyrus(shape, seed, stack=0, params=None, want_ink=False):
+    """Papyrus layer stack [dz][dy][dx] u8 (+ its [dy][dx] ink mask) (oracle/synth.c)."""
+    dz, dy, dx = shape
+    p = Papyrus(**(params or PAPYRUS_INK))
+    out = np.empty((dz, dy, dx), dtype=np.uint8)
+    ink = np.empty((dy, dx), dtype=np.uint8)
+    if lib().fxo_synth_papyrus(out.ctypes.data_as(C.POINTER(C.c_uint8)), ink.ctypes.data_as(C.POINTER(C.c_uint8)),
+                               dz, dy, dx, C.byref(p), seed, stack):
+        raise ValueError("fxo_synth_papyrus: bad arguments")
+    return (out, ink) if want_ink else out
+
+
 def synth_spiral(shape, seed, params=None, z_begin=0, z_end=None):
     """The spiral-sheet synthetic CT [z_end - z_begin][dy][dx] u8 (oracle/synth.c)."""
     dz, dy, dx = shape
@@ -80,6 +102,12 @@ def lib():
         L.fxv_morton3.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64]
         L.fxo_synth_spiral.restype = i32
         L.fxo_synth_spiral.argtypes = [u8p, i64, i64, i64, C.POINTER(Spiral), C.c_uint64, i64, i64]
+        L.fxo_net_forward_tiled.restype = i32
+        L.fxo_net_forward_tiled.argtypes = [vp, f32p, i32, i32, i32, i32, i32, i32, f32p]
+        L.fxo_predict_tiled.restype = i32
+        L.fxo_predict_tiled.argtypes = [vp, u8p, i64, i64, i64, i32, i32, i32, C.c_double, i32, i32, f32p]
+        L.fxo_synth_papyrus.restype = i32
+        L.fxo_synth_papyrus.argtypes = [u8p, u8p, i64, i64, i64, C.POINTER(Papyrus), C.c_uint64, i64]
         _lib = L
     return _lib
 
@@ -134,6 +162,23 @@ class Net:
         B, P = x.shape[0], x.shape[1]
         out = np.zeros_like(x)
         lib().fxo_net_forward(self.h, _fp(x), B, P, channel, sigmoid, _fp(out))
+        return out
+
+    def forward_tiled(self, x, channel=1, sigmoid=0):
+        """x: [B][tz][ty][tx] normalised f32 -> selected-class probability, same shape."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros_like(x)
+        if lib().fxo_net_forward_tiled(self.h, _fp(x), x.shape[0], *x.shape[1:], channel, sigmoid, _fp(out)):
+            raise ValueError("oracle forward_tiled: the tile does not halve evenly through the stages")
+        return out
+
+    def predict_tiled(self, vol, tile, overlap, channel=1, sigmoid=0):
+        """The sliding-window prediction with a (tz, ty, tx) tile (fxo_predict_tiled)."""
+        v = np.ascontiguousarray(vol, dtype=np.uint8)
+        out = np.zeros(v.shape, dtype=np.float32)
+        if lib().fxo_predict_tiled(self.h, v.ctypes.data_as(C.POINTER(C.c_uint8)), *v.shape, *tile, overlap, channel,
+                                   sigmoid, _fp(out)):
+            raise ValueError("oracle predict_tiled failed")
         return out
 
     def predict_surface(self, vol, P, overlap, channel=1, sigmoid=0):

@@ -156,3 +156,106 @@ int fxo_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fxo
     free(sheet);
     return rc;
 }
+
+/* ---- papyrus layer stacks with ink (the layer-stack workload's input) ---------------------------
+ * The recipe (the benchmark's description of that input: papyrus fibre as anisotropic
+ * Gaussian-filtered noise, a sparse ink blob mask adding a fixed intensity): white N(0, 1) noise
+ * per voxel (PCG stream per (stack, z, y) row), separable Gaussian passes along x, y, then z
+ * (radius ceil(3 sigma), normalised weights, edge clamp), rescaled to standard deviation sd
+ * around mean by the filter's noise gain sqrt(sum kz^2 sum ky^2 sum kx^2); ink = the
+ * floor(fraction * dy * dx) largest values of a 2D-filtered noise plane (PCG stream per
+ * (stack, y) row), + ink_delta on every layer of those columns; clip [0, 255], round half up. */
+typedef struct fxo_papyrus {
+    double sigma_z, sigma_y, sigma_x, mean, sd, ink_sigma, ink_fraction, ink_delta;
+} fxo_papyrus;
+
+static int gauss_taps(double sigma, float* k) {
+    const int r = sigma > 0 ? (int)ceil(3.0 * sigma) : 0;
+    if (r > 63) return -1;
+    if (!r) {
+        k[0] = 1.f;
+        return 0;
+    }
+    double s = 0;
+    for (int i = -r; i <= r; ++i) s += exp(-0.5 * i * i / (sigma * sigma));
+    for (int i = -r; i <= r; ++i) k[i + r] = (float)(exp(-0.5 * i * i / (sigma * sigma)) / s);
+    return r;
+}
+
+static double sum_sq(const float* k, int r) {
+    double s = 0;
+    for (int i = 0; i < 2 * r + 1; ++i) s += (double)k[i] * k[i];
+    return s;
+}
+
+static void filter_line(const float* src, float* dst, int64_t n, int64_t step, const float* k, int r) {
+    for (int64_t i = 0; i < n; ++i) {
+        float s = 0.f;
+        for (int j = -r; j <= r; ++j) s += k[j + r] * src[clampi(i + j, 0, n - 1) * step];
+        dst[i * step] = s;
+    }
+}
+
+static int cmp_desc(const void* a, const void* b) {
+    const float x = *(const float*)a, y = *(const float*)b;
+    return x < y ? 1 : (x > y ? -1 : 0);
+}
+
+int fxo_synth_papyrus(uint8_t* out, uint8_t* ink, int64_t dz, int64_t dy, int64_t dx, const fxo_papyrus* p,
+                      uint64_t seed, int64_t stack) {
+    if (!out || !p || dz < 1 || dy < 1 || dx < 1 || stack < 0) return 1;
+    float kz[127], ky[127], kx[127], ki[127];
+    const int rz = gauss_taps(p->sigma_z, kz), ry = gauss_taps(p->sigma_y, ky), rx = gauss_taps(p->sigma_x, kx);
+    const int ri = gauss_taps(p->ink_sigma, ki);
+    if (rz < 0 || ry < 0 || rx < 0 || ri < 0) return 1;
+    const int64_t plane = dy * dx, n = dz * plane;
+    float* a = malloc(sizeof(float) * (size_t)n);
+    float* b = malloc(sizeof(float) * (size_t)n);
+    float* f = malloc(sizeof(float) * (size_t)plane);
+    float* g = malloc(sizeof(float) * (size_t)plane);
+    uint8_t* mask = calloc((size_t)plane, 1);
+    if (!a || !b || !f || !g || !mask) {
+        free(a), free(b), free(f), free(g), free(mask);
+        return 1;
+    }
+#pragma omp parallel for schedule(static)
+    for (int64_t z = 0; z < dz; ++z) {
+        float* P = a + z * plane;
+        float* Q = b + z * plane;
+        for (int64_t y = 0; y < dy; ++y) {
+            pcg_t r = pcg_seed(seed ^ 0x5EED0F1B4E5ull, (uint64_t)((stack * dz + z) * dy + y) + 0x2545F4914F6CDD1Dull);
+            for (int64_t x = 0; x < dx; ++x) P[y * dx + x] = pcg_normal(&r);
+        }
+        for (int64_t y = 0; y < dy; ++y) filter_line(P + y * dx, Q + y * dx, dx, 1, kx, rx);
+        for (int64_t x = 0; x < dx; ++x) filter_line(Q + x, P + x, dy, dx, ky, ry);
+    }
+#pragma omp parallel for schedule(static)
+    for (int64_t y = 0; y < dy; ++y)
+        for (int64_t x = 0; x < dx; ++x) filter_line(a + y * dx + x, b + y * dx + x, dz, plane, kz, rz);
+    for (int64_t y = 0; y < dy; ++y) {
+        pcg_t r = pcg_seed(seed ^ 0x1A4B1075ull, (uint64_t)(stack * dy + y) + 0x9E3779B97F4A7C15ull);
+        for (int64_t x = 0; x < dx; ++x) f[y * dx + x] = pcg_normal(&r);
+    }
+    for (int64_t y = 0; y < dy; ++y) filter_line(f + y * dx, g + y * dx, dx, 1, ki, ri);
+    for (int64_t x = 0; x < dx; ++x) filter_line(g + x, f + x, dy, dx, ki, ri);
+    const int64_t kink = (int64_t)floor(p->ink_fraction * (double)plane);
+    if (kink > 0) {
+        memcpy(g, f, sizeof(float) * (size_t)plane);
+        qsort(g, (size_t)plane, sizeof(float), cmp_desc);
+        const float thr = g[kink - 1];
+        for (int64_t i = 0; i < plane; ++i) mask[i] = f[i] >= thr ? 1 : 0;
+    }
+    if (ink) memcpy(ink, mask, (size_t)plane);
+    const float scale = (float)(p->sd / sqrt(sum_sq(kz, rz) * sum_sq(ky, ry) * sum_sq(kx, rx)));
+    const float mean = (float)p->mean, delta = (float)p->ink_delta;
+#pragma omp parallel for schedule(static)
+    for (int64_t z = 0; z < dz; ++z)
+        for (int64_t i = 0; i < plane; ++i) {
+            float s = mean + scale * b[z * plane + i];
+            if (mask[i]) s += delta;
+            s = fminf(255.f, fmaxf(0.f, s));
+            out[z * plane + i] = (uint8_t)floorf(s + 0.5f);
+        }
+    free(a), free(b), free(f), free(g), free(mask);
+    return 0;
+}

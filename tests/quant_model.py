@@ -47,7 +47,9 @@ def layer_keys(S, nconv=2):
 
 def forward(params: dict, x: torch.Tensor, types: dict | None = None, scales: dict | None = None,
             default: str = "f32", prenorm: str | None = None, channel: int = 1) -> torch.Tensor:
-    """x: [B,1,P,P,P] z-scored input. types/scales keyed by layer name (see layer_keys)."""
+    """x: [B,1,D,H,W] z-scored input. types/scales keyed by layer name (see layer_keys). A stage's
+    stride is the kernel shape of the transposed conv that undoes it ((2, 2, 2), or (1, 2, 2) for a
+    y/x-only stage); a one-class head is a sigmoid."""
     types = types or {}
     scales = scales or {}
     T = {k: torch.from_numpy(np.asarray(v)) for k, v in params.items()}
@@ -71,21 +73,24 @@ def forward(params: dict, x: torch.Tensor, types: dict | None = None, scales: di
         y = (y - m) / torch.sqrt(v + 1e-5) * g + b
         return F.leaky_relu(y, 0.01) if act else y
 
+    stride = [(1, 1, 1)] + [tuple(T[f"decoder.transpconvs.{S - 1 - s}.weight"].shape[2:]) for s in range(1, S)]
     skips = []
     for s in range(S):
         for i in range(nconv):
-            x = cna(x, f"encoder.stages.{s}.convs.{i}", 2 if (i == 0 and s > 0) else 1, f"e{s}{i}")
+            x = cna(x, f"encoder.stages.{s}.convs.{i}", stride[s] if i == 0 else 1, f"e{s}{i}")
         skips.append(x)
     for t in range(S - 1):
         lv = S - 2 - t
         key = f"u{t}"
         k = ty(key)
         up = F.conv_transpose3d(_round(x, k, scales.get(key)), _wq(T[f"decoder.transpconvs.{t}.weight"], k, 1),
-                                T[f"decoder.transpconvs.{t}.bias"], stride=2)
+                                T[f"decoder.transpconvs.{t}.bias"], stride=stride[lv + 1])
         x = torch.cat([up, skips[lv]], 1)
         for i in range(nconv):
             x = cna(x, f"decoder.stages.{t}.convs.{i}", 1, f"d{t}{i}")
     h = F.conv3d(x, T[f"decoder.seg_layers.{S - 2}.weight"], T[f"decoder.seg_layers.{S - 2}.bias"])
+    if h.shape[1] == 1:
+        return torch.sigmoid(h[:, 0])
     return torch.softmax(h, 1)[:, channel]
 
 
