@@ -40,6 +40,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "Mvoxels/s fp8 3D-UNet sliding-window inference @1/2/4/8 B200; % tcgen05 peak"
 FEATURES = (32, 64, 128, 256, 320)
+INK_FEATURES_B = (64, 128, 256, 512)  # the layer-stack net (fenix_b200.weights.INK_*), restated for the
+INK_STRIDES_B = ((1, 1, 1), (1, 2, 2), (1, 2, 2), (2, 2, 2))  # reference arm, which imports no product code
 WEIGHT_SEED, VOLUME_SEED, CALIB_SEED0 = 1, 2, 1000
 SCHED_DICE = 0.993  # the fp8 schedule's agreement with the 16-bit forward on the calibration patches
 PARITY_CASE = ROOT / "tests" / "golden" / "net128_cfg3.npz"  # the reference's map of a 192^3 crop
@@ -299,6 +301,265 @@ def parity_check(fx, net, batch, precision):
             "meets_max_abs": bool(e.max() <= bound), "meets_dice": bool(dice >= 0.99)}
 
 
+INK_METRIC = "Mvoxels/s fp8 wide-ink 3D-UNet layer-stack inference @1/2/4/8 B200; % tcgen05 peak"
+INK_SHAPE, INK_TILE, INK_OVERLAP, INK_STACKS = (64, 512, 512), (64, 256, 256), 0.25, 8
+INK_WEIGHT_SEED, INK_VOLUME_SEED = 3, 3
+INK_PARITY_CASE = ROOT / "tests" / "golden" / "ink_small.npz"
+
+
+def ink_config(world, precision):
+    return {
+        "workload": f"wide-ink layer stacks: {INK_STACKS} stacks of {'x'.join(map(str, INK_SHAPE))} u8 per GPU, "
+                    f"{'x'.join(map(str, INK_TILE))} tiles at overlap {INK_OVERLAP} (1x3x3 per stack), Gaussian blend, "
+                    "u8 output; 4-stage UNet 64/128/256/512, stride (1,2,2) at stages 1-2 and 2 at stage 3, "
+                    "1 class + sigmoid",
+        "stack": list(INK_SHAPE), "tile": list(INK_TILE), "overlap": INK_OVERLAP, "stacks_per_gpu": INK_STACKS,
+        "batch": 8, "precision": precision, "parallelism": f"independent stacks x{world}",
+        "l2": "inputs larger than L2: 134 MB u8 stacks + 537 MB f32 accumulator per GPU per step",
+    }
+
+
+def ink_cpu_sample(w, threads=None):
+    """The C oracle's forward (fp32, OpenMP over all host threads) of one 16 x 64 x 64 tile of the
+    same net, projected per voxel to the workload's tiles (the net's FLOPs per tile voxel are within
+    1% between the two tile sizes). Returns (seconds per workload tile, threads, seconds)."""
+    from oracle import oracle as orc
+
+    n = orc.Net(w)
+    x = np.random.default_rng(0).normal(size=(1, 16, 64, 64)).astype(np.float32)
+    t0 = time.perf_counter()
+    n.forward_tiled(x, channel=0, sigmoid=1)
+    secs = time.perf_counter() - t0
+    scale = (INK_TILE[0] * INK_TILE[1] * INK_TILE[2]) / (16 * 64 * 64)
+    return secs * scale, os.cpu_count() or 1, secs
+
+
+def run_ink_reference(args):
+    """Reference arm of the layer-stack workload. The reference's nets take one int stride per stage
+    and its window tiles cubes, so it cannot run this net; the CPU baseline is the C oracle's
+    restatement (kind "port"), timed on a bounded sample (one 16 x 64 x 64 tile per step)."""
+    if env_int("RANK", 0) != 0:
+        return 0
+    from oracle import netgen
+
+    with tempfile.TemporaryDirectory() as td:
+        w = netgen.make_plain_unet(Path(td) / "w.fxweights", INK_FEATURES_B, ncls=1, seed=INK_WEIGHT_SEED,
+                                   strides=INK_STRIDES_B)
+        for _ in range(1):
+            ink_cpu_sample(w)
+        ts = [ink_cpu_sample(w)[0] for _ in range(args.steps)]
+    per_tile = sum(ts) / len(ts)
+    tiles = INK_STACKS * 9
+    value = INK_STACKS * float(np.prod(INK_SHAPE)) / (tiles * per_tile) / 1e6
+    thr = os.cpu_count() or 1
+    sample = (f"C oracle forward (fp32, {thr} threads) of one 16x64x64 tile per step, projected per voxel to the "
+              f"{tiles} 64x256x256 tiles of {INK_STACKS} stacks ({args.steps} steps)")
+    print(json.dumps({"metric": INK_METRIC, "value": value, "unit": "Mvoxels/s", "impl": "reference",
+                      "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": per_tile * tiles * 1e3, "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": ink_config(args.gpus, "f32"),
+                      "cpu_baseline": {"value": value, "unit": "Mvoxels/s", "cores": thr, "kind": "port",
+                                       "sample": sample},
+                      "e2e": {"value": value, "unit": "Mvoxels/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+    return 0
+
+
+def ink_parity(fx, wdir, precision, sched_dice):
+    """The workload's net (same weights) on the small layer stack of tests/golden/ink_small.npz in
+    16 x 64 x 64 tiles, against the C oracle's full map: max |dp| and Dice, 16-bit and the
+    calibrated schedule picked the same way as for the benchmark net."""
+    from fenix_b200.weights import make_plain_unet
+
+    g = np.load(INK_PARITY_CASE)
+    tile = tuple(int(v) for v in g["tile"])
+    w = make_plain_unet(Path(wdir) / "ink_small.fxweights", INK_FEATURES_B, ncls=1, seed=int(g["weight_seed"]),
+                        strides=INK_STRIDES_B)
+    vol = fx.synth_papyrus(tuple(int(v) for v in g["shape"]), int(g["volume_seed"]), int(g["stack"]))
+    ref = g["prob_u16"].astype(np.float32) / np.float32(65535.0)
+    out = {"case": f"{'x'.join(str(int(v)) for v in g['shape'])} papyrus stack in {'x'.join(map(str, tile))} tiles, "
+                   "reference = the C oracle's fp32 sliding window (the reference has no anisotropic net), every voxel"}
+    for tag, prec in (("f16", "f16"), ("schedule", "fp8")):
+        if tag == "schedule" and precision != "fp8":
+            continue
+        net = fx.Net(w, tile, max_batch=8, precision=prec)
+        if prec == "fp8":
+            cal = np.stack([fx.synth_papyrus(tile, 1000 + i, 0) for i in range(4)])
+            net.calibrate_schedule(cal, min_dice=sched_dice)
+        prob, _ = net.predict_volume(vol, overlap=float(g["overlap"]), batch=8, channel=0, sigmoid=1, want_u8=False)
+        net.close()
+        e = np.abs(prob - ref)
+        a, b = prob >= 0.5, ref >= 0.5
+        out[tag] = {"max_abs": float(e.max()), "mean_abs": float(e.mean()),
+                    "dice": float(2.0 * (a & b).sum() / max(int(a.sum() + b.sum()), 1))}
+    return out
+
+
+def run_ink(args):
+    """The layer-stack (wide-ink) workload: each GPU predicts a batch of 8 papyrus stacks of
+    64 x 512 x 512 in one call (fx_infer_opts.stacks = 8: 72 tiles of 64 x 256 x 256, 9 forwards of
+    8), stacks sharded across ranks with no data exchange (weak scaling). value = device-resident
+    fx_predict_volume_dev; e2e = fx_predict_volume with pinned host input and u8 output."""
+    import ctypes as C
+
+    import torch
+
+    import fenix_b200 as fx
+    from fenix_b200.weights import make_plain_unet
+
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    tmp = tempfile.mkdtemp(prefix=f"fxink{rank}_")
+    wpath = make_plain_unet(Path(tmp) / "ink.fxweights", INK_FEATURES_B, ncls=1, seed=INK_WEIGHT_SEED,
+                            strides=INK_STRIDES_B)
+    fp8 = args.precision.startswith("fp8")
+    net = fx.Net(wpath, INK_TILE, max_batch=8, precision="fp8" if fp8 else args.precision, device=local)
+    sched = None
+    if fp8:
+        got = [None]
+        if rank == 0:
+            calib = np.stack([fx.synth_papyrus(INK_TILE, CALIB_SEED0 + i, 0) for i in range(4)])
+            net.calibrate(calib)
+            if args.precision == "fp8":
+                d_cal, m_cal = net.calibrate_schedule(calib, min_dice=SCHED_DICE)
+                sched = {"calibration_dice": d_cal, "calibration_max_abs": m_cal, "target_dice": SCHED_DICE}
+            got = [(net.act_scales().tolist(), [l["precision"] for l in net.layers()], sched)]
+        if world > 1:
+            torch.distributed.broadcast_object_list(got, src=0)
+            if rank != 0:
+                scales, precs, sched = got[0]
+                net.set_act_scales(scales)
+                net.set_layer_precision(["fp8" if p == "fp8" else "f16" for p in precs])
+    dz = INK_SHAPE[0] * INK_STACKS
+    shape = (dz,) + INK_SHAPE[1:]
+    host = torch.from_numpy(np.concatenate([fx.synth_papyrus(INK_SHAPE, INK_VOLUME_SEED, rank * INK_STACKS + k)
+                                            for k in range(INK_STACKS)])).pin_memory()
+    host_out = torch.empty(shape, dtype=torch.uint8).pin_memory()
+    dv = host.cuda()
+    du = torch.empty(shape, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream(device=local)
+
+    def timed(fn, k):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(k):
+            fn()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = ev0.elapsed_time(ev1)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    def dev_step():
+        net.predict_volume_dev(dv.data_ptr(), shape, None, du.data_ptr(), overlap=INK_OVERLAP, batch=8, channel=0,
+                               sigmoid=1, stacks=INK_STACKS, stream=stream.cuda_stream)
+
+    opts = net._opts(INK_OVERLAP, 0, 1, 8, 0, stacks=INK_STACKS)
+    hv, hu = host.numpy(), host_out.numpy()
+
+    def e2e_step():
+        # fx_predict_volume runs on the net's own stream and returns after its D2H copy
+        fx.check(fx.lib().fx_predict_volume(net.handle, hv.ctypes.data_as(C.POINTER(C.c_uint8)), *shape,
+                                            C.byref(opts), None, hu.ctypes.data_as(C.POINTER(C.c_uint8))))
+
+    for _ in range(args.warmup):
+        dev_step()
+    torch.cuda.synchronize()
+    fx.check(fx.lib().fx_net_device_status(net.handle))
+    clocks = ClockSampler(local)
+    clocks.start()
+    l0 = fx.kernel_launches()
+    ms = timed(dev_step, args.steps)
+    launches = fx.kernel_launches() - l0
+    clk = clocks.stop()
+    fx.check(fx.lib().fx_net_device_status(net.handle))
+    e2e_step()
+    t0 = time.perf_counter()
+    barrier()
+    for _ in range(args.steps):
+        e2e_step()
+    barrier()
+    ms_e2e = (time.perf_counter() - t0) * 1e3
+    if world > 1:
+        t = torch.tensor([ms_e2e, float(launches)], dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_e2e = float(t[0].item())
+        launches *= world
+    net.profile(True)
+    dev_step()
+    torch.cuda.synchronize()
+    net.profile(False)
+    prof = net.profile_read()
+    vox = float(np.prod(shape)) * world
+    value = vox * args.steps / (ms / 1e3) / 1e6
+    e2e = vox * args.steps / (ms_e2e / 1e3) / 1e6
+    conv_tflops = prof["conv_flops"] / (prof["conv_ms"] / 1e3) / 1e12
+    f8 = prof["fp8_flops"] / max(prof["conv_flops"], 1.0)
+    cpu = parity = tc = None
+    if rank == 0:
+        tc = measure_tc_peaks(fx, local)
+        if world == 1:
+            parity = ink_parity(fx, tmp, "fp8" if fp8 else args.precision, SCHED_DICE) if INK_PARITY_CASE.exists() else None
+            if not args.no_cpu_baseline:
+                try:
+                    per_tile, thr, secs = ink_cpu_sample(wpath)
+                    cpu = {"value": INK_STACKS * float(np.prod(INK_SHAPE)) / (INK_STACKS * 9 * per_tile) / 1e6,
+                           "unit": "Mvoxels/s", "cores": thr, "kind": "port",
+                           "sample": f"C oracle forward (fp32) of one 16x64x64 tile ({secs:.2f} s), projected per voxel "
+                                     f"to the {INK_STACKS * 9} 64x256x256 tiles of a step"}
+                except Exception as e:
+                    cpu = {"value": None, "unit": "Mvoxels/s", "cores": None, "kind": "port", "sample": f"failed: {e}"}
+
+        def mixed(p8, p16):
+            return 1.0 / (f8 / p8 + (1.0 - f8) / p16)
+
+        peak = mixed(tc["e4m3"]["sustained"], tc["f16"]["sustained"])
+        line = {
+            "metric": INK_METRIC, "value": value, "unit": "Mvoxels/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": {"fp8": "e4m3 + f16 (calibrated schedule)", "fp8-all": "e4m3", "f16": "f16", "bf16": "bf16"}[args.precision],
+            "data": "synthetic: papyrus layer stacks (fibre texture sigma 4/1/1, 110 +- 20, 5% ink columns +25, seed 3, "
+                    "stack k of rank r = series index 8r + k); random-init Kaiming weights (seed 3)",
+            "config": ink_config(world, args.precision),
+            "roofline": {"bound": "tensor", "achieved": conv_tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": conv_tflops / peak, "traffic": None,
+                         "kernel": "conv_tc_kernel (every conv launch of one step, summed)",
+                         "peak_source": "fx_tc_peak sustained e4m3 / f16 rates weighted by the step's e4m3 FLOP share",
+                         "tc_peaks_measured": tc, "conv_ms_per_step": prof["conv_ms"],
+                         "conv_flops_per_step": prof["conv_flops"], "fp8_flop_share": f8,
+                         "conv_share_of_step": prof["conv_ms"] / (ms / args.steps)},
+            "precision_schedule": precision_report(net, sched),
+            "parity": parity,
+            "e2e": {"value": e2e, "unit": "Mvoxels/s", "h2d_bytes_per_step": int(np.prod(shape)) * world,
+                    "d2h_bytes_per_step": int(np.prod(shape)) * world,
+                    "path": "fx_predict_volume (C ABI), pinned host u8 stacks in, u8 out, host-timed per step"},
+            "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    net.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -312,9 +573,13 @@ def main():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fxvol", action="store_true")
+    ap.add_argument("--workload", default="surface", choices=["surface", "ink"],
+                    help="surface: the 1024^3 sliding-window benchmark (default); ink: batches of layer stacks")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "ink":
+        return run_ink_reference(args) if args.impl == "reference" else run_ink(args)
     if args.impl == "reference":
         return run_reference_arm(args)
 

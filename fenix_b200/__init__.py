@@ -63,6 +63,7 @@ class InferOpts(C.Structure):
         ("tile_filter", TileFilter),
         ("tile_filter_user", C.c_void_p),
         ("tile", C.c_int * 3),
+        ("stacks", C.c_int),
     ]
 
 
@@ -122,6 +123,7 @@ def lib():
     _sig(L, "fx_net_create", i32, [C.c_char_p, i32, i32, i32, i32, C.POINTER(vp)])
     _sig(L, "fx_net_destroy", None, [vp])
     _sig(L, "fx_net_patch", i32, [vp])
+    _sig(L, "fx_predict_volume_dev", i32, [vp, vp, i64, i64, i64, C.POINTER(InferOpts), vp, vp, vp])
     _sig(L, "fx_net_create_tiled", i32, [C.c_char_p, C.POINTER(i32), i32, i32, i32, C.POINTER(vp)])
     _sig(L, "fx_net_tile", i32, [vp, C.POINTER(i32), C.POINTER(i32), i32])
     _sig(L, "fx_net_max_batch", i32, [vp])
@@ -306,11 +308,21 @@ class Net:
         n = lib().fx_net_tile(self._h, None, m, 16)
         return list(m[:n])
 
-    def _opts(self, overlap, channel, sigmoid, batch, tta, norm=0, skip=0):
+    def _opts(self, overlap, channel, sigmoid, batch, tta, norm=0, skip=0, stacks=1):
         opts = InferOpts(self.patch or 0, overlap, channel, sigmoid, batch, tta, norm, skip)
         if self.patch is None:
             opts.tile[:] = list(self.tile)
+        opts.stacks = stacks
         return opts
+
+    def predict_volume_dev(self, dev_vol_ptr: int, shape, dev_prob_ptr: int | None, dev_u8_ptr: int | None,
+                           overlap: float = 0.5, batch: int = 1, channel: int = 1, sigmoid: int = 0, stacks: int = 1,
+                           stream: int | None = None) -> None:
+        """fx_predict_volume_dev: device u8 volume in, device f32 map and/or u8 out, asynchronous on
+        `stream`. ``stacks`` > 1: the volume is that many independent stacks along z."""
+        opts = self._opts(overlap, channel, sigmoid, batch, 0, stacks=stacks)
+        self._keep_opts = opts  # the call is asynchronous; the options are read before it returns
+        check(lib().fx_predict_volume_dev(self._h, dev_vol_ptr, *shape, C.byref(opts), dev_prob_ptr, dev_u8_ptr, stream))
 
     def close(self):
         if getattr(self, "_h", None):
@@ -397,12 +409,13 @@ class Net:
 
     def predict_volume(self, vol_u8: np.ndarray, overlap: float = 0.5, batch: int = 1, channel: int = 1,
                        sigmoid: int = 0, want_prob: bool = True, want_u8: bool = True, tta: int = 0,
-                       norm: str = "zscore", skip_constant: bool = False, core=None, tile_filter=None):
+                       norm: str = "zscore", skip_constant: bool = False, core=None, tile_filter=None,
+                       stacks: int = 1):
         """core = (z, y, x, dz, dy, dx) output crop (extents <= 0: to the end); tile_filter =
         callable(z0, y0, x0, patch) -> bool. Outputs have the crop's dims when cropped."""
         v = np.ascontiguousarray(vol_u8, dtype=np.uint8)
         dz, dy, dx = v.shape
-        opts = self._opts(overlap, channel, sigmoid, batch, tta, NORMS[norm], 1 if skip_constant else 0)
+        opts = self._opts(overlap, channel, sigmoid, batch, tta, NORMS[norm], 1 if skip_constant else 0, stacks)
         out_shape = v.shape
         if core is not None:
             opts.core_org[:] = list(core[:3])

@@ -105,6 +105,7 @@ RunOpts run_opts(const fx_infer_opts* o) {
         r.core_org[a] = o->core_org[a];
         r.core_ext[a] = o->core_ext[a];
     }
+    r.stacks = std::max(o->stacks, 1);
     return r;
 }
 
@@ -121,12 +122,16 @@ void crop_box(const fx_infer_opts* o, const int64_t d[3], int64_t co[3], int64_t
 // (resident, dims dz, dy, dx) -> Gaussian blend in d_acc (the crop's dims) -> normalised probability
 // in d_prob (may alias d_acc) and/or u8 in d_u8. Runs on the net's stream and synchronises it.
 fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx,
-                           const fx_infer_opts* o, float* d_acc, float* d_prob, uint8_t* d_u8) {
-    cudaStream_t s = n->net.stream();
+                           const fx_infer_opts* o, float* d_acc, float* d_prob, uint8_t* d_u8, cudaStream_t s,
+                           bool sync) {
+    if (!s) s = n->net.stream();
     const int64_t d[3] = {dz, dy, dx};
     int64_t co[3], ce[3];
     crop_box(o, d, co, ce);
     if (ce[0] < 1 || ce[1] < 1 || ce[2] < 1) return set_err(FX_INVALID_ARGUMENT, "predict: empty output crop");
+    const int ns = std::max(o->stacks, 1);
+    if (ns > 1 && (co[0] || co[1] || co[2] || ce[0] != dz || ce[1] != dy || ce[2] != dx))
+        return set_err(FX_UNSUPPORTED, "predict: stacks take no output crop");
     const size_t nv = static_cast<size_t>(ce[0]) * ce[1] * ce[2];
     cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
     fxk::TileDims tl{};
@@ -138,22 +143,28 @@ fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t 
     std::vector<float> w(static_cast<size_t>(ce[0] + ce[1] + ce[2]));
     size_t at = 0;
     for (int a = 0; a < 3; ++a) {
-        // the factorised weight over the crop's span of each axis (src/ml/infer.hpp:499-509)
+        // the factorised weight over the crop's span of each axis (src/ml/infer.hpp:499-509); with
+        // stacks, the z profile of one stack repeated
         const auto g = fenix::ml::gaussian1d(T[a]);
-        const auto starts = fenix::ml::tile_starts(d[a], T[a], o->overlap);
-        const auto W = fenix::ml::weight_profile(g, starts, co[a], ce[a], d[a], T[a]);
-        std::copy(W.begin(), W.end(), w.begin() + static_cast<std::ptrdiff_t>(at));
-        at += static_cast<size_t>(ce[a]);
+        const int64_t len = a == 0 ? d[0] / ns : d[a];
+        const auto starts = fenix::ml::tile_starts(len, T[a], o->overlap);
+        const auto W = fenix::ml::weight_profile(g, starts, a == 0 && ns > 1 ? 0 : co[a], a == 0 ? ce[0] / ns : ce[a],
+                                                 len, T[a]);
+        for (int k = 0; k < (a == 0 ? ns : 1); ++k) {
+            std::copy(W.begin(), W.end(), w.begin() + static_cast<std::ptrdiff_t>(at));
+            at += W.size();
+        }
     }
-    float* d_w = nullptr;
-    if (cudaMalloc(&d_w, sizeof(float) * w.size()) != cudaSuccess) return set_err(FX_INTERNAL, "cudaMalloc: weight profiles");
+    float* d_w = n->net.profile_buffer(w.size());
+    if (!d_w) return set_err(FX_INTERNAL, "cudaMalloc: weight profiles");
     cudaMemcpyAsync(d_w, w.data(), sizeof(float) * w.size(), cudaMemcpyHostToDevice, s);
     cudaError_t e = fxk::launch_accum_finalize(d_acc, ce[0], ce[1], ce[2], 0, ce[0], d_w, d_w + ce[0],
                                                d_w + ce[0] + ce[1], d_prob, d_u8, s);
-    cudaStreamSynchronize(s);
-    cudaFree(d_w);
     if (e != cudaSuccess) return set_err(cuda_status(e, "accum_finalize"));
-    if ((st = n->net.take_device_status()).code) return set_err(st);  // a bounded wait that gave up
+    if (sync) {
+        if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return set_err(cuda_status(e, "predict"));
+        if ((st = n->net.take_device_status()).code) return set_err(st);  // a bounded wait that gave up
+    }
     return FX_OK;
 }
 }  // namespace fxh
@@ -348,6 +359,31 @@ fx_status fx_net_forward(fx_net* n, const uint8_t* dev_tiles, int nb, float* dev
         if (e != cudaSuccess) return set_err(fxh::cuda_status(e, "forward"));
         if ((st = n->net.take_device_status()).code) return set_err(st);
         return FX_OK;
+    });
+}
+
+fx_status fx_predict_volume_dev(fx_net* n, const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx,
+                                const fx_infer_opts* o, float* dev_prob, uint8_t* dev_u8, void* stream) {
+    return guarded([&]() -> fx_status {
+        if (!n || !dev_vol || !o || (!dev_prob && !dev_u8))
+            return set_err(FX_INVALID_ARGUMENT, "fx_predict_volume_dev: null argument");
+        if (dz < 1 || dy < 1 || dx < 1) return set_err(FX_INVALID_ARGUMENT, "fx_predict_volume_dev: empty volume");
+        fxk::TileDims tl{};
+        if (fx_status r = fxh::opts_tile(o, &tl)) return r;
+        cudaSetDevice(n->net.device());
+        const int64_t d[3] = {dz, dy, dx};
+        int64_t co[3], ce[3];
+        fxh::crop_box(o, d, co, ce);
+        float* acc = dev_prob;
+        if (!acc) {
+            const size_t no = static_cast<size_t>(std::max<int64_t>(ce[0], 1)) * std::max<int64_t>(ce[1], 1) *
+                              std::max<int64_t>(ce[2], 1);
+            uint8_t* unused = nullptr;
+            fxh::Status st = n->net.workspace(0, no * sizeof(float), 0, &unused, &acc, nullptr);
+            if (!st.ok()) return set_err(st);
+        }
+        return fxh::predict_resident(n, dev_vol, dz, dy, dx, o, acc, dev_prob, dev_u8,
+                                     static_cast<cudaStream_t>(stream), false);
     });
 }
 

@@ -1533,6 +1533,20 @@ Status Net::workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint
     return ok();
 }
 
+float* Net::profile_buffer(size_t n) {
+    if (n <= ws_prof_cap_) return ws_prof_;
+    if (ws_prof_) {
+        cudaDeviceSynchronize();
+        cudaFree(ws_prof_);
+        allocs_.erase(std::remove(allocs_.begin(), allocs_.end(), static_cast<void*>(ws_prof_)), allocs_.end());
+        ws_prof_ = nullptr;
+        ws_prof_cap_ = 0;
+    }
+    ws_prof_ = static_cast<float*>(dalloc(sizeof(float) * n));
+    if (ws_prof_) ws_prof_cap_ = n;
+    return ws_prof_;
+}
+
 Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, int64_t z_origin, int64_t full_dz,
                           fxk::TileDims tl, double overlap, int channel, int sigmoid, int batch, int64_t tile_begin,
                           int64_t tile_end, float* d_acc, cudaStream_t s, int64_t acc_z_origin, int64_t acc_dz,
@@ -1543,8 +1557,21 @@ Status Net::predict_tiles(const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t 
     if (batch < 1) batch = 1;
     batch = std::min(batch, Bmax_);
     if (full_dz <= 0) full_dz = dz;
-    const auto zs = tile_starts(full_dz, tz_, overlap), ys = tile_starts(dy, ty_, overlap),
-               xs = tile_starts(dx, tx_, overlap);
+    const int ns = std::max(ro.stacks, 1);
+    std::vector<int64_t> zs;
+    if (ns == 1) {
+        zs = tile_starts(full_dz, tz_, overlap);
+    } else {
+        // independent stacks along z: each stack's own starts, offset to the stack
+        if (full_dz % ns || z_origin != 0 || dz != full_dz)
+            return fail(kInvalid, "predict: stacks must divide the whole volume's depth (no z-slabs)");
+        const int64_t sd = full_dz / ns;
+        if (sd < tz_) return fail(kInvalid, "predict: a stack is thinner than the tile");
+        const auto z1 = tile_starts(sd, tz_, overlap);
+        for (int k = 0; k < ns; ++k)
+            for (int64_t z : z1) zs.push_back(k * sd + z);
+    }
+    const auto ys = tile_starts(dy, ty_, overlap), xs = tile_starts(dx, tx_, overlap);
     const int64_t total = static_cast<int64_t>(zs.size()) * ys.size() * xs.size();
     if (tile_end < 0 || tile_end > total) tile_end = total;
     if (tile_begin < 0) tile_begin = 0;

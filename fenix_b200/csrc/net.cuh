@@ -136,6 +136,9 @@ struct RunOpts {
     // predict_tiles' acc_z_origin / acc_dz).
     int64_t core_org[3] = {0, 0, 0};
     int64_t core_ext[3] = {0, 0, 0};
+    // the volume is this many independent volumes of dz / stacks planes each, stacked along z:
+    // tile starts and the blend run per stack, no tile crosses a stack boundary
+    int stacks = 1;
 };
 
 class Net {
@@ -168,6 +171,9 @@ class Net {
     void set_norm(int norm) { norm_ = norm; }
     // Device workspace for whole-volume calls: grown on demand, kept for the net's lifetime.
     Status workspace(size_t vol_bytes, size_t acc_bytes, size_t out_bytes, uint8_t** vol, float** acc, uint8_t** out);
+    // A device buffer of at least n floats owned by the net (grown on demand; growing synchronises
+    // the device, so a buffer still read by earlier asynchronous work is never freed under it).
+    float* profile_buffer(size_t n);
 
     // the side of a cubic tile, 0 for an anisotropic one
     int patch() const { return tz_ == ty_ && ty_ == tx_ ? tz_ : 0; }
@@ -276,6 +282,8 @@ class Net {
     float* ws_acc_ = nullptr;
     uint8_t* ws_out_ = nullptr;
     size_t ws_vol_cap_ = 0, ws_acc_cap_ = 0, ws_out_cap_ = 0;
+    float* ws_prof_ = nullptr;
+    size_t ws_prof_cap_ = 0;
     cudaStream_t stream_ = nullptr;
     bool calibrated_ = false;
     std::vector<void*> allocs_;
@@ -295,6 +303,8 @@ RunOpts run_opts(const fx_infer_opts* o);
 fx_status opts_tile(const fx_infer_opts* o, fxk::TileDims* t);
 void crop_box(const fx_infer_opts* o, const int64_t d[3], int64_t co[3], int64_t ce[3]);
 // fx_predict_volume's device part (capi.cu), shared with the .fxvol entry points.
+// Runs on stream s (null: the net's stream); sync = wait for it before returning.
 fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx,
-                           const fx_infer_opts* o, float* d_acc, float* d_prob, uint8_t* d_u8);
+                           const fx_infer_opts* o, float* d_acc, float* d_prob, uint8_t* d_u8,
+                           cudaStream_t s = nullptr, bool sync = true);
 }  // namespace fxh

@@ -99,6 +99,13 @@ typedef struct fx_infer_opts {
                     the layer-stack (wide-ink) workload's 64 x 256 x 256, stepped per axis by
                     (int64)(tile[a] * (1 - overlap)) with a Gaussian of sigma tile[a] / 8 per axis.
                     The tile filter's `patch` argument is then tile[0]. TTA needs a cube. */
+    int stacks;  /* >= 2: the volume is `stacks` independent volumes of dz / stacks planes each,
+                    stacked along z (a batch of layer stacks): tile starts, Gaussian weights and
+                    the normalisation run per stack and no tile crosses a stack boundary, so the
+                    result equals predicting each stack alone while every forward fills the
+                    batch. Each stack must be at least one tile deep; no output crop, no z-slabs.
+                    0 or 1: one volume. No reference counterpart (the reference predicts one
+                    volume per call, src/ml/infer.hpp:456). */
 } fx_infer_opts;
 
 typedef struct fx_net fx_net;
@@ -181,6 +188,15 @@ fx_status fx_net_forward(fx_net* net, const uint8_t* dev_tiles, int nb, float* d
  * crop's dims when opts has an output crop (else the input's). */
 fx_status fx_predict_volume(fx_net* net, const uint8_t* host_vol, int64_t dz, int64_t dy, int64_t dx,
                             const fx_infer_opts* opts, float* host_prob, uint8_t* host_u8);
+
+/* fx_predict_volume on device buffers: dev_vol [dz][dy][dx] u8 resident on the net's device; the
+ * normalised probability map into dev_prob (f32, the output's dims; may be NULL) and/or its u8
+ * encoding into dev_u8 (may be NULL; one of the two is required). Runs asynchronously on `stream`
+ * (NULL: the net's stream); the accumulator is dev_prob when given, else the net's workspace. A
+ * bounded wait that gave up inside the call is reported by the next fx_net_device_status. No
+ * reference counterpart: the reference's predict reads and writes host memory. */
+fx_status fx_predict_volume_dev(fx_net* net, const uint8_t* dev_vol, int64_t dz, int64_t dy, int64_t dx,
+                                const fx_infer_opts* opts, float* dev_prob, uint8_t* dev_u8, void* stream);
 
 /* Device-resident sliding window restricted to the flat tile range [tile_begin, tile_end) of the
  * z-major tile grid over a (full_dz, dy, dx) volume (z-slab sharding, the tile grid of

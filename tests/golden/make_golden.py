@@ -8,7 +8,7 @@ Runs only where the reference tree is present (it compiles oracle/_ref from it):
                       + nets::ConvStack through libtorch, fp32, batch 2 so no fp16 round trip) on
                       seeded synthetic volumes with seeded random-init plain UNets: the u8-encoded
                       probability map, exact f32 values at 4096 sampled voxels, and sum / mean.
-  * net128_<case>.npz — the BASELINE configurations at their own 128^3 tile size, with the FULL
+  * net128_<case>.npz — the benchmark configurations at their own 128^3 tile size, with the FULL
                       probability map (quantised to u16: round(p * 65535), error <= 7.7e-6):
                       config 1 (one 128^3 tile, 16/32/64/128 net, weight seed 0), config 2 (two
                       128^3 patches in one batch of 2, 32..320 net, weight seed 1, volume seed 1) and
@@ -21,6 +21,12 @@ Runs only where the reference tree is present (it compiles oracle/_ref from it):
                       tile filter of predict-scroll, and a one-class sigmoid head.
   * resenc_<case>.npz — the same with the reference's own nets::ResEncUNet (residual encoder,
                       optional scSE, plain or task naming) loaded from seeded random-init weights.
+  * ink_<case>.npz — the layer-stack (wide-ink) net: 64/128/256/512 features, stride (1, 2, 2) at
+                      stages 1-2 and (2, 2, 2) at stage 3, one class + sigmoid, anisotropic tiles.
+                      The reference's nets take one int stride per stage and its window tiles cubes,
+                      so this map comes from the C ORACLE (fxo_predict_tiled), whose cube path the
+                      net_* / net128_* fixtures pin against the reference and whose anisotropic
+                      forward tests/test_ink_oracle.py checks against PyTorch fp32. Full map as u16.
   * fxvol_tiles.npz — the reference's encode_tile_dct payloads of the 64^3 chunks of
                       tests/golden/fxvol_cases.py, and SHA-256 digests of its decode_tile_dct output
                       (u8, and the f32 reconstruction) of those payloads (oracle/_ref/ref_fxvol).
@@ -95,6 +101,28 @@ def feat_volume(name):
     if name == "skipconst":
         vol[:72] = 40
     return vol
+
+
+# name: (weight seed, stack shape, papyrus seed, stack index, tile (z, y, x), overlap)
+INK = {
+    "small": (3, (24, 112, 112), 3, 0, (16, 64, 64), 0.25),
+}
+
+
+def ink_case(name):
+    from fenix_b200.weights import INK_FEATURES, INK_STRIDES
+    from oracle import netgen
+
+    wseed, shape, vseed, stack, tile, ov = INK[name]
+    vol = orc.synth_papyrus(shape, vseed, stack)
+    with tempfile.TemporaryDirectory() as td:
+        w = netgen.make_plain_unet(Path(td) / "w.fxweights", INK_FEATURES, ncls=1, seed=wseed, strides=INK_STRIDES)
+        prob = orc.Net(w).predict_tiled(vol, tile, ov, channel=0, sigmoid=1)
+    np.savez_compressed(HERE / f"ink_{name}.npz", features=np.array(INK_FEATURES), strides=np.array(INK_STRIDES),
+                        weight_seed=wseed, shape=np.array(shape), volume_seed=vseed, stack=stack, tile=np.array(tile),
+                        overlap=ov, prob_u16=np.round(prob.astype(np.float64) * 65535.0).astype(np.uint16),
+                        source="oracle")
+    print(f"ink_{name}: mean {prob.mean():.4f}, > 0.5: {(prob > 0.5).mean():.3f}")
 
 
 # name: (features, blocks, scSE, plain naming, weight seed, volume shape, volume seed, patch, overlap)
@@ -277,6 +305,9 @@ def main():
     for name in RESENC:
         if a.only in (None, "resenc_" + name):
             resenc_case(name)
+    for name in INK:
+        if a.only in (None, "ink_" + name):
+            ink_case(name)
     if a.only in (None, "fxvol"):
         fxvol()
 

@@ -52,7 +52,7 @@ def forward(params: dict, x: torch.Tensor, types: dict | None = None, scales: di
     y/x-only stage); a one-class head is a sigmoid."""
     types = types or {}
     scales = scales or {}
-    T = {k: torch.from_numpy(np.asarray(v)) for k, v in params.items()}
+    T = {k: torch.from_numpy(np.asarray(v)).to(x.device) for k, v in params.items()}
     S = sum(1 for k in T if k.startswith("encoder.stages.") and k.endswith(".convs.0.conv.weight"))
     nconv = sum(1 for k in T if k.startswith("encoder.stages.0.convs.") and k.endswith(".conv.weight"))
     pre_kind = prenorm if prenorm is not None else ("f32" if default == "f32" and not types else "f16")

@@ -11,6 +11,8 @@ a 1x1x1 head + sigmoid), so the parity reference is that network computed in fp3
 
 Bounds as everywhere: 16-bit operands max-abs <= 1e-2 against fp32; e4m3 operands against the
 model with the same operand rounding (kernel parity) and Dice against fp32."""
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -20,6 +22,7 @@ from fenix_b200.weights import INK_FEATURES, INK_STRIDES, make_plain_unet, plain
 pytestmark = pytest.mark.gpu
 
 TOL16 = 1e-2
+GOLD = Path(__file__).resolve().parent / "golden"
 
 
 def zscore(t):
@@ -117,4 +120,106 @@ def test_ink_tile_rejections(cuda_torch, tmp_path):
     vol = ink_tiles((16, 64, 64), 1, 5)[0]
     with pytest.raises(fx.FxError):
         net.predict_volume(vol, overlap=0.25, batch=1, sigmoid=1, channel=0, tta=8)
+    net.close()
+
+
+def test_ink_window_matches_oracle_map(cuda_torch, tmp_path):
+    """The anisotropic sliding window (per-axis tile starts, Gaussians of sigma tile / 8, blend,
+    normalisation) on a papyrus stack against the C oracle's full map (tests/golden/ink_small.npz):
+    every voxel, f16 <= 1e-2 max-abs; the calibrated fp8 schedule Dice >= 0.99."""
+    g = np.load(GOLD / "ink_small.npz")
+    w = make_plain_unet(tmp_path / "ink.fxweights", INK_FEATURES, ncls=1, seed=int(g["weight_seed"]),
+                        strides=INK_STRIDES)
+    tile = tuple(int(v) for v in g["tile"])
+    vol = fx.synth_papyrus(tuple(int(v) for v in g["shape"]), int(g["volume_seed"]), int(g["stack"]))
+    ref = g["prob_u16"].astype(np.float32) / np.float32(65535.0)
+    net = fx.Net(w, tile, max_batch=4, precision="f16")
+    prob, u8 = net.predict_volume(vol, overlap=float(g["overlap"]), batch=4, channel=0, sigmoid=1)
+    net.close()
+    e = np.abs(prob - ref)
+    d = dice(prob >= 0.5, ref >= 0.5)
+    print(f"ink window f16 vs oracle: max-abs {e.max():.3e} mean {e.mean():.3e} Dice {d:.5f} over {prob.size} voxels")
+    assert float(e.max()) <= TOL16 and d >= 0.99
+    assert np.abs(u8.astype(int) - np.clip(np.floor(ref * 255 + 0.5), 0, 255).astype(int)).max() <= 3
+    net = fx.Net(w, tile, max_batch=4, precision="fp8")
+    cal = np.stack([fx.synth_papyrus(tile, 1000 + i, 0) for i in range(4)])
+    dc, mc = net.calibrate_schedule(cal, min_dice=0.993)
+    f8 = [l["name"] for l in net.layers() if l["precision"] == "fp8"]
+    prob8, _ = net.predict_volume(vol, overlap=float(g["overlap"]), batch=4, channel=0, sigmoid=1)
+    net.close()
+    e8 = np.abs(prob8 - ref)
+    d8 = dice(prob8 >= 0.5, ref >= 0.5)
+    print(f"ink window fp8 schedule ({len(f8)} e4m3 layers {f8}, calibration Dice {dc:.5f}): vs oracle max-abs "
+          f"{e8.max():.3e} mean {e8.mean():.3e} Dice {d8:.5f}")
+    assert d8 >= 0.99
+
+
+def test_ink_full_stack_matches_fp32(cuda_torch, tmp_path):
+    """The workload's own sizes: one 64 x 512 x 512 papyrus stack in 64 x 256 x 256 tiles at
+    overlap 0.25 (1 x 3 x 3 tiles). Reference = every tile through the fp32 PyTorch network on the
+    GPU (TF32 off) and the per-axis Gaussian blend in float64; the f16 path must agree to 1e-2 on
+    every one of the 16.8 M voxels."""
+    torch = cuda_torch
+    import quant_model as qm
+    from oracle import oracle as orc
+
+    tile, ov, shape = (64, 256, 256), 0.25, (64, 512, 512)
+    params = plain_unet_params(INK_FEATURES, ncls=1, seed=3, strides=INK_STRIDES)
+    w = make_plain_unet(tmp_path / "ink.fxweights", INK_FEATURES, ncls=1, seed=3, strides=INK_STRIDES)
+    vol = fx.synth_papyrus(shape, 3, 0)
+    net = fx.Net(w, tile, max_batch=2, precision="f16")
+    prob, _ = net.predict_volume(vol, overlap=ov, batch=2, channel=0, sigmoid=1, want_u8=False)
+    net.close()
+    starts = [orc.tile_starts(shape[a], tile[a], ov) for a in range(3)]
+    gw = [orc.gaussian1d(tile[a]).astype(np.float64) for a in range(3)]
+    wt = gw[0][:, None, None] * gw[1][None, :, None] * gw[2][None, None, :]
+    acc = np.zeros(shape, np.float64)
+    wsum = np.zeros(shape, np.float64)
+    old = (torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32)
+    torch.backends.cudnn.allow_tf32 = torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for z0 in starts[0]:
+            for y0 in starts[1]:
+                for x0 in starts[2]:
+                    t = vol[z0:z0 + tile[0], y0:y0 + tile[1], x0:x0 + tile[2]]
+                    x = torch.from_numpy(zscore(t))[None, None].cuda()
+                    with torch.no_grad():
+                        p = qm.forward(params, x)[0].double().cpu().numpy()
+                    acc[z0:z0 + tile[0], y0:y0 + tile[1], x0:x0 + tile[2]] += wt * p
+                    wsum[z0:z0 + tile[0], y0:y0 + tile[1], x0:x0 + tile[2]] += wt
+    finally:
+        torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32 = old
+    ref = acc / wsum
+    e = np.abs(prob - ref)
+    d = dice(prob >= 0.5, ref >= 0.5)
+    print(f"ink full stack {shape} f16 vs fp32: max-abs {e.max():.3e} mean {e.mean():.3e} Dice {d:.5f}")
+    assert float(e.max()) <= TOL16 and d >= 0.99
+
+
+def test_ink_stacks_batch_equals_single_stacks(cuda_torch, tmp_path):
+    """A batch of layer stacks in one call (fx_infer_opts.stacks) equals predicting each stack
+    alone: tile starts and blend run per stack, no tile crosses a stack boundary (only the
+    grouping of tiles into forwards differs). The device-resident entry point
+    (fx_predict_volume_dev) equals the host one bit for bit."""
+    torch = cuda_torch
+    tile = (16, 64, 64)
+    w = make_plain_unet(tmp_path / "ink.fxweights", INK_FEATURES, ncls=1, seed=3, strides=INK_STRIDES)
+    stacks = [fx.synth_papyrus((24, 112, 96), 3, k) for k in range(3)]
+    net = fx.Net(w, tile, max_batch=8, precision="f16")
+    single = [net.predict_volume(v, overlap=0.25, batch=8, channel=0, sigmoid=1)[0] for v in stacks]
+    vol = np.concatenate(stacks, 0)
+    prob, u8 = net.predict_volume(vol, overlap=0.25, batch=8, channel=0, sigmoid=1, stacks=3)
+    err = max(float(np.abs(prob[24 * k:24 * (k + 1)] - single[k]).max()) for k in range(3))
+    print(f"ink stacks: batched vs single max-abs {err:.2e}")
+    assert err <= 1e-3
+    dv = torch.from_numpy(vol).cuda()
+    dp = torch.zeros(vol.shape, dtype=torch.float32, device="cuda")
+    du = torch.zeros(vol.shape, dtype=torch.uint8, device="cuda")
+    net.predict_volume_dev(dv.data_ptr(), vol.shape, dp.data_ptr(), du.data_ptr(), overlap=0.25, batch=8, channel=0,
+                           sigmoid=1, stacks=3, stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    fx.check(fx.lib().fx_net_device_status(net.handle))
+    assert np.array_equal(dp.cpu().numpy(), prob) and np.array_equal(du.cpu().numpy(), u8)
+    with pytest.raises(fx.FxError):  # a stack thinner than the tile
+        net.predict_volume(np.zeros((30, 64, 64), np.uint8), overlap=0.25, batch=2, channel=0, sigmoid=1, stacks=2)
     net.close()
