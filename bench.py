@@ -264,6 +264,22 @@ def measure_tc_peaks(fx, device):
     return out
 
 
+def layer_times(net, step, tiles):
+    """One more profiled step, summed per conv layer: ms per step, operand type and achieved
+    TFLOP/s (algorithmic FLOPs per tile x tiles of the step / the layer's summed launch time)."""
+    import torch
+
+    net.profile(True)
+    step()
+    torch.cuda.synchronize()
+    net.profile(False)
+    out = []
+    for l in net.profile_read_layers():
+        out.append({"layer": l["name"], "precision": l["precision"], "ms": round(l["ms"], 3),
+                    "tflops": round(l["flops"] * tiles / max(l["ms"], 1e-9) / 1e9, 1)})
+    return out
+
+
 def vox_of(S):
     return float(S) ** 3
 
@@ -506,6 +522,7 @@ def run_ink(args):
     torch.cuda.synchronize()
     net.profile(False)
     prof = net.profile_read()
+    layer_table = layer_times(net, dev_step, float(INK_STACKS * 9))
     vox = float(np.prod(shape)) * world
     value = vox * args.steps / (ms / 1e3) / 1e6
     e2e = vox * args.steps / (ms_e2e / 1e3) / 1e6
@@ -546,6 +563,7 @@ def run_ink(args):
                          "conv_flops_per_step": prof["conv_flops"], "fp8_flop_share": f8,
                          "conv_share_of_step": prof["conv_ms"] / (ms / args.steps)},
             "precision_schedule": precision_report(net, sched),
+            "conv_layers": layer_table,
             "parity": parity,
             "e2e": {"value": e2e, "unit": "Mvoxels/s", "h2d_bytes_per_step": int(np.prod(shape)) * world,
                     "d2h_bytes_per_step": int(np.prod(shape)) * world,
@@ -696,6 +714,7 @@ def main():
     dev_step()
     net.profile(False)
     prof = net.profile_read()
+    layer_table = layer_times(net, dev_step, float(len(fx.tile_starts(S, P, args.overlap)) ** 3))
     h2d, d2h = sp.h2d_bytes, sp.d2h_bytes
     if world > 1:
         t = torch.tensor([float(launches), float(h2d), float(d2h)], dtype=torch.float64)
@@ -779,6 +798,7 @@ def main():
                 "nominal": "4.5 PFLOP/s e4m3, 2.25 PFLOP/s 16-bit (dense)",
             },
             "precision_schedule": precision_report(net, sched),
+            "conv_layers": layer_table,
             "parity": parity,
             "other_schedules": others,
             "e2e": {"value": e2e, "unit": "Mvoxels/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -171,6 +171,7 @@ def lib():
     _sig(L, "fx_net_profile", i32, [vp, i32])
     _sig(L, "fx_net_profile_read", i32, [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_double),
                                          C.POINTER(C.c_int64), C.POINTER(C.c_double), i32])
+    _sig(L, "fx_net_profile_read_layers", i32, [vp, C.POINTER(C.c_double), i32])
     _sig(L, "fx_kernel_launches", C.c_ulonglong, [])
     _sig(L, "fx_tc_peak", i32, [i32, i32, C.c_double, i32, C.POINTER(C.c_double), C.POINTER(C.c_double)])
     _sig(L, "fx_synth_spiral", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
@@ -402,6 +403,15 @@ class Net:
         k = min(n.value, per_launch_cap)
         return {"conv_ms": ms.value, "conv_flops": fl.value, "fp8_flops": f8.value, "conv_launches": n.value,
                 "per_launch": per[: 2 * k].reshape(k, 2)}
+
+    def profile_read_layers(self) -> list[dict]:
+        """The profiled conv time per layer (fx_net_profile_read_layers), with each layer's name,
+        precision and algorithmic FLOPs per tile; clears the record."""
+        buf = np.zeros(1024, dtype=np.float64)
+        n = lib().fx_net_profile_read_layers(self._h, buf.ctypes.data_as(C.POINTER(C.c_double)), 1024)
+        if n < 0:
+            raise FxError(8, lib().fx_last_error().decode())
+        return [dict(l, ms=float(buf[i])) for i, l in enumerate(self.layers()[:n])]
 
     def forward_dev(self, dev_tiles_ptr: int, nb: int, dev_prob_ptr: int, channel: int = 1, sigmoid: int = 0,
                     stream: int | None = None) -> None:

@@ -532,6 +532,21 @@ fx_status fx_net_profile_read(fx_net* n, double* conv_ms, double* conv_flops, do
     });
 }
 
+int fx_net_profile_read_layers(fx_net* n, double* layer_ms, int cap) {
+    int out = -1;
+    const fx_status r = guarded([&]() -> fx_status {
+        if (!n) return set_err(FX_INVALID_ARGUMENT, "fx_net_profile_read_layers: null net");
+        fxh::Net::ProfileTotals t;
+        std::vector<double> per;
+        fxh::Status st = n->net.profile_read(t, nullptr, 0, &per);
+        if (!st.ok()) return set_err(st);
+        for (int i = 0; layer_ms && i < cap && i < static_cast<int>(per.size()); ++i) layer_ms[i] = per[i];
+        out = static_cast<int>(per.size());
+        return FX_OK;
+    });
+    return r == FX_OK ? out : -1;
+}
+
 unsigned long long fx_kernel_launches(void) { return fxk::launch_count(); }
 
 void fx_conv_trace_buffer(void* dev_counters) { fxh::g_conv_trace = static_cast<unsigned long long*>(dev_counters); }

@@ -262,6 +262,10 @@ fx_status fx_ipc_close(int device, void* dev_ptr);
 fx_status fx_net_profile(fx_net* net, int enable);
 fx_status fx_net_profile_read(fx_net* net, double* conv_ms, double* conv_flops, double* fp8_flops,
                               int64_t* conv_launches, double* per_launch, int cap);
+/* The same record summed per conv layer (fx_net_layer_precision order): layer_ms[i] = the summed
+ * duration of layer i's launches, for up to `cap` layers; also clears the record. Returns the
+ * layer count, or -1 on error (fx_last_error). */
+int fx_net_profile_read_layers(fx_net* net, double* layer_ms, int cap);
 /* The dense tcgen05 tensor rate of `device`, measured with this library's own kernel: one CTA per SM
  * issuing M = 128, N = 256 MMAs back to back on shared-memory-resident operands (kind::f8f6f4 e4m3
  * for FX_PREC_FP8, kind::f16 for bf16 / f16) into TMEM. `runs` launches of about ms_per_run each:

@@ -308,6 +308,54 @@ inline Expected<void> run(VolumeView<const u8> in, B200Net& net, const InferOpti
     return out;
 }
 
+// The same over several GPUs (the reference's one model replica per visible device,
+// src/ml/inference.cpp:1129-1188): the volume is split into z-slabs by contiguous ranges of the
+// tile grid, one host thread per net predicts its slab on its device, each owner adds the tile
+// overlap bands its neighbours accumulated by reading their device memory directly (peer access
+// over NVLink / NVSwitch, no NCCL), finalises the planes it owns and copies them to the output.
+// Equals predict_surface up to the order of the band sums. The nets share weights, precision and
+// (fp8) activation scales and schedule; two nets may share a device. No output crop.
+namespace detail {
+inline Expected<void> run_multi(VolumeView<const u8> in, std::span<B200Net* const> nets, const InferOptions& opt,
+                                float* prob, u8* u8out) {
+    if (nets.empty()) return err(Errc::invalid_argument, "predict_surface_multi: no nets");
+    std::vector<fx_net*> h;
+    int batch = 1 << 30;
+    for (B200Net* n : nets) {
+        if (!n || !*n) return err(Errc::invalid_argument, "predict_surface_multi: empty net");
+        if (opt.patch != n->patch()) return err(Errc::invalid_argument, "predict_surface_multi: patch differs from a net's");
+        h.push_back(n->handle());
+        batch = std::min(batch, n->batch());
+    }
+    const Extent3 d = in.dims();
+    if (d.z < 1 || d.y < 1 || d.x < 1 || !in.data()) return err(Errc::invalid_argument, "predict_surface_multi: empty volume");
+    auto o = to_fx(opt);
+    if (!o) return std::unexpected(o.error());
+    if (o->batch > batch) o->batch = batch;
+    std::vector<u8> tmp;
+    const u8* src = contiguous_input(in, tmp);
+    const fx_status st =
+        fx_predict_volume_multi(h.data(), static_cast<int>(h.size()), src, d.z, d.y, d.x, &*o, prob, u8out);
+    if (st != FX_OK) return err_status(st, "predict_surface_multi");
+    return {};
+}
+}  // namespace detail
+
+[[nodiscard]] inline Expected<Volume<f32>> predict_surface_multi(VolumeView<const u8> in, std::span<B200Net* const> nets,
+                                                                 const InferOptions& opt = {}) {
+    Volume<f32> out(in.dims());
+    if (auto r = detail::run_multi(in, nets, opt, out.data(), nullptr); !r) return std::unexpected(r.error());
+    return out;
+}
+
+[[nodiscard]] inline Expected<Volume<u8>> predict_surface_multi_u8(VolumeView<const u8> in,
+                                                                   std::span<B200Net* const> nets,
+                                                                   const InferOptions& opt = {}) {
+    Volume<u8> out(in.dims());
+    if (auto r = detail::run_multi(in, nets, opt, nullptr, out.data()); !r) return std::unexpected(r.error());
+    return out;
+}
+
 // predict_surface_filled (src/ml/infer.hpp:452-458): the input comes from a caller's filler,
 // fill(z0, y0, x0, P, float* out) writing the P^3 patch at that origin (out of the volume it must
 // clamp, as the reference's fillers do). The device path normalises u8 levels exactly, so every
@@ -467,13 +515,14 @@ private:
 
 // Arguments of the predict-surface stage: <in> <weights> <out> [patch] [overlap] [tta] [batch],
 // positional slots holding a key=value token are skipped, then key=value options. Keys this path
-// adds: precision=f16|bf16|fp8 and device=N.
+// adds: precision=f16|bf16|fp8, device=N and gpus=N (devices [device, device + N), one replica each).
 struct PredictArgs {
     std::string in, weights, out;
     InferOptions opt;
     bool batch_explicit = false;
     Precision precision = Precision::f16;
     int device = 0;
+    int gpus = 1;
 };
 
 [[nodiscard]] inline Expected<PredictArgs> parse_predict_args(std::span<const std::string_view> args,
@@ -530,6 +579,9 @@ struct PredictArgs {
             a.batch_explicit = true;
         } else if (k == "device") {
             if (auto r = to_int(v, a.device); !r) return std::unexpected(r.error());
+        } else if (k == "gpus") {
+            if (auto r = to_int(v, a.gpus); !r) return std::unexpected(r.error());
+            if (a.gpus < 1) return err(Errc::invalid_argument, "predict: gpus must be >= 1");
         } else if (k == "precision") {
             if (v == "f16" || v == "half") a.precision = Precision::f16;
             else if (v == "bf16") a.precision = Precision::bf16;

@@ -100,6 +100,21 @@ inline Expected<void> calibrate_fp8(B200Net& net, std::span<const u8> patches, i
     return {};
 }
 
+// The activation scales and per-layer precision schedule of a calibrated fp8 net, onto another
+// replica of the same weights.
+inline Expected<void> copy_fp8_state(const B200Net& from, B200Net& to) {
+    std::vector<float> sc(1024);
+    const int ns = fx_net_act_scales(from.handle(), sc.data(), static_cast<int>(sc.size()));
+    std::vector<int> pr(1024);
+    const int np = fx_net_layer_precision(from.handle(), pr.data(), nullptr, static_cast<int>(pr.size()));
+    if (ns < 0 || ns > static_cast<int>(sc.size()) || np < 0 || np > static_cast<int>(pr.size()))
+        return err(Errc::internal, "copy_fp8_state: too many layers");
+    fx_status st = fx_net_set_act_scales(to.handle(), sc.data(), ns);
+    if (st == FX_OK) st = fx_net_set_layer_precision(to.handle(), pr.data(), np);
+    if (st != FX_OK) return err_status(st, "copy_fp8_state");
+    return {};
+}
+
 inline float predict_q() {
     const char* e = std::getenv("FENIX_PREDICT_Q");
     const float q = e ? static_cast<float>(std::atof(e)) : 0.0f;
@@ -119,15 +134,29 @@ inline float predict_q() {
     auto net = B200Net::load(a->weights, a->opt.patch, a->opt.batch, a->precision, a->device);
     if (!net) return std::unexpected(net.error());
     const float q = detail::predict_q();
-    if (a->precision != Precision::fp8) {
+    if (a->precision != Precision::fp8 && a->gpus == 1) {
         if (auto r = predict_surface_fxvol(*net, a->in, a->out, a->opt, q); !r) return std::unexpected(r.error());
         return 0;
     }
     auto vol = in->read_volume_u8();
     if (!vol) return std::unexpected(vol.error());
-    const auto cal = detail::calibration_patches(static_cast<const Volume<u8>&>(*vol).view(), a->opt.patch, a->opt.overlap);
-    if (auto r = detail::calibrate_fp8(*net, cal, 4); !r) return std::unexpected(r.error());
-    auto pred = predict_surface_u8(static_cast<const Volume<u8>&>(*vol).view(), *net, a->opt);
+    const VolumeView<const u8> v = static_cast<const Volume<u8>&>(*vol).view();
+    if (a->precision == Precision::fp8) {
+        const auto cal = detail::calibration_patches(v, a->opt.patch, a->opt.overlap);
+        if (auto r = detail::calibrate_fp8(*net, cal, 4); !r) return std::unexpected(r.error());
+    }
+    // gpus = N: replicas on devices [device, device + N) with net 0's scales and schedule
+    std::vector<B200Net> more;
+    std::vector<B200Net*> all{&*net};
+    for (int g = 1; g < a->gpus; ++g) {
+        auto m = B200Net::load(a->weights, a->opt.patch, a->opt.batch, a->precision, a->device + g);
+        if (!m) return std::unexpected(m.error());
+        if (a->precision == Precision::fp8)
+            if (auto r = detail::copy_fp8_state(*net, *m); !r) return std::unexpected(r.error());
+        more.push_back(std::move(*m));
+    }
+    for (B200Net& m : more) all.push_back(&m);
+    auto pred = a->gpus == 1 ? predict_surface_u8(v, *net, a->opt) : predict_surface_multi_u8(v, all, a->opt);
     if (!pred) return std::unexpected(pred.error());
     auto out = codec::VolumeArchive::create(a->out, pred->dims(), {q}, codec::DType::u8, a->device);
     if (!out) return std::unexpected(out.error());

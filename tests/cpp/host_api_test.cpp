@@ -54,6 +54,8 @@ static int cpu() {
     CHECK(parse({"in", "w", "out", "scales=0.8,1.0"}).error().code == Errc::unsupported);
     CHECK(parse({"in", "w", "out", "bogus=1"}).error().code == Errc::invalid_argument);
     CHECK(parse({"in", "w", "out", "precision=int4"}).error().code == Errc::invalid_argument);
+    CHECK(parse({"in", "w", "out", "gpus=4"}) && parse({"in", "w", "out", "gpus=4"})->gpus == 4);
+    CHECK(parse({"in", "w", "out", "gpus=0"}).error().code == Errc::invalid_argument);
     {
         ml::InferOptions o;
         o.norm = ml::Norm::pct_minmax;
@@ -261,6 +263,25 @@ static int stages(const char* weights, const char* dir) {
             bool zero = true;
             for (s64 i = 0; i < 32 * d.y * d.x; ++i) zero &= q->data()[i] == 0.0f;
             CHECK(zero);
+        }
+    }
+    {  // the multi-GPU driver with two replicas (here on one device): z-slab shards, band sums
+        auto n2 = ml::B200Net::load(weights, 64, 2);
+        CHECK(n2.has_value());
+        if (n2) {
+            std::vector<ml::B200Net*> nets{&*net, &*n2};
+            auto m = ml::predict_surface_multi(in, nets, o);
+            auto p = ml::predict_surface(in, *net, o);
+            CHECK(m && p);
+            if (m && p) {
+                float worst = 0;
+                for (std::size_t i = 0; i < vol.size(); ++i) worst = std::max(worst, std::fabs(m->data()[i] - p->data()[i]));
+                std::fprintf(stderr, "predict_surface_multi (2 replicas) vs predict_surface: max |d| %.3g\n", worst);
+                CHECK(worst <= 1e-5f);
+            }
+            std::vector<ml::B200Net*> none;
+            auto e = ml::predict_surface_multi(in, none, o);
+            CHECK(!e && e.error().code == Errc::invalid_argument);
         }
     }
     std::printf("%s\n", fails ? "FAIL" : "ok");

@@ -200,7 +200,8 @@ def test_ink_stacks_batch_equals_single_stacks(cuda_torch, tmp_path):
     """A batch of layer stacks in one call (fx_infer_opts.stacks) equals predicting each stack
     alone: tile starts and blend run per stack, no tile crosses a stack boundary (only the
     grouping of tiles into forwards differs). The device-resident entry point
-    (fx_predict_volume_dev) equals the host one bit for bit."""
+    (fx_predict_volume_dev) equals the host one up to the order of the blend's atomic adds (up to
+    eight tiles cover a voxel here, so float sums may round differently)."""
     torch = cuda_torch
     tile = (16, 64, 64)
     w = make_plain_unet(tmp_path / "ink.fxweights", INK_FEATURES, ncls=1, seed=3, strides=INK_STRIDES)
@@ -219,7 +220,10 @@ def test_ink_stacks_batch_equals_single_stacks(cuda_torch, tmp_path):
                            sigmoid=1, stacks=3, stream=torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     fx.check(fx.lib().fx_net_device_status(net.handle))
-    assert np.array_equal(dp.cpu().numpy(), prob) and np.array_equal(du.cpu().numpy(), u8)
+    e_dev = float(np.abs(dp.cpu().numpy() - prob).max())
+    print(f"ink stacks: device entry vs host entry max-abs {e_dev:.2e}")
+    assert e_dev <= 1e-6
+    assert np.abs(du.cpu().numpy().astype(int) - u8.astype(int)).max() <= 1
     with pytest.raises(fx.FxError):  # a stack thinner than the tile
         net.predict_volume(np.zeros((30, 64, 64), np.uint8), overlap=0.25, batch=2, channel=0, sigmoid=1, stacks=2)
     net.close()
