@@ -578,6 +578,118 @@ def run_ink(args):
     return 0
 
 
+STREAM_METRIC = "Mvoxels/s fp8 out-of-core streaming surface inference (finalised u8 output) @1..8 B200"
+STREAM_SHAPE, STREAM_PATCH, STREAM_OVERLAP, STREAM_SEED = (2048, 4096, 4096), 192, 0.5, 4
+
+
+def run_stream(args):
+    """The out-of-core workload (a bounded sample of it): the 2048 x 4096 x 4096 spiral volume with
+    noise keyed per 64^3 chunk (seed 4, pitch 14), 192^3 tiles at overlap 0.5 (21 x 42 x 42 tile
+    grid), the benchmark's 5-stage net with the calibrated fp8 schedule. Input planes stream from
+    pinned host memory one tile row (1764 tiles) at a time into the device-resident global
+    accumulator (fx_gaccum_predict_row: H2D of the row's 192 planes, every tile of the row, blend),
+    and each row finalises the 64-plane chunk rows no later row reaches (fx_gaccum_finalize_below:
+    normalise, u8, D2H into pinned memory). One step = one tile row; value = finalised output
+    voxels / wall time of the steps, host copies included (the workload is the stream). Ranks take
+    disjoint row ranges of the grid with their own accumulators (no exchange: each rank's first
+    chunk rows lack the contributions of the rows below its range, which a full run would add)."""
+    import ctypes as C
+
+    import torch
+
+    import fenix_b200 as fx
+    from fenix_b200.gaccum import GlobalAccum
+    from fenix_b200.weights import make_plain_unet
+
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+    P, ov = STREAM_PATCH, STREAM_OVERLAP
+    dz, dy, dx = STREAM_SHAPE
+    zs = fx.tile_starts(dz, P, ov)
+    need = args.warmup + args.steps
+    if need > len(zs) - 1:
+        raise SystemExit(f"stream: warmup + steps must be < {len(zs) - 1} tile rows")
+    r0 = min(rank * need, len(zs) - 1 - need)
+    tmp = tempfile.mkdtemp(prefix=f"fxstream{rank}_")
+    wpath = make_plain_unet(Path(tmp) / "w.fxweights", FEATURES, seed=WEIGHT_SEED)
+    net = fx.Net(wpath, P, max_batch=args.batch, precision="fp8", device=local)
+    calib = np.stack([fx.synth_spiral((P, P, P), CALIB_SEED0 + i, fx.SPIRAL_CONFIG3) for i in range(4)])
+    net.calibrate(calib)
+    d_cal, m_cal = net.calibrate_schedule(calib, min_dice=SCHED_DICE)
+    z_lo, z_hi = int(zs[r0]), int(zs[r0 + need]) + P
+    host_in = torch.empty((z_hi - z_lo, dy, dx), dtype=torch.uint8).pin_memory()
+    fx.synth_spiral(STREAM_SHAPE, STREAM_SEED, fx.SPIRAL_CONFIG5, z_lo, z_hi, chunked=True, out=host_in.numpy())
+    host_out = torch.empty((2 * 64 * 2, dy, dx), dtype=torch.uint8).pin_memory()
+    acc = GlobalAccum((0, 0, 0), STREAM_SHAPE, P, ov, device=local)
+    acc.set_floor_row(z_lo // 64)
+    hin = host_in.numpy()
+    out_ptr = host_out.numpy().ctypes.data_as(C.POINTER(C.c_uint8))
+    fin = C.c_int64()
+    vox = [0]
+
+    def step(zi):
+        a = int(zs[zi]) - z_lo
+        acc.predict_row(net, zi, hin[a:a + P], batch=args.batch)
+        lim = int(zs[zi + 1]) // 64
+        fx.check(fx.lib().fx_gaccum_finalize_below(acc._h, lim, out_ptr, host_out.numel(), C.byref(fin)))
+        vox[0] += fin.value * dy * dx
+
+    for k in range(args.warmup):
+        step(r0 + k)
+    clocks = ClockSampler(local)
+    clocks.start()
+    l0 = fx.kernel_launches()
+    vox[0] = 0
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        step(r0 + args.warmup + k)
+    secs = time.perf_counter() - t0
+    launches = fx.kernel_launches() - l0
+    clk = clocks.stop()
+    tot = np.array([vox[0], secs, launches], dtype=np.float64)
+    if world > 1:
+        t = torch.tensor(tot)
+        torch.distributed.all_reduce(t)
+        m = torch.tensor([secs], dtype=torch.float64)
+        torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
+        tot = t.numpy()
+        secs = float(m.item())
+    value = tot[0] / secs / 1e6
+    if rank == 0:
+        rows = len(zs) * len(fx.tile_starts(dy, P, ov)) * len(fx.tile_starts(dx, P, ov))
+        print(json.dumps({
+            "metric": STREAM_METRIC, "value": value, "unit": "Mvoxels/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 + f16 (calibrated schedule)",
+            "data": "synthetic: 2048x4096x4096 u8 spiral sheet (pitch 14, thickness 3, N(170,15)/N(40,10), blur 1), "
+                    "noise keyed per 64^3 chunk, seed 4; random-init Kaiming weights (seed 1)",
+            "config": {"workload": f"out-of-core streaming sample: {args.steps} tile rows of 1764 192^3 tiles per GPU "
+                                   f"(grid {rows} tiles), overlap 0.5, global accumulator window on the device, "
+                                   "u8 chunk rows finalised per row", "volume": list(STREAM_SHAPE), "patch": P,
+                       "overlap": ov, "batch": args.batch, "first_row": r0, "parallelism": f"row ranges x{world}",
+                       "l2": "inputs larger than L2: 7 GB of input planes per step"},
+            "precision_schedule": dict(precision_report(net, None), calibration_dice=d_cal),
+            "e2e": {"value": value, "unit": "Mvoxels/s", "h2d_bytes_per_step": P * dy * dx * world,
+                    "d2h_bytes_per_step": int(tot[0] / args.steps),
+                    "path": "fx_gaccum_predict_row + fx_gaccum_finalize_below, pinned host planes in, u8 chunk rows out"},
+            "clocks": clk, "gpu_launches": int(tot[2]),
+        }))
+    acc.close()
+    net.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -591,13 +703,22 @@ def main():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fxvol", action="store_true")
-    ap.add_argument("--workload", default="surface", choices=["surface", "ink"],
-                    help="surface: the 1024^3 sliding-window benchmark (default); ink: batches of layer stacks")
+    ap.add_argument("--minimal", action="store_true",
+                    help="warm-up and timed steps only (no e2e, parity, peaks, baselines): for profiler launch lists")
+    ap.add_argument("--workload", default="surface", choices=["surface", "ink", "stream"],
+                    help="surface: the 1024^3 sliding-window benchmark (default); ink: batches of layer stacks; "
+                         "stream: the out-of-core 2048x4096x4096 run, a bounded sample of tile rows")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.workload == "ink":
         return run_ink_reference(args) if args.impl == "reference" else run_ink(args)
+    if args.workload == "stream":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the streaming sample has no separate reference arm; "
+                              "its per-tile reference time is the surface workload's (same net, CPU libtorch)"}))
+            return 0
+        return run_stream(args)
     if args.impl == "reference":
         return run_reference_arm(args)
 
@@ -700,6 +821,18 @@ def main():
     ms = timed(dev_step, args.steps)
     launches = fx.kernel_launches() - l0
     clk = clocks.stop()
+    if args.minimal:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": float(S) ** 3 * args.steps / (ms / 1e3) / 1e6,
+                              "unit": "Mvoxels/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                              "ms_per_step": ms / args.steps, "minimal": True, "gpu_launches": launches,
+                              "config": workload_config(args, len(fx.tile_starts(S, P, args.overlap)) ** 3, world)}))
+        sp.close()
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        net.close()
+        return 0
     for _ in range(1):
         e2e_step()
     ms_e2e = timed(e2e_step, args.steps)

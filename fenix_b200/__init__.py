@@ -175,6 +175,7 @@ def lib():
     _sig(L, "fx_kernel_launches", C.c_ulonglong, [])
     _sig(L, "fx_tc_peak", i32, [i32, i32, C.c_double, i32, C.POINTER(C.c_double), C.POINTER(C.c_double)])
     _sig(L, "fx_synth_spiral", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
+    _sig(L, "fx_synth_spiral_chunked", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
     _sig(L, "fx_synth_papyrus", i32, [u8p, u8p, i64, i64, i64, C.POINTER(PapyrusParams), C.c_uint64, i64])
     u64p, u32p = C.POINTER(C.c_uint64), C.POINTER(C.c_uint32)
     _sig(L, "fx_fxvol_open", i32, [C.c_char_p, C.POINTER(vp)])
@@ -236,13 +237,20 @@ def weight_profile(g: np.ndarray, patch: int, starts: np.ndarray, c0: int, cn: i
     return out
 
 
-def synth_spiral(shape, seed: int, params: dict | None = None, z_begin: int = 0, z_end: int | None = None) -> np.ndarray:
-    """Spiral-sheet synthetic CT [z_end-z_begin][dy][dx] u8 (deterministic; see fenix_b200_synth.h)."""
+def synth_spiral(shape, seed: int, params: dict | None = None, z_begin: int = 0, z_end: int | None = None,
+                 chunked: bool = False, out: np.ndarray | None = None) -> np.ndarray:
+    """Spiral-sheet synthetic CT [z_end-z_begin][dy][dx] u8 (deterministic; see fenix_b200_synth.h).
+    chunked: noise keyed per 64^3 chunk (fx_synth_spiral_chunked). out: an optional C-contiguous
+    u8 destination of that shape (e.g. a view of pinned memory)."""
     dz, dy, dx = shape
     z_end = dz if z_end is None else z_end
     p = SpiralParams(**(params or SPIRAL_CONFIG1))
-    out = np.empty((z_end - z_begin, dy, dx), dtype=np.uint8)
-    rc = lib().fx_synth_spiral(out.ctypes.data_as(C.POINTER(C.c_uint8)), dz, dy, dx, C.byref(p), seed, z_begin, z_end)
+    if out is None:
+        out = np.empty((z_end - z_begin, dy, dx), dtype=np.uint8)
+    elif out.shape != (z_end - z_begin, dy, dx) or out.dtype != np.uint8 or not out.flags.c_contiguous:
+        raise ValueError("synth_spiral: out must be a C-contiguous u8 array of the output's shape")
+    fn = lib().fx_synth_spiral_chunked if chunked else lib().fx_synth_spiral
+    rc = fn(out.ctypes.data_as(C.POINTER(C.c_uint8)), dz, dy, dx, C.byref(p), seed, z_begin, z_end)
     if rc != 0:
         raise ValueError("fx_synth_spiral: bad arguments")
     return out

@@ -69,8 +69,27 @@ float sheet_distance(double y, double x, double cy, double cx, double pitch) {
 }
 }  // namespace
 
-extern "C" int fx_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fx_spiral_params* prm,
-                               uint64_t seed, int64_t z_begin, int64_t z_end) {
+namespace {
+// The normals of one (z, y) row into f[0, dx): one PCG stream per row (row keying), or one per
+// 64-voxel run of the row inside its 64^3 chunk, keyed by the chunk's index and the run's (z, y)
+// within it (chunk keying: any chunk regenerates from its own streams).
+template <class F>
+void row_normals(uint64_t seed, uint64_t salt, bool chunked, int64_t z, int64_t y, int64_t dy, int64_t dx, F&& put) {
+    if (!chunked) {
+        Pcg rng(seed, static_cast<uint64_t>(z * dy + y) + salt);
+        for (int64_t x = 0; x < dx; ++x) put(x, rng.normal());
+        return;
+    }
+    const int64_t ncy = (dy + 63) / 64, ncx = (dx + 63) / 64;
+    for (int64_t x0 = 0; x0 < dx; x0 += 64) {
+        const uint64_t chunk = static_cast<uint64_t>(((z >> 6) * ncy + (y >> 6)) * ncx + (x0 >> 6));
+        Pcg rng(seed, ((chunk << 12) | (static_cast<uint64_t>(z & 63) << 6) | static_cast<uint64_t>(y & 63)) + salt);
+        for (int64_t x = x0; x < std::min(dx, x0 + 64); ++x) put(x, rng.normal());
+    }
+}
+
+int synth_spiral_impl(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fx_spiral_params* prm, uint64_t seed,
+                      int64_t z_begin, int64_t z_end, bool chunked) {
     if (!out || !prm || dz < 1 || dy < 1 || dx < 1 || z_begin < 0 || z_end > dz || z_begin >= z_end) return 1;
     const double cy = (dy - 1) / 2.0, cx = (dx - 1) / 2.0;
     const int rad = prm->blur_sigma > 0 ? static_cast<int>(std::ceil(3.0 * prm->blur_sigma)) : 0;
@@ -101,15 +120,12 @@ extern "C" int fx_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx,
         parallel_rows(ng, [&](int64_t zi) {
             const int64_t z = g0 + zi;
             float* p = a.data() + zi * plane;
-            for (int64_t y = 0; y < dy; ++y) {
-                Pcg rng(seed, static_cast<uint64_t>(z * dy + y) + 0x9E3779B97F4A7C15ull);
-                for (int64_t x = 0; x < dx; ++x) {
-                    const float n = rng.normal();
+            for (int64_t y = 0; y < dy; ++y)
+                row_normals(seed, 0x9E3779B97F4A7C15ull, chunked, z, y, dy, dx, [&](int64_t x, float n) {
                     p[y * dx + x] = sheet[y * dx + x]
                                         ? static_cast<float>(prm->sheet_mean + prm->sheet_sd * n)
                                         : static_cast<float>(prm->bg_mean + prm->bg_sd * n);
-                }
-            }
+                });
             if (!rad) return;
             std::vector<float> tmp(static_cast<size_t>(plane));
             for (int64_t y = 0; y < dy; ++y)
@@ -129,8 +145,11 @@ extern "C" int fx_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx,
         parallel_rows(c1 - c0, [&](int64_t zo) {
             const int64_t z = c0 + zo;
             uint8_t* o = out + (z - z_begin) * plane;
+            std::vector<float> sp(static_cast<size_t>(dx), 0.f);
             for (int64_t y = 0; y < dy; ++y) {
-                Pcg rng(seed ^ 0xA5A5A5A5DEADBEEFull, static_cast<uint64_t>(z * dy + y) + 0x632BE59BD9B4E019ull);
+                if (prm->speckle_sd > 0)
+                    row_normals(seed ^ 0xA5A5A5A5DEADBEEFull, 0x632BE59BD9B4E019ull, chunked, z, y, dy, dx,
+                                [&](int64_t x, float n) { sp[x] = n; });
                 for (int64_t x = 0; x < dx; ++x) {
                     float s;
                     if (rad) {
@@ -142,7 +161,7 @@ extern "C" int fx_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx,
                     } else {
                         s = a[(z - g0) * plane + y * dx + x];
                     }
-                    if (prm->speckle_sd > 0) s += static_cast<float>(prm->speckle_sd) * rng.normal();
+                    if (prm->speckle_sd > 0) s += static_cast<float>(prm->speckle_sd) * sp[x];
                     s = std::min(255.f, std::max(0.f, s));
                     o[y * dx + x] = static_cast<uint8_t>(std::floor(s + 0.5f));
                 }
@@ -150,6 +169,17 @@ extern "C" int fx_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx,
         });
     }
     return 0;
+}
+}  // namespace
+
+extern "C" int fx_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fx_spiral_params* prm,
+                               uint64_t seed, int64_t z_begin, int64_t z_end) {
+    return synth_spiral_impl(out, dz, dy, dx, prm, seed, z_begin, z_end, false);
+}
+
+extern "C" int fx_synth_spiral_chunked(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fx_spiral_params* prm,
+                                       uint64_t seed, int64_t z_begin, int64_t z_end) {
+    return synth_spiral_impl(out, dz, dy, dx, prm, seed, z_begin, z_end, true);
 }
 
 namespace {

@@ -29,6 +29,13 @@ typedef struct fx_spiral_params {
 /* out: [z_end - z_begin][dy][dx] */
 int fx_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fx_spiral_params* params, uint64_t seed,
                     int64_t z_begin, int64_t z_end);
+/* The same recipe with the noise keyed per 64^3 chunk (the out-of-core workload's volume): the
+ * normals of a 64-voxel run of row (z, y) inside chunk (z / 64, y / 64, x / 64) come from the PCG
+ * stream ((chunk index << 12) | (z % 64) << 6 | (y % 64)), chunk index = (cz * ncy + cy) * ncx + cx,
+ * so any chunk (with the blur's 3-voxel margin) regenerates from its own and its neighbours'
+ * streams. Bytes differ from fx_synth_spiral's. */
+int fx_synth_spiral_chunked(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fx_spiral_params* params,
+                            uint64_t seed, int64_t z_begin, int64_t z_end);
 
 /* Papyrus layer stacks with ink, the layer-stack (wide-ink) workload's input: one surface-normal
  * layer stack [dz][dy][dx] (z = the layer axis) per call, number `stack` of a seeded series.

@@ -30,6 +30,7 @@ class Spiral(C.Structure):
 SPIRAL_CONFIG1 = dict(pitch=12, thickness=3, sheet_mean=170, sheet_sd=15, bg_mean=40, bg_sd=10, blur_sigma=1.0,
                       speckle_sd=0.0)
 SPIRAL_CONFIG3 = dict(SPIRAL_CONFIG1, pitch=16, speckle_sd=8.0)
+SPIRAL_CONFIG5 = dict(SPIRAL_CONFIG1, pitch=14)
 
 
 class Papyrus(C.Structure):
@@ -54,14 +55,15 @@ def synth_papyrus(shape, seed, stack=0, params=None, want_ink=False):
     return (out, ink) if want_ink else out
 
 
-def synth_spiral(shape, seed, params=None, z_begin=0, z_end=None):
-    """The spiral-sheet synthetic CT [z_end - z_begin][dy][dx] u8 (oracle/synth.c)."""
+def synth_spiral(shape, seed, params=None, z_begin=0, z_end=None, chunked=False):
+    """The spiral-sheet synthetic CT [z_end - z_begin][dy][dx] u8 (oracle/synth.c); chunked: noise
+    keyed per 64^3 chunk."""
     dz, dy, dx = shape
     z_end = dz if z_end is None else z_end
     p = Spiral(**(params or SPIRAL_CONFIG1))
     out = np.empty((z_end - z_begin, dy, dx), dtype=np.uint8)
-    if lib().fxo_synth_spiral(out.ctypes.data_as(C.POINTER(C.c_uint8)), dz, dy, dx, C.byref(p), seed, z_begin,
-                              z_end):
+    fn = lib().fxo_synth_spiral_chunked if chunked else lib().fxo_synth_spiral
+    if fn(out.ctypes.data_as(C.POINTER(C.c_uint8)), dz, dy, dx, C.byref(p), seed, z_begin, z_end):
         raise ValueError("fxo_synth_spiral: bad arguments")
     return out
 
@@ -102,6 +104,8 @@ def lib():
         L.fxv_morton3.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64]
         L.fxo_synth_spiral.restype = i32
         L.fxo_synth_spiral.argtypes = [u8p, i64, i64, i64, C.POINTER(Spiral), C.c_uint64, i64, i64]
+        L.fxo_synth_spiral_chunked.restype = i32
+        L.fxo_synth_spiral_chunked.argtypes = [u8p, i64, i64, i64, C.POINTER(Spiral), C.c_uint64, i64, i64]
         L.fxo_net_forward_tiled.restype = i32
         L.fxo_net_forward_tiled.argtypes = [vp, f32p, i32, i32, i32, i32, i32, i32, f32p]
         L.fxo_predict_tiled.restype = i32

@@ -65,9 +65,25 @@ static float sheet_dist(double y, double x, double cy, double cx, double pitch) 
 
 static int64_t clampi(int64_t v, int64_t lo, int64_t hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
-/* out: [z_end - z_begin][dy][dx]; 0 on success */
-int fxo_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fxo_spiral* p, uint64_t seed,
-                     int64_t z_begin, int64_t z_end) {
+/* The normals of row (z, y) into f[0, dx): one PCG stream per row, or (chunked) one per 64-voxel
+ * run inside its 64^3 chunk, stream ((chunk << 12) | (z % 64) << 6 | (y % 64)) + salt. */
+static void row_normals(uint64_t seed, uint64_t salt, int chunked, int64_t z, int64_t y, int64_t dy, int64_t dx,
+                        float* f) {
+    if (!chunked) {
+        pcg_t r = pcg_seed(seed, (uint64_t)(z * dy + y) + salt);
+        for (int64_t x = 0; x < dx; ++x) f[x] = pcg_normal(&r);
+        return;
+    }
+    const int64_t ncy = (dy + 63) / 64, ncx = (dx + 63) / 64;
+    for (int64_t x0 = 0; x0 < dx; x0 += 64) {
+        const uint64_t chunk = (uint64_t)(((z >> 6) * ncy + (y >> 6)) * ncx + (x0 >> 6));
+        pcg_t r = pcg_seed(seed, ((chunk << 12) | ((uint64_t)(z & 63) << 6) | (uint64_t)(y & 63)) + salt);
+        for (int64_t x = x0; x < dx && x < x0 + 64; ++x) f[x] = pcg_normal(&r);
+    }
+}
+
+static int synth_spiral_impl(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fxo_spiral* p, uint64_t seed,
+                             int64_t z_begin, int64_t z_end, int chunked) {
     if (!out || !p || dz < 1 || dy < 1 || dx < 1 || z_begin < 0 || z_end > dz || z_begin >= z_end) return 1;
     const double cy = (dy - 1) / 2.0, cx = (dx - 1) / 2.0;
     const int rad = p->blur_sigma > 0 ? (int)ceil(3.0 * p->blur_sigma) : 0;
@@ -105,9 +121,9 @@ int fxo_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fxo
             const int64_t z = g0 + zi;
             float* q = a + zi * plane;
             for (int64_t y = 0; y < dy; ++y) {
-                pcg_t r = pcg_seed(seed, (uint64_t)(z * dy + y) + 0x9E3779B97F4A7C15ull);
+                row_normals(seed, 0x9E3779B97F4A7C15ull, chunked, z, y, dy, dx, q + y * dx);
                 for (int64_t x = 0; x < dx; ++x) {
-                    const float n = pcg_normal(&r);
+                    const float n = q[y * dx + x];
                     q[y * dx + x] = sheet[y * dx + x] ? (float)(p->sheet_mean + p->sheet_sd * n)
                                                       : (float)(p->bg_mean + p->bg_sd * n);
                 }
@@ -131,8 +147,10 @@ int fxo_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fxo
         for (int64_t zo = 0; zo < c1 - c0; ++zo) {
             const int64_t z = c0 + zo;
             uint8_t* o = out + (z - z_begin) * plane;
+            float* sp = malloc(sizeof(float) * (size_t)dx);
             for (int64_t y = 0; y < dy; ++y) {
-                pcg_t r = pcg_seed(seed ^ 0xA5A5A5A5DEADBEEFull, (uint64_t)(z * dy + y) + 0x632BE59BD9B4E019ull);
+                if (p->speckle_sd > 0)
+                    row_normals(seed ^ 0xA5A5A5A5DEADBEEFull, 0x632BE59BD9B4E019ull, chunked, z, y, dy, dx, sp);
                 for (int64_t x = 0; x < dx; ++x) {
                     float s;
                     if (rad) {
@@ -144,17 +162,30 @@ int fxo_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fxo
                     } else {
                         s = a[(z - g0) * plane + y * dx + x];
                     }
-                    if (p->speckle_sd > 0) s += (float)p->speckle_sd * pcg_normal(&r);
+                    if (p->speckle_sd > 0) s += (float)p->speckle_sd * sp[x];
                     s = fminf(255.f, fmaxf(0.f, s));
                     o[y * dx + x] = (uint8_t)floorf(s + 0.5f);
                 }
             }
+            free(sp);
         }
         free(a);
         free(tmps);
     }
     free(sheet);
     return rc;
+}
+
+/* out: [z_end - z_begin][dy][dx]; 0 on success */
+int fxo_synth_spiral(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fxo_spiral* p, uint64_t seed,
+                     int64_t z_begin, int64_t z_end) {
+    return synth_spiral_impl(out, dz, dy, dx, p, seed, z_begin, z_end, 0);
+}
+
+/* the same with the noise keyed per 64^3 chunk (the out-of-core workload's volume) */
+int fxo_synth_spiral_chunked(uint8_t* out, int64_t dz, int64_t dy, int64_t dx, const fxo_spiral* p, uint64_t seed,
+                             int64_t z_begin, int64_t z_end) {
+    return synth_spiral_impl(out, dz, dy, dx, p, seed, z_begin, z_end, 1);
 }
 
 /* ---- papyrus layer stacks with ink (the layer-stack workload's input) ---------------------------
