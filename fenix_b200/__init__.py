@@ -64,6 +64,10 @@ class InferOpts(C.Structure):
         ("tile_filter_user", C.c_void_p),
         ("tile", C.c_int * 3),
         ("stacks", C.c_int),
+        ("ckpt_path", C.c_char_p),
+        ("ckpt_every", C.c_int64),
+        ("weights_hash", C.c_uint64),
+        ("input_hash", C.c_uint64),
     ]
 
 
@@ -428,12 +432,16 @@ class Net:
     def predict_volume(self, vol_u8: np.ndarray, overlap: float = 0.5, batch: int = 1, channel: int = 1,
                        sigmoid: int = 0, want_prob: bool = True, want_u8: bool = True, tta: int = 0,
                        norm: str = "zscore", skip_constant: bool = False, core=None, tile_filter=None,
-                       stacks: int = 1):
+                       stacks: int = 1, ckpt_path=None, ckpt_every: int = 128, weights_hash: int = 0,
+                       input_hash: int = 0):
         """core = (z, y, x, dz, dy, dx) output crop (extents <= 0: to the end); tile_filter =
         callable(z0, y0, x0, patch) -> bool. Outputs have the crop's dims when cropped."""
         v = np.ascontiguousarray(vol_u8, dtype=np.uint8)
         dz, dy, dx = v.shape
         opts = self._opts(overlap, channel, sigmoid, batch, tta, NORMS[norm], 1 if skip_constant else 0, stacks)
+        if ckpt_path is not None:
+            opts.ckpt_path = str(ckpt_path).encode()
+            opts.ckpt_every, opts.weights_hash, opts.input_hash = ckpt_every, weights_hash, input_hash
         out_shape = v.shape
         if core is not None:
             opts.core_org[:] = list(core[:3])

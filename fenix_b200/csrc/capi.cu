@@ -11,13 +11,16 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <exception>
 #include <memory>
 #include <mutex>
 #include <new>
 #include <string>
+#include <thread>
 #include <vector>
 
 namespace fxh {
@@ -118,6 +121,185 @@ void crop_box(const fx_infer_opts* o, const int64_t d[3], int64_t co[3], int64_t
     }
 }
 
+// ---- resumable prediction: the reference's FXICKPT3 checkpoint (src/ml/infer.hpp:136-344) ----
+// The header is the reference's struct, field for field (the same bytes on disk, so either side
+// resumes the other's file); the trailing 4 bytes of padding are zero.
+struct CkptHeader {
+    char magic[8] = {'F', 'X', 'I', 'C', 'K', 'P', 'T', '3'};
+    int64_t dz = 0, dy = 0, dx = 0;
+    int64_t tile_shift = 0;
+    int64_t total_tiles = 0;
+    int64_t n_done = 0;
+    uint64_t weights_hash = 0, input_hash = 0;
+    double overlap = 0, acc_scale = 0;
+    int32_t patch = 0, tta = 0, channel = 0, sigmoid = 0, norm = 0;
+};
+static_assert(sizeof(CkptHeader) == 112, "FXICKPT3 header layout");
+
+// Load a checkpoint that matches `want` into host f32 acc (nvox values): its completed tile count,
+// or -1 (absent, mismatched, short or unreadable: acc untouched, start fresh).
+int64_t ckpt_load(const std::string& path, const CkptHeader& want, std::vector<float>& acc) {
+    std::FILE* f = std::fopen(path.c_str(), "rb");
+    if (!f) return -1;
+    CkptHeader h;
+    const bool ok = std::fread(&h, sizeof h, 1, f) == 1 && std::memcmp(h.magic, want.magic, 8) == 0 &&
+                    h.dz == want.dz && h.dy == want.dy && h.dx == want.dx && h.patch == want.patch &&
+                    h.overlap == want.overlap && h.tta == want.tta && h.tile_shift == want.tile_shift &&
+                    h.total_tiles == want.total_tiles && h.weights_hash == want.weights_hash &&
+                    h.input_hash == want.input_hash && h.channel == want.channel && h.sigmoid == want.sigmoid &&
+                    h.norm == want.norm && h.n_done >= 0 && h.n_done <= h.total_tiles;
+    const size_t nvox = acc.size();
+    int64_t n = -1;
+    if (ok) {
+        std::fseek(f, 0, SEEK_END);
+        const long fsize = std::ftell(f);
+        const long need = static_cast<long>(sizeof(CkptHeader) + (h.acc_scale > 0.0 ? nvox * sizeof(uint16_t) : 0));
+        if (fsize >= need && std::fseek(f, sizeof(CkptHeader), SEEK_SET) == 0) {
+            if (h.acc_scale <= 0.0) {
+                std::fill(acc.begin(), acc.end(), 0.0f);
+                n = h.n_done;
+            } else {
+                std::vector<uint16_t> q(nvox);
+                if (std::fread(q.data(), sizeof(uint16_t), nvox, f) == nvox) {
+                    const float sc = static_cast<float>(h.acc_scale / 65535.0);
+                    for (size_t i = 0; i < nvox; ++i) acc[i] = static_cast<float>(q[i]) * sc;
+                    n = h.n_done;
+                }
+            }
+        }
+    }
+    std::fclose(f);
+    return n;
+}
+
+// Header + u16 payload to path (temp + rename); best effort.
+void ckpt_write(const std::string& path, const CkptHeader& h, const std::vector<uint16_t>& q) {
+    const std::string tmp = path + ".tmp";
+    std::FILE* f = std::fopen(tmp.c_str(), "wb");
+    if (!f) return;
+    bool ok = std::fwrite(&h, sizeof h, 1, f) == 1;
+    if (ok && h.acc_scale > 0.0) ok = std::fwrite(q.data(), sizeof(uint16_t), q.size(), f) == q.size();
+    ok = std::fflush(f) == 0 && ok;
+    std::fclose(f);
+    if (ok) std::rename(tmp.c_str(), path.c_str());
+    else std::remove(tmp.c_str());
+}
+
+// The background writer: one write in flight; a save requested meanwhile is skipped.
+struct CkptWriter {
+    std::thread th;
+    std::atomic<bool> busy{false};
+    std::vector<uint16_t> q;
+    ~CkptWriter() { join(); }
+    void join() {
+        if (th.joinable()) th.join();
+    }
+    // Snapshot d_acc (device max, quantise, D2H on stream s) and hand it to the writer thread.
+    fx_status save(const std::string& path, CkptHeader h, const float* d_acc, size_t nvox, unsigned* d_max,
+                   uint16_t* d_q, cudaStream_t s) {
+        if (busy.load()) return FX_OK;
+        join();
+        unsigned bits = 0;
+        cudaError_t e = cudaMemsetAsync(d_max, 0, sizeof(unsigned), s);
+        if (e == cudaSuccess) e = fxk::launch_acc_max(d_acc, static_cast<int64_t>(nvox), d_max, s);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(&bits, d_max, sizeof bits, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return set_err(cuda_status(e, "checkpoint"));
+        float mx;
+        std::memcpy(&mx, &bits, sizeof mx);
+        h.acc_scale = mx > 0.0f ? static_cast<double>(mx) : 0.0;
+        if (h.acc_scale > 0.0) {
+            q.resize(nvox);
+            const float inv = static_cast<float>(65535.0 / h.acc_scale);
+            e = fxk::launch_acc_quant_u16(d_acc, static_cast<int64_t>(nvox), inv, d_q, s);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(q.data(), d_q, nvox * sizeof(uint16_t), cudaMemcpyDeviceToHost, s);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess) return set_err(cuda_status(e, "checkpoint"));
+        }
+        busy = true;
+        th = std::thread([this, path, h] {
+            ckpt_write(path, h, q);
+            busy = false;
+        });
+        return FX_OK;
+    }
+};
+
+// predict_tiles over the whole grid with checkpointing: resume from a matching file, save every
+// `every` tiles, remove the file on success (src/ml/infer.hpp:571-606, 790-861).
+fx_status predict_ckpt(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t dy, int64_t dx, fxk::TileDims tl,
+                       const fx_infer_opts* o, float* d_acc, cudaStream_t s) {
+    if (tl.z != tl.y || tl.y != tl.x || std::max(o->stacks, 1) > 1 || o->tile_filter || o->skip_constant)
+        return set_err(FX_UNSUPPORTED, "predict: checkpoints need a cubic tile, one volume, every tile (no filter)");
+    const int64_t d[3] = {dz, dy, dx};
+    int64_t co[3], ce[3];
+    crop_box(o, d, co, ce);
+    if (co[0] || co[1] || co[2] || ce[0] != dz || ce[1] != dy || ce[2] != dx)
+        return set_err(FX_UNSUPPORTED, "predict: checkpoints take no output crop (src/ml/infer.hpp:575)");
+    const std::string path(o->ckpt_path);
+    const int64_t total = static_cast<int64_t>(fenix::ml::tile_starts(dz, tl.z, o->overlap).size() *
+                                               fenix::ml::tile_starts(dy, tl.y, o->overlap).size() *
+                                               fenix::ml::tile_starts(dx, tl.x, o->overlap).size());
+    CkptHeader h;
+    h.dz = dz;
+    h.dy = dy;
+    h.dx = dx;
+    h.patch = tl.z;
+    h.overlap = o->overlap;
+    h.tta = o->tta;
+    h.total_tiles = total;
+    h.weights_hash = o->weights_hash;
+    h.input_hash = o->input_hash;
+    h.channel = o->channel;
+    h.sigmoid = o->sigmoid ? 1 : 0;
+    h.norm = o->norm;
+    const size_t nvox = static_cast<size_t>(dz) * dy * dx;
+    int64_t done = -1;
+    {
+        std::vector<float> host(nvox);
+        done = ckpt_load(path, h, host);
+        cudaError_t e = done >= 0 ? cudaMemcpyAsync(d_acc, host.data(), nvox * sizeof(float), cudaMemcpyHostToDevice, s)
+                                  : cudaMemsetAsync(d_acc, 0, nvox * sizeof(float), s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return set_err(cuda_status(e, "checkpoint load"));
+    }
+    if (done < 0) done = 0;
+    const int b = std::max(1, std::min(o->batch, n->net.max_batch()));
+    int64_t every = o->ckpt_every > 0 ? o->ckpt_every : 128;
+    every = (every + b - 1) / b * b;  // whole forwards between saves
+    unsigned* d_max = nullptr;
+    uint16_t* d_q = nullptr;
+    if (cudaMalloc(&d_max, sizeof(unsigned)) != cudaSuccess || cudaMalloc(&d_q, nvox * sizeof(uint16_t)) != cudaSuccess) {
+        cudaFree(d_max);
+        return set_err(FX_INTERNAL, "cudaMalloc: checkpoint snapshot");
+    }
+    fx_status r = FX_OK;
+    {
+        CkptWriter w;
+        for (int64_t t = done; t < total && r == FX_OK; t += every) {
+            const int64_t t1 = std::min(total, t + every);
+            Status st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, tl, o->overlap, o->channel, o->sigmoid, o->batch,
+                                             t, t1, d_acc, s, 0, dz, o->tta, run_opts(o));
+            if (!st.ok()) {
+                r = set_err(st);
+                break;
+            }
+            if (t1 < total) {
+                h.n_done = t1;
+                r = w.save(path, h, d_acc, nvox, d_max, d_q, s);
+            }
+        }
+        w.join();
+    }
+    cudaFree(d_max);
+    cudaFree(d_q);
+    if (r == FX_OK) {
+        std::remove(path.c_str());
+        std::remove((path + ".tmp").c_str());
+    }
+    return r;
+}
+
 // The device part of fx_predict_volume (src/ml/infer.hpp:456-864 + inference.cpp:343-351): d_vol
 // (resident, dims dz, dy, dx) -> Gaussian blend in d_acc (the crop's dims) -> normalised probability
 // in d_prob (may alias d_acc) and/or u8 in d_u8. Runs on the net's stream and synchronises it.
@@ -133,12 +315,17 @@ fx_status predict_resident(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t 
     if (ns > 1 && (co[0] || co[1] || co[2] || ce[0] != dz || ce[1] != dy || ce[2] != dx))
         return set_err(FX_UNSUPPORTED, "predict: stacks take no output crop");
     const size_t nv = static_cast<size_t>(ce[0]) * ce[1] * ce[2];
-    cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
     fxk::TileDims tl{};
     if (fx_status r = opts_tile(o, &tl)) return r;
-    Status st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, tl, o->overlap, o->channel, o->sigmoid, o->batch, 0, -1,
-                                     d_acc, s, co[0], ce[0], o->tta, run_opts(o));
-    if (!st.ok()) return set_err(st);
+    Status st = ok();
+    if (o->ckpt_path && *o->ckpt_path) {
+        if (fx_status r = predict_ckpt(n, d_vol, dz, dy, dx, tl, o, d_acc, s)) return r;
+    } else {
+        cudaMemsetAsync(d_acc, 0, nv * sizeof(float), s);
+        st = n->net.predict_tiles(d_vol, dz, dy, dx, 0, dz, tl, o->overlap, o->channel, o->sigmoid, o->batch, 0, -1,
+                                  d_acc, s, co[0], ce[0], o->tta, run_opts(o));
+        if (!st.ok()) return set_err(st);
+    }
     const int T[3] = {tl.z, tl.y, tl.x};
     std::vector<float> w(static_cast<size_t>(ce[0] + ce[1] + ce[2]));
     size_t at = 0;

@@ -6,6 +6,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
+#include <algorithm>
+
 namespace fxk {
 
 namespace {
@@ -891,6 +893,38 @@ cudaError_t launch_accum_add(float* dst, const float* src, int64_t n, cudaStream
         accum_add_scalar_kernel<<<grid_for(n, kEwThreads), kEwThreads, 0, s>>>(dst, src, n);
     else
         accum_add_kernel<<<grid_for(n / 4 + 1, kEwThreads), kEwThreads, 0, s>>>(dst, src, n);
+    return cudaGetLastError();
+}
+
+
+namespace {
+__global__ void acc_max_kernel(const float* __restrict__ acc, int64_t n, unsigned* max_bits) {
+    float m = 0.f;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        m = fmaxf(m, acc[i]);
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(max_bits, __float_as_uint(m));
+}
+
+__global__ void acc_quant_u16_kernel(const float* __restrict__ acc, int64_t n, float inv, uint16_t* __restrict__ q) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        q[i] = static_cast<uint16_t>(__fadd_rn(__fmul_rn(acc[i], inv), 0.5f));
+}
+}  // namespace
+
+cudaError_t launch_acc_max(const float* acc, int64_t n, unsigned* max_bits, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    count_launch();
+    acc_max_kernel<<<static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 16)), 256, 0, s>>>(acc, n, max_bits);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_acc_quant_u16(const float* acc, int64_t n, float inv, uint16_t* q, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    count_launch();
+    acc_quant_u16_kernel<<<static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 16)), 256, 0, s>>>(acc, n, inv, q);
     return cudaGetLastError();
 }
 

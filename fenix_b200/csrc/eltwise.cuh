@@ -91,6 +91,12 @@ struct NormDest {
     int64_t phase_stride;  // bytes between parity sub-volumes
 };
 
+// Checkpoint snapshot of a non-negative f32 accumulator: *max_bits = the float bits of max(acc)
+// (atomicMax on the bits, caller-zeroed), and q[i] = (u16)(acc[i] * inv + 0.5f) with the multiply
+// and the add rounded separately (src/ml/infer.hpp:177-182).
+cudaError_t launch_acc_max(const float* acc, int64_t n, unsigned* max_bits, cudaStream_t s);
+cudaError_t launch_acc_quant_u16(const float* acc, int64_t n, float inv, uint16_t* q, cudaStream_t s);
+
 // y = leaky_relu(x * scale[c] + shift[c], slope) over the interior of an f16 pre-norm tensor,
 // written to up to two destinations; optionally records max |y| into *amax (float bits).
 cudaError_t launch_norm_act(const uint8_t* pre, int64_t pre_batch_stride, int64_t pre_group_stride, GridGeom g,

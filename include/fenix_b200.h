@@ -106,6 +106,20 @@ typedef struct fx_infer_opts {
                     batch. Each stack must be at least one tile deep; no output crop, no z-slabs.
                     0 or 1: one volume. No reference counterpart (the reference predicts one
                     volume per call, src/ml/infer.hpp:456). */
+    /* Resumable prediction (InferOptions::ckpt_path / ckpt_every / weights_hash / input_hash,
+       src/ml/infer.hpp:78-96, 136-344), fx_predict_volume / fx_predict_volume_dev only: when
+       ckpt_path is set, a checkpoint written in the reference's FXICKPT3 layout (header: dims,
+       patch, overlap, tta, tile_shift 0, total / completed tile counts, the two identity hashes,
+       the u16 scale, channel, sigmoid, norm; then the accumulator as u16 = (u16)(acc / scale *
+       65535 + 0.5)) that matches this call is loaded and the run continues after its completed
+       tiles; every ckpt_every tiles (<= 0: 128) the accumulator is saved there (temp + rename, by
+       a background thread, a save skipped while the previous one is writing); on success the file
+       is removed. Tiles run in the fixed z-major order. Not with an output crop, stacks or a
+       non-cubic tile (FX_UNSUPPORTED). NULL: off. */
+    const char* ckpt_path;
+    int64_t ckpt_every;
+    uint64_t weights_hash; /* identity of the weights / input the checkpoint belongs to (0: none) */
+    uint64_t input_hash;
 } fx_infer_opts;
 
 typedef struct fx_net fx_net;

@@ -26,6 +26,7 @@
 #include <algorithm>
 #include <charconv>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <expected>
 #include <functional>
@@ -41,6 +42,7 @@ namespace fenix_b200 {
 
 using u8 = std::uint8_t;
 using s64 = std::int64_t;
+using u64 = std::uint64_t;
 using f32 = float;
 
 // Same enumerators in the same order as the reference's Errc; fx_status values equal them.
@@ -152,7 +154,73 @@ struct InferOptions {
     // predict-scroll's constant-input filter (src/ml/inference.cpp:1487-1496, 1885-1900), evaluated
     // on the device.
     bool skip_constant = false;
+    // Resumable prediction (src/ml/infer.hpp:78-96): checkpoint file (empty = off), the cadence in
+    // tiles, and the identity of the weights / input it belongs to (see weights_hash64 below).
+    std::string ckpt_path{};
+    long ckpt_every = 128;
+    u64 weights_hash = 0;
+    u64 input_hash = 0;
 };
+
+// The reference's 64-bit identity hash (src/core/hash.hpp:36-59): wyhash-style mixing (Wang Yi's
+// public-domain wyhash: a 64 x 64 -> 128-bit multiply folded by xor, 16-byte rounds, the 4-16 and
+// 1-3 byte tails), restated so that a checkpoint's weights / input identity equals the reference's
+// and either side resumes the other's file.
+inline u64 hash64(std::span<const u8> data, u64 seed = 0) {
+    constexpr u64 p0 = 0xa0761d6478bd642fULL, p1 = 0xe7037ed1a0b428dbULL;
+    auto mix = [](u64 a, u64 b) {
+        const __uint128_t r = static_cast<__uint128_t>(a) * b;
+        return static_cast<u64>(r) ^ static_cast<u64>(r >> 64);
+    };
+    auto r64 = [](const u8* q) {
+        u64 v;
+        std::memcpy(&v, q, 8);
+        return v;
+    };
+    auto r32 = [](const u8* q) {
+        uint32_t v;
+        std::memcpy(&v, q, 4);
+        return static_cast<u64>(v);
+    };
+    const u8* q = data.data();
+    std::size_t len = data.size();
+    u64 a = 0, b = 0;
+    seed ^= mix(seed ^ p0, p1);
+    if (len <= 16) {
+        if (len >= 4) {
+            a = (r32(q) << 32) | r32(q + ((len >> 3) << 2));
+            b = (r32(q + len - 4) << 32) | r32(q + len - 4 - ((len >> 3) << 2));
+        } else if (len > 0) {
+            a = (static_cast<u64>(q[0]) << 16) | (static_cast<u64>(q[len >> 1]) << 8) | q[len - 1];
+        }
+    } else {
+        std::size_t i = len;
+        while (i > 16) {
+            seed = mix(r64(q) ^ p1, r64(q + 8) ^ seed);
+            q += 16;
+            i -= 16;
+        }
+        a = r64(q + i - 16);
+        b = r64(q + i - 8);
+    }
+    return mix(p1 ^ len, mix(a ^ p1, b ^ seed));
+}
+
+// A weights file's checkpoint identity: hash64 chained over its bytes in 1 MiB chunks, as the
+// reference's predict computes it (src/ml/inference.cpp:256-274); 0 when it cannot be read.
+inline u64 weights_hash64(const std::string& path) {
+    std::FILE* f = std::fopen(path.c_str(), "rb");
+    if (!f) return 0;
+    std::vector<u8> chunk(1 << 20);
+    u64 h = 0;
+    for (;;) {
+        const std::size_t n = std::fread(chunk.data(), 1, chunk.size(), f);
+        if (n == 0) break;
+        h = hash64({chunk.data(), n}, h);
+    }
+    std::fclose(f);
+    return h;
+}
 
 namespace detail {
 inline int tile_filter_trampoline(int64_t z0, int64_t y0, int64_t x0, int64_t p, void* user) {
@@ -192,6 +260,12 @@ inline int tile_filter_trampoline(int64_t z0, int64_t y0, int64_t x0, int64_t p,
     if (o.tile_filter) {
         f.tile_filter = &detail::tile_filter_trampoline;
         f.tile_filter_user = const_cast<std::function<bool(s64, s64, s64, s64)>*>(&o.tile_filter);
+    }
+    if (!o.ckpt_path.empty()) {
+        f.ckpt_path = o.ckpt_path.c_str();
+        f.ckpt_every = o.ckpt_every;
+        f.weights_hash = o.weights_hash;
+        f.input_hash = o.input_hash;
     }
     return f;
 }
@@ -587,7 +661,13 @@ struct PredictArgs {
             else if (v == "bf16") a.precision = Precision::bf16;
             else if (v == "fp8") a.precision = Precision::fp8;
             else return err(Errc::invalid_argument, "predict: precision must be f16, bf16 or fp8");
-        } else if (k == "scales" || k == "rots" || k == "noise" || k == "offsets" || k == "ckpt") {
+        } else if (k == "ckpt") {
+            a.opt.ckpt_path = std::string(v);
+        } else if (k == "ckpt_every") {
+            int e = 0;
+            if (auto r = to_int(v, e); !r) return std::unexpected(r.error());
+            a.opt.ckpt_every = e;
+        } else if (k == "scales" || k == "rots" || k == "noise" || k == "offsets") {
             return err(Errc::unsupported, "predict: " + std::string(k) + "= is not implemented on the B200 path");
         } else {
             return err(Errc::invalid_argument, "predict: unknown option: " + std::string(k));

@@ -128,6 +128,10 @@ inline float predict_q() {
     auto a = parse_predict_args(args);
     if (!a) return std::unexpected(a.error());
     if (!a->batch_explicit) a->opt.batch = 8;
+    if (!a->opt.ckpt_path.empty()) {  // the checkpoint's identity, as the reference computes it
+        a->opt.weights_hash = weights_hash64(a->weights);
+        a->opt.input_hash = hash64({reinterpret_cast<const u8*>(a->in.data()), a->in.size()});
+    }
     auto in = codec::VolumeArchive::open(a->in, a->device);
     if (!in) return std::unexpected(in.error());
     if (in->src_dtype() != codec::DType::u8) return err(Errc::unsupported, "predict-surface: the input archive is not u8");

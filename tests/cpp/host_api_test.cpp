@@ -57,6 +57,11 @@ static int cpu() {
     CHECK(parse({"in", "w", "out", "gpus=4"}) && parse({"in", "w", "out", "gpus=4"})->gpus == 4);
     CHECK(parse({"in", "w", "out", "gpus=0"}).error().code == Errc::invalid_argument);
     {
+        auto a = parse({"in", "w", "out", "ckpt=/tmp/x.ckpt", "ckpt_every=64"});
+        CHECK(a && a->opt.ckpt_path == "/tmp/x.ckpt" && a->opt.ckpt_every == 64);
+        CHECK(a && ml::to_fx(a->opt) && std::string(ml::to_fx(a->opt)->ckpt_path) == "/tmp/x.ckpt");
+    }
+    {
         ml::InferOptions o;
         o.norm = ml::Norm::pct_minmax;
         CHECK(ml::to_fx(o) && ml::to_fx(o)->norm == FX_NORM_PCT_MINMAX);
@@ -380,7 +385,28 @@ static int fxvol(const char* in, const char* out) {
     return fails ? 1 : 0;
 }
 
+// The checkpoint identity hash on the same inputs as oracle/ref_hash.cpp (the reference's own).
+static int hash() {
+    const int lens[] = {0, 1, 2, 3, 4, 7, 8, 15, 16, 17, 31, 32, 33, 100, 4096};
+    for (int n : lens) {
+        std::vector<u8> b(static_cast<std::size_t>(n));
+        for (int i = 0; i < n; ++i) b[static_cast<std::size_t>(i)] = static_cast<u8>((i * 131 + 7) & 255);
+        std::printf("bytes %d %llu %llu\n", n, static_cast<unsigned long long>(ml::hash64(b)),
+                    static_cast<unsigned long long>(ml::hash64(b, 0x1234567890abcdefULL)));
+    }
+    std::vector<u8> chunk(1 << 20);
+    u64 h = 0;
+    for (int c = 0; c < 3; ++c) {
+        const std::size_t n = c < 2 ? chunk.size() : 12345;
+        for (std::size_t i = 0; i < n; ++i) chunk[i] = static_cast<u8>((i * 7 + static_cast<std::size_t>(c) * 13) & 255);
+        h = ml::hash64({chunk.data(), n}, h);
+    }
+    std::printf("chain %llu\n", static_cast<unsigned long long>(h));
+    return 0;
+}
+
 int main(int argc, char** argv) {
+    if (argc >= 2 && std::string_view(argv[1]) == "hash") return hash();
     if (argc >= 2 && std::string_view(argv[1]) == "cpu") return cpu();
     if (argc >= 4 && std::string_view(argv[1]) == "fxvol") return fxvol(argv[2], argv[3]);
     if (argc >= 4 && std::string_view(argv[1]) == "gpu") return gpu(argv[2], argv[3]);

@@ -27,6 +27,9 @@ Runs only where the reference tree is present (it compiles oracle/_ref from it):
                       so this map comes from the C ORACLE (fxo_predict_tiled), whose cube path the
                       net_* / net128_* fixtures pin against the reference and whose anisotropic
                       forward tests/test_ink_oracle.py checks against PyTorch fp32. Full map as u16.
+  * hash64.npz     — the reference's own hash64 (src/core/hash.hpp via oracle/_ref/ref_hash) of
+                      fixed byte strings and a chained 1 MiB stream: the identity hashes of its
+                      prediction checkpoints.
   * fxvol_tiles.npz — the reference's encode_tile_dct payloads of the 64^3 chunks of
                       tests/golden/fxvol_cases.py, and SHA-256 digests of its decode_tile_dct output
                       (u8, and the f32 reconstruction) of those payloads (oracle/_ref/ref_fxvol).
@@ -286,6 +289,20 @@ def fxvol():
     print(f"fxvol: {len(fc.TILE_CASES_U8) + len(fc.TILE_CASES_F32)} tiles, archive {out.stat().st_size} bytes")
 
 
+def hash64():
+    out = subprocess.run([str(orc.REF / "ref_hash")], capture_output=True, text=True, check=True).stdout
+    rows, chain = [], None
+    for line in out.splitlines():
+        f = line.split()
+        if f[0] == "bytes":
+            rows.append((int(f[1]), int(f[2]), int(f[3])))
+        elif f[0] == "chain":
+            chain = int(f[1])
+    a = np.array(rows, dtype=np.uint64)
+    np.savez_compressed(HERE / "hash64.npz", lens=a[:, 0], h0=a[:, 1], hseed=a[:, 2], chain=np.uint64(chain))
+    print(f"hash64: {len(rows)} strings + chain")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None)
@@ -308,6 +325,8 @@ def main():
     for name in INK:
         if a.only in (None, "ink_" + name):
             ink_case(name)
+    if a.only in (None, "hash64"):
+        hash64()
     if a.only in (None, "fxvol"):
         fxvol()
 

@@ -35,6 +35,21 @@ def test_host_api_cpu(host_api_bin):
     assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
 
 
+def test_hash64_matches_reference(host_api_bin):
+    """ml::hash64 (the checkpoint identity) equals the reference's own hash64 (src/core/hash.hpp,
+    tests/golden/hash64.npz from oracle/_ref/ref_hash) on every length class and a chained stream."""
+    g = np.load(ROOT / "tests" / "golden" / "hash64.npz")
+    r = subprocess.run([str(host_api_bin), "hash"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    got = {}
+    for line in r.stdout.splitlines():
+        f = line.split()
+        got[f[0] if f[0] == "chain" else int(f[1])] = tuple(int(v) for v in f[1:])
+    for n, h0, hs in zip(g["lens"], g["h0"], g["hseed"]):
+        assert got[int(n)] == (int(n), int(h0), int(hs))
+    assert got["chain"] == (int(g["chain"]),)
+
+
 def test_host_api_fxvol_rewrite(host_api_bin, tmp_path):
     gold = ROOT / "tests" / "golden" / "fxvol_small.fxvol"
     out = tmp_path / "rewrite.fxvol"
