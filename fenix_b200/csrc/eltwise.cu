@@ -339,12 +339,14 @@ __device__ __forceinline__ void store_dest(const NormDest& d, int b, int gout, i
 // MODE 0: any destinations (store_dest); 1: one plain e4m3 destination, the common case, the
 // store reduced to one 16-byte e4m3 cell; 2: an e4m3 phase-split destination d0 plus a plain e4m3
 // d1 (an encoder stage's output: the stride-2 conv's input and the decoder's skip half), both
-// stores resolved at compile time. The pass is bound by memory latency, not by bytes in flight per
+// stores resolved at compile time; 3 and 4: the same two shapes with 16-bit destinations (a pair
+// of 8-channel cells per 16 channels), for the layers that run on f16 / bf16 operands. The pass
+// is bound by memory latency, not by bytes in flight per
 // thread: two voxels per thread and registers for eight CTAs per SM (six for the two-destination
 // forms) measured 11% faster than four voxels at three CTAs.
 constexpr int kNormThreads = 256, kNormVox = 2;
 template <int CPT, int MODE>
-__global__ void __launch_bounds__(kNormThreads, MODE == 1 ? 8 : 6) norm_act_kernel(const uint8_t* __restrict__ pre,
+__global__ void __launch_bounds__(kNormThreads, MODE == 1 || MODE == 3 ? 8 : 6) norm_act_kernel(const uint8_t* __restrict__ pre,
                                                                          int64_t pbs, int64_t pgs, GridGeom g,
                                                                          FastDiv fw, int C,
                                                                          const float* __restrict__ ss, float slope,
@@ -419,6 +421,20 @@ __global__ void __launch_bounds__(kNormThreads, MODE == 1 ? 8 : 6) norm_act_kern
             w.z = pack_e4m3x4(v[8] * q1, v[9] * q1, v[10] * q1, v[11] * q1);
             w.w = pack_e4m3x4(v[12] * q1, v[13] * q1, v[14] * q1, v[15] * q1);
             *reinterpret_cast<uint4*>(d1.ptr + b * d1.batch_stride + go * d1.group_stride + row * 16) = w;
+        } else if constexpr (MODE == 3 || MODE == 4) {
+            // 16-bit destinations (two f16 / bf16 cells per 16 channels): d0 plain (MODE 3), or d0
+            // phase-split and d1 plain (MODE 4), the cell type fixed per launch by d0.dtype
+            const uint4 c0 = pack_cell16(v, d0.dtype), c1 = pack_cell16(v + 8, d0.dtype);
+            int64_t off0 = row * 16;
+            if constexpr (MODE == 4) off0 = phase_cell_offset(d0.phase, zp, yp[k], xp[k], d0.pHp, d0.pWp, d0.phase_stride);
+            uint8_t* o0 = d0.ptr + b * d0.batch_stride + gi0 * d0.group_stride + off0;
+            *reinterpret_cast<uint4*>(o0) = c0;
+            *reinterpret_cast<uint4*>(o0 + d0.group_stride) = c1;
+            if constexpr (MODE == 4) {
+                uint8_t* o1 = d1.ptr + b * d1.batch_stride + gi0 * d1.group_stride + row * 16;
+                *reinterpret_cast<uint4*>(o1) = c0;
+                *reinterpret_cast<uint4*>(o1 + d1.group_stride) = c1;
+            }
         } else {
             store_dest(d0, b, d0.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
             store_dest(d1, b, d1.dtype == kOpE4M3 ? go : gi0, row, zp, yp[k], xp[k], v, CPT);
@@ -766,7 +782,17 @@ cudaError_t launch_norm_act(const uint8_t* pre, int64_t pbs, int64_t pgs, GridGe
     // stores are independent): the phase-split one goes first
     const bool pair = cpt == 16 && d0.ptr && d1.ptr && d0.dtype == kOpE4M3 && d1.dtype == kOpE4M3 &&
                       (d0.phase != 0) != (d1.phase != 0);
-    if (e4)
+    // 16-bit destinations of one type: one plain cell pair, or a phase-split copy + a plain copy
+    const bool h0 = cpt == 16 && d0.ptr && d0.dtype != kOpE4M3;
+    const bool h_one = h0 && !d0.phase && !d1.ptr;
+    const bool h_pair = h0 && d1.ptr && d1.dtype == d0.dtype && (d0.phase != 0) != (d1.phase != 0);
+    if (h_one)
+        norm_act_kernel<16, 3><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+    else if (h_pair && d0.phase)
+        norm_act_kernel<16, 4><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
+    else if (h_pair)
+        norm_act_kernel<16, 4><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d1, d0, amax);
+    else if (e4)
         norm_act_kernel<16, 1><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
     else if (pair && d0.phase)
         norm_act_kernel<16, 2><<<grid, kNormThreads, 0, s>>>(pre, pbs, pgs, g, fw, C, ss, slope, d0, d1, amax);
