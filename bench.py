@@ -580,111 +580,112 @@ def run_ink(args):
     return 0
 
 
-STREAM_METRIC = "Mvoxels/s fp8 out-of-core streaming surface inference (finalised u8 output) @1..8 B200"
+STREAM_METRIC = "Mvoxels/s fp8 out-of-core streaming surface inference (finalised u8 output) @1/2/4/8 B200"
 STREAM_SHAPE, STREAM_PATCH, STREAM_OVERLAP, STREAM_SEED = (2048, 4096, 4096), 192, 0.5, 4
 
 
 def run_stream(args):
-    """The out-of-core workload (a bounded sample of it): the 2048 x 4096 x 4096 spiral volume with
-    noise keyed per 64^3 chunk (seed 4, pitch 14), 192^3 tiles at overlap 0.5 (21 x 42 x 42 tile
-    grid), the benchmark's 5-stage net with the calibrated fp8 schedule. Input planes stream from
-    pinned host memory one tile row (1764 tiles) at a time into the device-resident global
-    accumulator (fx_gaccum_predict_row: H2D of the row's 192 planes, every tile of the row, blend),
-    and each row finalises the 64-plane chunk rows no later row reaches (fx_gaccum_finalize_below:
-    normalise, u8, D2H into pinned memory). One step = one tile row; value = finalised output
-    voxels / wall time of the steps, host copies included (the workload is the stream). Ranks take
-    disjoint row ranges of the grid with their own accumulators (no exchange: each rank's first
-    chunk rows lack the contributions of the rows below its range, which a full run would add)."""
+    """The out-of-core workload: the 2048 x 4096 x 4096 spiral volume with noise keyed per 64^3
+    chunk (seed 4, pitch 14), 192^3 tiles at overlap 0.5 (a 21 x 42 x 42 tile grid, 1764 tiles per
+    tile row), the benchmark's 5-stage net with the calibrated fp8 schedule, streamed by tile row
+    (fenix_b200/stream.py): each GPU takes a contiguous range of the tile rows, copies each row's
+    192 input planes from pinned host memory into its device accumulator window, finalises u8
+    chunk rows into pinned host memory as soon as no later row reaches them, and the chunk rows a
+    range shares with the range below are handed to that rank's GPU over NVLink (CUDA IPC) and
+    finalised there. --stream-rows R runs the first R tile rows (default: all 21, the whole
+    volume). value = finalised output voxels of all GPUs / the slowest rank's wall time of its
+    whole share (host copies included: the workload is the stream). Warm-up: W forwards of 8
+    tiles on each GPU."""
     import ctypes as C
 
     import torch
 
     import fenix_b200 as fx
-    from fenix_b200.gaccum import GlobalAccum
+    from fenix_b200.stream import StreamRank
     from fenix_b200.weights import make_plain_unet
 
     rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
     torch.cuda.set_device(local)
+    group = None
     if world > 1:
         import datetime
 
         import torch.distributed as dist
 
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=1200))
+        group = dist.group.WORLD
     P, ov = STREAM_PATCH, STREAM_OVERLAP
     dz, dy, dx = STREAM_SHAPE
-    zs = fx.tile_starts(dz, P, ov)
-    need = args.warmup + args.steps
-    if need > len(zs) - 1:
-        raise SystemExit(f"stream: warmup + steps must be < {len(zs) - 1} tile rows")
-    r0 = min(rank * need, len(zs) - 1 - need)
     tmp = tempfile.mkdtemp(prefix=f"fxstream{rank}_")
     wpath = make_plain_unet(Path(tmp) / "w.fxweights", FEATURES, seed=WEIGHT_SEED)
     net = fx.Net(wpath, P, max_batch=args.batch, precision="fp8", device=local)
-    calib = np.stack([fx.synth_spiral((P, P, P), CALIB_SEED0 + i, fx.SPIRAL_CONFIG3) for i in range(4)])
-    net.calibrate(calib)
-    d_cal, m_cal = net.calibrate_schedule(calib, min_dice=SCHED_DICE)
-    z_lo, z_hi = int(zs[r0]), int(zs[r0 + need]) + P
+    got = [None]
+    if rank == 0:
+        calib = np.stack([fx.synth_spiral((P, P, P), CALIB_SEED0 + i, fx.SPIRAL_CONFIG3) for i in range(4)])
+        net.calibrate(calib)
+        d_cal, _ = net.calibrate_schedule(calib, min_dice=SCHED_DICE)
+        got = [(net.act_scales().tolist(), [l["precision"] for l in net.layers()], d_cal)]
+    if world > 1:
+        torch.distributed.broadcast_object_list(got, src=0)
+        if rank != 0:
+            net.set_act_scales(got[0][0])
+            net.set_layer_precision(["fp8" if q == "fp8" else "f16" for q in got[0][1]])
+    d_cal = got[0][2]
+    rows = args.stream_rows or None
+    sr = StreamRank(net, STREAM_SHAPE, ov, args.batch, rank=rank, world=world, group=group, rows=rows)
+    z_lo, z_hi = sr.input_planes
     host_in = torch.empty((z_hi - z_lo, dy, dx), dtype=torch.uint8).pin_memory()
     fx.synth_spiral(STREAM_SHAPE, STREAM_SEED, fx.SPIRAL_CONFIG5, z_lo, z_hi, chunked=True, out=host_in.numpy())
-    host_out = torch.empty((2 * 64 * 2, dy, dx), dtype=torch.uint8).pin_memory()
-    acc = GlobalAccum((0, 0, 0), STREAM_SHAPE, P, ov, device=local)
-    acc.set_floor_row(z_lo // 64)
     hin = host_in.numpy()
-    out_ptr = host_out.numpy().ctypes.data_as(C.POINTER(C.c_uint8))
-    fin = C.c_int64()
-    vox = [0]
-
-    def step(zi):
-        a = int(zs[zi]) - z_lo
-        acc.predict_row(net, zi, hin[a:a + P], batch=args.batch)
-        lim = int(zs[zi + 1]) // 64
-        fx.check(fx.lib().fx_gaccum_finalize_below(acc._h, lim, out_ptr, host_out.numel(), C.byref(fin)))
-        vox[0] += fin.value * dy * dx
-
-    for k in range(args.warmup):
-        step(r0 + k)
+    host_out = torch.empty((4 * 64, dy, dx), dtype=torch.uint8).pin_memory()
+    # warm-up: forwards of 8 tiles of this rank's input
+    tiles = torch.from_numpy(np.ascontiguousarray(hin[:P, :P, :P])).cuda().repeat(args.batch, 1, 1)
+    prob = torch.empty((args.batch, P, P, P), dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        net.forward_dev(tiles.data_ptr(), args.batch, prob.data_ptr())
+    torch.cuda.synchronize()
+    del tiles, prob
     clocks = ClockSampler(local)
     clocks.start()
     l0 = fx.kernel_launches()
-    vox[0] = 0
     if world > 1:
         torch.distributed.barrier()
     t0 = time.perf_counter()
-    for k in range(args.steps):
-        step(r0 + args.warmup + k)
+    sr.run(lambda a, b: hin[a - z_lo:b - z_lo], out=host_out.numpy())
     secs = time.perf_counter() - t0
     launches = fx.kernel_launches() - l0
     clk = clocks.stop()
-    tot = np.array([vox[0], secs, launches], dtype=np.float64)
+    fx.check(fx.lib().fx_net_device_status(net.handle))
+    tot = np.array([sr.finalised, launches, (z_hi - z_lo) * dy * dx], dtype=np.float64)
     if world > 1:
         t = torch.tensor(tot)
         torch.distributed.all_reduce(t)
         m = torch.tensor([secs], dtype=torch.float64)
         torch.distributed.all_reduce(m, op=torch.distributed.ReduceOp.MAX)
-        tot = t.numpy()
-        secs = float(m.item())
+        tot, secs = t.numpy(), float(m.item())
     value = tot[0] / secs / 1e6
     if rank == 0:
-        rows = len(zs) * len(fx.tile_starts(dy, P, ov)) * len(fx.tile_starts(dx, P, ov))
+        nrows = sr.rows
         print(json.dumps({
-            "metric": STREAM_METRIC, "value": value, "unit": "Mvoxels/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 + f16 (calibrated schedule)",
+            "metric": STREAM_METRIC, "value": value, "unit": "Mvoxels/s", "n_gpus": world, "steps": 1,
+            "warmup": args.warmup, "ms_per_step": secs * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "e4m3 + f16 (calibrated schedule)",
             "data": "synthetic: 2048x4096x4096 u8 spiral sheet (pitch 14, thickness 3, N(170,15)/N(40,10), blur 1), "
                     "noise keyed per 64^3 chunk, seed 4; random-init Kaiming weights (seed 1)",
-            "config": {"workload": f"out-of-core streaming sample: {args.steps} tile rows of 1764 192^3 tiles per GPU "
-                                   f"(grid {rows} tiles), overlap 0.5, global accumulator window on the device, "
-                                   "u8 chunk rows finalised per row", "volume": list(STREAM_SHAPE), "patch": P,
-                       "overlap": ov, "batch": args.batch, "first_row": r0, "parallelism": f"row ranges x{world}",
-                       "l2": "inputs larger than L2: 7 GB of input planes per step"},
+            "config": {"workload": f"out-of-core streaming: tile rows [0, {nrows}) of the 21 x 42 x 42 grid of 192^3 "
+                                   "tiles at overlap 0.5, one step = the whole run, rows split over the GPUs, "
+                                   "boundary chunk rows finalised by the lower GPU after an NVLink (IPC) band add",
+                       "volume": list(STREAM_SHAPE), "patch": P, "overlap": ov, "batch": args.batch,
+                       "tile_rows": nrows, "tiles": nrows * 42 * 42, "parallelism": f"tile-row ranges x{world}",
+                       "l2": "inputs larger than L2: 3.2 GB of input planes per tile row"},
             "precision_schedule": dict(precision_report(net, None), calibration_dice=d_cal),
-            "e2e": {"value": value, "unit": "Mvoxels/s", "h2d_bytes_per_step": P * dy * dx * world,
-                    "d2h_bytes_per_step": int(tot[0] / args.steps),
-                    "path": "fx_gaccum_predict_row + fx_gaccum_finalize_below, pinned host planes in, u8 chunk rows out"},
-            "clocks": clk, "gpu_launches": int(tot[2]),
+            "e2e": {"value": value, "unit": "Mvoxels/s", "h2d_bytes_per_step": int(tot[2]),
+                    "d2h_bytes_per_step": int(tot[0]),
+                    "path": "fenix_b200.stream.StreamRank: fx_gaccum_predict_row from pinned host planes, "
+                            "fx_gaccum_finalize_below to pinned host u8, band export / add over IPC"},
+            "clocks": clk, "gpu_launches": int(tot[1]),
         }))
-    acc.close()
+    sr.close()
     net.close()
     if world > 1:
         torch.distributed.barrier()
@@ -705,6 +706,8 @@ def main():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fxvol", action="store_true")
+    ap.add_argument("--stream-rows", type=int, default=0,
+                    help="stream workload: run the first R tile rows of the grid (0: all 21)")
     ap.add_argument("--minimal", action="store_true",
                     help="warm-up and timed steps only (no e2e, parity, peaks, baselines): for profiler launch lists")
     ap.add_argument("--workload", default="surface", choices=["surface", "ink", "stream"],

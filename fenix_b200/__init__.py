@@ -169,6 +169,9 @@ def lib():
     _sig(L, "fx_gaccum_scatter", i32, [vp, i64, i64, i64, f32p])
     _sig(L, "fx_gaccum_predict_row", i32, [vp, vp, i64, u8p, C.POINTER(InferOpts)])
     _sig(L, "fx_gaccum_finalize_below", i32, [vp, i64, u8p, i64, i64p])
+    _sig(L, "fx_gaccum_export_planes", i32, [vp, i64, i64, vp])
+    _sig(L, "fx_gaccum_add_planes", i32, [vp, i64, i64, vp])
+    _sig(L, "fx_gaccum_discard_below", i32, [vp, i64])
     _sig(L, "fx_conv3d", i32, [vp, i32, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp])
     _sig(L, "fx_conv_transpose2", i32, [vp, i32, i32, i32, i32, i32, vp, vp, i32, i32, vp, vp])
     _sig(L, "fx_accum_finalize", i32, [vp, i64, i64, i64, i64, i64, vp, vp, vp, vp, vp, vp])

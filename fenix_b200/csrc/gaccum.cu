@@ -260,4 +260,46 @@ fx_status fx_gaccum_finalize_below(fx_gaccum* a, int64_t row_lim, uint8_t* host_
     FX_ABI_CATCH
 }
 
+// ---- composing accumulators of several GPUs (disjoint tile-row ranges, one accumulator each) ----
+
+fx_status fx_gaccum_export_planes(fx_gaccum* a, int64_t z0, int64_t n, float* dev_dst) {
+    FX_ABI_TRY
+    if (!a || !dev_dst || n < 0) return abi_error(FX_INVALID_ARGUMENT, "fx_gaccum_export_planes: bad argument");
+    if (z0 < a->wz0 || z0 + n > a->wz0 + a->win_planes)
+        return abi_error(FX_INVALID_ARGUMENT, "fx_gaccum_export_planes: planes outside the accumulator window");
+    cudaSetDevice(a->dev);
+    const size_t pb = sizeof(float) * static_cast<size_t>(a->plane());
+    cudaError_t e = cudaMemcpyAsync(dev_dst, a->win[a->cur] + (z0 - a->wz0) * a->plane(), static_cast<size_t>(n) * pb,
+                                    cudaMemcpyDeviceToDevice, a->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(a->stream);
+    return e == cudaSuccess ? FX_OK : cuda_err(e, "fx_gaccum_export_planes");
+    FX_ABI_CATCH
+}
+
+fx_status fx_gaccum_add_planes(fx_gaccum* a, int64_t z0, int64_t n, const float* dev_src) {
+    FX_ABI_TRY
+    if (!a || !dev_src || n < 0) return abi_error(FX_INVALID_ARGUMENT, "fx_gaccum_add_planes: bad argument");
+    if (z0 < a->wz0 || z0 + n > a->wz0 + a->win_planes)
+        return abi_error(FX_INVALID_ARGUMENT, "fx_gaccum_add_planes: planes outside the accumulator window");
+    cudaSetDevice(a->dev);
+    cudaError_t e = fxk::launch_accum_add(a->win[a->cur] + (z0 - a->wz0) * a->plane(), dev_src, n * a->plane(), a->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(a->stream);
+    return e == cudaSuccess ? FX_OK : cuda_err(e, "fx_gaccum_add_planes");
+    FX_ABI_CATCH
+}
+
+fx_status fx_gaccum_discard_below(fx_gaccum* a, int64_t row_lim) {
+    FX_ABI_TRY
+    if (!a) return abi_error(FX_INVALID_ARGUMENT, "fx_gaccum_discard_below: null accumulator");
+    cudaSetDevice(a->dev);
+    row_lim = std::min(row_lim, a->ncz);
+    if (row_lim <= a->floor_row) return FX_OK;
+    cudaError_t e = slide(a, row_lim * fx_gaccum::T);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(a->stream);
+    if (e != cudaSuccess) return cuda_err(e, "fx_gaccum_discard_below");
+    a->floor_row = row_lim;
+    return FX_OK;
+    FX_ABI_CATCH
+}
+
 }  // extern "C"

@@ -325,6 +325,18 @@ fx_status fx_gaccum_predict_row(fx_gaccum* acc, fx_net* net, int64_t zi, const u
  * receives their count. The window then starts at row_lim. */
 fx_status fx_gaccum_finalize_below(fx_gaccum* acc, int64_t row_lim, uint8_t* host_u8, int64_t cap_bytes,
                                    int64_t* planes_out);
+/* Composing the accumulators of several GPUs that each run a contiguous range of tile rows (the
+ * out-of-core run over N GPUs; the reference shares one host GlobalAccum between its device
+ * threads, src/ml/inference.cpp:1402-1586). The chunk rows a range's first rows share with the
+ * range below are finished by the owner below: the upper accumulator copies those planes out
+ * (fx_gaccum_export_planes, bbox-local planes [z0, z0 + n) of its window into dev_dst, f32 on its
+ * device) and drops them from its window without finalizing (fx_gaccum_discard_below); the owner
+ * adds them into its own window (fx_gaccum_add_planes: dev_src may be a peer's or IPC-mapped
+ * memory, read by a kernel on the owner's device) before finalizing them. No reference
+ * counterpart as functions: they split GlobalAccum's shared state across devices. */
+fx_status fx_gaccum_export_planes(fx_gaccum* acc, int64_t z0, int64_t n, float* dev_dst);
+fx_status fx_gaccum_add_planes(fx_gaccum* acc, int64_t z0, int64_t n, const float* dev_src);
+fx_status fx_gaccum_discard_below(fx_gaccum* acc, int64_t row_lim);
 
 /* ---- tiling math (host) ---- */
 /* Start positions along one axis; returns the count (writes at most cap). */
