@@ -1,7 +1,8 @@
 """z-slab sharding on two GPUs against the one-GPU prediction of the same volume, both ways it runs:
 one process per GPU (fenix_b200.shard.ShardedPredictor: bands read from the neighbour's HBM through
 a CUDA IPC mapping, host barriers on a gloo group, no NCCL) and one process with a thread per GPU
-(fx_predict_volume_multi, bands read through peer mappings). Needs two devices; skipped otherwise.
+(fx_predict_volume_multi, bands read through peer mappings). Needs two devices, skipped otherwise;
+the same drivers with their ranks / shards sharing one device run on one.
 NVLS is off in every library the ranks use (NCCL_NVLS_ENABLE=0); the path itself uses no NCCL."""
 import ctypes as C
 import os
@@ -19,7 +20,7 @@ pytestmark = pytest.mark.gpu
 SHAPE, P, OV, BATCH = (160, 96, 80), 64, 0.5, 2
 
 
-def _rank(rank, world, port, wpath, outdir):
+def _rank(rank, world, port, wpath, outdir, one_device=False):
     import datetime
 
     import torch
@@ -28,10 +29,11 @@ def _rank(rank, world, port, wpath, outdir):
     from fenix_b200.shard import ShardedPredictor
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    torch.cuda.set_device(rank)
+    dev = 0 if one_device else rank
+    torch.cuda.set_device(dev)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
-        net = fx.Net(wpath, P, max_batch=BATCH, precision="f16", device=rank)
+        net = fx.Net(wpath, P, max_batch=BATCH, precision="f16", device=dev)
         vol = fx.synth_spiral(SHAPE, 7, fx.SPIRAL_CONFIG1)
         sp = ShardedPredictor(net, SHAPE, OV, BATCH, rank=rank, world=world, group=dist.group.WORLD)
         me = sp.me
@@ -75,6 +77,21 @@ def test_two_gpu_processes_match_one_gpu(cuda_torch, tmp_path):
         port = s.getsockname()[1]
     with tempfile.TemporaryDirectory() as td:
         mp.spawn(_rank, args=(2, port, str(w), td), nprocs=2, join=True)
+        got = np.concatenate([np.load(os.path.join(td, f"r{r}.npy")) for r in range(2)])
+    close_to(got, one_gpu(w))
+
+
+def test_two_processes_on_one_gpu_match_one_gpu(cuda_torch, tmp_path):
+    """The one-process-per-GPU driver's IPC hand-over, barriers and band fold with both ranks on one
+    device (host barriers only: no kernel waits on another rank's)."""
+    import torch.multiprocessing as mp
+
+    w = make_plain_unet(tmp_path / "c1.fxweights", CONFIG1_FEATURES, seed=0)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as td:
+        mp.spawn(_rank, args=(2, port, str(w), td, True), nprocs=2, join=True)
         got = np.concatenate([np.load(os.path.join(td, f"r{r}.npy")) for r in range(2)])
     close_to(got, one_gpu(w))
 
