@@ -563,7 +563,8 @@ def run_ink(args):
                          "peak_source": "fx_tc_peak sustained e4m3 / f16 rates weighted by the step's e4m3 FLOP share",
                          "tc_peaks_measured": tc, "conv_ms_per_step": prof["conv_ms"],
                          "conv_flops_per_step": prof["conv_flops"], "fp8_flop_share": f8,
-                         "conv_share_of_step": prof["conv_ms"] / (ms / args.steps)},
+                         "conv_share_of_step": prof["conv_ms"] / (ms / args.steps),
+                         "frac_step": prof["conv_flops"] / (ms / args.steps / 1e3) / 1e12 / peak},
             "precision_schedule": precision_report(net, sched),
             "conv_layers": layer_table,
             "parity": parity,
@@ -703,7 +704,7 @@ def main():
     ap.add_argument("--size", type=int, default=1024)
     ap.add_argument("--patch", type=int, default=128)
     ap.add_argument("--overlap", type=float, default=0.5)
-    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fxvol", action="store_true")
     ap.add_argument("--stream-rows", type=int, default=0,
@@ -934,6 +935,8 @@ def main():
                 "conv_ms_per_step": prof["conv_ms"], "conv_flops_per_step": prof["conv_flops"],
                 "fp8_flop_share": prof["fp8_flops"] / max(prof["conv_flops"], 1.0),
                 "conv_share_of_step": prof["conv_ms"] / (ms / args.steps),
+                # the whole step against the same denominator: its conv FLOPs over its device time
+                "frac_step": prof["conv_flops"] / (ms / args.steps / 1e3) / 1e12 / peak,
                 "frac_nominal": conv_tflops / mixed(4500.0, 2250.0),
                 "nominal": "4.5 PFLOP/s e4m3, 2.25 PFLOP/s 16-bit (dense)",
             },
