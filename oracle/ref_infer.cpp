@@ -15,7 +15,10 @@
 // usage: ref_infer <w.fxweights> <vol.u8> dz dy dx patch overlap batch <out.f32|-> [threads] [key=value ...]
 //   keys (InferOptions fields, src/ml/infer.hpp:38-103): tta=N, norm=zscore|pct_minmax|unit255,
 //   channel=N, sigmoid=0|1, core=z,y,x,dz,dy,dx (output crop), skipconst=1 (the constant-input tile
-//   filter of predict-scroll's region mode, src/ml/inference.cpp:1885-1900)
+//   filter of predict-scroll's region mode, src/ml/inference.cpp:1885-1900), ckpt=<path> with
+//   whash=<u64> ihash=<u64> (InferOptions::ckpt_path / weights_hash / input_hash), stopafter=K (the
+//   filler fails on its (K+1)-th patch: the reference then saves its progress to ckpt and exits 1,
+//   src/ml/infer.hpp:840-846 — the run a resume continues)
 // prints one JSON line: {"seconds": ..., "threads": ..., "tiles": ..., "dims": [z, y, x]} and writes the
 // f32 probability volume (the core's dims when cropped).
 #include "ml/infer.hpp"
@@ -24,6 +27,7 @@
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -120,6 +124,7 @@ int run(Net& net, int argc, char** argv, Extent3 d, const std::string& vpath, co
     opt.batch = std::atoi(argv[8]);
     opt.half = false;  // fp32 on the CPU
     const VolumeView<const u8> uv = vol.view();
+    long stop_after = -1;
     for (int i = 10; i < argc; ++i) {
         const std::string a = argv[i];
         const auto eq = a.find('=');
@@ -134,6 +139,14 @@ int run(Net& net, int argc, char** argv, Extent3 d, const std::string& vpath, co
             std::sscanf(v.c_str(), "%lld,%lld,%lld,%lld,%lld,%lld", &c[0], &c[1], &c[2], &c[3], &c[4], &c[5]);
             opt.core_org = {c[0], c[1], c[2]};
             opt.core_ext = {c[3], c[4], c[5]};
+        } else if (k == "ckpt") {
+            opt.ckpt_path = v;
+        } else if (k == "whash") {
+            opt.weights_hash = std::strtoull(v.c_str(), nullptr, 10);
+        } else if (k == "ihash") {
+            opt.input_hash = std::strtoull(v.c_str(), nullptr, 10);
+        } else if (k == "stopafter") {
+            stop_after = std::atol(v.c_str());
         } else if (k == "skipconst" && v == "1") {
             opt.tile_filter = [uv](s64 z0, s64 y0, s64 x0, s64 P) {
                 const Extent3 dd = uv.dims();
@@ -148,9 +161,11 @@ int run(Net& net, int argc, char** argv, Extent3 d, const std::string& vpath, co
         }
     }
     const auto t0 = std::chrono::steady_clock::now();
+    long filled = 0;
     auto prob = ml::predict_surface_filled(
         d,
-        [uv](s64 z0, s64 y0, s64 x0, int P, float* out) {
+        [uv, stop_after, &filled](s64 z0, s64 y0, s64 x0, int P, float* out) {
+            if (stop_after >= 0 && filled++ >= stop_after) throw std::runtime_error("stopafter: filler stops");
             parallel_for(0, P, [&](s64 z) {
                 for (int y = 0; y < P; ++y)
                     for (int x = 0; x < P; ++x)

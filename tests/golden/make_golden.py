@@ -27,6 +27,10 @@ Runs only where the reference tree is present (it compiles oracle/_ref from it):
                       so this map comes from the C ORACLE (fxo_predict_tiled), whose cube path the
                       net_* / net128_* fixtures pin against the reference and whose anisotropic
                       forward tests/test_ink_oracle.py checks against PyTorch fp32. Full map as u16.
+  * ckpt_ref.npz   — a checkpoint file written by the reference itself: predict_surface_filled with
+                      ckpt_path set, its filler failing after 3 patches so that it saves its
+                      progress (src/ml/infer.hpp:840-846), as raw bytes; and the same run's full map
+                      uninterrupted (u16). The GPU path must resume the reference's file.
   * hash64.npz     — the reference's own hash64 (src/core/hash.hpp via oracle/_ref/ref_hash) of
                       fixed byte strings and a chained 1 MiB stream: the identity hashes of its
                       prediction checkpoints.
@@ -289,6 +293,31 @@ def fxvol():
     print(f"fxvol: {len(fc.TILE_CASES_U8) + len(fc.TILE_CASES_F32)} tiles, archive {out.stat().st_size} bytes")
 
 
+CKPT = dict(features=(16, 32, 64, 128), weight_seed=0, shape=(96, 64, 128), volume_seed=13, patch=64, overlap=0.5,
+            batch=2, stop_after=3, whash=11, ihash=22)
+
+
+def ckpt_ref():
+    c = CKPT
+    vol = fx.synth_spiral(c["shape"], c["volume_seed"], fx.SPIRAL_CONFIG1)
+    with tempfile.TemporaryDirectory() as td:
+        w = make_plain_unet(Path(td) / "w.fxweights", c["features"], seed=c["weight_seed"])
+        ck = Path(td) / "run.ckpt"
+        try:
+            orc.ref_infer(w, vol, c["patch"], c["overlap"], batch=c["batch"], ckpt=str(ck), whash=c["whash"],
+                          ihash=c["ihash"], stopafter=c["stop_after"])
+            raise RuntimeError("ckpt_ref: the interrupted reference run did not fail")
+        except subprocess.CalledProcessError:
+            pass
+        raw = ck.read_bytes()
+        full, _ = orc.ref_infer(w, vol, c["patch"], c["overlap"], batch=c["batch"])
+    done = int.from_bytes(raw[48:56], "little")
+    np.savez_compressed(HERE / "ckpt_ref.npz", ckpt=np.frombuffer(raw, dtype=np.uint8),
+                        prob_u16=np.round(full.astype(np.float64) * 65535.0).astype(np.uint16),
+                        **{k: np.array(v) for k, v in c.items()})
+    print(f"ckpt_ref: {len(raw)} bytes, {done} tiles done")
+
+
 def hash64():
     out = subprocess.run([str(orc.REF / "ref_hash")], capture_output=True, text=True, check=True).stdout
     rows, chain = [], None
@@ -327,6 +356,8 @@ def main():
             ink_case(name)
     if a.only in (None, "hash64"):
         hash64()
+    if a.only in (None, "ckpt_ref"):
+        ckpt_ref()
     if a.only in (None, "fxvol"):
         fxvol()
 

@@ -78,3 +78,36 @@ def test_resume_from_reference_layout_checkpoint(cuda_torch, tmp_path):
     with pytest.raises(fx.FxError):  # checkpoints take no output crop (src/ml/infer.hpp:575)
         net.predict_volume(vol, overlap=ov, batch=batch, ckpt_path=ck, core=(8, 8, 8, 32, 32, 32))
     net.close()
+
+
+def test_resume_reference_written_checkpoint(cuda_torch, tmp_path):
+    """A checkpoint the reference itself wrote (tests/golden/ckpt_ref.npz: predict_surface_filled
+    interrupted by its filler after 3 patches, progress saved by its own CkptWriter) is resumed by
+    the GPU path, which finishes the run; the result matches the reference's uninterrupted map at
+    the f16 path's bound."""
+    from pathlib import Path
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "ckpt_ref.npz")
+    raw = g["ckpt"].tobytes()
+    f = HDR.unpack(raw[:112])
+    done, total = f[6], f[5]
+    assert f[0] == b"FXICKPT3" and 0 < done < total
+    w = make_plain_unet(tmp_path / "w.fxweights", tuple(int(v) for v in g["features"]), seed=int(g["weight_seed"]))
+    vol = fx.synth_spiral(tuple(int(v) for v in g["shape"]), int(g["volume_seed"]), fx.SPIRAL_CONFIG1)
+    ck = tmp_path / "ref.ckpt"
+    ck.write_bytes(raw)
+    P, ov, batch = int(g["patch"]), float(g["overlap"]), int(g["batch"])
+    net = fx.Net(w, P, max_batch=batch, precision="f16")
+    got, _ = net.predict_volume(vol, overlap=ov, batch=batch, ckpt_path=ck, weights_hash=int(g["whash"]),
+                                input_hash=int(g["ihash"]))
+    own, _ = net.predict_volume(vol, overlap=ov, batch=batch)
+    net.close()
+    assert not ck.exists()
+    ref = g["prob_u16"].astype(np.float32) / np.float32(65535.0)
+    e, e_own = np.abs(got - ref), np.abs(got - own)
+    print(f"resumed the reference's checkpoint ({done}/{total} tiles done): vs reference max-abs {e.max():.3e}, "
+          f"vs own uninterrupted run max-abs {e_own.max():.3e}")
+    assert float(e.max()) <= 1e-2
+    # the first tiles came from the reference's fp32 accumulator in the file, not from a rerun on the
+    # GPU: they differ from the GPU's own f16 run by its rounding (a rerun would agree to ~1e-7)
+    assert float(e_own.max()) > 1e-5
