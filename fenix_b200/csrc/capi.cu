@@ -256,8 +256,12 @@ fx_status predict_ckpt(fx_net* n, const uint8_t* d_vol, int64_t dz, int64_t dy, 
     const size_t nvox = static_cast<size_t>(dz) * dy * dx;
     int64_t done = -1;
     {
-        std::vector<float> host(nvox);
-        done = ckpt_load(path, h, host);
+        std::vector<float> host;
+        if (std::FILE* f = std::fopen(path.c_str(), "rb")) {  // host copy only when there is a file
+            std::fclose(f);
+            host.resize(nvox);
+            done = ckpt_load(path, h, host);
+        }
         cudaError_t e = done >= 0 ? cudaMemcpyAsync(d_acc, host.data(), nvox * sizeof(float), cudaMemcpyHostToDevice, s)
                                   : cudaMemsetAsync(d_acc, 0, nvox * sizeof(float), s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
