@@ -1,6 +1,8 @@
 // conv_tc.cu — persistent warp-specialised tcgen05 implicit-GEMM kernel (see conv_tc.cuh for
 // the data layout and the per-layer program it executes).
 #include "conv_tc.cuh"
+
+#include <atomic>
 #include "counters.hpp"
 #include "ptx.cuh"
 
@@ -1199,12 +1201,18 @@ size_t conv_tc_ctl_bytes() { return sizeof(SmemCtl); }
 size_t conv_tc_fold_bytes(int cout) { return static_cast<size_t>(2 * 2 * 4 * 3) * cout * sizeof(float); }
 
 cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cudaStream_t stream) {
-    static bool configured = false;
-    if (!configured) {
+    // the dynamic shared memory limit is a per-device function attribute: set it once on every device
+    // a launch comes to (threads driving several GPUs launch concurrently)
+    static std::atomic<uint64_t> configured[4] = {};
+    int dev = 0;
+    if (cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 256) return cudaErrorInvalidDevice;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(configured[dev >> 6].load(std::memory_order_acquire) & bit)) {
         cudaError_t e =
             cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
         if (e != cudaSuccess) return e;
-        configured = true;
+        configured[dev >> 6].fetch_or(bit, std::memory_order_acq_rel);
     }
     const int nch = p.N_tile / 16;
     if (!p.fold && (p.N_tile % 16 || !(nch == 1 || nch == 2 || nch == 4 || nch == 8 || nch == 16 || nch == 20)))
