@@ -134,6 +134,7 @@ def lib():
     _sig(L, "fx_net_classes", i32, [vp])
     _sig(L, "fx_net_features", i32, [vp, C.POINTER(C.c_int), i32])
     _sig(L, "fx_net_calibrate", i32, [vp, u8p, i32])
+    _sig(L, "fx_net_set_norm", i32, [vp, i32])
     _sig(L, "fx_net_act_scales", i32, [vp, f32p, i32])
     _sig(L, "fx_net_set_act_scales", i32, [vp, f32p, i32])
     _sig(L, "fx_net_set_layer_precision", i32, [vp, C.POINTER(C.c_int), i32])
@@ -367,6 +368,11 @@ class Net:
         buf = (C.c_int * 16)()
         n = lib().fx_net_features(self._h, buf, 16)
         return list(buf[:n])
+
+    def set_norm(self, norm) -> None:
+        """Input normalisation ("zscore", "pct_minmax", "unit255" or its fx_norm code) that
+        calibrate, calibrate_schedule and forward apply to u8 tiles (default zscore)."""
+        check(lib().fx_net_set_norm(self._h, NORMS[norm] if isinstance(norm, str) else int(norm)))
 
     def calibrate(self, patches_u8: np.ndarray) -> None:
         p = np.ascontiguousarray(patches_u8, dtype=np.uint8)

@@ -473,6 +473,13 @@ fx_status fx_net_calibrate(fx_net* n, const uint8_t* host_patches, int count) {
     });
 }
 
+fx_status fx_net_set_norm(fx_net* n, int norm) {
+    if (!n || norm < FX_NORM_ZSCORE || norm > FX_NORM_UNIT255)
+        return set_err(FX_INVALID_ARGUMENT, "fx_net_set_norm: bad argument");
+    n->net.set_norm(norm);
+    return FX_OK;
+}
+
 fx_status fx_net_set_act_scales(fx_net* n, const float* scales, int count) {
     return guarded([&]() -> fx_status {
         if (!n || !scales) return set_err(FX_INVALID_ARGUMENT, "fx_net_set_act_scales: null argument");

@@ -85,7 +85,16 @@ Status Net::parse(const WeightMap& wm) {
             const size_t k = n.find(".seg_layers.");
             if (n.rfind(pre, 0) == 0 && k != std::string::npos) return parse_resenc(wm, "shared_encoder", n.substr(0, k));
         }
-        return fail(kUnsupported, "fxweights: residual encoder without task_decoders.<task>.seg_layers");
+        // the ink checkpoints: shared_decoder.* without seg_layers + task_heads.<task> (one 1x1x1
+        // conv, src/ml/nets/resenc_unet.hpp:291-316)
+        if (get("shared_decoder.transpconvs.0.weight"))
+            for (const auto& kv : wm) {
+                const std::string& n = kv.first;
+                const std::string pre = "task_heads.";
+                if (n.rfind(pre, 0) == 0 && n.size() > 7 && n.compare(n.size() - 7, 7, ".weight") == 0)
+                    return parse_resenc(wm, "shared_encoder", "shared_decoder", n.substr(0, n.size() - 7));
+            }
+        return fail(kUnsupported, "fxweights: residual encoder without task_decoders.<task>.seg_layers or task_heads.<task>");
     }
     // encoder.stages.{s}.convs.{i}.conv.weight
     S_ = 0;
@@ -187,7 +196,7 @@ Status Net::parse(const WeightMap& wm) {
 // (1 conv), stages of BasicBlockD (conv1 with the stage's stride, conv2 without activation,
 // optional scSE, skip = [AvgPool(2)] + [1x1 conv + norm], add, LeakyReLU), and the plain decoder
 // (transpconvs, one ConvStack per stage, seg_layers) under `dec`.
-Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std::string& dec) {
+Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std::string& dec, const std::string& head) {
     auto get = [&](const std::string& n) -> const HostTensor* {
         auto it = wm.find(n);
         return it == wm.end() ? nullptr : &it->second;
@@ -333,12 +342,14 @@ Status Net::parse_resenc(const WeightMap& wm, const std::string& enc, const std:
             L.lin = L.lout = lvl;
         }
     }
-    const std::string sl = dec + ".seg_layers." + std::to_string(S_ - 2);
+    // the head: the deepest decoder stage's seg_layers, or a separate task head (ink checkpoints)
+    const std::string sl = head.empty() ? dec + ".seg_layers." + std::to_string(S_ - 2) : head;
     const HostTensor* hw = get(sl + ".weight");
     const HostTensor* hb = get(sl + ".bias");
     if (!hw || !hb) return fail(kDecode, "fxweights: missing " + sl + ".{weight,bias}");
     ncls_ = static_cast<int>(hw->shape[0]);
-    if (hw->shape[1] != F_[0] || ncls_ < 1 || ncls_ > 2) return fail(kUnsupported, "net: head must map F0 -> 1 or 2 classes");
+    if (hw->shape.size() != 5 || hw->shape[1] != F_[0] || ncls_ < 1 || ncls_ > 2)
+        return fail(kUnsupported, "net: head must map F0 -> 1 or 2 classes");
     head_w_ = hw->data;
     head_b_ = hb->data;
     return ok();

@@ -230,7 +230,10 @@ class Net {
     bool profile_ = false;
     std::vector<ProfEv> prof_;
     Status parse(const WeightMap& wm);
-    Status parse_resenc(const WeightMap& wm, const std::string& enc, const std::string& dec);
+    // head: the head conv's prefix when it sits outside the decoder ("task_heads.<task>"); empty:
+    // the decoder's seg_layers
+    Status parse_resenc(const WeightMap& wm, const std::string& enc, const std::string& dec,
+                        const std::string& head = "");
     Status alloc();
     Status build_layer(Layer& L, int q);
     Status run_conv(Layer& L, int q, const uint8_t* in_ptr, int64_t in_bs, int64_t in_gs, uint8_t* out_ptr,

@@ -151,7 +151,7 @@ def se_reduced(channels: int, rd_ratio: float = 1.0 / 16.0, divisor: int = 8) ->
 
 
 def resenc_unet_params(features, blocks, ncls: int = 2, se: bool = False, plain_naming: bool = True,
-                       task: str = "surface", seed: int = 0) -> dict[str, np.ndarray]:
+                       task: str = "surface", seed: int = 0, task_head: bool = False) -> dict[str, np.ndarray]:
     """Seeded random init of the residual-encoder UNet (src/ml/nets/resenc_unet.hpp:55-318) with
     its checkpoint names: ``{enc}.stem.convs.0.*``, ``{enc}.stages.{s}.blocks.{b}.conv1/conv2.*``,
     ``...squeeze_excitation.cSE.fc1/fc2`` + ``sSE.conv`` (scSE), ``...skip.{i}.conv/norm`` (the 1x1
@@ -169,7 +169,10 @@ def resenc_unet_params(features, blocks, ncls: int = 2, se: bool = False, plain_
     def small(n, base=0.0):
         return (base + 0.1 * torch.randn(n, generator=g)).numpy()
 
-    enc, dec = ("encoder", "decoder") if plain_naming else ("shared_encoder", f"task_decoders.{task}")
+    if task_head:  # the ink checkpoints: shared_decoder without seg_layers + task_heads.<task>
+        enc, dec = "shared_encoder", "shared_decoder"
+    else:
+        enc, dec = ("encoder", "decoder") if plain_naming else ("shared_encoder", f"task_decoders.{task}")
     P: dict[str, np.ndarray] = {}
 
     def cna(pre, cin, cout, k, bias=True):
@@ -205,12 +208,16 @@ def resenc_unet_params(features, blocks, ncls: int = 2, se: bool = False, plain_
         P[f"{dec}.transpconvs.{t}.weight"] = kaiming((below, skipc, 2, 2, 2), skipc * 8)
         P[f"{dec}.transpconvs.{t}.bias"] = small(skipc)
         cna(f"{dec}.stages.{t}.convs.0", 2 * skipc, skipc, 3)
-        P[f"{dec}.seg_layers.{t}.weight"] = kaiming((ncls, skipc, 1, 1, 1), skipc)
-        P[f"{dec}.seg_layers.{t}.bias"] = small(ncls)
+        if not task_head:
+            P[f"{dec}.seg_layers.{t}.weight"] = kaiming((ncls, skipc, 1, 1, 1), skipc)
+            P[f"{dec}.seg_layers.{t}.bias"] = small(ncls)
+    if task_head:
+        P[f"task_heads.{task}.weight"] = kaiming((ncls, features[0], 1, 1, 1), features[0])
+        P[f"task_heads.{task}.bias"] = small(ncls)
     return P
 
 
 def make_resenc_unet(path: str | Path, features, blocks, ncls: int = 2, se: bool = False,
-                     plain_naming: bool = True, seed: int = 0) -> Path:
-    write_fxweights(path, resenc_unet_params(features, blocks, ncls, se, plain_naming, seed=seed))
+                     plain_naming: bool = True, seed: int = 0, task: str = "surface", task_head: bool = False) -> Path:
+    write_fxweights(path, resenc_unet_params(features, blocks, ncls, se, plain_naming, task, seed, task_head))
     return Path(path)

@@ -10,6 +10,8 @@
  *                                     src/ml/weights.hpp:63-142), the TrtNet/AotiNet adapters'
  *                                     static batch/patch/classes (src/ml/trt_engine.hpp:35-106)
  *   fx_net_calibrate                — fp8 static calibration (tools/ml-export/fp8_forward.py:88-127)
+ *   fx_net_set_norm                 — the stage's input normalisation for calibration and
+ *                                     fx_net_forward (src/ml/inference.cpp:898-908, 721-740)
  *   fx_net_forward                  — the operator concept net->forward(x) followed by the
  *                                     softmax/sigmoid channel select + nan_to_num
  *                                     (src/ml/infer.hpp:760-767, src/ml/inference.cpp:226-233)
@@ -160,6 +162,10 @@ int fx_net_features(const fx_net* net, int* out, int cap); /* returns the stage 
 /* fp8 only: record per-tensor activation amax over `n` host u8 patches ([n][P][P][P]) in a
  * 16-bit (f16) calibration forward, and fix every activation scale to running-max(amax) / 448. */
 fx_status fx_net_calibrate(fx_net* net, const uint8_t* host_patches, int n);
+/* The input normalisation (fx_norm) that fx_net_calibrate, fx_net_calibrate_schedule and
+ * fx_net_forward apply to their u8 tiles (default zscore); the predict entry points set their own
+ * from fx_infer_opts. A net predicting with pct_minmax or unit255 is calibrated under the same. */
+fx_status fx_net_set_norm(fx_net* net, int norm);
 /* Per-tensor activation scales after calibration (cap entries); returns the count. One per conv
  * layer, in the order encoder convs (stage-major), transposed convs (finest level first),
  * decoder convs (finest level first): the scale of that layer's input activation. */

@@ -124,9 +124,14 @@ inline float predict_q() {
 }  // namespace detail
 
 // predict-surface (src/ml/inference.cpp:721-740 -> run_predict 362-714 -> run_predict_core 238-360).
-[[nodiscard]] inline Expected<int> run_predict_surface(std::span<const std::string_view> args) {
-    auto a = parse_predict_args(args);
+namespace detail {
+// run_predict (src/ml/inference.cpp:362-714) over the C ABI: the stage's options after the
+// argument grammar, the net, .fxvol in and out.
+[[nodiscard]] inline Expected<int> run_predict(std::span<const std::string_view> args, std::string_view name,
+                                               void (*stage_defaults)(InferOptions&)) {
+    auto a = parse_predict_args(args, name);
     if (!a) return std::unexpected(a.error());
+    if (stage_defaults) stage_defaults(a->opt);
     if (!a->batch_explicit) a->opt.batch = 8;
     if (!a->opt.ckpt_path.empty()) {  // the checkpoint's identity, as the reference computes it
         a->opt.weights_hash = weights_hash64(a->weights);
@@ -134,9 +139,15 @@ inline float predict_q() {
     }
     auto in = codec::VolumeArchive::open(a->in, a->device);
     if (!in) return std::unexpected(in.error());
-    if (in->src_dtype() != codec::DType::u8) return err(Errc::unsupported, "predict-surface: the input archive is not u8");
+    if (in->src_dtype() != codec::DType::u8)
+        return err(Errc::unsupported, std::string(name) + ": the input archive is not u8");
     auto net = B200Net::load(a->weights, a->opt.patch, a->opt.batch, a->precision, a->device);
     if (!net) return std::unexpected(net.error());
+    auto fx_norm_of = [](Norm n) {
+        return n == Norm::pct_minmax ? FX_NORM_PCT_MINMAX : (n == Norm::unit255 ? FX_NORM_UNIT255 : FX_NORM_ZSCORE);
+    };
+    if (fx_net_set_norm(net->handle(), fx_norm_of(a->opt.norm)) != FX_OK)  // calibration sees the stage's inputs
+        return err(Errc::internal, std::string(name) + ": fx_net_set_norm");
     const float q = detail::predict_q();
     if (a->precision != Precision::fp8 && a->gpus == 1) {
         if (auto r = predict_surface_fxvol(*net, a->in, a->out, a->opt, q); !r) return std::unexpected(r.error());
@@ -155,6 +166,7 @@ inline float predict_q() {
     for (int g = 1; g < a->gpus; ++g) {
         auto m = B200Net::load(a->weights, a->opt.patch, a->opt.batch, a->precision, a->device + g);
         if (!m) return std::unexpected(m.error());
+        fx_net_set_norm(m->handle(), fx_norm_of(a->opt.norm));
         if (a->precision == Precision::fp8)
             if (auto r = detail::copy_fp8_state(*net, *m); !r) return std::unexpected(r.error());
         more.push_back(std::move(*m));
@@ -167,6 +179,24 @@ inline float predict_q() {
     if (auto r = out->write_volume(static_cast<const Volume<u8>&>(*pred).view()); !r) return std::unexpected(r.error());
     if (auto r = out->close(); !r) return std::unexpected(r.error());
     return 0;
+}
+}  // namespace detail
+
+// predict-surface (src/ml/inference.cpp:721-740): the surface net, softmax channel 1, zscore.
+[[nodiscard]] inline Expected<int> run_predict_surface(std::span<const std::string_view> args) {
+    return detail::run_predict(args, "predict-surface", nullptr);
+}
+
+// predict-ink (src/ml/inference.cpp:898-908): the same driver with the ink net's options — one
+// class through a sigmoid, percentile (0.5 / 99.5) min-max normalisation. The net is whatever the
+// weights hold; the reference's ink checkpoints (nets::ResEncUNet with shared_decoder +
+// task_heads.ink) load as residual UNets with a task head.
+[[nodiscard]] inline Expected<int> run_predict_ink(std::span<const std::string_view> args) {
+    return detail::run_predict(args, "predict-ink", [](InferOptions& o) {
+        o.sigmoid = true;
+        o.channel = 0;
+        o.norm = Norm::pct_minmax;
+    });
 }
 
 // predict-scroll, global mode over a u8 .fxvol (src/ml/inference.cpp:989-1669). Zarr / URL roots,
@@ -350,11 +380,6 @@ inline float predict_q() {
     return 0;
 }
 
-// predict-ink (src/ml/inference.cpp, DINO-guided ink net): not part of this path.
-[[nodiscard]] inline Expected<int> run_predict_ink(std::span<const std::string_view>) {
-    return err(Errc::unsupported, "predict-ink: the ink-detection net is not part of the B200 surface-prediction path");
-}
-
 }  // namespace fenix_b200::ml
 
 // Stage registration (src/ml/ml.hpp:22-42): the same names and help lines as the reference's.
@@ -366,6 +391,6 @@ inline const int stage_predict_scroll = ::fenix_b200::register_stage(::fenix_b20
     "predict-scroll", "whole-scroll surface prediction (out-of-core, device-resident accumulator) -> .fxvol",
     [](std::span<const std::string_view> a, ::fenix_b200::Context&) { return ::fenix_b200::ml::run_predict_scroll(a); }});
 inline const int stage_predict_ink = ::fenix_b200::register_stage(::fenix_b200::Stage{
-    "predict-ink", "ink-detection inference (not part of the B200 path)",
+    "predict-ink", "ink-detection inference over a u8 .fxvol (sigmoid, percentile normalisation) -> .fxvol",
     [](std::span<const std::string_view> a, ::fenix_b200::Context&) { return ::fenix_b200::ml::run_predict_ink(a); }});
 }  // namespace fenix_b200::detail

@@ -226,9 +226,20 @@ int main(int argc, char** argv) {
             cfg.strides.push_back(s ? 2 : 1);
         }
         cfg.squeeze_excitation = wm->count(enc + ".stages.0.blocks.0.squeeze_excitation.sSE.conv.weight") > 0;
-        const std::string dec = cfg.plain_naming ? "decoder" : "task_decoders." + cfg.task;
-        cfg.num_classes = static_cast<int>(
-            wm->at(dec + ".seg_layers." + std::to_string(cfg.features.size() - 2) + ".weight").size(0));
+        // ink checkpoints: shared_decoder + task_heads.<task> (the reference's predict-ink config,
+        // src/ml/inference.cpp:898-908)
+        cfg.task_head = wm->count("shared_decoder.transpconvs.0.weight") > 0;
+        if (cfg.task_head) {
+            for (const auto& kv : *wm)
+                if (kv.first.rfind("task_heads.", 0) == 0 && kv.first.size() > 7 &&
+                    kv.first.compare(kv.first.size() - 7, 7, ".weight") == 0)
+                    cfg.task = kv.first.substr(11, kv.first.size() - 7 - 11);
+            cfg.num_classes = static_cast<int>(wm->at("task_heads." + cfg.task + ".weight").size(0));
+        } else {
+            const std::string dec = cfg.plain_naming ? "decoder" : "task_decoders." + cfg.task;
+            cfg.num_classes = static_cast<int>(
+                wm->at(dec + ".seg_layers." + std::to_string(cfg.features.size() - 2) + ".weight").size(0));
+        }
         nets::ResEncUNet rnet(cfg);
         rnet->eval();
         std::vector<std::string> miss;

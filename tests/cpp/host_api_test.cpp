@@ -123,7 +123,7 @@ static int cpu() {
         Context ctx;
         std::vector<std::string_view> a{"x"};
         auto r = find_stage("predict-ink")->run(a, ctx);
-        CHECK(!r && r.error().code == Errc::unsupported);
+        CHECK(!r && r.error().code == Errc::invalid_argument);  // the predict grammar wants 3 arguments
         std::vector<std::string_view> z{"s3://bucket/scroll.zarr", "0", "w.fxweights", "out.fxvol"};
         r = find_stage("predict-scroll")->run(z, ctx);
         CHECK(!r && r.error().code == Errc::unsupported);
@@ -188,6 +188,26 @@ static int stages(const char* weights, const char* dir) {
     auto gv = got ? got->read_volume_u8() : Expected<Volume<u8>>(std::unexpected(Error{}));
     const Volume<u8> wq = q32(*want);
     CHECK(gv && wq.data() && std::memcmp(gv->data(), wq.data(), vol.size()) == 0);
+    {  // predict-ink: the same driver with sigmoid on channel 0 and percentile normalisation
+        const std::string ik = std::string(dir) + "/ink.fxvol";
+        std::vector<std::string_view> a{ip, weights, ik, "64", "0.5", "0", "2"};
+        auto r = find_stage("predict-ink")->run(a, ctx);
+        if (!r) {
+            std::fprintf(stderr, "predict-ink: %s\n", r.error().message.c_str());
+            return 10;
+        }
+        ml::InferOptions io = o;
+        io.sigmoid = true;
+        io.channel = 0;
+        io.norm = ml::Norm::pct_minmax;
+        auto wi = ml::predict_surface_u8(dv, *net, io);
+        auto gi = codec::VolumeArchive::open(ik);
+        auto giv = gi ? gi->read_volume_u8() : Expected<Volume<u8>>(std::unexpected(Error{}));
+        const Volume<u8> wiq = wi ? q32(*wi) : Volume<u8>{};
+        CHECK(giv && wiq.data() && std::memcmp(giv->data(), wiq.data(), vol.size()) == 0);
+        // and it differs from the surface stage's output (other channel, activation, normalisation)
+        CHECK(giv && gv && std::memcmp(giv->data(), gv->data(), vol.size()) != 0);
+    }
     {  // predict-scroll over the same archive, global grid, no tta: the same tiles and blend
         std::vector<std::string_view> a{ip, "0", weights, sp2, "tta=0", "batch=2", "patch=64", "overlap=0.5"};
         auto r = find_stage("predict-scroll")->run(a, ctx);

@@ -21,6 +21,10 @@ Runs only where the reference tree is present (it compiles oracle/_ref from it):
                       tile filter of predict-scroll, and a one-class sigmoid head.
   * resenc_<case>.npz — the same with the reference's own nets::ResEncUNet (residual encoder,
                       optional scSE, plain or task naming) loaded from seeded random-init weights.
+  * resenc_ink.npz — the reference's predict-ink configuration (src/ml/inference.cpp:898-908): its
+                      nets::ResEncUNet with a task head (shared_encoder + shared_decoder +
+                      task_heads.ink, no scSE, one class), sigmoid and pct_minmax normalisation,
+                      through its own predict_surface_filled on a papyrus layer stack; full map u16.
   * ink_<case>.npz — the layer-stack (wide-ink) net: 64/128/256/512 features, stride (1, 2, 2) at
                       stages 1-2 and (2, 2, 2) at stage 3, one class + sigmoid, anisotropic tiles.
                       The reference's nets take one int stride per stage and its window tiles cubes,
@@ -297,6 +301,22 @@ CKPT = dict(features=(16, 32, 64, 128), weight_seed=0, shape=(96, 64, 128), volu
             batch=2, stop_after=3, whash=11, ihash=22)
 
 
+INK_RESENC = dict(features=(16, 32, 64), blocks=(1, 2, 2), weight_seed=12, shape=(64, 96, 112), volume_seed=3,
+                  stack=4, patch=64, overlap=0.25)
+
+
+def resenc_ink():
+    c = INK_RESENC
+    vol = orc.synth_papyrus(c["shape"], c["volume_seed"], c["stack"])
+    with tempfile.TemporaryDirectory() as td:
+        w = make_resenc_unet(Path(td) / "w.fxweights", c["features"], c["blocks"], ncls=1, se=False, plain_naming=False,
+                             seed=c["weight_seed"], task="ink", task_head=True)
+        prob, info = orc.ref_infer(w, vol, c["patch"], c["overlap"], batch=2, sigmoid=1, channel=0, norm="pct_minmax")
+    np.savez_compressed(HERE / "resenc_ink.npz", prob_u16=np.round(prob.astype(np.float64) * 65535.0).astype(np.uint16),
+                        **{k: np.array(v) for k, v in c.items()})
+    print(f"resenc_ink: mean {prob.mean():.4f}, > 0.5: {(prob > 0.5).mean():.3f}")
+
+
 def ckpt_ref():
     c = CKPT
     vol = fx.synth_spiral(c["shape"], c["volume_seed"], fx.SPIRAL_CONFIG1)
@@ -358,6 +378,8 @@ def main():
         hash64()
     if a.only in (None, "ckpt_ref"):
         ckpt_ref()
+    if a.only in (None, "resenc_ink"):
+        resenc_ink()
     if a.only in (None, "fxvol"):
         fxvol()
 

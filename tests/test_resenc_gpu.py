@@ -56,3 +56,24 @@ def test_resenc_fp8_runs_calibrated(cuda_torch, tmp_path):
     d = dice(u8 >= 128, g["u8"] >= 128)
     print(f"resenc plain fp8 vs reference: Dice {d:.5f} (e4m3 quantisation)")
     assert d >= 0.9
+
+
+def test_resenc_ink_task_head_matches_reference(cuda_torch, tmp_path):
+    """The reference's ink checkpoint layout (shared_encoder / shared_decoder / task_heads.ink, one
+    class) under predict-ink's options (sigmoid, percentile min-max) against the reference's own
+    inference (tests/golden/resenc_ink.npz)."""
+    g = np.load(GOLD / "resenc_ink.npz")
+    w = make_resenc_unet(tmp_path / "ink.fxweights", tuple(int(v) for v in g["features"]),
+                         tuple(int(v) for v in g["blocks"]), ncls=1, se=False, plain_naming=False,
+                         seed=int(g["weight_seed"]), task="ink", task_head=True)
+    vol = fx.synth_papyrus(tuple(int(v) for v in g["shape"]), int(g["volume_seed"]), int(g["stack"]))
+    want = g["prob_u16"].astype(np.float64) / 65535.0
+    net = fx.Net(w, int(g["patch"]), max_batch=2, precision="f16")
+    assert net.classes == 1
+    prob, u8 = net.predict_volume(vol, overlap=float(g["overlap"]), batch=2, channel=0, sigmoid=1, norm="pct_minmax")
+    net.close()
+    err = float(np.abs(prob - want).max())
+    d = dice(prob > 0.5, want > 0.5)
+    print(f"resenc ink task head f16 vs reference: max-abs {err:.2e}, Dice {d:.5f}")
+    assert err <= 1e-2 and d >= 0.99
+    assert np.array_equal(u8, orc.prob_to_u8(prob))
