@@ -199,14 +199,16 @@ namespace detail {
     });
 }
 
-// predict-scroll, global mode over a u8 .fxvol (src/ml/inference.cpp:989-1669). Zarr / URL roots,
-// region mode, the ink net, occupancy and raw-CT side inputs are not part of this path and give
+// predict-scroll, global mode over a u8 .fxvol (src/ml/inference.cpp:989-1669). net=ink takes the
+// ink net's contract (src/ml/inference.cpp:1084-1099: sigmoid on channel 0, percentile min-max).
+// Zarr / URL roots, region mode, occupancy and raw-CT side inputs are not part of this path and give
 // Errc::unsupported; gpuworkers / ahead / commit are accepted (the device window replaces them).
 [[nodiscard]] inline Expected<int> run_predict_scroll(std::span<const std::string_view> args) {
     if (args.size() < 4)
         return err(Errc::invalid_argument,
                    "usage: predict-scroll <ct.fxvol> <level> <weights.fxweights> <out_pred.fxvol> [tta=8] [batch=2] "
-                   "[patch=256] [overlap=0.5] [q=32] [bbox=z0,y0,x0,D,H,W] [precision=f16|bf16|fp8] [device=N]");
+                   "[patch=256] [overlap=0.5] [q=32] [bbox=z0,y0,x0,D,H,W] [net=surface|ink] [precision=f16|bf16|fp8] "
+                   "[device=N]");
     const std::string root(args[0]), wpath(args[2]), out_path(args[3]);
     if (root.size() < 6 || root.substr(root.size() - 6) != ".fxvol")
         return err(Errc::unsupported, "predict-scroll: only .fxvol inputs are read on the B200 path (zarr / URL roots are not)");
@@ -252,7 +254,17 @@ namespace detail {
         } else if (k == "mode") {
             if (v != "global") return err(Errc::unsupported, "predict-scroll: only mode=global runs on the B200 path");
         } else if (k == "net") {
-            if (v != "surface") return err(Errc::unsupported, "predict-scroll: only net=surface runs on the B200 path");
+            if (v == "ink") {
+                opt.sigmoid = true;
+                opt.channel = 0;
+                opt.norm = Norm::pct_minmax;
+            } else if (v == "surface") {
+                opt.sigmoid = false;
+                opt.channel = 1;
+                opt.norm = Norm::zscore;
+            } else {
+                return err(Errc::invalid_argument, "predict-scroll: net must be surface or ink");
+            }
         } else if (k == "gpuworkers" || k == "ahead" || k == "commit") {
             // replicas per device, lookahead rows and commit cadence: the device window replaces them
         } else if (k == "ct" || k == "occ" || k == "ctq" || k == "halo" || k == "region") {
@@ -281,6 +293,8 @@ namespace detail {
     auto net = B200Net::load(wpath, opt.patch, opt.batch, prec, device);
     if (!net) return std::unexpected(net.error());
     if (opt.batch > net->batch()) opt.batch = net->batch();
+    if (fx_net_set_norm(net->handle(), opt.norm == Norm::pct_minmax ? FX_NORM_PCT_MINMAX : FX_NORM_ZSCORE) != FX_OK)
+        return err(Errc::internal, "predict-scroll: fx_net_set_norm");
     auto acc = GlobalAccum::create({org[0], org[1], org[2]}, {ext[0], ext[1], ext[2]}, opt.patch, opt.overlap, 0, device);
     if (!acc) return std::unexpected(acc.error());
     auto out = codec::VolumeArchive::create(out_path, D, {q}, codec::DType::u8, device);

@@ -130,6 +130,9 @@ static int cpu() {
         std::vector<std::string_view> b{"ct.fxvol", "0", "w.fxweights", "out.fxvol", "bogus=1"};
         r = find_stage("predict-scroll")->run(b, ctx);
         CHECK(!r && r.error().code == Errc::invalid_argument);
+        std::vector<std::string_view> nk{"ct.fxvol", "0", "w.fxweights", "out.fxvol", "net=dino"};
+        r = find_stage("predict-scroll")->run(nk, ctx);
+        CHECK(!r && r.error().code == Errc::invalid_argument);
         std::vector<std::string_view> m{"ct.fxvol", "0", "w.fxweights", "out.fxvol", "mode=region"};
         r = find_stage("predict-scroll")->run(m, ctx);
         CHECK(!r && r.error().code == Errc::unsupported);
@@ -188,8 +191,56 @@ static int stages(const char* weights, const char* dir) {
     auto gv = got ? got->read_volume_u8() : Expected<Volume<u8>>(std::unexpected(Error{}));
     const Volume<u8> wq = q32(*want);
     CHECK(gv && wq.data() && std::memcmp(gv->data(), wq.data(), vol.size()) == 0);
+    // predict-scroll writes each finalised chunk with the voxels past the volume at 0 (the
+    // GlobalAccum sink), predict-surface's write_volume replicates the edge: encode an in-memory
+    // prediction's chunks the scroll's way and compare the decoded results
+    auto scroll_matches = [&](const Volume<u8>& want_v, const std::string& path, const char* label) -> bool {
+        auto s2 = codec::VolumeArchive::open(path);
+        auto sv = s2 ? s2->read_volume_u8() : Expected<Volume<u8>>(std::unexpected(Error{}));
+        if (!sv) return false;
+        const s64 T = 64, ncz = (d.z + T - 1) / T, ncy = (d.y + T - 1) / T, ncx = (d.x + T - 1) / T;
+        const std::size_t n = static_cast<std::size_t>(ncz * ncy * ncx), cv = static_cast<std::size_t>(T * T * T);
+        std::vector<u8> ch(n * cv, 0), enc(n * (cv + 4096)), dec(n * cv);
+        std::vector<uint64_t> offs(n);
+        std::vector<uint32_t> lens(n);
+        for (s64 k = 0; k < static_cast<s64>(n); ++k) {
+            const s64 cz = k / (ncy * ncx), cy = (k / ncx) % ncy, cx = k % ncx;
+            for (s64 z = 0; z < T && cz * T + z < d.z; ++z)
+                for (s64 y = 0; y < T && cy * T + y < d.y; ++y)
+                    for (s64 x = 0; x < T && cx * T + x < d.x; ++x)
+                        ch[k * cv + (z * T + y) * T + x] = want_v.data()[((cz * T + z) * d.y + cy * T + y) * d.x + cx * T + x];
+        }
+        if (fx_fxvol_encode_tiles(ch.data(), nullptr, static_cast<int64_t>(n), 32.0f, 0.65f, 0.80f, 0, enc.data(), enc.size(),
+                                  offs.data(), lens.data()) != FX_OK ||
+            fx_fxvol_decode_tiles(enc.data(), enc.size(), offs.data(), lens.data(), static_cast<int64_t>(n), 32.0f, 0.65f,
+                                  0.80f, 0, dec.data(), nullptr) != FX_OK)
+            return false;
+        std::size_t far = 0;
+        double sum = 0;
+        for (s64 z = 0; z < d.z; ++z)
+            for (s64 y = 0; y < d.y; ++y)
+                for (s64 x = 0; x < d.x; ++x) {
+                    const s64 k = ((z / T) * ncy + y / T) * ncx + x / T;
+                    const int w0 = dec[k * cv + ((z % T) * T + y % T) * T + x % T];
+                    const int dd = std::abs(int(sv->data()[(z * d.y + y) * d.x + x]) - w0);
+                    sum += dd;
+                    far += dd > 8;
+                }
+        std::fprintf(stderr, "%s (decoded q32): mean |d| %.4f, %zu voxels > 8\n", label,
+                     sum / static_cast<double>(vol.size()), far);
+        return sum / static_cast<double>(vol.size()) <= 0.25 && far * 1000 <= vol.size();
+    };
+    {  // predict-scroll over the same archive, global grid, no tta: the same tiles and blend
+        std::vector<std::string_view> a{ip, "0", weights, sp2, "tta=0", "batch=2", "patch=64", "overlap=0.5"};
+        auto r = find_stage("predict-scroll")->run(a, ctx);
+        if (!r) {
+            std::fprintf(stderr, "predict-scroll: %s\n", r.error().message.c_str());
+            return 9;
+        }
+        CHECK(scroll_matches(*want, sp2, "predict-scroll vs predict_surface"));
+    }
     {  // predict-ink: the same driver with sigmoid on channel 0 and percentile normalisation
-        const std::string ik = std::string(dir) + "/ink.fxvol";
+        const std::string ik = std::string(dir) + "/ink.fxvol", sk = std::string(dir) + "/scroll_ink.fxvol";
         std::vector<std::string_view> a{ip, weights, ik, "64", "0.5", "0", "2"};
         auto r = find_stage("predict-ink")->run(a, ctx);
         if (!r) {
@@ -207,52 +258,14 @@ static int stages(const char* weights, const char* dir) {
         CHECK(giv && wiq.data() && std::memcmp(giv->data(), wiq.data(), vol.size()) == 0);
         // and it differs from the surface stage's output (other channel, activation, normalisation)
         CHECK(giv && gv && std::memcmp(giv->data(), gv->data(), vol.size()) != 0);
-    }
-    {  // predict-scroll over the same archive, global grid, no tta: the same tiles and blend
-        std::vector<std::string_view> a{ip, "0", weights, sp2, "tta=0", "batch=2", "patch=64", "overlap=0.5"};
-        auto r = find_stage("predict-scroll")->run(a, ctx);
+        // predict-scroll net=ink: the ink contract over the global grid
+        std::vector<std::string_view> b{ip, "0", weights, sk, "tta=0", "batch=2", "patch=64", "overlap=0.5", "net=ink"};
+        r = find_stage("predict-scroll")->run(b, ctx);
         if (!r) {
-            std::fprintf(stderr, "predict-scroll: %s\n", r.error().message.c_str());
-            return 9;
+            std::fprintf(stderr, "predict-scroll net=ink: %s\n", r.error().message.c_str());
+            return 11;
         }
-        auto s2 = codec::VolumeArchive::open(sp2);
-        auto sv = s2 ? s2->read_volume_u8() : Expected<Volume<u8>>(std::unexpected(Error{}));
-        CHECK(sv.has_value());
-        if (sv) {
-            // predict-scroll writes each finalised chunk with the voxels past the volume at 0 (the
-            // GlobalAccum sink), predict-surface's write_volume replicates the edge: encode the
-            // in-memory prediction's chunks the scroll's way and compare the decoded results
-            const s64 T = 64, ncz = (d.z + T - 1) / T, ncy = (d.y + T - 1) / T, ncx = (d.x + T - 1) / T;
-            const std::size_t n = static_cast<std::size_t>(ncz * ncy * ncx), cv = static_cast<std::size_t>(T * T * T);
-            std::vector<u8> ch(n * cv, 0), enc(n * (cv + 4096)), dec(n * cv);
-            std::vector<uint64_t> offs(n);
-            std::vector<uint32_t> lens(n);
-            for (s64 k = 0; k < static_cast<s64>(n); ++k) {
-                const s64 cz = k / (ncy * ncx), cy = (k / ncx) % ncy, cx = k % ncx;
-                for (s64 z = 0; z < T && cz * T + z < d.z; ++z)
-                    for (s64 y = 0; y < T && cy * T + y < d.y; ++y)
-                        for (s64 x = 0; x < T && cx * T + x < d.x; ++x)
-                            ch[k * cv + (z * T + y) * T + x] = want->data()[((cz * T + z) * d.y + cy * T + y) * d.x + cx * T + x];
-            }
-            CHECK(fx_fxvol_encode_tiles(ch.data(), nullptr, static_cast<int64_t>(n), 32.0f, 0.65f, 0.80f, 0, enc.data(), enc.size(),
-                                        offs.data(), lens.data()) == FX_OK);
-            CHECK(fx_fxvol_decode_tiles(enc.data(), enc.size(), offs.data(), lens.data(), static_cast<int64_t>(n), 32.0f,
-                                        0.65f, 0.80f, 0, dec.data(), nullptr) == FX_OK);
-            std::size_t far = 0;
-            double sum = 0;
-            for (s64 z = 0; z < d.z; ++z)
-                for (s64 y = 0; y < d.y; ++y)
-                    for (s64 x = 0; x < d.x; ++x) {
-                        const s64 k = ((z / T) * ncy + y / T) * ncx + x / T;
-                        const int w0 = dec[k * cv + ((z % T) * T + y % T) * T + x % T];
-                        const int dd = std::abs(int(sv->data()[(z * d.y + y) * d.x + x]) - w0);
-                        sum += dd;
-                        far += dd > 8;
-                    }
-            std::fprintf(stderr, "predict-scroll vs predict_surface (decoded q32): mean |d| %.4f, %zu voxels > 8\n",
-                         sum / static_cast<double>(vol.size()), far);
-            CHECK(sum / static_cast<double>(vol.size()) <= 0.25 && far * 1000 <= vol.size());
-        }
+        CHECK(wi && scroll_matches(*wi, sk, "predict-scroll net=ink vs predict_surface (ink options)"));
     }
     {  // predict_surface_filled with a clamped filler = predict_surface on the dense view
         auto f = ml::predict_surface_filled(
