@@ -50,6 +50,10 @@ PARITY_CASE = ROOT / "tests" / "golden" / "net128_cfg3.npz"  # the reference's m
 # 4.563 GB read + 5.933 GB written per forward of 8 tiles). ncu cannot run inside the timed bench,
 # so the captured figure is carried here and re-captured when the conv kernel changes.
 CONV_DRAM_BYTES_PER_TILE = 1.2946e9  # ncu launch list of the 256^3 bench: (112.121 + 137.737) GB over 193 tiles
+# The same for the calibrated schedule (--precision fp8, the default): the 22 conv launches of the
+# first forward of `bench.py --size 256 --steps 1 --warmup 3 --minimal --batch 4` (4 tiles),
+# 3.935 GB read + 2.722 GB written.
+CONV_DRAM_BYTES_PER_TILE_SCHED = 1.6644e9
 
 
 def env_int(name, default):
@@ -922,7 +926,7 @@ def main():
             "config": workload_config(args, tiles, world),
             "roofline": {
                 "bound": "tensor", "achieved": conv_tflops, "peak": peak, "unit": "TFLOP/s", "frac": conv_tflops / peak,
-                "traffic": CONV_DRAM_BYTES_PER_TILE if args.precision == "fp8-all" else None,
+                "traffic": {"fp8-all": CONV_DRAM_BYTES_PER_TILE, "fp8": CONV_DRAM_BYTES_PER_TILE_SCHED}.get(args.precision),
                 "traffic_unit": "DRAM bytes per 128^3 tile over the 22 conv launches (ncu capture, 256^3 bench)",
                 "algorithmic_flops_per_tile": 945.2e9,
                 "kernel": "conv_tc_kernel (all 22 conv launches of one forward, summed)",

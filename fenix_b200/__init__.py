@@ -182,6 +182,7 @@ def lib():
     _sig(L, "fx_net_profile_read_layers", i32, [vp, C.POINTER(C.c_double), i32])
     _sig(L, "fx_kernel_launches", C.c_ulonglong, [])
     _sig(L, "fx_tc_peak", i32, [i32, i32, C.c_double, i32, C.POINTER(C.c_double), C.POINTER(C.c_double)])
+    _sig(L, "fx_tc_rate", i32, [i32, i32, i32, C.c_double, i32, C.POINTER(C.c_double), C.POINTER(C.c_double)])
     _sig(L, "fx_synth_spiral", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
     _sig(L, "fx_synth_spiral_chunked", i32, [u8p, i64, i64, i64, C.POINTER(SpiralParams), C.c_uint64, i64, i64])
     _sig(L, "fx_synth_papyrus", i32, [u8p, u8p, i64, i64, i64, C.POINTER(PapyrusParams), C.c_uint64, i64])
@@ -288,6 +289,13 @@ def tc_peak(precision: str = "fp8", ms_per_run: float = 50.0, runs: int = 10, de
     """Measured dense tensor rate (TFLOP/s) of this library's MMA-loop kernel: (best, mean) over runs."""
     b, m = C.c_double(), C.c_double()
     check(lib().fx_tc_peak(device, PRECISIONS[precision], ms_per_run, runs, C.byref(b), C.byref(m)))
+    return b.value, m.value
+
+
+def tc_rate(precision: str = "fp8", n_cols: int = 256, ms_per_run: float = 50.0, runs: int = 10, device: int = 0):
+    """Measured tensor rate (TFLOP/s) of M = 128 x N = n_cols MMAs: the ceiling of that MMA shape."""
+    b, m = C.c_double(), C.c_double()
+    check(lib().fx_tc_rate(device, PRECISIONS[precision], n_cols, ms_per_run, runs, C.byref(b), C.byref(m)))
     return b.value, m.value
 
 

@@ -1,8 +1,10 @@
 // peak.cu — the dense tcgen05 tensor rate of this GPU, measured with our own kernel: every SM keeps
-// one CTA whose elected thread issues back-to-back M = 128, N = 256 MMAs (kind::f8f6f4 with e4m3
-// operands, or kind::f16 with bf16 / f16) on operand tiles resident in shared memory into a TMEM
-// accumulator. No global memory is touched inside the loop, so the rate is the tensor pipe's: the
-// denominator the convolutions' tensor roofline is quoted against.
+// one CTA whose elected thread issues back-to-back M = 128 MMAs (kind::f8f6f4 with e4m3 operands,
+// or kind::f16 with bf16 / f16) on operand tiles resident in shared memory into a TMEM accumulator.
+// No global memory is touched inside the loop, so the rate is the tensor pipe's. At N = 256 it is
+// the denominator the convolutions' tensor roofline is quoted against; narrower N (the 32- to
+// 96-column MMAs of the narrow conv layers) gives the ceiling of that MMA shape, where the A tile's
+// shared-memory read is spread over fewer columns of math.
 #include "fenix_b200.h"
 #include "counters.hpp"
 #include "ptx.cuh"
@@ -23,7 +25,7 @@ namespace {
 constexpr int kPeakM = 128, kPeakN = 256;
 constexpr int kABytes = kPeakM * 32, kBBytes = kPeakN * 32;  // one MMA's K: 32 bytes per row
 
-__global__ void __launch_bounds__(128, 1) tc_peak_kernel(int optype, long long n_mma, uint32_t* status) {
+__global__ void __launch_bounds__(128, 1) tc_peak_kernel(int optype, int n_cols, long long n_mma, uint32_t* status) {
     __shared__ __align__(1024) uint8_t a_tile[kABytes];
     __shared__ __align__(1024) uint8_t b_tile[kBBytes];
     __shared__ uint64_t done;
@@ -57,8 +59,8 @@ __global__ void __launch_bounds__(128, 1) tc_peak_kernel(int optype, long long n
         // 16-byte K halves LBO = rows x 16 B apart
         const uint64_t hi = (static_cast<uint64_t>(128 >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
         const uint64_t adesc = hi | (static_cast<uint64_t>((kPeakM * 16) >> 4) << 16) | (smem_u32(a_tile) >> 4);
-        const uint64_t bdesc = hi | (static_cast<uint64_t>((kPeakN * 16) >> 4) << 16) | (smem_u32(b_tile) >> 4);
-        const uint32_t idesc = instr_desc(kPeakM, kPeakN, optype);
+        const uint64_t bdesc = hi | (static_cast<uint64_t>((n_cols * 16) >> 4) << 16) | (smem_u32(b_tile) >> 4);
+        const uint32_t idesc = instr_desc(kPeakM, n_cols, optype);
         const uint32_t d = tmem_base;
         uint32_t acc = 0;
         if (optype == kOpE4M3) {
@@ -92,28 +94,28 @@ __global__ void __launch_bounds__(128, 1) tc_peak_kernel(int optype, long long n
 }  // namespace
 }  // namespace fxk
 
-extern "C" fx_status fx_tc_peak(int device, int precision, double ms_per_run, int runs, double* best_tflops,
+extern "C" fx_status fx_tc_rate(int device, int precision, int n_cols, double ms_per_run, int runs, double* best_tflops,
                                 double* mean_tflops) {
-    if (!best_tflops || runs < 1 || !(ms_per_run > 0.0) ||
+    if (!best_tflops || runs < 1 || !(ms_per_run > 0.0) || n_cols < 16 || n_cols > fxk::kPeakN || n_cols % 16 ||
         (precision != FX_PREC_FP8 && precision != FX_PREC_BF16 && precision != FX_PREC_F16))
-        return fxh::abi_error(FX_INVALID_ARGUMENT, "fx_tc_peak: bad argument");
+        return fxh::abi_error(FX_INVALID_ARGUMENT, "fx_tc_rate: bad argument");
     if (cudaSetDevice(device) != cudaSuccess) return fxh::abi_error(FX_INVALID_ARGUMENT, "fx_tc_peak: no such device");
     int major = 0, sms = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    if (major != 10) return fxh::abi_error(FX_UNSUPPORTED, "fx_tc_peak: needs an sm_100 GPU");
+    if (major != 10) return fxh::abi_error(FX_UNSUPPORTED, "fx_tc_rate: needs an sm_100 GPU");
     const int optype = precision;  // fx_precision values are the kernel's operand types
-    const double flop_per_mma = 2.0 * fxk::kPeakM * fxk::kPeakN * (optype == fxk::kOpE4M3 ? 32 : 16);
+    const double flop_per_mma = 2.0 * fxk::kPeakM * n_cols * (optype == fxk::kOpE4M3 ? 32 : 16);
     uint32_t* d_status = nullptr;
     cudaEvent_t e0, e1;
-    if (cudaMalloc(&d_status, 4) != cudaSuccess) return fxh::abi_error(FX_INTERNAL, "fx_tc_peak: cudaMalloc");
+    if (cudaMalloc(&d_status, 4) != cudaSuccess) return fxh::abi_error(FX_INTERNAL, "fx_tc_rate: cudaMalloc");
     cudaMemset(d_status, 0, 4);
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     auto run = [&](long long n) -> double {  // ms of one launch of n MMAs per SM
         cudaEventRecord(e0);
         fxk::count_launch();
-        fxk::tc_peak_kernel<<<sms, 128>>>(optype, n, d_status);
+        fxk::tc_peak_kernel<<<sms, 128>>>(optype, n_cols, n, d_status);
         cudaEventRecord(e1);
         cudaEventSynchronize(e1);
         float ms = 0.f;
@@ -138,9 +140,14 @@ extern "C" fx_status fx_tc_peak(int device, int precision, double ms_per_run, in
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     cudaFree(d_status);
-    if (err != cudaSuccess) return fxh::abi_error(FX_INTERNAL, std::string("fx_tc_peak: ") + cudaGetErrorString(err));
-    if (status) return fxh::abi_error(FX_INTERNAL, "fx_tc_peak: the final wait timed out");
+    if (err != cudaSuccess) return fxh::abi_error(FX_INTERNAL, std::string("fx_tc_rate: ") + cudaGetErrorString(err));
+    if (status) return fxh::abi_error(FX_INTERNAL, "fx_tc_rate: the final wait timed out");
     *best_tflops = best;
     if (mean_tflops) *mean_tflops = sum / runs;
     return FX_OK;
+}
+
+extern "C" fx_status fx_tc_peak(int device, int precision, double ms_per_run, int runs, double* best_tflops,
+                                double* mean_tflops) {
+    return fx_tc_rate(device, precision, fxk::kPeakN, ms_per_run, runs, best_tflops, mean_tflops);
 }

@@ -293,6 +293,11 @@ int fx_net_profile_read_layers(fx_net* net, double* layer_ms, int cap);
  * run gives the sustained, power-capped rate. No reference counterpart (the reference measures
  * none). */
 fx_status fx_tc_peak(int device, int precision, double ms_per_run, int runs, double* best_tflops, double* mean_tflops);
+/* fx_tc_peak for MMAs of n_cols columns (16..256, a multiple of 16): the rate an M = 128 x N = n_cols
+ * tcgen05 MMA shape reaches with its operands in shared memory, i.e. the tensor ceiling of a layer
+ * whose MMAs have that width. fx_tc_peak is n_cols = 256. No reference counterpart. */
+fx_status fx_tc_rate(int device, int precision, int n_cols, double ms_per_run, int runs, double* best_tflops,
+                     double* mean_tflops);
 /* Kernel launches issued by this library since the process started. */
 unsigned long long fx_kernel_launches(void);
 /* Device buffer of 16 u64 cycle counters that conv launches add to when the library is built

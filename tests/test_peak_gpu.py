@@ -25,3 +25,23 @@ def test_tc_peak_arguments(cuda_torch):
     b = C.c_double()
     assert fx.lib().fx_tc_peak(0, 7, 10.0, 1, C.byref(b), None) == fx.FX_INVALID_ARGUMENT
     assert fx.lib().fx_tc_peak(0, 1, 0.0, 1, C.byref(b), None) == fx.FX_INVALID_ARGUMENT
+
+
+def test_tc_rate_narrow_mmas(cuda_torch):
+    """The MMA shapes of the narrow conv layers: N = 32 .. 256 columns. Every width runs within the
+    dense nominal, and the 32-column shape is clearly slower than the widest: its A tile's
+    shared-memory read is spread over a quarter of the columns of math of N = 128."""
+    rates = {n: fx.tc_rate("f16", n, 20.0, 3)[0] for n in (32, 64, 96, 128, 192, 256)}
+    print("f16 tcgen05 rate by N:", {n: round(r) for n, r in rates.items()})
+    top = max(rates.values())
+    assert all(r > 50.0 for r in rates.values())
+    assert top < 2400.0
+    assert rates[32] < 0.8 * top
+
+
+def test_tc_rate_arguments(cuda_torch):
+    import ctypes as C
+
+    b = C.c_double()
+    for n in (0, 8, 24, 272):
+        assert fx.lib().fx_tc_rate(0, 2, n, 10.0, 1, C.byref(b), None) == fx.FX_INVALID_ARGUMENT
