@@ -37,13 +37,12 @@ __device__ __forceinline__ uint64_t wait_limit(const ConvParams& p) { return p.w
 #define FX_TCNT(p, i, n) ((void)0)
 #endif
 constexpr int kMaxCols = 512;  // per-channel scale / bias table entries
-constexpr int kMaxRing = 8;    // z-plane ring: TMEM plane slots per segment
 
 struct SmemCtl {
     uint64_t full[16];
     uint64_t empty[16];
-    uint64_t accf[kMaxRing];  // accumulator slots (2), or the ring's plane slots
-    uint64_t acce[kMaxRing];
+    uint64_t accf[2];
+    uint64_t acce[2];
     uint64_t drain;
     uint64_t xready[2][2];  // fold epilogue: row exchange of [half][parity] published by its 4 warps
     uint64_t bres;          // z-plane fold: the resident weights have landed
@@ -73,7 +72,7 @@ __device__ __forceinline__ int64_t unit_q0(const ConvParams& p, int mu) {
     if (p.zfold) {
         const int64_t P2 = static_cast<int64_t>(p.Hp) * p.Wp;
         const int zg = mu / p.zseg, seg = mu - zg * p.zseg;
-        const int S = p.zring ? 2 : p.R / p.zplanes;
+        const int S = p.R / p.zplanes;
         return (1 + static_cast<int64_t>(zg) * p.zplanes) * P2 + (p.Wp + 1) + static_cast<int64_t>(seg) * 128 * S;
     }
     return p.row_begin + static_cast<int64_t>(mu) * p.block_rows * p.R;
@@ -392,171 +391,6 @@ __device__ void mma_loop_z(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int
         }
         if (aborted) break;
         mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->accf[aslot]));
-    }
-    mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->drain));
-    if (leader) {
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(smem_u32(&ctl->drain), 0u) && globaltimer_ns() - t0 < wait_limit(p)) {
-        }
-    }
-    __syncwarp();
-}
-
-// MMA warp of the z-plane ring (ConvParams::zring): a unit is two segments x a chunk of Zc planes;
-// stage j holds input plane j - 1 of the chunk and feeds planes j, j - 1, j - 2 (taps kz 0, 1, 2).
-// Plane i of this CTA (a running index across its units) accumulates in ring slot i mod K of each
-// segment, slots at descending TMEM columns, so the planes of a stacked MMA are adjacent columns
-// unless the ring wraps between them, where the MMA is split. Before stage j, plane j's slot must be
-// drained (acce); after it, plane j - 2 is final and its slot's accf barrier gets a commit.
-template <bool F8>
-__device__ void mma_loop_ring(const ConvParams& p, uint8_t* smem, SmemCtl* ctl, int n_units) {
-    constexpr int S = 2;
-    const bool leader = elect_one();
-    const uint32_t K = static_cast<uint32_t>(p.zring);  // a power of two
-    const uint32_t lk = static_cast<uint32_t>(__ffs(p.zring) - 1);
-    const int Zc = p.zplanes;
-    uint32_t k = 0;  // global stage counter
-    uint32_t g = 0;  // ring index of the current unit's plane 0
-    const uint32_t tbase = ctl->tmem_base;
-    const uint32_t ncol = static_cast<uint32_t>(p.N_tile);
-    const uint32_t smem_base = smem_u32(smem);
-    const uint64_t hi = (static_cast<uint64_t>(128 >> 4) << 32) | (static_cast<uint64_t>(1) << 46);
-    const uint64_t b_lbo = static_cast<uint64_t>((3 * p.zkstride) >> 4) << 16;
-    const uint32_t idesc1 = instr_desc(128, p.N_tile, p.optype);
-    const uint32_t idesc2 = instr_desc(128, 2 * p.N_tile, p.optype);
-    const uint32_t idesc3 = instr_desc(128, 3 * p.N_tile, p.optype);
-    const uint64_t bres = (hi | b_lbo) + ((smem_base + static_cast<uint32_t>(p.bres_off)) >> 4);
-    const uint64_t kzs = static_cast<uint64_t>(p.zkstride >> 4);  // B rows of tap kz -> kz + 1
-    const int nent = p.n_mmas;
-    {
-        const bool ok = mbar_wait(smem_u32(&ctl->bres), 0u, &ctl->abort, wait_limit(p));
-        if (!__all_sync(0xffffffffu, ok)) {
-            if (leader) {
-                set_status(p.status, kStatusTimeoutFull);
-                ctl->abort = 1;
-            }
-            n_units = 0;  // issue nothing; fall through to the drain
-        }
-    }
-    tc_fence_after();
-    bool aborted = false;
-    for (int unit = blockIdx.x; unit < n_units && !aborted; unit += gridDim.x, g += static_cast<uint32_t>(Zc)) {
-        for (int s = 0; s < Zc + 2; ++s, ++k) {
-            const int slot = k % p.n_pipe;
-            if (s < Zc) {  // plane s begins: the previous plane of its ring slot must be drained
-                const uint32_t i = g + static_cast<uint32_t>(s);
-                FX_T0();
-                const bool ok =
-                    mbar_wait(smem_u32(&ctl->acce[i & (K - 1u)]), ((i >> lk) & 1u) ^ 1u, &ctl->abort, wait_limit(p));
-                if (!__all_sync(0xffffffffu, ok)) {
-                    if (leader) {
-                        set_status(p.status, kStatusTimeoutAccFree);
-                        ctl->abort = 1;
-                    }
-                    aborted = true;
-                    break;
-                }
-                if (leader) FX_TADD(p, 2);
-            }
-            {
-                FX_T0();
-                const bool ok =
-                    mbar_wait(stage_full_bar(p, ctl, slot, k), (k / p.n_pipe) & 1u, &ctl->abort, wait_limit(p));
-                if (!__all_sync(0xffffffffu, ok)) {
-                    if (leader) {
-                        set_status(p.status, kStatusTimeoutFull);
-                        ctl->abort = 1;
-                    }
-                    aborted = true;
-                    break;
-                }
-                if (leader) FX_TADD(p, 3);
-            }
-            tc_fence_after();
-            FX_T0();
-            const int kz_lo = s - (Zc - 1) > 0 ? s - (Zc - 1) : 0;
-            const int kz_hi = s < 2 ? s : 2;
-            if (leader) {
-                const uint64_t ahi = hi + ((smem_base + static_cast<uint32_t>(slot * p.stage_bytes)) >> 4);
-                // The stage's runs of taps, computed once: taps kz_lo..kz_hi split where their planes
-                // wrap around the ring (at most 3 runs); each run is one MMA per entry and segment.
-                // Issuing is this loop's bound, so the per-MMA work is a few adds.
-                uint32_t rd[3], ri[3], rl[3];
-                uint64_t rb[3];
-                int nr = 0;
-                {
-                    int kz = kz_lo;
-#pragma unroll
-                    for (int r = 0; r < 3; ++r) {
-                        if (kz <= kz_hi) {
-                            const uint32_t sl = (g + static_cast<uint32_t>(s - kz)) & (K - 1u);
-                            int len = kz_hi - kz + 1;
-                            if (len > static_cast<int>(sl) + 1) len = static_cast<int>(sl) + 1;
-                            rd[r] = tbase + (K - 1u - sl) * ncol;
-                            ri[r] = len == 3 ? idesc3 : (len == 2 ? idesc2 : idesc1);
-                            rl[r] = static_cast<uint32_t>(len);
-                            rb[r] = static_cast<uint64_t>(kz) * kzs;
-                            nr = r + 1;
-                            kz += len;
-                        }
-                    }
-                }
-                const uint32_t segc = K * ncol;  // columns of one segment's ring
-                // entry 0: plane s (tap 0) starts its accumulator alone; the rest of its run and the
-                // other runs accumulate
-                {
-                    const ConvMma mm = p.mmas[0];
-                    const uint64_t a0 = ahi + mm.a;
-                    const uint64_t b0 = bres + mm.b;
-#pragma unroll
-                    for (int sg = 0; sg < S; ++sg) {
-                        const uint64_t ad = a0 + static_cast<uint64_t>(sg * 128);
-                        const uint32_t ds = static_cast<uint32_t>(sg) * segc;
-#pragma unroll
-                        for (int r = 0; r < 3; ++r) {
-                            if (r >= nr) break;
-                            if (r == 0 && kz_lo == 0) {
-                                if (F8) mma_f8_if(1u, rd[0] + ds, ad, b0 + rb[0], idesc1, 0u);
-                                else mma_f16_if(1u, rd[0] + ds, ad, b0 + rb[0], idesc1, 0u);
-                                if (rl[0] > 1u) {
-                                    const uint32_t id = rl[0] == 3u ? idesc2 : idesc1;
-                                    if (F8) mma_f8_if(1u, rd[0] + ds + ncol, ad, b0 + rb[0] + kzs, id, 1u);
-                                    else mma_f16_if(1u, rd[0] + ds + ncol, ad, b0 + rb[0] + kzs, id, 1u);
-                                }
-                            } else {
-                                if (F8) mma_f8_if(1u, rd[r] + ds, ad, b0 + rb[r], ri[r], 1u);
-                                else mma_f16_if(1u, rd[r] + ds, ad, b0 + rb[r], ri[r], 1u);
-                            }
-                        }
-                    }
-                }
-                for (int e = 1; e < nent; ++e) {
-                    const ConvMma mm = p.mmas[e];
-                    const uint64_t a0 = ahi + mm.a;
-                    const uint64_t b0 = bres + mm.b;
-#pragma unroll
-                    for (int sg = 0; sg < S; ++sg) {
-                        const uint64_t ad = a0 + static_cast<uint64_t>(sg * 128);
-                        const uint32_t ds = static_cast<uint32_t>(sg) * segc;
-                        if (F8) mma_f8_if(1u, rd[0] + ds, ad, b0 + rb[0], ri[0], 1u);
-                        else mma_f16_if(1u, rd[0] + ds, ad, b0 + rb[0], ri[0], 1u);
-                        if (nr > 1) {
-                            if (F8) mma_f8_if(1u, rd[1] + ds, ad, b0 + rb[1], ri[1], 1u);
-                            else mma_f16_if(1u, rd[1] + ds, ad, b0 + rb[1], ri[1], 1u);
-                        }
-                        if (nr > 2) {
-                            if (F8) mma_f8_if(1u, rd[2] + ds, ad, b0 + rb[2], ri[2], 1u);
-                            else mma_f16_if(1u, rd[2] + ds, ad, b0 + rb[2], ri[2], 1u);
-                        }
-                    }
-                }
-            }
-            __syncwarp();
-            mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->empty[slot]));
-            // plane s - 2 received its last tap (kz = 2) in this stage
-            if (s >= 2) mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->accf[(g + static_cast<uint32_t>(s - 2)) & (K - 1u)]));
-            if (leader) FX_TADD(p, 4);
-        }
     }
     mma_commit_if(leader ? 1u : 0u, smem_u32(&ctl->drain));
     if (leader) {
@@ -928,157 +762,6 @@ __device__ void epilogue_loop(const ConvParams& p, SmemCtl* ctl, int n_units) {
     if (prenorm && run_b >= 0) flush();
 }
 
-// Epilogue of the z-plane ring: the planes of a unit in order, each waited for on its ring slot's
-// accf barrier and handed back through acce once drained. The two warps of a TMEM lane quarter split
-// the 16-column chunks (N_tile >= 32: one statistics record per quarter) or the two segments
-// (N_tile = 16: one record per warp). Statistics accumulate in registers over a CTA's run of units
-// of one batch item and are added to its record at the run's end, as in epilogue_loop.
-template <int NCH>
-__device__ void epilogue_ring(const ConvParams& p, SmemCtl* ctl, int n_units) {
-    const int lane = threadIdx.x & 31;
-    const int wq = (threadIdx.x >> 5) & 3;
-    const int half = ((threadIdx.x >> 5) - 2) >> 2;
-    const uint32_t tbase = ctl->tmem_base;
-    const uint32_t K = static_cast<uint32_t>(p.zring);  // a power of two
-    const uint32_t lk = static_cast<uint32_t>(__ffs(p.zring) - 1);
-    const int Zc = p.zplanes;
-    const uint32_t ncol = static_cast<uint32_t>(p.N_tile);
-    const int64_t P2r = static_cast<int64_t>(p.Hp) * p.Wp;
-    RowDecomp rd;
-    rd.P2 = static_cast<uint32_t>(p.Hp * p.Wp);
-    rd.Wp = static_cast<uint32_t>(p.Wp);
-    rd.mP2 = ~0ull / rd.P2 + 1;
-    rd.mWp = ~0ull / rd.Wp + 1;
-    const uint32_t zmax = static_cast<uint32_t>(p.Dp - 2), ymax = static_cast<uint32_t>(p.Hp - 2),
-                   xmax = static_cast<uint32_t>(p.Wp - 2);
-    constexpr bool kSplitC = NCH >= 2;
-    constexpr int kMy = kSplitC ? NCH / 2 : NCH;  // 16-column chunks of a block drained by this warp
-    constexpr int kSegs = kSplitC ? 2 : 1;        // segments drained by this warp
-    const int c0 = kSplitC ? half : 0;
-    const int sg0 = kSplitC ? 0 : half;
-    const bool percol = p.col_scale != nullptr;
-    const float acc_scale = p.acc_scale;
-    float r1[kMy][16], r2[kMy][16];
-#pragma unroll
-    for (int c = 0; c < kMy; ++c)
-#pragma unroll
-        for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
-    int run_b = -1, run_nt = 0;
-    auto flush = [&]() {
-        float* dst = p.stats + ((static_cast<int64_t>(run_b) * gridDim.x + blockIdx.x) * p.stat_recs +
-                                (kSplitC ? wq : half * 4 + wq)) *
-                                   p.stats_C * 2;
-#pragma unroll
-        for (int c = 0; c < kMy; ++c) {
-            const float s1 = warp_transpose_reduce16(r1[c], lane);
-            const float s2 = warp_transpose_reduce16(r2[c], lane);
-            if (lane < 16) {
-                const int ch = (kSplitC ? c0 + 2 * c : c) * 16 + lane;
-                float2* q = reinterpret_cast<float2*>(dst + (run_nt * p.N_tile + ch) * 2);
-                const float2 o = *q;
-                *q = make_float2(o.x + s1, o.y + s2);
-            }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) r1[c][i] = r2[c][i] = 0.f;
-        }
-    };
-    uint32_t g = 0;
-    for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x, g += static_cast<uint32_t>(Zc)) {
-        int b, mu, nt;
-        unit_coords(p, unit, b, mu, nt);
-        if (b != run_b || nt != run_nt) {
-            if (run_b >= 0) flush();
-            run_b = b;
-            run_nt = nt;
-        }
-        const int zg = mu / p.zseg;
-        const uint32_t z0 = 1u + static_cast<uint32_t>(zg * Zc);
-        const int64_t q0 = unit_q0(p, mu);
-        // every plane of a segment has the same in-plane offset: ownership decided once per unit
-        uint32_t zok = 0;
-        {
-            const uint32_t o0 = static_cast<uint32_t>(q0 - static_cast<int64_t>(z0) * P2r) + wq * 32 + lane;
-#pragma unroll
-            for (int sg = 0; sg < 2; ++sg) {
-                const uint32_t o = o0 + sg * 128;
-                uint32_t y, x;
-                rd.split_plane(o, y, x);
-                const bool ok = o < rd.P2 && y >= 1 && y <= ymax && x >= 1 && x <= xmax;
-                zok |= (ok ? 1u : 0u) << sg;
-            }
-        }
-        uint8_t* ob = p.out + static_cast<int64_t>(b) * p.out_batch_stride;
-        for (int r = 0; r < Zc; ++r) {
-            const uint32_t i = g + static_cast<uint32_t>(r);
-            const uint32_t sl = i & (K - 1u);
-            {
-                FX_T0();
-                if (!mbar_wait(smem_u32(&ctl->accf[sl]), (i >> lk) & 1u, &ctl->abort, wait_limit(p))) {
-                    set_status(p.status, kStatusTimeoutAcc);
-                    ctl->abort = 1;
-                    return;
-                }
-                if (threadIdx.x == 64) FX_TADD(p, 5);
-            }
-            tc_fence_after();
-            const bool zin = z0 + static_cast<uint32_t>(r) <= zmax;
-            uint32_t raw[kSegs][kMy][16];
-#pragma unroll
-            for (int q = 0; q < kSegs; ++q)
-#pragma unroll
-                for (int c = 0; c < kMy; ++c) {
-                    const int sg = sg0 + q;
-                    const int ch = kSplitC ? c0 + 2 * c : c;
-                    tmem_ld16_nowait(tbase + (static_cast<uint32_t>(wq * 32) << 16) +
-                                         (static_cast<uint32_t>(sg) * K + (K - 1u - sl)) * ncol + ch * 16,
-                                     raw[q][c]);
-                }
-            tmem_wait();
-#pragma unroll
-            for (int q = 0; q < kSegs; ++q)
-#pragma unroll
-                for (int c = 0; c < kMy; ++c) tmem_regs_ready(raw[q][c]);
-#pragma unroll
-            for (int q = 0; q < kSegs; ++q) {
-                const int sg = sg0 + q;
-                const bool valid = zin && ((zok >> sg) & 1u);
-                const int64_t row = q0 + sg * 128 + static_cast<int64_t>(r) * P2r + wq * 32 + lane;
-#pragma unroll
-                for (int c = 0; c < kMy; ++c) {
-                    const int ch = kSplitC ? c0 + 2 * c : c;
-                    // rows that are no output (halo, other planes, past the end) may hold sums over
-                    // stale operands, NaN included: selected to zero
-                    float v[16];
-                    if (percol) {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e)
-                            v[e] = valid ? __uint_as_float(raw[q][c][e]) * ctl->colscale[ch * 16 + e] : 0.f;
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) v[e] = valid ? __uint_as_float(raw[q][c][e]) * acc_scale : 0.f;
-                    }
-                    if (valid) {
-                        uint8_t* o = ob + row * 16 + static_cast<int64_t>(ch * 2) * p.out_group_stride;
-                        *reinterpret_cast<uint4*>(o) = pack_cell_f16_sat(v);
-                        *reinterpret_cast<uint4*>(o + p.out_group_stride) = pack_cell_f16_sat(v + 8);
-                    }
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        r1[c][e] += v[e];
-                        r2[c][e] = fmaf(v[e], v[e], r2[c][e]);
-                    }
-                }
-            }
-            // plane drained: its ring slot goes back to the MMA issuer
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&ctl->acce[sl]));
-        }
-        if (threadIdx.x == 64) FX_TCNT(p, 8, 1);
-    }
-    if (run_b >= 0) flush();
-}
-
 // Epilogue of the transposed convolution (upsample mode, Cout a power of two): column n of the
 // accumulator is phase n / Cout, channel n % Cout. The warp's chunks are read from TMEM four per
 // wait, the phase / channel of each chunk and its byte offset are computed once per unit, and
@@ -1411,7 +1094,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             mbar_init(smem_u32(&ctl->full[i]), 1);
             mbar_init(smem_u32(&ctl->empty[i]), 1);
         }
-        for (int i = 0; i < kMaxRing; ++i) {
+        for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&ctl->accf[i]), 1);
             mbar_init(smem_u32(&ctl->acce[i]), kEpiWarps);
         }
@@ -1446,8 +1129,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
         if (threadIdx.x == 0) set_status(p.status, kStatusBadTmem);
     } else if (warp == 0) {
         producer_loop(p, smem, ctl, n_units);
-    } else if (warp == 1 && p.zring) {
-        p.optype == kOpE4M3 ? mma_loop_ring<true>(p, smem, ctl, n_units) : mma_loop_ring<false>(p, smem, ctl, n_units);
     } else if (warp == 1 && p.zfold) {
         const bool f8 = p.optype == kOpE4M3;
         if (p.zplanes == 4) f8 ? mma_loop_z<true, 4>(p, smem, ctl, n_units) : mma_loop_z<false, 4>(p, smem, ctl, n_units);
@@ -1470,13 +1151,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_tc_kernel(const __grid_c
             case 2: f8 ? mma_loop<2, true, false, false>(p, smem, ctl, n_units) : mma_loop<2, false, false, false>(p, smem, ctl, n_units); break;
             case 4: f8 ? mma_loop<4, true, false, false>(p, smem, ctl, n_units) : mma_loop<4, false, false, false>(p, smem, ctl, n_units); break;
             case 8: f8 ? mma_loop<8, true, false, false>(p, smem, ctl, n_units) : mma_loop<8, false, false, false>(p, smem, ctl, n_units); break;
-            default: break;  // rejected on the host (launch_conv_tc)
-        }
-    } else if (p.zring) {
-        switch (p.N_tile / 16) {
-            case 1: epilogue_ring<1>(p, ctl, n_units); break;
-            case 2: epilogue_ring<2>(p, ctl, n_units); break;
-            case 4: epilogue_ring<4>(p, ctl, n_units); break;
             default: break;  // rejected on the host (launch_conv_tc)
         }
     } else if (p.fold) {
@@ -1562,18 +1236,7 @@ cudaError_t launch_conv_tc(const ConvParams& p, int grid, size_t smem_bytes, cud
     } else if (p.block_rows != 128) {
         return cudaErrorInvalidValue;
     }
-    if (p.zring) {
-        const int nch = p.N_tile / 16;
-        if (!p.zfold || p.fold || p.mode != kModePrenorm || p.n_tiles != 1 || p.R != 2 || p.zring < 4 ||
-            (p.zring & (p.zring - 1)) ||
-            p.zring > kMaxRing || p.zplanes < 1 || p.zplanes > 64 || p.zseg <= 0 || p.n_stages != p.zplanes + 2 ||
-            !(nch == 1 || nch == 2 || nch == 4) || p.N_tile % 16 || p.n_mmas <= 0 || p.bres_off % 128 ||
-            p.bres_bytes % 16 || p.bres_bytes < 3 * p.n_mmas * p.N_tile * 32 || p.zkstride != p.N_tile * 16 ||
-            2 * p.zring * p.N_tile > static_cast<int>(p.tmem_cols) || p.tmem_cols > 512u ||
-            static_cast<size_t>(p.bres_off) < need)
-            return cudaErrorInvalidValue;
-        need = static_cast<size_t>(p.bres_off) + p.bres_bytes;
-    } else if (p.zfold) {
+    if (p.zfold) {
         if (p.fold || p.mode != kModePrenorm || p.n_tiles != 1 || !(p.R == 2 || p.R == 4 || p.R == 8) ||
             !(p.zplanes == 2 || p.zplanes == 4) || p.R != 2 * p.zplanes || p.zseg <= 0 || p.n_stages != p.zplanes + 2 || p.n_mmas <= 0 || p.bres_off % 128 || p.bres_bytes % 16 ||
             p.bres_bytes < 3 * p.n_mmas * p.N_tile * 32 || p.zkstride != p.N_tile * 16 ||

@@ -29,14 +29,6 @@
 // accumulators, unshifted. Stages are input-plane windows; the 27 taps' weights stay resident in
 // shared memory.
 //
-// z-plane ring (zring > 0): the same stages and MMA entries, but a unit is a whole z chunk of
-// `zplanes` planes (16 or 32) of two segments, and output planes rotate through zring TMEM slots per
-// segment (plane slot = running plane index mod zring, slots at descending columns). Stage j's
-// stacked MMA writes planes j, j-1, j-2; plane j-2 is final after it and is handed to the epilogue
-// through its own barrier, so no plane of the chunk waits for the others and each input plane is
-// staged once per chunk ((zplanes + 2) / zplanes A reads and copies per output plane instead of
-// (Z + 2) / Z with Z = 2 or 4). A stacked MMA whose planes wrap around the ring is split in two.
-//
 // The host compiles each layer into a small "program": a list of pipeline stages (one bulk
 // copy of a window of rows for a range of groups + the matching packed weight block) and, per
 // stage, the list of MMAs (A offset, K-half stride, B offset). The kernel is persistent and
@@ -111,10 +103,6 @@ struct ConvParams {
     int32_t zfold;               // 1: z-plane fold — the R blocks of a unit are one z plane apart
     int32_t zseg;                // z-plane fold: units per plane (each S adjacent 128-row segments)
     int32_t zplanes;             // z-plane fold: planes per unit; R = zplanes x S blocks
-    int32_t zring;               // z-plane ring (0 = off): the fold's planes rotate through zring
-                                 // TMEM plane slots per segment, each drained as soon as its last
-                                 // tap lands; a unit is then 2 segments x zplanes planes (a z chunk)
-                                 // and every input plane of the chunk is staged once
     int32_t zkstride;            // z-plane fold: bytes between the resident weight rows of kz and kz + 1
     int32_t bres_off, bres_bytes;  // z-plane fold: resident weights in shared memory (offset, size)
     int32_t n_units_m;           // ceil((row_end - row_begin) / (block_rows R))

@@ -372,12 +372,6 @@ static bool zfold_enabled() {
     return !(v && v[0] == '0');
 }
 
-// z-plane ring (fxk::ConvParams::zring) for the z-fold layers: FENIX_B200_CONV_ZRING=1 turns it on.
-static bool zring_enabled() {
-    const char* v = std::getenv("FENIX_B200_CONV_ZRING");
-    return v && v[0] == '1';
-}
-
 Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax, int sm_count,
                            std::vector<void*>& allocs_) {
     DevProgram& dp = L.prog[q];
@@ -562,25 +556,9 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
     const int N_total = sp.N_total;
     if (sp.zfold) {  // one N tile; 2 segments x Z planes (Z 4 at N 32, 2 at N 64); 2 TMEM slots
         const ActGeom& g = gout;
-        const int S = 2;
+        const int S = 2, Zp = N_total <= 32 ? 4 : 2, R = S * Zp;
         const int64_t Wp = g.W + 2, P2 = static_cast<int64_t>(g.H + 2) * Wp;
         const int zseg = static_cast<int>((P2 - 2 * (Wp + 1) + 128 * S - 1) / (128 * S));
-        // ring: K plane slots per segment fill the 512 TMEM columns; the z chunk is the largest of
-        // 32 / 16 / 8 planes that still gives every SM two units at the largest batch
-        const int K = zring_enabled() ? std::min(8, 256 / N_total) : 0;
-        int Zp = N_total <= 32 ? 4 : 2;
-        if (K) {
-            Zp = 8;
-            for (int zc : {32, 16}) {
-                const int64_t u = static_cast<int64_t>(Bmax_) * ((g.D + zc - 1) / zc) * zseg;
-                if (u >= 2LL * sm_count_) {
-                    Zp = zc;
-                    break;
-                }
-            }
-            Zp = std::min(Zp, g.D);
-        }
-        const int R = K ? S : S * Zp;
         sp.N_tile = N_total;
         sp.R = Zp;
         sp.zsegs = S;
@@ -593,11 +571,10 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
             dp.N_tile = N_total;
             dp.acc_slots = 2;
             uint32_t cols = 32;
-            while (cols < static_cast<uint32_t>(K ? 2 * K * N_total : 2 * R * N_total)) cols <<= 1;
+            while (cols < static_cast<uint32_t>(2 * R * N_total)) cols <<= 1;
             dp.tmem_cols = cols;
             dp.zseg = zseg;
             dp.zplanes = Zp;
-            dp.zring = K;
             dp.n_units_m = static_cast<int>((g.D + Zp - 1) / Zp) * zseg;
             dp.zfold = true;
             dp.fold = false;
@@ -899,7 +876,6 @@ Status launch_layer(Layer& L, int q, ActGeom gin, ActGeom gout, const uint8_t* i
     if (dp.zfold) {
         p.zseg = dp.zseg;
         p.zplanes = dp.zplanes;
-        p.zring = dp.zring;
         p.zkstride = dp.host.zkstride;
         p.bres_bytes = dp.host.bres_bytes;
         p.bres_off = static_cast<int32_t>((static_cast<size_t>(dp.host.n_pipe) * dp.host.stage_bytes +

@@ -58,8 +58,7 @@ struct DevProgram {
     bool fold = false;     // x-tap fold (fxk::ConvParams::fold)
     bool zfold = false;    // z-plane fold (fxk::ConvParams::zfold)
     int zseg = 0;          // z-plane fold: units per plane
-    int zplanes = 0;       // z-plane fold: planes per unit (the z chunk of the ring)
-    int zring = 0;         // z-plane ring: TMEM plane slots per segment (fxk::ConvParams::zring), 0 = off
+    int zplanes = 0;       // z-plane fold: planes per unit
     int block_rows = 128;
     bool built = false;
     size_t smem() const;
