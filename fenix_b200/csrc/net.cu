@@ -590,6 +590,11 @@ Status build_layer_program(Layer& L, int q, ActGeom gin, ActGeom gout, int Bmax,
         sp.zfold = false;  // weights do not fit next to three stages: the regular program
     }
     int N_tile = N_total <= 256 ? N_total : (N_total == 320 ? 320 : 256);
+    // A stride-2 conv 256 columns wide runs as two 128-column tiles: its phase-split windows hold
+    // few taps each, so halving the B block per K step doubles the groups per stage and the units
+    // (the 16^3 encoder conv of the surface net: 5.43 -> 3.62 ms per 343 tiles of 128^3; the
+    // stride-1 256-column layers measured no gain, and 64-column tiles lost).
+    if (L.kind == Layer::kConv && L.stride == 2 && N_total == 256) N_tile = 128;
     if (N_total % N_tile) return fail(kUnsupported, L.name + ": output width " + std::to_string(N_total) + " not tileable");
     int R = N_tile <= 32 ? 8 : (N_tile <= 64 ? 4 : (N_tile <= 128 ? 2 : 1));
     const int brows = fold ? 126 : 128;
