@@ -566,24 +566,31 @@ __constant__ float c_head_b[2];
 
 // Block = (plane chunk, z, batch item); thread = one voxel. Scale/shift of the batch item's C
 // channels sit in shared memory, the head weights in constant memory.
-__global__ void __launch_bounds__(kEwThreads) head_blend_kernel(HeadParams h, FastDiv fp) {
+// One thread per tile voxel, five 256-thread CTAs per SM (48 registers, no spill). The thread's
+// pre-norm cells are requested before the block's {scale, shift} table is loaded, so the two
+// latencies overlap (a block lives for one voxel per thread).
+__global__ void __launch_bounds__(kEwThreads, 5) head_blend_kernel(HeadParams h, FastDiv fp) {
     const int Hp = h.Py + 2, Wp = h.Px + 2;
     const int b = blockIdx.z, z = blockIdx.y;
     __shared__ float2 s_ss[64];
+    const uint32_t i = blockIdx.x * kEwThreads + threadIdx.x;
+    const bool live = i < static_cast<uint32_t>(h.Py) * h.Px;
+    const int G = h.C / 8;
+    int y = 0, x = 0;
+    uint4 cells[8];
+    if (live) {
+        y = static_cast<int>(fdiv(i, fp));
+        x = static_cast<int>(i - static_cast<uint32_t>(y) * h.Px);
+        const int64_t row = (static_cast<int64_t>(z + 1) * Hp + (y + 1)) * Wp + (x + 1);
+        const uint8_t* pb = h.pre + b * h.pre_batch_stride + row * 16;
+#pragma unroll
+        for (int gi = 0; gi < 8; ++gi)
+            if (gi < G) cells[gi] = __ldcs(reinterpret_cast<const uint4*>(pb + gi * h.pre_group_stride));
+    }
     if (threadIdx.x < h.C)
         s_ss[threadIdx.x] = __ldg(reinterpret_cast<const float2*>(h.ss) + static_cast<int64_t>(b) * h.C + threadIdx.x);
     __syncthreads();
-    const uint32_t i = blockIdx.x * kEwThreads + threadIdx.x;
-    if (i >= static_cast<uint32_t>(h.Py) * h.Px) return;
-    const int y = static_cast<int>(fdiv(i, fp));
-    const int x = static_cast<int>(i - static_cast<uint32_t>(y) * h.Px);
-    const int G = h.C / 8;
-    const int64_t row = (static_cast<int64_t>(z + 1) * Hp + (y + 1)) * Wp + (x + 1);
-    const uint8_t* pb = h.pre + b * h.pre_batch_stride + row * 16;
-    uint4 cells[8];
-#pragma unroll
-    for (int gi = 0; gi < 8; ++gi)
-        if (gi < G) cells[gi] = __ldcs(reinterpret_cast<const uint4*>(pb + gi * h.pre_group_stride));
+    if (!live) return;
     float l0 = c_head_b[0], l1 = h.ncls > 1 ? c_head_b[1] : 0.f;
 #pragma unroll
     for (int gi = 0; gi < 8; ++gi) {
