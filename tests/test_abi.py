@@ -35,3 +35,16 @@ def test_create_rejects_missing_file_without_gpu_work(tmp_path):
     with pytest.raises(fx.FxError) as ei:
         fx.Net(str(tmp_path / "absent.fxweights"), patch=64)
     assert ei.value.code in (1, 3)
+
+
+def test_tc_rate_rejects_bad_widths_before_device_work():
+    # Argument checks come first: widths outside 16..256 or not a multiple of 16, a bad precision,
+    # no runs or a null result pointer return FX_INVALID_ARGUMENT on any box, GPU or not.
+    import ctypes as C
+
+    b = C.c_double()
+    for n in (0, 8, 24, 272):
+        assert fx.lib().fx_tc_rate(0, fx.PREC_F16, n, 10.0, 1, C.byref(b), None) == fx.FX_INVALID_ARGUMENT
+    assert fx.lib().fx_tc_rate(0, 7, 64, 10.0, 1, C.byref(b), None) == fx.FX_INVALID_ARGUMENT
+    assert fx.lib().fx_tc_rate(0, fx.PREC_F16, 64, 10.0, 0, C.byref(b), None) == fx.FX_INVALID_ARGUMENT
+    assert fx.lib().fx_tc_rate(0, fx.PREC_F16, 64, 10.0, 1, None, None) == fx.FX_INVALID_ARGUMENT
